@@ -1,0 +1,118 @@
+"""Test-time routing and evaluation (reference ``src/opendipaco/inference.py:27-173``).
+
+* ``compose_path`` aliases the trained bank (no copy).
+* ``perplexity``: exp of the mean of per-batch mean losses.
+* ``routed_perplexity``: route each sequence by its first ``prefix_len`` tokens,
+  score only targets at positions >= prefix_len (the paper's protocol), token-level
+  sum / count, exp.
+* ``routed_window_perplexity``: re-route every ``window`` tokens from the previous
+  window and score each window under its path with the full preceding context
+  recomputed (no KV cache), the reference's definition.
+
+On CUDA the per-path batches run through the sm_100a forward kernels, and the
+scored CE sum uses the fused log-softmax kernel in "sum" mode (no [tokens, vocab]
+fp32 logits copy).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .config import DiPaCoConfig
+from .models.path import PathModel, build_path_model
+from .routing.base import Featurizer, Router
+from .topology import Path
+
+
+def compose_path(config: DiPaCoConfig, bank: dict[str, nn.Module], path: Path) -> PathModel:
+    return build_path_model(config, path, bank, deepcopy=False)
+
+
+def route(prefixes: list[torch.Tensor], router: Router, featurizer: Featurizer) -> torch.Tensor:
+    return router.predict(featurizer(prefixes))
+
+
+def _ce_sum(pred: torch.Tensor, tgt: torch.Tensor) -> float:
+    if pred.is_cuda:
+        from .ops import loss as L
+
+        return float(L.cross_entropy_sum(pred.reshape(-1, pred.size(-1)), tgt.reshape(-1)))
+    return float(F.cross_entropy(pred.reshape(-1, pred.size(-1)), tgt.reshape(-1), reduction="sum"))
+
+
+@torch.no_grad()
+def perplexity(model: PathModel, sequences: torch.Tensor, batch_size: int = 8) -> float:
+    model.eval()
+    dev = next(model.parameters()).device
+    total, n = 0.0, 0
+    for i in range(0, sequences.size(0), batch_size):
+        batch = sequences[i:i + batch_size].to(dev)
+        _, loss = model(batch, labels=batch)
+        total += float(loss)
+        n += 1
+    return float("nan") if n == 0 else float(torch.exp(torch.tensor(total / n)))
+
+
+def config_path(config: DiPaCoConfig, path_index: int) -> Path:
+    return config.build_topology().path_from_index(path_index)
+
+
+@torch.no_grad()
+def routed_perplexity(config: DiPaCoConfig, bank: dict[str, nn.Module], sequences: torch.Tensor,
+                      router: Router, featurizer: Featurizer, prefix_len: int = 32,
+                      batch_size: int = 8, compose_fn=None) -> float:
+    paths = route([s[:prefix_len] for s in sequences], router, featurizer)
+    start = max(prefix_len, 1)
+    total, count = 0.0, 0
+    for pidx in paths.unique().tolist():
+        path = config_path(config, pidx)
+        model = compose_fn(path) if compose_fn is not None else compose_path(config, bank, path)
+        dev = next(model.parameters()).device
+        seqs = sequences[paths == pidx]
+        for i in range(0, seqs.size(0), batch_size):
+            batch = seqs[i:i + batch_size].to(dev)
+            if batch.size(1) <= start:
+                continue
+            logits, _ = model(batch)
+            total += _ce_sum(logits[:, start - 1:-1, :], batch[:, start:])
+            count += batch[:, start:].numel()
+    return float("nan") if count == 0 else float(torch.exp(torch.tensor(total / count)))
+
+
+@torch.no_grad()
+def routed_window_perplexity(config: DiPaCoConfig, bank: dict[str, nn.Module],
+                             sequences: torch.Tensor, router: Router, featurizer: Featurizer,
+                             window: int = 64, batch_size: int = 8, compose_fn=None,
+                             prefix_len: int = 32) -> float:
+    if sequences.numel() == 0:
+        return float("nan")
+    dev = next(next(iter(bank.values())).parameters()).device
+    topo = config.build_topology()
+    nseq, slen = sequences.shape
+    models: dict[int, PathModel] = {}
+    total, count = 0.0, 0
+    for w in range(math.ceil(slen / window)):
+        w0, w1 = w * window, min((w + 1) * window, slen)
+        t0 = max(w0, prefix_len, 1)
+        if t0 >= w1:
+            continue
+        rc = w - 1 if w > 0 else 0
+        paths = route([sequences[n, rc * window:min((rc + 1) * window, slen)] for n in range(nseq)],
+                      router, featurizer)
+        for pidx in paths.unique().tolist():
+            rows = (paths == pidx).nonzero(as_tuple=True)[0]
+            model = models.get(pidx)
+            if model is None:
+                p = topo.path_from_index(pidx)
+                model = (compose_fn(p) if compose_fn is not None else compose_path(config, bank, p)).eval()
+                models[pidx] = model
+            for s in range(0, rows.numel(), batch_size):
+                batch = sequences[rows[s:s + batch_size], :w1].to(dev)
+                logits, _ = model(batch)
+                total += _ce_sum(logits[:, t0 - 1:w1 - 1, :], batch[:, t0:w1])
+                count += batch[:, t0:w1].numel()
+    return float("nan") if count == 0 else float(torch.exp(torch.tensor(total / count)))

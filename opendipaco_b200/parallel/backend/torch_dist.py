@@ -1,0 +1,73 @@
+"""NCCL / gloo backend over ``torch.distributed`` subgroups (the baseline).
+
+Reference ``src/opendipaco/backend/torch_dist.py:24-77``: one process group per
+module key (built in the same order on every rank), ``all_reduce(SUM)`` of every
+tensor of the key's summed delta plus a 1-element weight. Differences here:
+
+* placement accepts any ``num_paths >= world`` (balanced contiguous blocks);
+* the per-key tensors are flattened into ONE buffer before the all-reduce (one
+  NCCL call per key instead of one per parameter), and the weight rides in the
+  same buffer, so there is no extra scalar collective and no ``.item()`` per key
+  beyond the final one.
+
+The device outer step of the B200 engine does not go through this class; it is
+the NCCL baseline the fused NVLink kernel is compared against.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ...topology import Path, PathTopology
+from ..placement import path_ranks, rank_paths
+from .base import ReducedDelta, SyncBackend
+
+
+class TorchDistBackend(SyncBackend):
+    def __init__(self, topology: PathTopology, device: torch.device | None = None):
+        if not dist.is_initialized():
+            raise RuntimeError("torch.distributed is not initialized; call "
+                               "dist.init_process_group first")
+        self.topology = topology
+        self.world_size = dist.get_world_size()
+        self.rank = dist.get_rank()
+        self._ranks = path_ranks(topology.num_paths, self.world_size)
+        self._paths = [topology.path_from_index(i)
+                       for i in rank_paths(topology.num_paths, self.world_size, self.rank)]
+        if device is None:
+            device = (torch.device(f"cuda:{self.rank % torch.cuda.device_count()}")
+                      if torch.cuda.is_available() else torch.device("cpu"))
+        self.device = torch.device(device)
+        self._groups: dict[str, object] = {}
+        self._member: dict[str, bool] = {}
+        for key in topology.module_keys():
+            ranks = self.sharing_ranks(key)
+            self._groups[key] = dist.new_group(ranks=ranks)
+            self._member[key] = self.rank in ranks
+
+    def rank_of_path(self, path: Path) -> int:
+        return self._ranks[self.topology.path_index(path)]
+
+    def owned_paths(self) -> list[Path]:
+        return list(self._paths)
+
+    def owns_module(self, key: str) -> bool:
+        return self._member.get(key, False)
+
+    def process_group(self, key: str):
+        return self._groups[key]
+
+    def global_reduce(self, key: str, local: ReducedDelta) -> ReducedDelta:
+        ts = [t.to(self.device) for t in local.summed]
+        flat = torch.cat([t.reshape(-1).float() for t in ts]
+                         + [torch.tensor([local.weight], device=self.device, dtype=torch.float32)])
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self._groups[key])
+        out, off = [], 0
+        for t in ts:
+            out.append(flat[off:off + t.numel()].view_as(t).to(t.dtype))
+            off += t.numel()
+        return ReducedDelta(summed=out, weight=float(flat[-1].item()))
+
+    def barrier(self) -> None:
+        dist.barrier()
