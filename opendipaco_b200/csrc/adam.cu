@@ -1,0 +1,240 @@
+// Inner-optimizer kernels over flat per-path buffers [G][P] (fp32).
+//
+// grad_clip: deterministic global-norm clip per path. Stage 1 writes per-block sums of
+// squares; stage 2 sums them in a fixed order and stores
+//     coef[g] = min(1, max_norm / (sqrt(sum) + 1e-6))
+// (torch.nn.utils.clip_grad_norm_ semantics), which the update kernel folds into the
+// gradient, so no extra pass over the gradients is spent on scaling.
+//
+// adamw: decoupled weight decay, bias-corrected moments, eps outside the sqrt
+// (torch.optim.AdamW). Per-step scalars (lr, lr / (1 - b1^t), sqrt(1 - b2^t)) are read
+// from a device array so a whole round of steps can live in one CUDA graph. Writes the
+// fp32 master weight and its bf16 working copy for the GEMMs in the same pass.
+//
+// adam8bit: blockwise 8-bit AdamW (blocks of 256): one warp per block dequantises m
+// (int8, absmax / 127) and v (uint8 in the log domain: exp(q * scale + lo), floor
+// 1e-20), updates in fp32 registers, requantises (round half to even) and updates the
+// parameter from the unquantised moments -- a single pass over the state.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace odp {
+
+constexpr int kSqBlock = 256;
+constexpr int kSqElemsPerBlock = 1 << 16;
+
+__global__ void sumsq_kernel(const float* __restrict__ g, long long P, long long sg, int nblk, float* __restrict__ part) {
+  const int grp = blockIdx.y, b = blockIdx.x;
+  const float* base = g + grp * sg;
+  const long long e0 = (long long)b * kSqElemsPerBlock;
+  const long long e1 = min(e0 + kSqElemsPerBlock, P);
+  float s = 0.f;
+  for (long long i = e0 + threadIdx.x * 4; i < e1; i += kSqBlock * 4) {
+    if (i + 4 <= e1) {
+      float4 v = *reinterpret_cast<const float4*>(base + i);
+      s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    } else {
+      for (long long j = i; j < e1; ++j) s += base[j] * base[j];
+    }
+  }
+  __shared__ float red[kSqBlock / 32];
+  s = warp_sum(s);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < kSqBlock / 32; ++w) t += red[w];
+    part[(long long)grp * nblk + b] = t;
+  }
+}
+
+__global__ void clip_coef_kernel(const float* __restrict__ part, int nblk, float max_norm, float* __restrict__ coef,
+                                 float* __restrict__ norm_out) {
+  const int grp = blockIdx.x;
+  __shared__ float red[256];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < nblk; i += blockDim.x) s += part[(long long)grp * nblk + i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float n = sqrtf(red[0]);
+    if (norm_out) norm_out[grp] = n;
+    coef[grp] = max_norm > 0.f ? fminf(1.f, max_norm / (n + 1e-6f)) : 1.f;
+  }
+}
+
+// sched: [lr, step_size = lr / bc1, bc2_sqrt]
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, __nv_bfloat16* __restrict__ p16, long long P, long long sp,
+                             long long s16, const float* __restrict__ coef, const float* __restrict__ sched, float b1,
+                             float b2, float eps, float wd) {
+  const int grp = blockIdx.y;
+  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i >= P) return;
+  const float lr = sched[0], step_size = sched[1], bc2s = sched[2];
+  const float cf = coef ? coef[grp] : 1.f;
+  const float decay = 1.f - lr * wd;
+  const long long o = grp * sp + i;
+  const int n = (int)min((long long)4, P - i);
+  float pv[4], gv[4], mv[4], vv[4];
+  if (n == 4) {
+    *reinterpret_cast<float4*>(pv) = *reinterpret_cast<const float4*>(p + o);
+    *reinterpret_cast<float4*>(gv) = *reinterpret_cast<const float4*>(g + o);
+    *reinterpret_cast<float4*>(mv) = *reinterpret_cast<const float4*>(m + o);
+    *reinterpret_cast<float4*>(vv) = *reinterpret_cast<const float4*>(v + o);
+  } else {
+    for (int k = 0; k < 4; ++k) {
+      pv[k] = k < n ? p[o + k] : 0.f;
+      gv[k] = k < n ? g[o + k] : 0.f;
+      mv[k] = k < n ? m[o + k] : 0.f;
+      vv[k] = k < n ? v[o + k] : 0.f;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float gr = gv[k] * cf;
+    pv[k] *= decay;
+    mv[k] = mv[k] + (1.f - b1) * (gr - mv[k]);
+    vv[k] = vv[k] * b2 + (1.f - b2) * gr * gr;
+    const float den = sqrtf(vv[k]) / bc2s + eps;
+    pv[k] = pv[k] - step_size * (mv[k] / den);
+  }
+  if (n == 4) {
+    *reinterpret_cast<float4*>(p + o) = *reinterpret_cast<float4*>(pv);
+    *reinterpret_cast<float4*>(m + o) = *reinterpret_cast<float4*>(mv);
+    *reinterpret_cast<float4*>(v + o) = *reinterpret_cast<float4*>(vv);
+    uint2 w = make_uint2(pack_bf16(pv[0], pv[1]), pack_bf16(pv[2], pv[3]));
+    *reinterpret_cast<uint2*>(p16 + grp * s16 + i) = w;
+  } else {
+    for (int k = 0; k < n; ++k) {
+      p[o + k] = pv[k];
+      m[o + k] = mv[k];
+      v[o + k] = vv[k];
+      p16[grp * s16 + i + k] = __float2bfloat16(pv[k]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- 8-bit Adam
+// One warp per 256-element block (8 consecutive elements per lane).
+__global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__ g, long long n, int8_t* __restrict__ mq,
+                                float* __restrict__ mabs, uint8_t* __restrict__ vq, float* __restrict__ vlo,
+                                float* __restrict__ vsc, long long nblocks, long long blocks_per_group,
+                                const float* __restrict__ coef,
+                                const float* __restrict__ sched, float b1, float b2, float eps, float wd, int first,
+                                __nv_bfloat16* __restrict__ p16) {
+  const long long blk = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (blk >= nblocks) return;
+  const float lr = sched[0], step_size = sched[1], bc2s = sched[2];
+  const float cf = coef ? coef[blocks_per_group > 0 ? blk / blocks_per_group : 0] : 1.f;
+  const long long e0 = blk * 256 + lane * 8;
+  const float mscale = mabs[blk] / 127.f;
+  const float lo = vlo[blk], sc = vsc[blk];
+  float mv[8], vv[8], gv[8];
+  const int8_t* mqp = mq + e0;
+  const uint8_t* vqp = vq + e0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const long long e = e0 + k;
+    gv[k] = e < n ? g[e] * cf : 0.f;
+    mv[k] = (float)mqp[k] * mscale;
+    vv[k] = first ? 0.f : __expf((float)vqp[k] * sc + lo);
+    mv[k] = mv[k] * b1 + (1.f - b1) * gv[k];
+    vv[k] = vv[k] * b2 + (1.f - b2) * gv[k] * gv[k];
+  }
+  // requantise m: symmetric absmax
+  float amax = 0.f, lmin = INFINITY, lmax = -INFINITY;
+  float lv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    amax = fmaxf(amax, fabsf(mv[k]));
+    lv[k] = __logf(fmaxf(vv[k], 1e-20f));
+    lmin = fminf(lmin, lv[k]);
+    lmax = fmaxf(lmax, lv[k]);
+  }
+  amax = warp_max(amax);
+  lmax = warp_max(lmax);
+  lmin = -warp_max(-lmin);
+  const float qs = amax > 0.f ? amax / 127.f : 1.f;
+  const float vs = fmaxf((lmax - lmin) / 255.f, 1e-12f);
+  int8_t* mqo = mq + e0;
+  uint8_t* vqo = vq + e0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    mqo[k] = (int8_t)fminf(fmaxf(rintf(mv[k] / qs), -127.f), 127.f);
+    vqo[k] = (uint8_t)fminf(fmaxf(rintf((lv[k] - lmin) / vs), 0.f), 255.f);
+  }
+  if (lane == 0) {
+    mabs[blk] = amax;
+    vlo[blk] = lmin;
+    vsc[blk] = vs;
+  }
+  const float decay = 1.f - lr * wd;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const long long e = e0 + k;
+    if (e >= n) break;
+    const float den = sqrtf(vv[k]) / bc2s + eps;
+    const float nv = p[e] * decay - step_size * (mv[k] / den);
+    p[e] = nv;
+    if (p16) p16[e] = __float2bfloat16(nv);
+  }
+}
+
+}  // namespace odp
+
+void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, double max_norm, torch::Tensor work,
+                    torch::Tensor coef, c10::optional<torch::Tensor> norm_out) {
+  c10::cuda::CUDAGuard guard(grads.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int nblk = (int)((P + odp::kSqElemsPerBlock - 1) / odp::kSqElemsPerBlock);
+  TORCH_CHECK(work.numel() >= G * nblk, "grad_clip_coef: work buffer too small");
+  odp::sumsq_kernel<<<dim3(nblk, (unsigned)G), odp::kSqBlock, 0, st>>>(grads.data_ptr<float>(), P, sg, nblk,
+                                                                      work.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  odp::clip_coef_kernel<<<(unsigned)G, 256, 0, st>>>(work.data_ptr<float>(), nblk, (float)max_norm,
+                                                      coef.data_ptr<float>(),
+                                                      norm_out.has_value() ? norm_out->data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor p16, int64_t P,
+                int64_t sp, int64_t s16, int64_t G, c10::optional<torch::Tensor> coef, torch::Tensor sched, double b1,
+                double b2, double eps, double wd) {
+  c10::cuda::CUDAGuard guard(p.device());
+  TORCH_CHECK(P % 4 == 0 || G == 1, "adamw_step: per-group length must be a multiple of 4");
+  const long long threads = (P + 3) / 4;
+  dim3 grid((unsigned)((threads + 255) / 256), (unsigned)G);
+  odp::adamw_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), P, sp, s16,
+      coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
+      (float)eps, (float)wd);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void adam8bit_step(torch::Tensor p, torch::Tensor g, torch::Tensor mq, torch::Tensor mabs, torch::Tensor vq,
+                   torch::Tensor vlo, torch::Tensor vsc, c10::optional<torch::Tensor> coef, torch::Tensor sched,
+                   double b1, double b2, double eps, double wd, bool first, c10::optional<torch::Tensor> p16,
+                   int64_t blocks_per_group) {
+  c10::cuda::CUDAGuard guard(p.device());
+  const long long n = p.numel(), nb = mabs.numel();
+  TORCH_CHECK(mq.numel() == nb * 256 && vq.numel() == nb * 256, "adam8bit_step: state must be [nblocks, 256]");
+  TORCH_CHECK(nb * 256 >= n, "adam8bit_step: too few blocks");
+  const long long threads = nb * 32;
+  odp::adam8bit_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p.data_ptr<float>(), g.data_ptr<float>(), n, mq.data_ptr<int8_t>(), mabs.data_ptr<float>(),
+      vq.data_ptr<uint8_t>(), vlo.data_ptr<float>(), vsc.data_ptr<float>(), nb, blocks_per_group,
+      coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
+      (float)eps, (float)wd, first ? 1 : 0,
+      p16.has_value() ? reinterpret_cast<__nv_bfloat16*>(p16->data_ptr()) : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -1,0 +1,59 @@
+// Python bindings of the sm_100a kernels (module opendipaco_b200._C).
+#include <torch/extension.h>
+
+void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tensor B, int64_t ldb, int64_t sb,
+               bool b_mn, torch::Tensor C, int64_t ldc, int64_t sc, int64_t M, int64_t N, int64_t K, int64_t G,
+               int64_t epi, int64_t bn, c10::optional<torch::Tensor> R, int64_t ldr, int64_t sr,
+               c10::optional<torch::Tensor> aux, int64_t ldx, int64_t sx, c10::optional<torch::Tensor> part,
+               double beta, int64_t f_half, torch::Tensor err, int64_t max_ctas);
+void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor y, int64_t sy,
+                 torch::Tensor rstd, int64_t M, int64_t H, int64_t G, double eps);
+void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor rstd, torch::Tensor dy,
+                 int64_t sdy, c10::optional<torch::Tensor> dres, torch::Tensor dx, int64_t sdx, torch::Tensor dw,
+                 int64_t sdw, torch::Tensor work, int64_t M, int64_t H, int64_t G, double beta);
+void embedding_fwd(torch::Tensor ids, torch::Tensor E, int64_t se, torch::Tensor out, int64_t M, int64_t H,
+                   int64_t G, int64_t V);
+void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
+                   int64_t H, int64_t G, int64_t V);
+void attention_fwd(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                   torch::Tensor sinT, torch::Tensor o, torch::Tensor lse);
+void attention_bwd(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                   torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout, torch::Tensor delta,
+                   torch::Tensor dqkv);
+void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels,
+                int64_t M, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum,
+                torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out);
+void ce_backward(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor lse, torch::Tensor labels,
+                 torch::Tensor inv_count, int64_t M, int64_t V, int64_t G);
+torch::Tensor cross_entropy_rows(torch::Tensor logits, torch::Tensor target);
+void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, double max_norm, torch::Tensor work,
+                    torch::Tensor coef, c10::optional<torch::Tensor> norm_out);
+void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor p16, int64_t P,
+                int64_t sp, int64_t s16, int64_t G, c10::optional<torch::Tensor> coef, torch::Tensor sched, double b1,
+                double b2, double eps, double wd);
+void adam8bit_step(torch::Tensor p, torch::Tensor g, torch::Tensor mq, torch::Tensor mabs, torch::Tensor vq,
+                   torch::Tensor vlo, torch::Tensor vsc, c10::optional<torch::Tensor> coef, torch::Tensor sched,
+                   double b1, double b2, double eps, double wd, bool first, c10::optional<torch::Tensor> p16,
+                   int64_t blocks_per_group);
+void outer_step(torch::Tensor segs, int64_t nseg, torch::Tensor locals, int64_t total_chunks, double lr,
+                double momentum, bool nesterov, bool first, c10::optional<torch::Tensor> sq_part);
+int64_t outer_chunk_elems();
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "opendipaco_b200 sm_100a kernels";
+  m.def("gemm_bf16", &gemm_bf16);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
+  m.def("ce_forward", &ce_forward);
+  m.def("ce_backward", &ce_backward);
+  m.def("cross_entropy_rows", &cross_entropy_rows);
+  m.def("grad_clip_coef", &grad_clip_coef);
+  m.def("adamw_step", &adamw_step);
+  m.def("adam8bit_step", &adam8bit_step);
+  m.def("outer_step", &outer_step);
+  m.def("outer_chunk_elems", &outer_chunk_elems);
+}

@@ -1,0 +1,511 @@
+// Persistent warp-specialized tcgen05 GEMM for sm_100a, batched over G groups:
+//
+//     C[g] (M x N) = A[g] (M x K) . B[g] (N x K)^T        (fp32 accumulate in TMEM)
+//
+// Operands are bf16, staged by TMA (128-byte swizzle) from THIS GPU's memory only.
+// Each operand may be K-major (reduction dim contiguous) or MN-major (row dim
+// contiguous), so a Linear's forward (X W^T), input gradient (dY W) and weight
+// gradient (dY^T X) all map onto this one kernel without transposed copies.
+//
+// CTA = 6 warps: warp 0 issues TMA loads into an S-stage ring, warp 1 owns TMEM
+// and issues tcgen05.mma from one thread (128 x BN x 16 per instruction), warps 2-5
+// drain a double-buffered TMEM accumulator (2 x BN fp32 columns) through a fused
+// epilogue while the next tile's MMAs run. Tiles are distributed round-robin over a
+// persistent grid of one CTA per SM.
+//
+// Epilogues (template EPI):
+//   EPI_BF16     C = bf16(acc)
+//   EPI_F32      C = acc + beta * C                         (fp32)
+//   EPI_RESID    C = R + acc                                (fp32 residual stream)
+//   EPI_SWIGLU   B tile = [gate rows | up rows] of one 64-feature block;
+//                H = bf16(silu(bf16 g) * bf16 u), GU aux = bf16 g, u
+//   EPI_SWIGLU_BWD  acc = dH; reads g,u; writes dG, dU (bf16) into C = [dG | dU]
+//   EPI_LOGITS   C = bf16(acc) and per-row (max, sum exp) of the rounded tile values
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace odp {
+
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_SWIGLU_BWD = 4, EPI_LOGITS = 5 };
+
+struct GemmParams {
+  int M, N, K, G;
+  int tiles_m, tiles_n, num_tiles, num_kb;
+  void* C;
+  long long ldc, sc;
+  const float* R;
+  long long ldr, sr;
+  void* aux;  // swiglu: pre-activation [M, 2F] bf16 ([g | u]); bwd: same layout as input
+  long long ldx, sx;
+  float* part;  // logits: [G][M][tiles_n] float2
+  float beta;
+  int f_half;  // swiglu: F (rows of the gate block; up block starts at row F)
+  int* err;
+};
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct SmemLayout {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
+};
+
+ODP_DEVICE float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN, int EPI>
+ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int lane, int g, int tm, int tn) {
+  const int row = q * 32 + lane;
+  const long long grow = (long long)tm * BM + row;
+  const bool row_ok = grow < p.M;
+  const uint32_t tbase = tmem_acc + ((uint32_t)(q * 32) << 16);
+
+  if constexpr (EPI == EPI_SWIGLU) {
+    // accumulator columns [0, BN/2) = gate feature block, [BN/2, BN) = up feature block
+    constexpr int HALF = BN / 2;
+    const int f0 = tn * HALF;
+#pragma unroll 1
+    for (int c = 0; c < HALF; c += 16) {
+      float a[16], b[16];
+      tmem_ld16(tbase + c, a);
+      tmem_ld16(tbase + HALF + c, b);
+      if (!row_ok || f0 + c >= p.f_half) continue;
+      __nv_bfloat16* H = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + f0 + c;
+      __nv_bfloat16* GU = reinterpret_cast<__nv_bfloat16*>(p.aux) + g * p.sx + grow * p.ldx + f0 + c;
+      uint32_t hv[8], gv[8], uv[8];
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        float g0 = bf16_round(a[i]), g1 = bf16_round(a[i + 1]);
+        float u0 = bf16_round(b[i]), u1 = bf16_round(b[i + 1]);
+        float s0 = bf16_round(silu_f(g0)), s1 = bf16_round(silu_f(g1));
+        hv[i / 2] = pack_bf16(s0 * u0, s1 * u1);
+        gv[i / 2] = pack_bf16(g0, g1);
+        uv[i / 2] = pack_bf16(u0, u1);
+      }
+      uint4* hp = reinterpret_cast<uint4*>(H);
+      hp[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      hp[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+      uint4* gp = reinterpret_cast<uint4*>(GU);
+      gp[0] = make_uint4(gv[0], gv[1], gv[2], gv[3]);
+      gp[1] = make_uint4(gv[4], gv[5], gv[6], gv[7]);
+      uint4* up = reinterpret_cast<uint4*>(GU + p.f_half);
+      up[0] = make_uint4(uv[0], uv[1], uv[2], uv[3]);
+      up[1] = make_uint4(uv[4], uv[5], uv[6], uv[7]);
+    }
+    return;
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      tmem_ld16(tbase + c, v);
+      const int gcol = tn * BN + c;
+      if (!row_ok || gcol >= p.N) continue;
+      const bool full = gcol + 16 <= p.N;
+      if constexpr (EPI == EPI_BF16 || EPI == EPI_LOGITS) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
+        if (full) {
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) w[i / 2] = pack_bf16(v[i], v[i + 1]);
+          uint4* d4 = reinterpret_cast<uint4*>(dst);
+          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        } else {
+          for (int i = 0; i < 16 && gcol + i < p.N; ++i) dst[i] = __float2bfloat16(v[i]);
+        }
+      } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+        // acc = dH (gradient of silu(g) * u); aux = saved [g | u]; C = [dG | dU]
+        const __nv_bfloat16* gsrc = reinterpret_cast<const __nv_bfloat16*>(p.aux) + g * p.sx + grow * p.ldx + gcol;
+        const __nv_bfloat16* usrc = gsrc + p.f_half;
+        __nv_bfloat16* dg = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
+        __nv_bfloat16* du = dg + p.f_half;
+        for (int i = 0; i < 16; ++i) {
+          if (!full && gcol + i >= p.N) break;
+          const float gv = __bfloat162float(gsrc[i]), uv = __bfloat162float(usrc[i]);
+          const float dh = bf16_round(v[i]);
+          const float sg = 1.0f / (1.0f + __expf(-gv));
+          const float act = bf16_round(gv * sg);
+          du[i] = __float2bfloat16(dh * act);
+          const float da = bf16_round(dh * uv);
+          dg[i] = __float2bfloat16(da * sg * (1.0f + gv * (1.0f - sg)));
+        }
+      } else if constexpr (EPI == EPI_F32 || EPI == EPI_RESID) {
+        float* dst = reinterpret_cast<float*>(p.C) + g * p.sc + grow * p.ldc + gcol;
+        const float* rs = nullptr;
+        if constexpr (EPI == EPI_RESID) rs = p.R + g * p.sr + grow * p.ldr + gcol;
+        for (int i = 0; i < 16; ++i) {
+          if (!full && gcol + i >= p.N) break;
+          float x = v[i];
+          if constexpr (EPI == EPI_RESID) x += rs[i];
+          else if (p.beta != 0.f) x += p.beta * dst[i];
+          dst[i] = x;
+        }
+      }
+    }
+  }
+}
+
+// Logits epilogue: bf16 store + per-row (max, sum exp) over this tile's valid columns.
+template <int BN>
+ODP_DEVICE void epilogue_logits(const GemmParams& p, uint32_t tmem_acc, int q, int lane, int g, int tm, int tn) {
+  const int row = q * 32 + lane;
+  const long long grow = (long long)tm * BM + row;
+  const bool row_ok = grow < p.M;
+  const uint32_t tbase = tmem_acc + ((uint32_t)(q * 32) << 16);
+  float mx = -INFINITY, se = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 16) {
+    float v[16];
+    tmem_ld16(tbase + c, v);
+    const int gcol = tn * BN + c;
+    if (!row_ok || gcol >= p.N) continue;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
+    const int n = min(16, p.N - gcol);
+    float r[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = bf16_round(v[i]);
+    if (n == 16) {
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) w[i / 2] = pack_bf16(r[i], r[i + 1]);
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      for (int i = 0; i < n; ++i) dst[i] = __float2bfloat16(r[i]);
+    }
+    float cm = -INFINITY;
+    for (int i = 0; i < n; ++i) cm = fmaxf(cm, r[i]);
+    if (cm > mx) {
+      se *= __expf(mx - cm);
+      mx = cm;
+    }
+    for (int i = 0; i < n; ++i) se += __expf(r[i] - mx);
+  }
+  if (row_ok) {
+    float2* pp = reinterpret_cast<float2*>(p.part) + ((long long)g * p.M + grow) * p.tiles_n + tn;
+    *pp = make_float2(mx, se);
+  }
+}
+
+template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  using L = SmemLayout<BN, STAGES>;
+  constexpr bool SPLIT_B = (EPI == EPI_SWIGLU);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accfull = empty + STAGES;
+  uint64_t* accempty = accfull + 2;
+  uint64_t* drain = accempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int tiles_per_g = p.tiles_m * p.tiles_n;
+  constexpr uint32_t kIdesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      const int g = t / tiles_per_g, r = t % tiles_per_g;
+      const int tm = r / p.tiles_n, tn = r % p.tiles_n;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, ERR_TIMEOUT_EMPTY)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* sA = smem + stage * L::STAGE_BYTES;
+          uint8_t* sB = sA + L::A_BYTES;
+          mbar_expect_tx(&full[stage], L::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_3d(&tmA, &full[stage], sA, k0, tm * BM, g);
+          } else {
+            tma_load_3d(&tmA, &full[stage], sA, tm * BM, k0, g);
+            tma_load_3d(&tmA, &full[stage], sA + 8192, tm * BM + 64, k0, g);
+          }
+          if constexpr (SPLIT_B) {
+            tma_load_3d(&tmB, &full[stage], sB, k0, tn * (BN / 2), g);
+            tma_load_3d(&tmB, &full[stage], sB + (BN / 2) * 128, k0, p.f_half + tn * (BN / 2), g);
+          } else if constexpr (!B_MN) {
+            tma_load_3d(&tmB, &full[stage], sB, k0, tn * BN, g);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(&tmB, &full[stage], sB + j * 8192, tn * BN + j * 64, k0, g);
+          }
+        }
+        __syncwarp();
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    // drain: every issued stage's bytes must have landed before the CTA exits
+    long long n_wait = issued < STAGES ? issued : STAGES;
+    int s = stage;
+    uint32_t ph = phase;
+    for (long long i = 0; i < n_wait; ++i) {
+      if (--s < 0) {
+        s = STAGES - 1;
+        ph ^= 1;
+      }
+      mbar_wait(&full[s], ph, p.err, ERR_TIMEOUT_FULL);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t accphase = 0;
+    bool ok = true, any = false;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      if (!mbar_wait(&accempty[acc], accphase ^ 1, p.err, ERR_TIMEOUT_TMEM_FREE)) break;
+      tc_fence_after();
+      const uint32_t dtm = tmem_base + acc * BN;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&full[stage], phase, p.err, ERR_TIMEOUT_FULL)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t aaddr = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t baddr = aaddr + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t ad, bd;
+            if constexpr (!A_MN) ad = umma_smem_desc(aaddr + kk * 32, 16, 1024, kLayoutSW128);
+            else ad = umma_smem_desc(aaddr + kk * 2048, 8192, 1024, kLayoutSW128);
+            if constexpr (!B_MN) bd = umma_smem_desc(baddr + kk * 32, 16, 1024, kLayoutSW128);
+            else bd = umma_smem_desc(baddr + kk * 2048, 8192, 1024, kLayoutSW128);
+            umma_bf16(dtm, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          any = true;
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&accfull[acc]);
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) accphase ^= 1;
+    }
+    // drain: all issued MMAs complete before TMEM is released
+    if (lane == 0 && any) {
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, ERR_TIMEOUT_ACCUM);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp % 4;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t accphase = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      if (!mbar_wait(&accfull[acc], accphase, p.err, ERR_TIMEOUT_ACCUM)) break;
+      tc_fence_after();
+      const int g = t / tiles_per_g, r = t % tiles_per_g;
+      const int tm = r / p.tiles_n, tn = r % p.tiles_n;
+      const uint32_t tacc = tmem_base + acc * BN;
+      if constexpr (EPI == EPI_LOGITS) epilogue_logits<BN>(p, tacc, q, lane, g, tm, tn);
+      else epilogue_tile<BN, EPI>(p, tacc, q, lane, g, tm, tn);
+      tc_fence_before();
+      mbar_arrive(&accempty[acc]);
+      acc ^= 1;
+      if (acc == 0) accphase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
+}
+
+// ============================================================== host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && ptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// bf16 3-D map: x = contiguous dim (extent inner), y = rows (extent outer, stride ld),
+// z = group (extent G, stride sg). Box = {64, box_rows, 1}, 128-byte swizzle.
+static CUtensorMap make_map(const void* base, long long inner, long long outer, long long ld, int G,
+                            long long sg, int box_rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "row stride must be a multiple of 16 bytes");
+  TORCH_CHECK(G == 1 || (sg * 2) % 16 == 0, "group stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)G};
+  long long gstride = G > 1 ? sg * 2 : ((outer * ld * 2 + 15) / 16) * 16;
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)gstride};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
+static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams& p, cudaStream_t st, int max_ctas) {
+  using L = SmemLayout<BN, STAGES>;
+  auto kern = gemm_kernel<A_MN, B_MN, BN, STAGES, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    attr_set = true;
+  }
+  int grid = std::min(p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
+  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Operand description: data pointer, leading dim (elements), group stride (elements).
+struct Operand {
+  const void* ptr;
+  long long ld, sg;
+  bool mn;  // true: stored [K, rows] (rows contiguous); false: stored [rows, K]
+};
+
+template <int EPI>
+static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, cudaStream_t st, int max_ctas) {
+  const int rowsB = EPI == EPI_SWIGLU ? bn / 2 : bn;
+  CUtensorMap ma = A.mn ? make_map(A.ptr, p.M, p.K, A.ld, p.G, A.sg, 64) : make_map(A.ptr, p.K, p.M, A.ld, p.G, A.sg, BM);
+  long long b_rows_extent = EPI == EPI_SWIGLU ? 2LL * p.f_half : p.N;
+  CUtensorMap mb = B.mn ? make_map(B.ptr, p.N, p.K, B.ld, p.G, B.sg, 64)
+                        : make_map(B.ptr, p.K, b_rows_extent, B.ld, p.G, B.sg, rowsB);
+#define ODP_GO(AM, BMN, BNV, ST)                                        \
+  if (A.mn == AM && B.mn == BMN && bn == BNV) {                         \
+    launch_t<AM, BMN, BNV, ST, EPI>(ma, mb, p, st, max_ctas);           \
+    return;                                                             \
+  }
+  ODP_GO(false, false, 128, 6)
+  ODP_GO(false, true, 128, 6)
+  ODP_GO(true, false, 128, 6)
+  ODP_GO(true, true, 128, 6)
+  ODP_GO(false, false, 64, 8)
+  ODP_GO(false, true, 64, 8)
+  ODP_GO(true, false, 64, 8)
+  ODP_GO(true, true, 64, 8)
+  ODP_GO(false, false, 256, 4)
+#undef ODP_GO
+  TORCH_CHECK(false, "unsupported GEMM configuration");
+}
+
+}  // namespace odp
+
+// ---------------------------------------------------------------- torch entry
+// A: tensor whose storage holds G groups; a_mn selects its major; shapes are given
+// explicitly so callers can pass views into flat parameter buffers.
+void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tensor B, int64_t ldb, int64_t sb,
+               bool b_mn, torch::Tensor C, int64_t ldc, int64_t sc, int64_t M, int64_t N, int64_t K, int64_t G,
+               int64_t epi, int64_t bn, c10::optional<torch::Tensor> R, int64_t ldr, int64_t sr,
+               c10::optional<torch::Tensor> aux, int64_t ldx, int64_t sx, c10::optional<torch::Tensor> part,
+               double beta, int64_t f_half, torch::Tensor err, int64_t max_ctas) {
+  using namespace odp;
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
+  c10::cuda::CUDAGuard guard(A.device());
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.G = (int)G;
+  p.f_half = (int)f_half;
+  const int tile_n = (epi == EPI_SWIGLU) ? (int)bn / 2 : (int)bn;
+  p.tiles_m = (int)((M + BM - 1) / BM);
+  p.tiles_n = (int)(((epi == EPI_SWIGLU ? f_half : N) + tile_n - 1) / tile_n);
+  p.num_tiles = p.tiles_m * p.tiles_n * (int)G;
+  p.num_kb = (int)((K + BK - 1) / BK);
+  p.C = C.data_ptr();
+  p.ldc = ldc;
+  p.sc = sc;
+  p.R = R.has_value() ? R->data_ptr<float>() : nullptr;
+  p.ldr = ldr;
+  p.sr = sr;
+  p.aux = aux.has_value() ? aux->data_ptr() : nullptr;
+  p.ldx = ldx;
+  p.sx = sx;
+  p.part = part.has_value() ? part->data_ptr<float>() : nullptr;
+  p.beta = (float)beta;
+  p.err = err.data_ptr<int>();
+  Operand a{A.data_ptr(), lda, sa, a_mn}, b{B.data_ptr(), ldb, sb, b_mn};
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  switch (epi) {
+    case EPI_BF16: dispatch<EPI_BF16>(a, b, p, (int)bn, st, (int)max_ctas); break;
+    case EPI_F32: dispatch<EPI_F32>(a, b, p, (int)bn, st, (int)max_ctas); break;
+    case EPI_RESID: dispatch<EPI_RESID>(a, b, p, (int)bn, st, (int)max_ctas); break;
+    case EPI_SWIGLU: dispatch<EPI_SWIGLU>(a, b, p, (int)bn, st, (int)max_ctas); break;
+    case EPI_SWIGLU_BWD: dispatch<EPI_SWIGLU_BWD>(a, b, p, (int)bn, st, (int)max_ctas); break;
+    case EPI_LOGITS: dispatch<EPI_LOGITS>(a, b, p, (int)bn, st, (int)max_ctas); break;
+    default: TORCH_CHECK(false, "unknown epilogue ", epi);
+  }
+}

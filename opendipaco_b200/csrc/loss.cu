@@ -1,0 +1,182 @@
+// Cross-entropy over bf16 logits produced by the LM-head GEMM.
+//
+// The LM-head GEMM epilogue already wrote, for every row and every 128-column vocab
+// tile, the (max, sum exp) of the bf16-rounded logits. ce_finalize merges those
+// partials into the row log-sum-exp and the per-row loss lse - logit[target]
+// (ignore_index -100), then a fixed-order block reduction gives each path's loss sum
+// and valid-token count. ce_backward overwrites the logits in place with
+// dlogits = (softmax - onehot) / count (bf16), which the two backward GEMMs consume.
+//
+// cross_entropy_rows computes the same per-row loss straight from a logits tensor
+// (eval / EM scoring), one CTA per row.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace odp {
+
+__global__ void ce_finalize_kernel(const float2* __restrict__ part, int T, const __nv_bfloat16* __restrict__ logits,
+                                   long long ldl, long long sl, const int* __restrict__ labels, int M, int G,
+                                   float* __restrict__ lse, float* __restrict__ row_loss) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= G * M) return;
+  const float2* p = part + (long long)r * T;
+  float mx = -INFINITY;
+  for (int t = 0; t < T; ++t) mx = fmaxf(mx, p[t].x);
+  float s = 0.f;
+  for (int t = 0; t < T; ++t) s += p[t].y * __expf(p[t].x - mx);
+  const float l = mx + logf(s);
+  lse[r] = l;
+  const int y = labels[r];
+  const int g = r / M, m = r % M;
+  float loss = 0.f;
+  if (y >= 0) loss = l - __bfloat162float(logits[g * sl + (long long)m * ldl + y]);
+  row_loss[r] = loss;
+}
+
+// One block per group: loss_sum[g] = sum of row losses (fixed order), count[g] = valid rows.
+__global__ void group_sum_kernel(const float* __restrict__ row_loss, const int* __restrict__ labels, int M,
+                                 float* __restrict__ out_sum, float* __restrict__ out_inv_count,
+                                 float* __restrict__ out_loss) {
+  const int g = blockIdx.x;
+  __shared__ float ss[256];
+  __shared__ int sc[256];
+  float s = 0.f;
+  int c = 0;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) {
+    s += row_loss[(long long)g * M + i];
+    c += labels[(long long)g * M + i] >= 0;
+  }
+  ss[threadIdx.x] = s;
+  sc[threadIdx.x] = c;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) {
+      ss[threadIdx.x] += ss[threadIdx.x + o];
+      sc[threadIdx.x] += sc[threadIdx.x + o];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float cnt = (float)(sc[0] > 0 ? sc[0] : 1);
+    out_sum[g] = ss[0];
+    out_inv_count[g] = 1.f / cnt;
+    if (out_loss) out_loss[g] = ss[0] / cnt;
+  }
+}
+
+// In place: logits -> (softmax - onehot) * inv_count[g]; 8 bf16 per thread.
+__global__ void ce_backward_kernel(__nv_bfloat16* logits, long long ldl, long long sl, const float* __restrict__ lse,
+                                   const int* __restrict__ labels, const float* __restrict__ inv_count, int M, int V,
+                                   int G) {
+  const long long vec_per_row = V / 8;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)G * M * vec_per_row) return;
+  const long long r = idx / vec_per_row;
+  const int c0 = (int)(idx % vec_per_row) * 8;
+  const int g = (int)(r / M), m = (int)(r % M);
+  uint4* ptr = reinterpret_cast<uint4*>(logits + g * sl + (long long)m * ldl + c0);
+  const int y = labels[r];
+  if (y < 0) {
+    *ptr = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const float l = lse[r], sc = inv_count[g];
+  uint4 v = *ptr;
+  const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&v);
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    float p0 = __expf(__bfloat162float(x[e]) - l), p1 = __expf(__bfloat162float(x[e + 1]) - l);
+    if (c0 + e == y) p0 -= 1.f;
+    if (c0 + e + 1 == y) p1 -= 1.f;
+    o[e / 2] = pack_bf16(p0 * sc, p1 * sc);
+  }
+  *ptr = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Per-row CE (target < 0 -> 0) from bf16 or fp32 logits; one 256-thread CTA per row.
+template <typename T>
+__global__ void ce_rows_kernel(const T* __restrict__ logits, long long ld, const long long* __restrict__ tgt, int V,
+                               float* __restrict__ out) {
+  const long long r = blockIdx.x;
+  const T* x = logits + r * ld;
+  __shared__ float red[32];
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, (float)x[i]);
+  mx = warp_max(mx);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : -INFINITY;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) s += __expf((float)x[i] - mx);
+  s = warp_sum(s);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)blockDim.x / 32; ++w) t += red[w];
+    const long long y = tgt[r];
+    out[r] = y < 0 ? 0.f : (mx + logf(t) - (float)x[y]);
+  }
+}
+
+}  // namespace odp
+
+void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels,
+                int64_t M, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum,
+                torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out) {
+  c10::cuda::CUDAGuard guard(logits.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int R = (int)(G * M);
+  odp::ce_finalize_kernel<<<(R + 255) / 256, 256, 0, st>>>(
+      reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)T,
+      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)G,
+      lse.data_ptr<float>(), row_loss.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
+                                                 loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
+                                                 loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ce_backward(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor lse, torch::Tensor labels,
+                 torch::Tensor inv_count, int64_t M, int64_t V, int64_t G) {
+  TORCH_CHECK(V % 8 == 0 && ldl % 8 == 0, "ce_backward: vocab must be a multiple of 8");
+  c10::cuda::CUDAGuard guard(logits.device());
+  const long long n = G * M * (V / 8);
+  odp::ce_backward_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, lse.data_ptr<float>(), labels.data_ptr<int>(),
+      inv_count.data_ptr<float>(), (int)M, (int)V, (int)G);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+torch::Tensor cross_entropy_rows(torch::Tensor logits, torch::Tensor target) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "cross_entropy_rows: [R, V] row-major logits");
+  c10::cuda::CUDAGuard guard(logits.device());
+  auto tgt = target.to(torch::kLong).contiguous();
+  auto out = torch::empty({logits.size(0)}, logits.options().dtype(torch::kFloat));
+  if (logits.size(0) == 0) return out;
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (logits.scalar_type() == at::kBFloat16) {
+    odp::ce_rows_kernel<__nv_bfloat16><<<(unsigned)logits.size(0), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0), reinterpret_cast<const long long*>(tgt.data_ptr<int64_t>()),
+        (int)logits.size(1), out.data_ptr<float>());
+  } else {
+    TORCH_CHECK(logits.scalar_type() == at::kFloat, "cross_entropy_rows: bf16 or fp32 logits");
+    odp::ce_rows_kernel<float><<<(unsigned)logits.size(0), 256, 0, st>>>(
+        logits.data_ptr<float>(), logits.stride(0), reinterpret_cast<const long long*>(tgt.data_ptr<int64_t>()), (int)logits.size(1),
+        out.data_ptr<float>());
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}

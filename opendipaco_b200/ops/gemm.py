@@ -1,0 +1,67 @@
+"""tcgen05 GEMM entry points (``csrc/gemm.cu``).
+
+``gemm(A, B, ...)`` computes ``C[g] = A[g] @ B[g]^T`` for bf16 operands with fp32
+accumulation. Each operand is described by (tensor, leading dim, group stride,
+major): ``mn=False`` means the operand is stored ``[rows, K]`` (K contiguous),
+``mn=True`` means it is stored ``[K, rows]``. Views into flat parameter buffers
+are passed as (base tensor, offsets folded into a narrowed view).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._ext import err_word, ext
+
+EPI = {"bf16": 0, "f32": 1, "resid": 2, "swiglu": 3, "swiglu_bwd": 4, "logits": 5}
+
+
+def gemm(A, lda, sa, a_mn, B, ldb, sb, b_mn, C, ldc, sc, M, N, K, G=1, epi="bf16", bn=128, R=None, ldr=0,
+         sr=0, aux=None, ldx=0, sx=0, part=None, beta=0.0, f_half=0, max_ctas=0):
+    ext().gemm_bf16(A, lda, sa, a_mn, B, ldb, sb, b_mn, C, ldc, sc, M, N, K, G, EPI[epi], bn, R, ldr, sr,
+                    aux, ldx, sx, part, beta, f_half, err_word(A.device), max_ctas)
+    return C
+
+
+def _bn_for(n: int) -> int:
+    return 128 if n % 128 == 0 or n > 64 else 64
+
+
+def mm_nt(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, bn: int | None = None) -> torch.Tensor:
+    """``a @ b.T`` with a: [M, K], b: [N, K] (both K-major)."""
+    M, K = a.shape
+    N = b.shape[0]
+    c = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    gemm(a, a.stride(0), 0, False, b, b.stride(0), 0, False, c, c.stride(0), 0, M, N, K,
+         epi="bf16" if out_dtype == torch.bfloat16 else "f32", bn=bn or _bn_for(N))
+    return c
+
+
+def mm_nn(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, bn: int | None = None) -> torch.Tensor:
+    """``a @ b`` with a: [M, K] (K-major), b: [K, N] (N contiguous -> MN-major operand)."""
+    M, K = a.shape
+    N = b.shape[1]
+    c = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    gemm(a, a.stride(0), 0, False, b, b.stride(0), 0, True, c, c.stride(0), 0, M, N, K,
+         epi="bf16" if out_dtype == torch.bfloat16 else "f32", bn=bn or _bn_for(N))
+    return c
+
+
+def mm_tn(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, bn: int | None = None) -> torch.Tensor:
+    """``a.T @ b`` with a: [K, M], b: [K, N] (both MN-major) -- weight-gradient shape."""
+    K, M = a.shape
+    N = b.shape[1]
+    c = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    gemm(a, a.stride(0), 0, True, b, b.stride(0), 0, True, c, c.stride(0), 0, M, N, K,
+         epi="bf16" if out_dtype == torch.bfloat16 else "f32", bn=bn or _bn_for(N))
+    return c
+
+
+def mm_tt(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, bn: int | None = None) -> torch.Tensor:
+    """``a.T @ b.T`` with a: [K, M] (MN-major), b: [N, K] (K-major)."""
+    K, M = a.shape
+    N = b.shape[0]
+    c = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    gemm(a, a.stride(0), 0, True, b, b.stride(0), 0, False, c, c.stride(0), 0, M, N, K,
+         epi="bf16" if out_dtype == torch.bfloat16 else "f32", bn=bn or _bn_for(N))
+    return c

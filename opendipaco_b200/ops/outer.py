@@ -1,0 +1,96 @@
+"""Fused DiLoCo outer step (``csrc/outer.cu``) driven by a segment table.
+
+A *segment* is one shared module (its flat fp32 global buffer, momentum buffer and
+the list of local working copies that share it on this GPU, with their weights).
+:class:`OuterPlan` packs the table once (device pointers are stable because every
+buffer is a view into the executor's persistent flat arenas) and each round is one
+kernel launch.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ._ext import ext
+
+SEG_DTYPE = np.dtype([("glob", "<u8"), ("mom", "<u8"), ("n", "<i8"), ("first_local", "<i4"),
+                      ("nlocal", "<i4"), ("mode", "<i4"), ("scale", "<f4"), ("inv_den", "<f4"),
+                      ("pad", "<i4"), ("chunk0", "<i8")])
+LOC_DTYPE = np.dtype([("w32", "<u8"), ("w16", "<u8"), ("weight", "<f4"), ("pad", "<i4")])
+assert SEG_DTYPE.itemsize == 56 and LOC_DTYPE.itemsize == 24
+
+MODE_OUTER, MODE_COPY, MODE_BCAST = 0, 1, 2
+
+
+@dataclass
+class Segment:
+    key: str
+    glob: torch.Tensor                      # fp32 flat view
+    mom: torch.Tensor | None                # fp32 flat view (None for COPY/BCAST)
+    locals32: list[torch.Tensor]
+    locals16: list[torch.Tensor | None]
+    weights: list[float] = field(default_factory=list)
+    mode: int = MODE_OUTER
+    scale: float = 1.0
+    inv_den: float = 1.0
+
+
+class OuterPlan:
+    def __init__(self, segments: list[Segment], device):
+        self.segments = segments
+        self.device = torch.device(device)
+        self.chunk = int(ext().outer_chunk_elems())
+        self._tables = None
+        self.total_chunks = 0
+        self.key_chunks: list[tuple[str, int, int]] = []
+
+    def build(self) -> None:
+        segs = np.zeros(len(self.segments), dtype=SEG_DTYPE)
+        locs = []
+        chunk0 = 0
+        self.key_chunks = []
+        for i, s in enumerate(self.segments):
+            n = s.glob.numel()
+            nch = (n + self.chunk - 1) // self.chunk
+            segs[i] = (s.glob.data_ptr(), s.mom.data_ptr() if s.mom is not None else 0, n, len(locs),
+                       len(s.locals32), s.mode, s.scale, s.inv_den, 0, chunk0)
+            for j, l32 in enumerate(s.locals32):
+                assert l32.numel() == n
+                l16 = s.locals16[j]
+                w = s.weights[j] if j < len(s.weights) else 0.0
+                locs.append((l32.data_ptr(), l16.data_ptr() if l16 is not None else 0, w, 0))
+            self.key_chunks.append((s.key, chunk0, nch))
+            chunk0 += nch
+        self.total_chunks = chunk0
+        loc_arr = np.array(locs, dtype=LOC_DTYPE) if locs else np.zeros(1, dtype=LOC_DTYPE)
+        seg_t = torch.from_numpy(segs.view(np.int64).copy()).to(self.device)
+        loc_t = torch.from_numpy(loc_arr.view(np.int64).copy()).to(self.device)
+        self._tables = (seg_t, loc_t)
+        self.sq_part = torch.zeros(max(self.total_chunks, 1), device=self.device, dtype=torch.float32)
+
+    def set_weights(self, weights: dict[str, list[float]], inv_den: dict[str, float] | None = None) -> None:
+        changed = False
+        for s in self.segments:
+            if s.key in weights and list(weights[s.key]) != list(s.weights):
+                s.weights = list(weights[s.key])
+                changed = True
+            if inv_den and s.key in inv_den and inv_den[s.key] != s.inv_den:
+                s.inv_den = inv_den[s.key]
+                changed = True
+        if changed or self._tables is None:
+            self.build()
+
+    def run(self, lr: float, momentum: float, nesterov: bool, first: bool) -> None:
+        if self._tables is None:
+            self.build()
+        seg_t, loc_t = self._tables
+        ext().outer_step(seg_t, len(self.segments), loc_t, self.total_chunks, lr, momentum, nesterov, first,
+                         self.sq_part)
+
+    def delta_norms(self) -> dict[str, float]:
+        """Per-key ||delta|| of the last run (read back once per round)."""
+        part = self.sq_part.cpu()
+        return {k: float(part[c0:c0 + n].double().sum().sqrt()) for k, c0, n in self.key_chunks}
