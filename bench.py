@@ -1,0 +1,273 @@
+#!/usr/bin/env python
+"""Headline benchmark: DiLoCo training throughput (tokens/sec/box) on the 16-path DiPaCo.
+
+Workload (the reference's headline config): 4x4 DiPaCo = 16 paths, Llama-style
+backbone hidden 384, 6 heads (head_dim 64), FFN 1024, layers_per_level [2, 2] (4
+layers per path), vocab 32000, sequence 128, batch 24 per path, 20 inner AdamW steps
+per round, outer SGD-Nesterov lr 0.7 momentum 0.9; shared embedding / head; bf16
+compute with fp32 master weights. Data: 20,000 synthetic documents with Zipf(1.1)
+token ids and lengths uniform in [128, 2048], routed to the 16 paths by k-means over
+bag-of-tokens features; random-init weights.
+
+One benchmark *step* = one DiLoCo round: every path takes 20 inner steps on its
+shard, then the outer step syncs the shared modules. The 16 paths are split over the
+N GPUs (strong scaling: 16/N paths per GPU). Tokens per round = 16 * 20 * 24 * 128.
+
+Timing: W untimed warm-up rounds, then exactly K rounds bracketed by a barrier and
+``torch.cuda.synchronize()`` on both sides, CUDA events on the launching stream, max
+over ranks. ``value`` times the device work of a round (captured inner-step graph +
+outer step, inputs already resident); ``e2e`` times the same K rounds through the
+public API (``engine.fit``), which copies each round's token batches from pinned
+host memory and reads the losses back. The per-round working set (weights, grads
+and optimizer state: ~570 MB per path) is far larger than the 126 MB L2.
+
+``--impl reference`` runs the unmodified reference package installed in
+``baseline/_ref`` (its own DiPaCoEngine, LocalBackend / TorchDistBackend over NCCL,
+bf16 autocast) on the same documents and shards.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+CFG = dict(levels=[4, 4], hidden=384, heads=6, ffn=1024, layers=[2, 2], vocab=32000, seq=128, batch=24,
+           inner_steps=20, outer_lr=0.7, outer_momentum=0.9, docs=20000, min_len=128, max_len=2048,
+           zipf=1.1)
+BASELINE_VALUE = None  # the reference publishes no throughput number
+
+
+def _rank_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.rows: list[list[str]] = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def build_documents_and_assignments():
+    """Zipf documents + k-means path assignments (identical on every rank / both arms)."""
+    from opendipaco_b200.data import zipf_documents
+    from opendipaco_b200.routing import BagOfTokensFeaturizer, KMeansRouter
+    from opendipaco_b200.data.sharding import assign_paths
+
+    docs = zipf_documents(vocab_size=CFG["vocab"], num_documents=CFG["docs"], min_len=CFG["min_len"],
+                          max_len=CFG["max_len"], exponent=CFG["zipf"], topics=16, seed=0)
+    feat = BagOfTokensFeaturizer(CFG["vocab"], feature_dim=256, seed=0)
+    npaths = CFG["levels"][0] * CFG["levels"][1]
+    router = KMeansRouter(npaths, seed=0).fit(feat([d[:32] for d in docs]))
+    return docs, assign_paths(docs, router, feat)
+
+
+def make_configs(pkg):
+    bb = pkg.BackboneConfig(vocab_size=CFG["vocab"], hidden_size=CFG["hidden"],
+                            num_attention_heads=CFG["heads"], intermediate_size=CFG["ffn"],
+                            layers_per_level=list(CFG["layers"]), max_position_embeddings=2048)
+    cfg = pkg.DiPaCoConfig(backbone=bb, level_sizes=list(CFG["levels"]), sequence_length=CFG["seq"])
+    dl = pkg.DiLoCoConfig(inner_steps=CFG["inner_steps"], outer_lr=CFG["outer_lr"],
+                          outer_momentum=CFG["outer_momentum"], inner_autocast=True)
+    return cfg, dl
+
+
+def run(args) -> dict:
+    rank, world, local = _rank_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    docs, assign = build_documents_and_assignments()
+    npaths = CFG["levels"][0] * CFG["levels"][1]
+
+    if args.impl == "reference":
+        ref_dir = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref_dir, "opendipaco")):
+            return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+        sys.path.insert(0, ref_dir)
+        import opendipaco as pkg
+        from opendipaco.data import ShardedCorpus
+        backend_cls = pkg.LocalBackend if world == 1 else pkg.TorchDistBackend
+    else:
+        import opendipaco_b200 as pkg
+        from opendipaco_b200.data import ShardedCorpus
+        if world == 1:
+            backend_cls = pkg.LocalBackend
+        else:
+            from opendipaco_b200.parallel.backend.nvlink import NVLinkBackend as backend_cls
+
+    cfg, dl = make_configs(pkg)
+    corpus = ShardedCorpus.from_assignments(docs, assign, npaths, CFG["seq"])
+    topo = cfg.build_topology()
+    backend = backend_cls(topo) if world == 1 else backend_cls(topo, device=dev)
+    engine = pkg.DiPaCoEngine(cfg, dl, backend, device=dev, seed=0)
+    engine.total_rounds = args.warmup + 2 * args.steps + 1
+    B = CFG["batch"]
+    owned = backend.owned_paths()
+    tokens_per_round = npaths * CFG["inner_steps"] * B * CFG["seq"]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        engine.fit(corpus, num_rounds=1, batch_size=B, log_every=0)
+    barrier()
+
+    # -- kernel-only device time: inputs resident, graph replay + outer step ------------
+    device_ms = None
+    launches = None
+    if args.impl != "reference":
+        ex = engine._fused
+        st = torch.cuda.current_stream(dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        ev0.record(st)
+        for _ in range(args.steps):
+            ex.device_round()
+        ev1.record(st)
+        barrier()
+        device_ms = ev0.elapsed_time(ev1)
+        launches = ex.launches_per_round() * args.steps
+
+    # -- end to end through the public API ------------------------------------------------
+    st = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        t0 = time.perf_counter()
+        ev0.record(st)
+        for _ in range(args.steps):
+            engine.fit(corpus, num_rounds=1, batch_size=B, log_every=0)
+        ev1.record(st)
+        barrier()
+        wall_ms = (time.perf_counter() - t0) * 1e3
+    e2e_event_ms = ev0.elapsed_time(ev1)
+    if device_ms is None:
+        device_ms = e2e_event_ms
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    device_ms = max_over_ranks(device_ms)
+    wall_ms = max_over_ranks(wall_ms)
+    ms_per_round = device_ms / args.steps
+    value = tokens_per_round / (ms_per_round / 1e3)
+    e2e = tokens_per_round / (wall_ms / args.steps / 1e3)
+
+    if args.impl == "reference":
+        # shard tensors moved to the device per path per round + per-step batch views;
+        # one loss scalar per step read back, plus one delta-norm scalar per shared tensor
+        h2d = sum(int(corpus.shard(topo.path_index(p)).numel()) * 8 for p in owned)
+        n_shared = sum(1 for k in engine.bank for _ in engine.bank[k].parameters() if ".p" not in k)
+        d2h = 4 * CFG["inner_steps"] * len(owned) + 4 * n_shared
+    else:
+        ex = engine._fused
+        h2d = ex.h2d_bytes_per_round()
+        d2h = ex.d2h_bytes_per_round()
+
+    out = {
+        "metric": "tokens/sec/box", "value": round(value, 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_round, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+        "dtype": "bf16", "data": "synthetic (Zipf(1.1) token ids, 20k docs, len U[128,2048]); random init",
+        "config": {"model": "DiPaCo 4x4 (16 paths) Llama hidden 384, 6 heads, ffn 1024, layers [2,2], "
+                            "vocab 32000", "global_batch": 24 * npaths, "seq_len": CFG["seq"],
+                   "parallelism": f"paths{world}", "paths_per_gpu": len(owned),
+                   "inner_steps_per_step": CFG["inner_steps"],
+                   "l2": "per-round working set > L2 (weights+grads+optimizer ~570 MB/path)"},
+        "clocks": clocks.summary(),
+        "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "ms_per_step": round(wall_ms / args.steps, 3)},
+        "gpu_launches": launches if launches is not None else 0,
+    }
+    if args.impl == "reference":
+        out["impl"] = "reference"
+    if world > 1:
+        dist.barrier()
+        if hasattr(backend, "close"):
+            backend.close()
+        dist.destroy_process_group()
+    return out if rank == 0 else {}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    out = run(args)
+    if out:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -70,7 +70,7 @@ __global__ void clip_coef_kernel(const float* __restrict__ part, int nblk, float
   }
 }
 
-// sched: [lr, step_size = lr / bc1, bc2_sqrt]
+// sched: [G][4] = lr, step_size = lr / bc1, bc2_sqrt, active (0 -> leave this path untouched)
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ p16, long long P, long long sp,
                              long long s16, const float* __restrict__ coef, const float* __restrict__ sched, float b1,
@@ -78,7 +78,9 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   const int grp = blockIdx.y;
   const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (i >= P) return;
-  const float lr = sched[0], step_size = sched[1], bc2s = sched[2];
+  const float* sc = sched + grp * 4;  // per path: lr, lr / bc1, sqrt(bc2), active
+  if (sc[3] == 0.f) return;
+  const float lr = sc[0], step_size = sc[1], bc2s = sc[2];
   const float cf = coef ? coef[grp] : 1.f;
   const float decay = 1.f - lr * wd;
   const long long o = grp * sp + i;
@@ -133,8 +135,12 @@ __global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__
   const long long blk = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (blk >= nblocks) return;
-  const float lr = sched[0], step_size = sched[1], bc2s = sched[2];
-  const float cf = coef ? coef[blocks_per_group > 0 ? blk / blocks_per_group : 0] : 1.f;
+  const long long grp = blocks_per_group > 0 ? blk / blocks_per_group : 0;
+  const float* scd = sched + grp * 4;  // per path: lr, lr / bc1, sqrt(bc2), active
+  if (scd[3] == 0.f) return;
+  const float lr = scd[0], step_size = scd[1], bc2s = scd[2];
+  const bool first_step = first || scd[3] > 1.5f;  // 2.0 marks a path's first step
+  const float cf = coef ? coef[grp] : 1.f;
   const long long e0 = blk * 256 + lane * 8;
   const float mscale = mabs[blk] / 127.f;
   const float lo = vlo[blk], sc = vsc[blk];
@@ -146,7 +152,7 @@ __global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__
     const long long e = e0 + k;
     gv[k] = e < n ? g[e] * cf : 0.f;
     mv[k] = (float)mqp[k] * mscale;
-    vv[k] = first ? 0.f : __expf((float)vqp[k] * sc + lo);
+    vv[k] = first_step ? 0.f : __expf((float)vqp[k] * sc + lo);
     mv[k] = mv[k] * b1 + (1.f - b1) * gv[k];
     vv[k] = vv[k] * b2 + (1.f - b2) * gv[k] * gv[k];
   }

@@ -9,8 +9,9 @@ void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tenso
 void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor y, int64_t sy,
                  torch::Tensor rstd, int64_t M, int64_t H, int64_t G, double eps);
 void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor rstd, torch::Tensor dy,
-                 int64_t sdy, c10::optional<torch::Tensor> dres, torch::Tensor dx, int64_t sdx, torch::Tensor dw,
-                 int64_t sdw, torch::Tensor work, int64_t M, int64_t H, int64_t G, double beta);
+                 int64_t sdy, c10::optional<torch::Tensor> dres, torch::Tensor dx, int64_t sdx,
+                 c10::optional<torch::Tensor> dx16, torch::Tensor dw, int64_t sdw, torch::Tensor work, int64_t M,
+                 int64_t H, int64_t G, double beta);
 void embedding_fwd(torch::Tensor ids, torch::Tensor E, int64_t se, torch::Tensor out, int64_t M, int64_t H,
                    int64_t G, int64_t V);
 void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,

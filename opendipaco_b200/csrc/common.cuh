@@ -173,6 +173,30 @@ ODP_DEVICE void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Issue a 16-column TMEM load without waiting (pair with tmem_wait_tie*).
+ODP_DEVICE void tmem_ld16_nw(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+#define ODP_TIE16(r)                                                                                        \
+  "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), \
+      "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+
+// Wait for all outstanding TMEM loads; the registers are tied so no use of them can
+// be scheduled before the wait.
+ODP_DEVICE void tmem_wait_tie32(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : ODP_TIE16(r) : : "memory");
+  asm volatile("" : ODP_TIE16((r + 16)) : : "memory");
+}
+ODP_DEVICE void reg_tie32(uint32_t* r) {
+  asm volatile("" : ODP_TIE16(r) : : "memory");
+  asm volatile("" : ODP_TIE16((r + 16)) : : "memory");
+}
+
 // ---------------------------------------------------------------- misc
 ODP_DEVICE float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
 

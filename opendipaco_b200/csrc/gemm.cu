@@ -42,7 +42,7 @@ struct GemmParams {
   long long ldr, sr;
   void* aux;  // swiglu: pre-activation [M, 2F] bf16 ([g | u]); bwd: same layout as input
   long long ldx, sx;
-  float* part;  // logits: [G][M][tiles_n] float2
+  float* part;  // logits: [G][M][2 * tiles_n] float2 (one per tile column half)
   float beta;
   int f_half;  // swiglu: F (rows of the gate block; up block starts at row F)
   int* err;
@@ -50,7 +50,7 @@ struct GemmParams {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 
 template <int BN, int STAGES>
 struct SmemLayout {
@@ -63,137 +63,189 @@ struct SmemLayout {
 
 ODP_DEVICE float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
+// Load 32 accumulator columns [c, c+32) of this thread's TMEM lane into fp32.
+ODP_DEVICE void load32(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_ld16_nw(taddr, r);
+  tmem_ld16_nw(taddr + 16, r + 16);
+  tmem_wait_tie32(r);
+}
+
+ODP_DEVICE void store_bf16x32(__nv_bfloat16* dst, const float* v) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) w[i / 2] = pack_bf16(v[i], v[i + 1]);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+ODP_DEVICE void load_bf16x32(const __nv_bfloat16* src, float* v) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 q = s4[i];
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[8 * i + j] = __bfloat162float(h[j]);
+  }
+}
+
+// Epilogue of one tile for one thread: TMEM lane row q*32+lane, column half `ch`
+// (two warps share a lane quarter; each drains BN/2 columns).
 template <int BN, int EPI>
-ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int lane, int g, int tm, int tn) {
+ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int ch, int lane, int g, int tm,
+                              int tn) {
   const int row = q * 32 + lane;
   const long long grow = (long long)tm * BM + row;
   const bool row_ok = grow < p.M;
   const uint32_t tbase = tmem_acc + ((uint32_t)(q * 32) << 16);
+  constexpr int HALF = BN / 2;
 
   if constexpr (EPI == EPI_SWIGLU) {
-    // accumulator columns [0, BN/2) = gate feature block, [BN/2, BN) = up feature block
-    constexpr int HALF = BN / 2;
-    const int f0 = tn * HALF;
-#pragma unroll 1
-    for (int c = 0; c < HALF; c += 16) {
-      float a[16], b[16];
-      tmem_ld16(tbase + c, a);
-      tmem_ld16(tbase + HALF + c, b);
-      if (!row_ok || f0 + c >= p.f_half) continue;
-      __nv_bfloat16* H = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + f0 + c;
-      __nv_bfloat16* GU = reinterpret_cast<__nv_bfloat16*>(p.aux) + g * p.sx + grow * p.ldx + f0 + c;
-      uint32_t hv[8], gv[8], uv[8];
+    // columns [0, HALF) = gate block, [HALF, BN) = up block of the same HALF features;
+    // this thread takes HALF/2 of them.
+    constexpr int QW = HALF / 2;
+    static_assert(QW == 32, "swiglu epilogue expects BN == 128");
+    const int c0 = ch * QW;
+    const int f0 = tn * HALF + c0;
+    uint32_t a[32], b[32];
+    tmem_ld16_nw(tbase + c0, a);
+    tmem_ld16_nw(tbase + c0 + 16, a + 16);
+    tmem_ld16_nw(tbase + HALF + c0, b);
+    tmem_ld16_nw(tbase + HALF + c0 + 16, b + 16);
+    tmem_wait_tie32(a);
+    reg_tie32(b);
+    if (!row_ok || f0 >= p.f_half) return;
+    float h[32], gg[32], uu[32];
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        float g0 = bf16_round(a[i]), g1 = bf16_round(a[i + 1]);
-        float u0 = bf16_round(b[i]), u1 = bf16_round(b[i + 1]);
-        float s0 = bf16_round(silu_f(g0)), s1 = bf16_round(silu_f(g1));
-        hv[i / 2] = pack_bf16(s0 * u0, s1 * u1);
-        gv[i / 2] = pack_bf16(g0, g1);
-        uv[i / 2] = pack_bf16(u0, u1);
-      }
-      uint4* hp = reinterpret_cast<uint4*>(H);
-      hp[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-      hp[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
-      uint4* gp = reinterpret_cast<uint4*>(GU);
-      gp[0] = make_uint4(gv[0], gv[1], gv[2], gv[3]);
-      gp[1] = make_uint4(gv[4], gv[5], gv[6], gv[7]);
-      uint4* up = reinterpret_cast<uint4*>(GU + p.f_half);
-      up[0] = make_uint4(uv[0], uv[1], uv[2], uv[3]);
-      up[1] = make_uint4(uv[4], uv[5], uv[6], uv[7]);
+    for (int i = 0; i < 32; ++i) {
+      gg[i] = bf16_round(__uint_as_float(a[i]));
+      uu[i] = bf16_round(__uint_as_float(b[i]));
+      h[i] = bf16_round(silu_f(gg[i])) * uu[i];
     }
-    return;
+    __nv_bfloat16* H = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + f0;
+    __nv_bfloat16* GU = reinterpret_cast<__nv_bfloat16*>(p.aux) + g * p.sx + grow * p.ldx + f0;
+    store_bf16x32(H, h);
+    store_bf16x32(GU, gg);
+    store_bf16x32(GU + p.f_half, uu);
   } else {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      float v[16];
-      tmem_ld16(tbase + c, v);
+    for (int c = ch * HALF; c < (ch + 1) * HALF; c += 32) {
+      uint32_t r[32];
+      load32(tbase + c, r);
       const int gcol = tn * BN + c;
       if (!row_ok || gcol >= p.N) continue;
-      const bool full = gcol + 16 <= p.N;
-      if constexpr (EPI == EPI_BF16 || EPI == EPI_LOGITS) {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
-        if (full) {
-          uint32_t w[8];
+      float v[32];
 #pragma unroll
-          for (int i = 0; i < 16; i += 2) w[i / 2] = pack_bf16(v[i], v[i + 1]);
-          uint4* d4 = reinterpret_cast<uint4*>(dst);
-          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        } else {
-          for (int i = 0; i < 16 && gcol + i < p.N; ++i) dst[i] = __float2bfloat16(v[i]);
-        }
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      const bool full = gcol + 32 <= p.N;
+      if constexpr (EPI == EPI_BF16) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
+        if (full) store_bf16x32(dst, v);
+        else for (int i = 0; gcol + i < p.N; ++i) dst[i] = __float2bfloat16(v[i]);
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
         // acc = dH (gradient of silu(g) * u); aux = saved [g | u]; C = [dG | dU]
         const __nv_bfloat16* gsrc = reinterpret_cast<const __nv_bfloat16*>(p.aux) + g * p.sx + grow * p.ldx + gcol;
-        const __nv_bfloat16* usrc = gsrc + p.f_half;
         __nv_bfloat16* dg = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
-        __nv_bfloat16* du = dg + p.f_half;
-        for (int i = 0; i < 16; ++i) {
-          if (!full && gcol + i >= p.N) break;
-          const float gv = __bfloat162float(gsrc[i]), uv = __bfloat162float(usrc[i]);
+        float gv[32], uv[32], og[32], ou[32];
+        if (full) {
+          load_bf16x32(gsrc, gv);
+          load_bf16x32(gsrc + p.f_half, uv);
+        } else {
+          for (int i = 0; i < 32; ++i) {
+            gv[i] = gcol + i < p.N ? __bfloat162float(gsrc[i]) : 0.f;
+            uv[i] = gcol + i < p.N ? __bfloat162float(gsrc[p.f_half + i]) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
           const float dh = bf16_round(v[i]);
-          const float sg = 1.0f / (1.0f + __expf(-gv));
-          const float act = bf16_round(gv * sg);
-          du[i] = __float2bfloat16(dh * act);
-          const float da = bf16_round(dh * uv);
-          dg[i] = __float2bfloat16(da * sg * (1.0f + gv * (1.0f - sg)));
+          const float sg = 1.0f / (1.0f + __expf(-gv[i]));
+          ou[i] = dh * bf16_round(gv[i] * sg);
+          og[i] = bf16_round(dh * uv[i]) * sg * (1.0f + gv[i] * (1.0f - sg));
+        }
+        if (full) {
+          store_bf16x32(dg, og);
+          store_bf16x32(dg + p.f_half, ou);
+        } else {
+          for (int i = 0; gcol + i < p.N; ++i) {
+            dg[i] = __float2bfloat16(og[i]);
+            dg[p.f_half + i] = __float2bfloat16(ou[i]);
+          }
         }
       } else if constexpr (EPI == EPI_F32 || EPI == EPI_RESID) {
         float* dst = reinterpret_cast<float*>(p.C) + g * p.sc + grow * p.ldc + gcol;
-        const float* rs = nullptr;
-        if constexpr (EPI == EPI_RESID) rs = p.R + g * p.sr + grow * p.ldr + gcol;
-        for (int i = 0; i < 16; ++i) {
-          if (!full && gcol + i >= p.N) break;
-          float x = v[i];
-          if constexpr (EPI == EPI_RESID) x += rs[i];
-          else if (p.beta != 0.f) x += p.beta * dst[i];
-          dst[i] = x;
+        if (full) {
+          float4* d4 = reinterpret_cast<float4*>(dst);
+          if constexpr (EPI == EPI_RESID) {
+            const float4* r4 = reinterpret_cast<const float4*>(p.R + g * p.sr + grow * p.ldr + gcol);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float4 x = r4[i];
+              d4[i] = make_float4(x.x + v[4 * i], x.y + v[4 * i + 1], x.z + v[4 * i + 2], x.w + v[4 * i + 3]);
+            }
+          } else {
+            if (p.beta != 0.f) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float4 x = d4[i];
+                d4[i] = make_float4(v[4 * i] + p.beta * x.x, v[4 * i + 1] + p.beta * x.y,
+                                    v[4 * i + 2] + p.beta * x.z, v[4 * i + 3] + p.beta * x.w);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
+          }
+        } else {
+          for (int i = 0; gcol + i < p.N; ++i) {
+            float x = v[i];
+            if constexpr (EPI == EPI_RESID) x += p.R[g * p.sr + grow * p.ldr + gcol + i];
+            else if (p.beta != 0.f) x += p.beta * dst[i];
+            dst[i] = x;
+          }
         }
       }
     }
   }
 }
 
-// Logits epilogue: bf16 store + per-row (max, sum exp) over this tile's valid columns.
+// Logits epilogue: bf16 store + per-row (max, sum exp) over this thread's half of the
+// tile (partials indexed [row][2 * tn + ch]).
 template <int BN>
-ODP_DEVICE void epilogue_logits(const GemmParams& p, uint32_t tmem_acc, int q, int lane, int g, int tm, int tn) {
+ODP_DEVICE void epilogue_logits(const GemmParams& p, uint32_t tmem_acc, int q, int ch, int lane, int g, int tm,
+                                int tn) {
   const int row = q * 32 + lane;
   const long long grow = (long long)tm * BM + row;
   const bool row_ok = grow < p.M;
   const uint32_t tbase = tmem_acc + ((uint32_t)(q * 32) << 16);
+  constexpr int HALF = BN / 2;
   float mx = -INFINITY, se = 0.f;
 #pragma unroll 1
-  for (int c = 0; c < BN; c += 16) {
-    float v[16];
-    tmem_ld16(tbase + c, v);
+  for (int c = ch * HALF; c < (ch + 1) * HALF; c += 32) {
+    uint32_t rr[32];
+    load32(tbase + c, rr);
     const int gcol = tn * BN + c;
     if (!row_ok || gcol >= p.N) continue;
+    const int n = min(32, p.N - gcol);
+    float r[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = bf16_round(__uint_as_float(rr[i]));
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
-    const int n = min(16, p.N - gcol);
-    float r[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) r[i] = bf16_round(v[i]);
-    if (n == 16) {
-      uint32_t w[8];
-#pragma unroll
-      for (int i = 0; i < 16; i += 2) w[i / 2] = pack_bf16(r[i], r[i + 1]);
-      uint4* d4 = reinterpret_cast<uint4*>(dst);
-      d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    } else {
-      for (int i = 0; i < n; ++i) dst[i] = __float2bfloat16(r[i]);
-    }
+    if (n == 32) store_bf16x32(dst, r);
+    else for (int i = 0; i < n; ++i) dst[i] = __float2bfloat16(r[i]);
     float cm = -INFINITY;
-    for (int i = 0; i < n; ++i) cm = fmaxf(cm, r[i]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) cm = i < n ? fmaxf(cm, r[i]) : cm;
     if (cm > mx) {
       se *= __expf(mx - cm);
       mx = cm;
     }
-    for (int i = 0; i < n; ++i) se += __expf(r[i] - mx);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) se += i < n ? __expf(r[i] - mx) : 0.f;
   }
   if (row_ok) {
-    float2* pp = reinterpret_cast<float2*>(p.part) + ((long long)g * p.M + grow) * p.tiles_n + tn;
+    float2* pp = reinterpret_cast<float2*>(p.part) + ((long long)g * p.M + grow) * (2 * p.tiles_n) + 2 * tn + ch;
     *pp = make_float2(mx, se);
   }
 }
@@ -221,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accfull[b], 1);
-      mbar_init(&accempty[b], 128);
+      mbar_init(&accempty[b], 256);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -342,8 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp % 4;  // TMEM lane quarter this warp may access
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    const int q = warp % 4;         // TMEM lane quarter this warp may access
+    const int ch = (warp - 2) / 4;  // which column half of the tile
     int acc = 0;
     uint32_t accphase = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
@@ -352,8 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int g = t / tiles_per_g, r = t % tiles_per_g;
       const int tm = r / p.tiles_n, tn = r % p.tiles_n;
       const uint32_t tacc = tmem_base + acc * BN;
-      if constexpr (EPI == EPI_LOGITS) epilogue_logits<BN>(p, tacc, q, lane, g, tm, tn);
-      else epilogue_tile<BN, EPI>(p, tacc, q, lane, g, tm, tn);
+      if constexpr (EPI == EPI_LOGITS) epilogue_logits<BN>(p, tacc, q, ch, lane, g, tm, tn);
+      else epilogue_tile<BN, EPI>(p, tacc, q, ch, lane, g, tm, tn);
       tc_fence_before();
       mbar_arrive(&accempty[acc]);
       acc ^= 1;
@@ -435,6 +488,15 @@ struct Operand {
   bool mn;  // true: stored [K, rows] (rows contiguous); false: stored [rows, K]
 };
 
+// Which (epilogue, operand majors, tile width) combinations are instantiated.
+template <int EPI, bool AM, bool BMN, int BN>
+constexpr bool cfg_ok() {
+  if (EPI == EPI_SWIGLU || EPI == EPI_LOGITS) return !AM && !BMN && BN == 128;
+  if (EPI == EPI_SWIGLU_BWD) return !AM && BMN && BN != 256;
+  if (EPI == EPI_RESID || EPI == EPI_BF16) return !AM && BN != 256;
+  return BN != 256 || (!AM && !BMN);
+}
+
 template <int EPI>
 static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, cudaStream_t st, int max_ctas) {
   const int rowsB = EPI == EPI_SWIGLU ? bn / 2 : bn;
@@ -443,9 +505,11 @@ static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, 
   CUtensorMap mb = B.mn ? make_map(B.ptr, p.N, p.K, B.ld, p.G, B.sg, 64)
                         : make_map(B.ptr, p.K, b_rows_extent, B.ld, p.G, B.sg, rowsB);
 #define ODP_GO(AM, BMN, BNV, ST)                                        \
-  if (A.mn == AM && B.mn == BMN && bn == BNV) {                         \
-    launch_t<AM, BMN, BNV, ST, EPI>(ma, mb, p, st, max_ctas);           \
-    return;                                                             \
+  if constexpr (cfg_ok<EPI, AM, BMN, BNV>()) {                          \
+    if (A.mn == AM && B.mn == BMN && bn == BNV) {                       \
+      launch_t<AM, BMN, BNV, ST, EPI>(ma, mb, p, st, max_ctas);         \
+      return;                                                           \
+    }                                                                   \
   }
   ODP_GO(false, false, 128, 6)
   ODP_GO(false, true, 128, 6)

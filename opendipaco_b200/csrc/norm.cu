@@ -50,7 +50,7 @@ constexpr int kNormRowsPerBlock = 32;
 __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, long long sx, const float* __restrict__ w,
                                    long long sw, const float* __restrict__ rstd, const float* __restrict__ dy,
                                    long long sdy, const float* dres, float* dx, long long sdx,
-                                   float* __restrict__ dw_part, int M, int H, int G) {
+                                   __nv_bfloat16* dx16, float* __restrict__ dw_part, int M, int H, int G) {
   // block = 256 threads = 8 warps; block handles kNormRowsPerBlock rows of one group
   const int nblk = (M + kNormRowsPerBlock - 1) / kNormRowsPerBlock;
   const int g = blockIdx.x / nblk, b = blockIdx.x % nblk;
@@ -75,6 +75,7 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, long long sx, co
       float v = rs * (wg[i] * dyr[i] - xh * dot);
       if (drr) v += drr[i];
       dxr[i] = v;
+      if (dx16) dx16[g * sdx + (long long)r * H + i] = __float2bfloat16(v);
       sdw[warp * H + i] += dyr[i] * xh;
     }
   }
@@ -165,8 +166,9 @@ void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
 }
 
 void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor rstd, torch::Tensor dy,
-                 int64_t sdy, c10::optional<torch::Tensor> dres, torch::Tensor dx, int64_t sdx, torch::Tensor dw,
-                 int64_t sdw, torch::Tensor work, int64_t M, int64_t H, int64_t G, double beta) {
+                 int64_t sdy, c10::optional<torch::Tensor> dres, torch::Tensor dx, int64_t sdx,
+                 c10::optional<torch::Tensor> dx16, torch::Tensor dw, int64_t sdw, torch::Tensor work, int64_t M,
+                 int64_t H, int64_t G, double beta) {
   c10::cuda::CUDAGuard guard(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
   const int nblk = (int)((M + odp::kNormRowsPerBlock - 1) / odp::kNormRowsPerBlock);
@@ -176,7 +178,8 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
     cudaFuncSetAttribute(odp::rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   odp::rmsnorm_bwd_kernel<<<(int)G * nblk, 256, smem, st>>>(
       x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, rstd.data_ptr<float>(), dy.data_ptr<float>(), sdy,
-      dres.has_value() ? dres->data_ptr<float>() : nullptr, dx.data_ptr<float>(), sdx, work.data_ptr<float>(),
+      dres.has_value() ? dres->data_ptr<float>() : nullptr, dx.data_ptr<float>(), sdx,
+      dx16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx16->data_ptr()) : nullptr, work.data_ptr<float>(),
       (int)M, (int)H, (int)G);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::reduce_parts_kernel<<<blocks_for(G * H, 256), 256, 0, st>>>(work.data_ptr<float>(), nblk, (int)H, (int)G,

@@ -26,10 +26,12 @@ namespace odp {
 struct OuterSeg {
   float* glob;
   float* mom;       // null for COPY
+  float* delta;     // ACC writes sum_j w_j (global - local_j) here; APPLY reads it
   long long n;
   int first_local;  // index into the local table
   int nlocal;
-  int mode;         // 0 = outer step, 1 = copy local -> global, 2 = broadcast global -> locals
+  int mode;         // 0 = outer step, 1 = copy local -> global, 2 = broadcast global -> locals,
+                    // 3 = accumulate local pseudo-gradient into delta, 4 = apply delta (outer step)
   float scale;      // sqrt(sharing) (or 1)
   float inv_den;    // 1 / sum w  (normalize) or 1
   long long chunk0; // first chunk index of this segment in the flat chunk space
@@ -75,9 +77,17 @@ __global__ void outer_step_kernel(const OuterSeg* __restrict__ segs, int nseg, c
       }
       const float gv = s.glob[e];
       float acc = 0.f;
-      for (int j = 0; j < s.nlocal; ++j) {
-        const OuterLocal L = locs[s.first_local + j];
-        acc = __fadd_rn(acc, __fmul_rn(L.weight, __fsub_rn(gv, L.w32[e])));
+      if (s.mode == 4) {
+        acc = s.delta[e];
+      } else {
+        for (int j = 0; j < s.nlocal; ++j) {
+          const OuterLocal L = locs[s.first_local + j];
+          acc = __fadd_rn(acc, __fmul_rn(L.weight, __fsub_rn(gv, L.w32[e])));
+        }
+        if (s.mode == 3) {
+          s.delta[e] = acc;
+          continue;
+        }
       }
       float d = __fmul_rn(__fmul_rn(acc, s.inv_den), s.scale);
       sq += d * d;
@@ -112,7 +122,7 @@ __global__ void outer_step_kernel(const OuterSeg* __restrict__ segs, int nseg, c
 // locals: int64 tensor [nloc, 3]. Both must live on the device.
 void outer_step(torch::Tensor segs, int64_t nseg, torch::Tensor locals, int64_t total_chunks, double lr,
                 double momentum, bool nesterov, bool first, c10::optional<torch::Tensor> sq_part) {
-  static_assert(sizeof(odp::OuterSeg) == 56, "OuterSeg layout");
+  static_assert(sizeof(odp::OuterSeg) == 64, "OuterSeg layout");
   static_assert(sizeof(odp::OuterLocal) == 24, "OuterLocal layout");
   TORCH_CHECK(segs.is_cuda() && locals.is_cuda(), "outer_step: tables must be on the device");
   c10::cuda::CUDAGuard guard(segs.device());

@@ -82,6 +82,7 @@ class Attention(nn.Module):
         self.num_heads = bb.num_attention_heads
         self.num_kv = bb.kv_heads()
         self.head_dim = bb.hidden_size // bb.num_attention_heads
+        self.rope_theta = bb.rope_theta
         self.q_proj = nn.Linear(bb.hidden_size, self.num_heads * self.head_dim, bias=False)
         self.k_proj = nn.Linear(bb.hidden_size, self.num_kv * self.head_dim, bias=False)
         self.v_proj = nn.Linear(bb.hidden_size, self.num_kv * self.head_dim, bias=False)
@@ -182,6 +183,10 @@ class HeadModule(nn.Module):
         self.lm_head = nn.Linear(bb.hidden_size, bb.vocab_size, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if _use_kernels(x):
+            from ..ops import autograd as A
+
+            return A.linear(self.norm(x), self.lm_head.weight)
         return self.lm_head(self.norm(x))
 
 

@@ -11,10 +11,13 @@ from ._ext import ext
 SQ_ELEMS_PER_BLOCK = 1 << 16
 
 
-def sched_tensor(lr: float, b1: float, b2: float, step: int, device) -> torch.Tensor:
-    """[lr, lr / (1 - b1^t), sqrt(1 - b2^t)] for step t (1-based)."""
-    return torch.tensor([lr, lr / (1 - b1 ** step), math.sqrt(1 - b2 ** step)], dtype=torch.float32,
-                        device=device)
+def sched_row(lr: float, b1: float, b2: float, step: int, active: bool = True) -> list[float]:
+    """[lr, lr / (1 - b1^t), sqrt(1 - b2^t), active] for step t (1-based)."""
+    return [lr, lr / (1 - b1 ** step), math.sqrt(1 - b2 ** step), 1.0 if active else 0.0]
+
+
+def sched_tensor(lr: float, b1: float, b2: float, step: int, device, groups: int = 1) -> torch.Tensor:
+    return torch.tensor([sched_row(lr, b1, b2, step)] * groups, dtype=torch.float32, device=device)
 
 
 def clip_coef(grads: torch.Tensor, P: int, stride: int, G: int, max_norm: float | None,
@@ -36,7 +39,7 @@ def adamw(p, g, m, v, p16, P, stride, stride16, G, coef, sched, b1, b2, eps, wd)
 def adam8bit_step(p: torch.Tensor, grad: torch.Tensor, st: dict, *, lr, b1, b2, eps, wd, bc1, bc2_sqrt,
                   first: bool, coef=None, p16=None, blocks_per_group: int = 0) -> None:
     """One 8-bit AdamW update of ``p`` in place (state layout of :class:`Adam8bit`)."""
-    sched = torch.tensor([lr, lr / bc1, bc2_sqrt], dtype=torch.float32, device=p.device)
+    sched = torch.tensor([lr, lr / bc1, bc2_sqrt, 1.0], dtype=torch.float32, device=p.device)
     ext().adam8bit_step(p.data.reshape(-1), grad.reshape(-1).float().contiguous(), st["m_q"], st["m_absmax"],
                         st["v_q"], st["v_lo"], st["v_scale"], coef, sched, b1, b2, eps, wd, first, p16,
                         blocks_per_group)

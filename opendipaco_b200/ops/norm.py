@@ -23,7 +23,7 @@ def rms_norm_bwd(x, w, rstd, dy, dres=None):
     dw = torch.empty(H, device=x.device, dtype=torch.float32)
     nblk = (R + 31) // 32
     work = torch.empty(nblk * H, device=x.device, dtype=torch.float32)
-    ext().rmsnorm_bwd(x, 0, w, 0, rstd, dy.float().contiguous(), 0, dres, dx, 0, dw, 0, work, R, H, 1, 0.0)
+    ext().rmsnorm_bwd(x, 0, w, 0, rstd, dy.float().contiguous(), 0, dres, dx, 0, None, dw, 0, work, R, H, 1, 0.0)
     return dx, dw
 
 

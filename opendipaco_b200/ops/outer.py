@@ -16,13 +16,13 @@ import torch
 
 from ._ext import ext
 
-SEG_DTYPE = np.dtype([("glob", "<u8"), ("mom", "<u8"), ("n", "<i8"), ("first_local", "<i4"),
+SEG_DTYPE = np.dtype([("glob", "<u8"), ("mom", "<u8"), ("delta", "<u8"), ("n", "<i8"), ("first_local", "<i4"),
                       ("nlocal", "<i4"), ("mode", "<i4"), ("scale", "<f4"), ("inv_den", "<f4"),
                       ("pad", "<i4"), ("chunk0", "<i8")])
 LOC_DTYPE = np.dtype([("w32", "<u8"), ("w16", "<u8"), ("weight", "<f4"), ("pad", "<i4")])
-assert SEG_DTYPE.itemsize == 56 and LOC_DTYPE.itemsize == 24
+assert SEG_DTYPE.itemsize == 64 and LOC_DTYPE.itemsize == 24
 
-MODE_OUTER, MODE_COPY, MODE_BCAST = 0, 1, 2
+MODE_OUTER, MODE_COPY, MODE_BCAST, MODE_ACC, MODE_APPLY = 0, 1, 2, 3, 4
 
 
 @dataclass
@@ -36,6 +36,7 @@ class Segment:
     mode: int = MODE_OUTER
     scale: float = 1.0
     inv_den: float = 1.0
+    delta: torch.Tensor | None = None       # fp32 flat buffer for the ACC / APPLY phases
 
 
 class OuterPlan:
@@ -55,7 +56,8 @@ class OuterPlan:
         for i, s in enumerate(self.segments):
             n = s.glob.numel()
             nch = (n + self.chunk - 1) // self.chunk
-            segs[i] = (s.glob.data_ptr(), s.mom.data_ptr() if s.mom is not None else 0, n, len(locs),
+            segs[i] = (s.glob.data_ptr(), s.mom.data_ptr() if s.mom is not None else 0,
+                       s.delta.data_ptr() if s.delta is not None else 0, n, len(locs),
                        len(s.locals32), s.mode, s.scale, s.inv_den, 0, chunk0)
             for j, l32 in enumerate(s.locals32):
                 assert l32.numel() == n
@@ -89,6 +91,18 @@ class OuterPlan:
         seg_t, loc_t = self._tables
         ext().outer_step(seg_t, len(self.segments), loc_t, self.total_chunks, lr, momentum, nesterov, first,
                          self.sq_part)
+
+    def with_mode(self, mode_for_outer: int) -> "OuterPlan":
+        """A copy of this plan whose outer segments run in ``mode_for_outer``
+        (ACC or APPLY), sharing the same buffers."""
+        segs = [Segment(s.key, s.glob, s.mom, s.locals32, s.locals16, s.weights,
+                        mode_for_outer if s.mode == MODE_OUTER else s.mode, s.scale, s.inv_den, s.delta)
+                for s in self.segments]
+        if mode_for_outer == MODE_ACC:
+            segs = [s for s in segs if s.mode == MODE_ACC]
+        plan = OuterPlan(segs, self.device)
+        plan.build()
+        return plan
 
     def delta_norms(self) -> dict[str, float]:
         """Per-key ||delta|| of the last run (read back once per round)."""

@@ -47,11 +47,13 @@ class BagOfTokensFeaturizer:
             if self._proj_dev is None:
                 self._proj_dev = self.projection.to(self.device)
             return K.bag_of_tokens(prefixes, self._proj_dev, self.vocab_size).cpu()
+        # normalised counts @ projection == mean of the projection rows of the prefix
+        # tokens: gather the rows and take a per-prefix segment mean (no dense counts).
+        lens = torch.tensor([int(p.numel()) for p in prefixes], dtype=torch.long)
         feats = torch.zeros(len(prefixes), self.feature_dim)
-        for i, ids in enumerate(prefixes):
-            if ids.numel() == 0:
-                continue
-            c = torch.bincount(ids.clamp(max=self.vocab_size - 1), minlength=self.vocab_size).float()
-            c /= c.sum().clamp(min=1.0)
-            feats[i] = c @ self.projection
+        if lens.sum() > 0:
+            ids = torch.cat([p.reshape(-1).long() for p in prefixes]).clamp(max=self.vocab_size - 1)
+            seg = torch.repeat_interleave(torch.arange(len(prefixes)), lens)
+            feats.index_add_(0, seg, self.projection[ids])
+            feats /= lens.clamp(min=1).unsqueeze(1).float()
         return torch.nn.functional.normalize(feats, dim=-1)

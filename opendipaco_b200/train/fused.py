@@ -1,0 +1,629 @@
+"""Fused B200 executor for :class:`~opendipaco_b200.train.loop.DiPaCoEngine`.
+
+Memory layout (per GPU, G = owned paths):
+
+* one flat fp32 arena per quantity, shape ``[G, P]``: master weights, gradients,
+  AdamW moments (or the blockwise 8-bit state), plus a bf16 working copy of the
+  weights for the GEMMs. ``P`` is one path's parameter count with every tensor
+  padded to a multiple of 256 elements (so 8-bit blocks never straddle two tensors
+  and every TMA base is 512-byte aligned). Tensors appear in ``PathModel.parameters()``
+  order, so a path's modules are contiguous regions and ``q|k|v`` and ``gate|up``
+  are single ``[3H, H]`` / ``[2F, H]`` matrices.
+* the global bank: one flat fp32 buffer (+ momentum) per owned module key with the
+  same module-relative layout, so the outer step is elementwise over regions.
+* every ``nn.Parameter`` of ``engine.bank`` and of the per-path ``PathModel``s is a
+  view into these arenas: checkpoints, ``global_modules()`` and evaluation see the
+  live weights without copies.
+
+One inner step for all G paths = embedding gather, per layer RMSNorm -> QKV GEMM ->
+attention (RoPE fused) -> O GEMM (+residual) -> RMSNorm -> gate|up GEMM (SwiGLU
+epilogue) -> down GEMM (+residual), final RMSNorm -> LM-head GEMM (log-sum-exp
+partials in the epilogue) -> CE, and the mirror-image backward, then the
+deterministic grad-norm clip and one AdamW (or 8-bit Adam) launch over the whole
+arena. Every GEMM is the grouped tcgen05 kernel over the G paths' weights. A round
+(``inner_steps`` steps) is captured once in a CUDA graph; each round then costs one
+host->device copy of its token batches + schedule, one graph launch, one outer-step
+kernel and one device->host read of the last step's losses.
+
+Semantics match the module executor: same batch indices (drawn from the engine's
+CPU generator path by path), same cosine schedule, bf16 compute with fp32 master
+weights (the reference's ``inner_autocast`` numerics), fp32 pseudo-gradients and
+outer SGD-Nesterov.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+from ..models.llama import rope_cos_sin
+from ..models.path import build_path_model
+from ..ops._ext import check_errors, err_word, ext
+from ..ops.outer import MODE_COPY, MODE_OUTER, OuterPlan, Segment
+from ..optim.adam8bit import Adam8bit
+from ..optim.diloco import inner_lr_at, make_inner_optimizer
+from ..topology import Path, is_private_key
+
+ALIGN = 256
+
+
+def _ru(n: int, a: int = ALIGN) -> int:
+    return (n + a - 1) // a * a
+
+
+@dataclass
+class _LayerOffsets:
+    qkv: int
+    o: int
+    gu: int
+    down: int
+    ln1: int
+    ln2: int
+
+
+class PathLayout:
+    """Flat layout of one path's parameters (``PathModel.named_parameters`` order)."""
+
+    def __init__(self, pm: nn.Module, cfg):
+        self.entries: list[tuple[str, tuple, int, int]] = []
+        off = 0
+        for name, p in pm.named_parameters():
+            self.entries.append((name, tuple(p.shape), off, p.numel()))
+            off += _ru(p.numel())
+        self.P = off
+        self.by_name = {n: (s, o, k) for n, s, o, k in self.entries}
+        bb = cfg.backbone
+        self.layers: list[_LayerOffsets] = []
+        for i, _ in enumerate(pm._body_keys):
+            for j in range(len(pm.body[i].layers)):
+                pre = f"body.{i}.layers.{j}."
+                o = {k: self.by_name[pre + k][1] for k in (
+                    "self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                    "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
+                    "mlp.down_proj.weight", "input_layernorm.weight", "post_attention_layernorm.weight")}
+                H, Fd, D = bb.hidden_size, bb.intermediate_size, bb.head_dim
+                nq, nkv = bb.num_attention_heads, bb.kv_heads()
+                if (o["self_attn.k_proj.weight"] != o["self_attn.q_proj.weight"] + nq * D * H
+                        or o["self_attn.v_proj.weight"] != o["self_attn.k_proj.weight"] + nkv * D * H
+                        or o["mlp.up_proj.weight"] != o["mlp.gate_proj.weight"] + Fd * H):
+                    raise ValueError("fused executor needs q|k|v and gate|up to be contiguous "
+                                     "(hidden/intermediate sizes must keep 256-element alignment)")
+                self.layers.append(_LayerOffsets(o["self_attn.q_proj.weight"], o["self_attn.o_proj.weight"],
+                                                 o["mlp.gate_proj.weight"], o["mlp.down_proj.weight"],
+                                                 o["input_layernorm.weight"],
+                                                 o["post_attention_layernorm.weight"]))
+        self.emb = self.by_name["embed.embed_tokens.weight"][1]
+        self.normf = self.by_name["head.norm.weight"][1]
+        self.lm = self.by_name["head.lm_head.weight"][1]
+
+
+def _rebind(module: nn.Module, prefix_map, flat: torch.Tensor, layout_by_name, prefix: str) -> None:
+    """Point every parameter of ``module`` at its slice of ``flat`` (copying values)."""
+    for name, p in module.named_parameters():
+        shape, off, n = layout_by_name[prefix + name]
+        view = flat[off:off + n].view(shape)
+        view.copy_(p.data)
+        p.data = view
+
+
+class FusedExecutor:
+    def __init__(self, engine):
+        self.e = engine
+        cfg, dl = engine.config, engine.diloco
+        if cfg.tie_word_embeddings:
+            raise ValueError("the fused executor does not support tie_word_embeddings; "
+                             "use ExecOptions(fused=False)")
+        bb = cfg.backbone
+        if bb.head_dim != 64:
+            raise ValueError("the fused executor's attention kernel needs head_dim 64")
+        if bb.hidden_size % 128:
+            raise ValueError("the fused executor needs hidden_size % 128 == 0")
+        self.dev = engine.device
+        self.topo = engine.topology
+        self.paths: list[Path] = list(engine.backend.owned_paths())
+        self.G = len(self.paths)
+        if self.G == 0:
+            raise ValueError("no owned paths")
+        self.bb = bb
+        self.eps = bb.rms_norm_eps
+        self.opt8 = bool(getattr(dl, "optim_8bit", False))
+
+        # -- per-path models (views into the flat arenas) ------------------------------
+        pms = [build_path_model(cfg, p, engine.bank, deepcopy=True).to(self.dev) for p in self.paths]
+        self.layout = PathLayout(pms[0], cfg)
+        P, G = self.layout.P, self.G
+        self.P = P
+        self.W32 = torch.zeros(G, P, device=self.dev, dtype=torch.float32)
+        self.W16 = torch.zeros(G, P, device=self.dev, dtype=torch.bfloat16)
+        self.GRAD = torch.zeros(G, P, device=self.dev, dtype=torch.float32)
+        if self.opt8:
+            nb = P // ALIGN
+            self.MQ = torch.zeros(G * nb, ALIGN, device=self.dev, dtype=torch.int8)
+            self.MABS = torch.zeros(G * nb, device=self.dev)
+            self.VQ = torch.zeros(G * nb, ALIGN, device=self.dev, dtype=torch.uint8)
+            self.VLO = torch.zeros(G * nb, device=self.dev)
+            self.VSC = torch.zeros(G * nb, device=self.dev)
+        else:
+            self.MOM1 = torch.zeros(G, P, device=self.dev, dtype=torch.float32)
+            self.MOM2 = torch.zeros(G, P, device=self.dev, dtype=torch.float32)
+        for g, pm in enumerate(pms):
+            _rebind(pm, None, self.W32[g], self.layout.by_name, "")
+        self.W16.copy_(self.W32)
+        self.pms = dict(zip(self.paths, pms))
+        if engine.materialize == "eager":
+            engine.path_models.update(self.pms)
+        self.steps_taken = [0] * G
+        self._inner_opts: dict[Path, torch.optim.Optimizer] = {}
+
+        # -- global bank as flat buffers -------------------------------------------
+        self.glob: dict[str, torch.Tensor] = {}
+        self.mom: dict[str, torch.Tensor] = {}
+        for key, mod in engine.bank.items():
+            n = self._region_size(key)
+            buf = torch.zeros(n, device=self.dev, dtype=torch.float32)
+            self._rebind_bank(key, mod, buf)
+            self.glob[key] = buf
+            if not is_private_key(key):
+                self.mom[key] = torch.zeros(n, device=self.dev, dtype=torch.float32)
+        self.outer_steps = 0
+        self._plan: OuterPlan | None = None
+        self._plan_weights = None
+
+        # -- step buffers are sized on the first round ---------------------------------
+        self._shape = None
+        self._graph = None
+        self._warm = False
+
+    # ------------------------------------------------------------------ layout helpers
+    # Every path has the same segment structure, hence the same flat layout: module
+    # key -> parameter-name prefix -> one region, identical on all paths.
+    def _prefix(self, key: str) -> str:
+        role = self.topo.role_of_key(key)
+        if role in ("embed", "head"):
+            return role + "."
+        return f"body.{self.topo._segment_index_of_key(key) - 1}."
+
+    def _entries(self, key: str):
+        pre = self._prefix(key)
+        return pre, [(n, s, o, k) for n, s, o, k in self.layout.entries if n.startswith(pre)]
+
+    def _region(self, key: str) -> tuple[int, int]:
+        _, ents = self._entries(key)
+        return min(o for _, _, o, _ in ents), max(o + _ru(k) for _, _, o, k in ents)
+
+    def _rel_entries(self, key: str):
+        """(name within the module, shape, offset from the region start, numel)."""
+        pre, ents = self._entries(key)
+        start = self._region(key)[0]
+        return [(n[len(pre):], s, o - start, k) for n, s, o, k in ents]
+
+    def _region_size(self, key: str) -> int:
+        a, b = self._region(key)
+        return b - a
+
+    def _local_region(self, g: int, key: str) -> tuple[int, int]:
+        return self._region(key)
+
+    def _rebind_bank(self, key: str, mod: nn.Module, buf: torch.Tensor) -> None:
+        rel = {n: (s, o, k) for n, s, o, k in self._rel_entries(key)}
+        for name, p in mod.named_parameters():
+            s, o, k = rel[name]
+            view = buf[o:o + k].view(s)
+            view.copy_(p.data)
+            p.data = view
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc(self, B: int, S: int, steps: int) -> None:
+        bb, G, dev = self.bb, self.G, self.dev
+        H, Fd, V = bb.hidden_size, bb.intermediate_size, bb.vocab_size
+        nh, nkv = bb.num_attention_heads, bb.kv_heads()
+        C = (nh + 2 * nkv) * 64
+        M = B * S
+        L = len(self.layout.layers)
+        if S % 64:
+            raise ValueError("fused executor needs sequence_length % 64 == 0")
+        if V % 8:
+            raise ValueError("fused executor needs vocab_size % 8 == 0")
+        f32, b16 = torch.float32, torch.bfloat16
+        z = lambda *s, dt=f32: torch.zeros(*s, device=dev, dtype=dt)  # noqa: E731
+        self.B, self.S, self.M, self.C, self.L = B, S, M, C, L
+        self.T = 2 * ((V + 127) // 128)  # (max, sum exp) partials: two per 128-column tile
+        self.X = z(L + 1, G, M, H)
+        self.HR = z(max(L, 1), G, M, H)
+        self.XN1 = z(max(L, 1), G, M, H, dt=b16)
+        self.XN2 = z(max(L, 1), G, M, H, dt=b16)
+        self.RS1 = z(max(L, 1), G, M)
+        self.RS2 = z(max(L, 1), G, M)
+        self.QKV = z(max(L, 1), G, M, C, dt=b16)
+        self.O = z(max(L, 1), G, M, H, dt=b16)
+        self.LSEA = z(max(L, 1), G * B, nh, S)
+        self.GU = z(max(L, 1), G, M, 2 * Fd, dt=b16)
+        self.ACT = z(max(L, 1), G, M, Fd, dt=b16)
+        self.XNF = z(G, M, H, dt=b16)
+        self.RSF = z(G, M)
+        self.LOGITS = z(G, M, V, dt=b16)
+        self.PART = z(G, M, self.T, 2)
+        self.LSEC = z(G, M)
+        self.ROWLOSS = z(G, M)
+        self.LOSSSUM = z(G)
+        self.INVCNT = z(G)
+        self.DX = z(G, M, H)
+        self.DX16 = z(G, M, H, dt=b16)
+        self.DXN = z(G, M, H)
+        self.DGU = z(G, M, 2 * Fd, dt=b16)
+        self.DOUT = z(G, M, H, dt=b16)
+        self.DQKV = z(G, M, C, dt=b16)
+        self.DELTA = z(G * B, nh, S)
+        self.NORMWORK = z(G * ((M + 31) // 32) * H)
+        self.CLIPWORK = z(G * ((self.P + (1 << 16) - 1) // (1 << 16)))
+        self.COEF = z(G)
+        self.GNORM = z(G)
+        self.IDS = z(steps, G, M, dt=torch.int32)
+        self.LABELS = z(steps, G, M, dt=torch.int32)
+        self.SCHED = z(steps, G, 4)
+        self.LOSSES = z(steps, G)
+        self.ids_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
+        self.labels_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
+        self.sched_host = torch.zeros(steps, G, 4, dtype=torch.float32).pin_memory()
+        self.loss_host = torch.zeros(G, dtype=torch.float32).pin_memory()
+        self.cos, self.sin = rope_cos_sin(64, bb.rope_theta, S, dev)
+        self.err = err_word(dev)
+        self._shape = (B, S, steps)
+        self._graph = None
+        self._warm = False
+
+    # ------------------------------------------------------------------ GEMM helper
+    def _bn(self, M: int, N: int) -> int:
+        tiles128 = self.G * ((M + 127) // 128) * ((N + 127) // 128)
+        return 128 if tiles128 >= 148 else 64
+
+    def _gemm(self, A, lda, sa, amn, B, ldb, sb, bmn, C, ldc, sc, M, N, K, epi, bn=None, **kw):
+        from ..ops.gemm import EPI
+
+        ext().gemm_bf16(A, lda, sa, amn, B, ldb, sb, bmn, C, ldc, sc, M, N, K, self.G, EPI[epi],
+                        bn or self._bn(M, N), kw.get("R"), kw.get("ldr", 0), kw.get("sr", 0),
+                        kw.get("aux"), kw.get("ldx", 0), kw.get("sx", 0), kw.get("part"),
+                        kw.get("beta", 0.0), kw.get("f_half", 0), self.err, 0)
+
+    # ------------------------------------------------------------------ one inner step
+    def _step(self, s: int) -> None:
+        X_ = ext()
+        bb, G, P = self.bb, self.G, self.P
+        H, Fd, V = bb.hidden_size, bb.intermediate_size, bb.vocab_size
+        nh, nkv = bb.num_attention_heads, bb.kv_heads()
+        M, C, S, B = self.M, self.C, self.S, self.B
+        w32, w16, gr = self.W32.view(-1), self.W16.view(-1), self.GRAD.view(-1)
+        lay = self.layout
+        ids, labels = self.IDS[s], self.LABELS[s]
+        MH, MC, MF, MF2 = M * H, M * C, M * Fd, M * 2 * Fd
+
+        # ---------------- forward
+        X_.embedding_fwd(ids, w32[lay.emb:], P, self.X[0], M, H, G, V)
+        for l, lo in enumerate(lay.layers):
+            X_.rmsnorm_fwd(self.X[l], MH, w32[lo.ln1:], P, self.XN1[l], MH, self.RS1[l], M, H, G, self.eps)
+            self._gemm(self.XN1[l], H, MH, False, w16[lo.qkv:], H, P, False, self.QKV[l], C, MC, M, C, H, "bf16")
+            X_.attention_fwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l])
+            self._gemm(self.O[l], H, MH, False, w16[lo.o:], H, P, False, self.HR[l], H, MH, M, H, H, "resid",
+                       R=self.X[l], ldr=H, sr=MH)
+            X_.rmsnorm_fwd(self.HR[l], MH, w32[lo.ln2:], P, self.XN2[l], MH, self.RS2[l], M, H, G, self.eps)
+            self._gemm(self.XN2[l], H, MH, False, w16[lo.gu:], H, P, False, self.ACT[l], Fd, MF, M, 2 * Fd, H,
+                       "swiglu", bn=128, aux=self.GU[l], ldx=2 * Fd, sx=MF2, f_half=Fd)
+            self._gemm(self.ACT[l], Fd, MF, False, w16[lo.down:], Fd, P, False, self.X[l + 1], H, MH, M, H, Fd,
+                       "resid", R=self.HR[l], ldr=H, sr=MH)
+        L = self.L
+        X_.rmsnorm_fwd(self.X[L], MH, w32[lay.normf:], P, self.XNF, MH, self.RSF, M, H, G, self.eps)
+        self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "logits",
+                   bn=128, part=self.PART)
+        X_.ce_forward(self.PART, self.T, self.LOGITS, V, M * V, labels, M, G, self.LSEC, self.ROWLOSS,
+                      self.LOSSSUM, self.INVCNT, self.LOSSES[s])
+        # ---------------- backward
+        X_.ce_backward(self.LOGITS, V, M * V, self.LSEC, labels, self.INVCNT, M, V, G)
+        self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
+        self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32")
+        X_.rmsnorm_bwd(self.X[L], MH, w32[lay.normf:], P, self.RSF, self.DXN, MH, None, self.DX, MH, self.DX16,
+                       gr[lay.normf:], P, self.NORMWORK, M, H, G, 0.0)
+        for l in range(L - 1, -1, -1):
+            lo = lay.layers[l]
+            self._gemm(self.DX16, H, MH, False, w16[lo.down:], Fd, P, True, self.DGU, 2 * Fd, MF2, M, Fd, H,
+                       "swiglu_bwd", aux=self.GU[l], ldx=2 * Fd, sx=MF2, f_half=Fd)
+            self._gemm(self.DX16, H, MH, True, self.ACT[l], Fd, MF, True, gr[lo.down:], Fd, P, H, Fd, M, "f32")
+            self._gemm(self.DGU, 2 * Fd, MF2, False, w16[lo.gu:], H, P, True, self.DXN, H, MH, M, H, 2 * Fd, "f32")
+            self._gemm(self.DGU, 2 * Fd, MF2, True, self.XN2[l], H, MH, True, gr[lo.gu:], H, P, 2 * Fd, H, M,
+                       "f32")
+            X_.rmsnorm_bwd(self.HR[l], MH, w32[lo.ln2:], P, self.RS2[l], self.DXN, MH, self.DX, self.DX, MH,
+                           self.DX16, gr[lo.ln2:], P, self.NORMWORK, M, H, G, 0.0)
+            self._gemm(self.DX16, H, MH, False, w16[lo.o:], H, P, True, self.DOUT, H, MH, M, H, H, "bf16")
+            self._gemm(self.DX16, H, MH, True, self.O[l], H, MH, True, gr[lo.o:], H, P, H, H, M, "f32")
+            X_.attention_bwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l],
+                             self.DOUT, self.DELTA, self.DQKV)
+            self._gemm(self.DQKV, C, MC, False, w16[lo.qkv:], H, P, True, self.DXN, H, MH, M, H, C, "f32")
+            self._gemm(self.DQKV, C, MC, True, self.XN1[l], H, MH, True, gr[lo.qkv:], H, P, C, H, M, "f32")
+            X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[l], self.DXN, MH, self.DX, self.DX, MH,
+                           self.DX16, gr[lo.ln1:], P, self.NORMWORK, M, H, G, 0.0)
+        emb_n = bb.vocab_size * H
+        self.GRAD[:, lay.emb:lay.emb + emb_n].zero_()
+        X_.embedding_bwd(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V)
+        # ---------------- optimizer
+        clip = self.e.diloco.inner_grad_clip
+        X_.grad_clip_coef(self.GRAD, P, P, G, float(clip) if clip is not None else 0.0, self.CLIPWORK,
+                          self.COEF, self.GNORM)
+        dl = self.e.diloco
+        b1, b2 = dl.inner_betas
+        if self.opt8:
+            X_.adam8bit_step(self.W32.view(-1), self.GRAD.view(-1), self.MQ, self.MABS, self.VQ, self.VLO,
+                             self.VSC, self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay,
+                             False, self.W16.view(-1), P // ALIGN)
+        else:
+            X_.adamw_step(self.W32, self.GRAD, self.MOM1, self.MOM2, self.W16, P, P, P, G, self.COEF,
+                          self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay)
+
+    # ------------------------------------------------------------------ round inputs
+    def _prepare(self, corpus, batch_size: int, round_idx: int):
+        e = self.e
+        steps = e.diloco.inner_steps
+        S = corpus.seq_len
+        shards, active = [], []
+        for path in self.paths:
+            sh = corpus.shard(self.topo.path_index(path))
+            shards.append(sh)
+            active.append(sh.size(0) > 0)
+        B = batch_size
+        if self._shape != (B, S, steps):
+            self._alloc(B, S, steps)
+        ids = self.ids_host.view(steps, self.G, B, S)
+        lab = self.labels_host.view(steps, self.G, B, S)
+        ids.zero_()
+        lab.fill_(-100)
+        from .loop import batch_indices
+
+        total = e.total_rounds * steps if e.total_rounds else None
+        dl = e.diloco
+        b1, b2 = dl.inner_betas
+        sched = self.sched_host
+        sched.zero_()
+        for g, (sh, act) in enumerate(zip(shards, active)):
+            if not act:
+                continue
+            idx = batch_indices(sh.size(0), batch_size, steps, e._gen)
+            for i, rows in enumerate(idx):
+                seqs = sh[rows].to(torch.int32)
+                bs = seqs.size(0)
+                ids[i, g, :bs] = seqs
+                lab[i, g, :bs, :-1] = seqs[:, 1:]
+            for i in range(steps):
+                t = self.steps_taken[g] + i + 1
+                lr = inner_lr_at(round_idx * steps + i, total, dl)
+                # active flag 2.0 marks a path's very first optimizer step (8-bit Adam
+                # then treats the second moment as zero, like the reference)
+                sched[i, g] = torch.tensor([lr, lr / (1 - b1 ** t), math.sqrt(1 - b2 ** t),
+                                            2.0 if t == 1 else 1.0])
+        return active
+
+    def _upload(self) -> None:
+        self.IDS.copy_(self.ids_host, non_blocking=True)
+        self.LABELS.copy_(self.labels_host, non_blocking=True)
+        self.SCHED.copy_(self.sched_host, non_blocking=True)
+
+    # ------------------------------------------------------------------ round
+    def run_round(self, corpus, batch_size: int, round_idx: int):
+        e = self.e
+        steps = e.diloco.inner_steps
+        active = self._prepare(corpus, batch_size, round_idx)
+        self._upload()
+        self._run_inner(steps)
+        for g, a in enumerate(active):
+            if a:
+                self.steps_taken[g] += steps
+        norms = self._outer(corpus, active)
+        self.loss_host.copy_(self.LOSSES[steps - 1], non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        check_errors(self.dev)
+        losses = {p: float(self.loss_host[g]) for g, p in enumerate(self.paths) if active[g]}
+        return losses, norms
+
+    def _run_inner(self, steps: int) -> None:
+        """Run a round's inner steps: eagerly on the first round (initialises kernel
+        attributes), then from one captured CUDA graph."""
+        if not self.e.exec.cuda_graphs:
+            for s in range(steps):
+                self._step(s)
+            return
+        if self._graph is None:
+            if not self._warm:
+                for s in range(steps):
+                    self._step(s)
+                self._warm = True
+                return
+            torch.cuda.synchronize(self.dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for s in range(steps):
+                    self._step(s)
+            self._graph = graph
+        self._graph.replay()
+
+    # ------------------------------------------------------------------ outer step
+    def _build_plan(self, corpus, active) -> OuterPlan:
+        e = self.e
+        segs = []
+        for key in self.topo.module_keys():
+            if key not in e.bank:
+                continue
+            users = [g for g, p in enumerate(self.paths) if key in self.topo.path_module_keys(p)]
+            loc32, loc16, w = [], [], []
+            for g in users:
+                a, b = self._local_region(g, key)
+                loc32.append(self.W32[g, a:b])
+                loc16.append(self.W16[g, a:b])
+                pidx = self.topo.path_index(self.paths[g])
+                w.append(e._outer_weight(key, pidx, corpus) if active[g] else 0.0)
+            if is_private_key(key):
+                if users:
+                    segs.append(Segment(key, self.glob[key], None, loc32[:1], [None], [1.0], mode=MODE_COPY))
+                continue
+            den = sum(w)
+            inv = 1.0 / max(den, 1e-12) if e.diloco.normalize_outer_delta else 1.0
+            segs.append(Segment(key, self.glob[key], self.mom[key], loc32, loc16, w, MODE_OUTER,
+                                e.outer_scale(key), inv))
+        plan = OuterPlan(segs, self.dev)
+        plan.build()
+        return plan
+
+    def _outer(self, corpus, active):
+        e = self.e
+        wkey = (id(corpus), tuple(active))
+        if self._plan is None or self._plan_weights != wkey:
+            self._plan = self._build_plan(corpus, active)
+            self._plan_weights = wkey
+        backend = e.backend
+        dl = e.diloco
+        if getattr(backend, "world_size", 1) > 1 and hasattr(backend, "fused_outer_step"):
+            backend.fused_outer_step(self, self._plan, first=self.outer_steps == 0)
+        elif getattr(backend, "world_size", 1) > 1:
+            raise NotImplementedError("multi-rank fused outer step needs a backend with fused_outer_step")
+        else:
+            self._plan.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first=self.outer_steps == 0)
+        self.outer_steps += 1
+        norms = self._plan.delta_norms()
+        return [v for k, v in norms.items() if not is_private_key(k)]
+
+    # ------------------------------------------------------------------ benchmarking hooks
+    def device_round(self) -> None:
+        """Replay one round's device work (inner-step graph + outer step) on the inputs
+        already resident on the device: no host preparation, copies or reads."""
+        self._run_inner(self.e.diloco.inner_steps)
+        dl = self.e.diloco
+        if getattr(self.e.backend, "world_size", 1) > 1:
+            self.e.backend.fused_outer_step(self, self._plan, first=False)
+        else:
+            self._plan.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first=False)
+
+    def launches_per_round(self) -> int:
+        """Kernels of this package launched per round (inner steps + outer step)."""
+        per_step = 14 + 22 * self.L
+        outer = getattr(self.e.backend, "outer_launches", 1) if getattr(self.e.backend, "world_size", 1) > 1 else 1
+        return self.e.diloco.inner_steps * per_step + outer
+
+    def h2d_bytes_per_round(self) -> int:
+        return int(self.IDS.numel() * 4 + self.LABELS.numel() * 4 + self.SCHED.numel() * 4)
+
+    def d2h_bytes_per_round(self) -> int:
+        chunks = self._plan.total_chunks if self._plan is not None else 0
+        return int(self.G * 4 + 4 + chunks * 4)
+
+    # ------------------------------------------------------------------ API glue
+    def path_model(self, path: Path) -> nn.Module:
+        return self.pms[path]
+
+    def sync_bank_views(self) -> None:
+        """Bank parameters already alias the flat buffers; nothing to copy."""
+        torch.cuda.current_stream(self.dev).synchronize()
+
+    def _inner_opt(self, path: Path) -> torch.optim.Optimizer:
+        if path not in self._inner_opts:
+            self._inner_opts[path] = make_inner_optimizer(self.pms[path], self.e.diloco)
+        return self._inner_opts[path]
+
+    def inner_state_dicts(self) -> dict[Path, dict]:
+        from .loop import _opt_state_cpu
+
+        out = {}
+        for g, path in enumerate(self.paths):
+            opt = self._inner_opt(path)
+            opt.state.clear()
+            t = self.steps_taken[g]
+            if t > 0:
+                for name, p in self.pms[path].named_parameters():
+                    s, o, n = self.layout.by_name[name]
+                    if self.opt8:
+                        nb0, nbn = o // ALIGN, (n + ALIGN - 1) // ALIGN
+                        base = g * (self.P // ALIGN)
+                        sl = slice(base + nb0, base + nb0 + nbn)
+                        opt.state[p] = {"step": t, "m_q": self.MQ[sl], "m_absmax": self.MABS[sl],
+                                        "v_q": self.VQ[sl], "v_lo": self.VLO[sl], "v_scale": self.VSC[sl]}
+                    else:
+                        opt.state[p] = {"step": torch.tensor(float(t)),
+                                        "exp_avg": self.MOM1[g, o:o + n].view(s),
+                                        "exp_avg_sq": self.MOM2[g, o:o + n].view(s)}
+            out[path] = _opt_state_cpu(opt.state_dict())
+            opt.state.clear()
+        return out
+
+    def outer_state_dict(self) -> dict:
+        from .loop import _opt_state_cpu
+
+        opt = self.e.outer_opt
+        opt.state.clear()
+        if self.outer_steps > 0:
+            for key, mod in self.e.bank.items():
+                if is_private_key(key):
+                    continue
+                rel = {n: (s, o, k) for n, s, o, k in self._rel_entries(key)}
+                for name, p in mod.named_parameters():
+                    s, o, k = rel[name]
+                    opt.state[p] = {"momentum_buffer": self.mom[key][o:o + k].view(s)}
+        sd = _opt_state_cpu(opt.state_dict())
+        opt.state.clear()
+        return sd
+
+    @torch.no_grad()
+    def load_states(self, outer_sd: dict, inner: dict) -> None:
+        e = self.e
+        opt = e.outer_opt
+        opt.load_state_dict(outer_sd)
+        self.outer_steps = 0
+        for key, mod in e.bank.items():
+            if is_private_key(key):
+                continue
+            rel = {n: (s, o, k) for n, s, o, k in self._rel_entries(key)}
+            for name, p in mod.named_parameters():
+                st = opt.state.get(p, {})
+                if "momentum_buffer" in st and st["momentum_buffer"] is not None:
+                    s, o, k = rel[name]
+                    self.mom[key][o:o + k].copy_(st["momentum_buffer"].reshape(-1))
+                    self.outer_steps = 1
+        opt.state.clear()
+        # working copies = bank for shared keys; private keys = bank (authoritative)
+        for g, path in enumerate(self.paths):
+            for key in self.pms[path].modules_by_key():
+                if key in self.glob:
+                    a, b = self._local_region(g, key)
+                    self.W32[g, a:b].copy_(self.glob[key])
+        self.W16.copy_(self.W32)
+        if not self.opt8:
+            self.MOM1.zero_()
+            self.MOM2.zero_()
+        for g, path in enumerate(self.paths):
+            self.steps_taken[g] = 0
+            if path not in inner:
+                continue
+            iopt = self._inner_opt(path)
+            iopt.load_state_dict(inner[path])
+            for name, p in self.pms[path].named_parameters():
+                st = iopt.state.get(p)
+                if not st:
+                    continue
+                s, o, n = self.layout.by_name[name]
+                step = st["step"]
+                self.steps_taken[g] = int(step.item() if torch.is_tensor(step) else step)
+                if self.opt8:
+                    nb0, nbn = o // ALIGN, (n + ALIGN - 1) // ALIGN
+                    base = g * (self.P // ALIGN)
+                    sl = slice(base + nb0, base + nb0 + nbn)
+                    self.MQ[sl].copy_(st["m_q"])
+                    self.MABS[sl].copy_(st["m_absmax"])
+                    self.VQ[sl].copy_(st["v_q"])
+                    self.VLO[sl].copy_(st["v_lo"])
+                    self.VSC[sl].copy_(st["v_scale"])
+                else:
+                    self.MOM1[g, o:o + n].copy_(st["exp_avg"].reshape(-1))
+                    self.MOM2[g, o:o + n].copy_(st["exp_avg_sq"].reshape(-1))
+            iopt.state.clear()
+        self._graph = None
+        self._warm = False
+
+
+__all__ = ["FusedExecutor", "PathLayout", "Adam8bit"]

@@ -1,0 +1,131 @@
+"""The fused B200 executor against the module executor (CPU oracle) and itself."""
+
+import pytest
+import torch
+
+from opendipaco_b200 import (BackboneConfig, DiLoCoConfig, DiPaCoConfig, DiPaCoEngine, ExecOptions, LocalBackend,
+                             load_checkpoint, save_checkpoint)
+from opendipaco_b200.data import ShardedCorpus, zipf_documents
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg(embedding="shared", levels=(2, 2), layers=(1, 1), kv=None):
+    bb = BackboneConfig(vocab_size=512, hidden_size=128, num_attention_heads=2, num_key_value_heads=kv,
+                        intermediate_size=256, layers_per_level=list(layers), max_position_embeddings=128)
+    return DiPaCoConfig(backbone=bb, level_sizes=list(levels), sequence_length=64, embedding=embedding)
+
+
+def _corpus(cfg, n=160):
+    docs = zipf_documents(vocab_size=512, num_documents=n, min_len=64, max_len=400, seed=1)
+    a = torch.arange(len(docs)) % cfg.num_paths
+    return ShardedCorpus.from_assignments(docs, a, cfg.num_paths, cfg.sequence_length)
+
+
+def _engine(cfg, device, graphs=True, fused=None, **dl):
+    d = dict(inner_steps=3, inner_lr=1e-3, inner_autocast=True)
+    d.update(dl)
+    return DiPaCoEngine(cfg, DiLoCoConfig(**d), LocalBackend(cfg.build_topology()), device=device, seed=0,
+                        exec_options=ExecOptions(fused=fused, cuda_graphs=graphs))
+
+
+def _bank_maxdiff(a, b):
+    m = 0.0
+    for k in a.bank:
+        for x, y in zip(a.bank[k].state_dict().values(), b.bank[k].state_dict().values()):
+            m = max(m, (x.float().cpu() - y.float().cpu()).abs().max().item())
+    return m
+
+
+def test_fused_matches_cpu_oracle():
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    gpu = _engine(cfg, "cuda")
+    assert gpu.fused
+    cpu = _engine(cfg, "cpu")
+    hg = gpu.fit(corpus, 3, 4, log_every=0)
+    hc = cpu.fit(corpus, 3, 4, log_every=0)
+    for a, b in zip(hg, hc):
+        for p in a.per_path_loss:
+            assert abs(a.per_path_loss[p] - b.per_path_loss[p]) < 3e-2 * b.per_path_loss[p], (p, a, b)
+    assert _bank_maxdiff(gpu, cpu) < 1.5e-2
+
+
+def test_graph_replay_equals_eager_bitwise():
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    a, b = _engine(cfg, "cuda", graphs=True), _engine(cfg, "cuda", graphs=False)
+    ha = a.fit(corpus, 4, 4, log_every=0)
+    hb = b.fit(corpus, 4, 4, log_every=0)
+    assert [m.per_path_loss for m in ha] == [m.per_path_loss for m in hb]
+    assert _bank_maxdiff(a, b) == 0.0
+
+
+def test_fused_resume_bit_for_bit(tmp_path):
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    ref = _engine(cfg, "cuda")
+    ref.fit(corpus, 4, 4, log_every=0, total_rounds=4)
+    x = _engine(cfg, "cuda")
+    x.fit(corpus, 2, 4, log_every=0, total_rounds=4)
+    save_checkpoint(x, tmp_path / "c")
+    y = _engine(cfg, "cuda")
+    load_checkpoint(y, tmp_path / "c")
+    y.fit(corpus, 2, 4, log_every=0)
+    assert _bank_maxdiff(ref, y) == 0.0
+
+
+def test_fused_checkpoint_loads_into_module_executor(tmp_path):
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    g = _engine(cfg, "cuda")
+    g.fit(corpus, 2, 4, log_every=0)
+    save_checkpoint(g, tmp_path / "c")
+    c = _engine(cfg, "cpu")
+    load_checkpoint(c, tmp_path / "c")
+    assert _bank_maxdiff(g, c) == 0.0
+    st = c.inner_opts[(0, 0)].state_dict()["state"]
+    assert st and float(next(iter(st.values()))["step"]) == 6
+
+
+def test_fused_private_embedding_and_8bit():
+    cfg = _cfg(embedding="private")
+    corpus = _corpus(cfg)
+    gpu = _engine(cfg, "cuda", optim_8bit=True)
+    cpu = _engine(cfg, "cpu", optim_8bit=True)
+    hg = gpu.fit(corpus, 2, 4, log_every=0)
+    hc = cpu.fit(corpus, 2, 4, log_every=0)
+    for a, b in zip(hg, hc):
+        for p in a.per_path_loss:
+            assert abs(a.per_path_loss[p] - b.per_path_loss[p]) < 3e-2 * b.per_path_loss[p]
+    assert not torch.allclose(gpu.bank["embed.p0"].embed_tokens.weight, gpu.bank["embed.p3"].embed_tokens.weight)
+    assert _bank_maxdiff(gpu, cpu) < 1e-2
+
+
+def test_fused_gqa_and_deeper():
+    cfg = _cfg(layers=(2, 1), kv=1, levels=(3, 2))
+    corpus = _corpus(cfg, n=240)
+    gpu, cpu = _engine(cfg, "cuda"), _engine(cfg, "cpu")
+    hg, hc = gpu.fit(corpus, 2, 4, log_every=0), cpu.fit(corpus, 2, 4, log_every=0)
+    for p in hg[-1].per_path_loss:
+        assert abs(hg[-1].per_path_loss[p] - hc[-1].per_path_loss[p]) < 3e-2 * hc[-1].per_path_loss[p]
+
+
+def test_module_forward_on_cuda_kernels_matches_cpu():
+    from opendipaco_b200.models import build_path_model
+    from opendipaco_b200.models.path import build_module_bank
+
+    cfg = _cfg()
+    torch.manual_seed(0)
+    bank = build_module_bank(cfg)
+    pm_c = build_path_model(cfg, (0, 1), bank, deepcopy=True)
+    pm_g = build_path_model(cfg, (0, 1), bank, deepcopy=True).cuda()
+    ids = torch.randint(0, 512, (3, 96))
+    lc, loss_c = pm_c(ids, labels=ids)
+    lg, loss_g = pm_g(ids.cuda(), labels=ids.cuda())
+    assert abs(loss_c.item() - loss_g.item()) < 2e-2 * loss_c.item()
+    loss_g.backward()
+    loss_c.backward()
+    gc = pm_c.head.lm_head.weight.grad
+    gg = pm_g.head.lm_head.weight.grad.cpu()
+    assert (gc - gg).abs().max() < 5e-2 * gc.abs().max()

@@ -122,7 +122,7 @@ def test_logits_and_cross_entropy():
     M, H, V = 384, 384, 32000
     x = _bf(M, H, seed=15)
     w = _bf(V, H, scale=0.05, seed=16)
-    T = V // 128
+    T = 2 * (V // 128)
     logits = torch.empty(M, V, device=DEV, dtype=torch.bfloat16)
     part = torch.empty(M, T, 2, device=DEV)
     gemm(x, H, 0, False, w, H, 0, False, logits, V, 0, M, V, H, epi="logits", bn=128, part=part)
@@ -228,7 +228,7 @@ def test_adamw_matches_torch():
             torch.nn.utils.clip_grad_norm_([ref[i]], 1.0)
             opts[i].step()
         coef = clip_coef(g, P, P, G, 1.0)
-        adamw(p, g, m, v, p16, P, P, P, G, coef, sched_tensor(1e-3, 0.9, 0.95, step, DEV), 0.9, 0.95, 1e-8, 0.1)
+        adamw(p, g, m, v, p16, P, P, P, G, coef, sched_tensor(1e-3, 0.9, 0.95, step, DEV, groups=G), 0.9, 0.95, 1e-8, 0.1)
     _check_err()
     for i in range(G):
         _close(p[i], ref[i].detach(), 1e-5)
