@@ -39,6 +39,13 @@ void adam8bit_step(torch::Tensor p, torch::Tensor g, torch::Tensor mq, torch::Te
 void outer_step(torch::Tensor segs, int64_t nseg, torch::Tensor locals, int64_t total_chunks, double lr,
                 double momentum, bool nesterov, bool first, c10::optional<torch::Tensor> sq_part);
 int64_t outer_chunk_elems();
+void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks, torch::Tensor delta_ptrs,
+                        torch::Tensor glob_ptrs, torch::Tensor pads, torch::Tensor mom, int64_t rank, int64_t world,
+                        int64_t epoch, double lr, double m, bool nesterov, bool first, torch::Tensor sq_part,
+                        torch::Tensor err);
+void outer_nvlink_bcast(torch::Tensor cps, int64_t ncp, int64_t total_chunks, torch::Tensor pads, int64_t rank,
+                        int64_t world, int64_t epoch, torch::Tensor err);
+int64_t outer_nvlink_chunk_elems();
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opendipaco_b200 sm_100a kernels";
@@ -57,4 +64,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adam8bit_step", &adam8bit_step);
   m.def("outer_step", &outer_step);
   m.def("outer_chunk_elems", &outer_chunk_elems);
+  m.def("outer_nvlink_apply", &outer_nvlink_apply);
+  m.def("outer_nvlink_bcast", &outer_nvlink_bcast);
+  m.def("outer_nvlink_chunk_elems", &outer_nvlink_chunk_elems);
 }

@@ -1,0 +1,200 @@
+"""NVLink / NVSwitch backend: the DiLoCo outer step over peer memory, no NCCL.
+
+Placement and the generic ``global_reduce`` API are inherited from
+:class:`TorchDistBackend` (contiguous balanced path blocks, one NCCL subgroup per
+module key, used only off the hot path). The fused executor instead calls
+:meth:`NVLinkBackend.fused_outer_step` once per round, which runs three kernels:
+
+1. ACC (local, ``csrc/outer.cu``): this rank's weighted pseudo-gradient partial
+   ``sum_j w_j (global - local_j)`` for every shared key it owns, written into a
+   symmetric DELTA buffer (and private keys copied into the bank);
+2. APPLY (``csrc/outer_nvlink.cu``): cross-GPU barrier, then for the slice of every
+   shared key this rank owns: peer loads of all sharers' partials (rank order),
+   Nesterov on the momentum shard, peer stores of the new global into every
+   sharer's GLOB;
+3. BCAST: cross-GPU barrier, then the fresh globals are copied into the local
+   working copies (fp32 master + bf16).
+
+Buffers are allocated with ``torch.distributed._symmetric_memory`` (``empty`` +
+``rendezvous`` over the world group): the bank's GLOB, DELTA and momentum arenas
+(identical offsets on every rank: one region per module key in ``module_keys()``
+order) and a small flag pad for the epoch barriers. Device waits are bounded; a
+peer that never arrives makes the kernels record ``ERR_TIMEOUT_PEER`` and the host
+raises :class:`~opendipaco_b200.ops.KernelTimeout` after the round.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ...ops._ext import err_word, ext
+from ...ops.outer import MODE_ACC, MODE_COPY, MODE_OUTER
+from ...topology import is_private_key
+from .torch_dist import TorchDistBackend
+
+NVKEY = np.dtype([("off", "<i8"), ("s0", "<i8"), ("s1", "<i8"), ("chunk0", "<i8"), ("nsh", "<i4"),
+                  ("sh", "<i4", (8,)), ("scale", "<f4"), ("inv_den", "<f4"), ("pad", "<i4")])
+NVCOPY = np.dtype([("src", "<u8"), ("dst32", "<u8"), ("dst16", "<u8"), ("n", "<i8"), ("chunk0", "<i8")])
+assert NVKEY.itemsize == 80 and NVCOPY.itemsize == 40
+ALIGN = 256
+
+
+def _ru(n: int, a: int = ALIGN) -> int:
+    return (n + a - 1) // a * a
+
+
+class NVLinkBackend(TorchDistBackend):
+    outer_launches = 3
+
+    def __init__(self, topology, device: torch.device | None = None):
+        super().__init__(topology, device)
+        self._offs: dict[str, int] | None = None
+        self._tables = None
+        self._epoch = 0
+        self._sq_keys: list[tuple[str, int, int]] = []
+
+    # ------------------------------------------------------------------ arenas
+    def bank_arena(self, sizes: dict[str, int], device) -> tuple[dict, dict]:
+        """Symmetric GLOB / momentum arenas; returns per-key views for owned keys."""
+        import torch.distributed._symmetric_memory as symm
+
+        self._offs, off = {}, 0
+        for k in self.topology.module_keys():
+            self._offs[k] = off
+            off += _ru(sizes[k])
+        self._sizes = dict(sizes)
+        total = max(off, ALIGN)
+        group = dist.group.WORLD.group_name
+        self.dev = torch.device(device)
+
+        def sym(n, dtype):
+            t = symm.empty(n, dtype=dtype, device=self.dev)
+            t.zero_()
+            h = symm.rendezvous(t, group)
+            return t, h
+
+        self.GLOB, self._hg = sym(total, torch.float32)
+        self.DELTA, self._hd = sym(total, torch.float32)
+        self.MOM, self._hm = sym(total, torch.float32)
+        self.PAD, self._hp = sym(2 * self.world_size, torch.int32)
+        torch.cuda.synchronize(self.dev)
+        dist.barrier()
+        as_dev = lambda ptrs: torch.tensor(list(ptrs), dtype=torch.int64, device=self.dev)  # noqa: E731
+        self._gptrs = as_dev(self._hg.buffer_ptrs)
+        self._dptrs = as_dev(self._hd.buffer_ptrs)
+        self._pptrs = as_dev(self._hp.buffer_ptrs)
+        glob = {k: self.GLOB[o:o + sizes[k]] for k, o in self._offs.items() if self.owns_module(k)}
+        mom = {k: self.MOM[o:o + sizes[k]] for k, o in self._offs.items()
+               if self.owns_module(k) and not is_private_key(k)}
+        return glob, mom
+
+    # ------------------------------------------------------------------ slices
+    def slice_of(self, key: str) -> tuple[int, int]:
+        """[s0, s1) of ``key`` owned by this rank in the cross-GPU outer step."""
+        sh = self.sharing_ranks(key)
+        n = self._sizes[key]
+        per = _ru((n + len(sh) - 1) // len(sh), 4)
+        i = sh.index(self.rank)
+        return min(n, i * per), min(n, (i + 1) * per)
+
+    def _build(self, ex, plan) -> None:
+        chunk = int(ext().outer_nvlink_chunk_elems())
+        # ACC plan: outer segments write their partial into DELTA; private copies run too
+        for s in plan.segments:
+            if s.mode == MODE_OUTER:
+                s.delta = self.DELTA[self._offs[s.key]:self._offs[s.key] + s.glob.numel()]
+        acc = plan.with_mode(MODE_ACC)
+        copies = [s for s in plan.segments if s.mode == MODE_COPY]
+        if copies:
+            from ...ops.outer import OuterPlan
+
+            cplan = OuterPlan(copies, self.dev)
+            cplan.build()
+        else:
+            cplan = None
+        keys, cps, chunk0, c0 = [], [], 0, 0
+        self._sq_keys = []
+        for s in plan.segments:
+            if s.mode != MODE_OUTER:
+                continue
+            sh = self.sharing_ranks(s.key)
+            if len(sh) > 8:
+                raise ValueError("NVLink outer step supports at most 8 sharer GPUs per module")
+            s0, s1 = self.slice_of(s.key)
+            nch = (s1 - s0 + chunk - 1) // chunk if s1 > s0 else 0
+            rec = np.zeros(1, dtype=NVKEY)
+            rec["off"], rec["s0"], rec["s1"], rec["chunk0"], rec["nsh"] = self._offs[s.key], s0, s1, chunk0, len(sh)
+            rec["sh"][0, :len(sh)] = sh
+            rec["scale"], rec["inv_den"] = s.scale, s.inv_den
+            if nch:
+                keys.append(rec)
+                self._sq_keys.append((s.key, chunk0, nch))
+            chunk0 += nch
+            n = s.glob.numel()
+            for l32, l16 in zip(s.locals32, s.locals16):
+                cr = np.zeros(1, dtype=NVCOPY)
+                cr["src"], cr["dst32"], cr["dst16"], cr["n"], cr["chunk0"] = (
+                    s.glob.data_ptr(), l32.data_ptr(), l16.data_ptr(), n, c0)
+                cps.append(cr)
+                c0 += (n + chunk - 1) // chunk
+        key_arr = np.concatenate(keys) if keys else np.zeros(1, dtype=NVKEY)
+        cp_arr = np.concatenate(cps) if cps else np.zeros(1, dtype=NVCOPY)
+        to_dev = lambda a: torch.from_numpy(a.view(np.int64).copy()).to(self.dev)  # noqa: E731
+        self._tables = dict(plan_id=id(plan), acc=acc, cplan=cplan, keys=to_dev(key_arr), nkeys=len(keys),
+                            chunks=chunk0, cps=to_dev(cp_arr), ncp=len(cps), cchunks=c0,
+                            sq=torch.zeros(max(chunk0, 1), device=self.dev))
+        self._all_keys = [k for k in self.topology.module_keys() if not is_private_key(k)]
+
+    # ------------------------------------------------------------------ the round
+    def fused_outer_step(self, ex, plan, first: bool) -> None:
+        if self._tables is None or self._tables["plan_id"] != id(plan):
+            self._build(ex, plan)
+        t = self._tables
+        dl = ex.e.diloco
+        err = err_word(self.dev)
+        t["acc"].run(0.0, 0.0, False, False)
+        if t["cplan"] is not None:
+            t["cplan"].run(0.0, 0.0, False, False)
+        self._epoch += 1
+        ext().outer_nvlink_apply(t["keys"], t["nkeys"], t["chunks"], self._dptrs, self._gptrs, self._pptrs,
+                                 self.MOM, self.rank, self.world_size, self._epoch, dl.outer_lr,
+                                 dl.outer_momentum, dl.outer_nesterov, first, t["sq"], err)
+        ext().outer_nvlink_bcast(t["cps"], t["ncp"], t["cchunks"], self._pptrs, self.rank, self.world_size,
+                                 self._epoch, err)
+
+    def delta_norms(self) -> dict[str, float]:
+        """Per shared key ||delta||, summed over the key's slices on every rank."""
+        sq = self._tables["sq"].cpu() if self._tables else torch.zeros(1)
+        vec = torch.zeros(len(self._all_keys), dtype=torch.float64)
+        idx = {k: i for i, k in enumerate(self._all_keys)}
+        for k, c0, n in self._sq_keys:
+            vec[idx[k]] = sq[c0:c0 + n].double().sum()
+        v = vec.to(self.dev)
+        dist.all_reduce(v)
+        v = v.cpu()
+        return {k: float(v[idx[k]].sqrt()) for k in self._all_keys if self.owns_module(k)}
+
+    def gather_momentum(self, ex) -> None:
+        """Fill the non-owned slices of each owned key's momentum from its owners."""
+        torch.cuda.synchronize(self.dev)
+        dist.barrier()
+        for key, buf in ex.mom.items():
+            off = self._offs[key]
+            for r in self.sharing_ranks(key):
+                if r == self.rank:
+                    continue
+                peer = self._hm.get_buffer(r, (self.MOM.numel(),), torch.float32)
+                sh = self.sharing_ranks(key)
+                n = self._sizes[key]
+                per = _ru((n + len(sh) - 1) // len(sh), 4)
+                i = sh.index(r)
+                s0, s1 = min(n, i * per), min(n, (i + 1) * per)
+                if s1 > s0:
+                    buf[s0:s1].copy_(peer[off + s0:off + s1])
+        torch.cuda.synchronize(self.dev)
+        dist.barrier()
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.dev) if self._offs is not None else None

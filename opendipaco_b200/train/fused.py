@@ -161,13 +161,19 @@ class FusedExecutor:
         # -- global bank as flat buffers -------------------------------------------
         self.glob: dict[str, torch.Tensor] = {}
         self.mom: dict[str, torch.Tensor] = {}
+        arena = None
+        if hasattr(engine.backend, "bank_arena"):
+            # cross-GPU backends place the bank in peer-addressable (symmetric) memory
+            sizes = {k: self._region_size(k) for k in self.topo.module_keys()}
+            arena = engine.backend.bank_arena(sizes, self.dev)
         for key, mod in engine.bank.items():
             n = self._region_size(key)
-            buf = torch.zeros(n, device=self.dev, dtype=torch.float32)
+            buf = arena[0][key] if arena else torch.zeros(n, device=self.dev, dtype=torch.float32)
             self._rebind_bank(key, mod, buf)
             self.glob[key] = buf
             if not is_private_key(key):
-                self.mom[key] = torch.zeros(n, device=self.dev, dtype=torch.float32)
+                self.mom[key] = (arena[1][key] if arena else
+                                 torch.zeros(n, device=self.dev, dtype=torch.float32))
         self.outer_steps = 0
         self._plan: OuterPlan | None = None
         self._plan_weights = None
@@ -464,7 +470,12 @@ class FusedExecutor:
                 if users:
                     segs.append(Segment(key, self.glob[key], None, loc32[:1], [None], [1.0], mode=MODE_COPY))
                 continue
-            den = sum(w)
+            # the normaliser is global: every path through the key with a non-empty shard
+            den = 0.0
+            for p in self.topo.paths_through_module(key):
+                pi = self.topo.path_index(p)
+                if corpus.shard(pi).size(0) > 0:
+                    den += e._outer_weight(key, pi, corpus)
             inv = 1.0 / max(den, 1e-12) if e.diloco.normalize_outer_delta else 1.0
             segs.append(Segment(key, self.glob[key], self.mom[key], loc32, loc16, w, MODE_OUTER,
                                 e.outer_scale(key), inv))
@@ -480,14 +491,15 @@ class FusedExecutor:
             self._plan_weights = wkey
         backend = e.backend
         dl = e.diloco
-        if getattr(backend, "world_size", 1) > 1 and hasattr(backend, "fused_outer_step"):
+        if getattr(backend, "world_size", 1) > 1:
+            if not hasattr(backend, "fused_outer_step"):
+                raise NotImplementedError("multi-rank fused outer step needs a backend with fused_outer_step")
             backend.fused_outer_step(self, self._plan, first=self.outer_steps == 0)
-        elif getattr(backend, "world_size", 1) > 1:
-            raise NotImplementedError("multi-rank fused outer step needs a backend with fused_outer_step")
+            norms = backend.delta_norms()
         else:
             self._plan.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first=self.outer_steps == 0)
+            norms = self._plan.delta_norms()
         self.outer_steps += 1
-        norms = self._plan.delta_norms()
         return [v for k, v in norms.items() if not is_private_key(k)]
 
     # ------------------------------------------------------------------ benchmarking hooks
@@ -557,6 +569,8 @@ class FusedExecutor:
 
         opt = self.e.outer_opt
         opt.state.clear()
+        if self.outer_steps > 0 and hasattr(self.e.backend, "gather_momentum"):
+            self.e.backend.gather_momentum(self)
         if self.outer_steps > 0:
             for key, mod in self.e.bank.items():
                 if is_private_key(key):
