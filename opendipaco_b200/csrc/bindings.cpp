@@ -46,6 +46,13 @@ void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks,
 void outer_nvlink_bcast(torch::Tensor cps, int64_t ncp, int64_t total_chunks, torch::Tensor pads, int64_t rank,
                         int64_t world, int64_t epoch, torch::Tensor err);
 int64_t outer_nvlink_chunk_elems();
+std::vector<torch::Tensor> quant_int4(torch::Tensor x, bool want_resid);
+void dequant_int4(torch::Tensor packed, torch::Tensor scale, int64_t n, int64_t g, torch::Tensor out, double w,
+                  bool accumulate);
+std::vector<torch::Tensor> quant_int8(torch::Tensor x, bool want_resid);
+torch::Tensor robust_combine(torch::Tensor stack, int64_t mode);
+torch::Tensor bag_of_tokens(torch::Tensor ids, torch::Tensor offs, torch::Tensor proj);
+std::vector<torch::Tensor> kmeans_assign(torch::Tensor x, torch::Tensor c, int64_t topk, bool want_dist);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opendipaco_b200 sm_100a kernels";
@@ -67,4 +74,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("outer_nvlink_apply", &outer_nvlink_apply);
   m.def("outer_nvlink_bcast", &outer_nvlink_bcast);
   m.def("outer_nvlink_chunk_elems", &outer_nvlink_chunk_elems);
+  m.def("quant_int4", &quant_int4);
+  m.def("dequant_int4", &dequant_int4);
+  m.def("quant_int8", &quant_int8);
+  m.def("robust_combine", &robust_combine);
+  m.def("bag_of_tokens", &bag_of_tokens);
+  m.def("kmeans_assign", &kmeans_assign);
 }
