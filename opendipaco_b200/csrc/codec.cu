@@ -35,7 +35,7 @@ __global__ void quant_int4_kernel(const float* __restrict__ x, long long n, uint
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     q[i] = (int)fminf(fmaxf(rintf(v[i] / safe), -7.f), 7.f);
-    if (resid && e0 + i < n) resid[e0 + i] = v[i] - (float)q[i] * s;
+    if (resid && e0 + i < n) resid[e0 + i] = v[i] - __fmul_rn((float)q[i], s);  // no FMA: same rounding as the host
   }
   packed[grp * 64 + lane * 2] = (uint8_t)(((q[0] + 8) << 4) | (q[1] + 8));
   packed[grp * 64 + lane * 2 + 1] = (uint8_t)(((q[2] + 8) << 4) | (q[3] + 8));
@@ -85,7 +85,7 @@ __global__ void quant_int8_kernel(const float* __restrict__ x, long long n, cons
     int qi = 0;
     if (s != 0.f) qi = (int)fminf(fmaxf(rintf(v / s), -127.f), 127.f);
     q[i] = (int8_t)qi;
-    if (resid) resid[i] = s != 0.f ? v - (float)qi * s : v;
+    if (resid) resid[i] = s != 0.f ? v - __fmul_rn((float)qi, s) : v;  // no FMA: same rounding as the host
   }
 }
 
