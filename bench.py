@@ -125,6 +125,41 @@ def make_configs(pkg):
     return cfg, dl
 
 
+class _RefOuterTimer:
+    """CUDA-event timing of the reference engine's outer sync: wraps (at the instance
+    level, calling the originals unchanged) its backend's ``global_reduce`` and the outer
+    optimizer's ``step``; one round's sync runs from the first reduce to the end of step."""
+
+    def __init__(self, engine, dev):
+        self.dev, self.rounds, self._start = dev, [], None
+        reduce, step = engine.backend.global_reduce, engine.outer_opt.step
+
+        def timed_reduce(*a, **kw):
+            if self._start is None:
+                self._start = torch.cuda.Event(enable_timing=True)
+                self._start.record()
+            return reduce(*a, **kw)
+
+        def timed_step(*a, **kw):
+            out = step(*a, **kw)
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            if self._start is not None:
+                self.rounds.append((self._start, end))
+            self._start = None
+            return out
+
+        engine.backend.global_reduce = timed_reduce
+        engine.outer_opt.step = timed_step
+
+    def reset(self) -> None:
+        self.rounds = []
+
+    def mean_ms(self) -> float | None:
+        torch.cuda.synchronize(self.dev)
+        return sum(a.elapsed_time(b) for a, b in self.rounds) / len(self.rounds) if self.rounds else None
+
+
 def run(args) -> dict:
     rank, world, local = _rank_env()
     if world != args.gpus:
@@ -169,6 +204,7 @@ def run(args) -> dict:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
+    ref_outer = _RefOuterTimer(engine, dev) if args.impl == "reference" else None
     for _ in range(args.warmup):
         engine.fit(corpus, num_rounds=1, batch_size=B, log_every=0)
     barrier()
@@ -176,6 +212,7 @@ def run(args) -> dict:
     # -- kernel-only device time: inputs resident, graph replay + outer step ------------
     device_ms = None
     launches = None
+    outer_ms = None
     if args.impl != "reference":
         ex = engine._fused
         st = torch.cuda.current_stream(dev)
@@ -188,10 +225,20 @@ def run(args) -> dict:
         barrier()
         device_ms = ev0.elapsed_time(ev1)
         launches = ex.launches_per_round() * args.steps
+        # the outer step alone (reduce over sharers + Nesterov + write-back)
+        barrier()
+        ev0.record(st)
+        for _ in range(args.steps):
+            ex.device_outer()
+        ev1.record(st)
+        barrier()
+        outer_ms = ev0.elapsed_time(ev1) / args.steps
 
     # -- end to end through the public API ------------------------------------------------
     st = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ref_outer is not None:
+        ref_outer.reset()
     with ClockSampler(local) as clocks:
         barrier()
         t0 = time.perf_counter()
@@ -202,6 +249,8 @@ def run(args) -> dict:
         barrier()
         wall_ms = (time.perf_counter() - t0) * 1e3
     e2e_event_ms = ev0.elapsed_time(ev1)
+    if ref_outer is not None:
+        outer_ms = ref_outer.mean_ms()
     if device_ms is None:
         device_ms = e2e_event_ms
 
@@ -213,6 +262,7 @@ def run(args) -> dict:
         return float(t.item())
 
     device_ms = max_over_ranks(device_ms)
+    outer_ms = max_over_ranks(outer_ms) if outer_ms is not None else None
     wall_ms = max_over_ranks(wall_ms)
     ms_per_round = device_ms / args.steps
     value = tokens_per_round / (ms_per_round / 1e3)
@@ -244,6 +294,11 @@ def run(args) -> dict:
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(wall_ms / args.steps, 3)},
         "gpu_launches": launches if launches is not None else 0,
+        "outer_sync_ms": None if outer_ms is None else round(outer_ms, 3),
+        "outer_sync_scope": ("device time of the fused outer step (reduce over sharers + Nesterov + "
+                             "write-back), max over ranks" if args.impl != "reference" else
+                             "device time of the per-key global_reduce calls + outer optimizer step of "
+                             "the timed rounds, max over ranks"),
     }
     if args.impl == "reference":
         out["impl"] = "reference"

@@ -507,6 +507,10 @@ class FusedExecutor:
         """Replay one round's device work (inner-step graph + outer step) on the inputs
         already resident on the device: no host preparation, copies or reads."""
         self._run_inner(self.e.diloco.inner_steps)
+        self.device_outer()
+
+    def device_outer(self) -> None:
+        """Only the outer step (pseudo-gradient reduce + Nesterov + write-back) of a round."""
         dl = self.e.diloco
         if getattr(self.e.backend, "world_size", 1) > 1:
             self.e.backend.fused_outer_step(self, self._plan, first=False)
