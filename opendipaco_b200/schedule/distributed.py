@@ -87,11 +87,17 @@ class CoordinatorServer(ReactorServer):
             return self._next_task(msg)
         if kind == "submit":
             return {"type": "ack", "applied": self._receive(msg)}
+        if kind == "manifest":
+            return {"type": "manifest", "manifest": getattr(self, "_manifest", None)}
         if kind == "nack":
             self._nack(msg)
         elif kind == "heartbeat":
             self._heartbeat(msg)
         return None
+
+    def serve_manifest(self, manifest) -> None:
+        """Publish the run manifest that ``opendipaco join`` clients fetch."""
+        self._manifest = manifest
 
     def shutdown(self) -> None:
         with self._lock:

@@ -48,7 +48,8 @@ from .compress import (apply_state_delta, check_mode, compress_delta, compress_s
                        encode_state_delta, maybe_dequantize, pseudograd_digest, restore_shard, state_digest)
 from .guard import all_finite, clip_norm_, loss_ok
 from .identity import peer_id_of, sign_record, verify_record
-from .ownership import EpochManager, make_epoch_record, owners_for
+from .ownership import (EpochManager, derive_epoch, epoch_newer, make_epoch_record, owners_for,
+                        verify_epoch_record)
 from .probe import TrustedProbe, as_finite_float, is_harmful
 from .quorum import read_quorum_versions
 from .ratelimit import RateLimiter
@@ -158,11 +159,16 @@ class ParameterServer(ReactorServer):
                  identity=None, epoch_record=None, replicate_interval=10.0, peer_auth=None, bank_seed=0,
                  robustness="off", quorum_target=3, quorum_timeout=30.0, aggregate="trimmed_mean",
                  version_history=1, private_policy="overwrite", schedule_mode="central", down="full",
-                 coordinates=None, **kw):
+                 coordinates=None, scheduler_addr=None, peer_tls=None, private_quorum=2, salt="", k=3,
+                 lease_ttl=20.0, read_quorum=1, directory_ttl=30.0, reputation=None, rate_limiter=None,
+                 min_owner_reputation=0.0, corpus_weights=None, **kw):
         super().__init__(host=host, port=port, auth_key=auth_key, **kw)
         self.config, self.diloco, self.device = config, diloco, torch.device(device)
         self._topology = config.build_topology()
-        self.owned_keys = set(owned_keys)
+        # an owner with an identity and no fixed keys is dynamic: it holds the whole seeded
+        # bank and serves/writes only the keys the current epoch places on it
+        self.dynamic = not owned_keys and identity is not None
+        self.owned_keys = set(self._topology.module_keys()) if self.dynamic else set(owned_keys)
         self.grant_key, self.scheduler_pub = grant_key, scheduler_pub
         self.max_update_norm = max_update_norm
         self.compress = check_mode(compress)
@@ -177,6 +183,15 @@ class ParameterServer(ReactorServer):
         self.schedule_mode = schedule_mode
         self.down = down
         self.replicate_interval = replicate_interval
+        self.scheduler_addr = _addr(scheduler_addr) if scheduler_addr is not None else None
+        self.peer_tls, self.private_quorum = peer_tls, max(1, int(private_quorum))
+        self.salt, self.k, self.lease_ttl, self.read_quorum = salt, k, lease_ttl, read_quorum
+        self.directory_ttl = directory_ttl
+        self.reputation = reputation or Reputation()
+        self.rate_limiter = rate_limiter
+        self.min_owner_reputation = min_owner_reputation
+        self.corpus_weights = dict(corpus_weights) if corpus_weights else None
+        self._tracker = None
         full = build_module_bank(config, seed=bank_seed)
         self.bank = {k: full[k].to(self.device) for k in self.owned_keys}
         self._versions = {k: (0, 0) for k in self.bank}
@@ -191,7 +206,7 @@ class ParameterServer(ReactorServer):
         self._saved: dict = {}
         self._epoch = None
         self._epoch_num = 0
-        self._active = set(self.bank)
+        self._active = set() if self.dynamic else set(self.bank)
         self._draining = False
         self._repl_stop = threading.Event()
         self._repl_thread = None
@@ -222,7 +237,13 @@ class ParameterServer(ReactorServer):
         if kind == "generation":
             return self._generation(msg)
         if kind == "epoch":
-            self.apply_epoch(msg.get("record"))
+            rec = msg.get("record")
+            if not verify_epoch_record(rec, signer_pub=self.scheduler_pub,
+                                       allow_deterministic=self.schedule_mode == "decentralized"):
+                return {"type": "refused", "reason": "bad epoch record"}
+            if self._epoch is not None and not epoch_newer(rec, self._epoch):
+                return {"type": "ack", "stale": True}
+            self.apply_epoch(rec)
             return {"type": "ack"}
         if kind == "checkpoint":
             if self._epoch is not None:
@@ -238,7 +259,7 @@ class ParameterServer(ReactorServer):
     # -- ownership ---------------------------------------------------------------
     def _primary(self, key) -> bool:
         if self._epoch is None:
-            return True
+            return not self.dynamic
         if self._draining or key not in self._active:
             return False
         owners = owners_for(key, self._epoch)
@@ -250,18 +271,50 @@ class ParameterServer(ReactorServer):
         return self._primary(key)
 
     def apply_epoch(self, record, *, bootstrap: bool | None = None) -> None:
-        """Adopt an epoch: keys this peer is a replica of become active."""
+        """Adopt an epoch: keys this peer is a replica of become active. Keys gained in a
+        non-bootstrap epoch are first synced (highest version wins) from the replicas of
+        the previous epoch, so a joining owner never serves its freshly seeded bank."""
         if not record:
             return
+        boot = bool(record.get("bootstrap")) if bootstrap is None else bootstrap
+        with self._lock:
+            prev = self._epoch
+            act = {k for k in self.bank if self.peer_id in {o["peer_id"] for o in owners_for(k, record)}}
+            gained = act - self._active
+        if gained and not boot and prev is not None:
+            self._sync_keys(sorted(gained), prev)
         with self._lock:
             self._epoch = record
             self._epoch_num = int(record.get("epoch", 0))
-            act = set()
-            for k in self.bank:
-                ids = {o["peer_id"] for o in owners_for(k, record)}
-                if self.peer_id in ids:
-                    act.add(k)
             self._active = act
+
+    def _sync_keys(self, keys, epoch) -> None:
+        plan: dict = {}
+        for k in keys:
+            for o in owners_for(k, epoch):
+                if o["peer_id"] != self.peer_id:
+                    plan.setdefault(_addr(o["addr"]), []).append(k)
+        for addr, ks in plan.items():
+            try:
+                reply = self._peer_rpc(addr, {"type": "fetch", "keys": ks, "include_state": True, "have": {}})
+            except (OSError, ConnectionError, PermissionError):
+                continue
+            self._adopt(reply)
+
+    def _adopt(self, reply) -> dict:
+        """Take every key of an ``include_state`` fetch reply that is newer than ours."""
+        pulled = {}
+        with self._lock:
+            for k, sd in (reply.get("weights") or {}).items():
+                v = _safe_version((reply.get("versions") or {}).get(k))
+                if k in self.bank and v is not None and v > self._versions[k]:
+                    self.bank[k].load_state_dict({n: t.to(self.device) for n, t in sd.items()})
+                    st = (reply.get("state") or {}).get(k)
+                    if st is not None and k in self._outer_opts:
+                        self._outer_opts[k].load_state_dict(_opt_from_wire(st))
+                    self._versions[k] = v
+                    pulled[k] = v
+        return pulled
 
     def _bump(self, key) -> None:
         e, c = self._versions[key]
@@ -448,7 +501,15 @@ class ParameterServer(ReactorServer):
                     skipped.append(k)
                     continue
                 if self.private_policy == "proposal":
-                    self._proposals.setdefault(k, []).append((grant["token"], sd))
+                    # apply only once private_quorum proposals agree byte for byte
+                    dg = state_digest(sd)
+                    props = self._proposals.setdefault(k, [])
+                    props.append((dg, sd))
+                    if sum(1 for d, _ in props if d == dg) >= self.private_quorum:
+                        self._record_history(k)
+                        self.bank[k].load_state_dict({n: v.to(self.device) for n, v in sd.items()})
+                        self._bump(k)
+                        self._proposals.pop(k, None)
                     applied += 1
                     continue
                 self._record_history(k)
@@ -479,7 +540,11 @@ class ParameterServer(ReactorServer):
                 return {"type": "commit_ack", "accepted": False}
             self._gen_counters[path] = gen + 1
         keys = self._topology.path_module_keys(path)
-        w = float(msg.get("weight", 1.0))
+        if self.corpus_weights is not None:
+            w = float(self.corpus_weights.get(self._topology.path_index(path), 0.0))
+        else:
+            w = as_finite_float(msg.get("weight"))
+            w = 1.0 if w is None else min(max(w, 0.0), 1.0)
         grant = make_grant(path, keys, w, uuid.uuid4().hex, identity=self.identity)
         return {"type": "commit_ack", "accepted": True, "grant": grant, "push_weight": w}
 
@@ -509,7 +574,8 @@ class ParameterServer(ReactorServer):
         return {"type": "drained", "adopted": adopted}
 
     def _peer_rpc(self, addr, msg):
-        s = connect(_addr(addr), self.peer_auth if self.peer_auth is not None else self.auth_key, timeout=5.0)
+        cred = next((c for c in (self.peer_auth, self.auth_key, self.identity) if c is not None), None)
+        s = connect(_addr(addr), cred, timeout=5.0, tls=self.peer_tls)
         try:
             return rpc(s, msg)
         finally:
@@ -533,31 +599,84 @@ class ParameterServer(ReactorServer):
                                               "have": {k: list(have[k]) for k in keys}})
             except (OSError, ConnectionError, PermissionError):
                 continue
-            with self._lock:
-                for k, sd in (reply.get("weights") or {}).items():
-                    v = _safe_version(reply.get("versions", {}).get(k)) or _version_pair(reply["versions"][k])
-                    if k in self.bank and v > self._versions[k]:
-                        self.bank[k].load_state_dict({n: t.to(self.device) for n, t in sd.items()})
-                        st = (reply.get("state") or {}).get(k)
-                        if st is not None and k in self._outer_opts:
-                            self._outer_opts[k].load_state_dict(_opt_from_wire(st))
-                        self._versions[k] = v
-                        pulled[k] = v
+            pulled.update(self._adopt(reply))
         return pulled
+
+    def _poll_scheduler_epoch(self) -> None:
+        if self.scheduler_addr is None:
+            return
+        try:
+            cred = self.auth_key if self.auth_key is not None else self.identity
+            s = connect(self.scheduler_addr, cred, timeout=5.0, tls=self.peer_tls)
+            try:
+                rec = rpc(s, {"type": "epoch_get"}).get("record")
+            finally:
+                s.close()
+        except (OSError, ConnectionError, PermissionError):
+            return
+        if rec and verify_epoch_record(rec, signer_pub=self.scheduler_pub) and epoch_newer(rec, self._epoch):
+            self.apply_epoch(rec)
+
+    def _derive_from_directory(self) -> None:
+        """Decentralized: every owner derives the same epoch from the tracker directory."""
+        if self._tracker is None or self.schedule_mode != "decentralized":
+            return
+        from .tracker import fetch_directory
+
+        try:
+            recs = fetch_directory(self._tracker["addr"], roles=["owner"], auth_key=self._tracker["auth"],
+                                   tls=self._tracker["tls"])
+        except (OSError, ConnectionError, PermissionError):
+            return
+        eligible = (lambda pid: self.reputation.get(pid) >= self.min_owner_reputation) \
+            if self.min_owner_reputation else None
+        prev = self._epoch if self._epoch is not None and self._epoch.get("deterministic") else None
+        nxt = derive_epoch(recs, k=self.k, salt=self.salt, prev=prev, is_eligible=eligible)
+        if nxt is not prev and nxt["owners"]:
+            self.apply_epoch(nxt)
 
     def _replicate_loop(self) -> None:
         while not self._repl_stop.wait(self.replicate_interval):
             try:
                 self._sweep_buffers()
+                self._poll_scheduler_epoch()
+                self._derive_from_directory()
                 self._replicate_once()
             except Exception:
                 logger.exception("replication pass failed")
 
     def start(self) -> None:
         super().start()
-        if self._epoch is not None or self.robust != "off":
+        if self._epoch is not None or self.robust != "off" or self.dynamic or self.scheduler_addr is not None:
             self._repl_thread = threading.Thread(target=self._replicate_loop, daemon=True)
             self._repl_thread.start()
+            if self.scheduler_addr is not None:
+                threading.Thread(target=self._poll_scheduler_epoch, daemon=True).start()
+
+    def start_tracker_heartbeat(self, tracker_addr, advertise_host, *, interval=10.0, auth_key=None, tls=None,
+                                seeds=()):
+        """Keep this owner's signed record registered on the tracker(s) (re-register every
+        ``interval`` s, below the tracker's TTL); deregistered on a graceful shutdown."""
+        from .tracker import dedup_seeds, register_peer
+
+        if self.identity is None:
+            raise ValueError("a tracker heartbeat needs an owner identity")
+        addrs = dedup_seeds(tuple(tracker_addr), seeds)
+        self._tracker = {"addr": addrs[0], "all": addrs, "auth": auth_key, "tls": tls}
+        stop = self._repl_stop
+
+        def beat():
+            while True:
+                for a in addrs:
+                    try:
+                        register_peer(a, self.identity, reachability="public", peer_addr=(advertise_host, self.port),
+                                      roles=["owner"], auth_key=auth_key, tls=tls, timeout=5.0)
+                    except (OSError, ConnectionError, PermissionError):
+                        continue
+                if stop.wait(interval):
+                    return
+
+        threading.Thread(target=beat, daemon=True).start()
 
     def _drain_to_backups(self) -> dict:
         """A leaving primary pushes its latest state to each key's next owner."""
@@ -587,6 +706,15 @@ class ParameterServer(ReactorServer):
                 for k in list(self._buffers):
                     self._flush_buffer(k)
             self._drain_to_backups()
+            if self._tracker is not None:
+                from .tracker import deregister_peer
+
+                for a in self._tracker["all"]:
+                    try:
+                        deregister_peer(a, self.identity, auth_key=self._tracker["auth"], tls=self._tracker["tls"],
+                                        timeout=5.0)
+                    except (OSError, ConnectionError, PermissionError):
+                        continue
         self._repl_stop.set()
         super().shutdown()
 
@@ -663,7 +791,8 @@ class Scheduler(ReactorServer):
                  identity=None, compress="none", idle_backoff=None, reputation=None, rate_limiter=None,
                  redundancy=3, redundancy_rate=0.0, audit_timeout=60.0, private_policy="overwrite", down="full",
                  up_density=1.0, task_seconds=None, park_factor=3.0, min_task_rate=None, tailor_bandwidth=False,
-                 probe=None, probe_quorum=0, probe_abs_margin=0.05, probe_rel_margin=0.02, probe_debit=False, **kw):
+                 probe=None, probe_quorum=0, probe_abs_margin=0.05, probe_rel_margin=0.02, probe_debit=False,
+                 ps_tls=None, min_owner_reputation=0.0, **kw):
         super().__init__(host=host, port=port, auth_key=auth_key, **kw)
         self.config, self.corpus, self.diloco, self.batch_size = config, corpus, diloco, batch_size
         self.topology = config.build_topology()
@@ -683,6 +812,7 @@ class Scheduler(ReactorServer):
         self._probe = probe if isinstance(probe, TrustedProbe) or probe is None else TrustedProbe(probe)
         self.probe_quorum, self.probe_debit = probe_quorum, probe_debit
         self.probe_margin = {"abs_margin": probe_abs_margin, "rel_margin": probe_rel_margin}
+        self.ps_tls, self.min_owner_reputation = ps_tls, min_owner_reputation
         self._ps_addrs = [_addr(a) for a in ps_addrs or []]
         keys = self.topology.module_keys()
         self._static_routing = ({k: self._ps_addrs[i] for k, i in assign_shards(keys, len(self._ps_addrs)).items()}
@@ -721,6 +851,9 @@ class Scheduler(ReactorServer):
             return self._fresh_routing(msg)
         if kind == "manifest":
             return {"type": "manifest", "manifest": self._manifest}
+        if kind == "epoch_get":
+            with self._lock:
+                return {"type": "epoch", "record": self._epoch_record}
         return None
 
     def serve_manifest(self, manifest) -> None:
@@ -739,7 +872,7 @@ class Scheduler(ReactorServer):
             self._routing = {}
         for o in rec["owners"]:
             try:
-                s = connect(_addr(o["addr"]), self.auth_key, timeout=5.0)
+                s = connect(_addr(o["addr"]), self.auth_key, timeout=5.0, tls=self.ps_tls)
                 try:
                     rpc(s, {"type": "epoch", "record": rec})
                 finally:
@@ -749,21 +882,29 @@ class Scheduler(ReactorServer):
         return rec
 
     def watch_tracker(self, tracker_addr, *, k=3, salt="", owner_grace=240.0, min_epoch_interval=60.0,
-                      interval=5.0, auth_key=None):
+                      poll_interval=5.0, tracker_auth=None, tracker_tls=None):
+        """Publish a signed epoch whenever the tracker's live owner set changes
+        (hysteresis and rate limit of ``EpochManager``; owners below
+        ``min_owner_reputation`` are left out)."""
         from .tracker import fetch_directory_and_tombstones
 
-        mgr = EpochManager(owner_grace=owner_grace, min_epoch_interval=min_epoch_interval)
+        eligible = (lambda pid: self.reputation.get(pid) >= self.min_owner_reputation) \
+            if self.min_owner_reputation else None
+        mgr = EpochManager(owner_grace=owner_grace, min_epoch_interval=min_epoch_interval, is_eligible=eligible)
         stop = threading.Event()
 
         def watch():
-            while not stop.wait(interval) and not self._stop:
+            while not self._stop:
                 try:
-                    recs, tombs = fetch_directory_and_tombstones(tracker_addr, roles=["owner"], auth_key=auth_key)
+                    recs, tombs = fetch_directory_and_tombstones(tuple(tracker_addr), roles=["owner"],
+                                                                 auth_key=tracker_auth, tls=tracker_tls)
+                    nxt = mgr.observe(recs, tombstoned=tombs)
+                    if nxt:
+                        self.publish_epoch(nxt, k=k, salt=salt)
                 except Exception:
-                    continue
-                nxt = mgr.observe(recs, tombstoned=tombs)
-                if nxt:
-                    self.publish_epoch(nxt, k=k, salt=salt)
+                    logger.exception("tracker watch pass failed")
+                if stop.wait(poll_interval):
+                    return
 
         threading.Thread(target=watch, daemon=True).start()
         return stop
@@ -1078,13 +1219,32 @@ class Scheduler(ReactorServer):
 
 # ================================================================================ workers
 class _WorkerLink:
-    """A worker's connections: one to the scheduler, cached ones to owners."""
+    """A worker's connections: one to the scheduler (re-dialled after a drop when
+    ``reconnect``), cached ones to owners; all optionally TLS and bandwidth-throttled."""
 
-    def __init__(self, sch_sock, *, auth_key, max_msg_bytes, connect_timeout, tls=None):
-        self.sch, self.auth_key, self.max_msg_bytes = sch_sock, auth_key, max_msg_bytes
-        self.timeout, self.tls = connect_timeout, tls
+    def __init__(self, sch_addr, *, auth_key, max_msg_bytes=DEFAULT_MAX_MSG_BYTES, connect_timeout=10.0, tls=None,
+                 tls_hostname=None, bucket=None, reconnect=False, reconnect_timeout=30.0):
+        self.auth_key, self.max_msg_bytes = auth_key, max_msg_bytes
+        self.timeout, self.tls, self.tls_hostname, self.bucket = connect_timeout, tls, tls_hostname, bucket
+        self.reconnect, self.reconnect_timeout = reconnect, reconnect_timeout
         self._sch_lock = threading.Lock()
         self._ps: dict = {}
+        self.sch_addr = _addr(sch_addr) if sch_addr is not None else None
+        self.sch = self._dial(self.sch_addr, connect_timeout) if self.sch_addr is not None else None
+
+    def _dial(self, addr, timeout):
+        from .throttle import throttled
+
+        s = connect(addr, self.auth_key, self.max_msg_bytes, timeout, tls=self.tls,
+                    server_hostname=self.tls_hostname)
+        return throttled(s, self.bucket)
+
+    def _redial(self) -> None:
+        try:
+            self.sch.close()
+        except OSError:
+            pass
+        self.sch = self._dial(self.sch_addr, self.reconnect_timeout)
 
     def sch_send(self, msg) -> None:
         from .wire import send_msg
@@ -1094,12 +1254,18 @@ class _WorkerLink:
 
     def sch_rpc(self, msg):
         with self._sch_lock:
-            return rpc(self.sch, msg, self.max_msg_bytes)
+            try:
+                return rpc(self.sch, msg, self.max_msg_bytes)
+            except (OSError, ConnectionError):
+                if not self.reconnect:
+                    raise
+                self._redial()
+                return rpc(self.sch, msg, self.max_msg_bytes)
 
     def ps_rpc(self, addr, msg):
         a = _addr(addr)
         if a not in self._ps:
-            self._ps[a] = connect(a, self.auth_key, self.max_msg_bytes, self.timeout, tls=self.tls)
+            self._ps[a] = self._dial(a, self.timeout)
         try:
             return rpc(self._ps[a], msg, self.max_msg_bytes)
         except (OSError, ConnectionError):
@@ -1117,10 +1283,11 @@ class _WorkerLink:
     def close(self) -> None:
         for a in list(self._ps):
             self._drop(a)
-        try:
-            self.sch.close()
-        except OSError:
-            pass
+        if self.sch is not None:
+            try:
+                self.sch.close()
+            except OSError:
+                pass
 
 
 def _fetch_keys(link, routing, keys, versions, cold_keys, keyframes, pin=None):
@@ -1176,25 +1343,41 @@ def _build_engine(config, diloco, device, seed):
 
 def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, auth_key=None,
                        max_msg_bytes=DEFAULT_MAX_MSG_BYTES, connect_timeout=10.0, heartbeat_interval=3.0,
-                       poll_interval=0.02, max_tasks=None, fault_hook=None, tls=None, stop_event=None,
-                       max_batch_size=None, max_shards=4):
-    """Lease -> fetch from owners -> train -> commit (grant) -> push to owners."""
+                       poll_interval=0.02, max_tasks=None, fault_hook=None, tls=None, tls_hostname=None,
+                       stop_event=None, max_batch_size=None, max_shards=None, reconnect=True,
+                       reconnect_timeout=30.0, data_dir=None, data_source=None, data_tokenizer=None,
+                       verify_routing=False, bucket=None, identity=None):
+    """Lease -> fetch from owners -> train -> commit (grant) -> push to owners.
+
+    ``auth_key`` (or ``identity``) is the credential; ``bucket`` a shared
+    ``throttle.TokenBucket`` capping this worker's bandwidth; ``data_dir`` caches
+    shards materialised from shipped specs (``verify_routing`` re-fits the shipped
+    router from the public source first and refuses to train on a mismatch)."""
     from .distributed import _ShardCache, _heartbeat_loop, _materialize_from_spec
 
     engine = _build_engine(config, diloco, device, seed)
     worker = AsyncScheduler(engine, num_workers=1)
     wid = uuid.uuid4().hex
     topo = engine.topology
-    link = _WorkerLink(connect(_addr(scheduler_addr), auth_key, max_msg_bytes, connect_timeout, tls=tls),
-                       auth_key=auth_key, max_msg_bytes=max_msg_bytes, connect_timeout=connect_timeout, tls=tls)
+    cred = auth_key if auth_key is not None else identity
+    try:
+        link = _WorkerLink(scheduler_addr, auth_key=cred, max_msg_bytes=max_msg_bytes,
+                           connect_timeout=connect_timeout, tls=tls, tls_hostname=tls_hostname, bucket=bucket,
+                           reconnect=reconnect, reconnect_timeout=reconnect_timeout)
+    except ConnectionError:
+        return
+    data_ctx = {"dir": data_dir, "source": data_source, "tokenizer": data_tokenizer, "verify": verify_routing}
     warm, cache = set(), _ShardCache(max_shards)
     versions, keyframes, residuals = {}, {}, {}
     caps = {"device": str(device), **({"max_batch": int(max_batch_size)} if max_batch_size else {})}
     done = 0
     try:
         while stop_event is None or not stop_event.is_set():
-            msg = link.sch_rpc({"type": "request", "worker_id": wid, "warm_paths": list(warm),
-                                "cached_shards": list(cache), "capabilities": caps})
+            try:
+                msg = link.sch_rpc({"type": "request", "worker_id": wid, "warm_paths": list(warm),
+                                    "cached_shards": list(cache), "capabilities": caps})
+            except (OSError, ConnectionError):
+                return          # the scheduler is gone (and did not come back within reconnect_timeout)
             if msg["type"] == "stop":
                 return
             if msg["type"] == "idle":
@@ -1219,7 +1402,7 @@ def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, 
                 if msg.get("shard") is not None:
                     cache[path] = restore_shard(msg["shard"])
                 elif msg.get("shard_spec") is not None and path not in cache:
-                    cache[path] = _materialize_from_spec(msg["shard_spec"], {})
+                    cache[path] = _materialize_from_spec(msg["shard_spec"], data_ctx)
                 if path not in warm:
                     engine._opt_state.pop(path, None)
                 probe = TrustedProbe(msg["probe"], batch_size=msg.get("probe_batch", 8)) if msg.get("probe") is not None else None
@@ -1278,28 +1461,77 @@ def _decentralized_routing(topology, path, epoch) -> dict:
     return {k: [o["addr"] for o in owners_for(k, epoch)] for k in topology.path_module_keys(path)}
 
 
-def run_decentralized_worker(config, diloco, epoch_fn, corpus, *, identity, auth_key=None, device="cpu", seed=0,
-                             batch_size=8, workers_fn=None, salt="", lease_ttl=30.0, read_quorum=1,
-                             max_tasks=None, stop_event=None, poll_interval=0.05):
+def run_decentralized_worker(config, diloco, tracker, corpus, *, identity, auth_key=None, device="cpu", seed=0,
+                             batch_size=8, workers_fn=None, k=3, salt="", lease_ttl=30.0, read_quorum=1,
+                             max_tasks=None, stop_event=None, poll_interval=0.05, total_rounds=None, tls=None,
+                             bucket=None, heartbeat_interval=10.0, seeds=(), seed_quorum=1):
     """Scheduler-less worker: self-assign ``(path, generation)`` slots by HRW over the
     live worker set, read bases with quorum reads, commit to the path's coordinating
-    owner (which mints an Ed25519 grant), push to every owner of each key."""
+    owner (which mints an Ed25519 grant), push to every owner of each key.
+
+    ``tracker`` is the tracker's ``(host, port)`` -- the worker then registers itself
+    (role ``worker``) every ``heartbeat_interval`` s and derives the owner epoch and
+    the worker set from the (multi-seed) directory each pass -- or a callable that
+    returns the current epoch record (tests, embedded use). With ``total_rounds``
+    the worker stops taking a path once its generation reaches it."""
+    from .tracker import dedup_seeds, fetch_directory_multi, register_peer
+
     engine = _build_engine(config, diloco, device, seed)
+    engine.total_rounds = total_rounds
     worker = AsyncScheduler(engine, num_workers=1)
     topo = engine.topology
-    link = _WorkerLink(None, auth_key=auth_key, max_msg_bytes=DEFAULT_MAX_MSG_BYTES, connect_timeout=5.0)
-    done, t_open = 0, {}
+    link = _WorkerLink(None, auth_key=auth_key if auth_key is not None else identity, connect_timeout=5.0,
+                       tls=tls, bucket=bucket)
+    beat_stop = threading.Event()
+    state = {"epoch": None}
+    if callable(tracker):
+        epoch_fn = tracker
+    else:
+        seed_list = dedup_seeds(tuple(tracker), seeds)
+
+        def beat():
+            while True:
+                for a in seed_list:
+                    try:
+                        register_peer(a, identity, roles=["worker"], auth_key=auth_key, tls=tls, timeout=5.0)
+                    except (OSError, ConnectionError, PermissionError):
+                        continue
+                if beat_stop.wait(heartbeat_interval):
+                    return
+
+        threading.Thread(target=beat, daemon=True).start()
+
+        def epoch_fn():
+            recs, _ = fetch_directory_multi(seed_list, auth_key=auth_key, tls=tls, seed_quorum=seed_quorum)
+            owners = [r for r in recs if "owner" in (r.get("roles") or [])]
+            state["workers"] = _worker_directory_ids(recs)
+            if owners:
+                state["epoch"] = derive_epoch(owners, k=k, salt=salt, prev=state["epoch"])
+            return state["epoch"]
+
+        if workers_fn is None:
+            workers_fn = lambda: state.get("workers")  # noqa: E731
+    done, t_open, finished = 0, {}, set()
     try:
         while (stop_event is None or not stop_event.is_set()) and (max_tasks is None or done < max_tasks):
-            epoch = epoch_fn()
-            workers = (workers_fn() if workers_fn else None) or [identity.peer_id]
+            try:
+                epoch = epoch_fn()
+            except (OSError, ConnectionError, PermissionError):
+                epoch = None
+            if not epoch or not epoch.get("owners"):
+                time.sleep(poll_interval)
+                continue
+            workers = sorted(set((workers_fn() if workers_fn else None) or []) | {identity.peer_id})
             picked = None
             for path in topo.paths():
                 keys = topo.path_module_keys(path)
                 coord = owners_for(coordinator_key(keys), epoch)[0]
                 try:
                     gen = link.ps_rpc(coord["addr"], {"type": "generation", "path": path})["generation"]
-                except (OSError, ConnectionError):
+                except (OSError, ConnectionError, PermissionError):
+                    continue
+                if total_rounds is not None and gen >= total_rounds:
+                    finished.add(path)
                     continue
                 t0 = t_open.setdefault((path, gen), time.monotonic())
                 if is_assignee(identity.peer_id, path, gen, workers, salt=salt,
@@ -1307,37 +1539,52 @@ def run_decentralized_worker(config, diloco, epoch_fn, corpus, *, identity, auth
                     picked = (path, gen, coord)
                     break
             if picked is None:
+                if total_rounds is not None and len(finished) == topo.num_paths:
+                    return
                 time.sleep(poll_interval)
                 continue
             path, gen, coord = picked
-            routing = _decentralized_routing(topo, path, epoch)
-            keys = topo.path_module_keys(path)
-            shared = [k for k in keys if not is_private_key(k)]
-            confirmed = read_quorum_versions(list({_addr(a) for k in shared for a in routing[k]}), shared,
-                                             read_quorum, lambda a, m: link.ps_rpc(a, m)) if read_quorum > 1 else {}
-            versions: dict = {}
-            fetched = _fetch_keys(link, routing, keys, versions, {k for k in keys if is_private_key(k)}, {},
-                                  pin={k: list(v[0]) for k, v in confirmed.items()} or None)
-            for k, sd in fetched.items():
-                engine.bank[k].load_state_dict({n: v.to(engine.device) for n, v in sd.items()})
-            contrib = worker._train_path(path, corpus.shard(topo.path_index(path)), batch_size, gen)
-            ack = link.ps_rpc(coord["addr"], {"type": "commit", "path": path, "gen_id": gen, "loss": contrib.loss,
-                                             "empty": contrib.empty,
-                                             "weight": corpus.shard_weight(topo.path_index(path))})
-            if not ack.get("accepted"):
-                continue
-            for k in keys:
-                upd = {k: {"grad": contrib.shared_delta[k]}} if k in contrib.shared_delta else {}
-                priv = {k: contrib.private_state[k]} if k in contrib.private_state else {}
-                for a in routing[k]:
-                    try:
-                        link.ps_rpc(a, {"type": "push", "grant": ack["grant"], "updates": upd, "private": priv})
-                    except (OSError, ConnectionError):
-                        continue
-            done += 1
+            try:
+                if _decentralized_task(engine, worker, link, topo, corpus, epoch, path, gen, coord, batch_size,
+                                       read_quorum):
+                    done += 1
+            except (OSError, ConnectionError, PermissionError, ValueError):
+                time.sleep(poll_interval)
     finally:
-        for a in list(link._ps):
-            link._drop(a)
+        beat_stop.set()
+        link.close()
+
+
+def _decentralized_task(engine, worker, link, topo, corpus, epoch, path, gen, coord, batch_size, read_quorum) -> bool:
+    routing = _decentralized_routing(topo, path, epoch)
+    keys = topo.path_module_keys(path)
+    shared = [k for k in keys if not is_private_key(k)]
+    confirmed = read_quorum_versions(list({_addr(a) for k in shared for a in routing[k]}), shared, read_quorum,
+                                     lambda a, m: link.ps_rpc(a, m)) if read_quorum > 1 else {}
+    fetched = _fetch_keys(link, routing, keys, {}, {k for k in keys if is_private_key(k)}, {},
+                          pin={k: list(v[0]) for k, v in confirmed.items()} or None)
+    for k, sd in fetched.items():
+        engine.bank[k].load_state_dict({n: v.to(engine.device) for n, v in sd.items()})
+    contrib = worker._train_path(path, corpus.shard(topo.path_index(path)), batch_size, gen)
+    ack = link.ps_rpc(coord["addr"], {"type": "commit", "path": path, "gen_id": gen, "loss": contrib.loss,
+                                     "empty": contrib.empty, "weight": corpus.shard_weight(topo.path_index(path))})
+    if not ack.get("accepted"):
+        return False
+    # one push per owner (a grant token is single-use per owner), carrying every key it replicates
+    by_owner: dict = {}
+    for k in keys:
+        for a in routing[k]:
+            upd, priv = by_owner.setdefault(_addr(a), ({}, {}))
+            if k in contrib.shared_delta:
+                upd[k] = {"grad": contrib.shared_delta[k]}
+            if k in contrib.private_state:
+                priv[k] = contrib.private_state[k]
+    for a, (upd, priv) in by_owner.items():
+        try:
+            link.ps_rpc(a, {"type": "push", "grant": ack["grant"], "updates": upd, "private": priv})
+        except (OSError, ConnectionError):
+            continue
+    return True
 
 
 __all__ = ["ParameterServer", "Scheduler", "assign_shards", "make_grant", "verify_grant", "grant_signed_by",

@@ -31,4 +31,5 @@ setup(
                                extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC},
                                libraries=["cuda"])],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    entry_points={"console_scripts": ["opendipaco=opendipaco_b200.launch.cli:main"]},
 )
