@@ -1,0 +1,505 @@
+// Causal self-attention on the 5th-generation tensor cores (tcgen05 + TMEM) for
+// sequences of at most 128 tokens, head_dim 64, GQA, reading q/k/v straight out of the
+// fused QKV projection output [GB, S, (nh + 2 nkv) * 64] (bf16) with RoPE applied while
+// the tiles are staged (same rounding points as the mma.sync kernels in attention.cu).
+//
+// A whole (sequence, head) is one 128-row tile, so each CTA does the entire attention
+// of one head with single-tile MMAs (M = 128):
+//
+// forward, one CTA per (head, sequence), 128 threads, thread t owns query row t:
+//   S = Q K^T            -> TMEM columns [0, 128)       (4 MMAs, K = 64)
+//   row softmax in registers from tcgen05.ld (no cross-thread reduction), P in bf16
+//   written to shared memory over the Q/K tiles (both dead once S is done)
+//   O = P V              -> TMEM columns [0, 64)        (8 MMAs, K = 128)
+//   48 KB shared memory and 128 TMEM columns: four CTAs per SM.
+//
+// backward, one CTA per (kv head, sequence), 256 threads, looping over the query heads
+// of the kv group (dK, dV accumulate in TMEM across them):
+//   S = Q K^T -> [0,128), dP = dO V^T -> [128,256)
+//   P = exp2(S * scale * log2e - lse * log2e), dS = P (dP - delta) with delta = rowsum(dO O)
+//   computed in the kernel; P and dS stored once in shared memory as [query][key] tiles,
+//   read K-major for dQ = dS K and MN-major (as P^T, dS^T) for
+//   dV += P^T dO -> [256,320), dK += dS^T Q -> [320,384), dQ = dS K -> [384,448)
+//   scale and the transpose of RoPE are applied in the epilogues.
+//
+// Operand tiles are [128 rows][64 bf16] in the canonical 128-byte-swizzle layout (16-byte
+// chunk index XOR row % 8, 8-row groups 1024 bytes apart), written by the threads
+// themselves (RoPE has to be applied on the way in), then published to the tensor core
+// with fence.proxy.async. One elected thread issues every MMA; completion is signalled
+// through tcgen05.commit on an mbarrier whose waits are bounded (error word, no hang).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace odp {
+namespace attn_tc {
+
+constexpr int D = 64;
+constexpr int T = 128;               // rows of a tile = maximum sequence length
+constexpr int TILE = T * 128;        // bytes of one [128][64] bf16 tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kFwdSmem = 3 * TILE + 1024;
+constexpr int kBwdSmem = 8 * TILE + 1024;
+
+struct Args {
+  const __nv_bfloat16* qkv;
+  long long ld;  // (nh + 2 nkv) * 64
+  int S, nh, nkv;
+  const float* cosT;
+  const float* sinT;
+  __nv_bfloat16* o;  // [GB, S, nh * 64]
+  long long ldo;
+  float* lse;        // [GB, nh, S] natural-log log-sum-exp of the scaled scores
+  const __nv_bfloat16* dout;
+  __nv_bfloat16* dqkv;
+  float scale;
+  int* err;
+};
+
+ODP_DEVICE uint32_t sw_off(int row, int col) {
+  return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2);
+}
+
+ODP_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// K-major operand: a [128 rows][64] tile, k-step kk covers columns [16 kk, 16 kk + 16).
+ODP_DEVICE uint64_t desc_k(uint32_t tile, int kk) { return umma_smem_desc(tile + kk * 32, 16, 1024, kLayoutSW128); }
+// MN-major operand: rows are the K index, k-step kk covers rows [16 kk, 16 kk + 16);
+// consecutive 64-wide M/N chunks are separate tiles TILE bytes apart.
+ODP_DEVICE uint64_t desc_mn(uint32_t tile, int kk) {
+  return umma_smem_desc(tile + kk * 2048, TILE, 1024, kLayoutSW128);
+}
+
+ODP_DEVICE uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+ODP_DEVICE void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+ODP_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Start copying rows [0, 128) of 64 columns at col0 of a [S, ld] bf16 matrix into a
+// swizzled tile with cp.async (every copy of every tile in flight at once); rows >= S
+// are zero-filled. Complete with cp_async_wait_all + a barrier.
+template <int NT>
+ODP_DEVICE void stage_async(uint8_t* tile, const __nv_bfloat16* src, long long ld, int col0, int S) {
+  for (int i = threadIdx.x; i < T * 8; i += NT) {
+    const int r = i >> 3, c8 = (i & 7) * 8;
+    uint8_t* dst = tile + sw_off(r, c8);
+    if (r < S) cp_async16(dst, src + (long long)r * ld + col0 + c8);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+ODP_DEVICE void load8f(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Rotate one 8-column chunk pair (columns j.. and j+32..) of a staged row in place:
+//   out[j] = x[j] cos[j] - x[j+32] sin[j],  out[j+32] = x[j+32] cos[j+32] + x[j] sin[j+32]
+// (bf16 in, fp32 math, bf16 out).
+ODP_DEVICE void rope_pair(uint8_t* tile, int r, int j, const float (&c0)[8], const float (&s0)[8],
+                          const float (&c1)[8], const float (&s1)[8]) {
+  uint4* p0 = reinterpret_cast<uint4*>(tile + sw_off(r, j));
+  uint4* p1 = reinterpret_cast<uint4*>(tile + sw_off(r, j + 32));
+  const uint4 xv = *p0, yv = *p1;
+  const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&xv);
+  const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(&yv);
+  uint32_t a[4], b[4];
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    const float x0 = __bfloat162float(x[e]), x1 = __bfloat162float(x[e + 1]);
+    const float y0 = __bfloat162float(y[e]), y1 = __bfloat162float(y[e + 1]);
+    a[e / 2] = pack_bf16(x0 * c0[e] - y0 * s0[e], x1 * c0[e + 1] - y1 * s0[e + 1]);
+    b[e / 2] = pack_bf16(y0 * c1[e] + x0 * s1[e], y1 * c1[e + 1] + x1 * s1[e + 1]);
+  }
+  *p0 = make_uint4(a[0], a[1], a[2], a[3]);
+  *p1 = make_uint4(b[0], b[1], b[2], b[3]);
+}
+
+// RoPE in place on one or two staged tiles (position = row), cos/sin loaded once per
+// (row, chunk pair) with 16-byte loads and shared by both tiles.
+template <int NT>
+ODP_DEVICE void rope_tiles(uint8_t* t0, uint8_t* t1, int S, const float* cosT, const float* sinT) {
+  for (int i = threadIdx.x; i < T * 4; i += NT) {
+    const int r = i >> 2, j = (i & 3) * 8;
+    if (r >= S) continue;
+    float c0[8], s0[8], c1[8], s1[8];
+    load8f(cosT + (long long)r * D + j, c0);
+    load8f(sinT + (long long)r * D + j, s0);
+    load8f(cosT + (long long)r * D + j + 32, c1);
+    load8f(sinT + (long long)r * D + j + 32, s1);
+    rope_pair(t0, r, j, c0, s0, c1, s1);
+    if (t1) rope_pair(t1, r, j, c0, s0, c1, s1);
+  }
+}
+
+// Write 16 consecutive columns [c0, c0 + 16) of row `row` (c0 % 16 == 0) into a pair of
+// [128][64] tiles that together hold 128 columns.
+ODP_DEVICE void put16(uint8_t* tiles, int row, int c0, const float (&v)[16]) {
+  uint8_t* t = tiles + (c0 >> 6) * TILE;
+  const int c = c0 & 63;
+  uint4 lo = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+  uint4 hi = make_uint4(pack_bf16(v[8], v[9]), pack_bf16(v[10], v[11]), pack_bf16(v[12], v[13]),
+                        pack_bf16(v[14], v[15]));
+  *reinterpret_cast<uint4*>(t + sw_off(row, c)) = lo;
+  *reinterpret_cast<uint4*>(t + sw_off(row, c + 8)) = hi;
+}
+
+// Read the 64 fp32 columns [col, col + 64) of this thread's TMEM lane.
+ODP_DEVICE void tmem_row64(uint32_t taddr, float (&r)[64]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float v[16];
+    tmem_ld16(taddr + c * 16, v);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) r[c * 16 + e] = v[e];
+  }
+}
+
+// Store a 64-wide fp32 row as bf16 (8 x 16-byte stores), multiplied by `mul` and, if
+// asked, passed through the transpose of RoPE at position s:
+//   g[i] = r[i] cos[i] + r[i+32] sin[i+32],  g[i+32] = r[i+32] cos[i+32] - r[i] sin[i]   (i < 32)
+ODP_DEVICE void store_row64(__nv_bfloat16* dst, const float (&r)[64], float mul, const float* cosT,
+                            const float* sinT, int s, bool rope_t) {
+  uint4* out = reinterpret_cast<uint4*>(dst);
+  if (!rope_t) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      out[c] = make_uint4(pack_bf16(r[c * 8] * mul, r[c * 8 + 1] * mul), pack_bf16(r[c * 8 + 2] * mul, r[c * 8 + 3] * mul),
+                          pack_bf16(r[c * 8 + 4] * mul, r[c * 8 + 5] * mul), pack_bf16(r[c * 8 + 6] * mul, r[c * 8 + 7] * mul));
+    return;
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float c0[8], s0[8], c1[8], s1[8], lo[8], hi[8];
+    load8f(cosT + (long long)s * D + c * 8, c0);
+    load8f(sinT + (long long)s * D + c * 8, s0);
+    load8f(cosT + (long long)s * D + 32 + c * 8, c1);
+    load8f(sinT + (long long)s * D + 32 + c * 8, s1);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float x = r[c * 8 + e] * mul, y = r[32 + c * 8 + e] * mul;
+      lo[e] = x * c0[e] + y * s1[e];
+      hi[e] = y * c1[e] - x * s0[e];
+    }
+    out[c] = make_uint4(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]), pack_bf16(lo[4], lo[5]), pack_bf16(lo[6], lo[7]));
+    out[4 + c] = make_uint4(pack_bf16(hi[0], hi[1]), pack_bf16(hi[2], hi[3]), pack_bf16(hi[4], hi[5]),
+                            pack_bf16(hi[6], hi[7]));
+  }
+}
+
+__global__ void __launch_bounds__(128) fwd_kernel(Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* sQ = sm;
+  uint8_t* sK = sm + TILE;
+  uint8_t* sV = sm + 2 * TILE;
+  uint8_t* sP = sm;  // two tiles over Q and K, written once S = Q K^T has completed
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_holder;
+  const int h = blockIdx.x, gb = blockIdx.y;
+  const int warp = threadIdx.x / 32, row = threadIdx.x;
+  const int kvh = h / (a.nh / a.nkv);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_holder, 128);
+  const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
+  stage_async<128>(sQ, base, a.ld, h * D, a.S);
+  stage_async<128>(sK, base, a.ld, (a.nh + kvh) * D, a.S);
+  stage_async<128>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, a.S);
+  cp_async_wait_all();
+  __syncthreads();
+  rope_tiles<128>(sQ, sK, a.S, a.cosT, a.sinT);
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_holder;
+  const uint32_t trow = tm + ((uint32_t)(warp * 32) << 16);
+
+  if (threadIdx.x == 0) {
+    constexpr uint32_t idS = umma_idesc_bf16(T, T, false, false);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) umma_bf16(tm, desc_k(smem_u32(sQ), kk), desc_k(smem_u32(sK), kk), idS, kk > 0);
+    umma_commit(&bar);
+  }
+  __syncwarp();
+  bool ok = mbar_wait(&bar, 0, a.err, ERR_TIMEOUT_ACCUM);
+  tc_fence_after();
+
+  const float sl2 = a.scale * kLog2e;
+  const int nvalid = row < a.S ? row + 1 : 0;  // causal: keys [0, row]; padding rows see none
+  float mx = -INFINITY;
+#pragma unroll 1
+  for (int c = 0; c < T / 16; ++c) {
+    float v[16];
+    tmem_ld16(trow + c * 16, v);
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (c * 16 + e < nvalid) mx = fmaxf(mx, v[e] * sl2);
+  }
+  float l = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < T / 16; ++c) {
+    float v[16];
+    tmem_ld16(trow + c * 16, v);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float p = (c * 16 + e < nvalid) ? exp2f(v[e] * sl2 - mx) : 0.f;
+      v[e] = p;
+      l += p;
+    }
+    put16(sP, row, c * 16, v);
+  }
+  fence_async_smem();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);  // every thread agrees whether the second MMA is issued
+  tc_fence_after();
+  if (threadIdx.x == 0 && ok) {
+    constexpr uint32_t idO = umma_idesc_bf16(T, D, false, true);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+      umma_bf16(tm, desc_k(smem_u32(sP + (kk >> 2) * TILE), kk & 3), desc_mn(smem_u32(sV), kk), idO, kk > 0);
+    umma_commit(&bar);
+  }
+  __syncwarp();
+  if (ok) ok = mbar_wait(&bar, 1, a.err, ERR_TIMEOUT_ACCUM);
+  tc_fence_after();
+  float r[64];
+  tmem_row64(trow, r);
+  if (ok && row < a.S) {
+    store_row64(a.o + ((long long)gb * a.S + row) * a.ldo + h * D, r, 1.f / l, nullptr, nullptr, 0, false);
+    a.lse[((long long)gb * a.nh + h) * a.S + row] = (mx + log2f(l)) * kLn2;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 128);
+}
+
+__global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* sK = sm;
+  uint8_t* sV = sm + TILE;
+  uint8_t* sQ = sm + 2 * TILE;
+  uint8_t* sdO = sm + 3 * TILE;
+  uint8_t* sP = sm + 4 * TILE;   // 2 tiles
+  uint8_t* sdS = sm + 6 * TILE;  // 2 tiles
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ float sDelta[T], sLse[T];
+  const int kvh = blockIdx.x, gb = blockIdx.y;
+  const int grp = a.nh / a.nkv;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int quarter = warp % 4, half = warp / 4;
+  const int row = quarter * 32 + lane;  // TMEM lane / tile row this thread reads
+  const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_holder, 512);
+  const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
+  const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
+  stage_async<256>(sK, base, a.ld, (a.nh + kvh) * D, a.S);
+  stage_async<256>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, a.S);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_holder;
+  const uint32_t tS = tm, tdP = tm + 128, tdV = tm + 256, tdK = tm + 320, tdQ = tm + 384;
+  const float sl2 = a.scale * kLog2e;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  for (int hi = 0; hi < grp && ok; ++hi) {
+    const int h = kvh * grp + hi;
+    stage_async<256>(sQ, base, a.ld, h * D, a.S);
+    stage_async<256>(sdO, dobase, a.ldo, h * D, a.S);
+    float orow[64];
+    if (threadIdx.x < T && threadIdx.x < a.S) {  // this thread's O row, for delta = rowsum(dO O)
+      const uint4* op = reinterpret_cast<const uint4*>(a.o + ((long long)gb * a.S + threadIdx.x) * a.ldo + h * D);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 ov = op[c];
+        const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&ov);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) orow[c * 8 + e] = __bfloat162float(x[e]);
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    rope_tiles<256>(sQ, hi == 0 ? sK : nullptr, a.S, a.cosT, a.sinT);
+    if (threadIdx.x < T) {
+      const int r = threadIdx.x;
+      float dsum = 0.f, l2 = 0.f;
+      if (r < a.S) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 dv = *reinterpret_cast<const uint4*>(sdO + sw_off(r, c * 8));
+          const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(&dv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dsum += orow[c * 8 + e] * __bfloat162float(y[e]);
+        }
+        l2 = a.lse[((long long)gb * a.nh + h) * a.S + r] * kLog2e;
+      }
+      sDelta[r] = dsum;
+      sLse[r] = l2;
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+      constexpr uint32_t idSS = umma_idesc_bf16(T, T, false, false);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) umma_bf16(tS, desc_k(smem_u32(sQ), kk), desc_k(smem_u32(sK), kk), idSS, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16(tdP, desc_k(smem_u32(sdO), kk), desc_k(smem_u32(sV), kk), idSS, kk > 0);
+      umma_commit(&bar);
+    }
+    __syncwarp();
+    ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
+    phase ^= 1;
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    {
+      const int nvalid = row < a.S ? row + 1 : 0;
+      const float delta = sDelta[row], l2 = sLse[row];
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        const int c0 = half * 64 + c * 16;
+        float s[16], dp[16];
+        tmem_ld16(tS + lane_off + c0, s);
+        tmem_ld16(tdP + lane_off + c0, dp);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p = (c0 + e < nvalid) ? exp2f(s[e] * sl2 - l2) : 0.f;
+          s[e] = p;
+          dp[e] = p * (dp[e] - delta);
+        }
+        put16(sP, row, c0, s);
+        put16(sdS, row, c0, dp);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0 && ok) {
+      constexpr uint32_t idT = umma_idesc_bf16(T, D, true, true);    // A^T from [query][key] tiles
+      constexpr uint32_t idQ = umma_idesc_bf16(T, D, false, true);   // dS (K-major) x K (MN-major)
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tdV, desc_mn(smem_u32(sP), kk), desc_mn(smem_u32(sdO), kk), idT, (hi > 0 || kk > 0));
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tdK, desc_mn(smem_u32(sdS), kk), desc_mn(smem_u32(sQ), kk), idT, (hi > 0 || kk > 0));
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16(tdQ, desc_k(smem_u32(sdS + (kk >> 2) * TILE), kk & 3), desc_mn(smem_u32(sK), kk), idQ, kk > 0);
+      umma_commit(&bar);
+    }
+    __syncwarp();
+    if (ok) ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
+    phase ^= 1;
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (half == 0) {
+      float r[64];
+      tmem_row64(tdQ + lane_off, r);
+      if (ok && row < a.S)
+        store_row64(a.dqkv + ((long long)gb * a.S + row) * a.ld + h * D, r, a.scale, a.cosT, a.sinT, row, true);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  {
+    float r[64];
+    tmem_row64((half == 0 ? tdK : tdV) + lane_off, r);
+    if (ok && row < a.S) {
+      __nv_bfloat16* dst = a.dqkv + ((long long)gb * a.S + row) * a.ld;
+      if (half == 0) store_row64(dst + (a.nh + kvh) * D, r, a.scale, a.cosT, a.sinT, row, true);
+      else store_row64(dst + (a.nh + a.nkv + kvh) * D, r, 1.f, nullptr, nullptr, 0, false);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 512);
+}
+
+}  // namespace attn_tc
+}  // namespace odp
+
+static odp::attn_tc::Args tc_args(torch::Tensor qkv, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                                  torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err) {
+  TORCH_CHECK(S >= 1 && S <= odp::attn_tc::T, "tcgen05 attention handles 1 <= S <= 128");
+  TORCH_CHECK(nh % nkv == 0, "attention: heads must be a multiple of kv heads");
+  TORCH_CHECK(qkv.is_contiguous() && o.is_contiguous() && lse.is_contiguous(), "attention: contiguous tensors");
+  odp::attn_tc::Args a{};
+  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  a.ld = (nh + 2 * nkv) * odp::attn_tc::D;
+  a.S = (int)S;
+  a.nh = (int)nh;
+  a.nkv = (int)nkv;
+  a.cosT = cosT.data_ptr<float>();
+  a.sinT = sinT.data_ptr<float>();
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.ldo = nh * odp::attn_tc::D;
+  a.lse = lse.data_ptr<float>();
+  a.scale = 1.0f / sqrtf((float)odp::attn_tc::D);
+  a.err = err.data_ptr<int>();
+  return a;
+}
+
+// qkv: [GB, S, (nh+2nkv)*64] bf16 -> o: [GB, S, nh*64] bf16, lse: [GB, nh, S] fp32
+void attention_fwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                      torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        odp::attn_tc::kFwdSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        odp::attn_tc::kBwdSmem));
+    attr = true;
+  }
+  auto a = tc_args(qkv, S, nh, nkv, cosT, sinT, o, lse, err);
+  dim3 grid((unsigned)nh, (unsigned)GB);
+  odp::attn_tc::fwd_kernel<<<grid, 128, odp::attn_tc::kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// dqkv: [GB, S, (nh+2nkv)*64] bf16, the gradient w.r.t. the pre-RoPE q|k|v
+void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                      torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout, torch::Tensor dqkv,
+                      torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        odp::attn_tc::kFwdSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        odp::attn_tc::kBwdSmem));
+    attr = true;
+  }
+  TORCH_CHECK(dout.is_contiguous() && dqkv.is_contiguous(), "attention: contiguous tensors");
+  auto a = tc_args(qkv, S, nh, nkv, cosT, sinT, o, lse, err);
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  dim3 grid((unsigned)nkv, (unsigned)GB);
+  odp::attn_tc::bwd_kernel<<<grid, 256, odp::attn_tc::kBwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -41,6 +41,7 @@ from torch import nn
 
 from ..models.llama import rope_cos_sin
 from ..models.path import build_path_model
+from ..ops import attention as attn
 from ..ops._ext import check_errors, err_word, ext
 from ..ops.outer import MODE_COPY, MODE_OUTER, OuterPlan, Segment
 from ..optim.adam8bit import Adam8bit
@@ -311,7 +312,7 @@ class FusedExecutor:
         for l, lo in enumerate(lay.layers):
             X_.rmsnorm_fwd(self.X[l], MH, w32[lo.ln1:], P, self.XN1[l], MH, self.RS1[l], M, H, G, self.eps)
             self._gemm(self.XN1[l], H, MH, False, w16[lo.qkv:], H, P, False, self.QKV[l], C, MC, M, C, H, "bf16")
-            X_.attention_fwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l])
+            attn.fwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l], self.err)
             self._gemm(self.O[l], H, MH, False, w16[lo.o:], H, P, False, self.HR[l], H, MH, M, H, H, "resid",
                        R=self.X[l], ldr=H, sr=MH)
             X_.rmsnorm_fwd(self.HR[l], MH, w32[lo.ln2:], P, self.XN2[l], MH, self.RS2[l], M, H, G, self.eps)
@@ -343,8 +344,8 @@ class FusedExecutor:
                            self.DX16, gr[lo.ln2:], P, self.NORMWORK, M, H, G, 0.0)
             self._gemm(self.DX16, H, MH, False, w16[lo.o:], H, P, True, self.DOUT, H, MH, M, H, H, "bf16")
             self._gemm(self.DX16, H, MH, True, self.O[l], H, MH, True, gr[lo.o:], H, P, H, H, M, "f32")
-            X_.attention_bwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l],
-                             self.DOUT, self.DELTA, self.DQKV)
+            attn.bwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l], self.DOUT,
+                     self.DELTA, self.DQKV, self.err)
             self._gemm(self.DQKV, C, MC, False, w16[lo.qkv:], H, P, True, self.DXN, H, MH, M, H, C, "f32")
             self._gemm(self.DQKV, C, MC, True, self.XN1[l], H, MH, True, gr[lo.qkv:], H, P, C, H, M, "f32")
             X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[l], self.DXN, MH, self.DX, self.DX, MH,

@@ -1,0 +1,101 @@
+"""tcgen05 attention (csrc/attention_tc.cu) against an fp32 PyTorch reference of the same
+op (RoPE + causal softmax attention, GQA) and against the mma.sync kernels."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+D = 64
+
+
+def _bf(*shape, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(DEV).to(torch.bfloat16)
+
+
+def _close(a, b, tol):
+    a, b = a.float(), b.float()
+    err = (a - b).abs().max().item()
+    ref = b.abs().max().item() + 1e-6
+    assert err <= tol * ref, f"max err {err} vs ref max {ref} (tol {tol})"
+
+
+def _rope(x, cos, sin):
+    h = x.shape[-1] // 2
+    return x * cos + torch.cat([-x[..., h:], x[..., :h]], -1) * sin
+
+
+def _reference(qkv, nh, nkv, cos, sin):
+    B, S, _ = qkv.shape
+    x = qkv.float().requires_grad_(True)
+    q = x[..., :nh * D].view(B, S, nh, D).transpose(1, 2)
+    k = x[..., nh * D:(nh + nkv) * D].view(B, S, nkv, D).transpose(1, 2)
+    v = x[..., (nh + nkv) * D:].view(B, S, nkv, D).transpose(1, 2)
+    q, k = _rope(q, cos, sin), _rope(k, cos, sin)
+    k, v = k.repeat_interleave(nh // nkv, 1), v.repeat_interleave(nh // nkv, 1)
+    o = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(B, S, nh * D)
+    return x, o
+
+
+def _run(impl, qkv, nh, nkv, cos, sin, do, monkeypatch):
+    from opendipaco_b200.ops import check_errors
+    from opendipaco_b200.ops.attention import attention_bwd, attention_fwd
+
+    monkeypatch.setenv("ODP_ATTN_IMPL", impl)
+    o, lse = attention_fwd(qkv, nh, nkv, cos, sin)
+    dqkv = attention_bwd(qkv, o, lse, do, nh, nkv, cos, sin)
+    torch.cuda.synchronize()
+    check_errors()
+    return o, lse, dqkv
+
+
+@pytest.mark.parametrize("B,S,nh,nkv", [(3, 128, 6, 6), (2, 100, 8, 2), (4, 64, 4, 4), (2, 37, 4, 1)])
+def test_tc_attention_matches_fp32_reference(B, S, nh, nkv, monkeypatch):
+    from opendipaco_b200.models.llama import rope_cos_sin
+    from opendipaco_b200.ops.attention import use_tc
+
+    assert use_tc(S)
+    cos, sin = rope_cos_sin(D, 10000.0, S, DEV)
+    qkv = _bf(B, S, (nh + 2 * nkv) * D, seed=S)
+    do = _bf(B, S, nh * D, seed=S + 1)
+    o, lse, dqkv = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    x, ref = _reference(qkv, nh, nkv, cos, sin)
+    _close(o, ref, 2e-2)
+    ref.backward(do.float())
+    _close(dqkv, x.grad, 3e-2)
+    # log-sum-exp of the scaled causal scores
+    q = _rope(qkv.float()[..., :nh * D].view(B, S, nh, D).transpose(1, 2), cos, sin)
+    k = _rope(qkv.float()[..., nh * D:(nh + nkv) * D].view(B, S, nkv, D).transpose(1, 2), cos, sin)
+    s = (q @ k.repeat_interleave(nh // nkv, 1).transpose(-1, -2)) / D ** 0.5
+    s = s.masked_fill(torch.ones(S, S, device=DEV, dtype=torch.bool).triu(1), float("-inf"))
+    _close(lse, torch.logsumexp(s, -1), 1e-2)
+
+
+@pytest.mark.parametrize("S", [128, 64])
+def test_tc_attention_matches_mma_kernels(S, monkeypatch):
+    from opendipaco_b200.models.llama import rope_cos_sin
+
+    B, nh, nkv = 4, 6, 3
+    cos, sin = rope_cos_sin(D, 10000.0, S, DEV)
+    qkv = _bf(B, S, (nh + 2 * nkv) * D, seed=7)
+    do = _bf(B, S, nh * D, seed=8)
+    o1, l1, d1 = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    o2, l2, d2 = _run("mma", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    _close(o1, o2, 1e-2)
+    _close(l1, l2, 1e-4)
+    _close(d1, d2, 2e-2)
+
+
+def test_tc_attention_is_deterministic(monkeypatch):
+    from opendipaco_b200.models.llama import rope_cos_sin
+
+    B, S, nh, nkv = 2, 128, 4, 2
+    cos, sin = rope_cos_sin(D, 10000.0, S, DEV)
+    qkv = _bf(B, S, (nh + 2 * nkv) * D, seed=3)
+    do = _bf(B, S, nh * D, seed=4)
+    a = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    b = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
