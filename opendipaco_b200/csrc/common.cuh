@@ -106,6 +106,22 @@ ODP_DEVICE void tma_load_3d(const CUtensorMap* m, uint64_t* bar, void* dst, int 
       : "memory");
 }
 
+// 3-D tiled store shared -> global (bulk-group completion). The destination is this
+// GPU's memory; x (innermost coordinate) must be a multiple of 16 bytes.
+ODP_DEVICE void tma_store_3d(const CUtensorMap* m, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+ODP_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store has finished READING shared memory.
+ODP_DEVICE void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until every committed bulk store has completed.
+ODP_DEVICE void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy.
+ODP_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ---------------------------------------------------------------- tcgen05
 // UMMA shared-memory descriptor (sm100): start>>4 [0,14), LBO>>4 [16,30),
 // SBO>>4 [32,46), version=1 [46,48), base offset [49,52), layout [61,64).

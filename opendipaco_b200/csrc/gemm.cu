@@ -21,6 +21,11 @@
 //                H = bf16(silu(bf16 g) * bf16 u), GU aux = bf16 g, u
 //   EPI_SWIGLU_BWD  acc = dH; reads g,u; writes dG, dU (bf16) into C = [dG | dU]
 //   EPI_LOGITS   C = bf16(acc) and per-row (max, sum exp) of the rounded tile values
+//
+// bf16 outputs of 128-wide tiles (EPI_BF16, EPI_LOGITS) are written through shared
+// memory: each epilogue warp stages its 32 x 64 sub-tile in the 128-byte-swizzle layout
+// and one lane issues a TMA tensor store (no multicast; the destination is this GPU's
+// memory), so a warp's store is one bulk transfer instead of 32 row-strided ones.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <torch/extension.h>
@@ -45,6 +50,7 @@ struct GemmParams {
   float* part;  // logits: [G][M][2 * tiles_n] float2 (one per tile column half)
   float beta;
   int f_half;  // swiglu: F (rows of the gate block; up block starts at row F)
+  int tma_store;  // bf16 / logits with BN 128: stage each warp's 32 x 64 sub-tile in smem, TMA-store it
   int* err;
 };
 
@@ -57,9 +63,24 @@ struct SmemLayout {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES;  // epilogue staging: 8 warps x [32 rows][128 B]
+  static constexpr int STG_BYTES = 8 * 32 * 128;
+  static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
+  static_assert(TOTAL <= 232448, "shared memory budget");
 };
+
+// Write 32 bf16 values (columns [c0, c0 + 32) of a 64-column staging row) into a
+// [32 rows][64 bf16] staging buffer in the 128-byte-swizzle layout of the output map.
+ODP_DEVICE void stage_bf16x32(uint8_t* stg, int row, int c0, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int chunk = (c0 >> 3) + j;
+    uint4 w = make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                         pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+    *reinterpret_cast<uint4*>(stg + row * 128 + ((chunk ^ (row & 7)) << 4)) = w;
+  }
+}
 
 ODP_DEVICE float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
@@ -94,7 +115,7 @@ ODP_DEVICE void load_bf16x32(const __nv_bfloat16* src, float* v) {
 // (two warps share a lane quarter; each drains BN/2 columns).
 template <int BN, int EPI>
 ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int ch, int lane, int g, int tm,
-                              int tn) {
+                              int tn, uint8_t* stg, const CUtensorMap* tmC) {
   const int row = q * 32 + lane;
   const long long grow = (long long)tm * BM + row;
   const bool row_ok = grow < p.M;
@@ -129,6 +150,30 @@ ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int
     store_bf16x32(GU, gg);
     store_bf16x32(GU + p.f_half, uu);
   } else {
+    if constexpr (EPI == EPI_BF16 && BN == 128) {
+      if (p.tma_store) {
+        // the previous sub-tile stored from this buffer must have been read out
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 32) {
+          uint32_t r[32];
+          load32(tbase + ch * HALF + c, r);
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          stage_bf16x32(stg, lane, c, v);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(tmC, stg, tn * BN + ch * HALF, tm * BM + q * 32, g);
+          bulk_commit();
+        }
+        __syncwarp();
+        return;
+      }
+    }
 #pragma unroll 1
     for (int c = ch * HALF; c < (ch + 1) * HALF; c += 32) {
       uint32_t r[32];
@@ -214,26 +259,34 @@ ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int
 // tile (partials indexed [row][2 * tn + ch]).
 template <int BN>
 ODP_DEVICE void epilogue_logits(const GemmParams& p, uint32_t tmem_acc, int q, int ch, int lane, int g, int tm,
-                                int tn) {
+                                int tn, uint8_t* stg, const CUtensorMap* tmC) {
   const int row = q * 32 + lane;
   const long long grow = (long long)tm * BM + row;
   const bool row_ok = grow < p.M;
   const uint32_t tbase = tmem_acc + ((uint32_t)(q * 32) << 16);
   constexpr int HALF = BN / 2;
+  const bool staged = p.tma_store != 0;
+  if (staged) {
+    if (lane == 0) bulk_wait_read0();
+    __syncwarp();
+  }
   float mx = -INFINITY, se = 0.f;
 #pragma unroll 1
   for (int c = ch * HALF; c < (ch + 1) * HALF; c += 32) {
     uint32_t rr[32];
     load32(tbase + c, rr);
     const int gcol = tn * BN + c;
-    if (!row_ok || gcol >= p.N) continue;
-    const int n = min(32, p.N - gcol);
     float r[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) r[i] = bf16_round(__uint_as_float(rr[i]));
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
-    if (n == 32) store_bf16x32(dst, r);
-    else for (int i = 0; i < n; ++i) dst[i] = __float2bfloat16(r[i]);
+    if (staged) stage_bf16x32(stg, lane, c - ch * HALF, r);  // out-of-range rows/cols are clipped by the map
+    if (!row_ok || gcol >= p.N) continue;
+    const int n = min(32, p.N - gcol);
+    if (!staged) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + g * p.sc + grow * p.ldc + gcol;
+      if (n == 32) store_bf16x32(dst, r);
+      else for (int i = 0; i < n; ++i) dst[i] = __float2bfloat16(r[i]);
+    }
     float cm = -INFINITY;
 #pragma unroll
     for (int i = 0; i < 32; ++i) cm = i < n ? fmaxf(cm, r[i]) : cm;
@@ -244,6 +297,15 @@ ODP_DEVICE void epilogue_logits(const GemmParams& p, uint32_t tmem_acc, int q, i
 #pragma unroll
     for (int i = 0; i < 32; ++i) se += i < n ? __expf(r[i] - mx) : 0.f;
   }
+  if (staged) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(tmC, stg, tn * BN + ch * HALF, tm * BM + q * 32, g);
+      bulk_commit();
+    }
+    __syncwarp();
+  }
   if (row_ok) {
     float2* pp = reinterpret_cast<float2*>(p.part) + ((long long)g * p.M + grow) * (2 * p.tiles_n) + 2 * tn + ch;
     *pp = make_float2(mx, se);
@@ -252,7 +314,8 @@ ODP_DEVICE void epilogue_logits(const GemmParams& p, uint32_t tmem_acc, int q, i
 
 template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, GemmParams p) {
   using L = SmemLayout<BN, STAGES>;
   constexpr bool SPLIT_B = (EPI == EPI_SWIGLU);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -405,12 +468,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int g = t / tiles_per_g, r = t % tiles_per_g;
       const int tm = r / p.tiles_n, tn = r % p.tiles_n;
       const uint32_t tacc = tmem_base + acc * BN;
-      if constexpr (EPI == EPI_LOGITS) epilogue_logits<BN>(p, tacc, q, ch, lane, g, tm, tn);
-      else epilogue_tile<BN, EPI>(p, tacc, q, ch, lane, g, tm, tn);
+      uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;
+      if constexpr (EPI == EPI_LOGITS) epilogue_logits<BN>(p, tacc, q, ch, lane, g, tm, tn, stg, &tmC);
+      else epilogue_tile<BN, EPI>(p, tacc, q, ch, lane, g, tm, tn, stg, &tmC);
       tc_fence_before();
       mbar_arrive(&accempty[acc]);
       acc ^= 1;
       if (acc == 0) accphase ^= 1;
+    }
+    if (p.tma_store) {  // every staged store has landed before the CTA exits
+      if (lane == 0) bulk_wait0();
+      __syncwarp();
     }
   }
 
@@ -468,7 +536,8 @@ static int num_sms() {
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
-static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams& p, cudaStream_t st, int max_ctas) {
+static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmParams& p,
+                     cudaStream_t st, int max_ctas) {
   using L = SmemLayout<BN, STAGES>;
   auto kern = gemm_kernel<A_MN, B_MN, BN, STAGES, EPI>;
   static bool attr_set = false;
@@ -477,7 +546,7 @@ static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams& p
     attr_set = true;
   }
   int grid = std::min(p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
-  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, p);
+  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, mc, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -504,10 +573,16 @@ static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, 
   long long b_rows_extent = EPI == EPI_SWIGLU ? 2LL * p.f_half : p.N;
   CUtensorMap mb = B.mn ? make_map(B.ptr, p.N, p.K, B.ld, p.G, B.sg, 64)
                         : make_map(B.ptr, p.K, b_rows_extent, B.ld, p.G, B.sg, rowsB);
+  // bf16 outputs of 128-wide tiles leave through TMA stores when the layout allows it
+  const bool tma_ok = (EPI == EPI_BF16 || EPI == EPI_LOGITS) && bn == 128 &&
+                      reinterpret_cast<uintptr_t>(p.C) % 16 == 0 && (p.ldc * 2) % 16 == 0 &&
+                      (p.G == 1 || (p.sc * 2) % 16 == 0) && !getenv("ODP_GEMM_NO_TMA_STORE");
+  p.tma_store = tma_ok ? 1 : 0;
+  CUtensorMap mc = tma_ok ? make_map(p.C, p.N, p.M, p.ldc, p.G, p.sc, 32) : ma;
 #define ODP_GO(AM, BMN, BNV, ST)                                        \
   if constexpr (cfg_ok<EPI, AM, BMN, BNV>()) {                          \
     if (A.mn == AM && B.mn == BMN && bn == BNV) {                       \
-      launch_t<AM, BMN, BNV, ST, EPI>(ma, mb, p, st, max_ctas);         \
+      launch_t<AM, BMN, BNV, ST, EPI>(ma, mb, mc, p, st, max_ctas);     \
       return;                                                           \
     }                                                                   \
   }

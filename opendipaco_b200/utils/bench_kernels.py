@@ -64,6 +64,53 @@ def bench_attention(GB: int, S: int, nh: int, nkv: int, reps: int, flush) -> lis
     return out
 
 
+def bench_gemm(G: int, M: int, H: int, V: int, F: int, reps: int, flush) -> list[dict]:
+    """The vocab-sized GEMMs of the LM head and the MLP GEMMs of one layer, grouped over
+    G paths, with the epilogues the training step uses."""
+    from ..ops._ext import check_errors
+    from ..ops.gemm import gemm
+
+    dev = torch.device("cuda")
+    x = torch.randn(G, M, H, device=dev).to(torch.bfloat16)
+    w = (torch.randn(G, V, H, device=dev) * 0.02).to(torch.bfloat16)
+    logits = torch.empty(G, M, V, device=dev, dtype=torch.bfloat16)
+    tiles_n = (V + 127) // 128
+    part = torch.empty(G, M, 2 * tiles_n, 2, device=dev)
+    dx = torch.empty(G, M, H, device=dev)
+    dw = torch.empty(G, V, H, device=dev)
+    wgu = (torch.randn(G, 2 * F, H, device=dev) * 0.02).to(torch.bfloat16)
+    act = torch.empty(G, M, F, device=dev, dtype=torch.bfloat16)
+    gu = torch.empty(G, M, 2 * F, device=dev, dtype=torch.bfloat16)
+    wd = (torch.randn(G, H, F, device=dev) * 0.02).to(torch.bfloat16)
+    y = torch.empty(G, M, H, device=dev, dtype=torch.bfloat16)
+    cases = [
+        ("logits x W^T (bf16 + row max/sumexp)", M, V, H,
+         lambda: gemm(x, H, M * H, False, w, H, V * H, False, logits, V, M * V, M, V, H, G, "logits", part=part)),
+        ("dlogits x W (f32)", M, H, V,
+         lambda: gemm(logits, V, M * V, False, w, H, V * H, True, dx, H, M * H, M, H, V, G, "f32")),
+        ("dlogits^T x X (f32 dW)", V, H, M,
+         lambda: gemm(logits, V, M * V, True, x, H, M * H, True, dw, H, V * H, V, H, M, G, "f32")),
+        ("X x Wgu^T (swiglu)", M, 2 * F, H,
+         lambda: gemm(x, H, M * H, False, wgu, H, 2 * F * H, False, act, F, M * F, M, 2 * F, H, G, "swiglu",
+                      aux=gu, ldx=2 * F, sx=M * 2 * F, f_half=F)),
+        ("act x Wdown^T (bf16)", M, H, F,
+         lambda: gemm(act, F, M * F, False, wd, F, H * F, False, y, H, M * H, M, H, F, G, "bf16")),
+    ]
+    # library reference points (cuBLAS through torch) for the same shapes, bf16 out
+    cases += [
+        ("[cuBLAS] logits x W^T", M, V, H, lambda: torch.bmm(x, w.transpose(1, 2), out=logits)),
+        ("[cuBLAS] dlogits x W", M, H, V, lambda: torch.bmm(logits, w, out=y)),
+    ]
+    out = []
+    for name, m, n, k, fn in cases:
+        ms = _timeit(fn, reps, flush)
+        check_errors()
+        fl = 2.0 * G * m * n * k
+        out.append({"kernel": f"gemm {name}", "ms": round(ms, 4), "TFLOPs": round(fl / ms / 1e9, 1),
+                    "frac_of_fallback_bf16_peak": round(fl / ms / 1e9 / 1590.0, 3), "shape": [G, m, n, k]})
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--paths", type=int, default=16)
@@ -71,12 +118,17 @@ def main() -> None:
     ap.add_argument("--seq", type=int, default=128)
     ap.add_argument("--heads", type=int, default=6)
     ap.add_argument("--kv-heads", type=int, default=6)
+    ap.add_argument("--hidden", type=int, default=384)
+    ap.add_argument("--ffn", type=int, default=1024)
+    ap.add_argument("--vocab", type=int, default=32000)
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
     flush = torch.empty(64 * 1024 * 1024, device="cuda")
     cases = {"attention": lambda: bench_attention(args.paths * args.batch, args.seq, args.heads, args.kv_heads,
-                                                  args.reps, flush)}
+                                                  args.reps, flush),
+             "gemm": lambda: bench_gemm(args.paths, args.batch * args.seq, args.hidden, args.vocab, args.ffn,
+                                        args.reps, flush)}
     for name, fn in cases.items():
         if args.only and args.only != name:
             continue
