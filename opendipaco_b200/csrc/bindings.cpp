@@ -26,6 +26,9 @@ void attention_fwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
 void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                       torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout, torch::Tensor dqkv,
                       torch::Tensor err);
+void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t M, int64_t V, int64_t G,
+              torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum, torch::Tensor inv_count,
+              c10::optional<torch::Tensor> loss_out, torch::Tensor err);
 void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels,
                 int64_t M, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum,
                 torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out);
@@ -69,6 +72,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd", &attention_fwd);
   m.def("attention_bwd", &attention_bwd);
   m.def("attention_fwd_tc", &attention_fwd_tc);
+  m.def("ce_fused", &ce_fused);
   m.def("attention_bwd_tc", &attention_bwd_tc);
   m.def("ce_forward", &ce_forward);
   m.def("ce_backward", &ce_backward);

@@ -7,6 +7,9 @@
 // and valid-token count. ce_backward overwrites the logits in place with
 // dlogits = (softmax - onehot) / count (bf16), which the two backward GEMMs consume.
 //
+// ce_fused does loss and dlogits in one pass when the GEMM wrote plain bf16 logits: one
+// CTA per row keeps the row in registers, so the logits are read once and written once.
+//
 // cross_entropy_rows computes the same per-row loss straight from a logits tensor
 // (eval / EM scoring), one CTA per row.
 #include <torch/extension.h>
@@ -97,6 +100,133 @@ __global__ void ce_backward_kernel(__nv_bfloat16* logits, long long ldl, long lo
   *ptr = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// inv_count[g] = 1 / max(1, #labels >= 0 of group g): the dlogits scale, known before the loss.
+__global__ void label_count_kernel(const int* __restrict__ labels, int M, float* __restrict__ inv_count) {
+  const int g = blockIdx.x;
+  __shared__ int sc[256];
+  int c = 0;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) c += labels[(long long)g * M + i] >= 0;
+  sc[threadIdx.x] = c;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) sc[threadIdx.x] += sc[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) inv_count[g] = 1.f / (float)(sc[0] > 0 ? sc[0] : 1);
+}
+
+constexpr int kCeThreads = 256;
+constexpr int kCeMaxV = 32768;  // the row (<= 64 KB of bf16) is staged in shared memory
+
+ODP_DEVICE float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+ODP_DEVICE float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Online (max, sum exp) update with one value.
+ODP_DEVICE void online_add(float& m, float& s, float x) {
+  if (x > m) {
+    s = s * __expf(m - x) + 1.f;
+    m = x;
+  } else {
+    s += __expf(x - m);
+  }
+}
+ODP_DEVICE void online_merge(float& m, float& s, float m2, float s2) {
+  const float M = fmaxf(m, m2);
+  s = (m == -INFINITY ? 0.f : s * __expf(m - M)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - M));
+  m = M;
+}
+
+// One CTA per row. The whole bf16 row is brought into shared memory with one bulk copy
+// (completion on an mbarrier, bounded wait), then
+//   (max, sum exp) in one online pass -> lse = max + log(sum),  loss = lse - x[label]
+//   dlogits = (exp(x - lse) - onehot(label)) * inv_count[g]   written in place as bf16.
+// Rows with label < 0 get loss 0 and zero dlogits. 64 KB per CTA: three CTAs per SM
+// overlap one row's copy with another's arithmetic.
+__global__ void __launch_bounds__(kCeThreads) ce_fused_kernel(__nv_bfloat16* logits, long long ldl, long long sl,
+                                                              const int* __restrict__ labels, int M, int V,
+                                                              const float* __restrict__ inv_count,
+                                                              float* __restrict__ lse_out, float* __restrict__ row_loss,
+                                                              int* err) {
+  extern __shared__ __align__(16) uint8_t ce_smem[];
+  __shared__ uint64_t bar;
+  __shared__ float red_m[kCeThreads / 32], red_s[kCeThreads / 32];
+  const long long r = blockIdx.x;
+  const int g = (int)(r / M), m = (int)(r % M);
+  __nv_bfloat16* rowp = logits + g * sl + (long long)m * ldl;
+  uint4* row = reinterpret_cast<uint4*>(rowp);
+  const int nvec = V / 8;
+  const int y = labels[r];
+  if (y < 0) {
+    for (int i = threadIdx.x; i < nvec; i += kCeThreads) row[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+      row_loss[r] = 0.f;
+      lse_out[r] = 0.f;
+    }
+    return;
+  }
+  const uint4* srow = reinterpret_cast<const uint4*>(ce_smem);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const uint32_t bytes = (uint32_t)V * 2;
+    mbar_expect_tx(&bar, bytes);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(ce_smem)),
+                 "l"(rowp), "r"(bytes), "r"(smem_u32(&bar))
+                 : "memory");
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, err, ERR_TIMEOUT_FULL);
+  float mx = -INFINITY, se = 0.f;
+  if (ok) {
+    for (int i = threadIdx.x; i < nvec; i += kCeThreads) {
+      const uint4 v = srow[i];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        online_add(mx, se, bf_lo(w[e]));
+        online_add(mx, se, bf_hi(w[e]));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, mx, o), s2 = __shfl_xor_sync(0xffffffffu, se, o);
+    online_merge(mx, se, m2, s2);
+  }
+  if (threadIdx.x % 32 == 0) {
+    red_m[threadIdx.x / 32] = mx;
+    red_s[threadIdx.x / 32] = se;
+  }
+  __syncthreads();
+  mx = red_m[0];
+  se = red_s[0];
+#pragma unroll
+  for (int w = 1; w < kCeThreads / 32; ++w) online_merge(mx, se, red_m[w], red_s[w]);
+  if (!ok) return;  // the error word tells the host; this row is left as it was
+  const float l = mx + logf(se);
+  const float sc = inv_count[g];
+  if (threadIdx.x == 0) {
+    lse_out[r] = l;
+    const uint16_t raw = reinterpret_cast<const uint16_t*>(ce_smem)[y];
+    row_loss[r] = l - __uint_as_float((uint32_t)raw << 16);
+  }
+  for (int i = threadIdx.x; i < nvec; i += kCeThreads) {
+    const uint4 v = srow[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float p0 = __expf(bf_lo(w[e]) - l), p1 = __expf(bf_hi(w[e]) - l);
+      const int c = i * 8 + e * 2;
+      if (c == y) p0 -= 1.f;
+      if (c + 1 == y) p1 -= 1.f;
+      o[e] = pack_bf16(p0 * sc, p1 * sc);
+    }
+    row[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // Per-row CE (target < 0 -> 0) from bf16 or fp32 logits; one 256-thread CTA per row.
 template <typename T>
 __global__ void ce_rows_kernel(const T* __restrict__ logits, long long ld, const long long* __restrict__ tgt, int V,
@@ -142,6 +272,35 @@ void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl
       reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)T,
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)G,
       lse.data_ptr<float>(), row_loss.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
+                                                 loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
+                                                 loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Loss and dlogits in one pass over bf16 logits [G][M][V] (row stride ldl, group stride sl):
+// lse, row_loss per row, loss_sum / inv_count / optional per-group mean loss per group;
+// logits are overwritten with dlogits = (softmax - onehot) / count.
+void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t M, int64_t V, int64_t G,
+              torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum, torch::Tensor inv_count,
+              c10::optional<torch::Tensor> loss_out, torch::Tensor err) {
+  TORCH_CHECK(V % 8 == 0 && ldl % 8 == 0 && sl % 8 == 0 && V <= odp::kCeMaxV,
+              "ce_fused: vocab must be a multiple of 8 and at most 32768");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0, "ce_fused: logits must be 16-byte aligned");
+  c10::cuda::CUDAGuard guard(logits.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::ce_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        odp::kCeMaxV * 2));
+    attr = true;
+  }
+  odp::label_count_kernel<<<(int)G, 256, 0, st>>>(labels.data_ptr<int>(), (int)M, inv_count.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  odp::ce_fused_kernel<<<(unsigned)(G * M), odp::kCeThreads, (size_t)V * 2, st>>>(
+      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)V,
+      inv_count.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
                                                  loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),

@@ -34,6 +34,7 @@ outer SGD-Nesterov.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -252,7 +253,9 @@ class FusedExecutor:
         self.XNF = z(G, M, H, dt=b16)
         self.RSF = z(G, M)
         self.LOGITS = z(G, M, V, dt=b16)
-        self.PART = z(G, M, self.T, 2)
+        # one-pass CE keeps a row in registers (<= 32768 columns); wider vocabularies use GEMM partials
+        self.ce_fused = V % 8 == 0 and V <= 32768 and os.environ.get("ODP_CE_IMPL", "fused") == "fused"
+        self.PART = z(1) if self.ce_fused else z(G, M, self.T, 2)
         self.LSEC = z(G, M)
         self.ROWLOSS = z(G, M)
         self.LOSSSUM = z(G)
@@ -322,12 +325,19 @@ class FusedExecutor:
                        "resid", R=self.HR[l], ldr=H, sr=MH)
         L = self.L
         X_.rmsnorm_fwd(self.X[L], MH, w32[lay.normf:], P, self.XNF, MH, self.RSF, M, H, G, self.eps)
-        self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "logits",
-                   bn=128, part=self.PART)
-        X_.ce_forward(self.PART, self.T, self.LOGITS, V, M * V, labels, M, G, self.LSEC, self.ROWLOSS,
-                      self.LOSSSUM, self.INVCNT, self.LOSSES[s])
+        if self.ce_fused:
+            # plain bf16 logits (TMA-stored), then loss + dlogits in one pass over each row
+            self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "bf16",
+                       bn=128)
+            X_.ce_fused(self.LOGITS, V, M * V, labels, M, V, G, self.LSEC, self.ROWLOSS, self.LOSSSUM, self.INVCNT,
+                        self.LOSSES[s], self.err)
+        else:
+            self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "logits",
+                       bn=128, part=self.PART)
+            X_.ce_forward(self.PART, self.T, self.LOGITS, V, M * V, labels, M, G, self.LSEC, self.ROWLOSS,
+                          self.LOSSSUM, self.INVCNT, self.LOSSES[s])
+            X_.ce_backward(self.LOGITS, V, M * V, self.LSEC, labels, self.INVCNT, M, V, G)
         # ---------------- backward
-        X_.ce_backward(self.LOGITS, V, M * V, self.LSEC, labels, self.INVCNT, M, V, G)
         self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
         self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32")
         X_.rmsnorm_bwd(self.X[L], MH, w32[lay.normf:], P, self.RSF, self.DXN, MH, None, self.DX, MH, self.DX16,

@@ -86,6 +86,8 @@ def bench_gemm(G: int, M: int, H: int, V: int, F: int, reps: int, flush) -> list
     cases = [
         ("logits x W^T (bf16 + row max/sumexp)", M, V, H,
          lambda: gemm(x, H, M * H, False, w, H, V * H, False, logits, V, M * V, M, V, H, G, "logits", part=part)),
+        ("logits x W^T (plain bf16)", M, V, H,
+         lambda: gemm(x, H, M * H, False, w, H, V * H, False, logits, V, M * V, M, V, H, G, "bf16")),
         ("dlogits x W (f32)", M, H, V,
          lambda: gemm(logits, V, M * V, False, w, H, V * H, True, dx, H, M * H, M, H, V, G, "f32")),
         ("dlogits^T x X (f32 dW)", V, H, M,
@@ -111,6 +113,39 @@ def bench_gemm(G: int, M: int, H: int, V: int, F: int, reps: int, flush) -> list
     return out
 
 
+def bench_ce(G: int, M: int, V: int, reps: int, flush) -> list[dict]:
+    """The cross-entropy kernels of the LM head on bf16 logits [G, M, V]."""
+    from ..ops._ext import check_errors, err_word, ext
+
+    dev = torch.device("cuda")
+    logits = (torch.randn(G, M, V, device=dev) * 2).to(torch.bfloat16)
+    labels = torch.randint(0, V, (G * M,), device=dev, dtype=torch.int32)
+    tiles_n = (V + 127) // 128
+    part = torch.randn(G, M, 2 * tiles_n, 2, device=dev)
+    lse = torch.empty(G * M, device=dev)
+    row_loss = torch.empty(G * M, device=dev)
+    loss_sum = torch.empty(G, device=dev)
+    inv = torch.ones(G, device=dev)
+    x = ext()
+    out = []
+    cases = [
+        ("ce_forward (finalize partials + group sums)",
+         lambda: x.ce_forward(part, 2 * tiles_n, logits, V, M * V, labels, M, G, lse, row_loss, loss_sum, inv, None),
+         G * M * 2 * tiles_n * 8),
+        ("ce_backward (in place, bf16)", lambda: x.ce_backward(logits, V, M * V, lse.zero_(), labels, inv, M, V, G),
+         2 * logits.numel() * 2),
+    ]
+    if hasattr(x, "ce_fused"):
+        cases.append(("ce_fused (loss + dlogits in place, bf16)",
+                      lambda: x.ce_fused(logits, V, M * V, labels, M, V, G, lse, row_loss, loss_sum, inv, None, err_word(dev)),
+                      2 * logits.numel() * 2))
+    for name, fn, nbytes in cases:
+        ms = _timeit(fn, reps, flush)
+        check_errors()
+        out.append({"kernel": name, "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1), "shape": [G, M, V]})
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--paths", type=int, default=16)
@@ -128,7 +163,8 @@ def main() -> None:
     cases = {"attention": lambda: bench_attention(args.paths * args.batch, args.seq, args.heads, args.kv_heads,
                                                   args.reps, flush),
              "gemm": lambda: bench_gemm(args.paths, args.batch * args.seq, args.hidden, args.vocab, args.ffn,
-                                        args.reps, flush)}
+                                        args.reps, flush),
+             "ce": lambda: bench_ce(args.paths, args.batch * args.seq, args.vocab, args.reps, flush)}
     for name, fn in cases.items():
         if args.only and args.only != name:
             continue
