@@ -213,6 +213,62 @@ ODP_DEVICE void reg_tie32(uint32_t* r) {
   asm volatile("" : ODP_TIE16((r + 16)) : : "memory");
 }
 
+// ---------------------------------------------------------------- CTA pairs (cta_group::2)
+ODP_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of both CTAs of the cluster (unconditional call sites only).
+ODP_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of `p` (a shared variable of this CTA) in CTA `rank` of the cluster.
+ODP_DEVICE uint32_t mapa_rank(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+ODP_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Pair TMA load (no multicast): this CTA's tile lands in its own shared memory, the byte
+// count completes on the mbarrier at `bar_cluster` (the leader CTA's barrier).
+ODP_DEVICE void tma_load_3d_pair(const CUtensorMap* m, uint32_t bar_cluster, void* dst, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+ODP_DEVICE void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+ODP_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// M = 256 MMA over the CTA pair (issued by the leader; A rows and B rows are split
+// between the two CTAs' shared memory at the same offsets; D rows split across TMEMs).
+ODP_DEVICE void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrive on the mbarrier at this offset in both CTAs of the pair once the leader's
+// previously issued MMAs complete (multicast of the commit, not of any load).
+ODP_DEVICE void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((unsigned short)0x3)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- misc
 ODP_DEVICE float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
 

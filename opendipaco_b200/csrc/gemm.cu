@@ -150,27 +150,30 @@ ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int
     store_bf16x32(GU, gg);
     store_bf16x32(GU + p.f_half, uu);
   } else {
-    if constexpr (EPI == EPI_BF16 && BN == 128) {
+    if constexpr (EPI == EPI_BF16 && (BN == 128 || BN == 256)) {
       if (p.tma_store) {
-        // the previous sub-tile stored from this buffer must have been read out
-        if (lane == 0) bulk_wait_read0();
-        __syncwarp();
 #pragma unroll 1
-        for (int c = 0; c < HALF; c += 32) {
-          uint32_t r[32];
-          load32(tbase + ch * HALF + c, r);
-          float v[32];
+        for (int b = 0; b < HALF; b += 64) {  // one 32 x 64 box at a time through the 4 KB buffer
+          // the previous box stored from this buffer must have been read out
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+#pragma unroll 1
+          for (int c = 0; c < 64; c += 32) {
+            uint32_t r[32];
+            load32(tbase + ch * HALF + b + c, r);
+            float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          stage_bf16x32(stg, lane, c, v);
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            stage_bf16x32(stg, lane, c, v);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(tmC, stg, tn * BN + ch * HALF + b, tm * BM + q * 32, g);
+            bulk_commit();
+          }
+          __syncwarp();
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(tmC, stg, tn * BN + ch * HALF, tm * BM + q * 32, g);
-          bulk_commit();
-        }
-        __syncwarp();
         return;
       }
     }
@@ -488,6 +491,201 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
 }
 
+// ============================================================== CTA-pair variant
+// The same GEMM with each output tile (256 x BN) computed by a pair of CTAs on two SMs
+// (cluster of 2, tcgen05.mma.cta_group::2): each CTA loads its own 128 rows of A and its
+// own BN/2 rows of B, so every SM streams half as many bytes of B per FLOP as in the
+// single-CTA kernel (the LM-head GEMMs are L2-bandwidth bound at 128 x 128). Loads are
+// plain (never multicast) TMA copies into the issuing CTA's shared memory that complete
+// on the leader CTA's mbarrier; the leader alone issues MMAs; commits arrive on both
+// CTAs' barriers; each CTA's epilogue drains its own 128 TMEM lanes and the peer's
+// epilogue warps release the accumulator on the leader's barrier remotely.
+template <int BN, int STAGES>
+struct SmemLayout2 {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES;
+  static constexpr int STG_BYTES = 8 * 32 * 128;
+  static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+  static_assert(TOTAL <= 232448, "shared memory budget");
+};
+
+template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmC, GemmParams p) {
+  using L = SmemLayout2<BN, STAGES>;
+  constexpr int HB = BN / 2;  // B rows held by each CTA
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accfull = empty + STAGES;
+  uint64_t* accempty = accfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accempty + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], 16);  // one arrive per epilogue warp of both CTAs
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_holder, 2 * BN);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int tiles_per_g = p.tiles_m * p.tiles_n;
+  constexpr uint32_t kIdesc = umma_idesc_bf16(2 * BM, BN, A_MN, B_MN);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    const uint32_t full_leader = mapa_rank(&full[0], 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    bool ok = true;
+    for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+      const int g = t / tiles_per_g, r = t % tiles_per_g;
+      const int tm = r / p.tiles_n, tn = r % p.tiles_n;
+      const int row0 = tm * 2 * BM + (int)rank * BM;
+      const int col0 = tn * BN + (int)rank * HB;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, ERR_TIMEOUT_EMPTY)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* sA = smem + stage * L::STAGE_BYTES;
+          uint8_t* sB = sA + L::A_BYTES;
+          if (leader) mbar_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
+          const uint32_t fb = full_leader + stage * 8;
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_3d_pair(&tmA, fb, sA, k0, row0, g);
+          } else {
+            tma_load_3d_pair(&tmA, fb, sA, row0, k0, g);
+            tma_load_3d_pair(&tmA, fb, sA + 8192, row0 + 64, k0, g);
+          }
+          if constexpr (!B_MN) {
+            tma_load_3d_pair(&tmB, fb, sB, k0, col0, g);
+          } else {
+#pragma unroll
+            for (int j = 0; j < HB / 64; ++j) tma_load_3d_pair(&tmB, fb, sB + j * 8192, col0 + j * 64, k0, g);
+          }
+        }
+        __syncwarp();
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    // drain: the MMA has consumed (so the copies have landed in) every stage filled here
+    long long n_wait = issued < STAGES ? issued : STAGES;
+    int s = stage;
+    uint32_t ph = phase;
+    for (long long i = 0; i < n_wait; ++i) {
+      if (--s < 0) {
+        s = STAGES - 1;
+        ph ^= 1;
+      }
+      mbar_wait(&empty[s], ph, p.err, ERR_TIMEOUT_EMPTY);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t accphase = 0;
+      bool ok = true;
+      for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+        if (!mbar_wait(&accempty[acc], accphase ^ 1, p.err, ERR_TIMEOUT_TMEM_FREE)) break;
+        tc_fence_after();
+        const uint32_t dtm = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t aaddr = smem_u32(smem + stage * L::STAGE_BYTES);
+            const uint32_t baddr = aaddr + L::A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              uint64_t ad, bd;
+              if constexpr (!A_MN) ad = umma_smem_desc(aaddr + kk * 32, 16, 1024, kLayoutSW128);
+              else ad = umma_smem_desc(aaddr + kk * 2048, 8192, 1024, kLayoutSW128);
+              if constexpr (!B_MN) bd = umma_smem_desc(baddr + kk * 32, 16, 1024, kLayoutSW128);
+              else bd = umma_smem_desc(baddr + kk * 2048, 8192, 1024, kLayoutSW128);
+              umma_bf16_pair(dtm, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            }
+            umma_commit_pair(&empty[stage]);
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        if (lane == 0) umma_commit_pair(&accfull[acc]);
+        __syncwarp();
+        acc ^= 1;
+        if (acc == 0) accphase ^= 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp % 4;
+    const int ch = (warp - 2) / 4;
+    const uint32_t accempty_leader = mapa_rank(&accempty[0], 0);
+    uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;
+    int acc = 0;
+    uint32_t accphase = 0;
+    for (int t = pair; t < p.num_tiles; t += npairs) {
+      if (!mbar_wait(&accfull[acc], accphase, p.err, ERR_TIMEOUT_ACCUM)) break;
+      tc_fence_after();
+      const int g = t / tiles_per_g, r = t % tiles_per_g;
+      const int tm = r / p.tiles_n, tn = r % p.tiles_n;
+      // this CTA holds rows [tm * 256 + rank * 128, +128) of the pair tile: a 128-row tile index
+      epilogue_tile<BN, EPI>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, stg, &tmC);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(accempty_leader + acc * 8);
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) accphase ^= 1;
+    }
+    if (p.tma_store) {
+      if (lane == 0) bulk_wait0();
+      __syncwarp();
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // every MMA consumed, every remote arrival delivered, before TMEM goes away
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, 2 * BN);
+}
+
 // ============================================================== host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -550,6 +748,22 @@ static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
+static void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmParams& p,
+                        cudaStream_t st, int max_ctas) {
+  using L = SmemLayout2<BN, STAGES>;
+  auto kern = gemm2_kernel<A_MN, B_MN, BN, STAGES, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    attr_set = true;
+  }
+  int grid = std::min(2 * p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
+  grid &= ~1;  // whole CTA pairs
+  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, mc, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Operand description: data pointer, leading dim (elements), group stride (elements).
 struct Operand {
   const void* ptr;
@@ -566,8 +780,54 @@ constexpr bool cfg_ok() {
   return BN != 256 || (!AM && !BMN);
 }
 
+template <int EPI, bool AM, bool BMN, int BN>
+constexpr bool cfg2_ok() {
+  if (EPI == EPI_BF16) return !AM;
+  return EPI == EPI_F32;
+}
+
+// CTA-pair path: bf16 / fp32 epilogues with at least one full 256-row pair tile.
+template <int EPI>
+static bool dispatch_pair(const Operand& A, const Operand& B, GemmParams& p, cudaStream_t st, int max_ctas) {
+  if constexpr (EPI != EPI_BF16 && EPI != EPI_F32) {
+    return false;
+  } else {
+    const char* env = getenv("ODP_GEMM_2SM");
+    if ((env && env[0] == '0') || p.M < 2 * BM || (max_ctas > 0 && max_ctas < 2)) return false;
+    if (EPI == EPI_BF16 && A.mn) return false;
+    // 256-wide pair tiles only: for narrow N (e.g. 384 with a long K) the single-CTA kernel
+    // is as fast (measured), so the pair path is reserved for wide outputs.
+    if (!(p.N >= 256 && (p.N % 256 == 0 || p.N >= 2048))) return false;
+    const int bn = 256;
+    p.tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
+    p.tiles_n = (p.N + bn - 1) / bn;
+    p.num_tiles = p.tiles_m * p.tiles_n * p.G;
+    CUtensorMap ma = A.mn ? make_map(A.ptr, p.M, p.K, A.ld, p.G, A.sg, 64) : make_map(A.ptr, p.K, p.M, A.ld, p.G, A.sg, BM);
+    CUtensorMap mb = B.mn ? make_map(B.ptr, p.N, p.K, B.ld, p.G, B.sg, 64)
+                          : make_map(B.ptr, p.K, p.N, B.ld, p.G, B.sg, bn / 2);
+    const bool tma_ok = EPI == EPI_BF16 && reinterpret_cast<uintptr_t>(p.C) % 16 == 0 && (p.ldc * 2) % 16 == 0 &&
+                        (p.G == 1 || (p.sc * 2) % 16 == 0) && !getenv("ODP_GEMM_NO_TMA_STORE");
+    p.tma_store = tma_ok ? 1 : 0;
+    CUtensorMap mc = tma_ok ? make_map(p.C, p.N, p.M, p.ldc, p.G, p.sc, 32) : ma;
+#define ODP_GO2(AM, BMN, BNV, ST)                                       \
+  if constexpr (cfg2_ok<EPI, AM, BMN, BNV>()) {                         \
+    if (A.mn == AM && B.mn == BMN && bn == BNV) {                       \
+      launch_pair<AM, BMN, BNV, ST, EPI>(ma, mb, mc, p, st, max_ctas);  \
+      return true;                                                      \
+    }                                                                   \
+  }
+    ODP_GO2(false, false, 256, 6)
+    ODP_GO2(false, true, 256, 6)
+    ODP_GO2(true, false, 256, 6)
+    ODP_GO2(true, true, 256, 6)
+#undef ODP_GO2
+    return false;
+  }
+}
+
 template <int EPI>
 static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, cudaStream_t st, int max_ctas) {
+  if (dispatch_pair<EPI>(A, B, p, st, max_ctas)) return;
   const int rowsB = EPI == EPI_SWIGLU ? bn / 2 : bn;
   CUtensorMap ma = A.mn ? make_map(A.ptr, p.M, p.K, A.ld, p.G, A.sg, 64) : make_map(A.ptr, p.K, p.M, A.ld, p.G, A.sg, BM);
   long long b_rows_extent = EPI == EPI_SWIGLU ? 2LL * p.f_half : p.N;
