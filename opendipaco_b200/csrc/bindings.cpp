@@ -28,10 +28,17 @@ void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
                       torch::Tensor err);
 void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t M, int64_t V, int64_t G,
               torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum, torch::Tensor inv_count,
-              c10::optional<torch::Tensor> loss_out, torch::Tensor err);
+              c10::optional<torch::Tensor> loss_out, torch::Tensor err, c10::optional<torch::Tensor> inv_given);
+void dp_barrier(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, torch::Tensor err);
+void dp_grad_reduce_norm(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, int64_t G, int64_t P,
+                         int64_t stride, int64_t s0, int64_t s1, torch::Tensor part, double max_norm,
+                         torch::Tensor coef, torch::Tensor gnorm, torch::Tensor err);
+void dp_adamw(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, int64_t G, int64_t stride,
+              int64_t stride16, int64_t s0, int64_t s1, torch::Tensor coef, torch::Tensor sched, double b1, double b2,
+              double eps, double wd, torch::Tensor err);
 void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels,
                 int64_t M, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum,
-                torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out);
+                torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out, c10::optional<torch::Tensor> inv_given);
 void ce_backward(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor lse, torch::Tensor labels,
                  torch::Tensor inv_count, int64_t M, int64_t V, int64_t G);
 torch::Tensor cross_entropy_rows(torch::Tensor logits, torch::Tensor target);
@@ -73,6 +80,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_bwd", &attention_bwd);
   m.def("attention_fwd_tc", &attention_fwd_tc);
   m.def("ce_fused", &ce_fused);
+  m.def("dp_barrier", &dp_barrier);
+  m.def("dp_grad_reduce_norm", &dp_grad_reduce_norm);
+  m.def("dp_adamw", &dp_adamw);
   m.def("attention_bwd_tc", &attention_bwd_tc);
   m.def("ce_forward", &ce_forward);
   m.def("ce_backward", &ce_backward);

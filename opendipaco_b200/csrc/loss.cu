@@ -40,9 +40,11 @@ __global__ void ce_finalize_kernel(const float2* __restrict__ part, int T, const
 }
 
 // One block per group: loss_sum[g] = sum of row losses (fixed order), count[g] = valid rows.
+// With inv_given (the normaliser of a batch split over several GPUs, known on the host)
+// the mean uses it and out_inv_count is left alone.
 __global__ void group_sum_kernel(const float* __restrict__ row_loss, const int* __restrict__ labels, int M,
                                  float* __restrict__ out_sum, float* __restrict__ out_inv_count,
-                                 float* __restrict__ out_loss) {
+                                 float* __restrict__ out_loss, const float* __restrict__ inv_given) {
   const int g = blockIdx.x;
   __shared__ float ss[256];
   __shared__ int sc[256];
@@ -63,10 +65,14 @@ __global__ void group_sum_kernel(const float* __restrict__ row_loss, const int* 
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    const float cnt = (float)(sc[0] > 0 ? sc[0] : 1);
     out_sum[g] = ss[0];
-    out_inv_count[g] = 1.f / cnt;
-    if (out_loss) out_loss[g] = ss[0] / cnt;
+    if (inv_given) {
+      if (out_loss) out_loss[g] = ss[0] * inv_given[g];
+    } else {
+      const float cnt = (float)(sc[0] > 0 ? sc[0] : 1);
+      out_inv_count[g] = 1.f / cnt;
+      if (out_loss) out_loss[g] = ss[0] / cnt;
+    }
   }
 }
 
@@ -264,7 +270,8 @@ __global__ void ce_rows_kernel(const T* __restrict__ logits, long long ld, const
 
 void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels,
                 int64_t M, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum,
-                torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out) {
+                torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out,
+                c10::optional<torch::Tensor> inv_given) {
   c10::cuda::CUDAGuard guard(logits.device());
   auto st = at::cuda::getCurrentCUDAStream();
   const int R = (int)(G * M);
@@ -275,7 +282,8 @@ void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
                                                  loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
-                                                 loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr);
+                                                 loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr,
+                                                 inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -284,7 +292,7 @@ void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl
 // logits are overwritten with dlogits = (softmax - onehot) / count.
 void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t M, int64_t V, int64_t G,
               torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum, torch::Tensor inv_count,
-              c10::optional<torch::Tensor> loss_out, torch::Tensor err) {
+              c10::optional<torch::Tensor> loss_out, torch::Tensor err, c10::optional<torch::Tensor> inv_given) {
   TORCH_CHECK(V % 8 == 0 && ldl % 8 == 0 && sl % 8 == 0 && V <= odp::kCeMaxV,
               "ce_fused: vocab must be a multiple of 8 and at most 32768");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0, "ce_fused: logits must be 16-byte aligned");
@@ -296,15 +304,19 @@ void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor label
                                         odp::kCeMaxV * 2));
     attr = true;
   }
-  odp::label_count_kernel<<<(int)G, 256, 0, st>>>(labels.data_ptr<int>(), (int)M, inv_count.data_ptr<float>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const float* given = inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr;
+  if (!given) {
+    odp::label_count_kernel<<<(int)G, 256, 0, st>>>(labels.data_ptr<int>(), (int)M, inv_count.data_ptr<float>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
   odp::ce_fused_kernel<<<(unsigned)(G * M), odp::kCeThreads, (size_t)V * 2, st>>>(
       reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)V,
-      inv_count.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(), err.data_ptr<int>());
+      given ? given : inv_count.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(),
+      err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
                                                  loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
-                                                 loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr);
+                                                 loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr, given);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

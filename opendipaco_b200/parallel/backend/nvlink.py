@@ -48,8 +48,9 @@ def _ru(n: int, a: int = ALIGN) -> int:
 class NVLinkBackend(TorchDistBackend):
     outer_launches = 3
 
-    def __init__(self, topology, device: torch.device | None = None):
-        super().__init__(topology, device)
+    def __init__(self, topology, device: torch.device | None = None, dp: int = 1):
+        super().__init__(topology, device, dp=dp)
+        self._dp_handles: list = []
         self._offs: dict[str, int] | None = None
         self._tables = None
         self._epoch = 0
@@ -89,6 +90,36 @@ class NVLinkBackend(TorchDistBackend):
         mom = {k: self.MOM[o:o + sizes[k]] for k, o in self._offs.items()
                if self.owns_module(k) and not is_private_key(k)}
         return glob, mom
+
+    # ------------------------------------------------------------------ data parallelism
+    def dp_tensor(self, shape, dtype) -> torch.Tensor:
+        """A zeroed tensor in memory every member of this rank's data-parallel group can
+        address (symmetric allocation, rendezvous over the group)."""
+        import math
+
+        import torch.distributed._symmetric_memory as symm
+
+        n = max(math.prod(shape), 1)
+        t = symm.empty(n, dtype=dtype, device=self.device)
+        t.zero_()
+        h = symm.rendezvous(t, self.dp_group.group_name)
+        self._dp_handles.append((t, h))
+        return t.view(*shape)
+
+    def dp_table(self, w32, w16, grad, m1, m2, G: int) -> torch.Tensor:
+        """Device table int64 [7][8] of every member's W32, W16, GRAD, M1, M2, signal pad
+        and norm-exchange buffer (the layout the ``dp_*`` kernels read)."""
+        pad = self.dp_tensor((8,), torch.int32)
+        norm = self.dp_tensor((8 * max(G, 1),), torch.float32)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.dp_group)
+        handles = {t.data_ptr(): h for t, h in self._dp_handles}
+        tab = torch.zeros(7, 8, dtype=torch.int64)
+        for row, t in enumerate((w32, w16, grad, m1, m2, pad, norm)):
+            h = handles[t.data_ptr()]
+            for m, ptr in enumerate(h.buffer_ptrs):
+                tab[row, m] = ptr
+        return tab.to(self.device)
 
     # ------------------------------------------------------------------ slices
     def slice_of(self, key: str) -> tuple[int, int]:

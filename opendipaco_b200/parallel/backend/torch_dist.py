@@ -8,7 +8,12 @@ tensor of the key's summed delta plus a 1-element weight. Differences here:
 * the per-key tensors are flattened into ONE buffer before the all-reduce (one
   NCCL call per key instead of one per parameter), and the weight rides in the
   same buffer, so there is no extra scalar collective and no ``.item()`` per key
-  beyond the final one.
+  beyond the final one;
+* ``dp > 1`` (intra-path data parallelism, no counterpart in the reference): ranks
+  form groups of ``dp`` consecutive ranks, paths are placed over groups, and every
+  member of a group holds the group's paths. A path's ranks are all its group's
+  members; only the first member of a group contributes to the outer reduction (the
+  members hold identical pseudo-gradients).
 
 The device outer step of the B200 engine does not go through this class; it is
 the NCCL baseline the fused NVLink kernel is compared against.
@@ -25,16 +30,29 @@ from .base import ReducedDelta, SyncBackend
 
 
 class TorchDistBackend(SyncBackend):
-    def __init__(self, topology: PathTopology, device: torch.device | None = None):
+    def __init__(self, topology: PathTopology, device: torch.device | None = None, dp: int = 1):
         if not dist.is_initialized():
             raise RuntimeError("torch.distributed is not initialized; call "
                                "dist.init_process_group first")
         self.topology = topology
         self.world_size = dist.get_world_size()
         self.rank = dist.get_rank()
-        self._ranks = path_ranks(topology.num_paths, self.world_size)
-        self._paths = [topology.path_from_index(i)
-                       for i in rank_paths(topology.num_paths, self.world_size, self.rank)]
+        if dp < 1 or self.world_size % dp:
+            raise ValueError(f"data-parallel degree {dp} must divide the world size {self.world_size}")
+        self.dp = dp
+        self.dp_index = self.rank % dp
+        ngroups, grp = self.world_size // dp, self.rank // dp
+        self.dp_ranks = list(range(grp * dp, grp * dp + dp))
+        self._path_group = path_ranks(topology.num_paths, ngroups)
+        self._ranks = [g * dp for g in self._path_group]  # first member of each path's group
+        self._paths = [topology.path_from_index(i) for i in rank_paths(topology.num_paths, ngroups, grp)]
+        # one subgroup per data-parallel group (built in the same order on every rank)
+        self.dp_group = None
+        if dp > 1:
+            for g in range(ngroups):
+                pg = dist.new_group(ranks=list(range(g * dp, g * dp + dp)))
+                if g == grp:
+                    self.dp_group = pg
         if device is None:
             device = (torch.device(f"cuda:{self.rank % torch.cuda.device_count()}")
                       if torch.cuda.is_available() else torch.device("cpu"))
@@ -49,6 +67,19 @@ class TorchDistBackend(SyncBackend):
     def rank_of_path(self, path: Path) -> int:
         return self._ranks[self.topology.path_index(path)]
 
+    def sharing_ranks(self, key: str) -> list[int]:
+        """Sorted ranks holding >= 1 path through ``key`` (every member of its groups)."""
+        out = set()
+        for p in self.topology.paths_through_module(key):
+            g = self._path_group[self.topology.path_index(p)]
+            out.update(range(g * self.dp, g * self.dp + self.dp))
+        return sorted(out)
+
+    def dp_allreduce(self, t: torch.Tensor) -> None:
+        """Sum ``t`` over this rank's data-parallel group (host-side, off the hot path)."""
+        if self.dp > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.dp_group)
+
     def owned_paths(self) -> list[Path]:
         return list(self._paths)
 
@@ -62,6 +93,8 @@ class TorchDistBackend(SyncBackend):
         ts = [t.to(self.device) for t in local.summed]
         flat = torch.cat([t.reshape(-1).float() for t in ts]
                          + [torch.tensor([local.weight], device=self.device, dtype=torch.float32)])
+        if self.dp_index:
+            flat.zero_()  # the group's first member speaks for its identical replicas
         dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self._groups[key])
         out, off = [], 0
         for t in ts:
@@ -94,6 +127,8 @@ class TorchDistBackend(SyncBackend):
         _, acc, apply, outer = cache
         acc.run(0.0, 0.0, False, False)
         for s in outer:
+            if self.dp_index:
+                s.delta.zero_()
             dist.all_reduce(s.delta, op=dist.ReduceOp.SUM, group=self._groups[s.key])
         dl = ex.e.diloco
         apply.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first)

@@ -138,9 +138,21 @@ class FusedExecutor:
         self.layout = PathLayout(pms[0], cfg)
         P, G = self.layout.P, self.G
         self.P = P
-        self.W32 = torch.zeros(G, P, device=self.dev, dtype=torch.float32)
-        self.W16 = torch.zeros(G, P, device=self.dev, dtype=torch.bfloat16)
-        self.GRAD = torch.zeros(G, P, device=self.dev, dtype=torch.float32)
+        be = engine.backend
+        # intra-path data parallelism: this path group's batch is split over `dp` GPUs whose
+        # masters, bf16 copies, gradients and moments sit in peer-addressable memory
+        self.dp = int(getattr(be, "dp", 1))
+        if self.dp > 1:
+            if not hasattr(be, "dp_tensor"):
+                raise NotImplementedError("intra-path data parallelism needs a peer-memory backend (NVLinkBackend)")
+            if self.opt8:
+                raise NotImplementedError("intra-path data parallelism is implemented for the AdamW inner optimizer")
+            zeros = lambda *shape, dtype=torch.float32: be.dp_tensor(shape, dtype)  # noqa: E731
+        else:
+            zeros = lambda *shape, dtype=torch.float32: torch.zeros(*shape, device=self.dev, dtype=dtype)  # noqa: E731
+        self.W32 = zeros(G, P)
+        self.W16 = zeros(G, P, dtype=torch.bfloat16)
+        self.GRAD = zeros(G, P)
         if self.opt8:
             nb = P // ALIGN
             self.MQ = torch.zeros(G * nb, ALIGN, device=self.dev, dtype=torch.int8)
@@ -149,11 +161,18 @@ class FusedExecutor:
             self.VLO = torch.zeros(G * nb, device=self.dev)
             self.VSC = torch.zeros(G * nb, device=self.dev)
         else:
-            self.MOM1 = torch.zeros(G, P, device=self.dev, dtype=torch.float32)
-            self.MOM2 = torch.zeros(G, P, device=self.dev, dtype=torch.float32)
+            self.MOM1 = zeros(G, P)
+            self.MOM2 = zeros(G, P)
         for g, pm in enumerate(pms):
             _rebind(pm, None, self.W32[g], self.layout.by_name, "")
         self.W16.copy_(self.W32)
+        if self.dp > 1:
+            # member j of the group updates shard [j * PS, (j + 1) * PS) of every path
+            self.dp_index = be.dp_index
+            ps = _ru((P + self.dp - 1) // self.dp)
+            self.dp_s0, self.dp_s1 = min(P, self.dp_index * ps), min(P, (self.dp_index + 1) * ps)
+            self.dp_tab = be.dp_table(self.W32, self.W16, self.GRAD, self.MOM1, self.MOM2, G)
+            self.dp_counter = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.pms = dict(zip(self.paths, pms))
         if engine.materialize == "eager":
             engine.path_models.update(self.pms)
@@ -275,10 +294,12 @@ class FusedExecutor:
         self.LABELS = z(steps, G, M, dt=torch.int32)
         self.SCHED = z(steps, G, 4)
         self.LOSSES = z(steps, G)
+        self.INVC = z(steps, G)  # 1 / valid labels of each (step, path) batch, for split batches
         self.ids_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
         self.labels_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
         self.sched_host = torch.zeros(steps, G, 4, dtype=torch.float32).pin_memory()
         self.loss_host = torch.zeros(G, dtype=torch.float32).pin_memory()
+        self.invc_host = torch.zeros(steps, G, dtype=torch.float32).pin_memory()
         self.cos, self.sin = rope_cos_sin(64, bb.rope_theta, S, dev)
         self.err = err_word(dev)
         self._shape = (B, S, steps)
@@ -330,13 +351,15 @@ class FusedExecutor:
             self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "bf16",
                        bn=128)
             X_.ce_fused(self.LOGITS, V, M * V, labels, M, V, G, self.LSEC, self.ROWLOSS, self.LOSSSUM, self.INVCNT,
-                        self.LOSSES[s], self.err)
+                        self.LOSSES[s], self.err, self.INVC[s] if self.dp > 1 else None)
         else:
             self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "logits",
                        bn=128, part=self.PART)
+            given = self.INVC[s] if self.dp > 1 else None
             X_.ce_forward(self.PART, self.T, self.LOGITS, V, M * V, labels, M, G, self.LSEC, self.ROWLOSS,
-                          self.LOSSSUM, self.INVCNT, self.LOSSES[s])
-            X_.ce_backward(self.LOGITS, V, M * V, self.LSEC, labels, self.INVCNT, M, V, G)
+                          self.LOSSSUM, self.INVCNT, self.LOSSES[s], given)
+            X_.ce_backward(self.LOGITS, V, M * V, self.LSEC, labels, self.INVCNT if given is None else given, M, V,
+                           G)
         # ---------------- backward
         self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
         self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32")
@@ -365,10 +388,18 @@ class FusedExecutor:
         X_.embedding_bwd(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V)
         # ---------------- optimizer
         clip = self.e.diloco.inner_grad_clip
-        X_.grad_clip_coef(self.GRAD, P, P, G, float(clip) if clip is not None else 0.0, self.CLIPWORK,
-                          self.COEF, self.GNORM)
+        clipv = float(clip) if clip is not None else 0.0
         dl = self.e.diloco
         b1, b2 = dl.inner_betas
+        if self.dp > 1:
+            # reduce-scatter of the group's gradients + global clip norm, then AdamW on this
+            # member's shard storing weights and moments into every member (all-gather)
+            X_.dp_grad_reduce_norm(self.dp_tab, self.dp_counter, self.dp_index, self.dp, G, P, P, self.dp_s0,
+                                   self.dp_s1, self.CLIPWORK, clipv, self.COEF, self.GNORM, self.err)
+            X_.dp_adamw(self.dp_tab, self.dp_counter, self.dp_index, self.dp, G, P, P, self.dp_s0, self.dp_s1,
+                        self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, self.err)
+            return
+        X_.grad_clip_coef(self.GRAD, P, P, G, clipv, self.CLIPWORK, self.COEF, self.GNORM)
         if self.opt8:
             X_.adam8bit_step(self.W32.view(-1), self.GRAD.view(-1), self.MQ, self.MABS, self.VQ, self.VLO,
                              self.VSC, self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay,
@@ -387,7 +418,10 @@ class FusedExecutor:
             sh = corpus.shard(self.topo.path_index(path))
             shards.append(sh)
             active.append(sh.size(0) > 0)
-        B = batch_size
+        if batch_size % self.dp:
+            raise ValueError(f"batch_size {batch_size} must be divisible by the data-parallel degree {self.dp}")
+        B = batch_size // self.dp  # sequences of each step's batch trained on this GPU
+        j0 = (self.dp_index if self.dp > 1 else 0) * B
         if self._shape != (B, S, steps):
             self._alloc(B, S, steps)
         ids = self.ids_host.view(steps, self.G, B, S)
@@ -401,12 +435,17 @@ class FusedExecutor:
         b1, b2 = dl.inner_betas
         sched = self.sched_host
         sched.zero_()
+        invc = self.invc_host
+        invc.fill_(1.0)
         for g, (sh, act) in enumerate(zip(shards, active)):
             if not act:
                 continue
             idx = batch_indices(sh.size(0), batch_size, steps, e._gen)
             for i, rows in enumerate(idx):
-                seqs = sh[rows].to(torch.int32)
+                # the whole batch is sampled (same generator calls on every member), this
+                # GPU trains rows [j0, j0 + B); the loss is normalised by the whole batch
+                invc[i, g] = 1.0 / max(1, rows.numel() * (S - 1))
+                seqs = sh[rows[j0:j0 + B]].to(torch.int32)
                 bs = seqs.size(0)
                 ids[i, g, :bs] = seqs
                 lab[i, g, :bs, :-1] = seqs[:, 1:]
@@ -420,6 +459,7 @@ class FusedExecutor:
         return active
 
     def _upload(self) -> None:
+        self.INVC.copy_(self.invc_host, non_blocking=True)
         self.IDS.copy_(self.ids_host, non_blocking=True)
         self.LABELS.copy_(self.labels_host, non_blocking=True)
         self.SCHED.copy_(self.sched_host, non_blocking=True)
@@ -435,7 +475,11 @@ class FusedExecutor:
             if a:
                 self.steps_taken[g] += steps
         norms = self._outer(corpus, active)
-        self.loss_host.copy_(self.LOSSES[steps - 1], non_blocking=True)
+        last = self.LOSSES[steps - 1]
+        if self.dp > 1:
+            last = last.clone()
+            self.e.backend.dp_allreduce(last)  # partial losses of the group's batch slices
+        self.loss_host.copy_(last, non_blocking=True)
         torch.cuda.current_stream(self.dev).synchronize()
         check_errors(self.dev)
         losses = {p: float(self.loss_host[g]) for g, p in enumerate(self.paths) if active[g]}
@@ -476,7 +520,8 @@ class FusedExecutor:
                 loc32.append(self.W32[g, a:b])
                 loc16.append(self.W16[g, a:b])
                 pidx = self.topo.path_index(self.paths[g])
-                w.append(e._outer_weight(key, pidx, corpus) if active[g] else 0.0)
+                lead = self.dp == 1 or self.dp_index == 0  # a path's DP replicas hold the same delta
+                w.append(e._outer_weight(key, pidx, corpus) if active[g] and lead else 0.0)
             if is_private_key(key):
                 if users:
                     segs.append(Segment(key, self.glob[key], None, loc32[:1], [None], [1.0], mode=MODE_COPY))
@@ -530,12 +575,12 @@ class FusedExecutor:
 
     def launches_per_round(self) -> int:
         """Kernels of this package launched per round (inner steps + outer step)."""
-        per_step = 14 + 22 * self.L
+        per_step = 14 + 22 * self.L + (2 if self.dp > 1 else 0)
         outer = getattr(self.e.backend, "outer_launches", 1) if getattr(self.e.backend, "world_size", 1) > 1 else 1
         return self.e.diloco.inner_steps * per_step + outer
 
     def h2d_bytes_per_round(self) -> int:
-        return int(self.IDS.numel() * 4 + self.LABELS.numel() * 4 + self.SCHED.numel() * 4)
+        return int(self.IDS.numel() * 4 + self.LABELS.numel() * 4 + self.SCHED.numel() * 4 + self.INVC.numel() * 4)
 
     def d2h_bytes_per_round(self) -> int:
         chunks = self._plan.total_chunks if self._plan is not None else 0

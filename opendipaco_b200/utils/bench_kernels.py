@@ -130,14 +130,16 @@ def bench_ce(G: int, M: int, V: int, reps: int, flush) -> list[dict]:
     out = []
     cases = [
         ("ce_forward (finalize partials + group sums)",
-         lambda: x.ce_forward(part, 2 * tiles_n, logits, V, M * V, labels, M, G, lse, row_loss, loss_sum, inv, None),
+         lambda: x.ce_forward(part, 2 * tiles_n, logits, V, M * V, labels, M, G, lse, row_loss, loss_sum, inv, None,
+                              None),
          G * M * 2 * tiles_n * 8),
         ("ce_backward (in place, bf16)", lambda: x.ce_backward(logits, V, M * V, lse.zero_(), labels, inv, M, V, G),
          2 * logits.numel() * 2),
     ]
     if hasattr(x, "ce_fused"):
         cases.append(("ce_fused (loss + dlogits in place, bf16)",
-                      lambda: x.ce_fused(logits, V, M * V, labels, M, V, G, lse, row_loss, loss_sum, inv, None, err_word(dev)),
+                      lambda: x.ce_fused(logits, V, M * V, labels, M, V, G, lse, row_loss, loss_sum, inv, None, err_word(dev),
+                                         None),
                       2 * logits.numel() * 2))
     for name, fn, nbytes in cases:
         ms = _timeit(fn, reps, flush)

@@ -3,7 +3,8 @@
     python -m torch.distributed.run --nproc-per-node N tests/mp_worker.py OUT_DIR MODE
 
 MODE: "cpu" (gloo, module executor, TorchDistBackend), "nccl" (fused executor,
-NCCL outer step) or "nvlink" (fused executor, peer-memory outer step). Writes
+NCCL outer step) or "nvlink" (fused executor, peer-memory outer step); a "_dp2"
+suffix puts every path on a group of two ranks (intra-path data parallelism). Writes
 ``OUT_DIR/{MODE}_rank{r}.pt`` with the rank's bank, losses and a consistency flag.
 """
 
@@ -25,8 +26,10 @@ from opendipaco_b200.topology import is_private_key  # noqa: E402
 
 def main():
     out_dir, mode = sys.argv[1], sys.argv[2]
+    dp = 2 if mode.endswith("_dp2") else 1
+    base = mode[:-4] if dp > 1 else mode
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-    if mode == "cpu":
+    if base == "cpu":
         dist.init_process_group("gloo", timeout=timedelta(seconds=60))
         dev = torch.device("cpu")
         bb = BackboneConfig(vocab_size=128, hidden_size=32, num_attention_heads=4, intermediate_size=64,
@@ -41,16 +44,16 @@ def main():
                             layers_per_level=[1, 1], max_position_embeddings=128)
         seq = 64
     cfg = DiPaCoConfig(backbone=bb, level_sizes=[2, 2], sequence_length=seq)
-    dl = DiLoCoConfig(inner_steps=3, inner_lr=1e-3, inner_autocast=mode != "cpu")
+    dl = DiLoCoConfig(inner_steps=3, inner_lr=1e-3, inner_autocast=base != "cpu")
     docs = zipf_documents(vocab_size=bb.vocab_size, num_documents=160, min_len=64, max_len=400, seed=1)
     corpus = ShardedCorpus.from_assignments(docs, torch.arange(len(docs)) % 4, 4, seq)
     topo = cfg.build_topology()
-    if mode == "nvlink":
+    if base == "nvlink":
         from opendipaco_b200.parallel.backend.nvlink import NVLinkBackend
 
-        backend = NVLinkBackend(topo, device=dev)
+        backend = NVLinkBackend(topo, device=dev, dp=dp)
     else:
-        backend = TorchDistBackend(topo, device=dev)
+        backend = TorchDistBackend(topo, device=dev, dp=dp)
     eng = DiPaCoEngine(cfg, dl, backend, device=dev, seed=0)
     hist = eng.fit(corpus, num_rounds=3, batch_size=4, log_every=0)
     # shared modules must be identical on every rank that owns them
@@ -76,7 +79,7 @@ def main():
     # checkpoint round trip (momentum gathered from the slice owners)
     ck = os.path.join(out_dir, f"ckpt_{mode}")
     save_checkpoint(eng, ck)
-    eng2 = DiPaCoEngine(cfg, dl, (type(backend))(topo, device=dev), device=dev, seed=5)
+    eng2 = DiPaCoEngine(cfg, dl, (type(backend))(topo, device=dev, dp=dp), device=dev, seed=5)
     load_checkpoint(eng2, ck)
     same = all(torch.equal(a, b) for k in eng.bank
                for a, b in zip(eng.bank[k].state_dict().values(), eng2.bank[k].state_dict().values()))

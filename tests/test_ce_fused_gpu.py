@@ -27,7 +27,7 @@ def test_ce_fused_matches_fp32_reference(G, M, V):
     ref_loss = torch.stack([F.cross_entropy(x[i], labels[i], ignore_index=-100) for i in range(G)])
     ref_loss.sum().backward()
     d = logits.clone()
-    ext().ce_fused(d, V, M * V, lab32, M, V, G, lse, row_loss, loss_sum, inv, loss, err_word(DEV))
+    ext().ce_fused(d, V, M * V, lab32, M, V, G, lse, row_loss, loss_sum, inv, loss, err_word(DEV), None)
     torch.cuda.synchronize()
     check_errors()
     torch.testing.assert_close(row_loss, ref_rows.detach(), rtol=1e-4, atol=1e-4)

@@ -29,6 +29,46 @@ def test_gloo_two_ranks_consistent_and_resumable(tmp_path):
     assert set(outs[1]["losses"][0]) == {(1, 0), (1, 1)}
 
 
+def test_gloo_data_parallel_groups_match_plain_ranks(tmp_path):
+    """dp=2 on 4 ranks (groups {0,1}, {2,3}) gives the same banks as 2 plain ranks: the
+    replicas train identical copies and only each group's first member reduces."""
+    plain = _launch(tmp_path, "cpu", 2, 29617)
+    dp = _launch(tmp_path, "cpu_dp2", 4, 29619)
+    for o in dp:
+        assert o["consistent"] and o["ckpt_same"] and o["resumed"]
+    assert set(dp[0]["losses"][0]) == set(dp[1]["losses"][0]) == {(0, 0), (0, 1)}
+    assert set(dp[2]["losses"][0]) == {(1, 0), (1, 1)}
+    for r, p in ((0, 0), (1, 0), (2, 1), (3, 1)):
+        assert dp[r]["losses"] == plain[p]["losses"]
+        for k in plain[p]["bank"]:
+            for n in plain[p]["bank"][k]:
+                assert torch.equal(dp[r]["bank"][k][n], plain[p]["bank"][k][n]), (r, k, n)
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_nvlink_data_parallel_matches_one_rank_per_path_group(tmp_path):
+    """Fused executor with every path split over 2 GPUs (peer-memory gradient
+    reduce-scatter, sharded AdamW, fused all-gather) against the same four paths on ONE
+    GPU (one group = one rank: same placement, same batch generator): same losses and
+    banks up to float summation order."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    dp = _launch(tmp_path, "nvlink_dp2", 2, 29621)
+    one = _launch(tmp_path, "nccl", 1, 29623)[0]
+    for o in dp:
+        assert o["consistent"] and o["ckpt_same"] and o["resumed"]
+    # both members hold all four paths
+    assert set(dp[0]["losses"][0]) == set(dp[1]["losses"][0]) == {(0, 0), (0, 1), (1, 0), (1, 1)}
+    for rnd, (a, b) in enumerate(zip(dp[0]["losses"], one["losses"])):
+        for path, loss in a.items():
+            assert abs(loss - b[path]) < 5e-3 * abs(b[path]), (rnd, path, loss, b[path])
+    for k in dp[0]["bank"]:
+        for n in dp[0]["bank"][k]:
+            assert torch.allclose(dp[0]["bank"][k][n], one["bank"][k][n], atol=2e-3, rtol=2e-2), (k, n)
+            assert torch.equal(dp[0]["bank"][k][n], dp[1]["bank"][k][n]), (k, n)
+
+
 @pytest.mark.gpu
 @pytest.mark.multigpu
 def test_nvlink_outer_step_matches_nccl(tmp_path):

@@ -134,7 +134,7 @@ def test_logits_and_cross_entropy():
     lse = torch.empty(M, device=DEV)
     rl = torch.empty(M, device=DEV)
     ls, ic, lo = torch.empty(1, device=DEV), torch.empty(1, device=DEV), torch.empty(1, device=DEV)
-    ext().ce_forward(part, T, logits, V, 0, labels, M, 1, lse, rl, ls, ic, lo)
+    ext().ce_forward(part, T, logits, V, 0, labels, M, 1, lse, rl, ls, ic, lo, None)
     lf = logits.float().requires_grad_(True)
     ref_loss = F.cross_entropy(lf, labels.long(), ignore_index=-100)
     ref_loss.backward()
