@@ -16,6 +16,8 @@ void embedding_fwd(torch::Tensor ids, torch::Tensor E, int64_t se, torch::Tensor
                    int64_t G, int64_t V);
 void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
                    int64_t H, int64_t G, int64_t V);
+void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
+                          int64_t H, int64_t G, int64_t V, torch::Tensor keys);
 void attention_fwd(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                    torch::Tensor sinT, torch::Tensor o, torch::Tensor lse);
 void attention_bwd(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
@@ -36,6 +38,9 @@ void dp_grad_reduce_norm(torch::Tensor tab, torch::Tensor counter, int64_t me, i
 void dp_adamw(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, int64_t G, int64_t stride,
               int64_t stride16, int64_t s0, int64_t s1, torch::Tensor coef, torch::Tensor sched, double b1, double b2,
               double eps, double wd, torch::Tensor err);
+void dp_adam8bit(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, int64_t G, int64_t P, int64_t s0,
+                 int64_t s1, torch::Tensor coef, torch::Tensor sched, double b1, double b2, double eps, double wd,
+                 torch::Tensor err);
 void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels,
                 int64_t M, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum,
                 torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out, c10::optional<torch::Tensor> inv_given);
@@ -80,9 +85,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_bwd", &attention_bwd);
   m.def("attention_fwd_tc", &attention_fwd_tc);
   m.def("ce_fused", &ce_fused);
+  m.def("embedding_bwd_sorted", &embedding_bwd_sorted);
   m.def("dp_barrier", &dp_barrier);
   m.def("dp_grad_reduce_norm", &dp_grad_reduce_norm);
   m.def("dp_adamw", &dp_adamw);
+  m.def("dp_adam8bit", &dp_adam8bit);
   m.def("attention_bwd_tc", &attention_bwd_tc);
   m.def("ce_forward", &ce_forward);
   m.def("ce_backward", &ce_backward);

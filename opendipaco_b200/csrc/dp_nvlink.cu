@@ -16,6 +16,9 @@
 //                   storing the new fp32 master, its bf16 copy and both moments into
 //                   EVERY member's buffers: the reduce-scatter is fused with the update
 //                   and the all-gather is fused into the update's stores
+//   dp_adam8bit     the same with blockwise 8-bit Adam (blocks of 256 never straddle a
+//                   shard): the requantised moments, their scales and the new weights are
+//                   stored into every member
 //   dp_barrier      before the next forward reads the gathered weights
 //
 // Barriers compare monotonically increasing per-member counters kept in device memory,
@@ -33,8 +36,12 @@ namespace dp {
 constexpr int kMaxMembers = 8;
 constexpr int kBlockElems = 1 << 16;  // sum-of-squares partial granularity
 
-// Device pointer table (int64): rows W32, W16, GRAD, M1, M2, PAD, NORM; kMaxMembers each.
-enum Row { W32 = 0, W16 = 1, GRAD = 2, M1 = 3, M2 = 4, PAD = 5, NORM = 6, NROWS = 7 };
+// Device pointer table (int64): rows W32, W16, GRAD, M1, M2, PAD, NORM and the 8-bit Adam
+// state MQ, MABS, VQ, VLO, VSC; kMaxMembers each (unused rows are 0).
+enum Row {
+  W32 = 0, W16 = 1, GRAD = 2, M1 = 3, M2 = 4, PAD = 5, NORM = 6,
+  MQ = 7, MABS = 8, VQ = 9, VLO = 10, VSC = 11, NROWS = 12
+};
 
 ODP_DEVICE void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -182,6 +189,79 @@ __global__ void __launch_bounds__(256) adamw_kernel(const long long* tab, int me
   }
 }
 
+// One warp per 256-element block of the shard: grid covers G * nbs warps, nbs = blocks per
+// path in the shard, block b of path g is global block g * nb + b0 + b. Same update as the
+// single-GPU adam8bit kernel (int8 absmax m, log-domain uint8 v, round half to even).
+__global__ void adam8bit_kernel(const long long* tab, int me, int d, int G, long long P, long long nb, long long b0,
+                                long long nbs, const float* __restrict__ coef, const float* __restrict__ sched,
+                                float b1, float b2, float eps, float wd) {
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (w >= (long long)G * nbs) return;
+  const int g = (int)(w / nbs);
+  const long long blk = (long long)g * nb + b0 + (w % nbs);
+  const float* scd = sched + g * 4;
+  if (scd[3] == 0.f) return;
+  const float lr = scd[0], step_size = scd[1], bc2s = scd[2];
+  const bool first_step = scd[3] > 1.5f;
+  const float cf = coef[g];
+  const long long e0 = (long long)g * P + (b0 + (w % nbs)) * 256 + lane * 8;  // element offset in [G][P]
+  const long long q0 = blk * 256 + lane * 8;                                  // offset in the [G*nb][256] state
+  const float* gr = row_ptr<const float>(tab, GRAD, me);
+  const float* pw = row_ptr<const float>(tab, W32, me);
+  const int8_t* mq = row_ptr<const int8_t>(tab, MQ, me);
+  const uint8_t* vq = row_ptr<const uint8_t>(tab, VQ, me);
+  const float mscale = row_ptr<const float>(tab, MABS, me)[blk] / 127.f;
+  const float lo = row_ptr<const float>(tab, VLO, me)[blk], vsc = row_ptr<const float>(tab, VSC, me)[blk];
+  float mv[8], vv[8], lv[8];
+  float amax = 0.f, lmin = INFINITY, lmax = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float gv = gr[e0 + k] * cf;
+    const float m0 = (float)mq[q0 + k] * mscale;
+    const float v0 = first_step ? 0.f : __expf((float)vq[q0 + k] * vsc + lo);
+    mv[k] = m0 * b1 + (1.f - b1) * gv;
+    vv[k] = v0 * b2 + (1.f - b2) * gv * gv;
+    amax = fmaxf(amax, fabsf(mv[k]));
+    lv[k] = __logf(fmaxf(vv[k], 1e-20f));
+    lmin = fminf(lmin, lv[k]);
+    lmax = fmaxf(lmax, lv[k]);
+  }
+  amax = warp_max(amax);
+  lmax = warp_max(lmax);
+  lmin = -warp_max(-lmin);
+  const float qs = amax > 0.f ? amax / 127.f : 1.f;
+  const float vs = fmaxf((lmax - lmin) / 255.f, 1e-12f);
+  uint32_t mo[2] = {0, 0}, vo[2] = {0, 0};
+  float po[8];
+  const float decay = 1.f - lr * wd;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t mb = (uint32_t)(uint8_t)(int8_t)fminf(fmaxf(rintf(mv[k] / qs), -127.f), 127.f);
+    const uint32_t vb = (uint32_t)(uint8_t)fminf(fmaxf(rintf((lv[k] - lmin) / vs), 0.f), 255.f);
+    mo[k / 4] |= mb << (8 * (k % 4));
+    vo[k / 4] |= vb << (8 * (k % 4));
+    const float den = sqrtf(vv[k]) / bc2s + eps;
+    po[k] = pw[e0 + k] * decay - step_size * (mv[k] / den);
+  }
+  const float4 p0 = make_float4(po[0], po[1], po[2], po[3]), p1 = make_float4(po[4], po[5], po[6], po[7]);
+  const uint4 b16 = make_uint4(pack_bf16(po[0], po[1]), pack_bf16(po[2], po[3]), pack_bf16(po[4], po[5]),
+                               pack_bf16(po[6], po[7]));
+  for (int q = 0; q < d; ++q) {  // every member, this one included
+    float4* pd = reinterpret_cast<float4*>(row_ptr<float>(tab, W32, q) + e0);
+    pd[0] = p0;
+    pd[1] = p1;
+    *reinterpret_cast<uint4*>(row_ptr<__nv_bfloat16>(tab, W16, q) + e0) = b16;
+    *reinterpret_cast<uint2*>(row_ptr<int8_t>(tab, MQ, q) + q0) = make_uint2(mo[0], mo[1]);
+    *reinterpret_cast<uint2*>(row_ptr<uint8_t>(tab, VQ, q) + q0) = make_uint2(vo[0], vo[1]);
+    if (lane == 0) {
+      row_ptr<float>(tab, MABS, q)[blk] = amax;
+      row_ptr<float>(tab, VLO, q)[blk] = lmin;
+      row_ptr<float>(tab, VSC, q)[blk] = vs;
+    }
+  }
+}
+
 }  // namespace dp
 }  // namespace odp
 
@@ -231,6 +311,27 @@ void dp_adamw(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, i
     odp::dp::adamw_kernel<<<dim3(nb, (unsigned)G), 256, 0, st>>>(t, (int)me, (int)d, stride, stride16, s0, s1,
                                                                  coef.data_ptr<float>(), sched.data_ptr<float>(),
                                                                  (float)b1, (float)b2, (float)eps, (float)wd);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  odp::dp::barrier_kernel<<<1, 32, 0, st>>>(t, reinterpret_cast<unsigned*>(counter.data_ptr<int>()), (int)me,
+                                            (int)d, err.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// 8-bit Adam on the shard (s0, s1 multiples of 256) with stores into every member, then
+// the closing barrier.
+void dp_adam8bit(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, int64_t G, int64_t P, int64_t s0,
+                 int64_t s1, torch::Tensor coef, torch::Tensor sched, double b1, double b2, double eps, double wd,
+                 torch::Tensor err) {
+  TORCH_CHECK(P % 256 == 0 && s0 % 256 == 0 && (s1 % 256 == 0 || s1 == P), "dp_adam8bit: 256-element blocks");
+  auto st = at::cuda::getCurrentCUDAStream();
+  const long long* t = tab_ptr(tab);
+  const long long nb = P / 256, b0 = s0 / 256, nbs = (s1 - s0 + 255) / 256;
+  if (nbs > 0) {
+    const long long warps = G * nbs;
+    odp::dp::adam8bit_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+        t, (int)me, (int)d, (int)G, P, nb, b0, nbs, coef.data_ptr<float>(), sched.data_ptr<float>(), (float)b1,
+        (float)b2, (float)eps, (float)wd);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   odp::dp::barrier_kernel<<<1, 32, 0, st>>>(t, reinterpret_cast<unsigned*>(counter.data_ptr<int>()), (int)me,

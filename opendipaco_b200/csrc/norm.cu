@@ -59,24 +59,44 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, long long sx, co
   for (int i = threadIdx.x; i < 8 * H; i += blockDim.x) sdw[i] = 0.f;
   __syncthreads();
   const float* wg = w + g * sw;
+  const int n4 = H / 4;  // float4 columns (H % 128 == 0: n4 is a multiple of 32)
   for (int rr = warp; rr < kNormRowsPerBlock; rr += 8) {
     const int r = b * kNormRowsPerBlock + rr;
     if (r >= M) break;
-    const float* xr = x + g * sx + (long long)r * H;
-    const float* dyr = dy + g * sdy + (long long)r * H;
+    const float4* xr = reinterpret_cast<const float4*>(x + g * sx + (long long)r * H);
+    const float4* dyr = reinterpret_cast<const float4*>(dy + g * sdy + (long long)r * H);
+    const float4* w4 = reinterpret_cast<const float4*>(wg);
     const float rs = rstd[(long long)g * M + r];
     float dot = 0.f;
-    for (int i = lane; i < H; i += 32) dot += wg[i] * dyr[i] * (xr[i] * rs);
+    for (int i = lane; i < n4; i += 32) {
+      const float4 a = w4[i], d = dyr[i], xv = xr[i];
+      dot += a.x * d.x * (xv.x * rs) + a.y * d.y * (xv.y * rs) + a.z * d.z * (xv.z * rs) + a.w * d.w * (xv.w * rs);
+    }
     dot = warp_sum(dot) / H;
-    float* dxr = dx + g * sdx + (long long)r * H;
-    const float* drr = dres ? dres + g * sdx + (long long)r * H : nullptr;
-    for (int i = lane; i < H; i += 32) {
-      const float xh = xr[i] * rs;
-      float v = rs * (wg[i] * dyr[i] - xh * dot);
-      if (drr) v += drr[i];
+    float4* dxr = reinterpret_cast<float4*>(dx + g * sdx + (long long)r * H);
+    const float4* drr = dres ? reinterpret_cast<const float4*>(dres + g * sdx + (long long)r * H) : nullptr;
+    uint2* d16 = dx16 ? reinterpret_cast<uint2*>(dx16 + g * sdx + (long long)r * H) : nullptr;
+    float4* acc = reinterpret_cast<float4*>(sdw + warp * H);
+    for (int i = lane; i < n4; i += 32) {
+      const float4 a = w4[i], d = dyr[i], xv = xr[i];
+      const float4 xh = make_float4(xv.x * rs, xv.y * rs, xv.z * rs, xv.w * rs);
+      float4 v = make_float4(rs * (a.x * d.x - xh.x * dot), rs * (a.y * d.y - xh.y * dot),
+                             rs * (a.z * d.z - xh.z * dot), rs * (a.w * d.w - xh.w * dot));
+      if (drr) {
+        const float4 q = drr[i];
+        v.x += q.x;
+        v.y += q.y;
+        v.z += q.z;
+        v.w += q.w;
+      }
       dxr[i] = v;
-      if (dx16) dx16[g * sdx + (long long)r * H + i] = __float2bfloat16(v);
-      sdw[warp * H + i] += dyr[i] * xh;
+      if (d16) d16[i] = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+      float4 t = acc[i];
+      t.x += d.x * xh.x;
+      t.y += d.y * xh.y;
+      t.z += d.z * xh.z;
+      t.w += d.w * xh.w;
+      acc[i] = t;
     }
   }
   __syncthreads();
@@ -150,6 +170,86 @@ __global__ void embedding_bwd_kernel(const int* __restrict__ ids, const float* _
     if (t < nt) dst[t * 32 + lane] = acc[t];
 }
 
+// Deterministic O(M) embedding backward in two launches.
+// 1. One CTA per path sorts the keys (token id << 12 | row) of its <= 4096 rows with a
+//    bitonic network in shared memory, so every token's rows become one contiguous run
+//    in increasing row order.
+// 2. One warp per sorted position: the first position of each run sums the rows of the
+//    run (row order, the same additions as embedding_bwd_kernel) into dE[id].
+constexpr int kSortMax = 4096;
+
+__global__ void __launch_bounds__(1024) embed_sort_kernel(const int* __restrict__ ids, int M,
+                                                          unsigned* __restrict__ keys_out) {
+  __shared__ unsigned k[kSortMax];
+  const int g = blockIdx.x;
+  int n = 1;
+  while (n < M) n <<= 1;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    k[i] = i < M ? ((unsigned)ids[(long long)g * M + i] << 12) | (unsigned)i : 0xffffffffu;
+  __syncthreads();
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const unsigned a = k[lo], b = k[hi];
+        if ((a > b) == up) {
+          k[lo] = b;
+          k[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < M; i += blockDim.x) keys_out[(long long)g * M + i] = k[i];
+}
+
+template <int NT>
+__global__ void embed_runs_kernel(const unsigned* __restrict__ keys, const float* __restrict__ dx, long long sdx,
+                                  float* __restrict__ dE, long long se, int M, int H, int G, int V) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (warp >= G * M) return;
+  const int g = warp / M, i = warp % M;
+  const unsigned* gk = keys + (long long)g * M;
+  const unsigned id = gk[i] >> 12;
+  if (id >= (unsigned)V || (i > 0 && (gk[i - 1] >> 12) == id)) return;
+  // end of this token's run: first sorted position whose id differs (32 keys per probe)
+  int end = i + 1;
+  while (true) {
+    const int j = end + lane;
+    const unsigned differ = __ballot_sync(0xffffffffu, j >= M || (gk[j] >> 12) != id);
+    if (differ) {
+      end += __ffs(differ) - 1;
+      break;
+    }
+    end += 32;
+  }
+  const int nt = H / 32;
+  constexpr int BATCH = NT <= 16 ? 8 : 2;  // rows loaded before they are added (in row order)
+  float acc[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+  for (int j = i; j < end; j += BATCH) {
+    float v[BATCH][NT];
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) {
+      const bool in = j + b < end;
+      const float* src = dx + g * sdx + (long long)(in ? (gk[j + b] & 0xfffu) : 0) * H;
+#pragma unroll
+      for (int t = 0; t < NT; ++t) v[b][t] = (in && t < nt) ? src[t * 32 + lane] : 0.f;
+    }
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] += v[b][t];
+  }
+  float* dst = dE + g * se + (long long)id * H;
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+    if (t < nt) dst[t * 32 + lane] = acc[t];
+}
+
 }  // namespace odp
 
 static inline int blocks_for(long long threads, int per) { return (int)((threads + per - 1) / per); }
@@ -173,6 +273,11 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
   auto st = at::cuda::getCurrentCUDAStream();
   const int nblk = (int)((M + odp::kNormRowsPerBlock - 1) / odp::kNormRowsPerBlock);
   TORCH_CHECK(work.numel() >= G * nblk * H, "rmsnorm_bwd: work buffer too small");
+  auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  TORCH_CHECK(H % 4 == 0 && sx % 4 == 0 && sdy % 4 == 0 && sdx % 4 == 0 && sw % 4 == 0 && al16(x.data_ptr()) &&
+                  al16(dy.data_ptr()) && al16(dx.data_ptr()) && al16(w.data_ptr()) &&
+                  (!dres.has_value() || al16(dres->data_ptr())),
+              "rmsnorm_bwd: rows are read as float4 (16-byte aligned bases, strides multiple of 4)");
   const size_t smem = 8 * H * sizeof(float);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(odp::rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -204,5 +309,29 @@ void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tens
   auto st = at::cuda::getCurrentCUDAStream();
   odp::embedding_bwd_kernel<<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
       ids.data_ptr<int>(), dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// embedding_bwd through a per-path sort (same result, O(M)); keys: [G][M] int32 scratch.
+// Falls back to embedding_bwd for M > 4096 rows per path or V >= 2^20.
+void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
+                          int64_t H, int64_t G, int64_t V, torch::Tensor keys) {
+  if (M > odp::kSortMax || V >= (1 << 20)) {
+    embedding_bwd(ids, dx, sdx, dE, se, M, H, G, V);
+    return;
+  }
+  TORCH_CHECK(H % 32 == 0 && H <= 2048, "embedding_bwd: hidden size must be a multiple of 32 and <= 2048");
+  TORCH_CHECK(keys.numel() >= G * M, "embedding_bwd_sorted: key scratch too small");
+  c10::cuda::CUDAGuard guard(dE.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  unsigned* kp = reinterpret_cast<unsigned*>(keys.data_ptr<int>());
+  odp::embed_sort_kernel<<<(int)G, 1024, 0, st>>>(ids.data_ptr<int>(), (int)M, kp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (H <= 512)
+    odp::embed_runs_kernel<16><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
+        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V);
+  else
+    odp::embed_runs_kernel<64><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
+        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

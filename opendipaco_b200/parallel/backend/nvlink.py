@@ -106,16 +106,20 @@ class NVLinkBackend(TorchDistBackend):
         self._dp_handles.append((t, h))
         return t.view(*shape)
 
-    def dp_table(self, w32, w16, grad, m1, m2, G: int) -> torch.Tensor:
-        """Device table int64 [7][8] of every member's W32, W16, GRAD, M1, M2, signal pad
-        and norm-exchange buffer (the layout the ``dp_*`` kernels read)."""
+    def dp_table(self, w32, w16, grad, m1, m2, G: int, opt8=None) -> torch.Tensor:
+        """Device table int64 [12][8] of every member's W32, W16, GRAD, M1, M2 (AdamW),
+        signal pad, norm-exchange buffer and the 8-bit Adam state ``opt8 = (MQ, MABS,
+        VQ, VLO, VSC)`` -- the layout the ``dp_*`` kernels read; absent rows are 0."""
         pad = self.dp_tensor((8,), torch.int32)
         norm = self.dp_tensor((8 * max(G, 1),), torch.float32)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.dp_group)
         handles = {t.data_ptr(): h for t, h in self._dp_handles}
-        tab = torch.zeros(7, 8, dtype=torch.int64)
-        for row, t in enumerate((w32, w16, grad, m1, m2, pad, norm)):
+        tab = torch.zeros(12, 8, dtype=torch.int64)
+        rows = (w32, w16, grad, m1, m2, pad, norm) + tuple(opt8 or (None,) * 5)
+        for row, t in enumerate(rows):
+            if t is None:
+                continue
             h = handles[t.data_ptr()]
             for m, ptr in enumerate(h.buffer_ptrs):
                 tab[row, m] = ptr

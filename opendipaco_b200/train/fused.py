@@ -145,8 +145,6 @@ class FusedExecutor:
         if self.dp > 1:
             if not hasattr(be, "dp_tensor"):
                 raise NotImplementedError("intra-path data parallelism needs a peer-memory backend (NVLinkBackend)")
-            if self.opt8:
-                raise NotImplementedError("intra-path data parallelism is implemented for the AdamW inner optimizer")
             zeros = lambda *shape, dtype=torch.float32: be.dp_tensor(shape, dtype)  # noqa: E731
         else:
             zeros = lambda *shape, dtype=torch.float32: torch.zeros(*shape, device=self.dev, dtype=dtype)  # noqa: E731
@@ -155,11 +153,12 @@ class FusedExecutor:
         self.GRAD = zeros(G, P)
         if self.opt8:
             nb = P // ALIGN
-            self.MQ = torch.zeros(G * nb, ALIGN, device=self.dev, dtype=torch.int8)
-            self.MABS = torch.zeros(G * nb, device=self.dev)
-            self.VQ = torch.zeros(G * nb, ALIGN, device=self.dev, dtype=torch.uint8)
-            self.VLO = torch.zeros(G * nb, device=self.dev)
-            self.VSC = torch.zeros(G * nb, device=self.dev)
+            self.MQ = zeros(G * nb, ALIGN, dtype=torch.int8)
+            self.MABS = zeros(G * nb)
+            self.VQ = zeros(G * nb, ALIGN, dtype=torch.uint8)
+            self.VLO = zeros(G * nb)
+            self.VSC = zeros(G * nb)
+            self.MOM1 = self.MOM2 = None
         else:
             self.MOM1 = zeros(G, P)
             self.MOM2 = zeros(G, P)
@@ -171,7 +170,8 @@ class FusedExecutor:
             self.dp_index = be.dp_index
             ps = _ru((P + self.dp - 1) // self.dp)
             self.dp_s0, self.dp_s1 = min(P, self.dp_index * ps), min(P, (self.dp_index + 1) * ps)
-            self.dp_tab = be.dp_table(self.W32, self.W16, self.GRAD, self.MOM1, self.MOM2, G)
+            opt8 = (self.MQ, self.MABS, self.VQ, self.VLO, self.VSC) if self.opt8 else None
+            self.dp_tab = be.dp_table(self.W32, self.W16, self.GRAD, self.MOM1, self.MOM2, G, opt8)
             self.dp_counter = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.pms = dict(zip(self.paths, pms))
         if engine.materialize == "eager":
@@ -295,6 +295,7 @@ class FusedExecutor:
         self.SCHED = z(steps, G, 4)
         self.LOSSES = z(steps, G)
         self.INVC = z(steps, G)  # 1 / valid labels of each (step, path) batch, for split batches
+        self.EMBKEYS = z(G, M, dt=torch.int32)  # sorted (token, row) keys of the embedding backward
         self.ids_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
         self.labels_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
         self.sched_host = torch.zeros(steps, G, 4, dtype=torch.float32).pin_memory()
@@ -308,8 +309,9 @@ class FusedExecutor:
 
     # ------------------------------------------------------------------ GEMM helper
     def _bn(self, M: int, N: int) -> int:
+        # 128-wide tiles once they fill two thirds of a wave of 148 SMs; 64-wide below that
         tiles128 = self.G * ((M + 127) // 128) * ((N + 127) // 128)
-        return 128 if tiles128 >= 148 else 64
+        return 128 if tiles128 >= 100 else 64
 
     def _gemm(self, A, lda, sa, amn, B, ldb, sb, bmn, C, ldc, sc, M, N, K, epi, bn=None, **kw):
         from ..ops.gemm import EPI
@@ -385,7 +387,7 @@ class FusedExecutor:
                            self.DX16, gr[lo.ln1:], P, self.NORMWORK, M, H, G, 0.0)
         emb_n = bb.vocab_size * H
         self.GRAD[:, lay.emb:lay.emb + emb_n].zero_()
-        X_.embedding_bwd(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V)
+        X_.embedding_bwd_sorted(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V, self.EMBKEYS)
         # ---------------- optimizer
         clip = self.e.diloco.inner_grad_clip
         clipv = float(clip) if clip is not None else 0.0
@@ -396,8 +398,12 @@ class FusedExecutor:
             # member's shard storing weights and moments into every member (all-gather)
             X_.dp_grad_reduce_norm(self.dp_tab, self.dp_counter, self.dp_index, self.dp, G, P, P, self.dp_s0,
                                    self.dp_s1, self.CLIPWORK, clipv, self.COEF, self.GNORM, self.err)
-            X_.dp_adamw(self.dp_tab, self.dp_counter, self.dp_index, self.dp, G, P, P, self.dp_s0, self.dp_s1,
-                        self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, self.err)
+            if self.opt8:
+                X_.dp_adam8bit(self.dp_tab, self.dp_counter, self.dp_index, self.dp, G, P, self.dp_s0, self.dp_s1,
+                               self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, self.err)
+            else:
+                X_.dp_adamw(self.dp_tab, self.dp_counter, self.dp_index, self.dp, G, P, P, self.dp_s0, self.dp_s1,
+                            self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, self.err)
             return
         X_.grad_clip_coef(self.GRAD, P, P, G, clipv, self.CLIPWORK, self.COEF, self.GNORM)
         if self.opt8:

@@ -4,7 +4,8 @@
 
 MODE: "cpu" (gloo, module executor, TorchDistBackend), "nccl" (fused executor,
 NCCL outer step) or "nvlink" (fused executor, peer-memory outer step); a "_dp2"
-suffix puts every path on a group of two ranks (intra-path data parallelism). Writes
+suffix puts every path on a group of two ranks (intra-path data parallelism), a further
+"_8bit" suffix selects blockwise 8-bit Adam as the inner optimizer. Writes
 ``OUT_DIR/{MODE}_rank{r}.pt`` with the rank's bank, losses and a consistency flag.
 """
 
@@ -26,8 +27,10 @@ from opendipaco_b200.topology import is_private_key  # noqa: E402
 
 def main():
     out_dir, mode = sys.argv[1], sys.argv[2]
-    dp = 2 if mode.endswith("_dp2") else 1
-    base = mode[:-4] if dp > 1 else mode
+    opt8 = mode.endswith("_8bit")
+    core = mode[:-5] if opt8 else mode
+    dp = 2 if core.endswith("_dp2") else 1
+    base = core[:-4] if dp > 1 else core
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     if base == "cpu":
         dist.init_process_group("gloo", timeout=timedelta(seconds=60))
@@ -44,7 +47,7 @@ def main():
                             layers_per_level=[1, 1], max_position_embeddings=128)
         seq = 64
     cfg = DiPaCoConfig(backbone=bb, level_sizes=[2, 2], sequence_length=seq)
-    dl = DiLoCoConfig(inner_steps=3, inner_lr=1e-3, inner_autocast=base != "cpu")
+    dl = DiLoCoConfig(inner_steps=3, inner_lr=1e-3, inner_autocast=base != "cpu", optim_8bit=opt8)
     docs = zipf_documents(vocab_size=bb.vocab_size, num_documents=160, min_len=64, max_len=400, seed=1)
     corpus = ShardedCorpus.from_assignments(docs, torch.arange(len(docs)) % 4, 4, seq)
     topo = cfg.build_topology()

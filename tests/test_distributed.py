@@ -71,6 +71,26 @@ def test_nvlink_data_parallel_matches_one_rank_per_path_group(tmp_path):
 
 @pytest.mark.gpu
 @pytest.mark.multigpu
+def test_nvlink_data_parallel_8bit_adam_matches_one_rank(tmp_path):
+    """The same with blockwise 8-bit Adam: the shard owner requantises its 256-element
+    blocks and stores moments, scales and weights into both members."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    dp = _launch(tmp_path, "nvlink_dp2_8bit", 2, 29625)
+    one = _launch(tmp_path, "nccl_8bit", 1, 29627)[0]
+    for o in dp:
+        assert o["consistent"] and o["resumed"]
+    for rnd, (a, b) in enumerate(zip(dp[0]["losses"], one["losses"])):
+        for path, loss in a.items():
+            assert abs(loss - b[path]) < 1e-2 * abs(b[path]), (rnd, path, loss, b[path])
+    for k in dp[0]["bank"]:
+        for n in dp[0]["bank"][k]:
+            assert torch.allclose(dp[0]["bank"][k][n], one["bank"][k][n], atol=5e-3, rtol=5e-2), (k, n)
+            assert torch.equal(dp[0]["bank"][k][n], dp[1]["bank"][k][n]), (k, n)
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
 def test_nvlink_outer_step_matches_nccl(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
