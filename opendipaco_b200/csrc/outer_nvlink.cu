@@ -20,7 +20,14 @@
 //
 // So per round each rank reads (g-1)/g and writes (g-1)/g of every module it shares
 // over NVLink (two-shot reduce-scatter + all-gather), fused with the reduction, the
-// optimizer and the write-back. Waits never spin forever: after kWaitBoundNs they
+// optimizer and the write-back.
+//
+// Compressed mode (int4): before APPLY, outer_nvlink_quant turns each rank's DELTA
+// partial (plus its error-feedback residual) into 4-bit codes with one absmax/7 scale per
+// 128 elements (symmetric buffers QD, QS) and keeps what the codes miss as the residual
+// for the next round. APPLY then reads the sharers' codes and scales instead of their
+// fp32 partials (0.53 instead of 4 bytes per element over NVLink) and dequantises them in
+// registers inside the same reduction. Waits never spin forever: after kWaitBoundNs they
 // record ERR_TIMEOUT_PEER and the kernel returns.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -39,7 +46,7 @@ struct NvKey {
   int nsh;          // number of sharer ranks
   int sh[kMaxSharers];
   float scale, inv_den;
-  int pad;
+  int quant;        // 1: read the sharers' int4 codes + scales instead of their fp32 partials
 };
 
 constexpr int kNvChunk = 4096;
@@ -89,12 +96,57 @@ ODP_DEVICE bool cross_gpu_barrier(const unsigned long long* pads, int rank, int 
   return ok != 0;
 }
 
+constexpr int kQGroup = 128;
+
+// Quantise this rank's partials: one warp per 128-element group of the regions listed in
+// `regs` (off, n, group0), x = delta + res, codes q in [-7, 7] stored as q + 8 (two per
+// byte, element e in the low nibble of byte e/2 when e is even), res = x - q * scale.
+struct NvRegion {
+  long long off, n, group0;
+};
+
+__global__ void outer_nvlink_quant_kernel(const NvRegion* __restrict__ regs, int nregs, long long total_groups,
+                                          const float* __restrict__ delta, float* __restrict__ res,
+                                          uint8_t* __restrict__ qd, float* __restrict__ qs) {
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (w >= total_groups) return;
+  int lo = 0, hi = nregs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) / 2;
+    if (regs[mid].group0 <= w) lo = mid;
+    else hi = mid - 1;
+  }
+  const NvRegion r = regs[lo];
+  const long long e = r.off + (w - r.group0) * kQGroup + lane * 4;
+  const float4 dv = *reinterpret_cast<const float4*>(delta + e);
+  const float4 rv = *reinterpret_cast<const float4*>(res + e);
+  float x[4] = {__fadd_rn(dv.x, rv.x), __fadd_rn(dv.y, rv.y), __fadd_rn(dv.z, rv.z), __fadd_rn(dv.w, rv.w)};
+  float am = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+  am = warp_max(am);
+  const float sc = am / 7.f;
+  const float safe = sc > 0.f ? sc : 1.f;
+  uint32_t codes = 0;
+  float r4[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int q = (int)fminf(fmaxf(rintf(x[i] / safe), -7.f), 7.f);
+    r4[i] = __fsub_rn(x[i], __fmul_rn((float)q, sc));
+    codes |= (uint32_t)(q + 8) << (4 * i);
+  }
+  *reinterpret_cast<float4*>(res + e) = make_float4(r4[0], r4[1], r4[2], r4[3]);
+  *reinterpret_cast<uint16_t*>(qd + e / 2) = (uint16_t)codes;
+  if (lane == 0) qs[(r.off + (w - r.group0) * kQGroup) / kQGroup] = sc;
+}
+
 __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nkeys, long long total_chunks,
                                           const unsigned long long* __restrict__ delta_ptrs,
                                           const unsigned long long* __restrict__ glob_ptrs,
                                           const unsigned long long* __restrict__ pads, float* __restrict__ mom,
                                           int rank, int world, unsigned epoch, float lr, float m, int nesterov,
-                                          int first, float* __restrict__ sq_part, int* err) {
+                                          int first, float* __restrict__ sq_part, int* err,
+                                          const unsigned long long* __restrict__ qd_ptrs,
+                                          const unsigned long long* __restrict__ qs_ptrs) {
   if (!cross_gpu_barrier(pads, rank, world, 0, epoch, err, blockIdx.x == 0)) return;
   __shared__ float red[8];
   for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
@@ -112,7 +164,19 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
     for (long long e = e0 + threadIdx.x * 4; e < e1; e += blockDim.x * 4) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int j = 0; j < k.nsh; ++j) {
-        const float4 d = ld_cg4(reinterpret_cast<const float*>(delta_ptrs[k.sh[j]]) + k.off + e);
+        float4 d;
+        if (k.quant) {  // int4 codes + group scale of sharer j, dequantised in registers
+          const long long ge = k.off + e;
+          const uint16_t c = *reinterpret_cast<const volatile uint16_t*>(
+              reinterpret_cast<const uint8_t*>(qd_ptrs[k.sh[j]]) + ge / 2);
+          const float sc = *reinterpret_cast<const volatile float*>(
+              reinterpret_cast<const float*>(qs_ptrs[k.sh[j]]) + ge / kQGroup);
+          d = make_float4(__fmul_rn((float)((int)(c & 15u) - 8), sc), __fmul_rn((float)((int)((c >> 4) & 15u) - 8), sc),
+                          __fmul_rn((float)((int)((c >> 8) & 15u) - 8), sc),
+                          __fmul_rn((float)((int)((c >> 12) & 15u) - 8), sc));
+        } else {
+          d = ld_cg4(reinterpret_cast<const float*>(delta_ptrs[k.sh[j]]) + k.off + e);
+        }
         acc.x = __fadd_rn(acc.x, d.x);
         acc.y = __fadd_rn(acc.y, d.y);
         acc.z = __fadd_rn(acc.z, d.z);
@@ -186,7 +250,7 @@ __global__ void outer_nvlink_bcast_kernel(const NvCopy* __restrict__ cps, int nc
 void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks, torch::Tensor delta_ptrs,
                         torch::Tensor glob_ptrs, torch::Tensor pads, torch::Tensor mom, int64_t rank, int64_t world,
                         int64_t epoch, double lr, double m, bool nesterov, bool first, torch::Tensor sq_part,
-                        torch::Tensor err) {
+                        torch::Tensor err, c10::optional<torch::Tensor> qd_ptrs, c10::optional<torch::Tensor> qs_ptrs) {
   static_assert(sizeof(odp::NvKey) == 80, "NvKey layout");
   c10::cuda::CUDAGuard guard(mom.device());
   TORCH_CHECK(world <= 64, "outer_nvlink: world too large");
@@ -198,7 +262,23 @@ void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks,
       reinterpret_cast<const unsigned long long*>(glob_ptrs.data_ptr()),
       reinterpret_cast<const unsigned long long*>(pads.data_ptr()), mom.data_ptr<float>(), (int)rank, (int)world,
       (unsigned)epoch, (float)lr, (float)m, nesterov ? 1 : 0, first ? 1 : 0, sq_part.data_ptr<float>(),
-      err.data_ptr<int>());
+      err.data_ptr<int>(),
+      qd_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qd_ptrs->data_ptr()) : nullptr,
+      qs_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qs_ptrs->data_ptr()) : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// regs: int64 [nregs][3] = (element offset, elements, first group); offsets and sizes are
+// multiples of 128.
+void outer_nvlink_quant(torch::Tensor regs, int64_t nregs, int64_t total_groups, torch::Tensor delta,
+                        torch::Tensor res, torch::Tensor qd, torch::Tensor qs) {
+  static_assert(sizeof(odp::NvRegion) == 24, "NvRegion layout");
+  c10::cuda::CUDAGuard guard(delta.device());
+  if (total_groups == 0) return;
+  odp::outer_nvlink_quant_kernel<<<(unsigned)((total_groups * 32 + 255) / 256), 256, 0,
+                                   at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const odp::NvRegion*>(regs.data_ptr()), (int)nregs, total_groups, delta.data_ptr<float>(),
+      res.data_ptr<float>(), qd.data_ptr<uint8_t>(), qs.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

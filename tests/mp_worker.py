@@ -5,7 +5,8 @@
 MODE: "cpu" (gloo, module executor, TorchDistBackend), "nccl" (fused executor,
 NCCL outer step) or "nvlink" (fused executor, peer-memory outer step); a "_dp2"
 suffix puts every path on a group of two ranks (intra-path data parallelism), a further
-"_8bit" suffix selects blockwise 8-bit Adam as the inner optimizer. Writes
+"_8bit" suffix selects blockwise 8-bit Adam as the inner optimizer, and "nvlink_q4" sends
+int4 codes instead of fp32 partials through the NVLink outer step. Writes
 ``OUT_DIR/{MODE}_rank{r}.pt`` with the rank's bank, losses and a consistency flag.
 """
 
@@ -27,8 +28,10 @@ from opendipaco_b200.topology import is_private_key  # noqa: E402
 
 def main():
     out_dir, mode = sys.argv[1], sys.argv[2]
-    opt8 = mode.endswith("_8bit")
-    core = mode[:-5] if opt8 else mode
+    q4 = mode.endswith("_q4")
+    rest = mode[:-3] if q4 else mode
+    opt8 = rest.endswith("_8bit")
+    core = rest[:-5] if opt8 else rest
     dp = 2 if core.endswith("_dp2") else 1
     base = core[:-4] if dp > 1 else core
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -54,10 +57,11 @@ def main():
     if base == "nvlink":
         from opendipaco_b200.parallel.backend.nvlink import NVLinkBackend
 
-        backend = NVLinkBackend(topo, device=dev, dp=dp)
+        backend = NVLinkBackend(topo, device=dev, dp=dp, compress="int4" if q4 else None)
     else:
         backend = TorchDistBackend(topo, device=dev, dp=dp)
     eng = DiPaCoEngine(cfg, dl, backend, device=dev, seed=0)
+    init = {k: {n: t.detach().cpu().clone() for n, t in m.state_dict().items()} for k, m in eng.bank.items()}
     hist = eng.fit(corpus, num_rounds=3, batch_size=4, log_every=0)
     # shared modules must be identical on every rank that owns them
     consistent = True
@@ -82,7 +86,9 @@ def main():
     # checkpoint round trip (momentum gathered from the slice owners)
     ck = os.path.join(out_dir, f"ckpt_{mode}")
     save_checkpoint(eng, ck)
-    eng2 = DiPaCoEngine(cfg, dl, (type(backend))(topo, device=dev, dp=dp), device=dev, seed=5)
+    b2 = (NVLinkBackend(topo, device=dev, dp=dp, compress="int4" if q4 else None) if base == "nvlink"
+          else TorchDistBackend(topo, device=dev, dp=dp))
+    eng2 = DiPaCoEngine(cfg, dl, b2, device=dev, seed=5)
     load_checkpoint(eng2, ck)
     same = all(torch.equal(a, b) for k in eng.bank
                for a, b in zip(eng.bank[k].state_dict().values(), eng2.bank[k].state_dict().values()))
@@ -90,7 +96,7 @@ def main():
     h2 = eng2.fit(corpus, num_rounds=1, batch_size=4, log_every=0)
     resumed = h1[0].per_path_loss == h2[0].per_path_loss
     torch.save({"bank": {k: {n: t.detach().cpu() for n, t in m.state_dict().items()} for k, m in eng.bank.items()},
-                "losses": [m.per_path_loss for m in hist], "consistent": consistent, "ckpt_same": same,
+                "init": init, "losses": [m.per_path_loss for m in hist], "consistent": consistent, "ckpt_same": same,
                 "resumed": resumed},
                os.path.join(out_dir, f"{mode}_rank{rank}.pt"))
     dist.barrier()

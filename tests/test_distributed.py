@@ -103,3 +103,27 @@ def test_nvlink_outer_step_matches_nccl(tmp_path):
         for k in a["bank"]:
             for n in a["bank"][k]:
                 assert torch.allclose(a["bank"][k][n], b["bank"][k][n], atol=1e-6, rtol=0), (k, n)
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_nvlink_int4_outer_step_tracks_uncompressed(tmp_path):
+    """int4 codes with error feedback in the NVLink outer step: every sharer ends with the
+    same global, round-0 losses are unchanged, and the total update of every shared
+    module stays close to the uncompressed run's."""
+    from opendipaco_b200.topology import is_private_key
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    q4 = _launch(tmp_path, "nvlink_q4", 2, 29627)
+    nv = _launch(tmp_path, "nvlink", 2, 29629)
+    for a, b in zip(q4, nv):
+        assert a["consistent"] and a["ckpt_same"] and a["resumed"]
+        assert a["losses"][0] == b["losses"][0]
+        for k in a["bank"]:
+            if is_private_key(k):
+                continue
+            ua = torch.cat([(a["bank"][k][n] - a["init"][k][n]).float().reshape(-1) for n in a["bank"][k]])
+            ub = torch.cat([(b["bank"][k][n] - b["init"][k][n]).float().reshape(-1) for n in b["bank"][k]])
+            rel = ((ua - ub).norm() / ub.norm().clamp_min(1e-12)).item()
+            assert rel < 0.25, (k, rel)
