@@ -24,6 +24,12 @@ and optimizer state: ~570 MB per path) is far larger than the 126 MB L2.
 ``--impl reference`` runs the unmodified reference package installed in
 ``baseline/_ref`` (its own DiPaCoEngine, LocalBackend / TorchDistBackend over NCCL,
 bf16 autocast) on the same documents and shards.
+
+``--quality R`` (one GPU) measures model quality instead of speed: R rounds of training
+from the same random init on the same shards, then the held-out routed perplexity of
+the global modules on 512 unseen documents (256 tokens each, first 32 tokens route
+them) -- each arm with its own engine, k-means router, featuriser and
+``routed_perplexity``.
 """
 
 from __future__ import annotations
@@ -101,7 +107,7 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def build_documents_and_assignments():
+def build_documents_and_assignments(with_router: bool = False):
     """Zipf documents + k-means path assignments (identical on every rank / both arms)."""
     from opendipaco_b200.data import zipf_documents
     from opendipaco_b200.routing import BagOfTokensFeaturizer, KMeansRouter
@@ -112,7 +118,53 @@ def build_documents_and_assignments():
     feat = BagOfTokensFeaturizer(CFG["vocab"], feature_dim=256, seed=0)
     npaths = CFG["levels"][0] * CFG["levels"][1]
     router = KMeansRouter(npaths, seed=0).fit(feat([d[:32] for d in docs]))
+    if with_router:
+        return docs, assign_paths(docs, router, feat), router, feat
     return docs, assign_paths(docs, router, feat)
+
+
+def run_quality(args) -> dict:
+    """Held-out routed perplexity after ``args.quality`` rounds (one GPU)."""
+    from opendipaco_b200.data import zipf_documents
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    docs, assign = build_documents_and_assignments()
+    npaths = CFG["levels"][0] * CFG["levels"][1]
+    held = zipf_documents(vocab_size=CFG["vocab"], num_documents=512, min_len=256, max_len=1024,
+                          exponent=CFG["zipf"], topics=16, seed=1)
+    seqs = torch.stack([d[:256] for d in held])
+    if args.impl == "reference":
+        ref_dir = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref_dir, "opendipaco")):
+            return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+        sys.path.insert(0, ref_dir)
+        import opendipaco as pkg
+        from opendipaco.data import ShardedCorpus
+        from opendipaco.inference import routed_perplexity
+        from opendipaco.routing import BagOfTokensFeaturizer, KMeansRouter
+    else:
+        import opendipaco_b200 as pkg
+        from opendipaco_b200.data import ShardedCorpus
+        from opendipaco_b200.inference import routed_perplexity
+        from opendipaco_b200.routing import BagOfTokensFeaturizer, KMeansRouter
+    feat = BagOfTokensFeaturizer(CFG["vocab"], feature_dim=256, seed=0)
+    router = KMeansRouter(npaths, seed=0).fit(feat([d[:32] for d in docs]))
+    cfg, dl = make_configs(pkg)
+    corpus = ShardedCorpus.from_assignments(docs, assign, npaths, CFG["seq"])
+    engine = pkg.DiPaCoEngine(cfg, dl, pkg.LocalBackend(cfg.build_topology()), device=dev, seed=0)
+    engine.total_rounds = args.quality
+    hist = engine.fit(corpus, num_rounds=args.quality, batch_size=CFG["batch"], log_every=0)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        ppl = routed_perplexity(cfg, engine.global_modules(), seqs, router, feat, prefix_len=32, batch_size=16)
+    out = {"metric": "held-out routed perplexity", "value": round(float(ppl), 4), "unit": "ppl",
+           "higher_is_better": False, "rounds": args.quality, "final_inner_loss": round(hist[-1].inner_loss, 4),
+           "dtype": "bf16", "data": "synthetic Zipf(1.1), 512 held-out docs x 256 tokens, seed 1",
+           "config": {"model": "DiPaCo 4x4 (16 paths) Llama hidden 384, 6 heads, ffn 1024, layers [2,2], "
+                               "vocab 32000", "global_batch": 24 * npaths, "seq_len": CFG["seq"]}}
+    if args.impl == "reference":
+        out["impl"] = "reference"
+    return out
 
 
 def make_configs(pkg):
@@ -316,10 +368,12 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--quality", type=int, default=0, metavar="ROUNDS",
+                    help="train ROUNDS rounds on one GPU and print the held-out routed perplexity")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    out = run(args)
+    out = run_quality(args) if args.quality else run(args)
     if out:
         print(json.dumps(out), flush=True)
 

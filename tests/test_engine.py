@@ -99,3 +99,38 @@ def test_matches_reference_engine_bitwise(reference_pkg):
     for k in ref.bank:
         for a, b in zip(ref.bank[k].state_dict().values(), ours.bank[k].state_dict().values()):
             assert torch.equal(a, b)
+
+
+def test_routed_perplexity_matches_reference(reference_pkg):
+    """Held-out routed perplexity: both frameworks train the same 2x2 DiPaCo on the same
+    shards (bit-identical banks), route held-out documents with their own k-means router
+    over their own bag-of-tokens featuriser, and score them with their own
+    ``routed_perplexity`` -- the numbers are equal."""
+    R = reference_pkg
+    from opendipaco.data import ShardedCorpus as RSC
+    from opendipaco.inference import routed_perplexity as r_ppl
+    from opendipaco.routing import BagOfTokensFeaturizer as RBag, KMeansRouter as RKM
+
+    from opendipaco_b200.inference import routed_perplexity
+    from opendipaco_b200.routing import BagOfTokensFeaturizer, KMeansRouter
+
+    cfg = tiny_config(hidden=64, vocab=128, ffn=128, seq=32)
+    rcfg = R.DiPaCoConfig(backbone=R.BackboneConfig(**vars(cfg.backbone)), level_sizes=[2, 2],
+                          sequence_length=32)
+    docs = banded_docs(128, per=20, length=100)
+    train, held = docs[::2], docs[1::2]
+    feat, rfeat = BagOfTokensFeaturizer(128, feature_dim=32, seed=0), RBag(128, feature_dim=32, seed=0)
+    router = KMeansRouter(4, seed=0).fit(feat([d[:16] for d in train]))
+    rrouter = RKM(4, seed=0).fit(rfeat([d[:16] for d in train]))
+    assign = router.predict(feat([d[:16] for d in train]))
+    assert torch.equal(assign, rrouter.predict(rfeat([d[:16] for d in train])))
+    dl = dict(inner_steps=3, inner_lr=1e-3)
+    ours = DiPaCoEngine(cfg, DiLoCoConfig(**dl), LocalBackend(cfg.build_topology()), seed=3)
+    ref = R.DiPaCoEngine(rcfg, R.DiLoCoConfig(**dl), R.LocalBackend(rcfg.build_topology()), seed=3)
+    ours.fit(ShardedCorpus.from_assignments(train, assign, 4, 32), 3, 8, log_every=0)
+    ref.fit(RSC.from_assignments(train, assign, 4, 32), 3, 8, log_every=0)
+    seqs = torch.stack([d[:64] for d in held])
+    p_ours = routed_perplexity(cfg, ours.global_modules(), seqs, router, feat, prefix_len=16)
+    p_ref = r_ppl(rcfg, ref.global_modules(), seqs, rrouter, rfeat, prefix_len=16)
+    assert p_ours == p_ref, (p_ours, p_ref)
+    assert 1.0 < p_ours < float("inf")

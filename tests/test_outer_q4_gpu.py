@@ -13,7 +13,8 @@ G = 128
 
 def _ref_quant(x):
     g = x.view(-1, G)
-    sc = g.abs().amax(1) / 7
+    am = g.abs().amax(1)
+    sc = am / torch.full_like(am, 7.0)   # a true division (a scalar divisor becomes a reciprocal multiply)
     safe = torch.where(sc > 0, sc, torch.ones_like(sc))
     q = torch.clamp(torch.round(g / safe[:, None]), -7, 7)
     res = g - q * sc[:, None]
