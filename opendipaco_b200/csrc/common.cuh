@@ -135,6 +135,7 @@ ODP_DEVICE uint64_t umma_smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, u
   return d;
 }
 constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW64 = 4;
 
 // Instruction descriptor, kind::f16, bf16 x bf16 -> f32.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, bool a_mn, bool b_mn) {

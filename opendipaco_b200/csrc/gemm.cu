@@ -56,17 +56,36 @@ struct GemmParams {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+
+// TMEM columns for two accumulator buffers of width BN (allocations are powers of two).
+constexpr int tmem_cols(int bn) {
+  int c = 32;
+  while (c < 2 * bn) c *= 2;
+  return c;
+}
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 
-template <int BN, int STAGES>
+// Staging bytes per epilogue warp: one 4 KB box for bf16 / logits outputs, two for the
+// other epilogues of the single-CTA kernel (two fp32 boxes in flight, or the three bf16
+// boxes of a SwiGLU slab).
+constexpr int stg_warp_bytes(int epi, bool pair) { return (epi == EPI_BF16 || epi == EPI_LOGITS || pair) ? 4096 : 8192; }
+
+// Pipeline depth that fits next to the staging buffers and barriers.
+constexpr int fit_stages(int stage_bytes, int stg_total, int want) {
+  int s = want;
+  while (s > 2 && s * stage_bytes + stg_total + 512 + 1024 > 232448) --s;
+  return s;
+}
+
+template <int BN, int STAGES, int STGW = 4096>
 struct SmemLayout {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STG_OFF = STAGES * STAGE_BYTES;  // epilogue staging: 8 warps x [32 rows][128 B]
-  static constexpr int STG_BYTES = 8 * 32 * 128;
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES;  // epilogue staging: 8 warps x STGW bytes
+  static constexpr int STG_BYTES = 8 * STGW;
   static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
-  static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
+  static constexpr int TOTAL = BAR_OFF + 512 + 1024;  // + barriers + alignment slack
   static_assert(TOTAL <= 232448, "shared memory budget");
 };
 
@@ -258,6 +277,201 @@ ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int
   }
 }
 
+// ---------------------------------------------------------------- TMA-store epilogues
+// Each epilogue warp owns 32 TMEM lanes (rows) of the tile and a private staging buffer
+// of kStgWarp bytes. A thread holds one row, so it writes its row into the buffer in the
+// swizzled layout of the output tensor map, and one elected lane moves the whole 32-row
+// box with a bulk tensor store (full-line writes instead of 32 scattered rows per
+// instruction). Inputs of the epilogue (residual, saved gate/up pre-activations, C when
+// beta != 0) come in the same way, by a TMA load on the warp's own mbarrier.
+//   fp32 box: 32 rows x 32 floats (128-byte rows, 128-byte swizzle: chunk ^ row % 8)
+//   bf16 box: 32 rows x 32 bf16  (64-byte rows, 64-byte swizzle: chunk ^ (row / 2) % 4)
+ODP_DEVICE uint32_t f32_slot(int row, int j) { return row * 128 + ((j ^ (row & 7)) << 4); }
+ODP_DEVICE uint32_t b16_slot(int row, int j) { return row * 64 + ((j ^ ((row >> 1) & 3)) << 4); }
+
+ODP_DEVICE void stage_f32x32(uint8_t* buf, int row, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4*>(buf + f32_slot(row, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+ODP_DEVICE void unstage_f32x32(const uint8_t* buf, int row, float* v) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 x = *reinterpret_cast<const float4*>(buf + f32_slot(row, j));
+    v[4 * j] = x.x;
+    v[4 * j + 1] = x.y;
+    v[4 * j + 2] = x.z;
+    v[4 * j + 3] = x.w;
+  }
+}
+ODP_DEVICE void stage_b16x32(uint8_t* buf, int row, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(buf + b16_slot(row, j)) =
+        make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                   pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+}
+ODP_DEVICE void unstage_b16x32(const uint8_t* buf, int row, float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 q = *reinterpret_cast<const uint4*>(buf + b16_slot(row, j));
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      v[8 * j + 2 * e] = __uint_as_float(w[e] << 16);
+      v[8 * j + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+    }
+  }
+}
+
+template <int N>
+ODP_DEVICE void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+struct EpiCtx {
+  uint8_t* stg;              // this warp's staging buffer (stg_bytes)
+  int stg_bytes;
+  uint64_t* wbar;            // this warp's mbarrier for epilogue inputs
+  uint32_t* wphase;          // its phase parity
+  const CUtensorMap* tmC;    // output map
+  const CUtensorMap* tmX;    // input map (residual / saved gate-up / C)
+};
+
+// Warp-collective: bring `nbox` boxes of `box_bytes` at (x_i, y) into buf + i * box_bytes.
+ODP_DEVICE bool epi_load(const GemmParams& p, EpiCtx& e, uint8_t* buf, int nbox, int box_bytes, const int* xs, int y,
+                         int g, int lane) {
+  if (lane == 0) {
+    mbar_expect_tx(e.wbar, (uint32_t)(nbox * box_bytes));
+    for (int i = 0; i < nbox; ++i) tma_load_3d(e.tmX, e.wbar, buf + i * box_bytes, xs[i], y, g);
+  }
+  __syncwarp();
+  bool ok = mbar_wait(e.wbar, *e.wphase, p.err, ERR_TIMEOUT_FULL);
+  if (!ok) ok = mbar_wait(e.wbar, *e.wphase, p.err, ERR_TIMEOUT_FULL);  // drain: a late copy must land first
+  *e.wphase ^= 1u;
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Warp-collective: make the staged rows visible to the async proxy and store the boxes.
+ODP_DEVICE void epi_store(EpiCtx& e, const CUtensorMap* m, const uint8_t* buf, int nbox, int box_bytes, const int* xs,
+                          int y, int g, int lane) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    for (int i = 0; i < nbox; ++i) tma_store_3d(m, buf + i * box_bytes, xs[i], y, g);
+    bulk_commit();
+  }
+  __syncwarp();
+}
+
+// Returns false when an input box never arrived (error recorded): the caller stops.
+template <int BN, int EPI>
+ODP_DEVICE bool epilogue_tma(const GemmParams& p, uint32_t tmem_acc, int q, int ch, int lane, int g, int tm, int tn,
+                             EpiCtx& e) {
+  const uint32_t tbase = tmem_acc + ((uint32_t)(q * 32) << 16);
+  const int y = tm * BM + q * 32;  // first row of this warp's box (rows >= M are clipped)
+  constexpr int HALF = BN / 2;
+  if constexpr (EPI == EPI_SWIGLU) {
+    // gate columns [0, HALF), up columns [HALF, BN) of HALF features; this warp: 32 of them
+    const int c0 = ch * 32;
+    const int f0 = tn * HALF + c0;
+    uint32_t a[32], b[32];
+    tmem_ld16_nw(tbase + c0, a);
+    tmem_ld16_nw(tbase + c0 + 16, a + 16);
+    tmem_ld16_nw(tbase + HALF + c0, b);
+    tmem_ld16_nw(tbase + HALF + c0 + 16, b + 16);
+    tmem_wait_tie32(a);
+    reg_tie32(b);
+    if (f0 >= p.f_half) return true;
+    float h[32], gg[32], uu[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      gg[i] = bf16_round(__uint_as_float(a[i]));
+      uu[i] = bf16_round(__uint_as_float(b[i]));
+      h[i] = bf16_round(silu_f(gg[i])) * uu[i];
+    }
+    if (lane == 0) bulk_wait_read<0>();  // the previous tile's boxes have left the buffer
+    __syncwarp();
+    stage_b16x32(e.stg, lane, h);
+    stage_b16x32(e.stg + 2048, lane, gg);
+    stage_b16x32(e.stg + 4096, lane, uu);
+    const int xh[1] = {f0}, xgu[2] = {f0, p.f_half + f0};
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(e.tmC, e.stg, xh[0], y, g);
+      tma_store_3d(e.tmX, e.stg + 2048, xgu[0], y, g);
+      tma_store_3d(e.tmX, e.stg + 4096, xgu[1], y, g);
+      bulk_commit();
+    }
+    __syncwarp();
+  } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+    // acc = dH for features [tn * BN + ch * HALF, + HALF); aux = saved [g | u]; C = [dG | dU]
+#pragma unroll 1
+    for (int c = ch * HALF; c < (ch + 1) * HALF; c += 32) {
+      uint32_t r[32];
+      load32(tbase + c, r);
+      const int f = tn * BN + c;
+      if (f >= p.N) continue;
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+      const int xs[2] = {f, p.f_half + f};
+      if (!epi_load(p, e, e.stg, 2, 2048, xs, y, g, lane)) return false;
+      float gv[32], uv[32], og[32], ou[32];
+      unstage_b16x32(e.stg, lane, gv);
+      unstage_b16x32(e.stg + 2048, lane, uv);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float dh = bf16_round(__uint_as_float(r[i]));
+        const float sg = 1.0f / (1.0f + __expf(-gv[i]));
+        ou[i] = dh * bf16_round(gv[i] * sg);
+        og[i] = bf16_round(dh * uv[i]) * sg * (1.0f + gv[i] * (1.0f - sg));
+      }
+      stage_b16x32(e.stg, lane, og);
+      stage_b16x32(e.stg + 2048, lane, ou);
+      epi_store(e, e.tmC, e.stg, 2, 2048, xs, y, g, lane);
+    }
+  } else {
+    // fp32 C = acc (+ R for the residual epilogue, + beta * C when beta != 0)
+    const bool need_in = EPI == EPI_RESID || p.beta != 0.f;
+    const int nslot = e.stg_bytes / 4096;
+    int used = 0;
+#pragma unroll 1
+    for (int c = ch * HALF; c < (ch + 1) * HALF; c += 32) {
+      uint32_t r[32];
+      load32(tbase + c, r);
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      const int slot = used % nslot;
+      uint8_t* buf = e.stg + slot * 4096;
+      // the slot's previous box has been read out (at most nslot - 1 newer groups pending)
+      if (lane == 0) {
+        if (nslot == 1) bulk_wait_read<0>();
+        else bulk_wait_read<1>();
+      }
+      __syncwarp();
+      const int xs[1] = {tn * BN + c};
+      if (need_in) {
+        if (!epi_load(p, e, buf, 1, 4096, xs, y, g, lane)) return false;
+        float x[32];
+        unstage_f32x32(buf, lane, x);
+        if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = x[i] + v[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = v[i] + p.beta * x[i];
+        }
+      }
+      stage_f32x32(buf, lane, v);
+      epi_store(e, e.tmC, buf, 1, 4096, xs, y, g, lane);
+      ++used;
+    }
+  }
+  return true;
+}
+
 // Logits epilogue: bf16 store + per-row (max, sum exp) over this thread's half of the
 // tile (partials indexed [row][2 * tn + ch]).
 template <int BN>
@@ -318,8 +532,9 @@ ODP_DEVICE void epilogue_logits(const GemmParams& p, uint32_t tmem_acc, int q, i
 template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmC, GemmParams p) {
-  using L = SmemLayout<BN, STAGES>;
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
+  constexpr int STGW = stg_warp_bytes(EPI, false);
+  using L = SmemLayout<BN, STAGES, STGW>;
   constexpr bool SPLIT_B = (EPI == EPI_SWIGLU);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -328,7 +543,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accfull = empty + STAGES;
   uint64_t* accempty = accfull + 2;
   uint64_t* drain = accempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* wbar = drain + 1;  // one per epilogue warp: inputs of the TMA-store epilogue
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(wbar + 8);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -342,11 +558,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&accempty[b], 256);
     }
     mbar_init(drain, 1);
+    for (int w = 0; w < 8; ++w) mbar_init(&wbar[w], 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc(tmem_holder, 2 * BN);
+  if (warp == 1) tmem_alloc(tmem_holder, tmem_cols(BN));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -464,16 +681,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp % 4;         // TMEM lane quarter this warp may access
     const int ch = (warp - 2) / 4;  // which column half of the tile
     int acc = 0;
-    uint32_t accphase = 0;
+    uint32_t accphase = 0, wphase = 0;
+    EpiCtx ectx{smem + L::STG_OFF + (warp - 2) * STGW, STGW, &wbar[warp - 2], &wphase, &tmC, &tmX};
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       if (!mbar_wait(&accfull[acc], accphase, p.err, ERR_TIMEOUT_ACCUM)) break;
       tc_fence_after();
       const int g = t / tiles_per_g, r = t % tiles_per_g;
       const int tm = r / p.tiles_n, tn = r % p.tiles_n;
       const uint32_t tacc = tmem_base + acc * BN;
-      uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;
-      if constexpr (EPI == EPI_LOGITS) epilogue_logits<BN>(p, tacc, q, ch, lane, g, tm, tn, stg, &tmC);
-      else epilogue_tile<BN, EPI>(p, tacc, q, ch, lane, g, tm, tn, stg, &tmC);
+      uint8_t* stg = ectx.stg;
+      if constexpr (EPI == EPI_LOGITS) {
+        epilogue_logits<BN>(p, tacc, q, ch, lane, g, tm, tn, stg, &tmC);
+      } else if constexpr (EPI != EPI_BF16) {
+        if (p.tma_store) {
+          if (!epilogue_tma<BN, EPI>(p, tacc, q, ch, lane, g, tm, tn, ectx)) break;
+        } else {
+          epilogue_tile<BN, EPI>(p, tacc, q, ch, lane, g, tm, tn, stg, &tmC);
+        }
+      } else {
+        epilogue_tile<BN, EPI>(p, tacc, q, ch, lane, g, tm, tn, stg, &tmC);
+      }
       tc_fence_before();
       mbar_arrive(&accempty[acc]);
       acc ^= 1;
@@ -488,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
+  if (warp == 1) tmem_dealloc(tmem_base, tmem_cols(BN));
 }
 
 // ============================================================== CTA-pair variant
@@ -505,26 +732,32 @@ struct SmemLayout2 {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BN / 2) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages start on a swizzle-atom boundary");
   static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-  static constexpr int STG_BYTES = 8 * 32 * 128;
+  static constexpr int STG_BYTES = 8 * 4096;  // one staging box per epilogue warp
   static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
-  static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+  static constexpr int TOTAL = BAR_OFF + 512 + 1024;
   static_assert(TOTAL <= 232448, "shared memory budget");
 };
 
 template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const __grid_constant__ CUtensorMap tmC, GemmParams p) {
+                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
   using L = SmemLayout2<BN, STAGES>;
   constexpr int HB = BN / 2;  // B rows held by each CTA
+  // an MN-major B half that is not a whole number of 64-element 128-byte atoms (HB = 96)
+  // is held as 32-element 64-byte-swizzled atoms
+  constexpr bool B_SW64 = B_MN && (HB % 64) != 0;
+  static_assert(!B_MN || HB % 32 == 0, "MN-major B half must be a multiple of 32");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* empty = full + STAGES;
   uint64_t* accfull = empty + STAGES;
   uint64_t* accempty = accfull + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accempty + 2);
+  uint64_t* wbar = accempty + 2;  // one per epilogue warp: inputs of the TMA-store epilogue
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(wbar + 8);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
@@ -540,11 +773,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&accfull[b], 1);
       mbar_init(&accempty[b], 16);  // one arrive per epilogue warp of both CTAs
     }
+    for (int w = 0; w < 8; ++w) mbar_init(&wbar[w], 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc_pair(tmem_holder, 2 * BN);
+  if (warp == 1) tmem_alloc_pair(tmem_holder, tmem_cols(BN));
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers are initialised before any remote signal
   tc_fence_after();
@@ -583,6 +817,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           if constexpr (!B_MN) {
             tma_load_3d_pair(&tmB, fb, sB, k0, col0, g);
+          } else if constexpr (B_SW64) {
+#pragma unroll
+            for (int j = 0; j < HB / 32; ++j) tma_load_3d_pair(&tmB, fb, sB + j * 4096, col0 + j * 32, k0, g);
           } else {
 #pragma unroll
             for (int j = 0; j < HB / 64; ++j) tma_load_3d_pair(&tmB, fb, sB + j * 8192, col0 + j * 64, k0, g);
@@ -634,6 +871,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               if constexpr (!A_MN) ad = umma_smem_desc(aaddr + kk * 32, 16, 1024, kLayoutSW128);
               else ad = umma_smem_desc(aaddr + kk * 2048, 8192, 1024, kLayoutSW128);
               if constexpr (!B_MN) bd = umma_smem_desc(baddr + kk * 32, 16, 1024, kLayoutSW128);
+              else if constexpr (B_SW64) bd = umma_smem_desc(baddr + kk * 1024, 4096, 512, kLayoutSW64);
               else bd = umma_smem_desc(baddr + kk * 2048, 8192, 1024, kLayoutSW128);
               umma_bf16_pair(dtm, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
             }
@@ -659,18 +897,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t accempty_leader = mapa_rank(&accempty[0], 0);
     uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;
     int acc = 0;
-    uint32_t accphase = 0;
+    uint32_t accphase = 0, wphase = 0;
+    EpiCtx ectx{stg, 4096, &wbar[warp - 2], &wphase, &tmC, &tmX};
     for (int t = pair; t < p.num_tiles; t += npairs) {
       if (!mbar_wait(&accfull[acc], accphase, p.err, ERR_TIMEOUT_ACCUM)) break;
       tc_fence_after();
       const int g = t / tiles_per_g, r = t % tiles_per_g;
       const int tm = r / p.tiles_n, tn = r % p.tiles_n;
       // this CTA holds rows [tm * 256 + rank * 128, +128) of the pair tile: a 128-row tile index
-      epilogue_tile<BN, EPI>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, stg, &tmC);
+      bool ok = true;
+      if constexpr (EPI == EPI_F32) {
+        if (p.tma_store) ok = epilogue_tma<BN, EPI>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, ectx);
+        else epilogue_tile<BN, EPI>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, stg, &tmC);
+      } else {
+        epilogue_tile<BN, EPI>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, stg, &tmC);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(accempty_leader + acc * 8);
       __syncwarp();
+      if (!ok) break;
       acc ^= 1;
       if (acc == 0) accphase ^= 1;
     }
@@ -683,7 +929,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_before();
   cluster_sync();  // every MMA consumed, every remote arrival delivered, before TMEM goes away
   tc_fence_after();
-  if (warp == 1) tmem_dealloc_pair(tmem_base, 2 * BN);
+  if (warp == 1) tmem_dealloc_pair(tmem_base, tmem_cols(BN));
 }
 
 // ============================================================== host side
@@ -706,18 +952,20 @@ static EncodeTiledFn get_encode() {
 // bf16 3-D map: x = contiguous dim (extent inner), y = rows (extent outer, stride ld),
 // z = group (extent G, stride sg). Box = {64, box_rows, 1}, 128-byte swizzle.
 static CUtensorMap make_map(const void* base, long long inner, long long outer, long long ld, int G,
-                            long long sg, int box_rows) {
+                            long long sg, int box_rows, int box_inner = 64,
+                            CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
+                            CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, int esz = 2) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
-  TORCH_CHECK((ld * 2) % 16 == 0, "row stride must be a multiple of 16 bytes");
-  TORCH_CHECK(G == 1 || (sg * 2) % 16 == 0, "group stride must be a multiple of 16 bytes");
+  TORCH_CHECK((ld * esz) % 16 == 0, "row stride must be a multiple of 16 bytes");
+  TORCH_CHECK(G == 1 || (sg * esz) % 16 == 0, "group stride must be a multiple of 16 bytes");
   CUtensorMap m;
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)G};
-  long long gstride = G > 1 ? sg * 2 : ((outer * ld * 2 + 15) / 16) * 16;
-  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)gstride};
-  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  long long gstride = G > 1 ? sg * esz : ((outer * ld * esz + 15) / 16) * 16;
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * esz), (cuuint64_t)gstride};
+  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows, 1};
   cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  CUresult r = get_encode()(&m, dt, 3, const_cast<void*>(base), dims, strides, box, es,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
   return m;
@@ -733,10 +981,46 @@ static int num_sms() {
   return n;
 }
 
+static bool al16(const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; }
+
+// Output (and epilogue-input) maps of the TMA-store epilogues of fp32 / residual / SwiGLU
+// outputs; false when a base, row stride or group stride is not 16-byte aligned (those
+// calls keep the per-thread stores).
+template <int EPI>
+static bool out_maps(const GemmParams& p, CUtensorMap& mc, CUtensorMap& mx) {
+  if (getenv("ODP_GEMM_NO_TMA_STORE")) return false;
+  const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const auto B16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if constexpr (EPI == EPI_F32 || EPI == EPI_RESID) {
+    if (!al16(p.C) || (p.ldc * 4) % 16 || (p.G > 1 && (p.sc * 4) % 16)) return false;
+    mc = make_map(p.C, p.N, p.M, p.ldc, p.G, p.sc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, F32, 4);
+    if constexpr (EPI == EPI_RESID) {
+      if (!al16(p.R) || (p.ldr * 4) % 16 || (p.G > 1 && (p.sr * 4) % 16)) return false;
+      mx = make_map(p.R, p.N, p.M, p.ldr, p.G, p.sr, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, F32, 4);
+    } else {
+      mx = mc;
+    }
+    return true;
+  } else if constexpr (EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_BWD) {
+    const long long F = p.f_half;
+    if (F % 32 || !al16(p.C) || !al16(p.aux) || (p.ldc * 2) % 16 || (p.ldx * 2) % 16 ||
+        (p.G > 1 && ((p.sc * 2) % 16 || (p.sx * 2) % 16)))
+      return false;
+    // SwiGLU: C = H [M, F], aux = [g | u] [M, 2F]; backward: C = [dG | dU] [M, 2F], aux = [g | u]
+    const long long c_inner = EPI == EPI_SWIGLU ? F : 2 * F;
+    if (EPI == EPI_SWIGLU_BWD && p.N > F) return false;
+    mc = make_map(p.C, c_inner, p.M, p.ldc, p.G, p.sc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B, B16, 2);
+    mx = make_map(p.aux, 2 * F, p.M, p.ldx, p.G, p.sx, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B, B16, 2);
+    return true;
+  } else {
+    return false;
+  }
+}
+
 template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
-static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmParams& p,
-                     cudaStream_t st, int max_ctas) {
-  using L = SmemLayout<BN, STAGES>;
+static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mx,
+                     GemmParams& p, cudaStream_t st, int max_ctas) {
+  using L = SmemLayout<BN, STAGES, stg_warp_bytes(EPI, false)>;
   auto kern = gemm_kernel<A_MN, B_MN, BN, STAGES, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -744,13 +1028,13 @@ static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
     attr_set = true;
   }
   int grid = std::min(p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
-  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, mc, p);
+  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, mc, mx, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
-static void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmParams& p,
-                        cudaStream_t st, int max_ctas) {
+static void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mx,
+                        GemmParams& p, cudaStream_t st, int max_ctas) {
   using L = SmemLayout2<BN, STAGES>;
   auto kern = gemm2_kernel<A_MN, B_MN, BN, STAGES, EPI>;
   static bool attr_set = false;
@@ -760,7 +1044,7 @@ static void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   }
   int grid = std::min(2 * p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
   grid &= ~1;  // whole CTA pairs
-  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, mc, p);
+  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, mc, mx, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -776,12 +1060,16 @@ template <int EPI, bool AM, bool BMN, int BN>
 constexpr bool cfg_ok() {
   if (EPI == EPI_SWIGLU || EPI == EPI_LOGITS) return !AM && !BMN && BN == 128;
   if (EPI == EPI_SWIGLU_BWD) return !AM && BMN && BN != 256;
-  if (EPI == EPI_RESID || EPI == EPI_BF16) return !AM && BN != 256;
+  if (EPI == EPI_RESID || EPI == EPI_BF16) return !AM && BN != 256 && BN != 192;
+  // 192-wide tiles (N = 384 in two tiles): fp32 outputs of long-K products such as the
+  // LM-head input and weight gradients
+  if (BN == 192) return EPI == EPI_F32;
   return BN != 256 || (!AM && !BMN);
 }
 
 template <int EPI, bool AM, bool BMN, int BN>
 constexpr bool cfg2_ok() {
+  if (BN == 192) return EPI == EPI_F32;
   if (EPI == EPI_BF16) return !AM;
   return EPI == EPI_F32;
 }
@@ -795,31 +1083,47 @@ static bool dispatch_pair(const Operand& A, const Operand& B, GemmParams& p, cud
     const char* env = getenv("ODP_GEMM_2SM");
     if ((env && env[0] == '0') || p.M < 2 * BM || (max_ctas > 0 && max_ctas < 2)) return false;
     if (EPI == EPI_BF16 && A.mn) return false;
-    // 256-wide pair tiles only: for narrow N (e.g. 384 with a long K) the single-CTA kernel
-    // is as fast (measured), so the pair path is reserved for wide outputs.
-    if (!(p.N >= 256 && (p.N % 256 == 0 || p.N >= 2048))) return false;
-    const int bn = 256;
+    // 256-wide pair tiles for wide outputs; 192-wide pair tiles (each CTA holds 96 columns
+    // of B) for fp32 outputs whose width is a multiple of 192 but not of 256 (N = 384: the
+    // input and weight gradients of hidden-384 layers and LM heads). 128-wide pair tiles
+    // measured no faster than the single-CTA kernel.
+    const bool w256 = p.N >= 256 && (p.N % 256 == 0 || p.N >= 2048);
+    const bool w192 = EPI == EPI_F32 && !w256 && p.N % 192 == 0;
+    if (!w256 && !w192) return false;
+    const int bn = w256 ? 256 : 192;
     p.tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
     p.tiles_n = (p.N + bn - 1) / bn;
     p.num_tiles = p.tiles_m * p.tiles_n * p.G;
     CUtensorMap ma = A.mn ? make_map(A.ptr, p.M, p.K, A.ld, p.G, A.sg, 64) : make_map(A.ptr, p.K, p.M, A.ld, p.G, A.sg, BM);
-    CUtensorMap mb = B.mn ? make_map(B.ptr, p.N, p.K, B.ld, p.G, B.sg, 64)
-                          : make_map(B.ptr, p.K, p.N, B.ld, p.G, B.sg, bn / 2);
-    const bool tma_ok = EPI == EPI_BF16 && reinterpret_cast<uintptr_t>(p.C) % 16 == 0 && (p.ldc * 2) % 16 == 0 &&
-                        (p.G == 1 || (p.sc * 2) % 16 == 0) && !getenv("ODP_GEMM_NO_TMA_STORE");
+    CUtensorMap mb = !B.mn ? make_map(B.ptr, p.K, p.N, B.ld, p.G, B.sg, bn / 2)
+                     : (bn / 2) % 64 ? make_map(B.ptr, p.N, p.K, B.ld, p.G, B.sg, 64, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+                                     : make_map(B.ptr, p.N, p.K, B.ld, p.G, B.sg, 64);
+    CUtensorMap mc = ma, mx = ma;
+    bool tma_ok;
+    if constexpr (EPI == EPI_BF16) {
+      tma_ok = al16(p.C) && (p.ldc * 2) % 16 == 0 && (p.G == 1 || (p.sc * 2) % 16 == 0) &&
+               !getenv("ODP_GEMM_NO_TMA_STORE");
+      if (tma_ok) mc = make_map(p.C, p.N, p.M, p.ldc, p.G, p.sc, 32);
+    } else {
+      tma_ok = out_maps<EPI>(p, mc, mx);
+    }
     p.tma_store = tma_ok ? 1 : 0;
-    CUtensorMap mc = tma_ok ? make_map(p.C, p.N, p.M, p.ldc, p.G, p.sc, 32) : ma;
-#define ODP_GO2(AM, BMN, BNV, ST)                                       \
-  if constexpr (cfg2_ok<EPI, AM, BMN, BNV>()) {                         \
-    if (A.mn == AM && B.mn == BMN && bn == BNV) {                       \
-      launch_pair<AM, BMN, BNV, ST, EPI>(ma, mb, mc, p, st, max_ctas);  \
-      return true;                                                      \
-    }                                                                   \
+#define ODP_GO2(AM, BMN, BNV, ST)                                                                        \
+  if constexpr (cfg2_ok<EPI, AM, BMN, BNV>()) {                                                          \
+    if (A.mn == AM && B.mn == BMN && bn == BNV) {                                                        \
+      launch_pair<AM, BMN, BNV, fit_stages((BM + BNV / 2) * BK * 2, 8 * 4096, ST), EPI>(ma, mb, mc, mx, p, \
+                                                                                        st, max_ctas);   \
+      return true;                                                                                       \
+    }                                                                                                    \
   }
     ODP_GO2(false, false, 256, 6)
     ODP_GO2(false, true, 256, 6)
     ODP_GO2(true, false, 256, 6)
     ODP_GO2(true, true, 256, 6)
+    ODP_GO2(false, false, 192, 7)
+    ODP_GO2(false, true, 192, 7)
+    ODP_GO2(true, false, 192, 7)
+    ODP_GO2(true, true, 192, 7)
 #undef ODP_GO2
     return false;
   }
@@ -833,18 +1137,25 @@ static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, 
   long long b_rows_extent = EPI == EPI_SWIGLU ? 2LL * p.f_half : p.N;
   CUtensorMap mb = B.mn ? make_map(B.ptr, p.N, p.K, B.ld, p.G, B.sg, 64)
                         : make_map(B.ptr, p.K, b_rows_extent, B.ld, p.G, B.sg, rowsB);
-  // bf16 outputs of 128-wide tiles leave through TMA stores when the layout allows it
-  const bool tma_ok = (EPI == EPI_BF16 || EPI == EPI_LOGITS) && bn == 128 &&
-                      reinterpret_cast<uintptr_t>(p.C) % 16 == 0 && (p.ldc * 2) % 16 == 0 &&
-                      (p.G == 1 || (p.sc * 2) % 16 == 0) && !getenv("ODP_GEMM_NO_TMA_STORE");
+  // bf16 outputs of 128-wide tiles, and fp32 / residual / SwiGLU outputs of any tile
+  // width, leave through TMA stores when the layout allows it
+  CUtensorMap mc = ma, mx = ma;
+  bool tma_ok;
+  if constexpr (EPI == EPI_BF16 || EPI == EPI_LOGITS) {
+    tma_ok = bn == 128 && al16(p.C) && (p.ldc * 2) % 16 == 0 && (p.G == 1 || (p.sc * 2) % 16 == 0) &&
+             !getenv("ODP_GEMM_NO_TMA_STORE");
+    if (tma_ok) mc = make_map(p.C, p.N, p.M, p.ldc, p.G, p.sc, 32);
+  } else {
+    tma_ok = out_maps<EPI>(p, mc, mx);
+  }
   p.tma_store = tma_ok ? 1 : 0;
-  CUtensorMap mc = tma_ok ? make_map(p.C, p.N, p.M, p.ldc, p.G, p.sc, 32) : ma;
-#define ODP_GO(AM, BMN, BNV, ST)                                        \
-  if constexpr (cfg_ok<EPI, AM, BMN, BNV>()) {                          \
-    if (A.mn == AM && B.mn == BMN && bn == BNV) {                       \
-      launch_t<AM, BMN, BNV, ST, EPI>(ma, mb, mc, p, st, max_ctas);     \
-      return;                                                           \
-    }                                                                   \
+#define ODP_GO(AM, BMN, BNV, ST)                                                                       \
+  if constexpr (cfg_ok<EPI, AM, BMN, BNV>()) {                                                         \
+    if (A.mn == AM && B.mn == BMN && bn == BNV) {                                                      \
+      launch_t<AM, BMN, BNV, fit_stages((BM + BNV) * BK * 2, 8 * stg_warp_bytes(EPI, false), ST), EPI>( \
+          ma, mb, mc, mx, p, st, max_ctas);                                                            \
+      return;                                                                                          \
+    }                                                                                                  \
   }
   ODP_GO(false, false, 128, 6)
   ODP_GO(false, true, 128, 6)
@@ -855,6 +1166,10 @@ static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, 
   ODP_GO(true, false, 64, 8)
   ODP_GO(true, true, 64, 8)
   ODP_GO(false, false, 256, 4)
+  ODP_GO(false, false, 192, 4)
+  ODP_GO(false, true, 192, 4)
+  ODP_GO(true, false, 192, 4)
+  ODP_GO(true, true, 192, 4)
 #undef ODP_GO
   TORCH_CHECK(false, "unsupported GEMM configuration");
 }

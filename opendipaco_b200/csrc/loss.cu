@@ -124,27 +124,25 @@ __global__ void label_count_kernel(const int* __restrict__ labels, int M, float*
 constexpr int kCeThreads = 256;
 constexpr int kCeMaxV = 32768;  // the row (<= 64 KB of bf16) is staged in shared memory
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Two packed bf16 maxima (max.bf16x2) and the hardware base-2 exponential (ex2.approx).
+ODP_DEVICE uint32_t bmax2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ODP_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 ODP_DEVICE float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 ODP_DEVICE float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// Online (max, sum exp) update with one value.
-ODP_DEVICE void online_add(float& m, float& s, float x) {
-  if (x > m) {
-    s = s * __expf(m - x) + 1.f;
-    m = x;
-  } else {
-    s += __expf(x - m);
-  }
-}
-ODP_DEVICE void online_merge(float& m, float& s, float m2, float s2) {
-  const float M = fmaxf(m, m2);
-  s = (m == -INFINITY ? 0.f : s * __expf(m - M)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - M));
-  m = M;
-}
-
 // One CTA per row. The whole bf16 row is brought into shared memory with one bulk copy
 // (completion on an mbarrier, bounded wait), then
-//   (max, sum exp) in one online pass -> lse = max + log(sum),  loss = lse - x[label]
+//   max (packed bf16 pairs), sum exp -> lse = max + log(sum),  loss = lse - x[label]
 //   dlogits = (exp(x - lse) - onehot(label)) * inv_count[g]   written in place as bf16.
 // Rows with label < 0 get loss 0 and zero dlogits. 64 KB per CTA: three CTAs per SM
 // overlap one row's copy with another's arithmetic.
@@ -183,32 +181,41 @@ __global__ void __launch_bounds__(kCeThreads) ce_fused_kernel(__nv_bfloat16* log
   }
   __syncthreads();
   const bool ok = mbar_wait(&bar, 0, err, ERR_TIMEOUT_FULL);
-  float mx = -INFINITY, se = 0.f;
+  // pass 1: row max on packed bf16 pairs (exact in bf16)
+  uint32_t m2 = 0xff80ff80u;  // (-inf, -inf)
+  if (ok) {
+    for (int i = threadIdx.x; i < nvec; i += kCeThreads) {
+      const uint4 v = srow[i];
+      m2 = bmax2(m2, bmax2(bmax2(v.x, v.y), bmax2(v.z, v.w)));
+    }
+  }
+  float mx = fmaxf(bf_lo(m2), bf_hi(m2));
+  mx = warp_max(mx);
+  if (threadIdx.x % 32 == 0) red_m[threadIdx.x / 32] = mx;
+  __syncthreads();
+  mx = red_m[0];
+#pragma unroll
+  for (int w = 1; w < kCeThreads / 32; ++w) mx = fmaxf(mx, red_m[w]);
+  // pass 2: sum of exp(x - max) as 2^(x log2e - max log2e)
+  const float mb = mx * kLog2e;
+  float se0 = 0.f, se1 = 0.f;
   if (ok) {
     for (int i = threadIdx.x; i < nvec; i += kCeThreads) {
       const uint4 v = srow[i];
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        online_add(mx, se, bf_lo(w[e]));
-        online_add(mx, se, bf_hi(w[e]));
+        se0 += ex2_approx(fmaf(bf_lo(w[e]), kLog2e, -mb));
+        se1 += ex2_approx(fmaf(bf_hi(w[e]), kLog2e, -mb));
       }
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, mx, o), s2 = __shfl_xor_sync(0xffffffffu, se, o);
-    online_merge(mx, se, m2, s2);
-  }
-  if (threadIdx.x % 32 == 0) {
-    red_m[threadIdx.x / 32] = mx;
-    red_s[threadIdx.x / 32] = se;
-  }
+  float se = warp_sum(se0 + se1);
+  if (threadIdx.x % 32 == 0) red_s[threadIdx.x / 32] = se;
   __syncthreads();
-  mx = red_m[0];
-  se = red_s[0];
+  se = 0.f;
 #pragma unroll
-  for (int w = 1; w < kCeThreads / 32; ++w) online_merge(mx, se, red_m[w], red_s[w]);
+  for (int w = 0; w < kCeThreads / 32; ++w) se += red_s[w];
   if (!ok) return;  // the error word tells the host; this row is left as it was
   const float l = mx + logf(se);
   const float sc = inv_count[g];
@@ -217,19 +224,21 @@ __global__ void __launch_bounds__(kCeThreads) ce_fused_kernel(__nv_bfloat16* log
     const uint16_t raw = reinterpret_cast<const uint16_t*>(ce_smem)[y];
     row_loss[r] = l - __uint_as_float((uint32_t)raw << 16);
   }
+  // pass 3: dlogits = exp(x - lse) * sc = 2^(x log2e - (lse log2e - log2 sc)), the label's
+  // column minus sc afterwards by the thread that wrote its 16-byte group
+  const float ob = l * kLog2e - log2f(sc);
   for (int i = threadIdx.x; i < nvec; i += kCeThreads) {
     const uint4 v = srow[i];
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     uint32_t o[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float p0 = __expf(bf_lo(w[e]) - l), p1 = __expf(bf_hi(w[e]) - l);
-      const int c = i * 8 + e * 2;
-      if (c == y) p0 -= 1.f;
-      if (c + 1 == y) p1 -= 1.f;
-      o[e] = pack_bf16(p0 * sc, p1 * sc);
-    }
+    for (int e = 0; e < 4; ++e)
+      o[e] = pack_bf16(ex2_approx(fmaf(bf_lo(w[e]), kLog2e, -ob)), ex2_approx(fmaf(bf_hi(w[e]), kLog2e, -ob)));
     row[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if ((y / 8) % kCeThreads == (int)threadIdx.x) {
+    const float xy = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(ce_smem)[y] << 16);
+    rowp[y] = __float2bfloat16(ex2_approx(fmaf(xy, kLog2e, -ob)) - sc);
   }
 }
 

@@ -92,6 +92,10 @@ def bench_gemm(G: int, M: int, H: int, V: int, F: int, reps: int, flush) -> list
          lambda: gemm(logits, V, M * V, False, w, H, V * H, True, dx, H, M * H, M, H, V, G, "f32")),
         ("dlogits^T x X (f32 dW)", V, H, M,
          lambda: gemm(logits, V, M * V, True, x, H, M * H, True, dw, H, V * H, V, H, M, G, "f32")),
+        ("dlogits x W (f32, 192-wide tiles)", M, H, V,
+         lambda: gemm(logits, V, M * V, False, w, H, V * H, True, dx, H, M * H, M, H, V, G, "f32", bn=192)),
+        ("dlogits^T x X (f32 dW, 192-wide tiles)", V, H, M,
+         lambda: gemm(logits, V, M * V, True, x, H, M * H, True, dw, H, V * H, V, H, M, G, "f32", bn=192)),
         ("X x Wgu^T (swiglu)", M, 2 * F, H,
          lambda: gemm(x, H, M * H, False, wgu, H, 2 * F * H, False, act, F, M * F, M, 2 * F, H, G, "swiglu",
                       aux=gu, ldx=2 * F, sx=M * 2 * F, f_half=F)),
