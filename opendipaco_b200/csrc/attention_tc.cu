@@ -21,6 +21,11 @@
 //   read K-major for dQ = dS K and MN-major (as P^T, dS^T) for
 //   dV += P^T dO -> [256,320), dK += dS^T Q -> [320,384), dQ = dS K -> [384,448)
 //   scale and the transpose of RoPE are applied in the epilogues.
+// When every kv head serves one query head (no accumulation across heads), a lean variant
+// uses 256 TMEM columns and 96 KB of shared memory so that two CTAs share an SM: dV goes
+// into S's columns and dK, dQ into [64,128) and dP's [128,192) once S and dP are read
+// out; P and dS share one pair of tiles (dV = P^T dO is issued and completed before dS,
+// kept in registers meanwhile, overwrites P).
 //
 // Operand tiles are [128 rows][64 bf16] in the canonical 128-byte-swizzle layout (16-byte
 // chunk index XOR row % 8, 8-row groups 1024 bytes apart), written by the threads
@@ -43,6 +48,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kFwdSmem = 3 * TILE + 1024;
 constexpr int kBwdSmem = 8 * TILE + 1024;
+constexpr int kBwdSmemLean = 6 * TILE + 1024;
 
 struct Args {
   const __nv_bfloat16* qkv;
@@ -147,6 +153,14 @@ ODP_DEVICE void put16(uint8_t* tiles, int row, int c0, const float (&v)[16]) {
   uint4 lo = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
   uint4 hi = make_uint4(pack_bf16(v[8], v[9]), pack_bf16(v[10], v[11]), pack_bf16(v[12], v[13]),
                         pack_bf16(v[14], v[15]));
+  *reinterpret_cast<uint4*>(t + sw_off(row, c)) = lo;
+  *reinterpret_cast<uint4*>(t + sw_off(row, c + 8)) = hi;
+}
+
+// The same 16 columns already packed as bf16 pairs (lo = columns c0..c0+7, hi = +8..15).
+ODP_DEVICE void put16_packed(uint8_t* tiles, int row, int c0, uint4 lo, uint4 hi) {
+  uint8_t* t = tiles + (c0 >> 6) * TILE;
+  const int c = c0 & 63;
   *reinterpret_cast<uint4*>(t + sw_off(row, c)) = lo;
   *reinterpret_cast<uint4*>(t + sw_off(row, c + 8)) = hi;
 }
@@ -285,15 +299,17 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
   if (warp == 0) tmem_dealloc(tm, 128);
 }
 
-__global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
+template <bool LEAN>
+__global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
+  constexpr uint32_t kCols = LEAN ? 256 : 512;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t* sK = sm;
   uint8_t* sV = sm + TILE;
   uint8_t* sQ = sm + 2 * TILE;
   uint8_t* sdO = sm + 3 * TILE;
-  uint8_t* sP = sm + 4 * TILE;   // 2 tiles
-  uint8_t* sdS = sm + 6 * TILE;  // 2 tiles
+  uint8_t* sP = sm + 4 * TILE;                  // 2 tiles
+  uint8_t* sdS = LEAN ? sP : sm + 6 * TILE;     // 2 tiles (the lean variant reuses P's)
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_holder;
   __shared__ float sDelta[T], sLse[T];
@@ -307,7 +323,7 @@ __global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
     mbar_init(&bar, 1);
     fence_barrier_init();
   }
-  if (warp == 0) tmem_alloc(&tmem_holder, 512);
+  if (warp == 0) tmem_alloc(&tmem_holder, kCols);
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
   stage_async<256>(sK, base, a.ld, (a.nh + kvh) * D, a.S);
@@ -316,7 +332,8 @@ __global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tmem_holder;
-  const uint32_t tS = tm, tdP = tm + 128, tdV = tm + 256, tdK = tm + 320, tdQ = tm + 384;
+  const uint32_t tS = tm, tdP = tm + 128;
+  const uint32_t tdV = LEAN ? tm : tm + 256, tdK = LEAN ? tm + 64 : tm + 320, tdQ = LEAN ? tm + 128 : tm + 384;
   const float sl2 = a.scale * kLog2e;
   uint32_t phase = 0;
   bool ok = true;
@@ -325,15 +342,22 @@ __global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
     const int h = kvh * grp + hi;
     stage_async<256>(sQ, base, a.ld, h * D, a.S);
     stage_async<256>(sdO, dobase, a.ldo, h * D, a.S);
-    float orow[64];
-    if (threadIdx.x < T && threadIdx.x < a.S) {  // this thread's O row, for delta = rowsum(dO O)
+    // this thread's O row, for delta = rowsum(dO O): loaded while the tiles stream in
+    // (the lean variant keeps it packed, 32 registers instead of 64)
+    uint4 opk[8];
+    float orow[LEAN ? 1 : 64];
+    if (threadIdx.x < T && threadIdx.x < a.S) {
       const uint4* op = reinterpret_cast<const uint4*>(a.o + ((long long)gb * a.S + threadIdx.x) * a.ldo + h * D);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 ov = op[c];
-        const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&ov);
+        if constexpr (LEAN) {
+          opk[c] = ov;
+        } else {
+          const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&ov);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) orow[c * 8 + e] = __bfloat162float(x[e]);
+          for (int e = 0; e < 8; ++e) orow[c * 8 + e] = __bfloat162float(x[e]);
+        }
       }
     }
     cp_async_wait_all();
@@ -347,8 +371,12 @@ __global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
         for (int c = 0; c < 8; ++c) {
           const uint4 dv = *reinterpret_cast<const uint4*>(sdO + sw_off(r, c * 8));
           const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(&dv);
+          const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&opk[c]);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) dsum += orow[c * 8 + e] * __bfloat162float(y[e]);
+          for (int e = 0; e < 8; ++e) {
+            const float ov = LEAN ? __bfloat162float(x[e]) : orow[(c * 8 + e) % (LEAN ? 1 : 64)];
+            dsum += ov * __bfloat162float(y[e]);
+          }
         }
         l2 = a.lse[((long long)gb * a.nh + h) * a.S + r] * kLog2e;
       }
@@ -373,10 +401,11 @@ __global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
     phase ^= 1;
     ok = __syncthreads_and(ok);
     tc_fence_after();
+    uint4 dsk[LEAN ? 4 : 1][2];  // lean: this thread's dS (bf16 pairs) until P has been consumed
     {
       const int nvalid = row < a.S ? row + 1 : 0;
       const float delta = sDelta[row], l2 = sLse[row];
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int c0 = half * 64 + c * 16;
         float s[16], dp[16];
@@ -389,19 +418,49 @@ __global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
           dp[e] = p * (dp[e] - delta);
         }
         put16(sP, row, c0, s);
-        put16(sdS, row, c0, dp);
+        if constexpr (LEAN) {
+          dsk[c][0] = make_uint4(pack_bf16(dp[0], dp[1]), pack_bf16(dp[2], dp[3]), pack_bf16(dp[4], dp[5]),
+                                 pack_bf16(dp[6], dp[7]));
+          dsk[c][1] = make_uint4(pack_bf16(dp[8], dp[9]), pack_bf16(dp[10], dp[11]), pack_bf16(dp[12], dp[13]),
+                                 pack_bf16(dp[14], dp[15]));
+        } else {
+          put16(sdS, row, c0, dp);
+        }
       }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if constexpr (LEAN) {
+      // dV = P^T dO into S's columns (every thread has read S and dP), then dS over P
+      if (threadIdx.x == 0 && ok) {
+        constexpr uint32_t idT = umma_idesc_bf16(T, D, true, true);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tdV, desc_mn(smem_u32(sP), kk), desc_mn(smem_u32(sdO), kk), idT, kk > 0);
+        umma_commit(&bar);
+      }
+      __syncwarp();
+      if (ok) ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
+      phase ^= 1;
+      ok = __syncthreads_and(ok);
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) put16_packed(sdS, row, half * 64 + c * 16, dsk[c][0], dsk[c][1]);
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+    }
     if (threadIdx.x == 0 && ok) {
       constexpr uint32_t idT = umma_idesc_bf16(T, D, true, true);    // A^T from [query][key] tiles
       constexpr uint32_t idQ = umma_idesc_bf16(T, D, false, true);   // dS (K-major) x K (MN-major)
+      if constexpr (!LEAN) {
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        umma_bf16(tdV, desc_mn(smem_u32(sP), kk), desc_mn(smem_u32(sdO), kk), idT, (hi > 0 || kk > 0));
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tdV, desc_mn(smem_u32(sP), kk), desc_mn(smem_u32(sdO), kk), idT, (hi > 0 || kk > 0));
+      }
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
         umma_bf16(tdK, desc_mn(smem_u32(sdS), kk), desc_mn(smem_u32(sQ), kk), idT, (hi > 0 || kk > 0));
@@ -437,7 +496,7 @@ __global__ void __launch_bounds__(256, 1) bwd_kernel(Args a) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tm, 512);
+  if (warp == 0) tmem_dealloc(tm, kCols);
 }
 
 }  // namespace attn_tc
@@ -472,8 +531,6 @@ void attention_fwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         odp::attn_tc::kFwdSmem));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        odp::attn_tc::kBwdSmem));
     attr = true;
   }
   auto a = tc_args(qkv, S, nh, nkv, cosT, sinT, o, lse, err);
@@ -489,10 +546,10 @@ void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
   c10::cuda::CUDAGuard guard(qkv.device());
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        odp::attn_tc::kFwdSmem));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        odp::attn_tc::kBwdSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::bwd_kernel<false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, odp::attn_tc::kBwdSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::bwd_kernel<true>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, odp::attn_tc::kBwdSmemLean));
     attr = true;
   }
   TORCH_CHECK(dout.is_contiguous() && dqkv.is_contiguous(), "attention: contiguous tensors");
@@ -500,6 +557,10 @@ void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
   a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   dim3 grid((unsigned)nkv, (unsigned)GB);
-  odp::attn_tc::bwd_kernel<<<grid, 256, odp::attn_tc::kBwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
+  const char* env = getenv("ODP_ATTN_BWD_LEAN");
+  if (nh == nkv && !(env && env[0] == '0'))
+    odp::attn_tc::bwd_kernel<true><<<grid, 256, odp::attn_tc::kBwdSmemLean, at::cuda::getCurrentCUDAStream()>>>(a);
+  else
+    odp::attn_tc::bwd_kernel<false><<<grid, 256, odp::attn_tc::kBwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -63,7 +63,9 @@ void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks,
                         torch::Tensor glob_ptrs, torch::Tensor pads, torch::Tensor mom, int64_t rank, int64_t world,
                         int64_t epoch, double lr, double m, bool nesterov, bool first, torch::Tensor sq_part,
                         torch::Tensor err, c10::optional<torch::Tensor> qd_ptrs,
-                        c10::optional<torch::Tensor> qs_ptrs);
+                        c10::optional<torch::Tensor> qs_ptrs, int64_t kcap);
+void outer_nvlink_topk(torch::Tensor regs, int64_t nregs, int64_t total_blocks, double density, int64_t kcap,
+                       torch::Tensor delta, torch::Tensor res, torch::Tensor spi, torch::Tensor spv);
 void outer_nvlink_quant(torch::Tensor regs, int64_t nregs, int64_t total_groups, torch::Tensor delta,
                         torch::Tensor res, torch::Tensor qd, torch::Tensor qs);
 void outer_nvlink_bcast(torch::Tensor cps, int64_t ncp, int64_t total_chunks, torch::Tensor pads, int64_t rank,
@@ -94,6 +96,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_adamw", &dp_adamw);
   m.def("dp_adam8bit", &dp_adam8bit);
   m.def("outer_nvlink_quant", &outer_nvlink_quant);
+  m.def("outer_nvlink_topk", &outer_nvlink_topk);
   m.def("attention_bwd_tc", &attention_bwd_tc);
   m.def("ce_forward", &ce_forward);
   m.def("ce_backward", &ce_backward);

@@ -101,7 +101,10 @@ ODP_DEVICE void stage_bf16x32(uint8_t* stg, int row, int c0, const float* v) {
   }
 }
 
-ODP_DEVICE float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// silu and the logistic function with the fast reciprocal (__fdividef: 2 ulp, far below
+// the bf16 rounding that follows every use here; 0 when 1 + e^-x overflows).
+ODP_DEVICE float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+ODP_DEVICE float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // Load 32 accumulator columns [c, c+32) of this thread's TMEM lane into fp32.
 ODP_DEVICE void load32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -227,7 +230,7 @@ ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float dh = bf16_round(v[i]);
-          const float sg = 1.0f / (1.0f + __expf(-gv[i]));
+          const float sg = sigmoid_f(gv[i]);
           ou[i] = dh * bf16_round(gv[i] * sg);
           og[i] = bf16_round(dh * uv[i]) * sg * (1.0f + gv[i] * (1.0f - sg));
         }
@@ -423,7 +426,7 @@ ODP_DEVICE bool epilogue_tma(const GemmParams& p, uint32_t tmem_acc, int q, int 
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float dh = bf16_round(__uint_as_float(r[i]));
-        const float sg = 1.0f / (1.0f + __expf(-gv[i]));
+        const float sg = sigmoid_f(gv[i]);
         ou[i] = dh * bf16_round(gv[i] * sg);
         og[i] = bf16_round(dh * uv[i]) * sg * (1.0f + gv[i] * (1.0f - sg));
       }

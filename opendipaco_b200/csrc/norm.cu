@@ -43,6 +43,49 @@ __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, long long sx, co
   if (lane == 0) rstd[(long long)g * M + r] = rs;
 }
 
+// The same with the row held in registers (H = 128 * NV): x is read once, the weights
+// once per warp, and four rows are in flight per warp.
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_reg_kernel(const float* __restrict__ x, long long sx,
+                                                              const float* __restrict__ w, long long sw,
+                                                              __nv_bfloat16* __restrict__ y, long long sy,
+                                                              float* __restrict__ rstd, int M, int H, int G,
+                                                              float eps) {
+  constexpr int R = 4;
+  const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32 * R;
+  const int lane = threadIdx.x % 32;
+  float4 v[R][NV];
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    const long long wr_ = warp0 + k;
+    if (wr_ >= (long long)G * M) break;
+    const int g = (int)(wr_ / M), r = (int)(wr_ % M);
+    const float4* xr = reinterpret_cast<const float4*>(x + g * sx + (long long)r * H);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) v[k][j] = xr[lane + 32 * j];
+  }
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    const long long wr_ = warp0 + k;
+    if (wr_ >= (long long)G * M) break;
+    const int g = (int)(wr_ / M), r = (int)(wr_ % M);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) ss += v[k][j].x * v[k][j].x + v[k][j].y * v[k][j].y + v[k][j].z * v[k][j].z + v[k][j].w * v[k][j].w;
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / H + eps);
+    const float4* wr = reinterpret_cast<const float4*>(w + g * sw);
+    uint2* yr = reinterpret_cast<uint2*>(y + g * sy + (long long)r * H);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 ww = wr[lane + 32 * j], a = v[k][j];
+      yr[lane + 32 * j] = make_uint2(pack_bf16(ww.x * (a.x * rs), ww.y * (a.y * rs)),
+                                     pack_bf16(ww.z * (a.z * rs), ww.w * (a.w * rs)));
+    }
+    if (lane == 0) rstd[(long long)g * M + r] = rs;
+  }
+}
+
 // dy: [G][M][H] fp32 (grad w.r.t. the norm output); dres: optional residual grad added to dx.
 // dx may alias dres. dw_part: [G][nblk][H] partial sums of dy*xhat for rows of each block.
 constexpr int kNormRowsPerBlock = 32;
@@ -99,6 +142,84 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, long long sx, co
       acc[i] = t;
     }
   }
+  __syncthreads();
+  float* out = dw_part + ((long long)g * nblk + b) * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < 8; ++k) s += sdw[k * H + i];
+    out[i] = s;
+  }
+}
+
+// Register-resident variant (H = 128 * NV): each warp loads its row's x, dy and residual
+// grad once, keeps the weights and its dw partial in registers, and folds the partials of
+// its block's 8 warps in a fixed order at the end. Same arithmetic as rmsnorm_bwd_kernel.
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const float* __restrict__ x, long long sx,
+                                                              const float* __restrict__ w, long long sw,
+                                                              const float* __restrict__ rstd,
+                                                              const float* __restrict__ dy, long long sdy,
+                                                              const float* dres, float* dx, long long sdx,
+                                                              __nv_bfloat16* dx16, float* __restrict__ dw_part, int M,
+                                                              int H, int G) {
+  const int nblk = (M + kNormRowsPerBlock - 1) / kNormRowsPerBlock;
+  const int g = blockIdx.x / nblk, b = blockIdx.x % nblk;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  extern __shared__ float sdw[];  // [8 warps][H]
+  const float4* w4 = reinterpret_cast<const float4*>(w + g * sw);
+  float4 wv[NV], acc[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    wv[j] = w4[lane + 32 * j];
+    acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll 1
+  for (int rr = warp; rr < kNormRowsPerBlock; rr += 8) {
+    const int r = b * kNormRowsPerBlock + rr;
+    if (r >= M) break;
+    const float4* xr = reinterpret_cast<const float4*>(x + g * sx + (long long)r * H);
+    const float4* dyr = reinterpret_cast<const float4*>(dy + g * sdy + (long long)r * H);
+    const float4* drr = dres ? reinterpret_cast<const float4*>(dres + g * sdx + (long long)r * H) : nullptr;
+    float4 d[NV], xv[NV], q[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      d[j] = dyr[lane + 32 * j];
+      xv[j] = xr[lane + 32 * j];
+      q[j] = drr ? drr[lane + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float rs = rstd[(long long)g * M + r];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 a = wv[j], dd = d[j], xx = xv[j];
+      dot += a.x * dd.x * (xx.x * rs) + a.y * dd.y * (xx.y * rs) + a.z * dd.z * (xx.z * rs) + a.w * dd.w * (xx.w * rs);
+    }
+    dot = warp_sum(dot) / H;
+    float4* dxr = reinterpret_cast<float4*>(dx + g * sdx + (long long)r * H);
+    uint2* d16 = dx16 ? reinterpret_cast<uint2*>(dx16 + g * sdx + (long long)r * H) : nullptr;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 a = wv[j], dd = d[j], xx = xv[j];
+      const float4 xh = make_float4(xx.x * rs, xx.y * rs, xx.z * rs, xx.w * rs);
+      float4 v = make_float4(rs * (a.x * dd.x - xh.x * dot), rs * (a.y * dd.y - xh.y * dot),
+                             rs * (a.z * dd.z - xh.z * dot), rs * (a.w * dd.w - xh.w * dot));
+      if (drr) {
+        v.x += q[j].x;
+        v.y += q[j].y;
+        v.z += q[j].z;
+        v.w += q[j].w;
+      }
+      dxr[lane + 32 * j] = v;
+      if (d16) d16[lane + 32 * j] = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+      acc[j].x += dd.x * xh.x;
+      acc[j].y += dd.y * xh.y;
+      acc[j].z += dd.z * xh.z;
+      acc[j].w += dd.w * xh.w;
+    }
+  }
+  float4* mine = reinterpret_cast<float4*>(sdw + warp * H);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) mine[lane + 32 * j] = acc[j];
   __syncthreads();
   float* out = dw_part + ((long long)g * nblk + b) * H;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -259,6 +380,20 @@ void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
   TORCH_CHECK(H % 128 == 0, "rmsnorm: hidden size must be a multiple of 128");
   c10::cuda::CUDAGuard guard(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
+  auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const bool reg = al16(x.data_ptr()) && al16(w.data_ptr()) && al16(y.data_ptr()) && sx % 4 == 0 && sw % 4 == 0 &&
+                   sy % 4 == 0;
+  const int nv = (int)(H / 128);
+#define ODP_RMS_FWD(NV)                                                                                          \
+  if (reg && nv == NV) {                                                                                         \
+    odp::rmsnorm_fwd_reg_kernel<NV><<<blocks_for(G * M * 8, 256), 256, 0, st>>>(                                 \
+        x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,    \
+        rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);                                             \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                              \
+    return;                                                                                                      \
+  }
+  ODP_RMS_FWD(1) ODP_RMS_FWD(2) ODP_RMS_FWD(3) ODP_RMS_FWD(4) ODP_RMS_FWD(8)
+#undef ODP_RMS_FWD
   odp::rmsnorm_fwd_kernel<<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
       x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,
       rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);
@@ -279,6 +414,22 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
                   (!dres.has_value() || al16(dres->data_ptr())),
               "rmsnorm_bwd: rows are read as float4 (16-byte aligned bases, strides multiple of 4)");
   const size_t smem = 8 * H * sizeof(float);
+  const int nv = (int)(H / 128);
+  bool launched = false;
+#define ODP_RMS_BWD(NV)                                                                                           \
+  if (!launched && H % 128 == 0 && nv == NV) {                                                                    \
+    if (smem > 48 * 1024)                                                                                         \
+      cudaFuncSetAttribute(odp::rmsnorm_bwd_reg_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    odp::rmsnorm_bwd_reg_kernel<NV><<<(int)G * nblk, 256, smem, st>>>(                                            \
+        x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, rstd.data_ptr<float>(), dy.data_ptr<float>(), sdy,      \
+        dres.has_value() ? dres->data_ptr<float>() : nullptr, dx.data_ptr<float>(), sdx,                          \
+        dx16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx16->data_ptr()) : nullptr, work.data_ptr<float>(),  \
+        (int)M, (int)H, (int)G);                                                                                  \
+    launched = true;                                                                                              \
+  }
+  ODP_RMS_BWD(1) ODP_RMS_BWD(2) ODP_RMS_BWD(3) ODP_RMS_BWD(4) ODP_RMS_BWD(8)
+#undef ODP_RMS_BWD
+  if (!launched) {
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(odp::rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   odp::rmsnorm_bwd_kernel<<<(int)G * nblk, 256, smem, st>>>(
@@ -286,6 +437,7 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
       dres.has_value() ? dres->data_ptr<float>() : nullptr, dx.data_ptr<float>(), sdx,
       dx16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx16->data_ptr()) : nullptr, work.data_ptr<float>(),
       (int)M, (int)H, (int)G);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::reduce_parts_kernel<<<blocks_for(G * H, 256), 256, 0, st>>>(work.data_ptr<float>(), nblk, (int)H, (int)G,
                                                                     dw.data_ptr<float>(), sdw, (float)beta);

@@ -27,7 +27,15 @@
 // 128 elements (symmetric buffers QD, QS) and keeps what the codes miss as the residual
 // for the next round. APPLY then reads the sharers' codes and scales instead of their
 // fp32 partials (0.53 instead of 4 bytes per element over NVLink) and dequantises them in
-// registers inside the same reduction. Waits never spin forever: after kWaitBoundNs they
+// registers inside the same reduction.
+//
+// Sparse mode (top-k): outer_nvlink_topk keeps, in every 4096-element block of each
+// rank's partial (plus residual), the k = ceil(density * len) entries of largest
+// magnitude (exact radix select, ties in index order) as (uint16 index, fp32 value)
+// pairs in symmetric buffers; the dropped entries stay in the residual. APPLY then adds
+// the sharers' pairs of its block into a zeroed shared-memory block, sharer by sharer
+// (deterministic), and runs the same update. Key regions and slices are 4096-aligned in
+// this mode, so an APPLY chunk is exactly one block. Waits never spin forever: after kWaitBoundNs they
 // record ERR_TIMEOUT_PEER and the kernel returns.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -46,7 +54,7 @@ struct NvKey {
   int nsh;          // number of sharer ranks
   int sh[kMaxSharers];
   float scale, inv_den;
-  int quant;        // 1: read the sharers' int4 codes + scales instead of their fp32 partials
+  int quant;        // 1: the sharers' int4 codes + scales; 2: their top-k (index, value) pairs
 };
 
 constexpr int kNvChunk = 4096;
@@ -139,6 +147,157 @@ __global__ void outer_nvlink_quant_kernel(const NvRegion* __restrict__ regs, int
   if (lane == 0) qs[(r.off + (w - r.group0) * kQGroup) / kQGroup] = sc;
 }
 
+// Block-wide exclusive prefix sum of one value per thread (256 threads); returns the
+// exclusive prefix, writes the total.
+ODP_DEVICE unsigned block_excl_scan256(unsigned v, unsigned* total) {
+  __shared__ unsigned wsum[8];
+  const int lane = threadIdx.x % 32, w = threadIdx.x / 32;
+  unsigned x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[w] = x;
+  __syncthreads();
+  unsigned before = 0, all = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    before += i < w ? wsum[i] : 0u;
+    all += wsum[i];
+  }
+  __syncthreads();
+  *total = all;
+  return before + x - v;
+}
+
+constexpr int kSpPer = kNvChunk / 256;  // elements per thread in the top-k kernel
+constexpr uint16_t kSpEmpty = 0xFFFF;
+
+// One 256-thread CTA per 4096-element block of the regions in `regs` (off, n = the key's
+// true size, group0 = the region's first block in launch order). Keys: |x| bits + 1 for
+// valid elements (0 for the block's tail past n), so the k-th largest key is found by a
+// 4-pass 8-bit radix select. Output slots are indexed by the block's position in the
+// arena ((off + b * 4096) / 4096) and padded with kSpEmpty.
+__global__ void __launch_bounds__(256) outer_nvlink_topk_kernel(const NvRegion* __restrict__ regs, int nregs,
+                                                                double density, int kcap,
+                                                                const float* __restrict__ delta,
+                                                                float* __restrict__ res, uint16_t* __restrict__ spi,
+                                                                float* __restrict__ spv) {
+  __shared__ unsigned hist[256];
+  __shared__ unsigned s_digit, s_remain;
+  const long long blk = blockIdx.x;
+  int lo = 0, hi = nregs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) / 2;
+    if (regs[mid].group0 <= blk) lo = mid;
+    else hi = mid - 1;
+  }
+  const NvRegion r = regs[lo];
+  const long long b = blk - r.group0;
+  const long long start = r.off + b * kNvChunk;
+  const int len = (int)min((long long)kNvChunk, r.n - b * kNvChunk);
+  const int kb = min(kcap, max(1, (int)ceil(density * (double)len)));
+  const int t = threadIdx.x, i0 = t * kSpPer;
+  float x[kSpPer];
+  unsigned key[kSpPer];
+#pragma unroll
+  for (int v = 0; v < kSpPer / 4; ++v) {
+    const float4 dv = *reinterpret_cast<const float4*>(delta + start + i0 + 4 * v);
+    const float4 rv = *reinterpret_cast<const float4*>(res + start + i0 + 4 * v);
+    x[4 * v] = __fadd_rn(dv.x, rv.x);
+    x[4 * v + 1] = __fadd_rn(dv.y, rv.y);
+    x[4 * v + 2] = __fadd_rn(dv.z, rv.z);
+    x[4 * v + 3] = __fadd_rn(dv.w, rv.w);
+  }
+#pragma unroll
+  for (int c = 0; c < kSpPer; ++c) key[c] = i0 + c < len ? __float_as_uint(fabsf(x[c])) + 1u : 0u;
+  // radix select: prefix of the kb-th largest key, 8 bits a pass from the top
+  unsigned prefix = 0, mask = 0, remain = (unsigned)kb;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    hist[t] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < kSpPer; ++c)
+      if ((key[c] & mask) == prefix) atomicAdd(&hist[(key[c] >> shift) & 255u], 1u);
+    __syncthreads();
+    if (t < 32) {
+      // lane l sums bins [255 - 8l - 7, 255 - 8l] (highest bins first)
+      unsigned cnt = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cnt += hist[255 - 8 * t - j];
+      unsigned cum = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, cum, o);
+        if (t >= o) cum += y;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, cum >= remain);
+      const int L = hit ? __ffs(hit) - 1 : -1;  // remain <= count of candidates, so some lane hits
+      if (L < 0 && t == 0) {
+        s_digit = 0;
+        s_remain = remain;
+      }
+      if (t == L) {
+        unsigned before = cum - cnt;
+        for (int j = 0; j < 8; ++j) {
+          const int bin = 255 - 8 * t - j;
+          if (before + hist[bin] >= remain) {
+            s_digit = (unsigned)bin;
+            s_remain = remain - before;
+            break;
+          }
+          before += hist[bin];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= s_digit << shift;
+    mask |= 0xFFu << shift;
+    remain = s_remain;
+    __syncthreads();
+  }
+  // keep key > T, and the first `remain` keys == T in index order
+  unsigned n_eq = 0;
+#pragma unroll
+  for (int c = 0; c < kSpPer; ++c) n_eq += key[c] == prefix;
+  unsigned tot;
+  unsigned eq_before = block_excl_scan256(n_eq, &tot);
+  bool keep[kSpPer];
+  unsigned n_keep = 0;
+#pragma unroll
+  for (int c = 0; c < kSpPer; ++c) {
+    bool k = key[c] > prefix;
+    if (key[c] == prefix) {
+      k = eq_before < remain;
+      ++eq_before;
+    }
+    keep[c] = k;
+    n_keep += k;
+  }
+  unsigned pos = block_excl_scan256(n_keep, &tot);
+  uint16_t* oi = spi + (start / kNvChunk) * kcap;
+  float* ov = spv + (start / kNvChunk) * kcap;
+  float rnew[kSpPer];
+#pragma unroll
+  for (int c = 0; c < kSpPer; ++c) {
+    rnew[c] = keep[c] ? 0.f : (i0 + c < len ? x[c] : 0.f);
+    if (keep[c]) {
+      oi[pos] = (uint16_t)(i0 + c);
+      ov[pos] = x[c];
+      ++pos;
+    }
+  }
+  for (int i = (int)tot + t; i < kcap; i += 256) {
+    oi[i] = kSpEmpty;
+    ov[i] = 0.f;
+  }
+#pragma unroll
+  for (int v = 0; v < kSpPer / 4; ++v)
+    *reinterpret_cast<float4*>(res + start + i0 + 4 * v) =
+        make_float4(rnew[4 * v], rnew[4 * v + 1], rnew[4 * v + 2], rnew[4 * v + 3]);
+}
+
 __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nkeys, long long total_chunks,
                                           const unsigned long long* __restrict__ delta_ptrs,
                                           const unsigned long long* __restrict__ glob_ptrs,
@@ -146,9 +305,10 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
                                           int rank, int world, unsigned epoch, float lr, float m, int nesterov,
                                           int first, float* __restrict__ sq_part, int* err,
                                           const unsigned long long* __restrict__ qd_ptrs,
-                                          const unsigned long long* __restrict__ qs_ptrs) {
+                                          const unsigned long long* __restrict__ qs_ptrs, int kcap) {
   if (!cross_gpu_barrier(pads, rank, world, 0, epoch, err, blockIdx.x == 0)) return;
   __shared__ float red[8];
+  __shared__ __align__(16) float dense[kNvChunk];  // top-k mode: this chunk's summed pairs
   for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
     int lo = 0, hi = nkeys - 1;
     while (lo < hi) {
@@ -161,9 +321,26 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
     const long long e1 = min(e0 + kNvChunk, k.s1);
     float sq = 0.f;
     const float* gl = reinterpret_cast<const float*>(glob_ptrs[rank]) + k.off;
+    if (k.quant == 2) {
+      // the chunk is one 4096-element block: add every sharer's (index, value) pairs
+      __syncthreads();
+      for (int i = threadIdx.x; i < kNvChunk; i += blockDim.x) dense[i] = 0.f;
+      __syncthreads();
+      const long long blk = (k.off + e0) / kNvChunk;
+      for (int j = 0; j < k.nsh; ++j) {
+        const uint16_t* si = reinterpret_cast<const uint16_t*>(qd_ptrs[k.sh[j]]) + blk * kcap;
+        const float* sv = reinterpret_cast<const float*>(qs_ptrs[k.sh[j]]) + blk * kcap;
+        for (int i = threadIdx.x; i < kcap; i += blockDim.x) {
+          const uint16_t ix = *reinterpret_cast<const volatile uint16_t*>(si + i);
+          if (ix != kSpEmpty && ix < kNvChunk) dense[ix] = __fadd_rn(dense[ix], *reinterpret_cast<const volatile float*>(sv + i));
+        }
+        __syncthreads();  // indices are unique within a sharer; sharers add in rank order
+      }
+    }
     for (long long e = e0 + threadIdx.x * 4; e < e1; e += blockDim.x * 4) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int j = 0; j < k.nsh; ++j) {
+      if (k.quant == 2) acc = *reinterpret_cast<const float4*>(dense + (e - e0));
+      for (int j = 0; j < (k.quant == 2 ? 0 : k.nsh); ++j) {
         float4 d;
         if (k.quant) {  // int4 codes + group scale of sharer j, dequantised in registers
           const long long ge = k.off + e;
@@ -250,7 +427,8 @@ __global__ void outer_nvlink_bcast_kernel(const NvCopy* __restrict__ cps, int nc
 void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks, torch::Tensor delta_ptrs,
                         torch::Tensor glob_ptrs, torch::Tensor pads, torch::Tensor mom, int64_t rank, int64_t world,
                         int64_t epoch, double lr, double m, bool nesterov, bool first, torch::Tensor sq_part,
-                        torch::Tensor err, c10::optional<torch::Tensor> qd_ptrs, c10::optional<torch::Tensor> qs_ptrs) {
+                        torch::Tensor err, c10::optional<torch::Tensor> qd_ptrs, c10::optional<torch::Tensor> qs_ptrs,
+                        int64_t kcap) {
   static_assert(sizeof(odp::NvKey) == 80, "NvKey layout");
   c10::cuda::CUDAGuard guard(mom.device());
   TORCH_CHECK(world <= 64, "outer_nvlink: world too large");
@@ -264,7 +442,21 @@ void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks,
       (unsigned)epoch, (float)lr, (float)m, nesterov ? 1 : 0, first ? 1 : 0, sq_part.data_ptr<float>(),
       err.data_ptr<int>(),
       qd_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qd_ptrs->data_ptr()) : nullptr,
-      qs_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qs_ptrs->data_ptr()) : nullptr);
+      qs_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qs_ptrs->data_ptr()) : nullptr, (int)kcap);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// regs: int64 [nregs][3] = (element offset (4096-aligned), true size, first block in
+// launch order); spi / spv: [arena blocks][kcap] pair slots.
+void outer_nvlink_topk(torch::Tensor regs, int64_t nregs, int64_t total_blocks, double density, int64_t kcap,
+                       torch::Tensor delta, torch::Tensor res, torch::Tensor spi, torch::Tensor spv) {
+  c10::cuda::CUDAGuard guard(delta.device());
+  TORCH_CHECK(kcap >= 1 && kcap <= odp::kNvChunk, "outer_nvlink_topk: bad capacity");
+  if (total_blocks == 0) return;
+  odp::outer_nvlink_topk_kernel<<<(unsigned)total_blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const odp::NvRegion*>(regs.data_ptr()), (int)nregs, density, (int)kcap,
+      delta.data_ptr<float>(), res.data_ptr<float>(), reinterpret_cast<uint16_t*>(spi.data_ptr()),
+      spv.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -24,6 +24,14 @@ GPU are not compressed. This is the NVLink counterpart of the int4 wire compress
 of outer gradients in the reference's control plane (src/opendipaco/schedule/compress.py:92);
 the residual is not checkpointed and restarts at zero after a resume.
 
+``compress="topk"`` (with ``density``, default 0.01) keeps instead, in every 4096-element
+block of a rank's partial plus residual, the ``ceil(density * len)`` entries of largest
+magnitude as (uint16 index, fp32 value) pairs (a TOPK kernel, exact radix select); APPLY
+sums the sharers' pairs of its block in shared memory. This is the blockwise analogue of
+the reference's per-row top-k sparsification with error feedback
+(src/opendipaco/schedule/compress.py:183); key regions and slices are 4096-aligned so an
+APPLY chunk is one block.
+
 Buffers are allocated with ``torch.distributed._symmetric_memory`` (``empty`` +
 ``rendezvous`` over the world group): the bank's GLOB, DELTA and momentum arenas
 (identical offsets on every rank: one region per module key in ``module_keys()``
@@ -33,6 +41,8 @@ raises :class:`~opendipaco_b200.ops.KernelTimeout` after the round.
 """
 
 from __future__ import annotations
+
+import math
 
 import numpy as np
 import torch
@@ -50,6 +60,7 @@ assert NVKEY.itemsize == 80 and NVCOPY.itemsize == 40
 NVREGION = np.dtype([("off", "<i8"), ("n", "<i8"), ("group0", "<i8")])
 ALIGN = 256
 QGROUP = 128
+SPBLOCK = 4096  # top-k block = one APPLY chunk
 
 
 def _ru(n: int, a: int = ALIGN) -> int:
@@ -59,11 +70,17 @@ def _ru(n: int, a: int = ALIGN) -> int:
 class NVLinkBackend(TorchDistBackend):
     outer_launches = 3
 
-    def __init__(self, topology, device: torch.device | None = None, dp: int = 1, compress: str | None = None):
+    def __init__(self, topology, device: torch.device | None = None, dp: int = 1, compress: str | None = None,
+                 density: float = 0.01):
         super().__init__(topology, device, dp=dp)
-        if compress not in (None, "none", "int4"):
-            raise ValueError(f"unknown NVLink outer-step compression {compress!r} (None or 'int4')")
+        if compress not in (None, "none", "int4", "topk"):
+            raise ValueError(f"unknown NVLink outer-step compression {compress!r} (None, 'int4' or 'topk')")
+        if not 0.0 < density <= 1.0:
+            raise ValueError("density must be in (0, 1]")
         self.compress = compress if compress != "none" else None
+        self.density = float(density)
+        self.kcap = max(1, math.ceil(self.density * SPBLOCK))
+        self._align = SPBLOCK if self.compress == "topk" else ALIGN
         if self.compress:
             self.outer_launches = 4
         self._dp_handles: list = []
@@ -80,7 +97,7 @@ class NVLinkBackend(TorchDistBackend):
         self._offs, off = {}, 0
         for k in self.topology.module_keys():
             self._offs[k] = off
-            off += _ru(sizes[k])
+            off += _ru(sizes[k], self._align)
         self._sizes = dict(sizes)
         total = max(off, ALIGN)
         group = dist.group.WORLD.group_name
@@ -96,9 +113,14 @@ class NVLinkBackend(TorchDistBackend):
         self.DELTA, self._hd = sym(total, torch.float32)
         self.MOM, self._hm = sym(total, torch.float32)
         self.PAD, self._hp = sym(2 * self.world_size, torch.int32)
-        if self.compress:
+        if self.compress == "int4":
             self.QD, self._hqd = sym(total // 8, torch.int32)       # 4-bit codes, two per byte
             self.QS, self._hqs = sym(total // QGROUP, torch.float32)  # one scale per 128 elements
+        elif self.compress == "topk":
+            nblk = total // SPBLOCK
+            self.QD, self._hqd = sym((nblk * self.kcap + 1) // 2, torch.int32)  # uint16 indices
+            self.QS, self._hqs = sym(nblk * self.kcap, torch.float32)         # values
+        if self.compress:
             self.RES = torch.zeros(total, dtype=torch.float32, device=self.dev)
         torch.cuda.synchronize(self.dev)
         dist.barrier()
@@ -149,12 +171,14 @@ class NVLinkBackend(TorchDistBackend):
         return tab.to(self.device)
 
     # ------------------------------------------------------------------ slices
-    def slice_of(self, key: str) -> tuple[int, int]:
-        """[s0, s1) of ``key`` owned by this rank in the cross-GPU outer step."""
+    def slice_of(self, key: str, rank: int | None = None) -> tuple[int, int]:
+        """[s0, s1) of ``key`` owned by ``rank`` (default: this rank) in the cross-GPU outer
+        step: the key's sharers split it evenly, in multiples of 4 elements (of whole
+        4096-element blocks in top-k mode)."""
         sh = self.sharing_ranks(key)
         n = self._sizes[key]
-        per = _ru((n + len(sh) - 1) // len(sh), 4)
-        i = sh.index(self.rank)
+        per = _ru((n + len(sh) - 1) // len(sh), SPBLOCK if self.compress == "topk" else 4)
+        i = sh.index(self.rank if rank is None else rank)
         return min(n, i * per), min(n, (i + 1) * per)
 
     def _build(self, ex, plan) -> None:
@@ -188,10 +212,15 @@ class NVLinkBackend(TorchDistBackend):
             rec["sh"][0, :len(sh)] = sh
             rec["scale"], rec["inv_den"] = s.scale, s.inv_den
             if self.compress and len(sh) > 1:
-                rec["quant"] = 1
                 r = np.zeros(1, dtype=NVREGION)
-                ng = _ru(s.glob.numel(), QGROUP) // QGROUP
-                r["off"], r["n"], r["group0"] = self._offs[s.key], ng * QGROUP, g0
+                if self.compress == "int4":
+                    rec["quant"] = 1
+                    ng = _ru(s.glob.numel(), QGROUP) // QGROUP
+                    r["off"], r["n"], r["group0"] = self._offs[s.key], ng * QGROUP, g0
+                else:
+                    rec["quant"] = 2
+                    ng = _ru(s.glob.numel(), SPBLOCK) // SPBLOCK
+                    r["off"], r["n"], r["group0"] = self._offs[s.key], s.glob.numel(), g0
                 regs.append(r)
                 g0 += ng
             if nch:
@@ -226,14 +255,18 @@ class NVLinkBackend(TorchDistBackend):
         if t["cplan"] is not None:
             t["cplan"].run(0.0, 0.0, False, False)
         qd = qs = None
-        if self.compress:
+        if self.compress == "int4":
             ext().outer_nvlink_quant(t["regs"], t["nregs"], t["groups"], self.DELTA, self.RES,
                                      self.QD.view(torch.uint8), self.QS)
+        elif self.compress == "topk":
+            ext().outer_nvlink_topk(t["regs"], t["nregs"], t["groups"], self.density, self.kcap, self.DELTA,
+                                    self.RES, self.QD.view(torch.int16), self.QS)
+        if self.compress:
             qd, qs = self._qdptrs, self._qsptrs
         self._epoch += 1
         ext().outer_nvlink_apply(t["keys"], t["nkeys"], t["chunks"], self._dptrs, self._gptrs, self._pptrs,
                                  self.MOM, self.rank, self.world_size, self._epoch, dl.outer_lr,
-                                 dl.outer_momentum, dl.outer_nesterov, first, t["sq"], err, qd, qs)
+                                 dl.outer_momentum, dl.outer_nesterov, first, t["sq"], err, qd, qs, self.kcap)
         ext().outer_nvlink_bcast(t["cps"], t["ncp"], t["cchunks"], self._pptrs, self.rank, self.world_size,
                                  self._epoch, err)
 
@@ -259,11 +292,7 @@ class NVLinkBackend(TorchDistBackend):
                 if r == self.rank:
                     continue
                 peer = self._hm.get_buffer(r, (self.MOM.numel(),), torch.float32)
-                sh = self.sharing_ranks(key)
-                n = self._sizes[key]
-                per = _ru((n + len(sh) - 1) // len(sh), 4)
-                i = sh.index(r)
-                s0, s1 = min(n, i * per), min(n, (i + 1) * per)
+                s0, s1 = self.slice_of(key, r)
                 if s1 > s0:
                     buf[s0:s1].copy_(peer[off + s0:off + s1])
         torch.cuda.synchronize(self.dev)

@@ -6,7 +6,8 @@ MODE: "cpu" (gloo, module executor, TorchDistBackend), "nccl" (fused executor,
 NCCL outer step) or "nvlink" (fused executor, peer-memory outer step); a "_dp2"
 suffix puts every path on a group of two ranks (intra-path data parallelism), a further
 "_8bit" suffix selects blockwise 8-bit Adam as the inner optimizer, and "nvlink_q4" sends
-int4 codes instead of fp32 partials through the NVLink outer step. Writes
+int4 codes instead of fp32 partials through the NVLink outer step ("nvlink_topk": the
+top 5% of each 4096-element block as (index, value) pairs). Writes
 ``OUT_DIR/{MODE}_rank{r}.pt`` with the rank's bank, losses and a consistency flag.
 """
 
@@ -29,7 +30,8 @@ from opendipaco_b200.topology import is_private_key  # noqa: E402
 def main():
     out_dir, mode = sys.argv[1], sys.argv[2]
     q4 = mode.endswith("_q4")
-    rest = mode[:-3] if q4 else mode
+    topk = mode.endswith("_topk")
+    rest = mode[:-3] if q4 else mode[:-5] if topk else mode
     opt8 = rest.endswith("_8bit")
     core = rest[:-5] if opt8 else rest
     dp = 2 if core.endswith("_dp2") else 1
@@ -57,7 +59,8 @@ def main():
     if base == "nvlink":
         from opendipaco_b200.parallel.backend.nvlink import NVLinkBackend
 
-        backend = NVLinkBackend(topo, device=dev, dp=dp, compress="int4" if q4 else None)
+        backend = NVLinkBackend(topo, device=dev, dp=dp, compress="int4" if q4 else "topk" if topk else None,
+                                density=0.05)
     else:
         backend = TorchDistBackend(topo, device=dev, dp=dp)
     eng = DiPaCoEngine(cfg, dl, backend, device=dev, seed=0)
@@ -86,7 +89,8 @@ def main():
     # checkpoint round trip (momentum gathered from the slice owners)
     ck = os.path.join(out_dir, f"ckpt_{mode}")
     save_checkpoint(eng, ck)
-    b2 = (NVLinkBackend(topo, device=dev, dp=dp, compress="int4" if q4 else None) if base == "nvlink"
+    b2 = (NVLinkBackend(topo, device=dev, dp=dp, compress="int4" if q4 else "topk" if topk else None,
+                                density=0.05) if base == "nvlink"
           else TorchDistBackend(topo, device=dev, dp=dp))
     eng2 = DiPaCoEngine(cfg, dl, b2, device=dev, seed=5)
     load_checkpoint(eng2, ck)

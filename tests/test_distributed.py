@@ -127,3 +127,27 @@ def test_nvlink_int4_outer_step_tracks_uncompressed(tmp_path):
             ub = torch.cat([(b["bank"][k][n] - b["init"][k][n]).float().reshape(-1) for n in b["bank"][k]])
             rel = ((ua - ub).norm() / ub.norm().clamp_min(1e-12)).item()
             assert rel < 0.25, (k, rel)
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_nvlink_topk_outer_step_stays_consistent(tmp_path):
+    """Top-k (5% per 4096-element block) pairs with error feedback in the NVLink outer
+    step: sharers stay identical, checkpoints round-trip, round-0 losses are unchanged and
+    the shared modules move in the direction of the uncompressed update."""
+    from opendipaco_b200.topology import is_private_key
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    sp = _launch(tmp_path, "nvlink_topk", 2, 29631)
+    nv = _launch(tmp_path, "nvlink", 2, 29633)
+    for a, b in zip(sp, nv):
+        assert a["consistent"] and a["ckpt_same"] and a["resumed"]
+        assert a["losses"][0] == b["losses"][0]
+        for k in a["bank"]:
+            if is_private_key(k):
+                continue
+            ua = torch.cat([(a["bank"][k][n] - a["init"][k][n]).float().reshape(-1) for n in a["bank"][k]])
+            ub = torch.cat([(b["bank"][k][n] - b["init"][k][n]).float().reshape(-1) for n in b["bank"][k]])
+            cos = torch.nn.functional.cosine_similarity(ua, ub, dim=0).item()
+            assert cos > 0.3, (k, cos)
