@@ -53,6 +53,7 @@ CFG = dict(levels=[4, 4], hidden=384, heads=6, ffn=1024, layers=[2, 2], vocab=32
            inner_steps=20, outer_lr=0.7, outer_momentum=0.9, docs=20000, min_len=128, max_len=2048,
            zipf=1.1)
 BASELINE_VALUE = None  # the reference publishes no throughput number
+PEER_GBPS = 770.0      # measured peer-copy bandwidth per direction per GPU on this hardware (GB/s)
 
 
 def _rank_env():
@@ -265,6 +266,7 @@ def run(args) -> dict:
     device_ms = None
     launches = None
     outer_ms = None
+    phases = None
     if args.impl != "reference":
         ex = engine._fused
         st = torch.cuda.current_stream(dev)
@@ -285,6 +287,16 @@ def run(args) -> dict:
         ev1.record(st)
         barrier()
         outer_ms = ev0.elapsed_time(ev1) / args.steps
+        if world > 1 and hasattr(backend, "phase_times"):
+            # the same outer steps once more with events between the phases, and the bytes
+            # the APPLY phase moves over NVLink: achieved fraction of its roofline
+            backend.timing = True
+            barrier()
+            for _ in range(args.steps):
+                ex.device_outer()
+            barrier()
+            backend.timing = False
+            phases = backend.phase_times()
 
     # -- end to end through the public API ------------------------------------------------
     st = torch.cuda.current_stream(dev)
@@ -313,6 +325,18 @@ def run(args) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    outer_fields = {}
+    if phases is not None:
+        ph = {k: max_over_ranks(v) for k, v in phases.items()}
+        b_in = max_over_ranks(float(backend.nvlink_bytes["in"]))
+        b_out = max_over_ranks(float(backend.nvlink_bytes["out"]))
+        roof_ms = max(b_in, b_out) / PEER_GBPS / 1e6
+        outer_fields = {
+            "outer_phases_ms": {k: round(v, 4) for k, v in ph.items()},
+            "outer_apply_nvlink_MB_per_gpu": {"in": round(b_in / 1e6, 2), "out": round(b_out / 1e6, 2)},
+            "outer_apply_roofline_frac": round(roof_ms / ph["apply"], 3) if ph["apply"] > 0 else None,
+            "outer_apply_roofline_basis": f"max(in, out) bytes / {PEER_GBPS:.0f} GB/s measured peer copy per direction",
+        }
     device_ms = max_over_ranks(device_ms)
     outer_ms = max_over_ranks(outer_ms) if outer_ms is not None else None
     wall_ms = max_over_ranks(wall_ms)
@@ -347,6 +371,7 @@ def run(args) -> dict:
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(wall_ms / args.steps, 3)},
         "gpu_launches": launches if launches is not None else 0,
         "outer_sync_ms": None if outer_ms is None else round(outer_ms, 3),
+        **outer_fields,
         "outer_sync_scope": ("device time of the fused outer step (reduce over sharers + Nesterov + "
                              "write-back), max over ranks" if args.impl != "reference" else
                              "device time of the per-key global_reduce calls + outer optimizer step of "

@@ -11,6 +11,12 @@
 // from a device array so a whole round of steps can live in one CUDA graph. Writes the
 // fp32 master weight and its bf16 working copy for the GEMMs in the same pass.
 //
+// Skipped rows: both kernels can take the touched-row flags of one row-major region of
+// every path (the embedding, whose backward writes only the rows of the batch's tokens):
+// an element of an unflagged row counts as gradient 0, so the region needs no zeroing
+// between steps. The gradient and the flag are loaded side by side and selected (a load
+// that waited for the flag would double the latency chain of these memory-bound passes).
+//
 // adam8bit: blockwise 8-bit AdamW (blocks of 256): one warp per block dequantises m
 // (int8, absmax / 127) and v (uint8 in the log domain: exp(q * scale + lo), floor
 // 1e-20), updates in fp32 registers, requantises (round half to even) and updates the
@@ -23,10 +29,33 @@
 
 namespace odp {
 
+// rows != nullptr: elements [r0, r0 + V * H) of each path are V rows of H; row v of path
+// grp counts only when rows[grp * V + v] != 0.
+struct RowSkip {
+  const uint8_t* rows;
+  long long r0;
+  int H, V;
+};
+
+// True when the 4-element group at element i (i % 4 == 0, H % 4 == 0) lies in an unflagged row.
+ODP_DEVICE bool row_skipped(const RowSkip& rs, int grp, long long i) {
+  if (!rs.rows) return false;
+  const long long d = i - rs.r0;
+  if (d < 0 || d >= (long long)rs.V * rs.H) return false;
+  // row = d / H without an integer division (this runs per 4 elements of a memory-bound
+  // pass): d < 2^24 in practice is exact in fp32, and the estimate is fixed up by one step
+  int r = __float2int_rz(__int2float_rn((int)d) * __frcp_rn((float)rs.H));
+  const int di = (int)d;
+  if (r * rs.H > di) --r;
+  else if ((r + 1) * rs.H <= di) ++r;
+  return rs.rows[(long long)grp * rs.V + r] == 0;
+}
+
 constexpr int kSqBlock = 256;
 constexpr int kSqElemsPerBlock = 1 << 16;
 
-__global__ void sumsq_kernel(const float* __restrict__ g, long long P, long long sg, int nblk, float* __restrict__ part) {
+__global__ void sumsq_kernel(const float* __restrict__ g, long long P, long long sg, int nblk, float* __restrict__ part,
+                             RowSkip skip) {
   const int grp = blockIdx.y, b = blockIdx.x;
   const float* base = g + grp * sg;
   const long long e0 = (long long)b * kSqElemsPerBlock;
@@ -35,6 +64,7 @@ __global__ void sumsq_kernel(const float* __restrict__ g, long long P, long long
   for (long long i = e0 + threadIdx.x * 4; i < e1; i += kSqBlock * 4) {
     if (i + 4 <= e1) {
       float4 v = *reinterpret_cast<const float4*>(base + i);
+      if (row_skipped(skip, grp, i)) v = make_float4(0.f, 0.f, 0.f, 0.f);
       s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     } else {
       for (long long j = i; j < e1; ++j) s += base[j] * base[j];
@@ -74,7 +104,7 @@ __global__ void clip_coef_kernel(const float* __restrict__ part, int nblk, float
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ p16, long long P, long long sp,
                              long long s16, const float* __restrict__ coef, const float* __restrict__ sched, float b1,
-                             float b2, float eps, float wd) {
+                             float b2, float eps, float wd, RowSkip skip) {
   const int grp = blockIdx.y;
   const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (i >= P) return;
@@ -88,7 +118,8 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   float pv[4], gv[4], mv[4], vv[4];
   if (n == 4) {
     *reinterpret_cast<float4*>(pv) = *reinterpret_cast<const float4*>(p + o);
-    *reinterpret_cast<float4*>(gv) = *reinterpret_cast<const float4*>(g + o);
+    const float4 gl = *reinterpret_cast<const float4*>(g + o);
+    *reinterpret_cast<float4*>(gv) = row_skipped(skip, grp, i) ? make_float4(0.f, 0.f, 0.f, 0.f) : gl;
     *reinterpret_cast<float4*>(mv) = *reinterpret_cast<const float4*>(m + o);
     *reinterpret_cast<float4*>(vv) = *reinterpret_cast<const float4*>(v + o);
   } else {
@@ -197,14 +228,24 @@ __global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__
 
 }  // namespace odp
 
+static odp::RowSkip row_skip(const c10::optional<torch::Tensor>& rows, int64_t r0, int64_t H, int64_t V) {
+  odp::RowSkip s{nullptr, 0, 1, 0};
+  if (rows.has_value()) {
+    TORCH_CHECK(rows->scalar_type() == at::kByte && H % 4 == 0 && r0 % 4 == 0, "row flags: uint8, H and r0 % 4 == 0");
+    s = odp::RowSkip{rows->data_ptr<uint8_t>(), r0, (int)H, (int)V};
+  }
+  return s;
+}
+
 void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, double max_norm, torch::Tensor work,
-                    torch::Tensor coef, c10::optional<torch::Tensor> norm_out) {
+                    torch::Tensor coef, c10::optional<torch::Tensor> norm_out, c10::optional<torch::Tensor> rows,
+                    int64_t r0, int64_t H, int64_t V) {
   c10::cuda::CUDAGuard guard(grads.device());
   auto st = at::cuda::getCurrentCUDAStream();
   const int nblk = (int)((P + odp::kSqElemsPerBlock - 1) / odp::kSqElemsPerBlock);
   TORCH_CHECK(work.numel() >= G * nblk, "grad_clip_coef: work buffer too small");
   odp::sumsq_kernel<<<dim3(nblk, (unsigned)G), odp::kSqBlock, 0, st>>>(grads.data_ptr<float>(), P, sg, nblk,
-                                                                      work.data_ptr<float>());
+                                                                      work.data_ptr<float>(), row_skip(rows, r0, H, V));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::clip_coef_kernel<<<(unsigned)G, 256, 0, st>>>(work.data_ptr<float>(), nblk, (float)max_norm,
                                                       coef.data_ptr<float>(),
@@ -214,7 +255,8 @@ void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, doubl
 
 void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor p16, int64_t P,
                 int64_t sp, int64_t s16, int64_t G, c10::optional<torch::Tensor> coef, torch::Tensor sched, double b1,
-                double b2, double eps, double wd) {
+                double b2, double eps, double wd, c10::optional<torch::Tensor> rows, int64_t r0, int64_t H,
+                int64_t V) {
   c10::cuda::CUDAGuard guard(p.device());
   TORCH_CHECK(P % 4 == 0 || G == 1, "adamw_step: per-group length must be a multiple of 4");
   const long long threads = (P + 3) / 4;
@@ -223,7 +265,7 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
       p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), P, sp, s16,
       coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
-      (float)eps, (float)wd);
+      (float)eps, (float)wd, row_skip(rows, r0, H, V));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -65,6 +65,28 @@ struct Args {
   int* err;
 };
 
+// bf16 round-to-nearest-even on the integer pipe: add 0x7FFF plus the lowest kept bit and
+// keep the high half. Identical to cvt.rn.bf16 for every finite value and infinity (a NaN
+// with a payload only in the low 16 bits would become infinity; none arise here). This
+// kernel packs about as many values as it multiplies, and the conversion unit, not the
+// tensor core or HBM, bounded it; this form runs on the far wider integer ALUs. It hides
+// the common pack_bf16 inside this namespace.
+ODP_DEVICE uint32_t bf16_rne_bits(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return u + 0x7FFFu + ((u >> 16) & 1u);
+}
+ODP_DEVICE uint32_t pack_bf16(float lo, float hi) {
+  return __byte_perm(bf16_rne_bits(lo), bf16_rne_bits(hi), 0x7632);
+}
+
+// The hardware base-2 exponential (ex2.approx, flush-to-zero): the softmax probabilities
+// are rounded to bf16 right after, far coarser than its error.
+ODP_DEVICE float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 ODP_DEVICE uint32_t sw_off(int row, int col) {
   return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2);
 }
@@ -246,30 +268,43 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
     umma_commit(&bar);
   }
   __syncwarp();
-  bool ok = mbar_wait(&bar, 0, a.err, ERR_TIMEOUT_ACCUM);
+  // one thread waits for the MMAs (bounded); the rest sleep in the block barrier instead of
+  // polling the mbarrier alongside the other CTAs of the SM
+  bool ok = true;
+  if (threadIdx.x == 0) ok = mbar_wait(&bar, 0, a.err, ERR_TIMEOUT_ACCUM);
+  ok = __syncthreads_and(ok);
   tc_fence_after();
 
   const float sl2 = a.scale * kLog2e;
   const int nvalid = row < a.S ? row + 1 : 0;  // causal: keys [0, row]; padding rows see none
+  // causal: chunks at or past nvalid are all masked; their TMEM loads still run (the
+  // load is warp-collective) but they cost no exponentials
   float mx = -INFINITY;
 #pragma unroll 1
   for (int c = 0; c < T / 16; ++c) {
     float v[16];
     tmem_ld16(trow + c * 16, v);
+    if (c * 16 < nvalid) {
 #pragma unroll
-    for (int e = 0; e < 16; ++e)
-      if (c * 16 + e < nvalid) mx = fmaxf(mx, v[e] * sl2);
+      for (int e = 0; e < 16; ++e)
+        if (c * 16 + e < nvalid) mx = fmaxf(mx, v[e] * sl2);
+    }
   }
   float l = 0.f;
 #pragma unroll 1
   for (int c = 0; c < T / 16; ++c) {
     float v[16];
     tmem_ld16(trow + c * 16, v);
+    if (c * 16 < nvalid) {
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float p = (c * 16 + e < nvalid) ? exp2f(v[e] * sl2 - mx) : 0.f;
-      v[e] = p;
-      l += p;
+      for (int e = 0; e < 16; ++e) {
+        const float p = (c * 16 + e < nvalid) ? ex2_fast(v[e] * sl2 - mx) : 0.f;
+        v[e] = p;
+        l += p;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = 0.f;
     }
     put16(sP, row, c * 16, v);
   }
@@ -285,7 +320,8 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
     umma_commit(&bar);
   }
   __syncwarp();
-  if (ok) ok = mbar_wait(&bar, 1, a.err, ERR_TIMEOUT_ACCUM);
+  if (ok && threadIdx.x == 0) ok = mbar_wait(&bar, 1, a.err, ERR_TIMEOUT_ACCUM);
+  ok = __syncthreads_and(ok);
   tc_fence_after();
   float r[64];
   tmem_row64(trow, r);
@@ -397,7 +433,7 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
       umma_commit(&bar);
     }
     __syncwarp();
-    ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
+    if (threadIdx.x == 0) ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
     phase ^= 1;
     ok = __syncthreads_and(ok);
     tc_fence_after();
@@ -411,11 +447,16 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
         float s[16], dp[16];
         tmem_ld16(tS + lane_off + c0, s);
         tmem_ld16(tdP + lane_off + c0, dp);
+        if (c0 < nvalid) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p = (c0 + e < nvalid) ? exp2f(s[e] * sl2 - l2) : 0.f;
-          s[e] = p;
-          dp[e] = p * (dp[e] - delta);
+          for (int e = 0; e < 16; ++e) {
+            const float p = (c0 + e < nvalid) ? ex2_fast(s[e] * sl2 - l2) : 0.f;
+            s[e] = p;
+            dp[e] = p * (dp[e] - delta);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) s[e] = dp[e] = 0.f;
         }
         put16(sP, row, c0, s);
         if constexpr (LEAN) {
@@ -442,7 +483,7 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
         umma_commit(&bar);
       }
       __syncwarp();
-      if (ok) ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
+      if (ok && threadIdx.x == 0) ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
       phase ^= 1;
       ok = __syncthreads_and(ok);
       tc_fence_after();
@@ -470,7 +511,7 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
       umma_commit(&bar);
     }
     __syncwarp();
-    if (ok) ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
+    if (ok && threadIdx.x == 0) ok = mbar_wait(&bar, phase, a.err, ERR_TIMEOUT_ACCUM);
     phase ^= 1;
     ok = __syncthreads_and(ok);
     tc_fence_after();

@@ -17,7 +17,7 @@ void embedding_fwd(torch::Tensor ids, torch::Tensor E, int64_t se, torch::Tensor
 void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
                    int64_t H, int64_t G, int64_t V);
 void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
-                          int64_t H, int64_t G, int64_t V, torch::Tensor keys);
+                          int64_t H, int64_t G, int64_t V, torch::Tensor keys, c10::optional<torch::Tensor> rows);
 void attention_fwd(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                    torch::Tensor sinT, torch::Tensor o, torch::Tensor lse);
 void attention_bwd(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
@@ -48,10 +48,12 @@ void ce_backward(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor ls
                  torch::Tensor inv_count, int64_t M, int64_t V, int64_t G);
 torch::Tensor cross_entropy_rows(torch::Tensor logits, torch::Tensor target);
 void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, double max_norm, torch::Tensor work,
-                    torch::Tensor coef, c10::optional<torch::Tensor> norm_out);
+                    torch::Tensor coef, c10::optional<torch::Tensor> norm_out, c10::optional<torch::Tensor> rows,
+                    int64_t r0, int64_t H, int64_t V);
 void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor p16, int64_t P,
                 int64_t sp, int64_t s16, int64_t G, c10::optional<torch::Tensor> coef, torch::Tensor sched, double b1,
-                double b2, double eps, double wd);
+                double b2, double eps, double wd, c10::optional<torch::Tensor> rows, int64_t r0, int64_t H,
+                int64_t V);
 void adam8bit_step(torch::Tensor p, torch::Tensor g, torch::Tensor mq, torch::Tensor mabs, torch::Tensor vq,
                    torch::Tensor vlo, torch::Tensor vsc, c10::optional<torch::Tensor> coef, torch::Tensor sched,
                    double b1, double b2, double eps, double wd, bool first, c10::optional<torch::Tensor> p16,

@@ -328,13 +328,15 @@ __global__ void __launch_bounds__(1024) embed_sort_kernel(const int* __restrict_
 
 template <int NT>
 __global__ void embed_runs_kernel(const unsigned* __restrict__ keys, const float* __restrict__ dx, long long sdx,
-                                  float* __restrict__ dE, long long se, int M, int H, int G, int V) {
+                                  float* __restrict__ dE, long long se, int M, int H, int G, int V,
+                                  uint8_t* __restrict__ rows) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= G * M) return;
   const int g = warp / M, i = warp % M;
   const unsigned* gk = keys + (long long)g * M;
   const unsigned id = gk[i] >> 12;
   if (id >= (unsigned)V || (i > 0 && (gk[i - 1] >> 12) == id)) return;
+  if (rows && lane == 0) rows[(long long)g * V + id] = 1;  // this row of dE is written below
   // end of this token's run: first sorted position whose id differs (32 keys per probe)
   int end = i + 1;
   while (true) {
@@ -466,9 +468,13 @@ void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tens
 
 // embedding_bwd through a per-path sort (same result, O(M)); keys: [G][M] int32 scratch.
 // Falls back to embedding_bwd for M > 4096 rows per path or V >= 2^20.
+// rows (optional, uint8 [G][V]): cleared, then set to 1 for every vocabulary row whose
+// gradient this call writes; the other rows of dE are left as they were (not zeroed), and
+// consumers given `rows` read them as zero. Needs the sorted path (M <= 4096, V < 2^20).
 void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
-                          int64_t H, int64_t G, int64_t V, torch::Tensor keys) {
+                          int64_t H, int64_t G, int64_t V, torch::Tensor keys, c10::optional<torch::Tensor> rows) {
   if (M > odp::kSortMax || V >= (1 << 20)) {
+    TORCH_CHECK(!rows.has_value(), "embedding_bwd_sorted: touched-row flags need M <= 4096 and V < 2^20");
     embedding_bwd(ids, dx, sdx, dE, se, M, H, G, V);
     return;
   }
@@ -477,13 +483,19 @@ void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torc
   c10::cuda::CUDAGuard guard(dE.device());
   auto st = at::cuda::getCurrentCUDAStream();
   unsigned* kp = reinterpret_cast<unsigned*>(keys.data_ptr<int>());
+  uint8_t* rp = nullptr;
+  if (rows.has_value()) {
+    TORCH_CHECK(rows->numel() >= G * V && rows->scalar_type() == at::kByte, "embedding_bwd_sorted: rows is uint8 [G][V]");
+    rp = rows->data_ptr<uint8_t>();
+    C10_CUDA_CHECK(cudaMemsetAsync(rp, 0, (size_t)(G * V), st));
+  }
   odp::embed_sort_kernel<<<(int)G, 1024, 0, st>>>(ids.data_ptr<int>(), (int)M, kp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (H <= 512)
     odp::embed_runs_kernel<16><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V);
+        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp);
   else
     odp::embed_runs_kernel<64><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V);
+        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -28,12 +28,12 @@ def clip_coef(grads: torch.Tensor, P: int, stride: int, G: int, max_norm: float 
         work = torch.empty(G * nblk, device=grads.device, dtype=torch.float32)
     if coef is None:
         coef = torch.empty(G, device=grads.device, dtype=torch.float32)
-    ext().grad_clip_coef(grads, P, stride, G, float(max_norm or 0.0), work, coef, norm_out)
+    ext().grad_clip_coef(grads, P, stride, G, float(max_norm or 0.0), work, coef, norm_out, None, 0, 4, 0)
     return coef
 
 
 def adamw(p, g, m, v, p16, P, stride, stride16, G, coef, sched, b1, b2, eps, wd):
-    ext().adamw_step(p, g, m, v, p16, P, stride, stride16, G, coef, sched, b1, b2, eps, wd)
+    ext().adamw_step(p, g, m, v, p16, P, stride, stride16, G, coef, sched, b1, b2, eps, wd, None, 0, 4, 0)
 
 
 def adam8bit_step(p: torch.Tensor, grad: torch.Tensor, st: dict, *, lr, b1, b2, eps, wd, bc1, bc2_sqrt,

@@ -88,6 +88,10 @@ class NVLinkBackend(TorchDistBackend):
         self._tables = None
         self._epoch = 0
         self._sq_keys: list[tuple[str, int, int]] = []
+        # timing=True brackets the outer step's launches with CUDA events (phase_times())
+        self.timing = False
+        self._tev: list = []
+        self.nvlink_bytes = {"in": 0, "out": 0}
 
     # ------------------------------------------------------------------ arenas
     def bank_arena(self, sizes: dict[str, int], device) -> tuple[dict, dict]:
@@ -198,6 +202,7 @@ class NVLinkBackend(TorchDistBackend):
             cplan = None
         keys, cps, chunk0, c0 = [], [], 0, 0
         regs, g0 = [], 0
+        b_in = b_out = 0
         self._sq_keys = []
         for s in plan.segments:
             if s.mode != MODE_OUTER:
@@ -223,6 +228,17 @@ class NVLinkBackend(TorchDistBackend):
                     r["off"], r["n"], r["group0"] = self._offs[s.key], s.glob.numel(), g0
                 regs.append(r)
                 g0 += ng
+            # bytes of this rank's APPLY slice that cross NVLink: the other sharers' partials
+            # come in (fp32, int4 codes + scales, or top-k pairs), the new global goes out
+            L = max(s1 - s0, 0)
+            if rec["quant"][0] == 1:
+                bpe = 0.5 + 4.0 / QGROUP
+            elif rec["quant"][0] == 2:
+                bpe = 6.0 * self.kcap / SPBLOCK
+            else:
+                bpe = 4.0
+            b_in += int(L * (len(sh) - 1) * bpe)
+            b_out += L * (len(sh) - 1) * 4
             if nch:
                 keys.append(rec)
                 self._sq_keys.append((s.key, chunk0, nch))
@@ -243,6 +259,7 @@ class NVLinkBackend(TorchDistBackend):
                             sq=torch.zeros(max(chunk0, 1), device=self.dev), regs=to_dev(reg_arr),
                             nregs=len(regs), groups=g0)
         self._all_keys = [k for k in self.topology.module_keys() if not is_private_key(k)]
+        self.nvlink_bytes = {"in": b_in, "out": b_out}
 
     # ------------------------------------------------------------------ the round
     def fused_outer_step(self, ex, plan, first: bool) -> None:
@@ -251,9 +268,14 @@ class NVLinkBackend(TorchDistBackend):
         t = self._tables
         dl = ex.e.diloco
         err = err_word(self.dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if self.timing else None
+        if ev:
+            ev[0].record()
         t["acc"].run(0.0, 0.0, False, False)
         if t["cplan"] is not None:
             t["cplan"].run(0.0, 0.0, False, False)
+        if ev:
+            ev[1].record()
         qd = qs = None
         if self.compress == "int4":
             ext().outer_nvlink_quant(t["regs"], t["nregs"], t["groups"], self.DELTA, self.RES,
@@ -263,12 +285,32 @@ class NVLinkBackend(TorchDistBackend):
                                     self.RES, self.QD.view(torch.int16), self.QS)
         if self.compress:
             qd, qs = self._qdptrs, self._qsptrs
+        if ev:
+            ev[2].record()
         self._epoch += 1
         ext().outer_nvlink_apply(t["keys"], t["nkeys"], t["chunks"], self._dptrs, self._gptrs, self._pptrs,
                                  self.MOM, self.rank, self.world_size, self._epoch, dl.outer_lr,
                                  dl.outer_momentum, dl.outer_nesterov, first, t["sq"], err, qd, qs, self.kcap)
+        if ev:
+            ev[3].record()
         ext().outer_nvlink_bcast(t["cps"], t["ncp"], t["cchunks"], self._pptrs, self.rank, self.world_size,
                                  self._epoch, err)
+        if ev:
+            ev[4].record()
+            self._tev.append(ev)
+
+    def phase_times(self) -> dict[str, float]:
+        """Mean device time (ms) of the outer step's phases over the timed calls since the
+        last read: acc (local partials), quant (compression), apply (cross-GPU barrier +
+        peer-memory reduce, Nesterov, write-back), bcast (barrier + local copies)."""
+        torch.cuda.synchronize(self.dev)
+        n = len(self._tev)
+        out = {k: 0.0 for k in ("acc", "quant", "apply", "bcast")}
+        for ev in self._tev:
+            for i, k in enumerate(out):
+                out[k] += ev[i].elapsed_time(ev[i + 1]) / n
+        self._tev = []
+        return out
 
     def delta_norms(self) -> dict[str, float]:
         """Per shared key ||delta||, summed over the key's slices on every rank."""

@@ -296,6 +296,11 @@ class FusedExecutor:
         self.LOSSES = z(steps, G)
         self.INVC = z(steps, G)  # 1 / valid labels of each (step, path) batch, for split batches
         self.EMBKEYS = z(G, M, dt=torch.int32)  # sorted (token, row) keys of the embedding backward
+        # touched-row flags of the embedding gradient: rows of tokens absent from a step are
+        # neither zeroed nor read (the norm and AdamW kernels take them as gradient 0);
+        # plain AdamW on one GPU per path group with the sorted embedding backward
+        self.emb_rows = (z(G, V, dt=torch.uint8) if (M <= 4096 and V < (1 << 20) and V * H < (1 << 31) and self.dp == 1 and not self.opt8
+                                                     and os.environ.get("ODP_EMB_ROWS", "1") != "0") else None)
         self.ids_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
         self.labels_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
         self.sched_host = torch.zeros(steps, G, 4, dtype=torch.float32).pin_memory()
@@ -386,8 +391,10 @@ class FusedExecutor:
             X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[l], self.DXN, MH, self.DX, self.DX, MH,
                            self.DX16, gr[lo.ln1:], P, self.NORMWORK, M, H, G, 0.0)
         emb_n = bb.vocab_size * H
-        self.GRAD[:, lay.emb:lay.emb + emb_n].zero_()
-        X_.embedding_bwd_sorted(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V, self.EMBKEYS)
+        rows = self.emb_rows
+        if rows is None:
+            self.GRAD[:, lay.emb:lay.emb + emb_n].zero_()
+        X_.embedding_bwd_sorted(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V, self.EMBKEYS, rows)
         # ---------------- optimizer
         clip = self.e.diloco.inner_grad_clip
         clipv = float(clip) if clip is not None else 0.0
@@ -405,14 +412,14 @@ class FusedExecutor:
                 X_.dp_adamw(self.dp_tab, self.dp_counter, self.dp_index, self.dp, G, P, P, self.dp_s0, self.dp_s1,
                             self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, self.err)
             return
-        X_.grad_clip_coef(self.GRAD, P, P, G, clipv, self.CLIPWORK, self.COEF, self.GNORM)
+        X_.grad_clip_coef(self.GRAD, P, P, G, clipv, self.CLIPWORK, self.COEF, self.GNORM, rows, lay.emb, H, V)
         if self.opt8:
             X_.adam8bit_step(self.W32.view(-1), self.GRAD.view(-1), self.MQ, self.MABS, self.VQ, self.VLO,
                              self.VSC, self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay,
                              False, self.W16.view(-1), P // ALIGN)
         else:
             X_.adamw_step(self.W32, self.GRAD, self.MOM1, self.MOM2, self.W16, P, P, P, G, self.COEF,
-                          self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay)
+                          self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, rows, lay.emb, H, V)
 
     # ------------------------------------------------------------------ round inputs
     def _prepare(self, corpus, batch_size: int, round_idx: int):

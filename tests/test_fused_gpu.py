@@ -129,3 +129,21 @@ def test_module_forward_on_cuda_kernels_matches_cpu():
     gc = pm_c.head.lm_head.weight.grad
     gg = pm_g.head.lm_head.weight.grad.cpu()
     assert (gc - gg).abs().max() < 5e-2 * gc.abs().max()
+
+
+def test_embedding_row_flags_equal_zeroed_gradient_bitwise(monkeypatch):
+    """Skipping the embedding rows a step did not touch (flags from the sorted embedding
+    backward, read as gradient 0 by the norm and AdamW kernels) gives bit-identical
+    training to zeroing the whole embedding gradient every step."""
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    monkeypatch.setenv("ODP_EMB_ROWS", "1")
+    a = _engine(cfg, "cuda")
+    ha = a.fit(corpus, 3, 4, log_every=0)
+    assert a._fused.emb_rows is not None
+    monkeypatch.setenv("ODP_EMB_ROWS", "0")
+    b = _engine(cfg, "cuda")
+    hb = b.fit(corpus, 3, 4, log_every=0)
+    assert b._fused.emb_rows is None
+    assert [m.per_path_loss for m in ha] == [m.per_path_loss for m in hb]
+    assert _bank_maxdiff(a, b) == 0.0
