@@ -439,36 +439,41 @@ class FusedExecutor:
             self._alloc(B, S, steps)
         ids = self.ids_host.view(steps, self.G, B, S)
         lab = self.labels_host.view(steps, self.G, B, S)
-        ids.zero_()
-        lab.fill_(-100)
         from .loop import batch_indices
 
         total = e.total_rounds * steps if e.total_rounds else None
         dl = e.diloco
         b1, b2 = dl.inner_betas
         sched = self.sched_host
-        sched.zero_()
         invc = self.invc_host
-        invc.fill_(1.0)
         for g, (sh, act) in enumerate(zip(shards, active)):
+            sched[:, g].zero_()
+            invc[:, g].fill_(1.0)
             if not act:
+                ids[:, g].zero_()
+                lab[:, g].fill_(-100)
                 continue
-            idx = batch_indices(sh.size(0), batch_size, steps, e._gen)
-            for i, rows in enumerate(idx):
-                # the whole batch is sampled (same generator calls on every member), this
-                # GPU trains rows [j0, j0 + B); the loss is normalised by the whole batch
-                invc[i, g] = 1.0 / max(1, rows.numel() * (S - 1))
-                seqs = sh[rows[j0:j0 + B]].to(torch.int32)
-                bs = seqs.size(0)
-                ids[i, g, :bs] = seqs
-                lab[i, g, :bs, :-1] = seqs[:, 1:]
+            # every step of a round samples the same number of rows: gather the round at once
+            idx = torch.stack(batch_indices(sh.size(0), batch_size, steps, e._gen))  # [steps, rows]
+            # the whole batch is sampled (same generator calls on every member), this GPU
+            # trains rows [j0, j0 + B); the loss is normalised by the whole batch
+            invc[:, g] = 1.0 / max(1, idx.size(1) * (S - 1))
+            seqs = sh[idx[:, j0:j0 + B]].to(torch.int32)  # [steps, b, S]
+            b = seqs.size(1)
+            ids[:, g, :b] = seqs
+            lab[:, g, :b, :-1] = seqs[..., 1:]
+            lab[:, g, :b, -1] = -100
+            if b < B:
+                ids[:, g, b:] = 0
+                lab[:, g, b:] = -100
+            rows = []
             for i in range(steps):
                 t = self.steps_taken[g] + i + 1
                 lr = inner_lr_at(round_idx * steps + i, total, dl)
                 # active flag 2.0 marks a path's very first optimizer step (8-bit Adam
                 # then treats the second moment as zero, like the reference)
-                sched[i, g] = torch.tensor([lr, lr / (1 - b1 ** t), math.sqrt(1 - b2 ** t),
-                                            2.0 if t == 1 else 1.0])
+                rows.append([lr, lr / (1 - b1 ** t), math.sqrt(1 - b2 ** t), 2.0 if t == 1 else 1.0])
+            sched[:, g] = torch.tensor(rows, dtype=sched.dtype)
         return active
 
     def _upload(self) -> None:
