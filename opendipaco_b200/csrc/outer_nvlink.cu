@@ -337,45 +337,77 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
         __syncthreads();  // indices are unique within a sharer; sharers add in rank order
       }
     }
-    for (long long e = e0 + threadIdx.x * 4; e < e1; e += blockDim.x * 4) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k.quant == 2) acc = *reinterpret_cast<const float4*>(dense + (e - e0));
-      for (int j = 0; j < (k.quant == 2 ? 0 : k.nsh); ++j) {
-        float4 d;
-        if (k.quant) {  // int4 codes + group scale of sharer j, dequantised in registers
-          const long long ge = k.off + e;
-          const uint16_t c = *reinterpret_cast<const volatile uint16_t*>(
-              reinterpret_cast<const uint8_t*>(qd_ptrs[k.sh[j]]) + ge / 2);
-          const float sc = *reinterpret_cast<const volatile float*>(
-              reinterpret_cast<const float*>(qs_ptrs[k.sh[j]]) + ge / kQGroup);
-          d = make_float4(__fmul_rn((float)((int)(c & 15u) - 8), sc), __fmul_rn((float)((int)((c >> 4) & 15u) - 8), sc),
-                          __fmul_rn((float)((int)((c >> 8) & 15u) - 8), sc),
-                          __fmul_rn((float)((int)((c >> 12) & 15u) - 8), sc));
-        } else {
-          d = ld_cg4(reinterpret_cast<const float*>(delta_ptrs[k.sh[j]]) + k.off + e);
-        }
-        acc.x = __fadd_rn(acc.x, d.x);
-        acc.y = __fadd_rn(acc.y, d.y);
-        acc.z = __fadd_rn(acc.z, d.z);
-        acc.w = __fadd_rn(acc.w, d.w);
-      }
-      const float4 gv = *reinterpret_cast<const float4*>(gl + e);
-      float4 mb = *reinterpret_cast<const float4*>(mom + k.off + e);
-      float a4[4] = {acc.x, acc.y, acc.z, acc.w}, g4[4] = {gv.x, gv.y, gv.z, gv.w};
-      float b4[4] = {mb.x, mb.y, mb.z, mb.w}, n4[4];
+    // two float4 positions per thread and every sharer's load issued before any is used:
+    // the peer loads cross NVLink, so the loads in flight, not the arithmetic, set the pace
+    const long long stride = (long long)blockDim.x * 4;
+    for (long long e = e0 + threadIdx.x * 4; e < e1; e += 2 * stride) {
+      const long long ev[2] = {e, e + stride};
+      const bool has[2] = {true, e + stride < e1};
+      float4 acc[2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float d = __fmul_rn(__fmul_rn(a4[i], k.inv_den), k.scale);
-        sq += d * d;
-        const float b = first ? d : __fadd_rn(__fmul_rn(b4[i], m), d);
-        b4[i] = b;
-        const float upd = nesterov ? __fadd_rn(d, __fmul_rn(m, b)) : b;
-        n4[i] = __fadd_rn(g4[i], __fmul_rn(-lr, upd));
+      for (int u = 0; u < 2; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k.quant == 2) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if (has[u]) acc[u] = *reinterpret_cast<const float4*>(dense + (ev[u] - e0));
+      } else {
+        float4 d[2][kMaxSharers];
+#pragma unroll
+        for (int j = 0; j < kMaxSharers; ++j) {
+          if (j >= k.nsh) break;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            if (!has[u]) continue;
+            if (k.quant) {  // int4 codes + group scale of sharer j, dequantised in registers
+              const long long ge = k.off + ev[u];
+              const uint16_t c = *reinterpret_cast<const volatile uint16_t*>(
+                  reinterpret_cast<const uint8_t*>(qd_ptrs[k.sh[j]]) + ge / 2);
+              const float sc = *reinterpret_cast<const volatile float*>(
+                  reinterpret_cast<const float*>(qs_ptrs[k.sh[j]]) + ge / kQGroup);
+              d[u][j] = make_float4(__fmul_rn((float)((int)(c & 15u) - 8), sc),
+                                    __fmul_rn((float)((int)((c >> 4) & 15u) - 8), sc),
+                                    __fmul_rn((float)((int)((c >> 8) & 15u) - 8), sc),
+                                    __fmul_rn((float)((int)((c >> 12) & 15u) - 8), sc));
+            } else {
+              d[u][j] = ld_cg4(reinterpret_cast<const float*>(delta_ptrs[k.sh[j]]) + k.off + ev[u]);
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kMaxSharers; ++j) {  // rank order: deterministic sums
+          if (j >= k.nsh) break;
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            if (!has[u]) continue;
+            acc[u].x = __fadd_rn(acc[u].x, d[u][j].x);
+            acc[u].y = __fadd_rn(acc[u].y, d[u][j].y);
+            acc[u].z = __fadd_rn(acc[u].z, d[u][j].z);
+            acc[u].w = __fadd_rn(acc[u].w, d[u][j].w);
+          }
+        }
       }
-      *reinterpret_cast<float4*>(mom + k.off + e) = make_float4(b4[0], b4[1], b4[2], b4[3]);
-      const float4 nv = make_float4(n4[0], n4[1], n4[2], n4[3]);
-      for (int j = 0; j < k.nsh; ++j)
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(glob_ptrs[k.sh[j]]) + k.off + e) = nv;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (!has[u]) continue;
+        const long long eu = ev[u];
+        const float4 gv = *reinterpret_cast<const float4*>(gl + eu);
+        float4 mb = *reinterpret_cast<const float4*>(mom + k.off + eu);
+        float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w}, g4[4] = {gv.x, gv.y, gv.z, gv.w};
+        float b4[4] = {mb.x, mb.y, mb.z, mb.w}, n4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float dd = __fmul_rn(__fmul_rn(a4[i], k.inv_den), k.scale);
+          sq += dd * dd;
+          const float b = first ? dd : __fadd_rn(__fmul_rn(b4[i], m), dd);
+          b4[i] = b;
+          const float upd = nesterov ? __fadd_rn(dd, __fmul_rn(m, b)) : b;
+          n4[i] = __fadd_rn(g4[i], __fmul_rn(-lr, upd));
+        }
+        *reinterpret_cast<float4*>(mom + k.off + eu) = make_float4(b4[0], b4[1], b4[2], b4[3]);
+        const float4 nv = make_float4(n4[0], n4[1], n4[2], n4[3]);
+        for (int j = 0; j < k.nsh; ++j)
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(glob_ptrs[k.sh[j]]) + k.off + eu) = nv;
+      }
     }
     if (sq_part) {
       sq = warp_sum(sq);
