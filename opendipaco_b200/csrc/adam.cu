@@ -100,6 +100,37 @@ __global__ void clip_coef_kernel(const float* __restrict__ part, int nblk, float
   }
 }
 
+// Clip coefficient from sums of squares made by the gradients' producers: per path g,
+// parts[g][0, nslot) (fp32 GEMM epilogues, one per 32 x 32 output box), esq[g][0, M)
+// (embedding backward, one per written row) and the norm-weight gradients read directly
+// (n_norm regions of H floats at offsets norm_offs within the path's gradient). One
+// 256-thread block per path; fixed summation order.
+__global__ void clip_coef_parts_kernel(const float* __restrict__ parts, long long nslot, const float* __restrict__ esq,
+                                       int M, const float* __restrict__ grads, long long P,
+                                       const long long* __restrict__ norm_offs, int n_norm, int H, float max_norm,
+                                       float* __restrict__ coef, float* __restrict__ norm_out) {
+  const int g = blockIdx.x;
+  float s = 0.f;
+  for (long long i = threadIdx.x; i < nslot; i += blockDim.x) s += parts[g * nslot + i];
+  for (int i = threadIdx.x; i < M; i += blockDim.x) s += esq[(long long)g * M + i];
+  for (int r = 0; r < n_norm; ++r) {
+    const float* w = grads + g * P + norm_offs[r];
+    for (int i = threadIdx.x; i < H; i += blockDim.x) s = fmaf(w[i], w[i], s);
+  }
+  __shared__ float red[256];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float n = sqrtf(red[0]);
+    if (norm_out) norm_out[g] = n;
+    coef[g] = max_norm > 0.f ? fminf(1.f, max_norm / (n + 1e-6f)) : 1.f;
+  }
+}
+
 // sched: [G][4] = lr, step_size = lr / bc1, bc2_sqrt, active (0 -> leave this path untouched)
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ p16, long long P, long long sp,
@@ -250,6 +281,18 @@ void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, doubl
   odp::clip_coef_kernel<<<(unsigned)G, 256, 0, st>>>(work.data_ptr<float>(), nblk, (float)max_norm,
                                                       coef.data_ptr<float>(),
                                                       norm_out.has_value() ? norm_out->data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void grad_clip_coef_parts(torch::Tensor parts, int64_t nslot, torch::Tensor esq, int64_t M, torch::Tensor grads,
+                          int64_t P, torch::Tensor norm_offs, int64_t H, int64_t G, double max_norm, torch::Tensor coef,
+                          c10::optional<torch::Tensor> norm_out) {
+  c10::cuda::CUDAGuard guard(grads.device());
+  TORCH_CHECK(parts.numel() >= G * nslot && esq.numel() >= G * M, "grad_clip_coef_parts: partials too small");
+  odp::clip_coef_parts_kernel<<<(unsigned)G, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      parts.data_ptr<float>(), nslot, esq.data_ptr<float>(), (int)M, grads.data_ptr<float>(), P,
+      reinterpret_cast<const long long*>(norm_offs.data_ptr<int64_t>()), (int)norm_offs.numel(), (int)H,
+      (float)max_norm, coef.data_ptr<float>(), norm_out.has_value() ? norm_out->data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

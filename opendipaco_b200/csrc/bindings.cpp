@@ -5,7 +5,8 @@ void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tenso
                bool b_mn, torch::Tensor C, int64_t ldc, int64_t sc, int64_t M, int64_t N, int64_t K, int64_t G,
                int64_t epi, int64_t bn, c10::optional<torch::Tensor> R, int64_t ldr, int64_t sr,
                c10::optional<torch::Tensor> aux, int64_t ldx, int64_t sx, c10::optional<torch::Tensor> part,
-               double beta, int64_t f_half, torch::Tensor err, int64_t max_ctas);
+               double beta, int64_t f_half, torch::Tensor err, int64_t max_ctas,
+               c10::optional<torch::Tensor> sq_part, int64_t sq_ld);
 void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor y, int64_t sy,
                  torch::Tensor rstd, int64_t M, int64_t H, int64_t G, double eps);
 void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor rstd, torch::Tensor dy,
@@ -17,7 +18,11 @@ void embedding_fwd(torch::Tensor ids, torch::Tensor E, int64_t se, torch::Tensor
 void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
                    int64_t H, int64_t G, int64_t V);
 void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
-                          int64_t H, int64_t G, int64_t V, torch::Tensor keys, c10::optional<torch::Tensor> rows);
+                          int64_t H, int64_t G, int64_t V, torch::Tensor keys, c10::optional<torch::Tensor> rows,
+                          c10::optional<torch::Tensor> sq);
+void grad_clip_coef_parts(torch::Tensor parts, int64_t nslot, torch::Tensor esq, int64_t M, torch::Tensor grads,
+                          int64_t P, torch::Tensor norm_offs, int64_t H, int64_t G, double max_norm, torch::Tensor coef,
+                          c10::optional<torch::Tensor> norm_out);
 void attention_fwd(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                    torch::Tensor sinT, torch::Tensor o, torch::Tensor lse);
 void attention_bwd(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
@@ -84,6 +89,7 @@ std::vector<torch::Tensor> kmeans_assign(torch::Tensor x, torch::Tensor c, int64
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opendipaco_b200 sm_100a kernels";
   m.def("gemm_bf16", &gemm_bf16);
+  m.def("grad_clip_coef_parts", &grad_clip_coef_parts);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("embedding_fwd", &embedding_fwd);

@@ -48,6 +48,10 @@ struct GemmParams {
   void* aux;  // swiglu: pre-activation [M, 2F] bf16 ([g | u]); bwd: same layout as input
   long long ldx, sx;
   float* part;  // logits: [G][M][2 * tiles_n] float2 (one per tile column half)
+  // fp32 outputs (TMA-store epilogue): sum of squares of every 32 x 32 output box, at
+  // sqp[g * sq_ld + (row / 32) * ceil(N / 32) + col / 32] (each box written once)
+  float* sqp;
+  long long sq_ld;
   float beta;
   int f_half;  // swiglu: F (rows of the gate block; up block starts at row F)
   int tma_store;  // bf16 / logits with BN 128: stage each warp's 32 x 64 sub-tile in smem, TMA-store it
@@ -466,6 +470,14 @@ ODP_DEVICE bool epilogue_tma(const GemmParams& p, uint32_t tmem_acc, int q, int 
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = v[i] + p.beta * x[i];
         }
+      }
+      if (p.sqp) {
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) q = fmaf(v[i], v[i], q);
+        q = warp_sum(q);
+        if (lane == 0 && y < p.M && xs[0] < p.N)
+          p.sqp[(long long)g * p.sq_ld + (long long)(y / 32) * ((p.N + 31) / 32) + xs[0] / 32] = q;
       }
       stage_f32x32(buf, lane, v);
       epi_store(e, e.tmC, buf, 1, 4096, xs, y, g, lane);
@@ -1110,6 +1122,7 @@ static bool dispatch_pair(const Operand& A, const Operand& B, GemmParams& p, cud
     } else {
       tma_ok = out_maps<EPI>(p, mc, mx);
     }
+    TORCH_CHECK(tma_ok || !p.sqp, "gemm: box sums of squares need a TMA-storable fp32 output");
     p.tma_store = tma_ok ? 1 : 0;
 #define ODP_GO2(AM, BMN, BNV, ST)                                                                        \
   if constexpr (cfg2_ok<EPI, AM, BMN, BNV>()) {                                                          \
@@ -1151,6 +1164,7 @@ static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, 
   } else {
     tma_ok = out_maps<EPI>(p, mc, mx);
   }
+  TORCH_CHECK(tma_ok || !p.sqp, "gemm: box sums of squares need a TMA-storable fp32 output");
   p.tma_store = tma_ok ? 1 : 0;
 #define ODP_GO(AM, BMN, BNV, ST)                                                                       \
   if constexpr (cfg_ok<EPI, AM, BMN, BNV>()) {                                                         \
@@ -1186,7 +1200,8 @@ void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tenso
                bool b_mn, torch::Tensor C, int64_t ldc, int64_t sc, int64_t M, int64_t N, int64_t K, int64_t G,
                int64_t epi, int64_t bn, c10::optional<torch::Tensor> R, int64_t ldr, int64_t sr,
                c10::optional<torch::Tensor> aux, int64_t ldx, int64_t sx, c10::optional<torch::Tensor> part,
-               double beta, int64_t f_half, torch::Tensor err, int64_t max_ctas) {
+               double beta, int64_t f_half, torch::Tensor err, int64_t max_ctas,
+               c10::optional<torch::Tensor> sq_part, int64_t sq_ld) {
   using namespace odp;
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
@@ -1212,6 +1227,9 @@ void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tenso
   p.ldx = ldx;
   p.sx = sx;
   p.part = part.has_value() ? part->data_ptr<float>() : nullptr;
+  p.sqp = sq_part.has_value() ? sq_part->data_ptr<float>() : nullptr;
+  p.sq_ld = sq_ld;
+  TORCH_CHECK(!p.sqp || epi == EPI_F32, "gemm: box sums of squares are produced by the fp32 epilogue only");
   p.beta = (float)beta;
   p.err = err.data_ptr<int>();
   Operand a{A.data_ptr(), lda, sa, a_mn}, b{B.data_ptr(), ldb, sb, b_mn};

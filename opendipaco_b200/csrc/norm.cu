@@ -329,13 +329,16 @@ __global__ void __launch_bounds__(1024) embed_sort_kernel(const int* __restrict_
 template <int NT>
 __global__ void embed_runs_kernel(const unsigned* __restrict__ keys, const float* __restrict__ dx, long long sdx,
                                   float* __restrict__ dE, long long se, int M, int H, int G, int V,
-                                  uint8_t* __restrict__ rows) {
+                                  uint8_t* __restrict__ rows, float* __restrict__ sq) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= G * M) return;
   const int g = warp / M, i = warp % M;
   const unsigned* gk = keys + (long long)g * M;
   const unsigned id = gk[i] >> 12;
-  if (id >= (unsigned)V || (i > 0 && (gk[i - 1] >> 12) == id)) return;
+  if (id >= (unsigned)V || (i > 0 && (gk[i - 1] >> 12) == id)) {
+    if (sq && lane == 0) sq[(long long)g * M + i] = 0.f;  // not the start of a run
+    return;
+  }
   if (rows && lane == 0) rows[(long long)g * V + id] = 1;  // this row of dE is written below
   // end of this token's run: first sorted position whose id differs (32 keys per probe)
   int end = i + 1;
@@ -368,9 +371,17 @@ __global__ void embed_runs_kernel(const unsigned* __restrict__ keys, const float
       for (int t = 0; t < NT; ++t) acc[t] += v[b][t];
   }
   float* dst = dE + g * se + (long long)id * H;
+  float q = 0.f;
 #pragma unroll
   for (int t = 0; t < NT; ++t)
-    if (t < nt) dst[t * 32 + lane] = acc[t];
+    if (t < nt) {
+      dst[t * 32 + lane] = acc[t];
+      q = fmaf(acc[t], acc[t], q);
+    }
+  if (sq) {  // sum of squares of this gradient row, at the run's first sorted position
+    q = warp_sum(q);
+    if (lane == 0) sq[(long long)g * M + i] = q;
+  }
 }
 
 }  // namespace odp
@@ -468,13 +479,17 @@ void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tens
 
 // embedding_bwd through a per-path sort (same result, O(M)); keys: [G][M] int32 scratch.
 // Falls back to embedding_bwd for M > 4096 rows per path or V >= 2^20.
+// sq (optional, fp32 [G][M]): sum of squares of each written gradient row at its run's
+// first sorted position, 0 at the other positions (for the gradient-norm clip).
 // rows (optional, uint8 [G][V]): cleared, then set to 1 for every vocabulary row whose
 // gradient this call writes; the other rows of dE are left as they were (not zeroed), and
 // consumers given `rows` read them as zero. Needs the sorted path (M <= 4096, V < 2^20).
 void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
-                          int64_t H, int64_t G, int64_t V, torch::Tensor keys, c10::optional<torch::Tensor> rows) {
+                          int64_t H, int64_t G, int64_t V, torch::Tensor keys, c10::optional<torch::Tensor> rows,
+                          c10::optional<torch::Tensor> sq) {
   if (M > odp::kSortMax || V >= (1 << 20)) {
-    TORCH_CHECK(!rows.has_value(), "embedding_bwd_sorted: touched-row flags need M <= 4096 and V < 2^20");
+    TORCH_CHECK(!rows.has_value() && !sq.has_value(),
+                "embedding_bwd_sorted: touched-row flags and row sums of squares need M <= 4096 and V < 2^20");
     embedding_bwd(ids, dx, sdx, dE, se, M, H, G, V);
     return;
   }
@@ -493,9 +508,11 @@ void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torc
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (H <= 512)
     odp::embed_runs_kernel<16><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp);
+        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp,
+        sq.has_value() ? sq->data_ptr<float>() : nullptr);
   else
     odp::embed_runs_kernel<64><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp);
+        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp,
+        sq.has_value() ? sq->data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -22,7 +22,7 @@ def _g(A, lda, amn, B, ldb, bmn, C, ldc, M, N, K, epi="bf16", bn=None, **kw):
     ext().gemm_bf16(A, lda, 0, amn, B, ldb, 0, bmn, C, ldc, 0, M, N, K, 1, EPI[epi],
                     bn or (128 if tiles >= 148 else 64), kw.get("R"), kw.get("ldr", 0), 0, kw.get("aux"),
                     kw.get("ldx", 0), 0, kw.get("part"), kw.get("beta", 0.0), kw.get("f_half", 0),
-                    err_word(A.device), 0)
+                    err_word(A.device), 0, None, 0)
     return C
 
 

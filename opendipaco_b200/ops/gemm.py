@@ -17,9 +17,9 @@ EPI = {"bf16": 0, "f32": 1, "resid": 2, "swiglu": 3, "swiglu_bwd": 4, "logits": 
 
 
 def gemm(A, lda, sa, a_mn, B, ldb, sb, b_mn, C, ldc, sc, M, N, K, G=1, epi="bf16", bn=128, R=None, ldr=0,
-         sr=0, aux=None, ldx=0, sx=0, part=None, beta=0.0, f_half=0, max_ctas=0):
+         sr=0, aux=None, ldx=0, sx=0, part=None, beta=0.0, f_half=0, max_ctas=0, sq_part=None, sq_ld=0):
     ext().gemm_bf16(A, lda, sa, a_mn, B, ldb, sb, b_mn, C, ldc, sc, M, N, K, G, EPI[epi], bn, R, ldr, sr,
-                    aux, ldx, sx, part, beta, f_half, err_word(A.device), max_ctas)
+                    aux, ldx, sx, part, beta, f_half, err_word(A.device), max_ctas, sq_part, sq_ld)
     return C
 
 

@@ -203,6 +203,7 @@ class FusedExecutor:
         self._shape = None
         self._graph = None
         self._warm = False
+        self.sq_bases = None
 
     # ------------------------------------------------------------------ layout helpers
     # Every path has the same segment structure, hence the same flat layout: module
@@ -301,6 +302,30 @@ class FusedExecutor:
         # plain AdamW on one GPU per path group with the sorted embedding backward
         self.emb_rows = (z(G, V, dt=torch.uint8) if (M <= 4096 and V < (1 << 20) and V * H < (1 << 31) and self.dp == 1 and not self.opt8
                                                      and os.environ.get("ODP_EMB_ROWS", "1") != "0") else None)
+        # gradient-norm clip without re-reading the gradients: the weight-gradient GEMMs
+        # write a sum of squares per 32 x 32 output box, the embedding backward one per
+        # written row, and the norm weights are read directly (same condition as the row
+        # flags: the embedding backward must be the sorted one)
+        self.sq_bases = None
+        if self.emb_rows is not None and os.environ.get("ODP_FUSED_NORM", "1") != "0":
+            lay = self.layout
+            cb = lambda m, n: ((m + 31) // 32) * ((n + 31) // 32)  # noqa: E731
+            bases, nslot = {}, 0
+            for name, (m, n) in [("lm", (V, H))] + [(f"{k}{i}", mn) for i in range(L) for k, mn in
+                                                    (("down", (H, Fd)), ("gu", (2 * Fd, H)), ("o", (H, H)),
+                                                     ("qkv", (C, H)))]:
+                bases[name] = nslot
+                nslot += cb(m, n)
+            covered = 2 * V * H + L * (C * H + H * nh * 64 + 3 * Fd * H + 2 * H) + H
+            total = sum(k for _, _, _, k in lay.entries)
+            if covered == total:  # every parameter has a producer that reports its squares
+                self.sq_bases, self.sq_nslot = bases, nslot
+        if self.sq_bases is not None:
+            lay = self.layout
+            self.SQPARTS = z(G, self.sq_nslot)
+            self.EMBSQ = z(G, M)
+            offs = [o for lo in lay.layers for o in (lo.ln1, lo.ln2)] + [lay.normf]
+            self.NORMOFFS = torch.tensor(offs, dtype=torch.int64, device=dev)
         self.ids_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
         self.labels_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
         self.sched_host = torch.zeros(steps, G, 4, dtype=torch.float32).pin_memory()
@@ -318,13 +343,20 @@ class FusedExecutor:
         tiles128 = self.G * ((M + 127) // 128) * ((N + 127) // 128)
         return 128 if tiles128 >= 100 else 64
 
+    def _sq(self, name: str) -> dict:
+        """GEMM keyword arguments that make a weight-gradient GEMM write its box sums of
+        squares into this step's slots (none when the fused clip norm is off)."""
+        if self.sq_bases is None:
+            return {}
+        return {"sq": self.SQPARTS.view(-1)[self.sq_bases[name]:], "sq_ld": self.sq_nslot}
+
     def _gemm(self, A, lda, sa, amn, B, ldb, sb, bmn, C, ldc, sc, M, N, K, epi, bn=None, **kw):
         from ..ops.gemm import EPI
 
         ext().gemm_bf16(A, lda, sa, amn, B, ldb, sb, bmn, C, ldc, sc, M, N, K, self.G, EPI[epi],
                         bn or self._bn(M, N), kw.get("R"), kw.get("ldr", 0), kw.get("sr", 0),
                         kw.get("aux"), kw.get("ldx", 0), kw.get("sx", 0), kw.get("part"),
-                        kw.get("beta", 0.0), kw.get("f_half", 0), self.err, 0)
+                        kw.get("beta", 0.0), kw.get("f_half", 0), self.err, 0, kw.get("sq"), kw.get("sq_ld", 0))
 
     # ------------------------------------------------------------------ one inner step
     def _step(self, s: int) -> None:
@@ -369,32 +401,37 @@ class FusedExecutor:
                            G)
         # ---------------- backward
         self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
-        self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32")
+        self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32",
+                   **self._sq("lm"))
         X_.rmsnorm_bwd(self.X[L], MH, w32[lay.normf:], P, self.RSF, self.DXN, MH, None, self.DX, MH, self.DX16,
                        gr[lay.normf:], P, self.NORMWORK, M, H, G, 0.0)
         for l in range(L - 1, -1, -1):
             lo = lay.layers[l]
             self._gemm(self.DX16, H, MH, False, w16[lo.down:], Fd, P, True, self.DGU, 2 * Fd, MF2, M, Fd, H,
                        "swiglu_bwd", aux=self.GU[l], ldx=2 * Fd, sx=MF2, f_half=Fd)
-            self._gemm(self.DX16, H, MH, True, self.ACT[l], Fd, MF, True, gr[lo.down:], Fd, P, H, Fd, M, "f32")
+            self._gemm(self.DX16, H, MH, True, self.ACT[l], Fd, MF, True, gr[lo.down:], Fd, P, H, Fd, M, "f32",
+                       **self._sq(f"down{l}"))
             self._gemm(self.DGU, 2 * Fd, MF2, False, w16[lo.gu:], H, P, True, self.DXN, H, MH, M, H, 2 * Fd, "f32")
             self._gemm(self.DGU, 2 * Fd, MF2, True, self.XN2[l], H, MH, True, gr[lo.gu:], H, P, 2 * Fd, H, M,
-                       "f32")
+                       "f32", **self._sq(f"gu{l}"))
             X_.rmsnorm_bwd(self.HR[l], MH, w32[lo.ln2:], P, self.RS2[l], self.DXN, MH, self.DX, self.DX, MH,
                            self.DX16, gr[lo.ln2:], P, self.NORMWORK, M, H, G, 0.0)
             self._gemm(self.DX16, H, MH, False, w16[lo.o:], H, P, True, self.DOUT, H, MH, M, H, H, "bf16")
-            self._gemm(self.DX16, H, MH, True, self.O[l], H, MH, True, gr[lo.o:], H, P, H, H, M, "f32")
+            self._gemm(self.DX16, H, MH, True, self.O[l], H, MH, True, gr[lo.o:], H, P, H, H, M, "f32",
+                       **self._sq(f"o{l}"))
             attn.bwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l], self.DOUT,
                      self.DELTA, self.DQKV, self.err)
             self._gemm(self.DQKV, C, MC, False, w16[lo.qkv:], H, P, True, self.DXN, H, MH, M, H, C, "f32")
-            self._gemm(self.DQKV, C, MC, True, self.XN1[l], H, MH, True, gr[lo.qkv:], H, P, C, H, M, "f32")
+            self._gemm(self.DQKV, C, MC, True, self.XN1[l], H, MH, True, gr[lo.qkv:], H, P, C, H, M, "f32",
+                       **self._sq(f"qkv{l}"))
             X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[l], self.DXN, MH, self.DX, self.DX, MH,
                            self.DX16, gr[lo.ln1:], P, self.NORMWORK, M, H, G, 0.0)
         emb_n = bb.vocab_size * H
         rows = self.emb_rows
         if rows is None:
             self.GRAD[:, lay.emb:lay.emb + emb_n].zero_()
-        X_.embedding_bwd_sorted(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V, self.EMBKEYS, rows)
+        X_.embedding_bwd_sorted(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V, self.EMBKEYS, rows,
+                                self.EMBSQ if self.sq_bases is not None else None)
         # ---------------- optimizer
         clip = self.e.diloco.inner_grad_clip
         clipv = float(clip) if clip is not None else 0.0
@@ -412,7 +449,11 @@ class FusedExecutor:
                 X_.dp_adamw(self.dp_tab, self.dp_counter, self.dp_index, self.dp, G, P, P, self.dp_s0, self.dp_s1,
                             self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, self.err)
             return
-        X_.grad_clip_coef(self.GRAD, P, P, G, clipv, self.CLIPWORK, self.COEF, self.GNORM, rows, lay.emb, H, V)
+        if self.sq_bases is not None:
+            X_.grad_clip_coef_parts(self.SQPARTS, self.sq_nslot, self.EMBSQ, M, self.GRAD, P, self.NORMOFFS, H, G,
+                                    clipv, self.COEF, self.GNORM)
+        else:
+            X_.grad_clip_coef(self.GRAD, P, P, G, clipv, self.CLIPWORK, self.COEF, self.GNORM, rows, lay.emb, H, V)
         if self.opt8:
             X_.adam8bit_step(self.W32.view(-1), self.GRAD.view(-1), self.MQ, self.MABS, self.VQ, self.VLO,
                              self.VSC, self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay,
@@ -593,7 +634,7 @@ class FusedExecutor:
 
     def launches_per_round(self) -> int:
         """Kernels of this package launched per round (inner steps + outer step)."""
-        per_step = 14 + 22 * self.L + (2 if self.dp > 1 else 0)
+        per_step = 14 + 22 * self.L + (2 if self.dp > 1 else 0) - (1 if self.sq_bases is not None else 0)
         outer = getattr(self.e.backend, "outer_launches", 1) if getattr(self.e.backend, "world_size", 1) > 1 else 1
         return self.e.diloco.inner_steps * per_step + outer
 

@@ -22,7 +22,7 @@ def test_sorted_embedding_bwd(G, M, H, V):
     b = torch.zeros(G, V, H, device=DEV)
     keys = torch.zeros(G, M, dtype=torch.int32, device=DEV)
     ext().embedding_bwd(ids, dx, M * H, a, V * H, M, H, G, V)
-    ext().embedding_bwd_sorted(ids, dx, M * H, b, V * H, M, H, G, V, keys, None)
+    ext().embedding_bwd_sorted(ids, dx, M * H, b, V * H, M, H, G, V, keys, None, None)
     torch.cuda.synchronize()
     check_errors()
     assert torch.equal(a, b)

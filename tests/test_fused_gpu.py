@@ -147,3 +147,22 @@ def test_embedding_row_flags_equal_zeroed_gradient_bitwise(monkeypatch):
     assert b._fused.emb_rows is None
     assert [m.per_path_loss for m in ha] == [m.per_path_loss for m in hb]
     assert _bank_maxdiff(a, b) == 0.0
+
+
+def test_fused_gradient_norm_matches_gradient_pass(monkeypatch):
+    """The clip norm assembled from the producers' sums of squares (GEMM epilogue boxes,
+    embedding rows, norm weights) equals the norm of a separate pass over the gradients
+    (summation order differs: fp32 rounding only)."""
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    runs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ODP_FUSED_NORM", flag)
+        eng = _engine(cfg, "cuda")
+        eng.fit(corpus, 2, 4, log_every=0)
+        assert (eng._fused.sq_bases is not None) == (flag == "1")
+        runs[flag] = (eng._fused.GNORM.clone(), eng)
+    a, b = runs["1"][0], runs["0"][0]
+    assert torch.all(a > 0)
+    assert torch.allclose(a, b, rtol=2e-5, atol=0), (a, b)
+    assert _bank_maxdiff(runs["1"][1], runs["0"][1]) < 1e-4
