@@ -137,6 +137,7 @@ def test_embedding_row_flags_equal_zeroed_gradient_bitwise(monkeypatch):
     training to zeroing the whole embedding gradient every step."""
     cfg = _cfg()
     corpus = _corpus(cfg)
+    monkeypatch.setenv("ODP_FUSED_NORM", "0")  # the same gradient-norm pass in both runs
     monkeypatch.setenv("ODP_EMB_ROWS", "1")
     a = _engine(cfg, "cuda")
     ha = a.fit(corpus, 3, 4, log_every=0)
