@@ -307,8 +307,8 @@ def run(args) -> dict:
         barrier()
         t0 = time.perf_counter()
         ev0.record(st)
-        for _ in range(args.steps):
-            engine.fit(corpus, num_rounds=1, batch_size=B, log_every=0)
+        # K rounds in one fit call, as a user trains (both arms)
+        engine.fit(corpus, num_rounds=args.steps, batch_size=B, log_every=0)
         ev1.record(st)
         barrier()
         wall_ms = (time.perf_counter() - t0) * 1e3

@@ -326,11 +326,19 @@ class FusedExecutor:
             self.EMBSQ = z(G, M)
             offs = [o for lo in lay.layers for o in (lo.ln1, lo.ln2)] + [lay.normf]
             self.NORMOFFS = torch.tensor(offs, dtype=torch.int64, device=dev)
-        self.ids_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
-        self.labels_host = torch.zeros(steps, G, M, dtype=torch.int32).pin_memory()
-        self.sched_host = torch.zeros(steps, G, 4, dtype=torch.float32).pin_memory()
+        # two sets of pinned round inputs: while the GPU runs round r from one set, the host
+        # samples round r + 1 into the other (engine.fit looks ahead when the next round is
+        # certain to follow; the generator is consumed in the same order either way)
+        self._host = [dict(ids=torch.zeros(steps, G, M, dtype=torch.int32).pin_memory(),
+                           labels=torch.zeros(steps, G, M, dtype=torch.int32).pin_memory(),
+                           sched=torch.zeros(steps, G, 4, dtype=torch.float32).pin_memory(),
+                           invc=torch.zeros(steps, G, dtype=torch.float32).pin_memory()) for _ in range(2)]
+        self._slot = 0
+        self._ahead = None
+        self.ids_host, self.labels_host = self._host[0]["ids"], self._host[0]["labels"]
+        self.sched_host = self._host[0]["sched"]
         self.loss_host = torch.zeros(G, dtype=torch.float32).pin_memory()
-        self.invc_host = torch.zeros(steps, G, dtype=torch.float32).pin_memory()
+        self.invc_host = self._host[0]["invc"]
         self.cos, self.sin = rope_cos_sin(64, bb.rope_theta, S, dev)
         self.err = err_word(dev)
         self._shape = (B, S, steps)
@@ -463,7 +471,7 @@ class FusedExecutor:
                           self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, rows, lay.emb, H, V)
 
     # ------------------------------------------------------------------ round inputs
-    def _prepare(self, corpus, batch_size: int, round_idx: int):
+    def _prepare(self, corpus, batch_size: int, round_idx: int, slot: int = 0):
         e = self.e
         steps = e.diloco.inner_steps
         S = corpus.seq_len
@@ -478,15 +486,16 @@ class FusedExecutor:
         j0 = (self.dp_index if self.dp > 1 else 0) * B
         if self._shape != (B, S, steps):
             self._alloc(B, S, steps)
-        ids = self.ids_host.view(steps, self.G, B, S)
-        lab = self.labels_host.view(steps, self.G, B, S)
+        hs = self._host[slot]
+        ids = hs["ids"].view(steps, self.G, B, S)
+        lab = hs["labels"].view(steps, self.G, B, S)
         from .loop import batch_indices
 
         total = e.total_rounds * steps if e.total_rounds else None
         dl = e.diloco
         b1, b2 = dl.inner_betas
-        sched = self.sched_host
-        invc = self.invc_host
+        sched = hs["sched"]
+        invc = hs["invc"]
         for g, (sh, act) in enumerate(zip(shards, active)):
             sched[:, g].zero_()
             invc[:, g].fill_(1.0)
@@ -517,22 +526,37 @@ class FusedExecutor:
             sched[:, g] = torch.tensor(rows, dtype=sched.dtype)
         return active
 
-    def _upload(self) -> None:
-        self.INVC.copy_(self.invc_host, non_blocking=True)
-        self.IDS.copy_(self.ids_host, non_blocking=True)
-        self.LABELS.copy_(self.labels_host, non_blocking=True)
-        self.SCHED.copy_(self.sched_host, non_blocking=True)
+    def _upload(self, slot: int = 0) -> None:
+        hs = self._host[slot]
+        self.INVC.copy_(hs["invc"], non_blocking=True)
+        self.IDS.copy_(hs["ids"], non_blocking=True)
+        self.LABELS.copy_(hs["labels"], non_blocking=True)
+        self.SCHED.copy_(hs["sched"], non_blocking=True)
 
     # ------------------------------------------------------------------ round
-    def run_round(self, corpus, batch_size: int, round_idx: int):
+    def run_round(self, corpus, batch_size: int, round_idx: int, next_round: int | None = None):
+        """One round. ``next_round``: index of the round the caller will certainly run next
+        with the same corpus and batch size; its batches are then sampled on the host while
+        the GPU runs this round."""
         e = self.e
         steps = e.diloco.inner_steps
-        active = self._prepare(corpus, batch_size, round_idx)
-        self._upload()
+        key = (id(corpus), batch_size, round_idx)
+        if self._ahead is not None and self._ahead[0] == key and self._shape is not None:
+            slot, active = self._ahead[1], self._ahead[2]
+        else:
+            slot = self._slot
+            active = self._prepare(corpus, batch_size, round_idx, slot)
+        self._ahead = None
+        self._upload(slot)
         self._run_inner(steps)
         for g, a in enumerate(active):
             if a:
                 self.steps_taken[g] += steps
+        if next_round is not None:
+            nxt = 1 - slot  # the set this round's copies are not reading from
+            self._ahead = ((id(corpus), batch_size, next_round), nxt,
+                           self._prepare(corpus, batch_size, next_round, nxt))
+            self._slot = nxt
         norms = self._outer(corpus, active)
         last = self.LOSSES[steps - 1]
         if self.dp > 1:

@@ -243,9 +243,10 @@ class DiPaCoEngine:
                                diloco=self.diloco, device=self.device)
 
     # -- one round ------------------------------------------------------------
-    def run_round(self, corpus: ShardedCorpus, batch_size: int, round_idx: int = 0) -> RoundMetrics:
+    def run_round(self, corpus: ShardedCorpus, batch_size: int, round_idx: int = 0,
+                  _next_round: int | None = None) -> RoundMetrics:
         if self._fused is not None:
-            per_path_loss, delta_norms = self._fused.run_round(corpus, batch_size, round_idx)
+            per_path_loss, delta_norms = self._fused.run_round(corpus, batch_size, round_idx, _next_round)
         else:
             per_path_loss, delta_norms = self._module_round(corpus, batch_size, round_idx)
         val = self._track_best(corpus, batch_size) if corpus.has_validation else None
@@ -339,7 +340,10 @@ class DiPaCoEngine:
             self.total_rounds = self._global_round + num_rounds
         hist = []
         for i in range(num_rounds):
-            m = self.run_round(corpus, batch_size, round_idx=self._global_round)
+            # the fused executor samples the next round's batches while this one runs on
+            # the GPU, when that round is certain to follow (no validation pass in between)
+            ahead = (self._global_round + 1 if i + 1 < num_rounds and not corpus.has_validation else None)
+            m = self.run_round(corpus, batch_size, round_idx=self._global_round, _next_round=ahead)
             self._global_round += 1
             hist.append(m)
             if log_every and (m.round % log_every == 0 or i == num_rounds - 1):
