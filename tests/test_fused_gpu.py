@@ -167,3 +167,17 @@ def test_fused_gradient_norm_matches_gradient_pass(monkeypatch):
     assert torch.all(a > 0)
     assert torch.allclose(a, b, rtol=2e-5, atol=0), (a, b)
     assert _bank_maxdiff(runs["1"][1], runs["0"][1]) < 1e-4
+
+
+def test_lookahead_fit_equals_round_by_round_bitwise():
+    """fit(num_rounds=3) samples each next round's batches while the GPU runs the current
+    one; training is bit-identical to three fit(num_rounds=1) calls (same generator order)."""
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    a, b = _engine(cfg, "cuda"), _engine(cfg, "cuda")
+    a.total_rounds = b.total_rounds = 3
+    ha = a.fit(corpus, 3, 4, log_every=0)
+    hb = [m for _ in range(3) for m in b.fit(corpus, 1, 4, log_every=0)]
+    assert [m.per_path_loss for m in ha] == [m.per_path_loss for m in hb]
+    assert _bank_maxdiff(a, b) == 0.0
+    assert torch.equal(a._gen.get_state(), b._gen.get_state())
