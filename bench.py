@@ -17,8 +17,9 @@ Timing: W untimed warm-up rounds, then exactly K rounds bracketed by a barrier a
 ``torch.cuda.synchronize()`` on both sides, CUDA events on the launching stream, max
 over ranks. ``value`` times the device work of a round (captured inner-step graph +
 outer step, inputs already resident); ``e2e`` times the same K rounds through the
-public API (``engine.fit``), which copies each round's token batches from pinned
-host memory and reads the losses back. The per-round working set (weights, grads
+public API (one ``engine.fit(corpus, num_rounds=K)`` call in both arms), which samples
+each round's token batches on the host, copies them from pinned host memory and reads
+the losses back every round. The per-round working set (weights, grads
 and optimizer state: ~570 MB per path) is far larger than the 126 MB L2.
 
 ``--impl reference`` runs the unmodified reference package installed in
