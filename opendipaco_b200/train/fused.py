@@ -201,6 +201,8 @@ class FusedExecutor:
 
         # -- step buffers are sized on the first round ---------------------------------
         self._shape = None
+        self._ahead = None  # (round key, host slot, active flags) sampled ahead of time
+        self._slot = 0
         self._graph = None
         self._warm = False
         self.sq_bases = None
