@@ -201,6 +201,11 @@ class FusedExecutor:
 
         # -- step buffers are sized on the first round ---------------------------------
         self._shape = None
+        # ODP_HEAD_DW_CTAS=n > 0: LM-head weight gradient on a side stream with n CTAs
+        self._side_ctas = int(os.environ.get("ODP_HEAD_DW_CTAS", "0"))
+        self._side = torch.cuda.Stream(device=self.dev) if self._side_ctas > 0 else None
+        self._ev_fork = torch.cuda.Event() if self._side_ctas > 0 else None
+        self._ev_join = torch.cuda.Event() if self._side_ctas > 0 else None
         self._ahead = None  # (round key, host slot, active flags) sampled ahead of time
         self._slot = 0
         self._graph = None
@@ -366,7 +371,8 @@ class FusedExecutor:
         ext().gemm_bf16(A, lda, sa, amn, B, ldb, sb, bmn, C, ldc, sc, M, N, K, self.G, EPI[epi],
                         bn or self._bn(M, N), kw.get("R"), kw.get("ldr", 0), kw.get("sr", 0),
                         kw.get("aux"), kw.get("ldx", 0), kw.get("sx", 0), kw.get("part"),
-                        kw.get("beta", 0.0), kw.get("f_half", 0), self.err, 0, kw.get("sq"), kw.get("sq_ld", 0))
+                        kw.get("beta", 0.0), kw.get("f_half", 0), self.err, kw.get("max_ctas", 0), kw.get("sq"),
+                        kw.get("sq_ld", 0))
 
     # ------------------------------------------------------------------ one inner step
     def _step(self, s: int) -> None:
@@ -411,8 +417,21 @@ class FusedExecutor:
                            G)
         # ---------------- backward
         self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
-        self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32",
-                   **self._sq("lm"))
+        side = self._side
+        if side is not None:
+            # the LM-head weight gradient is needed only by the optimizer: on a side stream
+            # with a capped grid it runs under the layers' backward, whose small GEMMs and
+            # attention leave SMs idle; joined before the gradient norm
+            cur = torch.cuda.current_stream(self.dev)
+            self._ev_fork.record(cur)
+            side.wait_event(self._ev_fork)
+            with torch.cuda.stream(side):
+                self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32",
+                           max_ctas=self._side_ctas, **self._sq("lm"))
+                self._ev_join.record(side)
+        else:
+            self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32",
+                       **self._sq("lm"))
         X_.rmsnorm_bwd(self.X[L], MH, w32[lay.normf:], P, self.RSF, self.DXN, MH, None, self.DX, MH, self.DX16,
                        gr[lay.normf:], P, self.NORMWORK, M, H, G, 0.0)
         for l in range(L - 1, -1, -1):
@@ -442,6 +461,8 @@ class FusedExecutor:
             self.GRAD[:, lay.emb:lay.emb + emb_n].zero_()
         X_.embedding_bwd_sorted(ids, self.DX, MH, gr[lay.emb:], P, M, H, G, V, self.EMBKEYS, rows,
                                 self.EMBSQ if self.sq_bases is not None else None)
+        if side is not None:
+            torch.cuda.current_stream(self.dev).wait_event(self._ev_join)
         # ---------------- optimizer
         clip = self.e.diloco.inner_grad_clip
         clipv = float(clip) if clip is not None else 0.0
