@@ -20,6 +20,8 @@ void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tens
 void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
                           int64_t H, int64_t G, int64_t V, torch::Tensor keys, c10::optional<torch::Tensor> rows,
                           c10::optional<torch::Tensor> sq);
+void gemm_splitk_reduce(torch::Tensor ws, int64_t S, int64_t G, int64_t M, int64_t N, torch::Tensor C, int64_t ldc,
+                        int64_t sc, c10::optional<torch::Tensor> sq_part, int64_t sq_ld, double beta);
 void grad_clip_coef_parts(torch::Tensor parts, int64_t nslot, torch::Tensor esq, int64_t M, torch::Tensor grads,
                           int64_t P, torch::Tensor norm_offs, int64_t H, int64_t G, double max_norm, torch::Tensor coef,
                           c10::optional<torch::Tensor> norm_out);
@@ -89,6 +91,7 @@ std::vector<torch::Tensor> kmeans_assign(torch::Tensor x, torch::Tensor c, int64
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opendipaco_b200 sm_100a kernels";
   m.def("gemm_bf16", &gemm_bf16);
+  m.def("gemm_splitk_reduce", &gemm_splitk_reduce);
   m.def("grad_clip_coef_parts", &grad_clip_coef_parts);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);

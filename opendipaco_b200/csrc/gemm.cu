@@ -1193,6 +1193,61 @@ static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, 
 
 }  // namespace odp
 
+namespace odp {
+
+// ---------------------------------------------------------------- split-K reduction
+// A weight-gradient GEMM whose output tiles cannot fill the GPU runs as S times as many
+// groups over K / S each (for these operands group g's K rows start at g * K * ld, so the
+// splits are plain groups of the same GEMM): ws[g * S + s] holds split s of group g.
+// C[g] = sum_s ws[g * S + s] (+ beta * C) in split order, and, if sqp is given, the sum of
+// squares of every 32 x 32 box of C at sqp[g * sq_ld + (row / 32) * ceil(N / 32) + col / 32].
+// One 256-thread block per 32 x 32 box: 32 rows x 8 threads x 4 columns.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int S, int M, int N,
+                                                            float* __restrict__ C, long long ldc, long long sc,
+                                                            float* __restrict__ sqp, long long sq_ld, float beta) {
+  const int nbc = (N + 31) / 32, nbr = (M + 31) / 32;
+  const int g = blockIdx.y, br = blockIdx.x / nbc, bc = blockIdx.x % nbc;
+  const int r = br * 32 + threadIdx.x / 8, c = bc * 32 + (threadIdx.x % 8) * 4;
+  float q = 0.f;
+  if (r < M && c < N) {
+    const long long mn = (long long)M * N;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    const int n = min(4, N - c);
+    for (int sp = 0; sp < S; ++sp) {
+      const float* w = ws + ((long long)g * S + sp) * mn + (long long)r * N + c;
+      if (n == 4 && (N % 4) == 0) {
+        const float4 x = *reinterpret_cast<const float4*>(w);
+        v[0] += x.x;
+        v[1] += x.y;
+        v[2] += x.z;
+        v[3] += x.w;
+      } else {
+        for (int i = 0; i < n; ++i) v[i] += w[i];
+      }
+    }
+    float* dst = C + g * sc + (long long)r * ldc + c;
+    for (int i = 0; i < n; ++i) {
+      const float o = beta != 0.f ? v[i] + beta * dst[i] : v[i];
+      dst[i] = o;
+      q = fmaf(o, o, q);
+    }
+  }
+  if (sqp) {
+    q = warp_sum(q);
+    __shared__ float red[8];
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = q;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int w = 0; w < 8; ++w) t += red[w];
+      sqp[(long long)g * sq_ld + (long long)br * nbc + bc] = t;
+    }
+  }
+  (void)nbr;
+}
+
+}  // namespace odp
+
 // ---------------------------------------------------------------- torch entry
 // A: tensor whose storage holds G groups; a_mn selects its major; shapes are given
 // explicitly so callers can pass views into flat parameter buffers.
@@ -1243,4 +1298,16 @@ void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tenso
     case EPI_LOGITS: dispatch<EPI_LOGITS>(a, b, p, (int)bn, st, (int)max_ctas); break;
     default: TORCH_CHECK(false, "unknown epilogue ", epi);
   }
+}
+
+// ws: [G * S][M][N] fp32 split partials (group-major); C: G groups of [M][N] at (ldc, sc).
+void gemm_splitk_reduce(torch::Tensor ws, int64_t S, int64_t G, int64_t M, int64_t N, torch::Tensor C, int64_t ldc,
+                        int64_t sc, c10::optional<torch::Tensor> sq_part, int64_t sq_ld, double beta) {
+  c10::cuda::CUDAGuard guard(ws.device());
+  TORCH_CHECK(ws.numel() >= G * S * M * N, "gemm_splitk_reduce: workspace too small");
+  dim3 grid((unsigned)(((M + 31) / 32) * ((N + 31) / 32)), (unsigned)G);
+  odp::splitk_reduce_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ws.data_ptr<float>(), (int)S, (int)M, (int)N, C.data_ptr<float>(), ldc, sc,
+      sq_part.has_value() ? sq_part->data_ptr<float>() : nullptr, sq_ld, (float)beta);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

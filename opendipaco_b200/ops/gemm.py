@@ -9,6 +9,8 @@ are passed as (base tensor, offsets folded into a narrowed view).
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from ._ext import err_word, ext
@@ -65,3 +67,41 @@ def mm_tt(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, bn: int | N
     gemm(a, a.stride(0), 0, True, b, b.stride(0), 0, False, c, c.stride(0), 0, M, N, K,
          epi="bf16" if out_dtype == torch.bfloat16 else "f32", bn=bn or _bn_for(N))
     return c
+
+
+def splitk_factor(M: int, N: int, K: int, G: int, sms: int = 148) -> int:
+    """Number of K splits for a weight-gradient GEMM whose 128 x 128 output tiles leave
+    most SMs idle: doubled while the split grid still fits one wave and each split keeps
+    at least 384 of K in whole 64-wide k-blocks (``ODP_SPLITK`` forces a value)."""
+    forced = os.environ.get("ODP_SPLITK")
+    tiles = G * ((M + 127) // 128) * ((N + 127) // 128)
+    s = 1
+    if forced:
+        want = int(forced)
+        while s < want and K % (2 * s * 64) == 0 and K // (2 * s) >= 64:
+            s *= 2
+        return s
+    while s < 8 and tiles * s * 2 <= sms and K % (2 * s * 64) == 0 and K // (2 * s) >= 384:
+        s *= 2
+    return s
+
+
+def gemm_wgrad(A, lda, sa, B, ldb, sb, C, ldc, sc, M, N, K, G, S, ws, sq_part=None, sq_ld=0, err=None,
+               beta=0.0, bn=128):
+    """fp32 weight gradient C[g] = A[g] B[g]^T with both operands MN-major (K = tokens),
+    split over K into S parts when S > 1: the splits run as G * S groups of one GEMM into
+    the workspace ``ws`` and are summed in a fixed order by ``gemm_splitk_reduce`` (which
+    also writes the 32 x 32 box sums of squares). Needs sa == K * lda and sb == K * ldb."""
+    x = ext()
+    e = err if err is not None else err_word(A.device)
+    if S <= 1:
+        x.gemm_bf16(A, lda, sa, True, B, ldb, sb, True, C, ldc, sc, M, N, K, G, EPI["f32"], bn, None, 0, 0,
+                    None, 0, 0, None, beta, 0, e, 0, sq_part, sq_ld)
+        return C
+    if sa != K * lda or sb != K * ldb or K % (S * 64):
+        raise ValueError("gemm_wgrad: split-K needs contiguous groups along K and K % (64 S) == 0")
+    ks = K // S
+    x.gemm_bf16(A, lda, ks * lda, True, B, ldb, ks * ldb, True, ws, N, M * N, M, N, ks, G * S, EPI["f32"], 128,
+                None, 0, 0, None, 0, 0, None, 0.0, 0, e, 0, None, 0)
+    x.gemm_splitk_reduce(ws, S, G, M, N, C, ldc, sc, sq_part, sq_ld, beta)
+    return C

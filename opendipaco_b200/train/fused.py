@@ -201,6 +201,7 @@ class FusedExecutor:
 
         # -- step buffers are sized on the first round ---------------------------------
         self._shape = None
+        self.wg_split: dict[str, int] = {}
         # ODP_HEAD_DW_CTAS=n > 0: LM-head weight gradient on a side stream with n CTAs
         self._side_ctas = int(os.environ.get("ODP_HEAD_DW_CTAS", "0"))
         self._side = torch.cuda.Stream(device=self.dev) if self._side_ctas > 0 else None
@@ -309,6 +310,17 @@ class FusedExecutor:
         # plain AdamW on one GPU per path group with the sorted embedding backward
         self.emb_rows = (z(G, V, dt=torch.uint8) if (M <= 4096 and V < (1 << 20) and V * H < (1 << 31) and self.dp == 1 and not self.opt8
                                                      and os.environ.get("ODP_EMB_ROWS", "1") != "0") else None)
+        # K splits of the weight-gradient GEMMs (tokens are K) that cannot fill the GPU alone
+        # (few paths per GPU), and their shared workspace
+        from ..ops.gemm import splitk_factor
+
+        self.wg_shapes = {"lm": (V, H)}
+        for i in range(L):
+            self.wg_shapes.update({f"down{i}": (H, Fd), f"gu{i}": (2 * Fd, H), f"o{i}": (H, H), f"qkv{i}": (C, H)})
+        self.wg_split = {k: splitk_factor(m, n, M, G) for k, (m, n) in self.wg_shapes.items()}
+        ws = max([G * sp * self.wg_shapes[k][0] * self.wg_shapes[k][1] for k, sp in self.wg_split.items()
+                  if sp > 1] or [1])
+        self.WGWS = z(ws)
         # gradient-norm clip without re-reading the gradients: the weight-gradient GEMMs
         # write a sum of squares per 32 x 32 output box, the embedding backward one per
         # written row, and the norm weights are read directly (same condition as the row
@@ -364,6 +376,15 @@ class FusedExecutor:
         if self.sq_bases is None:
             return {}
         return {"sq": self.SQPARTS.view(-1)[self.sq_bases[name]:], "sq_ld": self.sq_nslot}
+
+    def _wgrad(self, name: str, A, lda, sa, B, ldb, sb, C, ldc, sc, M, N, K) -> None:
+        """fp32 weight gradient (both operands MN-major, K = tokens), split over K when
+        few paths per GPU leave the tile grid short of the SM count."""
+        from ..ops.gemm import gemm_wgrad
+
+        sq = self._sq(name)
+        gemm_wgrad(A, lda, sa, B, ldb, sb, C, ldc, sc, M, N, K, self.G, self.wg_split[name], self.WGWS,
+                   sq.get("sq"), sq.get("sq_ld", 0), self.err, bn=self._bn(M, N))
 
     def _gemm(self, A, lda, sa, amn, B, ldb, sb, bmn, C, ldc, sc, M, N, K, epi, bn=None, **kw):
         from ..ops.gemm import EPI
@@ -430,29 +451,24 @@ class FusedExecutor:
                            max_ctas=self._side_ctas, **self._sq("lm"))
                 self._ev_join.record(side)
         else:
-            self._gemm(self.LOGITS, V, M * V, True, self.XNF, H, MH, True, gr[lay.lm:], H, P, V, H, M, "f32",
-                       **self._sq("lm"))
+            self._wgrad("lm", self.LOGITS, V, M * V, self.XNF, H, MH, gr[lay.lm:], H, P, V, H, M)
         X_.rmsnorm_bwd(self.X[L], MH, w32[lay.normf:], P, self.RSF, self.DXN, MH, None, self.DX, MH, self.DX16,
                        gr[lay.normf:], P, self.NORMWORK, M, H, G, 0.0)
         for l in range(L - 1, -1, -1):
             lo = lay.layers[l]
             self._gemm(self.DX16, H, MH, False, w16[lo.down:], Fd, P, True, self.DGU, 2 * Fd, MF2, M, Fd, H,
                        "swiglu_bwd", aux=self.GU[l], ldx=2 * Fd, sx=MF2, f_half=Fd)
-            self._gemm(self.DX16, H, MH, True, self.ACT[l], Fd, MF, True, gr[lo.down:], Fd, P, H, Fd, M, "f32",
-                       **self._sq(f"down{l}"))
+            self._wgrad(f"down{l}", self.DX16, H, MH, self.ACT[l], Fd, MF, gr[lo.down:], Fd, P, H, Fd, M)
             self._gemm(self.DGU, 2 * Fd, MF2, False, w16[lo.gu:], H, P, True, self.DXN, H, MH, M, H, 2 * Fd, "f32")
-            self._gemm(self.DGU, 2 * Fd, MF2, True, self.XN2[l], H, MH, True, gr[lo.gu:], H, P, 2 * Fd, H, M,
-                       "f32", **self._sq(f"gu{l}"))
+            self._wgrad(f"gu{l}", self.DGU, 2 * Fd, MF2, self.XN2[l], H, MH, gr[lo.gu:], H, P, 2 * Fd, H, M)
             X_.rmsnorm_bwd(self.HR[l], MH, w32[lo.ln2:], P, self.RS2[l], self.DXN, MH, self.DX, self.DX, MH,
                            self.DX16, gr[lo.ln2:], P, self.NORMWORK, M, H, G, 0.0)
             self._gemm(self.DX16, H, MH, False, w16[lo.o:], H, P, True, self.DOUT, H, MH, M, H, H, "bf16")
-            self._gemm(self.DX16, H, MH, True, self.O[l], H, MH, True, gr[lo.o:], H, P, H, H, M, "f32",
-                       **self._sq(f"o{l}"))
+            self._wgrad(f"o{l}", self.DX16, H, MH, self.O[l], H, MH, gr[lo.o:], H, P, H, H, M)
             attn.bwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l], self.DOUT,
                      self.DELTA, self.DQKV, self.err)
             self._gemm(self.DQKV, C, MC, False, w16[lo.qkv:], H, P, True, self.DXN, H, MH, M, H, C, "f32")
-            self._gemm(self.DQKV, C, MC, True, self.XN1[l], H, MH, True, gr[lo.qkv:], H, P, C, H, M, "f32",
-                       **self._sq(f"qkv{l}"))
+            self._wgrad(f"qkv{l}", self.DQKV, C, MC, self.XN1[l], H, MH, gr[lo.qkv:], H, P, C, H, M)
             X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[l], self.DXN, MH, self.DX, self.DX, MH,
                            self.DX16, gr[lo.ln1:], P, self.NORMWORK, M, H, G, 0.0)
         emb_n = bb.vocab_size * H
@@ -681,7 +697,8 @@ class FusedExecutor:
 
     def launches_per_round(self) -> int:
         """Kernels of this package launched per round (inner steps + outer step)."""
-        per_step = 14 + 22 * self.L + (2 if self.dp > 1 else 0) - (1 if self.sq_bases is not None else 0)
+        per_step = (14 + 22 * self.L + (2 if self.dp > 1 else 0) - (1 if self.sq_bases is not None else 0)
+                    + sum(1 for sp in self.wg_split.values() if sp > 1))
         outer = getattr(self.e.backend, "outer_launches", 1) if getattr(self.e.backend, "world_size", 1) > 1 else 1
         return self.e.diloco.inner_steps * per_step + outer
 

@@ -181,3 +181,21 @@ def test_lookahead_fit_equals_round_by_round_bitwise():
     assert [m.per_path_loss for m in ha] == [m.per_path_loss for m in hb]
     assert _bank_maxdiff(a, b) == 0.0
     assert torch.equal(a._gen.get_state(), b._gen.get_state())
+
+
+def test_split_k_weight_gradients_track_unsplit(monkeypatch):
+    """Forcing the K split of every weight-gradient GEMM (fixed-order reduction of the
+    splits) trains like the unsplit GEMMs up to fp32 summation order."""
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    runs = {}
+    for forced in ("2", "1"):
+        monkeypatch.setenv("ODP_SPLITK", forced)
+        eng = _engine(cfg, "cuda")
+        h = eng.fit(corpus, 2, 4, log_every=0)
+        assert max(eng._fused.wg_split.values()) == int(forced)
+        runs[forced] = (h, eng)
+    for a, b in zip(runs["2"][0], runs["1"][0]):
+        for p in a.per_path_loss:
+            assert abs(a.per_path_loss[p] - b.per_path_loss[p]) < 1e-3 * b.per_path_loss[p]
+    assert _bank_maxdiff(runs["2"][1], runs["1"][1]) < 1e-3

@@ -152,3 +152,37 @@ def test_tma_store_epilogues_match_per_thread_stores(epi, G, M, N, K, monkeypatc
         monkeypatch.delenv("ODP_GEMM_NO_TMA_STORE")
         for a, b in zip(tma, plain):
             assert torch.equal(a, b), (pair, (a.float() - b.float()).abs().max().item())
+
+
+@pytest.mark.parametrize("S", [1, 2, 4, 8])
+@pytest.mark.parametrize("G,M,N,K", [(2, 384, 384, 3072), (2, 1152, 384, 1024), (1, 300, 200, 512)])
+def test_split_k_weight_gradient_matches_reference(S, G, M, N, K, monkeypatch):
+    """Weight gradient C[g] = A[g] B[g]^T (both MN-major, K = tokens) split over K into S
+    groups of one GEMM plus a fixed-order reduction: against fp32 PyTorch, against the
+    unsplit GEMM, and its 32 x 32 box sums of squares against PyTorch's."""
+    from opendipaco_b200.ops.gemm import gemm_wgrad
+
+    monkeypatch.setenv("ODP_GEMM_2SM", "1")
+    A = _bf(G, K, M, seed=5)
+    B = _bf(G, K, N, seed=6)
+    nb = ((M + 31) // 32) * ((N + 31) // 32)
+    ws = torch.empty(G * S * M * N, device=DEV)
+
+    def run(split):
+        C = torch.full((G, M, N), 3.0, device=DEV)
+        sq = torch.full((G, nb), -1.0, device=DEV)
+        gemm_wgrad(A, M, K * M, B, N, K * N, C, N, M * N, M, N, K, G, split, ws, sq, nb)
+        torch.cuda.synchronize()
+        return C, sq
+
+    if K % (64 * S):
+        pytest.skip("K not divisible into 64-wide splits")
+    c, sq = run(S)
+    c1, _ = run(1)
+    ref = A.float().transpose(1, 2) @ B.float()
+    _close(c, ref, 2e-3)
+    _close(c, c1, 1e-5)
+    pad = torch.zeros(G, (M + 31) // 32 * 32, (N + 31) // 32 * 32, device=DEV)
+    pad[:, :M, :N] = c
+    boxes = pad.view(G, (M + 31) // 32, 32, (N + 31) // 32, 32).pow(2).sum((2, 4)).reshape(G, -1)
+    _close(sq, boxes, 1e-4)
