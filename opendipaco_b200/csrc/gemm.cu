@@ -1213,17 +1213,24 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     const long long mn = (long long)M * N;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     const int n = min(4, N - c);
-    for (int sp = 0; sp < S; ++sp) {
-      const float* w = ws + ((long long)g * S + sp) * mn + (long long)r * N + c;
-      if (n == 4 && (N % 4) == 0) {
-        const float4 x = *reinterpret_cast<const float4*>(w);
-        v[0] += x.x;
-        v[1] += x.y;
-        v[2] += x.z;
-        v[3] += x.w;
-      } else {
-        for (int i = 0; i < n; ++i) v[i] += w[i];
-      }
+    const float* w0 = ws + (long long)g * S * mn + (long long)r * N + c;
+    if (n == 4 && (N % 4) == 0 && S <= 8) {
+      // every split's load in flight at once, then the sum in split order
+      float4 x[8];
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp)
+        if (sp < S) x[sp] = *reinterpret_cast<const float4*>(w0 + sp * mn);
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp)
+        if (sp < S) {
+          v[0] += x[sp].x;
+          v[1] += x[sp].y;
+          v[2] += x[sp].z;
+          v[3] += x[sp].w;
+        }
+    } else {
+      for (int sp = 0; sp < S; ++sp)
+        for (int i = 0; i < n; ++i) v[i] += w0[sp * mn + i];
     }
     float* dst = C + g * sc + (long long)r * ldc + c;
     for (int i = 0; i < n; ++i) {

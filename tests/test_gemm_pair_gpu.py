@@ -155,7 +155,7 @@ def test_tma_store_epilogues_match_per_thread_stores(epi, G, M, N, K, monkeypatc
 
 
 @pytest.mark.parametrize("S", [1, 2, 4, 8])
-@pytest.mark.parametrize("G,M,N,K", [(2, 384, 384, 3072), (2, 1152, 384, 1024), (1, 300, 200, 512)])
+@pytest.mark.parametrize("G,M,N,K", [(2, 384, 384, 3072), (2, 1152, 384, 1024), (1, 320, 200, 512)])
 def test_split_k_weight_gradient_matches_reference(S, G, M, N, K, monkeypatch):
     """Weight gradient C[g] = A[g] B[g]^T (both MN-major, K = tokens) split over K into S
     groups of one GEMM plus a fixed-order reduction: against fp32 PyTorch, against the
