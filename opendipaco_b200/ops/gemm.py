@@ -72,7 +72,10 @@ def mm_tt(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, bn: int | N
 def splitk_factor(M: int, N: int, K: int, G: int, sms: int = 148) -> int:
     """Number of K splits for a weight-gradient GEMM whose 128 x 128 output tiles leave
     most SMs idle: doubled while the split grid still fits one wave and each split keeps
-    at least 384 of K in whole 64-wide k-blocks (``ODP_SPLITK`` forces a value)."""
+    at least 384 of K in whole 64-wide k-blocks (``ODP_SPLITK`` forces a value). Only
+    grids of at most an eighth of the SMs are split: measured at 2 paths per GPU, the
+    extra reduction launch (~8 us) cancels the gain for grids of 48-54 tiles, while the
+    18-tile attention-output gradient goes from 27 to 15 us."""
     forced = os.environ.get("ODP_SPLITK")
     tiles = G * ((M + 127) // 128) * ((N + 127) // 128)
     s = 1
@@ -81,6 +84,8 @@ def splitk_factor(M: int, N: int, K: int, G: int, sms: int = 148) -> int:
         while s < want and K % (2 * s * 64) == 0 and K // (2 * s) >= 64:
             s *= 2
         return s
+    if tiles * 8 > sms:
+        return 1
     while s < 8 and tiles * s * 2 <= sms and K % (2 * s * 64) == 0 and K // (2 * s) >= 384:
         s *= 2
     return s
