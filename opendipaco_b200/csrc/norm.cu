@@ -93,9 +93,10 @@ constexpr int kNormRowsPerBlock = 32;
 __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, long long sx, const float* __restrict__ w,
                                    long long sw, const float* __restrict__ rstd, const float* __restrict__ dy,
                                    long long sdy, const float* dres, float* dx, long long sdx,
-                                   __nv_bfloat16* dx16, float* __restrict__ dw_part, int M, int H, int G) {
+                                   __nv_bfloat16* dx16, float* __restrict__ dw_part, int M, int H, int G,
+                                   int rpb) {
   // block = 256 threads = 8 warps; block handles kNormRowsPerBlock rows of one group
-  const int nblk = (M + kNormRowsPerBlock - 1) / kNormRowsPerBlock;
+  const int nblk = (M + rpb - 1) / rpb;
   const int g = blockIdx.x / nblk, b = blockIdx.x % nblk;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   extern __shared__ float sdw[];  // [8 warps][H]
@@ -103,8 +104,8 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, long long sx, co
   __syncthreads();
   const float* wg = w + g * sw;
   const int n4 = H / 4;  // float4 columns (H % 128 == 0: n4 is a multiple of 32)
-  for (int rr = warp; rr < kNormRowsPerBlock; rr += 8) {
-    const int r = b * kNormRowsPerBlock + rr;
+  for (int rr = warp; rr < rpb; rr += 8) {
+    const int r = b * rpb + rr;
     if (r >= M) break;
     const float4* xr = reinterpret_cast<const float4*>(x + g * sx + (long long)r * H);
     const float4* dyr = reinterpret_cast<const float4*>(dy + g * sdy + (long long)r * H);
@@ -161,8 +162,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const float* __res
                                                               const float* __restrict__ dy, long long sdy,
                                                               const float* dres, float* dx, long long sdx,
                                                               __nv_bfloat16* dx16, float* __restrict__ dw_part, int M,
-                                                              int H, int G) {
-  const int nblk = (M + kNormRowsPerBlock - 1) / kNormRowsPerBlock;
+                                                              int H, int G, int rpb) {
+  const int nblk = (M + rpb - 1) / rpb;
   const int g = blockIdx.x / nblk, b = blockIdx.x % nblk;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   extern __shared__ float sdw[];  // [8 warps][H]
@@ -174,8 +175,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const float* __res
     acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 #pragma unroll 1
-  for (int rr = warp; rr < kNormRowsPerBlock; rr += 8) {
-    const int r = b * kNormRowsPerBlock + rr;
+  for (int rr = warp; rr < rpb; rr += 8) {
+    const int r = b * rpb + rr;
     if (r >= M) break;
     const float4* xr = reinterpret_cast<const float4*>(x + g * sx + (long long)r * H);
     const float4* dyr = reinterpret_cast<const float4*>(dy + g * sdy + (long long)r * H);
@@ -419,7 +420,11 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
                  int64_t H, int64_t G, double beta) {
   c10::cuda::CUDAGuard guard(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  const int nblk = (int)((M + odp::kNormRowsPerBlock - 1) / odp::kNormRowsPerBlock);
+  // rows per block: 32, or 8 when 32-row blocks would not give two blocks per SM (few paths
+  // per GPU) and the partial buffer has room for the extra blocks
+  int rpb = odp::kNormRowsPerBlock;
+  if (G * ((M + 31) / 32) < 2 * 148 && work.numel() >= G * ((M + 7) / 8) * H) rpb = 8;
+  const int nblk = (int)((M + rpb - 1) / rpb);
   TORCH_CHECK(work.numel() >= G * nblk * H, "rmsnorm_bwd: work buffer too small");
   auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   TORCH_CHECK(H % 4 == 0 && sx % 4 == 0 && sdy % 4 == 0 && sdx % 4 == 0 && sw % 4 == 0 && al16(x.data_ptr()) &&
@@ -437,7 +442,7 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
         x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, rstd.data_ptr<float>(), dy.data_ptr<float>(), sdy,      \
         dres.has_value() ? dres->data_ptr<float>() : nullptr, dx.data_ptr<float>(), sdx,                          \
         dx16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx16->data_ptr()) : nullptr, work.data_ptr<float>(),  \
-        (int)M, (int)H, (int)G);                                                                                  \
+        (int)M, (int)H, (int)G, rpb);                                                                             \
     launched = true;                                                                                              \
   }
   ODP_RMS_BWD(1) ODP_RMS_BWD(2) ODP_RMS_BWD(3) ODP_RMS_BWD(4) ODP_RMS_BWD(8)
@@ -449,7 +454,7 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
       x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, rstd.data_ptr<float>(), dy.data_ptr<float>(), sdy,
       dres.has_value() ? dres->data_ptr<float>() : nullptr, dx.data_ptr<float>(), sdx,
       dx16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx16->data_ptr()) : nullptr, work.data_ptr<float>(),
-      (int)M, (int)H, (int)G);
+      (int)M, (int)H, (int)G, rpb);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::reduce_parts_kernel<<<blocks_for(G * H, 256), 256, 0, st>>>(work.data_ptr<float>(), nblk, (int)H, (int)G,

@@ -295,7 +295,7 @@ class FusedExecutor:
         self.DOUT = z(G, M, H, dt=b16)
         self.DQKV = z(G, M, C, dt=b16)
         self.DELTA = z(G * B, nh, S)
-        self.NORMWORK = z(G * ((M + 31) // 32) * H)
+        self.NORMWORK = z(G * ((M + 7) // 8) * H)  # RMSNorm weight-gradient partials (8-row blocks at most)
         self.CLIPWORK = z(G * ((self.P + (1 << 16) - 1) // (1 << 16)))
         self.COEF = z(G)
         self.GNORM = z(G)
