@@ -45,13 +45,12 @@ __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, long long sx, co
 
 // The same with the row held in registers (H = 128 * NV): x is read once, the weights
 // once per warp, and four rows are in flight per warp.
-template <int NV>
+template <int NV, int R>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_reg_kernel(const float* __restrict__ x, long long sx,
                                                               const float* __restrict__ w, long long sw,
                                                               __nv_bfloat16* __restrict__ y, long long sy,
                                                               float* __restrict__ rstd, int M, int H, int G,
                                                               float eps) {
-  constexpr int R = 4;
   const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32 * R;
   const int lane = threadIdx.x % 32;
   float4 v[R][NV];
@@ -398,11 +397,18 @@ void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
   const bool reg = al16(x.data_ptr()) && al16(w.data_ptr()) && al16(y.data_ptr()) && sx % 4 == 0 && sw % 4 == 0 &&
                    sy % 4 == 0;
   const int nv = (int)(H / 128);
+  // four rows per warp, or one when four would leave fewer than two blocks per SM
+  const bool few = G * M / 32 < 2 * 148;
 #define ODP_RMS_FWD(NV)                                                                                          \
   if (reg && nv == NV) {                                                                                         \
-    odp::rmsnorm_fwd_reg_kernel<NV><<<blocks_for(G * M * 8, 256), 256, 0, st>>>(                                 \
-        x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,    \
-        rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);                                             \
+    if (few)                                                                                                     \
+      odp::rmsnorm_fwd_reg_kernel<NV, 1><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(                           \
+          x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,  \
+          rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);                                           \
+    else                                                                                                         \
+      odp::rmsnorm_fwd_reg_kernel<NV, 4><<<blocks_for(G * M * 8, 256), 256, 0, st>>>(                            \
+          x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,  \
+          rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);                                           \
     C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                              \
     return;                                                                                                      \
   }
