@@ -426,10 +426,9 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
                  int64_t H, int64_t G, double beta) {
   c10::cuda::CUDAGuard guard(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  // rows per block: 32, or 8 when 32-row blocks would not give two blocks per SM (few paths
-  // per GPU) and the partial buffer has room for the extra blocks
-  int rpb = odp::kNormRowsPerBlock;
-  if (G * ((M + 31) / 32) < 2 * 148 && work.numel() >= G * ((M + 7) / 8) * H) rpb = 8;
+  // rows per block (32): 8-row blocks for few paths per GPU were measured slower (4x the
+  // weight-gradient partials to write and reduce outweigh the extra parallelism)
+  const int rpb = odp::kNormRowsPerBlock;
   const int nblk = (int)((M + rpb - 1) / rpb);
   TORCH_CHECK(work.numel() >= G * nblk * H, "rmsnorm_bwd: work buffer too small");
   auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
