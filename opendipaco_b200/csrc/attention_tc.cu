@@ -61,6 +61,7 @@ struct Args {
   float* lse;        // [GB, nh, S] natural-log log-sum-exp of the scaled scores
   const __nv_bfloat16* dout;
   __nv_bfloat16* dqkv;
+  float* delta;      // [GB, nh, S] rowsum(dO o), written by the flash dQ kernel
   float scale;
   int* err;
 };
@@ -540,12 +541,457 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
   if (warp == 0) tmem_dealloc(tm, kCols);
 }
 
+
+// ============================================================================ S > 128
+// Flash-style kernels for sequences longer than one tile (any S >= 1; used for S > 128).
+// Same operand layout, RoPE staging, exponentials and bounded mbarrier waits as above;
+// the sequence is now cut into tiles and the softmax runs online across key tiles.
+//
+// flash_fwd_kernel: one CTA per (128-query tile, head, sequence), 128 threads, thread t
+//   owns query row t. Per 64-key tile j (causal: only keys <= the tile's last query):
+//     S = Q K_j^T             -> TMEM [0, 64)     (M 128, N 64, K 64)
+//     online softmax: m' = max(m, rowmax), alpha = 2^(m - m'), P = 2^(S log2e/sqrt(d) - m')
+//     (bf16, over the P tile), l = alpha l + rowsum P
+//     O_j = P V_j             -> TMEM [64, 128)   (M 128, N 64, K 64), acc = alpha acc + O_j
+//   o = acc / l, lse = (m + log2 l) ln 2. 128 TMEM columns and 48 KB of shared memory:
+//   four CTAs per SM, whose MMAs and softmax phases interleave.
+// flash_bwd_dq_kernel: one CTA per (128-query tile, head, sequence), 256 threads (warp w
+//   reads TMEM lanes 32 (w % 4).., columns half (w / 4) of each tile). It first computes
+//   delta = rowsum(dO o) for its rows (written out for the dK/dV kernel), then per 64-key
+//   tile: S = Q K_j^T, dP = dO V_j^T, dS = P (dP - delta) in shared memory,
+//   dQ += dS K_j in TMEM. dQ is scaled and passed through the transpose of RoPE.
+// flash_bwd_dkv_kernel: one CTA per (128-key tile, kv head, sequence), 256 threads; keys
+//   are the TMEM lanes. For every query head of the kv group and every 64-query tile at
+//   or after the diagonal: S^T = K Q_i^T, dP^T = V dO_i^T, P^T and dS^T = P^T (dP^T -
+//   delta) written as [key][query] tiles, dV += P^T dO_i, dK += dS^T Q_i in TMEM.
+//   Each CTA owns its dK / dV rows: no atomics, deterministic, and dQ comes from its own
+//   kernel (the S / dP products are recomputed there rather than accumulated across
+//   key tiles with atomics).
+// Both backward kernels use 256 TMEM columns and 64 / 80 KB of shared memory: two CTAs
+// per SM.
+
+constexpr int KT = 64;              // keys (forward, dQ) or queries (dK / dV) per inner tile
+constexpr int TILE64 = KT * 128;    // bytes of a [64][64] bf16 tile
+constexpr int kFlashFwdSmem = 2 * TILE + 2 * TILE64 + 1024;
+constexpr int kFlashDqSmem = 3 * TILE + 2 * TILE64 + 1024;
+constexpr int kFlashDkvSmem = 4 * TILE + 2 * TILE64 + 1024;
+
+// Stage rows [r0, r0 + nrows) of 64 columns at col0 of a [S, ld] bf16 matrix into a
+// swizzled tile (tile row r = matrix row r0 + r); rows >= S are zero-filled.
+template <int NT>
+ODP_DEVICE void stage_rows(uint8_t* tile, const __nv_bfloat16* src, long long ld, int col0, int r0, int nrows,
+                           int S) {
+  for (int i = threadIdx.x; i < nrows * 8; i += NT) {
+    const int r = i >> 3, c8 = (i & 7) * 8;
+    uint8_t* dst = tile + sw_off(r, c8);
+    if (r0 + r < S) cp_async16(dst, src + (long long)(r0 + r) * ld + col0 + c8);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// RoPE in place on a staged tile whose row r holds position r0 + r.
+template <int NT>
+ODP_DEVICE void rope_rows(uint8_t* tile, int r0, int nrows, int S, const float* cosT, const float* sinT) {
+  for (int i = threadIdx.x; i < nrows * 4; i += NT) {
+    const int r = i >> 2, j = (i & 3) * 8;
+    const int pos = r0 + r;
+    if (pos >= S) continue;
+    float c0[8], s0[8], c1[8], s1[8];
+    load8f(cosT + (long long)pos * D + j, c0);
+    load8f(sinT + (long long)pos * D + j, s0);
+    load8f(cosT + (long long)pos * D + j + 32, c1);
+    load8f(sinT + (long long)pos * D + j + 32, s1);
+    rope_pair(tile, r, j, c0, s0, c1, s1);
+  }
+}
+
+// Every thread of the CTA: publish shared-memory writes to the tensor core and order the
+// block around tcgen05 operations.
+ODP_DEVICE void publish_smem_sync() {
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+// Thread 0 waits (bounded) for the next completion of `bar`; every thread returns whether
+// all waits so far succeeded.
+ODP_DEVICE bool wait_mma(uint64_t* bar, uint32_t& phase, bool ok, int* err) {
+  if (ok && threadIdx.x == 0) ok = mbar_wait(bar, phase, err, ERR_TIMEOUT_ACCUM);
+  phase ^= 1;
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  return ok;
+}
+
+__global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* sQ = sm;
+  uint8_t* sP = sm + TILE;
+  uint8_t* sK = sm + 2 * TILE;
+  uint8_t* sV = sK + TILE64;
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_holder;
+  const int nqt = (a.S + T - 1) / T;
+  const int qt = nqt - 1 - (int)blockIdx.x;  // longest (latest) query tiles first
+  const int h = blockIdx.y, gb = blockIdx.z;
+  const int warp = threadIdx.x / 32, row = threadIdx.x;
+  const int q0 = qt * T, q = q0 + row;
+  const int kvh = h / (a.nh / a.nkv);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_holder, 128);
+  const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
+  const int kend = min(a.S, q0 + T);  // causal: this tile needs keys [0, kend)
+  const int nkt = (kend + KT - 1) / KT;
+  stage_rows<128>(sQ, base, a.ld, h * D, q0, T, a.S);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_holder;
+  const uint32_t trow = tm + ((uint32_t)(warp * 32) << 16);
+  const uint32_t tS = trow, tO = trow + 64;
+  const float sl2 = a.scale * kLog2e;
+  float acc[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int j = 0; j < nkt && ok; ++j) {
+    const int k0 = j * KT;
+    stage_rows<128>(sK, base, a.ld, (a.nh + kvh) * D, k0, KT, a.S);
+    stage_rows<128>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, k0, KT, a.S);
+    cp_async_wait_all();
+    __syncthreads();
+    if (j == 0) rope_rows<128>(sQ, q0, T, a.S, a.cosT, a.sinT);
+    rope_rows<128>(sK, k0, KT, a.S, a.cosT, a.sinT);
+    publish_smem_sync();
+    if (threadIdx.x == 0) {
+      constexpr uint32_t idS = umma_idesc_bf16(T, KT, false, false);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) umma_bf16(tm, desc_k(smem_u32(sQ), kk), desc_k(smem_u32(sK), kk), idS, kk > 0);
+      umma_commit(&bar);
+    }
+    __syncwarp();
+    ok = wait_mma(&bar, phase, ok, a.err);
+    // valid keys of this row in the tile: k0 + e <= q and k0 + e < S
+    const int nvalid = q < a.S ? max(0, min(KT, min(q + 1, a.S) - k0)) : 0;
+    float tmax = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < KT / 16; ++c) {
+      float v[16];
+      tmem_ld16(tS + c * 16, v);
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (c * 16 + e < nvalid) tmax = fmaxf(tmax, v[e] * sl2);
+    }
+    const float mn = fmaxf(m, tmax);
+    const float alpha = mn == -INFINITY ? 1.f : ex2_fast(m - mn);  // m = -inf -> alpha 0 (acc, l are 0 then)
+    float psum = 0.f;
+#pragma unroll
+    for (int c = 0; c < KT / 16; ++c) {
+      float v[16];
+      tmem_ld16(tS + c * 16, v);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float p = (c * 16 + e < nvalid) ? ex2_fast(v[e] * sl2 - mn) : 0.f;
+        v[e] = p;
+        psum += p;
+      }
+      put16(sP, row, c * 16, v);
+    }
+    l = l * alpha + psum;
+    m = mn;
+    publish_smem_sync();
+    if (threadIdx.x == 0 && ok) {
+      constexpr uint32_t idO = umma_idesc_bf16(T, D, false, true);
+#pragma unroll
+      for (int kk = 0; kk < KT / 16; ++kk)
+        umma_bf16(tm + 64, desc_k(smem_u32(sP), kk), desc_mn(smem_u32(sV), kk), idO, kk > 0);
+      umma_commit(&bar);
+    }
+    __syncwarp();
+    ok = wait_mma(&bar, phase, ok, a.err);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float v[16];
+      tmem_ld16(tO + c * 16, v);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[c * 16 + e] = fmaf(acc[c * 16 + e], alpha, v[e]);
+    }
+    tc_fence_before();
+    __syncthreads();  // every thread is done with S, O_j and the tiles before they are restaged
+    tc_fence_after();
+  }
+  if (ok && q < a.S) {
+    store_row64(a.o + ((long long)gb * a.S + q) * a.ldo + h * D, acc, 1.f / l, nullptr, nullptr, 0, false);
+    a.lse[((long long)gb * a.nh + h) * a.S + q] = (m + log2f(l)) * kLn2;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 128);
+}
+
+__global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* sQ = sm;
+  uint8_t* sdO = sm + TILE;
+  uint8_t* sdS = sm + 2 * TILE;  // [128 queries][64 keys]
+  uint8_t* sK = sm + 3 * TILE;
+  uint8_t* sV = sK + TILE64;
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ float sDelta[T], sLse[T];
+  const int nqt = (a.S + T - 1) / T;
+  const int qt = nqt - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, gb = blockIdx.z;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int quarter = warp % 4, half = warp / 4;
+  const int row = quarter * 32 + lane;
+  const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+  const int q0 = qt * T, q = q0 + row;
+  const int kvh = h / (a.nh / a.nkv);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_holder, 256);
+  const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
+  const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
+  stage_rows<256>(sQ, base, a.ld, h * D, q0, T, a.S);
+  stage_rows<256>(sdO, dobase, a.ldo, h * D, q0, T, a.S);
+  // this thread's O row (threads < 128), for delta = rowsum(dO o), loaded while the tiles stream in
+  uint4 opk[8];
+  const int qr = q0 + (int)threadIdx.x;
+  if (threadIdx.x < T && qr < a.S) {
+    const uint4* op = reinterpret_cast<const uint4*>(a.o + ((long long)gb * a.S + qr) * a.ldo + h * D);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) opk[c] = op[c];
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (threadIdx.x < T) {
+    float dsum = 0.f, l2 = 0.f;
+    if (qr < a.S) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 dv = *reinterpret_cast<const uint4*>(sdO + sw_off(threadIdx.x, c * 8));
+        const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(&dv);
+        const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&opk[c]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dsum += __bfloat162float(x[e]) * __bfloat162float(y[e]);
+      }
+      const long long li = ((long long)gb * a.nh + h) * a.S + qr;
+      l2 = a.lse[li] * kLog2e;
+      a.delta[li] = dsum;
+    }
+    sDelta[threadIdx.x] = dsum;
+    sLse[threadIdx.x] = l2;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_holder;
+  const uint32_t tS = tm, tdP = tm + 64, tdQ = tm + 128;
+  const float sl2 = a.scale * kLog2e;
+  const float delta = sDelta[row], l2 = sLse[row];
+  const int kend = min(a.S, q0 + T);
+  const int nkt = (kend + KT - 1) / KT;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int j = 0; j < nkt && ok; ++j) {
+    const int k0 = j * KT;
+    stage_rows<256>(sK, base, a.ld, (a.nh + kvh) * D, k0, KT, a.S);
+    stage_rows<256>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, k0, KT, a.S);
+    cp_async_wait_all();
+    __syncthreads();
+    if (j == 0) rope_rows<256>(sQ, q0, T, a.S, a.cosT, a.sinT);
+    rope_rows<256>(sK, k0, KT, a.S, a.cosT, a.sinT);
+    publish_smem_sync();
+    if (threadIdx.x == 0) {
+      constexpr uint32_t idS = umma_idesc_bf16(T, KT, false, false);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) umma_bf16(tS, desc_k(smem_u32(sQ), kk), desc_k(smem_u32(sK), kk), idS, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16(tdP, desc_k(smem_u32(sdO), kk), desc_k(smem_u32(sV), kk), idS, kk > 0);
+      umma_commit(&bar);
+    }
+    __syncwarp();
+    ok = wait_mma(&bar, phase, ok, a.err);
+    const int nvalid = q < a.S ? max(0, min(KT, min(q + 1, a.S) - k0)) : 0;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int c0 = half * 32 + c * 16;
+      float s[16], dp[16];
+      tmem_ld16(tS + lane_off + c0, s);
+      tmem_ld16(tdP + lane_off + c0, dp);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float p = (c0 + e < nvalid) ? ex2_fast(s[e] * sl2 - l2) : 0.f;
+        dp[e] = p * (dp[e] - delta);
+      }
+      put16(sdS, row, c0, dp);
+    }
+    publish_smem_sync();
+    if (threadIdx.x == 0 && ok) {
+      constexpr uint32_t idQ = umma_idesc_bf16(T, D, false, true);
+#pragma unroll
+      for (int kk = 0; kk < KT / 16; ++kk)
+        umma_bf16(tdQ, desc_k(smem_u32(sdS), kk), desc_mn(smem_u32(sK), kk), idQ, (j > 0 || kk > 0));
+      umma_commit(&bar);
+    }
+    __syncwarp();
+    ok = wait_mma(&bar, phase, ok, a.err);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  if (half == 0) {
+    float r[64];
+    tmem_row64(tdQ + lane_off, r);
+    if (ok && q < a.S)
+      store_row64(a.dqkv + ((long long)gb * a.S + q) * a.ld + h * D, r, a.scale, a.cosT, a.sinT, q, true);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 256);
+}
+
+__global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* sK = sm;
+  uint8_t* sV = sm + TILE;
+  uint8_t* sPT = sm + 2 * TILE;   // [128 keys][64 queries]
+  uint8_t* sdST = sm + 3 * TILE;  // [128 keys][64 queries]
+  uint8_t* sQ = sm + 4 * TILE;    // [64 queries][64]
+  uint8_t* sdO = sQ + TILE64;
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ float sDelta[KT], sLse[KT];
+  const int kt = blockIdx.x, kvh = blockIdx.y, gb = blockIdx.z;
+  const int grp = a.nh / a.nkv;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int quarter = warp % 4, half = warp / 4;
+  const int row = quarter * 32 + lane;
+  const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+  const int k0 = kt * T, k = k0 + row;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_holder, 256);
+  const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
+  const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
+  stage_rows<256>(sK, base, a.ld, (a.nh + kvh) * D, k0, T, a.S);
+  stage_rows<256>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, k0, T, a.S);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_holder;
+  const uint32_t tS = tm, tdP = tm + 64, tdV = tm + 128, tdK = tm + 192;
+  const float sl2 = a.scale * kLog2e;
+  const int i0 = k0 / KT, nq = (a.S + KT - 1) / KT;  // query tiles at or after the diagonal
+  uint32_t phase = 0;
+  bool ok = true, accumulated = false;
+  for (int hi = 0; hi < grp && ok; ++hi) {
+    const int h = kvh * grp + hi;
+    for (int i = i0; i < nq && ok; ++i) {
+      const int qs = i * KT;
+      stage_rows<256>(sQ, base, a.ld, h * D, qs, KT, a.S);
+      stage_rows<256>(sdO, dobase, a.ldo, h * D, qs, KT, a.S);
+      if (threadIdx.x < KT) {
+        const int qq = qs + (int)threadIdx.x;
+        const long long li = ((long long)gb * a.nh + h) * a.S + qq;
+        sLse[threadIdx.x] = qq < a.S ? a.lse[li] * kLog2e : 0.f;
+        sDelta[threadIdx.x] = qq < a.S ? a.delta[li] : 0.f;
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      if (hi == 0 && i == i0) rope_rows<256>(sK, k0, T, a.S, a.cosT, a.sinT);
+      rope_rows<256>(sQ, qs, KT, a.S, a.cosT, a.sinT);
+      publish_smem_sync();
+      if (threadIdx.x == 0) {
+        constexpr uint32_t idS = umma_idesc_bf16(T, KT, false, false);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tS, desc_k(smem_u32(sK), kk), desc_k(smem_u32(sQ), kk), idS, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tdP, desc_k(smem_u32(sV), kk), desc_k(smem_u32(sdO), kk), idS, kk > 0);
+        umma_commit(&bar);
+      }
+      __syncwarp();
+      ok = wait_mma(&bar, phase, ok, a.err);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int c0 = half * 32 + c * 16;
+        float s[16], dp[16];
+        tmem_ld16(tS + lane_off + c0, s);
+        tmem_ld16(tdP + lane_off + c0, dp);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int qq = qs + c0 + e;
+          const bool valid = k <= qq && qq < a.S && k < a.S;
+          const float p = valid ? ex2_fast(s[e] * sl2 - sLse[c0 + e]) : 0.f;
+          s[e] = p;
+          dp[e] = p * (dp[e] - sDelta[c0 + e]);
+        }
+        put16(sPT, row, c0, s);
+        put16(sdST, row, c0, dp);
+      }
+      publish_smem_sync();
+      if (threadIdx.x == 0 && ok) {
+        constexpr uint32_t idG = umma_idesc_bf16(T, D, false, true);
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk)
+          umma_bf16(tdV, desc_k(smem_u32(sPT), kk), desc_mn(smem_u32(sdO), kk), idG, (accumulated || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk)
+          umma_bf16(tdK, desc_k(smem_u32(sdST), kk), desc_mn(smem_u32(sQ), kk), idG, (accumulated || kk > 0));
+        umma_commit(&bar);
+      }
+      __syncwarp();
+      accumulated = true;
+      ok = wait_mma(&bar, phase, ok, a.err);
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+    }
+  }
+  {
+    float r[64];
+    tmem_row64((half == 0 ? tdK : tdV) + lane_off, r);
+    if (!accumulated) {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) r[i] = 0.f;
+    }
+    if (ok && k < a.S) {
+      __nv_bfloat16* dst = a.dqkv + ((long long)gb * a.S + k) * a.ld;
+      if (half == 0) store_row64(dst + (a.nh + kvh) * D, r, a.scale, a.cosT, a.sinT, k, true);
+      else store_row64(dst + (a.nh + a.nkv + kvh) * D, r, 1.f, nullptr, nullptr, 0, false);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 256);
+}
+
 }  // namespace attn_tc
 }  // namespace odp
 
 static odp::attn_tc::Args tc_args(torch::Tensor qkv, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                                   torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err) {
-  TORCH_CHECK(S >= 1 && S <= odp::attn_tc::T, "tcgen05 attention handles 1 <= S <= 128");
+  TORCH_CHECK(S >= 1, "attention: S >= 1");
   TORCH_CHECK(nh % nkv == 0, "attention: heads must be a multiple of kv heads");
   TORCH_CHECK(qkv.is_contiguous() && o.is_contiguous() && lse.is_contiguous(), "attention: contiguous tensors");
   odp::attn_tc::Args a{};
@@ -567,6 +1013,7 @@ static odp::attn_tc::Args tc_args(torch::Tensor qkv, int64_t S, int64_t nh, int6
 // qkv: [GB, S, (nh+2nkv)*64] bf16 -> o: [GB, S, nh*64] bf16, lse: [GB, nh, S] fp32
 void attention_fwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                       torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err) {
+  TORCH_CHECK(S <= odp::attn_tc::T, "attention_fwd_tc: one-tile kernel, S <= 128 (longer: attention_fwd_flash)");
   c10::cuda::CUDAGuard guard(qkv.device());
   static bool attr = false;
   if (!attr) {
@@ -584,6 +1031,7 @@ void attention_fwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
 void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                       torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout, torch::Tensor dqkv,
                       torch::Tensor err) {
+  TORCH_CHECK(S <= odp::attn_tc::T, "attention_bwd_tc: one-tile kernel, S <= 128 (longer: attention_bwd_flash)");
   c10::cuda::CUDAGuard guard(qkv.device());
   static bool attr = false;
   if (!attr) {
@@ -603,5 +1051,54 @@ void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
     odp::attn_tc::bwd_kernel<true><<<grid, 256, odp::attn_tc::kBwdSmemLean, at::cuda::getCurrentCUDAStream()>>>(a);
   else
     odp::attn_tc::bwd_kernel<false><<<grid, 256, odp::attn_tc::kBwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Any S >= 1 (used for S > 128): qkv [GB, S, (nh+2nkv)*64] bf16 -> o [GB, S, nh*64] bf16,
+// lse [GB, nh, S] fp32.
+void attention_fwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                         torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        odp::attn_tc::kFlashFwdSmem));
+    attr = true;
+  }
+  TORCH_CHECK(cosT.size(0) >= S && sinT.size(0) >= S, "attention: RoPE tables shorter than S");
+  auto a = tc_args(qkv, S, nh, nkv, cosT, sinT, o, lse, err);
+  const unsigned nqt = (unsigned)((S + odp::attn_tc::T - 1) / odp::attn_tc::T);
+  dim3 grid(nqt, (unsigned)nh, (unsigned)GB);
+  odp::attn_tc::flash_fwd_kernel<<<grid, 128, odp::attn_tc::kFlashFwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Backward for any S >= 1: dQ (and delta = rowsum(dO o) into `delta` [GB, nh, S]), then
+// dK / dV, both into dqkv [GB, S, (nh+2nkv)*64] (gradients w.r.t. the pre-RoPE q|k|v).
+void attention_bwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                         torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout,
+                         torch::Tensor delta, torch::Tensor dqkv, torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::flash_bwd_dq_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, odp::attn_tc::kFlashDqSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::attn_tc::flash_bwd_dkv_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, odp::attn_tc::kFlashDkvSmem));
+    attr = true;
+  }
+  TORCH_CHECK(dout.is_contiguous() && dqkv.is_contiguous() && delta.is_contiguous(), "attention: contiguous tensors");
+  TORCH_CHECK(delta.numel() >= GB * nh * S && delta.scalar_type() == at::kFloat, "attention: delta [GB, nh, S] fp32");
+  TORCH_CHECK(cosT.size(0) >= S && sinT.size(0) >= S, "attention: RoPE tables shorter than S");
+  auto a = tc_args(qkv, S, nh, nkv, cosT, sinT, o, lse, err);
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  a.delta = delta.data_ptr<float>();
+  auto st = at::cuda::getCurrentCUDAStream();
+  const unsigned nt = (unsigned)((S + odp::attn_tc::T - 1) / odp::attn_tc::T);
+  odp::attn_tc::flash_bwd_dq_kernel<<<dim3(nt, (unsigned)nh, (unsigned)GB), 256, odp::attn_tc::kFlashDqSmem, st>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  odp::attn_tc::flash_bwd_dkv_kernel<<<dim3(nt, (unsigned)nkv, (unsigned)GB), 256, odp::attn_tc::kFlashDkvSmem,
+                                       st>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -9,6 +9,8 @@ void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tenso
                c10::optional<torch::Tensor> sq_part, int64_t sq_ld);
 void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor y, int64_t sy,
                  torch::Tensor rstd, int64_t M, int64_t H, int64_t G, double eps);
+void rmsnorm_fwd_rpw(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor y, int64_t sy,
+                     torch::Tensor rstd, int64_t M, int64_t H, int64_t G, double eps, int64_t rows_per_warp);
 void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor rstd, torch::Tensor dy,
                  int64_t sdy, c10::optional<torch::Tensor> dres, torch::Tensor dx, int64_t sdx,
                  c10::optional<torch::Tensor> dx16, torch::Tensor dw, int64_t sdw, torch::Tensor work, int64_t M,
@@ -35,6 +37,11 @@ void attention_fwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
 void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                       torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout, torch::Tensor dqkv,
                       torch::Tensor err);
+void attention_fwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                         torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err);
+void attention_bwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
+                         torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout,
+                         torch::Tensor delta, torch::Tensor dqkv, torch::Tensor err);
 void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t M, int64_t V, int64_t G,
               torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum, torch::Tensor inv_count,
               c10::optional<torch::Tensor> loss_out, torch::Tensor err, c10::optional<torch::Tensor> inv_given);
@@ -80,6 +87,7 @@ void outer_nvlink_quant(torch::Tensor regs, int64_t nregs, int64_t total_groups,
 void outer_nvlink_bcast(torch::Tensor cps, int64_t ncp, int64_t total_chunks, torch::Tensor pads, int64_t rank,
                         int64_t world, int64_t epoch, torch::Tensor err);
 int64_t outer_nvlink_chunk_elems();
+int64_t set_peer_wait_ns(int64_t ns);
 std::vector<torch::Tensor> quant_int4(torch::Tensor x, bool want_resid);
 void dequant_int4(torch::Tensor packed, torch::Tensor scale, int64_t n, int64_t g, torch::Tensor out, double w,
                   bool accumulate);
@@ -94,12 +102,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_splitk_reduce", &gemm_splitk_reduce);
   m.def("grad_clip_coef_parts", &grad_clip_coef_parts);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_fwd_rpw", &rmsnorm_fwd_rpw);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("attention_fwd", &attention_fwd);
   m.def("attention_bwd", &attention_bwd);
   m.def("attention_fwd_tc", &attention_fwd_tc);
+  m.def("attention_fwd_flash", &attention_fwd_flash);
+  m.def("attention_bwd_flash", &attention_bwd_flash);
   m.def("ce_fused", &ce_fused);
   m.def("embedding_bwd_sorted", &embedding_bwd_sorted);
   m.def("dp_barrier", &dp_barrier);
@@ -120,6 +131,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("outer_nvlink_apply", &outer_nvlink_apply);
   m.def("outer_nvlink_bcast", &outer_nvlink_bcast);
   m.def("outer_nvlink_chunk_elems", &outer_nvlink_chunk_elems);
+  m.def("set_peer_wait_ns", &set_peer_wait_ns);
   m.def("quant_int4", &quant_int4);
   m.def("dequant_int4", &dequant_int4);
   m.def("quant_int8", &quant_int8);

@@ -87,11 +87,13 @@ int reject(int code, const char* why) {
   return code;
 }
 
-// True when `p` is device (or managed) memory of device `dev`.
+// True when `p` is device (or managed) memory of device `dev`. Called only once the entry
+// point has checked that no earlier error was pending, so an error left behind here was
+// recorded by this query and is the one to clear.
 bool on_device(const void* p, int dev) {
   cudaPointerAttributes a{};
   if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-    cudaGetLastError();  // drop the error this failed query recorded
+    cudaGetLastError();
     return false;
   }
   return (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) && a.device == dev;
@@ -127,10 +129,18 @@ extern "C" int odp_grad_clip_coef_noalloc(const float* grads, long long P, long 
     return reject(ODP_NOALLOC_ETOO_LONG, "P is above 4096 * 65536 elements per path");
   if ((reinterpret_cast<uintptr_t>(grads) & 15u) != 0 || (stride & 3) != 0)
     return reject(ODP_NOALLOC_EALIGN, "grads must be 16-byte aligned and stride a multiple of 4");
+  // An error an earlier call left pending is returned as it is (and left pending): the
+  // caller sees its own failure, and the launch checks below report only these launches.
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) return (int)e;
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
   if (dev < 0 || dev >= kMaxDevices) return reject(ODP_NOALLOC_EDEVICE, "device ordinal above 63");
+  int stream_dev = dev;
+  e = cudaStreamGetDevice(stream, &stream_dev);
+  if (e != cudaSuccess) return (int)e;
+  if (stream_dev != dev) return reject(ODP_NOALLOC_EDEVICE, "the stream belongs to another device than the current one");
   if (!on_device(grads, dev) || !on_device(coef, dev) || (norm_out != nullptr && !on_device(norm_out, dev)))
     return reject(ODP_NOALLOC_EDEVICE, "grads, coef and norm_out must be memory of the current device");
   float* scratch = nullptr;

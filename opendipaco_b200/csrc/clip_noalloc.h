@@ -24,7 +24,14 @@
 //
 // Set-up: the first call on each device looks up the device address of the scratch
 // array (cudaGetSymbolAddress) with that device current. Make that first call before
-// any stream capture begins on that device.
+// any stream capture begins on that device. The address is cached for the life of the
+// process: it assumes the device's primary context lives that long. After a
+// cudaDeviceReset (or any teardown of the primary context) the cached address is stale
+// and the entry point must not be called again in that process.
+//
+// Errors: an error already pending on the calling thread (cudaPeekAtLastError) is
+// returned unchanged before anything is done, and stays pending. `stream` must belong to
+// the current device (cudaStreamGetDevice), else ODP_NOALLOC_EDEVICE.
 //
 // Sharing: every call on a device uses the same scratch array, and the array keeps what
 // the last call left in it. Each call overwrites every scratch slot it later reads, so

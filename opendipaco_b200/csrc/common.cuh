@@ -31,6 +31,15 @@ enum ErrCode : int {
 // Default bound of any single wait: 2 s of wall time (a healthy wait is < 1 ms).
 constexpr unsigned long long kWaitBoundNs = 2000000000ull;
 
+// Bound of the waits on flags that OTHER GPUs write (cross-GPU barriers of the outer step
+// and of intra-path data parallelism). Host state of this library (one value per process),
+// passed to every such kernel as a launch argument, so a launch captured in a CUDA graph
+// keeps the bound it was captured with. Set through `set_peer_wait_ns`.
+inline unsigned long long& peer_wait_bound_ns() {
+  static unsigned long long v = kWaitBoundNs;
+  return v;
+}
+
 ODP_DEVICE unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -23,7 +23,8 @@
 //
 // Barriers compare monotonically increasing per-member counters kept in device memory,
 // so the sequence is valid inside a CUDA graph replayed many times. Every wait is
-// bounded: on timeout the kernel records ERR_TIMEOUT_PEER and returns.
+// bounded by the launch argument `bound_ns` (peer_wait_bound_ns, 2 s by default): on
+// timeout the kernel records ERR_TIMEOUT_PEER and returns.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -64,7 +65,8 @@ ODP_DEVICE T* row_ptr(const long long* tab, int row, int member) {
 
 // Thread 0 only. pad (uint32 [kMaxMembers]) of every member holds the last counter value
 // each member published; counter (uint32, this member's device memory) counts barriers.
-ODP_DEVICE bool group_barrier(const long long* tab, unsigned* counter, int me, int d, int* err) {
+ODP_DEVICE bool group_barrier(const long long* tab, unsigned* counter, int me, int d, int* err,
+                              unsigned long long bound_ns) {
   const unsigned v = *counter + 1;
   *counter = v;
   __threadfence_system();  // this member's earlier peer and local stores precede the signal
@@ -73,7 +75,7 @@ ODP_DEVICE bool group_barrier(const long long* tab, unsigned* counter, int me, i
   const unsigned long long t0 = globaltimer();
   for (int p = 0; p < d; ++p) {
     while ((int)(ld_acquire_sys(mine + p) - v) < 0) {
-      if (globaltimer() - t0 > kWaitBoundNs) {
+      if (globaltimer() - t0 > bound_ns) {
         record_error(err, ERR_TIMEOUT_PEER);
         return false;
       }
@@ -82,8 +84,9 @@ ODP_DEVICE bool group_barrier(const long long* tab, unsigned* counter, int me, i
   return true;
 }
 
-__global__ void barrier_kernel(const long long* tab, unsigned* counter, int me, int d, int* err) {
-  if (threadIdx.x == 0) group_barrier(tab, counter, me, d, err);
+__global__ void barrier_kernel(const long long* tab, unsigned* counter, int me, int d, int* err,
+                               unsigned long long bound_ns) {
+  if (threadIdx.x == 0) group_barrier(tab, counter, me, d, err, bound_ns);
 }
 
 // grid (nblk, G): block b of path g covers [s0 + b * kBlockElems, ...) of the shard.
@@ -121,7 +124,8 @@ __global__ void __launch_bounds__(256) grad_reduce_kernel(const long long* tab, 
 // One CTA: shard sums of squares -> every member's NORM[me][g]; barrier; global norm.
 __global__ void __launch_bounds__(256) norm_kernel(const long long* tab, unsigned* counter, int me, int d, int G,
                                                     const float* __restrict__ part, int nblk, float max_norm,
-                                                    float* __restrict__ coef, float* __restrict__ gnorm, int* err) {
+                                                    float* __restrict__ coef, float* __restrict__ gnorm, int* err,
+                                                    unsigned long long bound_ns) {
   __shared__ float red[256];
   __shared__ int ok;
   for (int g = 0; g < G; ++g) {
@@ -136,7 +140,7 @@ __global__ void __launch_bounds__(256) norm_kernel(const long long* tab, unsigne
     if (threadIdx.x < d) row_ptr<float>(tab, NORM, threadIdx.x)[me * G + g] = red[0];
     __syncthreads();
   }
-  if (threadIdx.x == 0) ok = group_barrier(tab, counter, me, d, err) ? 1 : 0;
+  if (threadIdx.x == 0) ok = group_barrier(tab, counter, me, d, err, bound_ns) ? 1 : 0;
   __syncthreads();
   if (!ok) return;
   const float* mine = row_ptr<const float>(tab, NORM, me);
@@ -267,14 +271,15 @@ __global__ void adam8bit_kernel(const long long* tab, int me, int d, int G, long
 
 static const long long* tab_ptr(torch::Tensor tab) {
   TORCH_CHECK(tab.is_cuda() && tab.scalar_type() == at::kLong && tab.numel() == odp::dp::NROWS * odp::dp::kMaxMembers,
-              "dp: pointer table must be int64 [7][8] on the device");
+              "dp: pointer table must be int64 [12][8] on the device");
   return reinterpret_cast<const long long*>(tab.data_ptr<int64_t>());
 }
 
 void dp_barrier(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, torch::Tensor err) {
   TORCH_CHECK(d >= 1 && d <= odp::dp::kMaxMembers && me >= 0 && me < d, "dp_barrier: bad group");
   odp::dp::barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      tab_ptr(tab), reinterpret_cast<unsigned*>(counter.data_ptr<int>()), (int)me, (int)d, err.data_ptr<int>());
+      tab_ptr(tab), reinterpret_cast<unsigned*>(counter.data_ptr<int>()), (int)me, (int)d, err.data_ptr<int>(),
+      odp::peer_wait_bound_ns());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -289,14 +294,14 @@ void dp_grad_reduce_norm(torch::Tensor tab, torch::Tensor counter, int64_t me, i
   auto st = at::cuda::getCurrentCUDAStream();
   const long long* t = tab_ptr(tab);
   unsigned* cnt = reinterpret_cast<unsigned*>(counter.data_ptr<int>());
-  odp::dp::barrier_kernel<<<1, 32, 0, st>>>(t, cnt, (int)me, (int)d, err.data_ptr<int>());
+  odp::dp::barrier_kernel<<<1, 32, 0, st>>>(t, cnt, (int)me, (int)d, err.data_ptr<int>(), odp::peer_wait_bound_ns());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::dp::grad_reduce_kernel<<<dim3(nblk, (unsigned)G), 256, 0, st>>>(t, (int)me, (int)d, P, stride, s0, s1, nblk,
                                                                        part.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::dp::norm_kernel<<<1, 256, 0, st>>>(t, cnt, (int)me, (int)d, (int)G, part.data_ptr<float>(), nblk,
                                            (float)max_norm, coef.data_ptr<float>(), gnorm.data_ptr<float>(),
-                                           err.data_ptr<int>());
+                                           err.data_ptr<int>(), odp::peer_wait_bound_ns());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -314,7 +319,7 @@ void dp_adamw(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, i
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   odp::dp::barrier_kernel<<<1, 32, 0, st>>>(t, reinterpret_cast<unsigned*>(counter.data_ptr<int>()), (int)me,
-                                            (int)d, err.data_ptr<int>());
+                                            (int)d, err.data_ptr<int>(), odp::peer_wait_bound_ns());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -335,6 +340,6 @@ void dp_adam8bit(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   odp::dp::barrier_kernel<<<1, 32, 0, st>>>(t, reinterpret_cast<unsigned*>(counter.data_ptr<int>()), (int)me,
-                                            (int)d, err.data_ptr<int>());
+                                            (int)d, err.data_ptr<int>(), odp::peer_wait_bound_ns());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -388,17 +388,20 @@ __global__ void embed_runs_kernel(const unsigned* __restrict__ keys, const float
 
 static inline int blocks_for(long long threads, int per) { return (int)((threads + per - 1) / per); }
 
-void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor y, int64_t sy,
-                 torch::Tensor rstd, int64_t M, int64_t H, int64_t G, double eps) {
+// rows_per_warp: 1 or 4 forces the register-resident variant's rows per warp; 0 chooses
+// four rows per warp, or one when four would leave fewer than two blocks per SM.
+void rmsnorm_fwd_rpw(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor y, int64_t sy,
+                     torch::Tensor rstd, int64_t M, int64_t H, int64_t G, double eps, int64_t rows_per_warp) {
   TORCH_CHECK(H % 128 == 0, "rmsnorm: hidden size must be a multiple of 128");
+  TORCH_CHECK(rows_per_warp == 0 || rows_per_warp == 1 || rows_per_warp == 4, "rmsnorm: rows_per_warp is 0, 1 or 4");
   c10::cuda::CUDAGuard guard(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
   auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   const bool reg = al16(x.data_ptr()) && al16(w.data_ptr()) && al16(y.data_ptr()) && sx % 4 == 0 && sw % 4 == 0 &&
                    sy % 4 == 0;
   const int nv = (int)(H / 128);
-  // four rows per warp, or one when four would leave fewer than two blocks per SM
-  const bool few = G * M / 32 < 2 * 148;
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  const bool few = rows_per_warp ? rows_per_warp == 1 : G * M / 32 < 2 * sms;
 #define ODP_RMS_FWD(NV)                                                                                          \
   if (reg && nv == NV) {                                                                                         \
     if (few)                                                                                                     \
@@ -418,6 +421,11 @@ void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
       x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,
       rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rmsnorm_fwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor y, int64_t sy,
+                 torch::Tensor rstd, int64_t M, int64_t H, int64_t G, double eps) {
+  rmsnorm_fwd_rpw(x, sx, w, sw, y, sy, rstd, M, H, G, eps, 0);
 }
 
 void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch::Tensor rstd, torch::Tensor dy,

@@ -35,8 +35,9 @@
 // pairs in symmetric buffers; the dropped entries stay in the residual. APPLY then adds
 // the sharers' pairs of its block into a zeroed shared-memory block, sharer by sharer
 // (deterministic), and runs the same update. Key regions and slices are 4096-aligned in
-// this mode, so an APPLY chunk is exactly one block. Waits never spin forever: after kWaitBoundNs they
-// record ERR_TIMEOUT_PEER and the kernel returns.
+// this mode, so an APPLY chunk is exactly one block. Waits never spin forever: after the
+// bound passed at launch (peer_wait_bound_ns, 2 s by default) they record ERR_TIMEOUT_PEER
+// and the kernel returns.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -76,7 +77,7 @@ ODP_DEVICE float4 ld_cg4(const float* p) {
 // Publish `epoch` on channel `ch` of every rank's pad, then wait for all ranks.
 // pads[r] points at rank r's pad: uint32 [2][world]. Returns false on timeout.
 ODP_DEVICE bool cross_gpu_barrier(const unsigned long long* pads, int rank, int world, int ch, unsigned epoch,
-                                  int* err, bool publish) {
+                                  int* err, bool publish, unsigned long long bound_ns) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     if (publish) {
@@ -91,7 +92,7 @@ ODP_DEVICE bool cross_gpu_barrier(const unsigned long long* pads, int rank, int 
     unsigned long long t0 = globaltimer();
     for (int r = 0; r < world; ++r) {
       while (ld_acquire_sys(mine + r) < epoch) {
-        if (globaltimer() - t0 > kWaitBoundNs) {
+        if (globaltimer() - t0 > bound_ns) {
           record_error(err, ERR_TIMEOUT_PEER);
           ok = 0;
           break;
@@ -305,8 +306,9 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
                                           int rank, int world, unsigned epoch, float lr, float m, int nesterov,
                                           int first, float* __restrict__ sq_part, int* err,
                                           const unsigned long long* __restrict__ qd_ptrs,
-                                          const unsigned long long* __restrict__ qs_ptrs, int kcap) {
-  if (!cross_gpu_barrier(pads, rank, world, 0, epoch, err, blockIdx.x == 0)) return;
+                                          const unsigned long long* __restrict__ qs_ptrs, int kcap,
+                                          unsigned long long wait_ns) {
+  if (!cross_gpu_barrier(pads, rank, world, 0, epoch, err, blockIdx.x == 0, wait_ns)) return;
   __shared__ float red[8];
   __shared__ __align__(16) float dense[kNvChunk];  // top-k mode: this chunk's summed pairs
   for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
@@ -434,8 +436,8 @@ struct NvCopy {
 
 __global__ void outer_nvlink_bcast_kernel(const NvCopy* __restrict__ cps, int ncp, long long total_chunks,
                                           const unsigned long long* __restrict__ pads, int rank, int world,
-                                          unsigned epoch, int* err) {
-  if (!cross_gpu_barrier(pads, rank, world, 1, epoch, err, blockIdx.x == 0)) return;
+                                          unsigned epoch, int* err, unsigned long long wait_ns) {
+  if (!cross_gpu_barrier(pads, rank, world, 1, epoch, err, blockIdx.x == 0, wait_ns)) return;
   for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
     int lo = 0, hi = ncp - 1;
     while (lo < hi) {
@@ -474,7 +476,8 @@ void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks,
       (unsigned)epoch, (float)lr, (float)m, nesterov ? 1 : 0, first ? 1 : 0, sq_part.data_ptr<float>(),
       err.data_ptr<int>(),
       qd_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qd_ptrs->data_ptr()) : nullptr,
-      qs_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qs_ptrs->data_ptr()) : nullptr, (int)kcap);
+      qs_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qs_ptrs->data_ptr()) : nullptr, (int)kcap,
+      odp::peer_wait_bound_ns());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -514,8 +517,16 @@ void outer_nvlink_bcast(torch::Tensor cps, int64_t ncp, int64_t total_chunks, to
   odp::outer_nvlink_bcast_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const odp::NvCopy*>(cps.data_ptr()), (int)ncp, total_chunks,
       reinterpret_cast<const unsigned long long*>(pads.data_ptr()), (int)rank, (int)world, (unsigned)epoch,
-      err.data_ptr<int>());
+      err.data_ptr<int>(), odp::peer_wait_bound_ns());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 int64_t outer_nvlink_chunk_elems() { return odp::kNvChunk; }
+
+// Sets the bound of every later cross-GPU wait (outer step and intra-path data
+// parallelism) in nanoseconds; 0 restores the 2 s default. Returns the previous bound.
+int64_t set_peer_wait_ns(int64_t ns) {
+  const int64_t old = (int64_t)odp::peer_wait_bound_ns();
+  odp::peer_wait_bound_ns() = ns > 0 ? (unsigned long long)ns : odp::kWaitBoundNs;
+  return old;
+}

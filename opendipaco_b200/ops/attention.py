@@ -1,8 +1,17 @@
-"""Causal GQA attention with fused RoPE, head_dim 64.
+"""Causal GQA attention with fused RoPE, head_dim 64, on the tcgen05 tensor cores.
 
-Two kernel families: ``csrc/attention_tc.cu`` (tcgen05 + TMEM, one 128-row tile per
-(sequence, head): used whenever S <= 128) and ``csrc/attention.cu`` (mma.sync, 64-row
-blocks, any S that is a multiple of 64). ``ODP_ATTN_IMPL=mma`` forces the latter.
+Two kernel families in ``csrc/attention_tc.cu``, both tcgen05 + TMEM with RoPE applied
+while the tiles are staged:
+
+* S <= 128: one 128-row tile per (sequence, head) (``attention_{fwd,bwd}_tc``);
+* S > 128: flash kernels (``attention_{fwd,bwd}_flash``) -- online softmax over 64-key
+  tiles in the forward, a dQ kernel (which also writes delta = rowsum(dO o)) and an
+  atomic-free dK / dV kernel in the backward.
+
+``ODP_ATTN_IMPL=mma`` selects the older ``mma.sync`` kernels of ``csrc/attention.cu``
+(S a multiple of 64) instead, for comparison only; no training path uses them otherwise.
+The reference computes the same op with ``F.scaled_dot_product_attention(is_causal=True)``
+after HF-style RoPE (``src/opendipaco/modules.py:38``).
 """
 
 from __future__ import annotations
@@ -16,25 +25,39 @@ from ._ext import err_word, ext
 TC_MAX_S = 128
 
 
+def impl_for(S: int) -> str:
+    """Kernel family used for sequence length S: "tc" (one tile), "flash" or "mma"."""
+    if os.environ.get("ODP_ATTN_IMPL", "auto") == "mma":
+        return "mma"
+    return "tc" if S <= TC_MAX_S else "flash"
+
+
 def use_tc(S: int) -> bool:
-    impl = os.environ.get("ODP_ATTN_IMPL", "auto")
-    return impl != "mma" and S <= TC_MAX_S
+    return impl_for(S) != "mma"
 
 
 def fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, err=None) -> None:
     """Launch the forward kernel on preallocated outputs (no allocation)."""
-    if use_tc(S):
-        ext().attention_fwd_tc(qkv, GB, S, nh, nkv, cos, sin, o, lse, err if err is not None else err_word(qkv.device))
+    impl = impl_for(S)
+    e = err if err is not None else err_word(qkv.device)
+    if impl == "tc":
+        ext().attention_fwd_tc(qkv, GB, S, nh, nkv, cos, sin, o, lse, e)
+    elif impl == "flash":
+        ext().attention_fwd_flash(qkv, GB, S, nh, nkv, cos, sin, o, lse, e)
     else:
         ext().attention_fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse)
 
 
 def bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv, err=None) -> None:
-    """Launch the backward kernels on preallocated buffers (``delta`` is scratch of the
-    mma.sync path; the tcgen05 path computes it in the kernel)."""
-    if use_tc(S):
-        ext().attention_bwd_tc(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, dqkv,
-                               err if err is not None else err_word(qkv.device))
+    """Launch the backward kernels on preallocated buffers. ``delta`` [GB, nh, S] fp32
+    receives rowsum(dO o) (flash and mma paths); the one-tile kernel computes it in
+    registers and leaves ``delta`` untouched."""
+    impl = impl_for(S)
+    e = err if err is not None else err_word(qkv.device)
+    if impl == "tc":
+        ext().attention_bwd_tc(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, dqkv, e)
+    elif impl == "flash":
+        ext().attention_bwd_flash(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv, e)
     else:
         ext().attention_bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv)
 
@@ -42,7 +65,7 @@ def bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv, err=None) -> N
 def attention_fwd(qkv: torch.Tensor, nh: int, nkv: int, cos: torch.Tensor, sin: torch.Tensor):
     """qkv: [B, S, (nh+2nkv)*64] bf16 (q|k|v, pre-RoPE) -> (o [B, S, nh*64] bf16, lse [B, nh, S])."""
     B, S, C = qkv.shape
-    assert C == (nh + 2 * nkv) * 64 and (S <= TC_MAX_S or S % 64 == 0)
+    assert C == (nh + 2 * nkv) * 64 and (impl_for(S) != "mma" or S % 64 == 0)
     o = torch.empty(B, S, nh * 64, device=qkv.device, dtype=torch.bfloat16)
     lse = torch.empty(B, nh, S, device=qkv.device, dtype=torch.float32)
     fwd(qkv, B, S, nh, nkv, cos, sin, o, lse)

@@ -69,13 +69,23 @@ def mm_tt(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, bn: int | N
     return c
 
 
-def splitk_factor(M: int, N: int, K: int, G: int, sms: int = 148) -> int:
+def sm_count(device=None) -> int:
+    """Streaming multiprocessors of ``device`` (the current CUDA device by default); 148,
+    a full B200, when no device is visible (CPU-side planning)."""
+    if not torch.cuda.is_available():
+        return 148
+    d = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return torch.cuda.get_device_properties(d).multi_processor_count
+
+
+def splitk_factor(M: int, N: int, K: int, G: int, sms: int | None = None) -> int:
     """Number of K splits for a weight-gradient GEMM whose 128 x 128 output tiles leave
     most SMs idle: doubled while the split grid still fits one wave and each split keeps
     at least 384 of K in whole 64-wide k-blocks (``ODP_SPLITK`` forces a value). Only
     grids of at most an eighth of the SMs are split: measured at 2 paths per GPU, the
     extra reduction launch (~8 us) cancels the gain for grids of 48-54 tiles, while the
     18-tile attention-output gradient goes from 27 to 15 us."""
+    sms = sm_count() if sms is None else sms
     forced = os.environ.get("ODP_SPLITK")
     tiles = G * ((M + 127) // 128) * ((N + 127) // 128)
     s = 1

@@ -124,6 +124,9 @@ class FusedExecutor:
         if bb.hidden_size % 128:
             raise ValueError("the fused executor needs hidden_size % 128 == 0")
         self.dev = engine.device
+        from ..ops.gemm import sm_count
+
+        self.sms = sm_count(self.dev)
         self.topo = engine.topology
         self.paths: list[Path] = list(engine.backend.owned_paths())
         self.G = len(self.paths)
@@ -317,7 +320,7 @@ class FusedExecutor:
         self.wg_shapes = {"lm": (V, H)}
         for i in range(L):
             self.wg_shapes.update({f"down{i}": (H, Fd), f"gu{i}": (2 * Fd, H), f"o{i}": (H, H), f"qkv{i}": (C, H)})
-        self.wg_split = {k: splitk_factor(m, n, M, G) for k, (m, n) in self.wg_shapes.items()}
+        self.wg_split = {k: splitk_factor(m, n, M, G, self.sms) for k, (m, n) in self.wg_shapes.items()}
         ws = max([G * sp * self.wg_shapes[k][0] * self.wg_shapes[k][1] for k, sp in self.wg_split.items()
                   if sp > 1] or [1])
         self.WGWS = z(ws)
@@ -366,9 +369,10 @@ class FusedExecutor:
 
     # ------------------------------------------------------------------ GEMM helper
     def _bn(self, M: int, N: int) -> int:
-        # 128-wide tiles once they fill two thirds of a wave of 148 SMs; 64-wide below that
+        # 128-wide tiles once they fill about two thirds of a wave (100 tiles on 148 SMs);
+        # 64-wide below that
         tiles128 = self.G * ((M + 127) // 128) * ((N + 127) // 128)
-        return 128 if tiles128 >= 100 else 64
+        return 128 if tiles128 * 148 >= 100 * self.sms else 64
 
     def _sq(self, name: str) -> dict:
         """GEMM keyword arguments that make a weight-gradient GEMM write its box sums of

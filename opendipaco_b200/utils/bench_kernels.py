@@ -61,9 +61,14 @@ def bench_attention(GB: int, S: int, nh: int, nkv: int, reps: int, flush) -> lis
     delta = torch.empty(GB, nh, S, device=dev)
     dqkv = torch.empty_like(qkv)
     out = []
+    # causal attention FLOPs: forward Q K^T and P V over the lower triangle (S (S + 1) / 2
+    # scores per head), backward five such products (S, dP, dV, dK, dQ)
+    tri = GB * nh * S * (S + 1) / 2
+    fwd_flops, bwd_flops = 2 * 2 * tri * D, 5 * 2 * tri * D
+    tf, _, lab = _peaks()
     for impl in ("auto", "mma"):
         os.environ["ODP_ATTN_IMPL"] = impl
-        name = "tcgen05" if attn.use_tc(S) else "mma.sync"
+        name = {"tc": "tcgen05 one-tile", "flash": "tcgen05 flash", "mma": "mma.sync"}[attn.impl_for(S)]
         f = _timeit(lambda: attn.fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse), reps, flush)
         b = _timeit(lambda: attn.bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, do, delta, dqkv), reps, flush)
         check_errors()
@@ -71,9 +76,11 @@ def bench_attention(GB: int, S: int, nh: int, nkv: int, reps: int, flush) -> lis
         fb = qkv.numel() * 2 + o.numel() * 2 + lse.numel() * 4
         bb = qkv.numel() * 4 + o.numel() * 4 + lse.numel() * 4
         out.append({"kernel": f"attention_fwd[{name}]", "ms": round(f, 4), "GBps": round(fb / f / 1e6, 1),
-                    "shape": [GB, S, nh, nkv]})
+                    "TFLOPs": round(fwd_flops / f / 1e9, 1),
+                    f"frac_of_{lab}_bf16_peak": round(fwd_flops / f / 1e9 / tf, 3), "shape": [GB, S, nh, nkv]})
         out.append({"kernel": f"attention_bwd[{name}]", "ms": round(b, 4), "GBps": round(bb / b / 1e6, 1),
-                    "shape": [GB, S, nh, nkv]})
+                    "TFLOPs": round(bwd_flops / b / 1e9, 1),
+                    f"frac_of_{lab}_bf16_peak": round(bwd_flops / b / 1e9 / tf, 3), "shape": [GB, S, nh, nkv]})
     os.environ.pop("ODP_ATTN_IMPL", None)
     return out
 

@@ -99,3 +99,63 @@ def test_tc_attention_is_deterministic(monkeypatch):
     b = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+# ---------------------------------------------------------------- S > 128: flash kernels
+def _lse_ref(qkv, nh, nkv, cos, sin):
+    B, S, _ = qkv.shape
+    q = _rope(qkv.float()[..., :nh * D].view(B, S, nh, D).transpose(1, 2), cos, sin)
+    k = _rope(qkv.float()[..., nh * D:(nh + nkv) * D].view(B, S, nkv, D).transpose(1, 2), cos, sin)
+    s = (q @ k.repeat_interleave(nh // nkv, 1).transpose(-1, -2)) / D ** 0.5
+    s = s.masked_fill(torch.ones(S, S, device=DEV, dtype=torch.bool).triu(1), float("-inf"))
+    return torch.logsumexp(s, -1)
+
+
+@pytest.mark.parametrize("B,S,nh,nkv", [(1, 256, 32, 8), (1, 512, 32, 8), (1, 1024, 32, 8), (2, 200, 4, 1),
+                                        (2, 320, 6, 6)])
+def test_flash_attention_matches_fp32_reference(B, S, nh, nkv, monkeypatch):
+    """Long sequences (GQA 32 query / 8 kv heads as in the 1B Llama shape, a ragged S = 200
+    with one kv head, a 64-multiple S = 320 without GQA) against fp32 SDPA."""
+    from opendipaco_b200.models.llama import rope_cos_sin
+    from opendipaco_b200.ops.attention import impl_for
+
+    assert impl_for(S) == "flash"
+    cos, sin = rope_cos_sin(D, 10000.0, S, DEV)
+    qkv = _bf(B, S, (nh + 2 * nkv) * D, seed=S + nh)
+    do = _bf(B, S, nh * D, seed=S + nh + 1)
+    o, lse, dqkv = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    x, ref = _reference(qkv, nh, nkv, cos, sin)
+    _close(o, ref, 2e-2)
+    _close(lse, _lse_ref(qkv, nh, nkv, cos, sin), 1e-2)
+    ref.backward(do.float())
+    _close(dqkv, x.grad, 3e-2)
+    # each of q, k and v gradients on its own scale (k and v sum over GQA heads)
+    for lo, hi in ((0, nh * D), (nh * D, (nh + nkv) * D), ((nh + nkv) * D, (nh + 2 * nkv) * D)):
+        _close(dqkv[..., lo:hi], x.grad[..., lo:hi], 3e-2)
+
+
+def test_flash_attention_matches_mma_kernels(monkeypatch):
+    from opendipaco_b200.models.llama import rope_cos_sin
+
+    B, S, nh, nkv = 2, 512, 8, 2
+    cos, sin = rope_cos_sin(D, 10000.0, S, DEV)
+    qkv = _bf(B, S, (nh + 2 * nkv) * D, seed=11)
+    do = _bf(B, S, nh * D, seed=12)
+    o1, l1, d1 = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    o2, l2, d2 = _run("mma", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    _close(o1, o2, 1e-2)
+    _close(l1, l2, 1e-4)
+    _close(d1, d2, 2e-2)
+
+
+def test_flash_attention_is_deterministic(monkeypatch):
+    from opendipaco_b200.models.llama import rope_cos_sin
+
+    B, S, nh, nkv = 2, 384, 8, 2
+    cos, sin = rope_cos_sin(D, 10000.0, S, DEV)
+    qkv = _bf(B, S, (nh + 2 * nkv) * D, seed=5)
+    do = _bf(B, S, nh * D, seed=6)
+    a = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    b = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)

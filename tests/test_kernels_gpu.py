@@ -166,6 +166,35 @@ def test_rmsnorm_fwd_bwd(H):
     _close(dw, wr.grad, 1e-4)
 
 
+@pytest.mark.parametrize("H", [128, 256, 384, 512, 1024])
+def test_rmsnorm_fwd_four_rows_per_warp(H):
+    """The 4-rows-per-warp forward (the production variant at 16 paths per GPU) on a row
+    count that is not a multiple of 4, against the fp32 reference and against the
+    one-row-per-warp launch of the same register width."""
+    from opendipaco_b200.ops._ext import ext
+
+    G, M = 2, 4737                      # G * M / 32 >= 2 * 148: the automatic choice is 4 rows per warp
+    torch.manual_seed(H)
+    x = torch.randn(G, M, H, device=DEV)
+    w = torch.rand(G, H, device=DEV) + 0.5
+    outs = {}
+    for rpw in (0, 4, 1):
+        y = torch.full((G, M, H), float("nan"), device=DEV, dtype=torch.bfloat16)
+        rstd = torch.full((G, M), float("nan"), device=DEV)
+        ext().rmsnorm_fwd_rpw(x, M * H, w, H, y, M * H, rstd, M, H, G, 1e-5, rpw)
+        outs[rpw] = (y, rstd)
+    torch.cuda.synchronize()
+    rs_ref = torch.rsqrt(x.pow(2).mean(-1) + 1e-5)
+    y_ref = w[:, None, :] * (x * rs_ref[..., None])
+    for rpw, (y, rstd) in outs.items():
+        assert not torch.isnan(y.float()).any() and not torch.isnan(rstd).any(), rpw
+        _close(rstd, rs_ref, 1e-5)
+        _close(y, y_ref, 1e-2)
+    assert torch.equal(outs[0][0], outs[4][0]) and torch.equal(outs[0][1], outs[4][1])
+    torch.testing.assert_close(outs[4][1], outs[1][1], rtol=1e-6, atol=0)
+    torch.testing.assert_close(outs[4][0].float(), outs[1][0].float(), rtol=8e-3, atol=0)
+
+
 def test_embedding_fwd_bwd_deterministic():
     from opendipaco_b200.ops.norm import embedding_bwd, embedding_fwd
 
