@@ -57,6 +57,16 @@ BASELINE_VALUE = None  # the reference publishes no throughput number
 PEER_GBPS = 770.0      # measured peer-copy bandwidth per direction per GPU on this hardware (GB/s)
 
 
+def _hbm_gbps() -> tuple[float, str]:
+    """Measured copy bandwidth of this pool's B200s (MEASURED_PEAKS.json next to this
+    file), else an earlier measurement (6650 GB/s)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
 def _rank_env():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -327,6 +337,19 @@ def run(args) -> dict:
         return float(t.item())
 
     outer_fields = {}
+    hbm, hbm_lab = _hbm_gbps()
+    roof_total = None
+    if args.impl != "reference":
+        if world == 1:
+            plan = engine._fused._plan
+            roof_total = plan.hbm_bytes() / hbm / 1e6
+            roof_basis = f"HBM bytes of the outer launch / {hbm:.0f} GB/s ({hbm_lab} copy bandwidth)"
+        elif hasattr(backend, "outer_roofline_ms"):
+            rf = backend.outer_roofline_ms(hbm, PEER_GBPS)
+            roof_total = max_over_ranks(rf["total"])
+            outer_fields["outer_roofline_ms"] = {k: round(max_over_ranks(v), 4) for k, v in rf.items()}
+            roof_basis = (f"sum over phases of max(local HBM bytes / {hbm:.0f} GB/s ({hbm_lab}), NVLink bytes / "
+                          f"{PEER_GBPS:.0f} GB/s measured peer copy per direction)")
     if phases is not None:
         ph = {k: max_over_ranks(v) for k, v in phases.items()}
         b_in = max_over_ranks(float(backend.nvlink_bytes["in"]))
@@ -340,6 +363,10 @@ def run(args) -> dict:
         }
     device_ms = max_over_ranks(device_ms)
     outer_ms = max_over_ranks(outer_ms) if outer_ms is not None else None
+    if roof_total is not None and outer_ms:
+        outer_fields["outer_sync_roofline_frac"] = round(roof_total / outer_ms, 3)
+        outer_fields["outer_sync_roofline_ms"] = round(roof_total, 4)
+        outer_fields["outer_sync_roofline_basis"] = roof_basis
     wall_ms = max_over_ranks(wall_ms)
     ms_per_round = device_ms / args.steps
     value = tokens_per_round / (ms_per_round / 1e3)
@@ -374,7 +401,11 @@ def run(args) -> dict:
         "outer_sync_ms": None if outer_ms is None else round(outer_ms, 3),
         **outer_fields,
         "outer_sync_scope": ("device time of the fused outer step (reduce over sharers + Nesterov + "
-                             "write-back), max over ranks" if args.impl != "reference" else
+                             "write-back), max over ranks"
+                             + ("; the pseudo-gradient accumulation runs inside the last inner step's AdamW "
+                                "kernel (timed in the inner steps)" if getattr(engine, "_fused", None) is not None
+                                and engine._fused.acc_fused else "")
+                             if args.impl != "reference" else
                              "device time of the per-key global_reduce calls + outer optimizer step of "
                              "the timed rounds, max over ranks"),
     }

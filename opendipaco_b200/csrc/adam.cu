@@ -131,6 +131,21 @@ __global__ void clip_coef_parts_kernel(const float* __restrict__ parts, long lon
   }
 }
 
+// AdamW on four elements in registers (torch.optim.AdamW: decoupled decay, bias-corrected
+// moments, eps outside the sqrt); the gradient is scaled by the clip coefficient first.
+ODP_DEVICE void adamw4(float (&pv)[4], const float (&gv)[4], float (&mv)[4], float (&vv)[4], float cf, float decay,
+                       float step_size, float bc2s, float b1, float b2, float eps) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float gr = gv[k] * cf;
+    pv[k] *= decay;
+    mv[k] = mv[k] + (1.f - b1) * (gr - mv[k]);
+    vv[k] = vv[k] * b2 + (1.f - b2) * gr * gr;
+    const float den = sqrtf(vv[k]) / bc2s + eps;
+    pv[k] = pv[k] - step_size * (mv[k] / den);
+  }
+}
+
 // sched: [G][4] = lr, step_size = lr / bc1, bc2_sqrt, active (0 -> leave this path untouched)
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ p16, long long P, long long sp,
@@ -161,15 +176,7 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
       vv[k] = k < n ? v[o + k] : 0.f;
     }
   }
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float gr = gv[k] * cf;
-    pv[k] *= decay;
-    mv[k] = mv[k] + (1.f - b1) * (gr - mv[k]);
-    vv[k] = vv[k] * b2 + (1.f - b2) * gr * gr;
-    const float den = sqrtf(vv[k]) / bc2s + eps;
-    pv[k] = pv[k] - step_size * (mv[k] / den);
-  }
+  adamw4(pv, gv, mv, vv, cf, decay, step_size, bc2s, b1, b2, eps);
   if (n == 4) {
     *reinterpret_cast<float4*>(p + o) = *reinterpret_cast<float4*>(pv);
     *reinterpret_cast<float4*>(m + o) = *reinterpret_cast<float4*>(mv);
@@ -182,6 +189,124 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
       m[o + k] = mv[k];
       v[o + k] = vv[k];
       p16[grp * s16 + i + k] = __float2bfloat16(pv[k]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- AdamW + pseudo-gradient
+// The last inner step of a round: AdamW for every path, and in the same pass the outer
+// step's pseudo-gradient partial sum_j w_j (global - new local_j) of every module key,
+// so the outer step reads one partial per key instead of every local copy again.
+//
+// The path layout is cut into regions (a module's parameters sit at the same offsets in
+// every path); region r lists (path, key) entries sorted by key and then path. A thread
+// owns four consecutive elements of one region and walks its entries: AdamW for that
+// path, then acc += w * (glob - new) -- the same fp32 operations in the same path order as
+// the outer step's own accumulation -- storing acc into the key's pseudo-gradient buffer
+// after the key's last entry. Private keys (one path) copy the new weight into the global.
+struct AccRegion {
+  long long begin, end;  // element range in every path's layout (begin % 4 == 0)
+  int first, count;      // entries of this region (count <= kAccMaxEntries)
+  long long cta0;        // first CTA of the region (each CTA covers kAccCtaElems elements of one region)
+};
+constexpr int kAccMaxEntries = 128;
+constexpr int kAccCtaElems = 1024;
+struct AccEntry {
+  float* delta;  // key's pseudo-gradient buffer at the region start (null: private key)
+  float* glob;   // key's global buffer at the region start
+  int g;         // path
+  int flags;     // 1: last entry of its key in this region
+  float weight;
+  int pad;
+};
+
+// Every CTA lies in one region: its entries, their schedules and clip coefficients are
+// staged in shared memory once, so a thread's loads of a path's state wait on nothing
+// but their own addresses. Entries are handled two at a time, every load of both paths
+// issued before either's stores (stores through the same base pointers would otherwise
+// keep the compiler from moving the next path's loads ahead of them).
+constexpr int kAccBatch = 2;
+
+__global__ void __launch_bounds__(256) adamw_acc_kernel(
+    float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
+    __nv_bfloat16* __restrict__ p16, long long sp, long long s16, const float* __restrict__ coef,
+    const float* __restrict__ sched, float b1, float b2, float eps, float wd, RowSkip skip,
+    const AccRegion* __restrict__ regs, int nregs, const AccEntry* __restrict__ ents) {
+  __shared__ AccRegion sR;
+  __shared__ AccEntry sE[kAccMaxEntries];
+  __shared__ float4 sS[kAccMaxEntries];  // lr, lr / bc1, sqrt(bc2), active of the entry's path
+  __shared__ float sC[kAccMaxEntries];   // clip coefficient of the entry's path
+  if (threadIdx.x == 0) {
+    int lo = 0, hi = nregs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) / 2;
+      if (regs[mid].cta0 <= (long long)blockIdx.x) lo = mid;
+      else hi = mid - 1;
+    }
+    sR = regs[lo];
+  }
+  __syncthreads();
+  const AccRegion R = sR;
+  for (int k = threadIdx.x; k < R.count; k += blockDim.x) {
+    const AccEntry e = ents[R.first + k];
+    sE[k] = e;
+    sS[k] = *reinterpret_cast<const float4*>(sched + e.g * 4);
+    sC[k] = coef ? coef[e.g] : 1.f;
+  }
+  __syncthreads();
+  const long long off = (blockIdx.x - R.cta0) * kAccCtaElems + threadIdx.x * 4;
+  const long long i = R.begin + off;
+  if (i >= R.end) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 gl = make_float4(0.f, 0.f, 0.f, 0.f);
+  bool have_glob = false;
+  for (int k0 = 0; k0 < R.count; k0 += kAccBatch) {
+    float pv[kAccBatch][4], gv[kAccBatch][4], mv[kAccBatch][4], vv[kAccBatch][4];
+#pragma unroll
+    for (int u = 0; u < kAccBatch; ++u) {
+      if (k0 + u >= R.count) continue;
+      const int grp = sE[k0 + u].g;
+      const long long o = grp * sp + i;
+      *reinterpret_cast<float4*>(pv[u]) = *reinterpret_cast<const float4*>(p + o);
+      if (sS[k0 + u].w != 0.f) {
+        const float4 gr = *reinterpret_cast<const float4*>(g + o);
+        *reinterpret_cast<float4*>(gv[u]) = row_skipped(skip, grp, i) ? make_float4(0.f, 0.f, 0.f, 0.f) : gr;
+        *reinterpret_cast<float4*>(mv[u]) = *reinterpret_cast<const float4*>(m + o);
+        *reinterpret_cast<float4*>(vv[u]) = *reinterpret_cast<const float4*>(v + o);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kAccBatch; ++u) {
+      if (k0 + u >= R.count) break;
+      const AccEntry& E = sE[k0 + u];
+      const float4 sc = sS[k0 + u];
+      if (sc.w != 0.f) {
+        const long long o = E.g * sp + i;
+        adamw4(pv[u], gv[u], mv[u], vv[u], sC[k0 + u], 1.f - sc.x * wd, sc.y, sc.z, b1, b2, eps);
+        *reinterpret_cast<float4*>(p + o) = *reinterpret_cast<float4*>(pv[u]);
+        *reinterpret_cast<float4*>(m + o) = *reinterpret_cast<float4*>(mv[u]);
+        *reinterpret_cast<float4*>(v + o) = *reinterpret_cast<float4*>(vv[u]);
+        *reinterpret_cast<uint2*>(p16 + E.g * s16 + i) =
+            make_uint2(pack_bf16(pv[u][0], pv[u][1]), pack_bf16(pv[u][2], pv[u][3]));
+      }
+      if (E.delta == nullptr) {  // private key: the global is the path's own copy
+        *reinterpret_cast<float4*>(E.glob + off) = *reinterpret_cast<float4*>(pv[u]);
+        continue;
+      }
+      if (!have_glob) {
+        gl = *reinterpret_cast<const float4*>(E.glob + off);
+        have_glob = true;
+      }
+      const float w = E.weight;
+      acc.x = __fadd_rn(acc.x, __fmul_rn(w, __fsub_rn(gl.x, pv[u][0])));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(w, __fsub_rn(gl.y, pv[u][1])));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(w, __fsub_rn(gl.z, pv[u][2])));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(w, __fsub_rn(gl.w, pv[u][3])));
+      if (E.flags & 1) {
+        *reinterpret_cast<float4*>(E.delta + off) = acc;
+        acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        have_glob = false;
+      }
     }
   }
 }
@@ -309,6 +434,28 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
       reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), P, sp, s16,
       coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
       (float)eps, (float)wd, row_skip(rows, r0, H, V));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// AdamW of the last inner step fused with the outer pseudo-gradient accumulation.
+// regions: int64 [nregs, 4] AccRegion records (their CTAs, kAccCtaElems elements each, in
+// region order: ctas = total CTA count); entries: int64 [nents, 4] AccEntry records.
+// Regions begin at multiples of 4 elements; buffers are 16-byte aligned.
+void adamw_acc_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor p16, int64_t ctas,
+                    int64_t sp, int64_t s16, c10::optional<torch::Tensor> coef, torch::Tensor sched, double b1,
+                    double b2, double eps, double wd, c10::optional<torch::Tensor> rows, int64_t r0, int64_t H,
+                    int64_t V, torch::Tensor regions, int64_t nregs, torch::Tensor entries) {
+  static_assert(sizeof(odp::AccRegion) == 32 && sizeof(odp::AccEntry) == 32, "AccRegion / AccEntry layout");
+  c10::cuda::CUDAGuard guard(p.device());
+  TORCH_CHECK(sp % 4 == 0 && s16 % 4 == 0, "adamw_acc_step: strides must be multiples of 4");
+  TORCH_CHECK(regions.is_cuda() && entries.is_cuda() && nregs >= 1 && ctas >= 1, "adamw_acc_step: tables on the device");
+  TORCH_CHECK(odp::kAccCtaElems == 256 * 4, "adamw_acc_step: one CTA covers 256 x 4 elements");
+  odp::adamw_acc_kernel<<<(unsigned)ctas, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), sp, s16,
+      coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
+      (float)eps, (float)wd, row_skip(rows, r0, H, V), reinterpret_cast<const odp::AccRegion*>(regions.data_ptr()),
+      (int)nregs, reinterpret_cast<const odp::AccEntry*>(entries.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

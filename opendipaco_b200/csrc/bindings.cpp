@@ -68,24 +68,29 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
                 int64_t sp, int64_t s16, int64_t G, c10::optional<torch::Tensor> coef, torch::Tensor sched, double b1,
                 double b2, double eps, double wd, c10::optional<torch::Tensor> rows, int64_t r0, int64_t H,
                 int64_t V);
+void adamw_acc_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor p16, int64_t ctas,
+                    int64_t sp, int64_t s16, c10::optional<torch::Tensor> coef, torch::Tensor sched, double b1,
+                    double b2, double eps, double wd, c10::optional<torch::Tensor> rows, int64_t r0, int64_t H,
+                    int64_t V, torch::Tensor regions, int64_t nregs, torch::Tensor entries);
 void adam8bit_step(torch::Tensor p, torch::Tensor g, torch::Tensor mq, torch::Tensor mabs, torch::Tensor vq,
                    torch::Tensor vlo, torch::Tensor vsc, c10::optional<torch::Tensor> coef, torch::Tensor sched,
                    double b1, double b2, double eps, double wd, bool first, c10::optional<torch::Tensor> p16,
                    int64_t blocks_per_group);
 void outer_step(torch::Tensor segs, int64_t nseg, torch::Tensor locals, int64_t total_chunks, double lr,
-                double momentum, bool nesterov, bool first, c10::optional<torch::Tensor> sq_part);
+                double momentum, bool nesterov, bool first, c10::optional<torch::Tensor> sq_part,
+                c10::optional<torch::Tensor> status);
 int64_t outer_chunk_elems();
 void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks, torch::Tensor delta_ptrs,
                         torch::Tensor glob_ptrs, torch::Tensor pads, torch::Tensor mom, int64_t rank, int64_t world,
                         int64_t epoch, double lr, double m, bool nesterov, bool first, torch::Tensor sq_part,
                         torch::Tensor err, c10::optional<torch::Tensor> qd_ptrs,
-                        c10::optional<torch::Tensor> qs_ptrs, int64_t kcap);
+                        c10::optional<torch::Tensor> qs_ptrs, int64_t kcap, c10::optional<torch::Tensor> status);
 void outer_nvlink_topk(torch::Tensor regs, int64_t nregs, int64_t total_blocks, double density, int64_t kcap,
                        torch::Tensor delta, torch::Tensor res, torch::Tensor spi, torch::Tensor spv);
 void outer_nvlink_quant(torch::Tensor regs, int64_t nregs, int64_t total_groups, torch::Tensor delta,
                         torch::Tensor res, torch::Tensor qd, torch::Tensor qs);
-void outer_nvlink_bcast(torch::Tensor cps, int64_t ncp, int64_t total_chunks, torch::Tensor pads, int64_t rank,
-                        int64_t world, int64_t epoch, torch::Tensor err);
+void outer_nvlink_bcast(torch::Tensor segs, int64_t nseg, torch::Tensor locals, int64_t total_chunks,
+                        torch::Tensor pads, int64_t rank, int64_t world, int64_t epoch, torch::Tensor err);
 int64_t outer_nvlink_chunk_elems();
 int64_t set_peer_wait_ns(int64_t ns);
 std::vector<torch::Tensor> quant_int4(torch::Tensor x, bool want_resid);
@@ -126,6 +131,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_clip_coef", &grad_clip_coef);
   m.def("adamw_step", &adamw_step);
   m.def("adam8bit_step", &adam8bit_step);
+  m.def("adamw_acc_step", &adamw_acc_step);
   m.def("outer_step", &outer_step);
   m.def("outer_chunk_elems", &outer_chunk_elems);
   m.def("outer_nvlink_apply", &outer_nvlink_apply);

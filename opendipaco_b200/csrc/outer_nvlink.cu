@@ -16,7 +16,10 @@
 //      stores into GLOB_s[e] of every sharer s (this rank included).
 // outer_nvlink_bcast (next launch):
 //   3. CTA 0 publishes "my peer stores are complete"; every CTA waits for all ranks;
-//      then the fresh globals are copied into this GPU's working copies (fp32 + bf16).
+//      then the fresh globals are copied into this GPU's working copies (fp32 + bf16),
+//      each global read once for all of its local sharers.
+// Guard: an element whose pseudo-gradient is not finite is not applied (global and
+// momentum unchanged) and is counted in a status word the host reads after the round.
 //
 // So per round each rank reads (g-1)/g and writes (g-1)/g of every module it shares
 // over NVLink (two-shot reduce-scatter + all-gather), fused with the reduction, the
@@ -42,7 +45,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
-#include "common.cuh"
+#include "outer_common.cuh"
 
 namespace odp {
 
@@ -307,9 +310,8 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
                                           int first, float* __restrict__ sq_part, int* err,
                                           const unsigned long long* __restrict__ qd_ptrs,
                                           const unsigned long long* __restrict__ qs_ptrs, int kcap,
-                                          unsigned long long wait_ns) {
+                                          unsigned long long wait_ns, int* status) {
   if (!cross_gpu_barrier(pads, rank, world, 0, epoch, err, blockIdx.x == 0, wait_ns)) return;
-  __shared__ float red[8];
   __shared__ __align__(16) float dense[kNvChunk];  // top-k mode: this chunk's summed pairs
   for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
     int lo = 0, hi = nkeys - 1;
@@ -322,6 +324,7 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
     const long long e0 = k.s0 + (ch - k.chunk0) * kNvChunk;
     const long long e1 = min(e0 + kNvChunk, k.s1);
     float sq = 0.f;
+    int bad = 0;
     const float* gl = reinterpret_cast<const float*>(glob_ptrs[rank]) + k.off;
     if (k.quant == 2) {
       // the chunk is one 4096-element block: add every sharer's (index, value) pairs
@@ -399,6 +402,11 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float dd = __fmul_rn(__fmul_rn(a4[i], k.inv_den), k.scale);
+          if (!isfinite(dd)) {  // guard: a non-finite contribution leaves global and momentum as they are
+            ++bad;
+            n4[i] = g4[i];
+            continue;
+          }
           sq += dd * dd;
           const float b = first ? dd : __fadd_rn(__fmul_rn(b4[i], m), dd);
           b4[i] = b;
@@ -411,48 +419,27 @@ __global__ void outer_nvlink_apply_kernel(const NvKey* __restrict__ keys, int nk
           *reinterpret_cast<float4*>(reinterpret_cast<float*>(glob_ptrs[k.sh[j]]) + k.off + eu) = nv;
       }
     }
-    if (sq_part) {
-      sq = warp_sum(sq);
-      if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = sq;
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        float t = 0.f;
-        for (int w = 0; w < (int)blockDim.x / 32; ++w) t += red[w];
-        sq_part[ch] = t;
-      }
-      __syncthreads();
-    }
+    outer_chunk_reduce(sq, bad, ch, sq_part, status);
   }
 }
 
-// Copy the fresh globals into this GPU's working copies after all ranks' stores.
-struct NvCopy {
-  const float* src;
-  float* dst32;
-  __nv_bfloat16* dst16;
-  long long n;
-  long long chunk0;
-};
-
-__global__ void outer_nvlink_bcast_kernel(const NvCopy* __restrict__ cps, int ncp, long long total_chunks,
-                                          const unsigned long long* __restrict__ pads, int rank, int world,
-                                          unsigned epoch, int* err, unsigned long long wait_ns) {
+// After all ranks' peer stores: copy the fresh globals into this GPU's working copies
+// (fp32 + bf16). One segment per module key with every local sharer, so each global is
+// read once however many local paths use it.
+__global__ void __launch_bounds__(256) outer_nvlink_bcast_kernel(const OuterSeg* __restrict__ segs, int nseg,
+                                                                 const OuterLocal* __restrict__ locs,
+                                                                 long long total_chunks,
+                                                                 const unsigned long long* __restrict__ pads, int rank,
+                                                                 int world, unsigned epoch, int* err,
+                                                                 unsigned long long wait_ns) {
   if (!cross_gpu_barrier(pads, rank, world, 1, epoch, err, blockIdx.x == 0, wait_ns)) return;
   for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
-    int lo = 0, hi = ncp - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) / 2;
-      if (cps[mid].chunk0 <= ch) lo = mid;
-      else hi = mid - 1;
-    }
-    const NvCopy c = cps[lo];
-    const long long e0 = (ch - c.chunk0) * kNvChunk;
-    const long long e1 = min(e0 + kNvChunk, c.n);
-    for (long long e = e0 + threadIdx.x * 4; e < e1; e += blockDim.x * 4) {
-      const float4 v = ld_cg4(c.src + e);
-      *reinterpret_cast<float4*>(c.dst32 + e) = v;
-      *reinterpret_cast<uint2*>(c.dst16 + e) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
-    }
+    const OuterSeg sg = segs[find_seg(segs, nseg, ch)];
+    const long long e0 = (ch - sg.chunk0) * kOuterChunk;
+    const long long e1 = min(e0 + kOuterChunk, sg.n);
+    float sq = 0.f;
+    int bad = 0;
+    outer_chunk(sg, locs, e0, e1, 0.f, 0.f, 0, 0, sq, bad);
   }
 }
 
@@ -462,7 +449,7 @@ void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks,
                         torch::Tensor glob_ptrs, torch::Tensor pads, torch::Tensor mom, int64_t rank, int64_t world,
                         int64_t epoch, double lr, double m, bool nesterov, bool first, torch::Tensor sq_part,
                         torch::Tensor err, c10::optional<torch::Tensor> qd_ptrs, c10::optional<torch::Tensor> qs_ptrs,
-                        int64_t kcap) {
+                        int64_t kcap, c10::optional<torch::Tensor> status) {
   static_assert(sizeof(odp::NvKey) == 80, "NvKey layout");
   c10::cuda::CUDAGuard guard(mom.device());
   TORCH_CHECK(world <= 64, "outer_nvlink: world too large");
@@ -477,7 +464,7 @@ void outer_nvlink_apply(torch::Tensor keys, int64_t nkeys, int64_t total_chunks,
       err.data_ptr<int>(),
       qd_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qd_ptrs->data_ptr()) : nullptr,
       qs_ptrs.has_value() ? reinterpret_cast<const unsigned long long*>(qs_ptrs->data_ptr()) : nullptr, (int)kcap,
-      odp::peer_wait_bound_ns());
+      odp::peer_wait_bound_ns(), status.has_value() ? status->data_ptr<int>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -509,13 +496,16 @@ void outer_nvlink_quant(torch::Tensor regs, int64_t nregs, int64_t total_groups,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void outer_nvlink_bcast(torch::Tensor cps, int64_t ncp, int64_t total_chunks, torch::Tensor pads, int64_t rank,
-                        int64_t world, int64_t epoch, torch::Tensor err) {
-  static_assert(sizeof(odp::NvCopy) == 40, "NvCopy layout");
+// segs / locals: OuterSeg / OuterLocal tables (mode BCAST) of this GPU's shared keys.
+void outer_nvlink_bcast(torch::Tensor segs, int64_t nseg, torch::Tensor locals, int64_t total_chunks,
+                        torch::Tensor pads, int64_t rank, int64_t world, int64_t epoch, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(pads.device());
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total_chunks, 148 * 4));
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  // always launched: every rank must take part in the barrier
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total_chunks, (int64_t)sms * 8));
   odp::outer_nvlink_bcast_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const odp::NvCopy*>(cps.data_ptr()), (int)ncp, total_chunks,
+      reinterpret_cast<const odp::OuterSeg*>(segs.data_ptr()), (int)nseg,
+      reinterpret_cast<const odp::OuterLocal*>(locals.data_ptr()), total_chunks,
       reinterpret_cast<const unsigned long long*>(pads.data_ptr()), (int)rank, (int)world, (unsigned)epoch,
       err.data_ptr<int>(), odp::peer_wait_bound_ns());
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -1,7 +1,8 @@
 """Fused DiLoCo outer step (``csrc/outer.cu``) driven by a segment table.
 
-A *segment* is one shared module (its flat fp32 global buffer, momentum buffer and
-the list of local working copies that share it on this GPU, with their weights).
+A *segment* is one shared module (its flat fp32 global buffer, momentum buffer,
+pseudo-gradient buffer and the list of local working copies that share it on this GPU,
+with their weights).
 :class:`OuterPlan` packs the table once (device pointers are stable because every
 buffer is a view into the executor's persistent flat arenas) and each round is one
 kernel launch.
@@ -55,6 +56,8 @@ class OuterPlan:
         self.key_chunks = []
         for i, s in enumerate(self.segments):
             n = s.glob.numel()
+            if n % 4 or s.glob.data_ptr() % 16:
+                raise ValueError(f"outer step: module {s.key} must be 16-byte aligned with a multiple of 4 elements")
             nch = (n + self.chunk - 1) // self.chunk
             segs[i] = (s.glob.data_ptr(), s.mom.data_ptr() if s.mom is not None else 0,
                        s.delta.data_ptr() if s.delta is not None else 0, n, len(locs),
@@ -85,24 +88,54 @@ class OuterPlan:
         if changed or self._tables is None:
             self.build()
 
-    def run(self, lr: float, momentum: float, nesterov: bool, first: bool) -> None:
+    def tables(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """(segment table, local table) on the device."""
         if self._tables is None:
             self.build()
-        seg_t, loc_t = self._tables
+        return self._tables
+
+    def run(self, lr: float, momentum: float, nesterov: bool, first: bool,
+            status: torch.Tensor | None = None) -> None:
+        """One launch. ``status`` (int32 [1]) counts elements whose pseudo-gradient was not
+        finite and were therefore left unchanged."""
+        seg_t, loc_t = self.tables()
         ext().outer_step(seg_t, len(self.segments), loc_t, self.total_chunks, lr, momentum, nesterov, first,
-                         self.sq_part)
+                         self.sq_part, status)
 
     def with_mode(self, mode_for_outer: int) -> "OuterPlan":
-        """A copy of this plan whose outer segments run in ``mode_for_outer``
-        (ACC or APPLY), sharing the same buffers."""
+        """A copy of this plan whose outer segments (OUTER or APPLY) run in
+        ``mode_for_outer`` (ACC, APPLY or BCAST), sharing the same buffers. ACC and BCAST
+        plans keep only those segments (private-module copies are dropped)."""
         segs = [Segment(s.key, s.glob, s.mom, s.locals32, s.locals16, s.weights,
-                        mode_for_outer if s.mode == MODE_OUTER else s.mode, s.scale, s.inv_den, s.delta)
+                        mode_for_outer if s.mode in (MODE_OUTER, MODE_APPLY) else s.mode, s.scale, s.inv_den,
+                        s.delta)
                 for s in self.segments]
-        if mode_for_outer == MODE_ACC:
-            segs = [s for s in segs if s.mode == MODE_ACC]
+        if mode_for_outer in (MODE_ACC, MODE_BCAST):
+            segs = [s for s in segs if s.mode == mode_for_outer]
         plan = OuterPlan(segs, self.device)
         plan.build()
         return plan
+
+    def hbm_bytes(self) -> int:
+        """Bytes one launch must move through HBM (each buffer read / written once): the
+        algorithmic traffic the roofline of this plan's launch is computed from."""
+        total = 0
+        for s in self.segments:
+            n, nl = s.glob.numel(), len(s.locals32)
+            n16 = sum(1 for t in s.locals16 if t is not None)
+            write_back = 4 * nl + 2 * n16
+            if s.mode == MODE_COPY:
+                per = 8
+            elif s.mode == MODE_BCAST:
+                per = 4 + write_back
+            elif s.mode == MODE_ACC:
+                per = 4 + 4 * nl + 4
+            elif s.mode == MODE_APPLY:
+                per = 3 * 4 + 2 * 4 + write_back       # delta, global, momentum in; momentum, global out
+            else:
+                per = 4 + 4 * nl + 4 + 2 * 4 + write_back
+            total += per * n
+        return total
 
     def delta_norms(self) -> dict[str, float]:
         """Per-key ||delta|| of the last run (read back once per round)."""

@@ -49,14 +49,13 @@ import torch
 import torch.distributed as dist
 
 from ...ops._ext import err_word, ext
-from ...ops.outer import MODE_ACC, MODE_COPY, MODE_OUTER
+from ...ops.outer import MODE_ACC, MODE_BCAST, MODE_COPY, MODE_OUTER
 from ...topology import is_private_key
 from .torch_dist import TorchDistBackend
 
 NVKEY = np.dtype([("off", "<i8"), ("s0", "<i8"), ("s1", "<i8"), ("chunk0", "<i8"), ("nsh", "<i4"),
                   ("sh", "<i4", (8,)), ("scale", "<f4"), ("inv_den", "<f4"), ("quant", "<i4")])
-NVCOPY = np.dtype([("src", "<u8"), ("dst32", "<u8"), ("dst16", "<u8"), ("n", "<i8"), ("chunk0", "<i8")])
-assert NVKEY.itemsize == 80 and NVCOPY.itemsize == 40
+assert NVKEY.itemsize == 80
 NVREGION = np.dtype([("off", "<i8"), ("n", "<i8"), ("group0", "<i8")])
 ALIGN = 256
 QGROUP = 128
@@ -68,7 +67,6 @@ def _ru(n: int, a: int = ALIGN) -> int:
 
 
 class NVLinkBackend(TorchDistBackend):
-    outer_launches = 3
 
     def __init__(self, topology, device: torch.device | None = None, dp: int = 1, compress: str | None = None,
                  density: float = 0.01):
@@ -81,8 +79,6 @@ class NVLinkBackend(TorchDistBackend):
         self.density = float(density)
         self.kcap = max(1, math.ceil(self.density * SPBLOCK))
         self._align = SPBLOCK if self.compress == "topk" else ALIGN
-        if self.compress:
-            self.outer_launches = 4
         self._dp_handles: list = []
         self._offs: dict[str, int] | None = None
         self._tables = None
@@ -185,22 +181,36 @@ class NVLinkBackend(TorchDistBackend):
         i = sh.index(self.rank if rank is None else rank)
         return min(n, i * per), min(n, (i + 1) * per)
 
+    def delta_view(self, key: str) -> torch.Tensor:
+        """This rank's pseudo-gradient partial of ``key`` in the symmetric DELTA buffer (the
+        peers read it during APPLY); the fused executor's last optimizer step writes it."""
+        return self.DELTA[self._offs[key]:self._offs[key] + self._sizes[key]]
+
+    def outer_launch_count(self, ex) -> int:
+        """Kernels of one outer step: [ACC (+ private copies)] [QUANT | TOPK] APPLY BCAST."""
+        t = self._tables
+        acc = 0 if getattr(ex, "acc_fused", False) else 1 + (1 if t and t["cplan"] is not None else 0)
+        return acc + (1 if self.compress else 0) + 2
+
     def _build(self, ex, plan) -> None:
         chunk = int(ext().outer_nvlink_chunk_elems())
+        fused = getattr(ex, "acc_fused", False)
         # ACC plan: outer segments write their partial into DELTA; private copies run too
+        # (unless the last inner step's optimizer kernel already did both)
         for s in plan.segments:
             if s.mode == MODE_OUTER:
-                s.delta = self.DELTA[self._offs[s.key]:self._offs[s.key] + s.glob.numel()]
-        acc = plan.with_mode(MODE_ACC)
+                s.delta = self.delta_view(s.key)
+        acc = None if fused else plan.with_mode(MODE_ACC)
         copies = [s for s in plan.segments if s.mode == MODE_COPY]
-        if copies:
+        if copies and not fused:
             from ...ops.outer import OuterPlan
 
             cplan = OuterPlan(copies, self.dev)
             cplan.build()
         else:
             cplan = None
-        keys, cps, chunk0, c0 = [], [], 0, 0
+        keys, chunk0 = [], 0
+        apply_elems = 0
         regs, g0 = [], 0
         b_in = b_out = 0
         self._sq_keys = []
@@ -231,6 +241,7 @@ class NVLinkBackend(TorchDistBackend):
             # bytes of this rank's APPLY slice that cross NVLink: the other sharers' partials
             # come in (fp32, int4 codes + scales, or top-k pairs), the new global goes out
             L = max(s1 - s0, 0)
+            apply_elems += L
             if rec["quant"][0] == 1:
                 bpe = 0.5 + 4.0 / QGROUP
             elif rec["quant"][0] == 2:
@@ -243,21 +254,23 @@ class NVLinkBackend(TorchDistBackend):
                 keys.append(rec)
                 self._sq_keys.append((s.key, chunk0, nch))
             chunk0 += nch
-            n = s.glob.numel()
-            for l32, l16 in zip(s.locals32, s.locals16):
-                cr = np.zeros(1, dtype=NVCOPY)
-                cr["src"], cr["dst32"], cr["dst16"], cr["n"], cr["chunk0"] = (
-                    s.glob.data_ptr(), l32.data_ptr(), l16.data_ptr(), n, c0)
-                cps.append(cr)
-                c0 += (n + chunk - 1) // chunk
         key_arr = np.concatenate(keys) if keys else np.zeros(1, dtype=NVKEY)
-        cp_arr = np.concatenate(cps) if cps else np.zeros(1, dtype=NVCOPY)
         to_dev = lambda a: torch.from_numpy(a.view(np.int64).copy()).to(self.dev)  # noqa: E731
         reg_arr = np.concatenate(regs) if regs else np.zeros(1, dtype=NVREGION)
+        # BCAST: one segment per shared key with all of this GPU's sharers (the global is
+        # read once per key)
+        bplan = plan.with_mode(MODE_BCAST)
+        # local HBM bytes of each phase (for the roofline of the whole outer step): APPLY
+        # reads this rank's partial, global and momentum of its slices and writes momentum
+        # and global (20 bytes per element); the peers' partials and the peer stores cross
+        # NVLink (counted in b_in / b_out)
+        self.phase_hbm_bytes = {"acc": acc.hbm_bytes() if acc is not None else 0,
+                                "apply": 20 * apply_elems, "bcast": bplan.hbm_bytes()}
+        if cplan is not None:
+            self.phase_hbm_bytes["acc"] += cplan.hbm_bytes()
         self._tables = dict(plan_id=id(plan), acc=acc, cplan=cplan, keys=to_dev(key_arr), nkeys=len(keys),
-                            chunks=chunk0, cps=to_dev(cp_arr), ncp=len(cps), cchunks=c0,
-                            sq=torch.zeros(max(chunk0, 1), device=self.dev), regs=to_dev(reg_arr),
-                            nregs=len(regs), groups=g0)
+                            chunks=chunk0, bplan=bplan, sq=torch.zeros(max(chunk0, 1), device=self.dev),
+                            regs=to_dev(reg_arr), nregs=len(regs), groups=g0)
         self._all_keys = [k for k in self.topology.module_keys() if not is_private_key(k)]
         self.nvlink_bytes = {"in": b_in, "out": b_out}
 
@@ -271,7 +284,8 @@ class NVLinkBackend(TorchDistBackend):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if self.timing else None
         if ev:
             ev[0].record()
-        t["acc"].run(0.0, 0.0, False, False)
+        if t["acc"] is not None:
+            t["acc"].run(0.0, 0.0, False, False)
         if t["cplan"] is not None:
             t["cplan"].run(0.0, 0.0, False, False)
         if ev:
@@ -290,14 +304,28 @@ class NVLinkBackend(TorchDistBackend):
         self._epoch += 1
         ext().outer_nvlink_apply(t["keys"], t["nkeys"], t["chunks"], self._dptrs, self._gptrs, self._pptrs,
                                  self.MOM, self.rank, self.world_size, self._epoch, dl.outer_lr,
-                                 dl.outer_momentum, dl.outer_nesterov, first, t["sq"], err, qd, qs, self.kcap)
+                                 dl.outer_momentum, dl.outer_nesterov, first, t["sq"], err, qd, qs, self.kcap,
+                                 getattr(ex, "OUTER_STATUS", None))
         if ev:
             ev[3].record()
-        ext().outer_nvlink_bcast(t["cps"], t["ncp"], t["cchunks"], self._pptrs, self.rank, self.world_size,
-                                 self._epoch, err)
+        bp = t["bplan"]
+        seg_t, loc_t = bp.tables()
+        ext().outer_nvlink_bcast(seg_t, len(bp.segments), loc_t, bp.total_chunks, self._pptrs, self.rank,
+                                 self.world_size, self._epoch, err)
         if ev:
             ev[4].record()
             self._tev.append(ev)
+
+    def outer_roofline_ms(self, hbm_gbps: float, link_gbps: float) -> dict[str, float]:
+        """Roofline time (ms) of each outer-step phase: its local HBM bytes at ``hbm_gbps``
+        or, for APPLY, the slower of that and its bytes over NVLink at ``link_gbps`` per
+        direction; "total" sums the phases (they run one after another)."""
+        hb = getattr(self, "phase_hbm_bytes", {"acc": 0, "apply": 0, "bcast": 0})
+        link = max(self.nvlink_bytes["in"], self.nvlink_bytes["out"]) / link_gbps / 1e6
+        out = {"acc": hb["acc"] / hbm_gbps / 1e6, "apply": max(hb["apply"] / hbm_gbps / 1e6, link),
+               "bcast": hb["bcast"] / hbm_gbps / 1e6}
+        out["total"] = sum(out.values())
+        return out
 
     def phase_times(self) -> dict[str, float]:
         """Mean device time (ms) of the outer step's phases over the timed calls since the

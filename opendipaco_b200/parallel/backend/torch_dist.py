@@ -106,32 +106,37 @@ class TorchDistBackend(SyncBackend):
         dist.barrier()
 
     # -- fused-executor outer step over NCCL (the in-framework baseline) -------------
-    outer_launches = 2
+    def outer_launch_count(self, ex) -> int:
+        """Kernels of one outer step (the NCCL all-reduces are not counted)."""
+        return 1 if getattr(ex, "acc_fused", False) else 2
 
     def fused_outer_step(self, ex, plan, first: bool) -> None:
-        """Local partial (kernel) -> NCCL all-reduce per key group -> apply (kernel).
+        """Local partial (kernel, unless the last inner step's optimizer kernel already
+        wrote it) -> NCCL all-reduce per key group -> apply (kernel).
 
         Every sharer applies the full Nesterov update redundantly, as the reference
         does after its per-key all-reduce.
         """
         from ...ops.outer import MODE_ACC, MODE_APPLY, MODE_OUTER
 
+        fused = getattr(ex, "acc_fused", False)
         cache = getattr(self, "_nccl_plans", None)
         if cache is None or cache[0] != id(plan):
             for s in plan.segments:
-                if s.mode == MODE_OUTER:
+                if s.mode == MODE_OUTER and s.delta is None:
                     s.delta = torch.zeros_like(s.glob)
-            cache = (id(plan), plan.with_mode(MODE_ACC), plan.with_mode(MODE_APPLY),
+            cache = (id(plan), None if fused else plan.with_mode(MODE_ACC), plan.with_mode(MODE_APPLY),
                      [s for s in plan.segments if s.mode == MODE_OUTER])
             self._nccl_plans = cache
         _, acc, apply, outer = cache
-        acc.run(0.0, 0.0, False, False)
+        if acc is not None:
+            acc.run(0.0, 0.0, False, False)
         for s in outer:
             if self.dp_index:
                 s.delta.zero_()
             dist.all_reduce(s.delta, op=dist.ReduceOp.SUM, group=self._groups[s.key])
         dl = ex.e.diloco
-        apply.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first)
+        apply.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first, status=getattr(ex, "OUTER_STATUS", None))
 
     def delta_norms(self) -> dict[str, float]:
         apply = self._nccl_plans[2]

@@ -1,398 +1,224 @@
-"""Selector-based TCP server core and transport metrics (reference ``schedule/reactor.py``).
+"""TCP server core of the control plane and its transport metrics.
 
-``ReactorServer`` accepts connections on one thread and spreads them over
-``io_threads`` selector loops (non-blocking sockets, optional non-blocking TLS
-handshake). Each connection must first answer a challenge with an HMAC over one of
-the accepted shared secrets or an Ed25519 signature from an admitted identity;
-afterwards every complete frame is decoded with the pickle-free codec and handed to
-the subclass hook :meth:`ReactorServer._handle`, whose optional reply is queued
-back. Frames longer than ``max_msg_bytes`` close the connection; beyond
-``max_connections`` new sockets are refused. ``TransportMetrics`` counts tasks,
-submissions, bytes by category (``bytes_opt`` must stay 0: optimizer state never
-crosses the wire), rejections and staleness, with Prometheus text output.
+``ReactorServer`` is the base of the coordinator, the sharded scheduler, the parameter
+servers and the tracker. It runs one asyncio event loop on a background thread: the loop
+owns every socket (accepting, the optional TLS handshake, framed reads and writes with
+back-pressure), and a pool of ``io_threads`` worker threads decodes each frame, runs the
+subclass hook :meth:`ReactorServer._handle` and encodes its reply, so a large tensor
+payload or a slow handler never stalls the other connections. Messages of one connection
+are handled strictly in order; different connections are handled concurrently.
+
+A connection that must authenticate (shared secrets and/or admitted Ed25519 identities)
+gets a challenge first and is closed unless its first message answers it (wire.py has
+the exchange). Frames longer than ``max_msg_bytes``, bodies that do not decode and
+handler exceptions close the connection; beyond ``max_connections`` new sockets are
+closed at once.
+
+Behaviour follows the reference's selector-based reactor (``src/opendipaco/schedule/
+reactor.py``): same handshake, limits and metrics names (Prometheus scrapes and the
+``opendipaco`` report lines stay comparable); the event-loop design is this module's own.
 """
 
 from __future__ import annotations
 
+import asyncio
 import os
-import selectors
 import socket
 import ssl
 import threading
 import time
-from dataclasses import dataclass, field
+from concurrent.futures import ThreadPoolExecutor
 
 import torch
 
 from .identity import peer_id_of, verify_auth
 from .wire import DEFAULT_MAX_MSG_BYTES, _LEN, acceptable_keys, decode, encode, verify_mac
 
+# ---------------------------------------------------------------------- metrics
+# Counters in exposition order. ``bytes_opt`` counts optimizer state seen on the wire in
+# either direction: it must stay 0 (inner-optimizer state never leaves a worker).
+_COUNTERS = (
+    "generations", "tasks_sent", "submits", "heartbeats", "nacks", "idle", "reclaims", "dropped",
+    "tasks_with_shard", "tasks_with_private_down",
+    "bytes_down", "bytes_up", "bytes_control", "bytes_shared_weights", "bytes_private_down", "bytes_shard",
+    "bytes_shared_grad", "bytes_private_up", "bytes_opt",
+    "accepted_updates", "stale_rejected", "invalid_rejected", "norm_clipped", "poison_flagged", "handler_errors",
+    "staleness_sum", "max_staleness",
+)
+_GAUGES = ("max_staleness", "mean_staleness", "throughput_tasks_per_s", "active_workers")
+# per message type: (count counter, total-bytes counter, {payload field: bytes counter},
+# {payload field: (counter of messages carrying it, whether a value counts as carried)})
+_TRAFFIC_OUT = {"task": ("tasks_sent", "bytes_down",
+                         {"shared_weights": "bytes_shared_weights", "opt_state": "bytes_opt",
+                          "private_weights": "bytes_private_down", "shard": "bytes_shard"},
+                         {"private_weights": ("tasks_with_private_down", bool),
+                          "shard": ("tasks_with_shard", lambda x: x is not None)}),
+                "idle": ("idle", "bytes_control", {}, {})}
+_TRAFFIC_IN = {"submit": ("submits", "bytes_up",
+                          {"shared_grad": "bytes_shared_grad", "private_weights": "bytes_private_up",
+                           "opt_state": "bytes_opt"}, {}),
+               "heartbeat": ("heartbeats", "bytes_control", {}, {}),
+               "nack": ("nacks", "bytes_control", {}, {})}
 
-def _pubkey_hex(p) -> str:
-    return getattr(p, "public_key_hex", p).lower()
 
-
-def _tensor_bytes(obj) -> int:
-    if obj is None:
-        return 0
+def payload_bytes(obj) -> int:
+    """Bytes of every tensor inside a (nested) message field."""
     if torch.is_tensor(obj):
         return obj.numel() * obj.element_size()
     if isinstance(obj, dict):
-        return sum(_tensor_bytes(v) for v in obj.values())
-    if isinstance(obj, (list, tuple)):
-        return sum(_tensor_bytes(v) for v in obj)
-    return 0
+        obj = obj.values()
+    elif not isinstance(obj, (list, tuple)):
+        return 0
+    return sum(payload_bytes(x) for x in obj)
 
 
-def _fmt(n: float) -> str:
-    for unit in ("B", "KB", "MB", "GB"):
-        if n < 1024 or unit == "GB":
-            return f"{int(n)}B" if unit == "B" else f"{n:.1f}{unit}"
+def human_bytes(n: float) -> str:
+    if n < 1024:
+        return f"{int(n)}B"
+    for unit in ("KB", "MB", "GB"):
         n /= 1024
+        if n < 1024 or unit == "GB":
+            return f"{n:.1f}{unit}"
     return f"{n:.1f}GB"
 
 
-@dataclass
 class TransportMetrics:
-    _GAUGES = frozenset({"max_staleness", "mean_staleness", "throughput_tasks_per_s", "active_workers"})
-    _LIVENESS_WINDOW = 60.0
-    generations: int = 0
-    tasks_sent: int = 0
-    submits: int = 0
-    heartbeats: int = 0
-    nacks: int = 0
-    idle: int = 0
-    reclaims: int = 0
-    dropped: int = 0
-    tasks_with_shard: int = 0
-    tasks_with_private_down: int = 0
-    bytes_down: int = 0
-    bytes_up: int = 0
-    bytes_control: int = 0
-    bytes_shared_weights: int = 0
-    bytes_private_down: int = 0
-    bytes_shard: int = 0
-    bytes_shared_grad: int = 0
-    bytes_private_up: int = 0
-    bytes_opt: int = 0
-    accepted_updates: int = 0
-    stale_rejected: int = 0
-    invalid_rejected: int = 0
-    norm_clipped: int = 0
-    poison_flagged: int = 0
-    handler_errors: int = 0
-    staleness_sum: int = 0
-    max_staleness: int = 0
-    _wall: float = 0.0
-    _worker_seen: dict = field(default_factory=dict)
-    _lock: threading.Lock = field(default_factory=threading.Lock)
+    """Thread-safe counters of one server's traffic and outcomes. Every counter is also
+    an attribute (``metrics.reclaims += 1`` works); derived gauges come from
+    :meth:`summary`."""
 
-    def _bump(self, name: str, by: int = 1) -> None:
+    LIVENESS_WINDOW = 60.0  # a worker counts as active for this long after its last message
+
+    def __init__(self):
+        object.__setattr__(self, "_values", dict.fromkeys(_COUNTERS, 0))
+        object.__setattr__(self, "_lock", threading.Lock())
+        object.__setattr__(self, "_last_seen", {})
+        object.__setattr__(self, "_wall", 0.0)  # seconds the server spent serving (throughput)
+
+    def __getattr__(self, name):
+        values = self.__dict__["_values"]
+        if name in values:
+            return values[name]
+        raise AttributeError(name)
+
+    def __setattr__(self, name, value):
+        if name in self._values:
+            with self._lock:
+                self._values[name] = value
+        else:
+            object.__setattr__(self, name, value)
+
+    def _add(self, name: str, by: int = 1) -> None:
         with self._lock:
-            setattr(self, name, getattr(self, name) + by)
+            self._values[name] += by
 
+    # -- events
     def record_worker(self, worker_id) -> None:
         with self._lock:
-            self._worker_seen[worker_id] = time.monotonic()
+            self._last_seen[worker_id] = time.monotonic()
 
     def active_workers(self, window: float | None = None) -> int:
-        w = self._LIVENESS_WINDOW if window is None else window
-        now = time.monotonic()
+        horizon = time.monotonic() - (self.LIVENESS_WINDOW if window is None else window)
         with self._lock:
-            return sum(1 for t in self._worker_seen.values() if now - t <= w)
+            return sum(t >= horizon for t in self._last_seen.values())
 
     def record_update(self, staleness: int) -> None:
         with self._lock:
-            self.accepted_updates += 1
-            self.staleness_sum += staleness
-            self.max_staleness = max(self.max_staleness, staleness)
+            v = self._values
+            v["accepted_updates"] += 1
+            v["staleness_sum"] += staleness
+            v["max_staleness"] = max(v["max_staleness"], staleness)
 
     def record_stale_reject(self) -> None:
-        self._bump("stale_rejected")
+        self._add("stale_rejected")
 
     def record_invalid_reject(self) -> None:
-        self._bump("invalid_rejected")
+        self._add("invalid_rejected")
 
     def record_norm_clip(self) -> None:
-        self._bump("norm_clipped")
+        self._add("norm_clipped")
 
     def record_poison_flag(self) -> None:
-        self._bump("poison_flagged")
+        self._add("poison_flagged")
 
     def record_handler_error(self) -> None:
-        self._bump("handler_errors")
+        self._add("handler_errors")
+
+    def _traffic(self, table: dict, msg: dict, nbytes: int) -> None:
+        count, total, fields, carried = table.get(msg.get("type"), (None, "bytes_control", {}, {}))
+        sizes = {f: payload_bytes(msg.get(f)) for f in fields}
+        with self._lock:
+            v = self._values
+            if count:
+                v[count] += 1
+            v[total] += nbytes
+            for f, counter in fields.items():
+                v[counter] += sizes[f]
+            for f, (counter, carries) in carried.items():
+                if carries(msg.get(f)):
+                    v[counter] += 1
 
     def record_out(self, msg: dict, nbytes: int) -> None:
-        with self._lock:
-            if msg.get("type") == "task":
-                self.tasks_sent += 1
-                self.bytes_down += nbytes
-                self.bytes_shared_weights += _tensor_bytes(msg.get("shared_weights"))
-                self.bytes_opt += _tensor_bytes(msg.get("opt_state"))
-                if msg.get("private_weights"):
-                    self.tasks_with_private_down += 1
-                    self.bytes_private_down += _tensor_bytes(msg["private_weights"])
-                if msg.get("shard") is not None:
-                    self.tasks_with_shard += 1
-                    self.bytes_shard += _tensor_bytes(msg["shard"])
-                return
-            if msg.get("type") == "idle":
-                self.idle += 1
-            self.bytes_control += nbytes
+        self._traffic(_TRAFFIC_OUT, msg, nbytes)
 
     def record_in(self, msg: dict, nbytes: int) -> None:
-        with self._lock:
-            kind = msg.get("type")
-            if kind == "submit":
-                self.submits += 1
-                self.bytes_up += nbytes
-                self.bytes_shared_grad += _tensor_bytes(msg.get("shared_grad"))
-                self.bytes_private_up += _tensor_bytes(msg.get("private_weights"))
-                self.bytes_opt += _tensor_bytes(msg.get("opt_state"))
-                return
-            if kind == "heartbeat":
-                self.heartbeats += 1
-            elif kind == "nack":
-                self.nacks += 1
-            self.bytes_control += nbytes
+        self._traffic(_TRAFFIC_IN, msg, nbytes)
 
+    # -- views
     def summary(self) -> dict:
         now = time.monotonic()
         with self._lock:
-            d = {k: v for k, v in self.__dict__.items() if not k.startswith("_")}
-            d["throughput_tasks_per_s"] = self.tasks_sent / self._wall if self._wall else 0.0
-            d["mean_staleness"] = self.staleness_sum / self.accepted_updates if self.accepted_updates else 0.0
-            d["active_workers"] = sum(1 for t in self._worker_seen.values() if now - t <= self._LIVENESS_WINDOW)
-            return d
+            out = dict(self._values)
+            live = sum(now - t <= self.LIVENESS_WINDOW for t in self._last_seen.values())
+        out["throughput_tasks_per_s"] = out["tasks_sent"] / self._wall if self._wall else 0.0
+        out["mean_staleness"] = out["staleness_sum"] / out["accepted_updates"] if out["accepted_updates"] else 0.0
+        out["active_workers"] = live
+        return out
 
     def prometheus(self, namespace: str = "opendipaco_transport") -> str:
-        out = []
-        for k, v in self.summary().items():
-            gauge = k in self._GAUGES
-            name = f"{namespace}_{k}" if gauge else f"{namespace}_{k}_total"
-            out += [f"# TYPE {name} {'gauge' if gauge else 'counter'}", f"{name} {v}"]
-        return "\n".join(out) + "\n"
+        """Prometheus text exposition: counters as ``<ns>_<name>_total``, gauges as
+        ``<ns>_<name>``."""
+        lines = []
+        for name, value in self.summary().items():
+            kind = "gauge" if name in _GAUGES else "counter"
+            metric = f"{namespace}_{name}" if kind == "gauge" else f"{namespace}_{name}_total"
+            lines.append(f"# TYPE {metric} {kind}\n{metric} {value}")
+        return "\n".join(lines) + "\n"
 
     def report(self) -> str:
         s = self.summary()
-        return "\n".join([
-            f"accepted={s['accepted_updates']} stale_rejected={s['stale_rejected']} "
-            f"mean_staleness={s['mean_staleness']:.1f} max_staleness={s['max_staleness']} "
-            f"tasks={s['tasks_sent']} throughput={s['throughput_tasks_per_s']:.1f}/s",
-            f"reclaims={s['reclaims']} nacks={s['nacks']} heartbeats={s['heartbeats']}",
-            f"bytes  down={_fmt(s['bytes_down'])}  up={_fmt(s['bytes_up'])}  control={_fmt(s['bytes_control'])}",
-            f"  optimizer-on-wire={_fmt(s['bytes_opt'])}",
-        ])
+        return (f"accepted={s['accepted_updates']} stale_rejected={s['stale_rejected']} "
+                f"mean_staleness={s['mean_staleness']:.1f} max_staleness={s['max_staleness']} "
+                f"tasks={s['tasks_sent']} throughput={s['throughput_tasks_per_s']:.1f}/s\n"
+                f"reclaims={s['reclaims']} nacks={s['nacks']} heartbeats={s['heartbeats']}\n"
+                f"bytes  down={human_bytes(s['bytes_down'])}  up={human_bytes(s['bytes_up'])}  "
+                f"control={human_bytes(s['bytes_control'])}\n"
+                f"  optimizer-on-wire={human_bytes(s['bytes_opt'])}")
 
 
-@dataclass(eq=False)
-class _Conn:
-    sock: socket.socket
-    inbuf: bytearray = field(default_factory=bytearray)
-    outbuf: bytearray = field(default_factory=bytearray)
-    authed: bool = False
-    peer_id: str | None = None
-    nonce: bytes | None = None
-    want_write: bool = False
-    closed: bool = False
-    tls: bool = False
-    handshaking: bool = False
-
-
-class _Loop:
-    """One selector thread serving many non-blocking connections."""
-
-    def __init__(self, server: "ReactorServer"):
-        self.srv = server
-        self.sel = selectors.DefaultSelector()
-        self._rd, self._wr = socket.socketpair()
-        self._rd.setblocking(False)
-        self.sel.register(self._rd, selectors.EVENT_READ, data=None)
-        self._pending: list[_Conn] = []
-        self._plock = threading.Lock()
-        self.thread = threading.Thread(target=self._run, daemon=True)
-
-    def add(self, conn: _Conn) -> None:
-        with self._plock:
-            self._pending.append(conn)
-        self.wake()
-
-    def wake(self) -> None:
+# ---------------------------------------------------------------------- server
+def _listen(host: str, port: int) -> socket.socket:
+    """A listening socket on (host, port); a port still held by a closing predecessor
+    is retried for up to 3 s (restart-in-place tests rebind the same port)."""
+    sock = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
+    sock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+    give_up = time.monotonic() + 3.0
+    while True:
         try:
-            self._wr.send(b"!")
+            sock.bind((host, port))
+            break
         except OSError:
-            pass
+            if time.monotonic() > give_up:
+                sock.close()
+                raise
+            time.sleep(0.1)
+    sock.listen(128)
+    sock.setblocking(False)
+    return sock
 
-    def _run(self) -> None:
-        while not self.srv._io_stop and not self.srv._dead:
-            try:
-                events = self.sel.select(timeout=0.2)
-            except OSError:
-                break
-            for key, mask in events:
-                if key.data is None:
-                    try:
-                        self._rd.recv(65536)
-                    except OSError:
-                        pass
-                    self._adopt()
-                    continue
-                conn = key.data
-                if conn.handshaking:
-                    self._tls_step(conn)
-                    continue
-                if mask & selectors.EVENT_READ:
-                    self._read(conn)
-                if not conn.closed and mask & selectors.EVENT_WRITE:
-                    self._flush(conn)
-        for key in list(self.sel.get_map().values()):
-            if key.data is not None:
-                self._close(key.data)
-        try:
-            self.sel.close()
-        except OSError:
-            pass
 
-    def _adopt(self) -> None:
-        with self._plock:
-            new, self._pending = self._pending, []
-        for conn in new:
-            try:
-                self.sel.register(conn.sock, selectors.EVENT_READ, data=conn)
-            except (KeyError, ValueError, OSError):
-                self._close(conn)
-                continue
-            self._tls_step(conn) if conn.handshaking else self._greet(conn)
-
-    def _greet(self, conn: _Conn) -> None:
-        if self.srv.auth_keys is not None or self.srv.admitted_peers is not None:
-            conn.nonce = os.urandom(32)
-            self._send(conn, {"type": "challenge", "nonce": conn.nonce.hex()})
-        else:
-            conn.authed = True
-
-    def _tls_step(self, conn: _Conn) -> None:
-        try:
-            conn.sock.do_handshake()
-        except ssl.SSLWantReadError:
-            self._want_write(conn, False)
-            return
-        except ssl.SSLWantWriteError:
-            self._want_write(conn, True)
-            return
-        except (ssl.SSLError, OSError):
-            self._close(conn)
-            return
-        conn.handshaking = False
-        self._want_write(conn, False)
-        self._greet(conn)
-
-    def _read(self, conn: _Conn) -> None:
-        while not conn.closed:
-            try:
-                data = conn.sock.recv(1 << 20)
-            except (BlockingIOError, ssl.SSLWantReadError):
-                return
-            except ssl.SSLWantWriteError:
-                self._want_write(conn, True)
-                return
-            except OSError:
-                self._close(conn)
-                return
-            if not data:
-                self._close(conn)
-                return
-            conn.inbuf += data
-            self._frames(conn)
-            if not (conn.tls and conn.sock.pending()):
-                return
-
-    def _frames(self, conn: _Conn) -> None:
-        while not conn.closed and len(conn.inbuf) >= _LEN.size:
-            (n,) = _LEN.unpack_from(conn.inbuf, 0)
-            if n > self.srv.max_msg_bytes:
-                self._close(conn)
-                return
-            if len(conn.inbuf) < _LEN.size + n:
-                return
-            body = bytes(conn.inbuf[_LEN.size:_LEN.size + n])
-            del conn.inbuf[:_LEN.size + n]
-            try:
-                msg = decode(body)
-            except Exception:
-                self._close(conn)
-                return
-            try:
-                self._dispatch(conn, msg, n + _LEN.size)
-            except Exception:
-                self.srv.metrics.record_handler_error()
-                self._close(conn)
-                return
-
-    def _dispatch(self, conn: _Conn, msg: dict, nin: int) -> None:
-        srv = self.srv
-        if not conn.authed:
-            ok = False
-            if conn.nonce is not None and msg.get("type") == "auth":
-                if srv.auth_keys is not None and "mac" in msg:
-                    ok = verify_mac(msg.get("mac", ""), conn.nonce, srv.auth_keys)
-                if not ok and srv.admitted_peers is not None and "pub" in msg:
-                    pub = msg.get("pub", "")
-                    if srv.peer_admitted(pub) and verify_auth(pub, msg.get("sig", ""), conn.nonce):
-                        ok, conn.peer_id = True, peer_id_of(pub)
-            if ok:
-                conn.authed = True
-                self._send(conn, {"type": "welcome"})
-            else:
-                self._close(conn)
-            return
-        if msg.get("worker_id") is not None:
-            srv.metrics.record_worker(msg["worker_id"])
-        srv.metrics.record_in(msg, nin)
-        reply = srv._handle(msg, nin, conn.peer_id)
-        if reply is not None:
-            srv.metrics.record_out(reply, self._send(conn, reply))
-
-    def _send(self, conn: _Conn, msg: dict) -> int:
-        data = encode(msg)
-        frame = _LEN.pack(len(data)) + data
-        conn.outbuf += frame
-        self._flush(conn)
-        return len(frame)
-
-    def _flush(self, conn: _Conn) -> None:
-        if conn.closed:
-            return
-        if conn.outbuf:
-            try:
-                sent = conn.sock.send(conn.outbuf)
-                del conn.outbuf[:sent]
-            except (BlockingIOError, ssl.SSLWantWriteError, ssl.SSLWantReadError):
-                pass
-            except OSError:
-                self._close(conn)
-                return
-        self._want_write(conn, bool(conn.outbuf))
-
-    def _want_write(self, conn: _Conn, on: bool) -> None:
-        if conn.closed or conn.want_write == on:
-            return
-        try:
-            self.sel.modify(conn.sock, selectors.EVENT_READ | (selectors.EVENT_WRITE if on else 0), data=conn)
-            conn.want_write = on
-        except (KeyError, OSError):
-            self._close(conn)
-
-    def _close(self, conn: _Conn) -> None:
-        if conn.closed:
-            return
-        conn.closed = True
-        for fn in (lambda: self.sel.unregister(conn.sock), conn.sock.close):
-            try:
-                fn()
-            except (KeyError, OSError, ValueError):
-                pass
-        self.srv._conn_closed(conn)
+class _Closed(Exception):
+    """The connection is to be dropped (protocol violation, peer gone, shutdown)."""
 
 
 class ReactorServer:
@@ -403,147 +229,218 @@ class ReactorServer:
                  max_connections: int = 1024, tls: "ssl.SSLContext | None" = None):
         self.auth_key = auth_key
         self.auth_keys = acceptable_keys(auth_key, accept_keys)
-        self._peer_lock = threading.Lock()
-        self.admitted_peers = {_pubkey_hex(p) for p in admitted_peers} if admitted_peers is not None else None
+        self._admit_lock = threading.Lock()
+        self.admitted_peers = None if admitted_peers is None else {self._hex(p) for p in admitted_peers}
         self.max_msg_bytes = max_msg_bytes
         self.tls = tls
         self.io_threads = max(1, io_threads)
         self.max_connections = max_connections
         self.metrics = TransportMetrics()
-        self._sock = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
-        self._sock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
-        deadline = time.monotonic() + 3.0
-        while True:
-            try:
-                self._sock.bind((host, port))
-                break
-            except OSError:
-                if time.monotonic() >= deadline:
-                    raise
-                time.sleep(0.1)
-        self._sock.listen(128)
-        self.port = self._sock.getsockname()[1]
-        self._stop = self._io_stop = self._dead = False
-        self._loops: list[_Loop] = []
-        self._accept_thread = None
-        self._conn_lock = threading.Lock()
-        self._registry: set = set()
-        self._open = 0
-        self._rr = 0
-        self._exporter = self._logger = None
+        self._listener = _listen(host, port)
+        self.port = self._listener.getsockname()[1]
+        self._stop = False  # graceful shutdown requested (handlers may answer "stop")
+        self._dead = False  # crashed: every connection dropped
+        self._loop: asyncio.AbstractEventLoop | None = None
+        self._thread: threading.Thread | None = None
+        self._workers: ThreadPoolExecutor | None = None
+        self._server = None
+        self._writers: set = set()
+        self._observers: list = []
+
+    @staticmethod
+    def _hex(pub) -> str:
+        return getattr(pub, "public_key_hex", pub).lower()
 
     def _handle(self, msg: dict, nbytes: int, peer_id: str | None = None):
         raise NotImplementedError
 
-    # identity admission
+    # -------------------------------------------------------------- admission
     def peer_admitted(self, pub: str) -> bool:
-        with self._peer_lock:
+        with self._admit_lock:
             return self.admitted_peers is not None and pub.lower() in self.admitted_peers
 
     def peer_id_admitted(self, peer_id: str) -> bool:
-        with self._peer_lock:
-            return self.admitted_peers is None or peer_id in {peer_id_of(p) for p in self.admitted_peers}
+        with self._admit_lock:
+            if self.admitted_peers is None:
+                return True
+            return any(peer_id_of(p) == peer_id for p in self.admitted_peers)
 
     def admit_peer(self, pub) -> None:
-        with self._peer_lock:
+        with self._admit_lock:
             if self.admitted_peers is None:
                 self.admitted_peers = set()
-            self.admitted_peers.add(_pubkey_hex(pub))
+            self.admitted_peers.add(self._hex(pub))
 
     def revoke_peer(self, pub) -> None:
-        with self._peer_lock:
+        with self._admit_lock:
             if self.admitted_peers is not None:
-                self.admitted_peers.discard(_pubkey_hex(pub))
+                self.admitted_peers.discard(self._hex(pub))
 
-    # observability
-    def start_metrics_server(self, *, host: str = "0.0.0.0", port: int = 0,
-                             namespace: str = "opendipaco_transport"):
+    # -------------------------------------------------------------- observability
+    def start_metrics_server(self, *, host: str = "0.0.0.0", port: int = 0, namespace: str = "opendipaco_transport"):
         from .observability import MetricsExporter
 
-        self._exporter = MetricsExporter(self.metrics, host=host, port=port, namespace=namespace).start()
-        return self._exporter
+        exporter = MetricsExporter(self.metrics, host=host, port=port, namespace=namespace).start()
+        self._observers.append(exporter)
+        return exporter
 
     def start_metrics_logging(self, *, interval: float = 10.0, sink=None):
         from .observability import MetricsLogger
 
-        self._logger = MetricsLogger(self.metrics, interval=interval, sink=sink).start()
-        return self._logger
+        logger = MetricsLogger(self.metrics, interval=interval, sink=sink).start()
+        self._observers.append(logger)
+        return logger
 
-    # lifecycle
+    # -------------------------------------------------------------- lifecycle
     def start(self) -> None:
-        self._loops = [_Loop(self) for _ in range(self.io_threads)]
-        for lp in self._loops:
-            lp.thread.start()
-        self._accept_thread = threading.Thread(target=self._accept, daemon=True)
-        self._accept_thread.start()
+        self._workers = ThreadPoolExecutor(max_workers=self.io_threads, thread_name_prefix="odp-io")
+        self._loop = asyncio.new_event_loop()
+        up = threading.Event()
 
-    def _accept(self) -> None:
-        while not self._stop and not self._dead:
+        def run():
+            asyncio.set_event_loop(self._loop)
+            self._server = self._loop.run_until_complete(
+                asyncio.start_server(self._session, sock=self._listener, limit=1 << 22,
+                                     **({"ssl": self.tls, "ssl_handshake_timeout": 30.0} if self.tls else {})))
+            up.set()
             try:
-                sock, _ = self._sock.accept()
-            except OSError:
-                return
-            with self._conn_lock:
-                if self._open >= self.max_connections:
-                    sock.close()
-                    continue
-                self._open += 1
-            sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
-            sock.setblocking(False)
-            if self.tls is not None:
-                try:
-                    sock = self.tls.wrap_socket(sock, server_side=True, do_handshake_on_connect=False)
-                except (ssl.SSLError, OSError):
-                    sock.close()
-                    with self._conn_lock:
-                        self._open -= 1
-                    continue
-                conn = _Conn(sock=sock, tls=True, handshaking=True)
-            else:
-                conn = _Conn(sock=sock)
-            with self._conn_lock:
-                self._registry.add(conn)
-            self._loops[self._rr % len(self._loops)].add(conn)
-            self._rr += 1
+                self._loop.run_forever()
+            finally:
+                self._loop.run_until_complete(self._loop.shutdown_asyncgens())
+                self._loop.close()
 
-    def _conn_closed(self, conn: _Conn) -> None:
-        with self._conn_lock:
-            if conn in self._registry:
-                self._registry.discard(conn)
-                self._open -= 1
+        self._thread = threading.Thread(target=run, name=f"odp-reactor-{self.port}", daemon=True)
+        self._thread.start()
+        if not up.wait(10.0):
+            raise RuntimeError("reactor event loop did not start")
+
+    def _on_loop(self, fn) -> None:
+        loop = self._loop
+        if loop is not None and loop.is_running():
+            try:
+                loop.call_soon_threadsafe(fn)
+            except RuntimeError:  # the loop closed meanwhile
+                pass
+
+    def _teardown(self, abort: bool) -> None:
+        """On the loop: stop accepting, drop every connection (RST when ``abort``), stop."""
+        if self._server is not None:
+            self._server.close()
+        for w in list(self._writers):
+            if abort:
+                w.transport.abort()
+            else:
+                w.close()
+        self._loop.call_later(0.05, self._loop.stop)
+
+    def _finish(self) -> None:
+        if self._thread is not None:
+            self._thread.join(timeout=5.0)
+        if self._workers is not None:
+            self._workers.shutdown(wait=False, cancel_futures=True)
+        try:
+            self._listener.close()
+        except OSError:
+            pass
 
     def shutdown(self) -> None:
+        """Graceful stop: no new connections; connections still being served get a short
+        grace period (handlers answer "stop" from now on), then all are closed."""
         self._stop = True
-        for obs in (self._exporter, self._logger):
-            if obs is not None:
-                obs.stop()
-        try:
-            self._sock.close()
-        except OSError:
-            pass
-        time.sleep(0.2)
-        self._io_stop = True
-        for lp in self._loops:
-            lp.wake()
-        time.sleep(0.1)
+        for obs in self._observers:
+            obs.stop()
+        self._on_loop(lambda: self._server.close() if self._server is not None else None)
+        time.sleep(0.25)
+        self._on_loop(lambda: self._teardown(abort=False))
+        self._finish()
 
     def simulate_crash(self) -> None:
-        """Drop every connection abruptly (tests of restart / reconnect)."""
-        self._dead = self._io_stop = True
-        with self._conn_lock:
-            conns = list(self._registry)
-        for conn in conns:
-            for fn in (lambda: conn.sock.shutdown(socket.SHUT_RDWR), conn.sock.close):
-                try:
-                    fn()
-                except OSError:
-                    pass
+        """Drop every connection abruptly and stop serving, as a killed process would (for
+        tests of failover, reconnect and restart-in-place)."""
+        self._dead = True
+        self._stop = True
+        self._on_loop(lambda: self._teardown(abort=True))
+        self._finish()
+
+    # -------------------------------------------------------------- one connection
+    async def _read_frame(self, reader: asyncio.StreamReader, cap: int) -> tuple[bytes, int]:
+        head = await reader.readexactly(_LEN.size)
+        (n,) = _LEN.unpack(head)
+        if n > cap:
+            raise _Closed(f"frame of {n} bytes above the cap {cap}")
+        return await reader.readexactly(n), _LEN.size + n
+
+    @staticmethod
+    def _frame(msg: dict) -> bytes:
+        body = encode(msg)
+        return _LEN.pack(len(body)) + body
+
+    async def _authenticate(self, reader, writer) -> tuple[bool, str | None]:
+        """Challenge / response when the server requires it: (accepted, peer id)."""
+        if self.auth_keys is None and self.admitted_peers is None:
+            return True, None
+        nonce = os.urandom(32)
+        writer.write(self._frame({"type": "challenge", "nonce": nonce.hex()}))
+        await writer.drain()
+        body, _ = await self._read_frame(reader, self.max_msg_bytes)
+        msg = decode(body)
+        if msg.get("type") != "auth":
+            return False, None
+        if self.auth_keys is not None and "mac" in msg and verify_mac(msg.get("mac", ""), nonce, self.auth_keys):
+            accepted, peer = True, None
+        elif (self.admitted_peers is not None and "pub" in msg and self.peer_admitted(msg.get("pub", ""))
+              and verify_auth(msg["pub"], msg.get("sig", ""), nonce)):
+            accepted, peer = True, peer_id_of(msg["pub"])
+        else:
+            return False, None
+        writer.write(self._frame({"type": "welcome"}))
+        await writer.drain()
+        return accepted, peer
+
+    def _serve_one(self, body: bytes, nbytes: int, peer_id):
+        """Worker thread: decode, account, handle, encode. Returns (reply, frame) or None."""
+        msg = decode(body)
+        if msg.get("worker_id") is not None:
+            self.metrics.record_worker(msg["worker_id"])
+        self.metrics.record_in(msg, nbytes)
         try:
-            self._sock.close()
-        except OSError:
+            reply = self._handle(msg, nbytes, peer_id)
+        except Exception:
+            self.metrics.record_handler_error()
+            raise
+        return None if reply is None else (reply, self._frame(reply))
+
+    async def _session(self, reader: asyncio.StreamReader, writer: asyncio.StreamWriter) -> None:
+        if self._stop or len(self._writers) >= self.max_connections:
+            writer.transport.abort()
+            return
+        self._writers.add(writer)
+        sock = writer.get_extra_info("socket")
+        if sock is not None:
+            try:
+                sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
+            except OSError:
+                pass
+        loop = asyncio.get_running_loop()
+        try:
+            accepted, peer_id = await self._authenticate(reader, writer)
+            while accepted and not self._dead:
+                body, nbytes = await self._read_frame(reader, self.max_msg_bytes)
+                out = await loop.run_in_executor(self._workers, self._serve_one, body, nbytes, peer_id)
+                if out is not None:
+                    reply, frame = out
+                    writer.write(frame)
+                    await writer.drain()
+                    self.metrics.record_out(reply, len(frame))
+        except (_Closed, asyncio.IncompleteReadError, ConnectionError, ssl.SSLError, OSError, ValueError,
+                TypeError, KeyError, RuntimeError):
             pass
-        for lp in self._loops:
-            lp.wake()
+        except Exception:  # a handler failure: already counted; the connection is dropped
+            pass
+        finally:
+            self._writers.discard(writer)
+            if not writer.is_closing():
+                writer.close()
 
 
 _ReactorServer = ReactorServer

@@ -33,9 +33,13 @@ outer SGD-Nesterov.
 
 from __future__ import annotations
 
+import logging
 import math
 import os
+from collections import defaultdict
 from dataclasses import dataclass
+
+import numpy as np
 
 import torch
 from torch import nn
@@ -44,12 +48,21 @@ from ..models.llama import rope_cos_sin
 from ..models.path import build_path_model
 from ..ops import attention as attn
 from ..ops._ext import check_errors, err_word, ext
-from ..ops.outer import MODE_COPY, MODE_OUTER, OuterPlan, Segment
+from ..ops.outer import MODE_APPLY, MODE_COPY, MODE_OUTER, OuterPlan, Segment
 from ..optim.adam8bit import Adam8bit
 from ..optim.diloco import inner_lr_at, make_inner_optimizer
 from ..topology import Path, is_private_key
 
 ALIGN = 256
+log = logging.getLogger(__name__)
+
+# tables of the last inner step's AdamW + pseudo-gradient kernel (csrc/adam.cu)
+ACC_REGION = np.dtype([("begin", "<i8"), ("end", "<i8"), ("first", "<i4"), ("count", "<i4"), ("cta0", "<i8")])
+ACC_CTA_ELEMS = 1024  # elements of one region per CTA of adamw_acc_step
+ACC_MAX_ENTRIES = 128  # (path, key) entries of one region
+ACC_ENTRY = np.dtype([("delta", "<u8"), ("glob", "<u8"), ("g", "<i4"), ("flags", "<i4"), ("weight", "<f4"),
+                      ("pad", "<i4")])
+assert ACC_REGION.itemsize == 32 and ACC_ENTRY.itemsize == 32
 
 
 def _ru(n: int, a: int = ALIGN) -> int:
@@ -100,6 +113,23 @@ class PathLayout:
         self.emb = self.by_name["embed.embed_tokens.weight"][1]
         self.normf = self.by_name["head.norm.weight"][1]
         self.lm = self.by_name["head.lm_head.weight"][1]
+
+
+def acc_region_table(regions: dict) -> tuple[np.ndarray, list, int]:
+    """Region records of ``adamw_acc_step`` for ``{(begin, end): [entries]}``: each region
+    gets ceil((end - begin) / ACC_CTA_ELEMS) CTAs, in ascending order of ``begin``.
+    Returns (records, an empty entry list to fill in the same order, total CTAs)."""
+    reg = np.zeros(len(regions), dtype=ACC_REGION)
+    first = cta = 0
+    for ri, ((a, b), lst) in enumerate(sorted(regions.items())):
+        if len(lst) > ACC_MAX_ENTRIES:
+            raise ValueError(f"adamw_acc_step: {len(lst)} (path, key) entries in one region (max {ACC_MAX_ENTRIES})")
+        if a % 4:
+            raise ValueError("adamw_acc_step: regions must begin at a multiple of 4 elements")
+        reg[ri] = (a, b, first, len(lst), cta)
+        first += len(lst)
+        cta += (b - a + ACC_CTA_ELEMS - 1) // ACC_CTA_ELEMS
+    return reg, [], cta
 
 
 def _rebind(module: nn.Module, prefix_map, flat: torch.Tensor, layout_by_name, prefix: str) -> None:
@@ -201,6 +231,17 @@ class FusedExecutor:
         self.outer_steps = 0
         self._plan: OuterPlan | None = None
         self._plan_weights = None
+        # the last inner step's AdamW also accumulates the outer pseudo-gradient of every
+        # module key (plain AdamW, one GPU per path group); the outer step then reads one
+        # partial per key instead of every working copy again
+        self.acc_fused = (not self.opt8 and self.dp == 1 and os.environ.get("ODP_ACC_FUSED", "1") != "0")
+        self._deltas: dict[str, torch.Tensor] = {}
+        self._acc_w: dict[tuple[str, int], float] = {}
+        self.ACC_REG = self.ACC_ENT = None
+        self.acc_nregs = self.acc_ctas = 0
+        # elements the outer step's guard skipped because their pseudo-gradient was not finite
+        self.OUTER_STATUS = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.outer_nonfinite = 0
 
         # -- step buffers are sized on the first round ---------------------------------
         self._shape = None
@@ -360,6 +401,7 @@ class FusedExecutor:
         self.ids_host, self.labels_host = self._host[0]["ids"], self._host[0]["labels"]
         self.sched_host = self._host[0]["sched"]
         self.loss_host = torch.zeros(G, dtype=torch.float32).pin_memory()
+        self.status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.invc_host = self._host[0]["invc"]
         self.cos, self.sin = rope_cos_sin(64, bb.rope_theta, S, dev)
         self.err = err_word(dev)
@@ -400,7 +442,7 @@ class FusedExecutor:
                         kw.get("sq_ld", 0))
 
     # ------------------------------------------------------------------ one inner step
-    def _step(self, s: int) -> None:
+    def _step(self, s: int, last: bool = False) -> None:
         X_ = ext()
         bb, G, P = self.bb, self.G, self.P
         H, Fd, V = bb.hidden_size, bb.intermediate_size, bb.vocab_size
@@ -509,6 +551,10 @@ class FusedExecutor:
             X_.adam8bit_step(self.W32.view(-1), self.GRAD.view(-1), self.MQ, self.MABS, self.VQ, self.VLO,
                              self.VSC, self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay,
                              False, self.W16.view(-1), P // ALIGN)
+        elif last and self.acc_fused:
+            X_.adamw_acc_step(self.W32, self.GRAD, self.MOM1, self.MOM2, self.W16, self.acc_ctas, P, P, self.COEF,
+                              self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, rows, lay.emb, H, V, self.ACC_REG,
+                              self.acc_nregs, self.ACC_ENT)
         else:
             X_.adamw_step(self.W32, self.GRAD, self.MOM1, self.MOM2, self.W16, P, P, P, G, self.COEF,
                           self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, rows, lay.emb, H, V)
@@ -590,6 +636,7 @@ class FusedExecutor:
             slot = self._slot
             active = self._prepare(corpus, batch_size, round_idx, slot)
         self._ahead = None
+        self._ensure_plan(corpus, active)
         self._upload(slot)
         self._run_inner(steps)
         for g, a in enumerate(active):
@@ -606,8 +653,15 @@ class FusedExecutor:
             last = last.clone()
             self.e.backend.dp_allreduce(last)  # partial losses of the group's batch slices
         self.loss_host.copy_(last, non_blocking=True)
+        self.status_host.copy_(self.OUTER_STATUS, non_blocking=True)
+        self.OUTER_STATUS.zero_()
         torch.cuda.current_stream(self.dev).synchronize()
         check_errors(self.dev)
+        bad = int(self.status_host[0])
+        if bad:
+            self.outer_nonfinite += bad
+            log.warning("outer step: %d element(s) with a non-finite pseudo-gradient were left unchanged "
+                        "(a path diverged)", bad)
         losses = {p: float(self.loss_host[g]) for g, p in enumerate(self.paths) if active[g]}
         return losses, norms
 
@@ -616,26 +670,77 @@ class FusedExecutor:
         attributes), then from one captured CUDA graph."""
         if not self.e.exec.cuda_graphs:
             for s in range(steps):
-                self._step(s)
+                self._step(s, last=s == steps - 1)
             return
         if self._graph is None:
             if not self._warm:
                 for s in range(steps):
-                    self._step(s)
+                    self._step(s, last=s == steps - 1)
                 self._warm = True
                 return
             torch.cuda.synchronize(self.dev)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 for s in range(steps):
-                    self._step(s)
+                    self._step(s, last=s == steps - 1)
             self._graph = graph
         self._graph.replay()
 
     # ------------------------------------------------------------------ outer step
+    def _delta(self, key: str) -> torch.Tensor:
+        """The pseudo-gradient buffer of a shared key: the backend's peer-addressable one
+        when it has one (cross-GPU outer step), else a local buffer."""
+        if key not in self._deltas:
+            be = self.e.backend
+            if hasattr(be, "delta_view"):
+                self._deltas[key] = be.delta_view(key)
+            else:
+                self._deltas[key] = torch.zeros(self._region_size(key), device=self.dev, dtype=torch.float32)
+        return self._deltas[key]
+
+    def _ensure_plan(self, corpus, active) -> None:
+        """Build the outer plan (and the fused-optimizer tables) for these shard weights
+        before the round's inner steps run."""
+        wkey = (id(corpus), tuple(active))
+        if self._plan is None or self._plan_weights != wkey:
+            self._plan = self._build_plan(corpus, active)
+            self._plan_weights = wkey
+            if self.acc_fused:
+                self._build_acc_tables()
+
+    def _build_acc_tables(self) -> None:
+        """Region / entry tables of ``adamw_acc_step``: per region of the path layout, every
+        (path, key) pair sorted by key then path, with the key's pseudo-gradient and global
+        buffers and the path's outer weight."""
+        order = {k: i for i, k in enumerate(self.topo.module_keys())}
+        regions = defaultdict(list)
+        for g, path in enumerate(self.paths):
+            for key in self.topo.path_module_keys(path):
+                regions[self._region(key)].append((order[key], g, key))
+        reg, ents, ctas = acc_region_table(regions)
+        for ri, ((a, b), lst) in enumerate(sorted(regions.items())):
+            lst.sort()
+            for idx, (_, g, key) in enumerate(lst):
+                last = idx + 1 == len(lst) or lst[idx + 1][2] != key
+                delta = 0 if is_private_key(key) else self._delta(key).data_ptr()
+                ents.append((delta, self.glob[key].data_ptr(), g, 1 if last else 0, self._acc_w.get((key, g), 0.0),
+                             0))
+        ent = np.array(ents, dtype=ACC_ENTRY)
+        r_t = torch.from_numpy(reg.view(np.int64).copy())
+        e_t = torch.from_numpy(ent.view(np.int64).copy())
+        if self.ACC_REG is not None and self.ACC_REG.shape == r_t.shape and self.ACC_ENT.shape == e_t.shape:
+            # same storage: a captured graph reads the new weights on its next replay
+            self.ACC_REG.copy_(r_t)
+            self.ACC_ENT.copy_(e_t)
+        else:
+            self.ACC_REG, self.ACC_ENT = r_t.to(self.dev), e_t.to(self.dev)
+            self._graph, self._warm = None, False
+        self.acc_nregs, self.acc_ctas = len(reg), ctas
+
     def _build_plan(self, corpus, active) -> OuterPlan:
         e = self.e
         segs = []
+        single = getattr(e.backend, "world_size", 1) == 1
         for key in self.topo.module_keys():
             if key not in e.bank:
                 continue
@@ -648,8 +753,10 @@ class FusedExecutor:
                 pidx = self.topo.path_index(self.paths[g])
                 lead = self.dp == 1 or self.dp_index == 0  # a path's DP replicas hold the same delta
                 w.append(e._outer_weight(key, pidx, corpus) if active[g] and lead else 0.0)
+                self._acc_w[(key, g)] = w[-1]
             if is_private_key(key):
-                if users:
+                # with the fused optimizer the last inner step already copied it
+                if users and not self.acc_fused:
                     segs.append(Segment(key, self.glob[key], None, loc32[:1], [None], [1.0], mode=MODE_COPY))
                 continue
             # the normaliser is global: every path through the key with a non-empty shard
@@ -659,18 +766,18 @@ class FusedExecutor:
                 if corpus.shard(pi).size(0) > 0:
                     den += e._outer_weight(key, pi, corpus)
             inv = 1.0 / max(den, 1e-12) if e.diloco.normalize_outer_delta else 1.0
-            segs.append(Segment(key, self.glob[key], self.mom[key], loc32, loc16, w, MODE_OUTER,
-                                e.outer_scale(key), inv))
+            # one GPU with the fused optimizer: the pseudo-gradient is ready, apply it;
+            # cross-GPU backends split OUTER segments into their own phases
+            mode = MODE_APPLY if (self.acc_fused and single) else MODE_OUTER
+            segs.append(Segment(key, self.glob[key], self.mom[key], loc32, loc16, w, mode,
+                                e.outer_scale(key), inv, self._delta(key) if self.acc_fused else None))
         plan = OuterPlan(segs, self.dev)
         plan.build()
         return plan
 
     def _outer(self, corpus, active):
         e = self.e
-        wkey = (id(corpus), tuple(active))
-        if self._plan is None or self._plan_weights != wkey:
-            self._plan = self._build_plan(corpus, active)
-            self._plan_weights = wkey
+        self._ensure_plan(corpus, active)
         backend = e.backend
         dl = e.diloco
         if getattr(backend, "world_size", 1) > 1:
@@ -679,7 +786,8 @@ class FusedExecutor:
             backend.fused_outer_step(self, self._plan, first=self.outer_steps == 0)
             norms = backend.delta_norms()
         else:
-            self._plan.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first=self.outer_steps == 0)
+            self._plan.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first=self.outer_steps == 0,
+                           status=self.OUTER_STATUS)
             norms = self._plan.delta_norms()
         self.outer_steps += 1
         return [v for k, v in norms.items() if not is_private_key(k)]
@@ -697,13 +805,14 @@ class FusedExecutor:
         if getattr(self.e.backend, "world_size", 1) > 1:
             self.e.backend.fused_outer_step(self, self._plan, first=False)
         else:
-            self._plan.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first=False)
+            self._plan.run(dl.outer_lr, dl.outer_momentum, dl.outer_nesterov, first=False, status=self.OUTER_STATUS)
 
     def launches_per_round(self) -> int:
         """Kernels of this package launched per round (inner steps + outer step)."""
         per_step = (14 + 22 * self.L + (2 if self.dp > 1 else 0) - (1 if self.sq_bases is not None else 0)
                     + sum(1 for sp in self.wg_split.values() if sp > 1))
-        outer = getattr(self.e.backend, "outer_launches", 1) if getattr(self.e.backend, "world_size", 1) > 1 else 1
+        be = self.e.backend
+        outer = be.outer_launch_count(self) if getattr(be, "world_size", 1) > 1 else 1
         return self.e.diloco.inner_steps * per_step + outer
 
     def h2d_bytes_per_round(self) -> int:
@@ -711,7 +820,7 @@ class FusedExecutor:
 
     def d2h_bytes_per_round(self) -> int:
         chunks = self._plan.total_chunks if self._plan is not None else 0
-        return int(self.G * 4 + 4 + chunks * 4)
+        return int(self.G * 4 + 4 + chunks * 4 + 4)  # losses, error word, delta-norm partials, guard status
 
     # ------------------------------------------------------------------ API glue
     def path_model(self, path: Path) -> nn.Module:

@@ -176,6 +176,66 @@ def bench_ce(G: int, M: int, V: int, reps: int, flush) -> list[dict]:
     return out
 
 
+def bench_optim(G: int, H: int, V: int, F: int, layers: list[int], levels: list[int], reps: int, flush) -> list[dict]:
+    """The inner optimizer on G paths of the DiPaCo layout (embedding, one region per
+    level, head): plain AdamW, and the last step's AdamW that also accumulates the outer
+    pseudo-gradient of every module key (paths on a level split over its experts)."""
+    import numpy as np
+
+    from ..ops._ext import check_errors, ext
+    from ..train.fused import ACC_ENTRY, acc_region_table
+
+    dev = torch.device("cuda")
+    ru = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    per_layer = ru(3 * H * H) + ru(H * H) + ru(2 * F * H) + ru(H * F) + 2 * ru(H)
+    sizes = [ru(V * H)] + [per_layer * n for n in layers] + [ru(H) + ru(V * H)]
+    P = sum(sizes)
+    w32, gr = torch.randn(G, P, device=dev), torch.randn(G, P, device=dev) * 1e-3
+    m1, m2 = torch.zeros(G, P, device=dev), torch.zeros(G, P, device=dev)
+    w16 = torch.empty(G, P, device=dev, dtype=torch.bfloat16)
+    coef = torch.ones(G, device=dev)
+    sched = torch.tensor([[1e-3, 1e-3 / 0.1, 0.3, 1.0]] * G, device=dev)
+    # keys: the embedding and head shared by all G paths; level l's region split over
+    # levels[l] experts (path g uses expert (g // stride) % levels[l])
+    spans, o = [], 0
+    for n in sizes:
+        spans.append((o, o + n))
+        o += n
+    reg, ents, ctas = acc_region_table({sp: [0] * G for sp in spans})
+    bufs, off = [], 0
+    for r, n in enumerate(sizes):
+        groups: dict[int, list[int]] = {}
+        for g in range(G):
+            if r in (0, len(sizes) - 1):
+                expert = 0
+            else:  # digit r - 1 of the mixed-radix path index g
+                expert = (g // int(np.prod(levels[r:]))) % levels[r - 1]
+            groups.setdefault(expert, []).append(g)
+        for key in sorted(groups):
+            d, gl = torch.zeros(n, device=dev), torch.randn(n, device=dev)
+            bufs += [d, gl]
+            for j, g in enumerate(groups[key]):
+                ents.append((d.data_ptr(), gl.data_ptr(), g, int(j + 1 == len(groups[key])), 1.0 / G, 0))
+        off += n
+    rt = torch.from_numpy(reg.view(np.int64).copy()).to(dev)
+    et = torch.from_numpy(np.array(ents, dtype=ACC_ENTRY).view(np.int64).copy()).to(dev)
+    x = ext()
+    nbytes = G * P * (4 * 4 + 3 * 4 + 2)  # p, g, m, v in; p, m, v, bf16 p out
+    cases = [("adamw_step", lambda: x.adamw_step(w32, gr, m1, m2, w16, P, P, P, G, coef, sched, 0.9, 0.95, 1e-8, 0.1,
+                                                 None, 0, 1, 1)),
+             ("adamw_acc_step (+ outer pseudo-gradient)",
+              lambda: x.adamw_acc_step(w32, gr, m1, m2, w16, ctas, P, P, coef, sched, 0.9, 0.95, 1e-8, 0.1, None, 0,
+                                       1, 1, rt, len(sizes), et))]
+    out = []
+    _, bw, lab = _peaks()
+    for name, fn in cases:
+        ms = _timeit(fn, reps, flush)
+        check_errors()
+        out.append({"kernel": name, "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1),
+                    f"frac_of_{lab}_hbm": round(nbytes / ms / 1e6 / bw, 3), "shape": [G, P]})
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--paths", type=int, default=16)
@@ -194,7 +254,9 @@ def main() -> None:
                                                   args.reps, flush),
              "gemm": lambda: bench_gemm(args.paths, args.batch * args.seq, args.hidden, args.vocab, args.ffn,
                                         args.reps, flush),
-             "ce": lambda: bench_ce(args.paths, args.batch * args.seq, args.vocab, args.reps, flush)}
+             "ce": lambda: bench_ce(args.paths, args.batch * args.seq, args.vocab, args.reps, flush),
+             "optim": lambda: bench_optim(args.paths, args.hidden, args.vocab, args.ffn, [2, 2], [4, 4], args.reps,
+                                          flush)}
     for name, fn in cases.items():
         if args.only and args.only != name:
             continue

@@ -73,3 +73,32 @@ def test_wire_roundtrip_and_reference_compat(reference_pkg):
     with pytest.raises(TypeError):
         W.encode({1: 2})
     assert math.isfinite(back["f"])
+
+
+def test_payloads_and_digests_match_reference(reference_pkg):
+    """Uploads encoded here decode to the same values in the reference and vice versa,
+    the payload bytes on the wire are identical, and audit digests agree."""
+    from opendipaco.schedule import compress as RC
+    from opendipaco.schedule import wire as RW
+
+    torch.manual_seed(7)
+    delta = [torch.randn(12, 40), torch.randn(333), torch.zeros(5)]
+    for mode, density in (("int8", 1.0), ("int4", 1.0), ("bf16", 1.0), ("int8", 0.1), ("int4", 0.05),
+                          ("none", 0.2)):
+        ours, ours_r = C.compress_delta(delta, mode, density=density)
+        theirs, theirs_r = RC.compress_delta(delta, mode, density=density)
+        assert RW.encode({"p": ours}) == RW.encode({"p": theirs}), (mode, density)
+        for a, b in zip(C.maybe_dequantize(theirs), RC.maybe_dequantize(ours)):
+            assert torch.equal(a, b)
+        for a, b in zip(ours_r, theirs_r):
+            assert torch.equal(a, b)
+    g = {"L0E0": delta, "embed": [torch.randn(7, 3)]}
+    assert C.pseudograd_digest(g) == RC.pseudograd_digest(g)
+    sd = {"w": torch.randn(4, 4), "n": torch.arange(3)}
+    assert C.state_digest(sd) == RC.state_digest(sd)
+    base = {"w": torch.randn(6, 6)}
+    cur = {"w": base["w"] + 0.1}
+    for mode in ("int8", "int4"):
+        enc = C.encode_state_delta(cur, base, mode)
+        assert RW.encode(enc) == RW.encode(RC.encode_state_delta(cur, base, mode))
+        assert torch.equal(RC.apply_state_delta(base, enc)["w"], C.apply_state_delta(base, enc)["w"])

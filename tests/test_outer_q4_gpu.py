@@ -107,7 +107,7 @@ def test_compressed_apply_one_sharer_matches_reference(first, nesterov):
     lr, m = 0.7, 0.9
     g0, m0 = glob.clone(), mom.clone()
     ext().outer_nvlink_apply(keys, 1, nch, ptr(delta), ptr(glob), ptr(pad), mom, 0, 1, 1, lr, m, nesterov, first,
-                             sq, err_word(torch.device(DEV)), ptr(qd), ptr(qs), 0)
+                             sq, err_word(torch.device(DEV)), ptr(qd), ptr(qs), 0, None)
     torch.cuda.synchronize()
     check_errors()
     d = deq[off:off + n] * 0.25 * 0.5
@@ -203,7 +203,7 @@ def test_topk_apply_one_sharer_matches_reference():
     sq = torch.zeros(2, device=DEV)
     g0 = glob.clone()
     ext().outer_nvlink_apply(keys, 1, 2, ptr(delta), ptr(glob), ptr(pad), mom, 0, 1, 1, 0.7, 0.9, True, True, sq,
-                             err_word(torch.device(DEV)), ptr(spi), ptr(spv), kcap)
+                             err_word(torch.device(DEV)), ptr(spi), ptr(spv), kcap, None)
     torch.cuda.synchronize()
     check_errors()
     d = sparse[off:off + n]

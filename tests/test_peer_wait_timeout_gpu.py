@@ -57,7 +57,7 @@ def test_outer_apply_peer_wait_times_out_and_context_survives(short_wait):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     ext().outer_nvlink_apply(keys, 1, 1, _ptrs(delta, delta), _ptrs(glob, glob), _ptrs(pad0, pad1), mom, 0, 2, 1,
-                             0.5, 0.9, True, True, sq, err, None, None, 0)
+                             0.5, 0.9, True, True, sq, err, None, None, 0, None)
     ev1.record()
     torch.cuda.synchronize()
     waited_ms = ev0.elapsed_time(ev1)
@@ -70,7 +70,7 @@ def test_outer_apply_peer_wait_times_out_and_context_survives(short_wait):
     assert torch.equal(glob, torch.zeros(n, device=DEV)) and torch.equal(mom, torch.zeros(n, device=DEV))
     # the context is intact: a one-rank APPLY on the same buffers runs to completion
     ext().outer_nvlink_apply(keys, 1, 1, _ptrs(delta), _ptrs(glob), _ptrs(pad0), mom, 0, 1, 2,
-                             0.5, 0.9, True, True, sq, err, None, None, 0)
+                             0.5, 0.9, True, True, sq, err, None, None, 0, None)
     torch.cuda.synchronize()
     check_errors()
     # first outer step, Nesterov: b = d, update = d + m * d, glob = -lr * 1.9 * d
