@@ -71,7 +71,7 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
 void adamw_acc_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor p16, int64_t ctas,
                     int64_t sp, int64_t s16, c10::optional<torch::Tensor> coef, torch::Tensor sched, double b1,
                     double b2, double eps, double wd, c10::optional<torch::Tensor> rows, int64_t r0, int64_t H,
-                    int64_t V, torch::Tensor regions, int64_t nregs, torch::Tensor entries);
+                    int64_t V, torch::Tensor regions, int64_t nregs, torch::Tensor entries, bool accumulate);
 void adam8bit_step(torch::Tensor p, torch::Tensor g, torch::Tensor mq, torch::Tensor mabs, torch::Tensor vq,
                    torch::Tensor vlo, torch::Tensor vsc, c10::optional<torch::Tensor> coef, torch::Tensor sched,
                    double b1, double b2, double eps, double wd, bool first, c10::optional<torch::Tensor> p16,

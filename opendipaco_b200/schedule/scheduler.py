@@ -1,23 +1,29 @@
-"""In-process, fault-tolerant task-queue scheduler (reference ``schedule/scheduler.py``).
+"""In-process, fault-tolerant generations of path tasks.
 
-Worker threads lease path-tasks of a *generation* from a queue, train them and hand
-back a :class:`Contribution` (shared pseudo-gradients, private weights, the path's
-inner-optimizer state). A worker that raises :class:`TransientFault` nacks (the path
-is re-queued at once); one that raises :class:`Preempt` dies silently and the
-monitor re-queues its lease when it expires. A path that exhausts ``max_attempts``
-is dropped for the generation. Every task trains with its own generator seeded from
-``(seed, path, generation)`` (same mixing constants as the reference, so a run is
-reproducible across the two frameworks), and the reduce folds contributions in path
-order, so results do not depend on worker count or on the pattern of recovered
-failures. The outer step reuses the engine's weighting and optimizer.
+One *generation* trains every path once from the current global modules and then takes
+one outer step from their pseudo-gradients. ``AsyncScheduler`` runs a generation on a
+pool of worker threads that lease path tasks from a :class:`LeaseBoard`:
+
+* a task whose worker raises :class:`TransientFault` is returned at once (re-queued);
+* a worker that raises :class:`Preempt` vanishes with its lease; the lease expires after
+  ``lease_timeout`` and the path is re-queued;
+* a path that fails ``max_attempts`` times is dropped for the generation.
+
+Each task samples its batches with its own generator seeded by :func:`task_seed`
+(seed, path, generation) -- the reference's mixing constants, so a run reproduces
+across the two frameworks -- and the :class:`DeltaReducer` folds the finished tasks in
+path order, so the result depends on neither the worker count nor the pattern of
+recovered failures. The outer step reuses the engine's weighting and outer optimizer.
+Behaviour follows the reference's ``src/opendipaco/schedule/scheduler.py``.
 """
 
 from __future__ import annotations
 
-import collections
+import enum
 import math
 import threading
 import time
+from collections import deque
 from dataclasses import dataclass, field
 
 import torch
@@ -37,146 +43,208 @@ class Preempt(Exception):
     """Raised by a fault hook: the worker vanishes -> re-queue after lease expiry."""
 
 
+def task_seed(seed: int, path_idx: int, generation: int) -> int:
+    """Seed of a task's batch generator (the reference's hash, for cross-framework runs)."""
+    return ((seed * 0x9E3779B1) ^ (path_idx * 0x85EBCA77) ^ (generation * 0xC2B2AE35)) & 0x7FFFFFFFFFFFFFFF
+
+
 @dataclass
 class Contribution:
+    """What one finished path task hands back."""
+
     path: Path
     path_idx: int
     loss: float
-    shared_delta: dict[str, list[torch.Tensor]]
-    private_state: dict[str, dict]
-    opt_state: dict
-    empty: bool = False
+    shared_delta: dict[str, list[torch.Tensor]]  # module key -> pseudo-gradient per parameter
+    private_state: dict[str, dict]                # private module key -> its new state dict
+    opt_state: dict                               # the path's inner-optimizer state
+    empty: bool = False                           # the path had no data this generation
     probe_before: float | None = None
     probe_after: float | None = None
 
 
-@dataclass
-class _OuterAccumulator:
-    acc_sum: dict[str, list[torch.Tensor]]
-    acc_w: dict[str, float]
-    per_path_loss: dict
+# ---------------------------------------------------------------------- leases
+class _State(enum.Enum):
+    PENDING = 0
+    LEASED = 1
+    DONE = 2
+    FAILED = 3
 
 
 @dataclass
-class _Generation:
-    """Thread-safe lease / complete / nack / reclaim bookkeeping for one generation."""
+class _Task:
+    state: _State = _State.PENDING
+    attempts: int = 0
+    deadline: float = 0.0
+    result: Contribution | None = None
 
-    paths: list[Path]
-    lease_timeout: float
-    max_attempts: int
-    min_success: int
-    _cv: threading.Condition = field(default_factory=threading.Condition)
-    _pending: collections.deque = field(default_factory=collections.deque)
-    _leased: dict = field(default_factory=dict)
-    _attempts: collections.Counter = field(default_factory=collections.Counter)
-    results: dict = field(default_factory=dict)
-    failed: set = field(default_factory=set)
-    reclaimed: int = 0
 
-    def __post_init__(self):
-        self._pending.extend(self.paths)
+class LeaseBoard:
+    """Per-path task states of one generation behind one condition variable. Pending
+    paths are handed out first-in first-out; a returned or expired task goes to the back
+    of the queue unless it used up its attempts."""
 
-    def _expire(self) -> None:
+    def __init__(self, paths, lease_timeout: float, max_attempts: int):
+        self.lease_timeout, self.max_attempts = lease_timeout, max_attempts
+        self.tasks = {p: _Task() for p in paths}
+        self.queue: deque = deque(paths)
+        self.reclaimed = 0
+        self._cv = threading.Condition()
+
+    # -- transitions (caller holds the lock)
+    def _requeue(self, path: Path) -> None:
+        t = self.tasks[path]
+        if t.attempts >= self.max_attempts:
+            t.state = _State.FAILED
+        else:
+            t.state = _State.PENDING
+            self.queue.append(path)
+
+    def _sweep(self) -> None:
         now = time.monotonic()
-        for path, deadline in list(self._leased.items()):
-            if now < deadline:
-                continue
-            del self._leased[path]
-            if path in self.results:
-                continue
-            if self._attempts[path] >= self.max_attempts:
-                self.failed.add(path)
-            else:
-                self._pending.append(path)
-                self.reclaimed += 1
+        for path, t in self.tasks.items():
+            if t.state is _State.LEASED and now >= t.deadline:
+                if t.attempts < self.max_attempts:
+                    self.reclaimed += 1
+                self._requeue(path)
 
-    def _finished(self) -> bool:
-        return not self._pending and not self._leased and \
-            len(self.results) + len(self.failed) >= len(self.paths)
+    def _settled(self) -> bool:
+        return all(t.state in (_State.DONE, _State.FAILED) for t in self.tasks.values())
 
-    def _take(self, path: Path):
-        self._attempts[path] += 1
-        self._leased[path] = time.monotonic() + self.lease_timeout
-        return path, self._attempts[path]
+    def _hand_out(self, path: Path) -> tuple[Path, int]:
+        t = self.tasks[path]
+        t.state, t.attempts = _State.LEASED, t.attempts + 1
+        t.deadline = time.monotonic() + self.lease_timeout
+        return path, t.attempts
 
+    # -- API
     def lease(self, wait: float = 0.05):
+        """Block until a task is available: ``(path, attempt)``; None once every task is
+        settled (done or failed)."""
         with self._cv:
             while True:
-                self._expire()
-                if self._finished():
+                self._sweep()
+                if self._settled():
                     return None
-                if self._pending:
-                    return self._take(self._pending.popleft())
+                if self.queue:
+                    return self._hand_out(self.queue.popleft())
                 self._cv.wait(wait)
 
     def poll_lease(self, pick=None):
-        """Non-blocking: ``(path, attempt)``, ``"done"`` or ``"idle"``; ``pick(pending)``
-        may choose which pending path to hand out (data locality)."""
+        """Non-blocking lease: ``(path, attempt)``, ``"done"`` or ``"idle"``. ``pick`` may
+        choose among the pending paths (e.g. one whose data the worker holds)."""
         with self._cv:
-            self._expire()
-            if self._finished():
+            self._sweep()
+            if self._settled():
                 return "done"
-            if not self._pending:
+            if not self.queue:
                 return "idle"
-            if pick is None:
-                path = self._pending.popleft()
-            else:
-                path = pick(list(self._pending))
-                if path is None:
-                    return "idle"
-                self._pending.remove(path)
-            return self._take(path)
+            path = self.queue[0] if pick is None else pick(list(self.queue))
+            if path is None:
+                return "idle"
+            self.queue.remove(path)
+            return self._hand_out(path)
 
     def refresh_lease(self, path: Path) -> None:
         with self._cv:
-            if path in self._leased:
-                self._leased[path] = time.monotonic() + self.lease_timeout
+            t = self.tasks[path]
+            if t.state is _State.LEASED:
+                t.deadline = time.monotonic() + self.lease_timeout
 
     def complete(self, path: Path, contrib: Contribution) -> None:
+        """Record a result (the first one wins, even from a lease that had expired)."""
         with self._cv:
-            if path in self.results:
+            t = self.tasks[path]
+            if t.state is _State.DONE:
                 return
-            self._leased.pop(path, None)
-            self.failed.discard(path)
-            try:
-                self._pending.remove(path)
-            except ValueError:
-                pass
-            self.results[path] = contrib
+            if t.state is _State.PENDING and path in self.queue:
+                self.queue.remove(path)
+            t.state, t.result = _State.DONE, contrib
             self._cv.notify_all()
 
     def nack(self, path: Path) -> None:
         with self._cv:
-            self._leased.pop(path, None)
-            if path in self.results:
-                return
-            if self._attempts[path] >= self.max_attempts:
-                self.failed.add(path)
-            else:
-                self._pending.append(path)
+            t = self.tasks[path]
+            if t.state is _State.LEASED:
+                self._requeue(path)
             self._cv.notify_all()
 
     def reclaim(self) -> None:
         with self._cv:
-            self._expire()
+            self._sweep()
             self._cv.notify_all()
 
     def is_done(self) -> bool:
         with self._cv:
-            return self._finished()
+            return self._settled()
 
     def pending_paths(self) -> list:
         with self._cv:
-            self._expire()
-            return list(self._pending)
+            self._sweep()
+            return list(self.queue)
+
+    @property
+    def results(self) -> dict:
+        with self._cv:
+            return {p: t.result for p, t in self.tasks.items() if t.state is _State.DONE}
+
+    @property
+    def failed(self) -> set:
+        with self._cv:
+            return {p for p, t in self.tasks.items() if t.state is _State.FAILED}
 
 
-def task_seed(seed: int, path_idx: int, generation: int) -> int:
-    return ((seed * 0x9E3779B1) ^ (path_idx * 0x85EBCA77) ^ (generation * 0xC2B2AE35)) & 0x7FFFFFFFFFFFFFFF
+# ---------------------------------------------------------------------- reduce
+class DeltaReducer:
+    """Weighted sum of the pseudo-gradients of one generation per shared key, then one
+    outer step (normalised by the weight sum, optionally times sqrt(sharing))."""
+
+    def __init__(self, engine: DiPaCoEngine, corpus):
+        self.e, self.corpus = engine, corpus
+        keys = [k for k in engine.topology.module_keys() if not is_private_key(k) and k in engine.bank]
+        self.sums = {k: [torch.zeros_like(p) for p in engine.bank[k].parameters()] for k in keys}
+        self.weights = dict.fromkeys(keys, 0.0)
+        self.losses: dict = {}
+
+    def add(self, c: Contribution, *, persist_opt: bool = True) -> None:
+        if c.empty:
+            return
+        e = self.e
+        self.losses[c.path] = c.loss
+        for key, sd in c.private_state.items():
+            e.bank[key].load_state_dict({n: v.to(e.device) for n, v in sd.items()})
+        for key, delta in c.shared_delta.items():
+            w = e._outer_weight(key, c.path_idx, self.corpus)
+            for acc, d in zip(self.sums[key], delta):
+                acc.add_(w * d.to(e.device))
+            self.weights[key] += w
+        if persist_opt and c.opt_state:
+            e._opt_state[c.path] = c.opt_state
+
+    def step(self, generation: int, batch_size: int) -> RoundMetrics:
+        e = self.e
+        norms = []
+        for key, w in self.weights.items():
+            if w == 0.0:
+                continue
+            scale = 1.0 / max(w, 1e-12) if e.diloco.normalize_outer_delta else 1.0
+            if e.diloco.rescale_by_sqrt_sharing:
+                scale *= math.sqrt(e.topology.sharing_count(key))
+            grads = [s * scale for s in self.sums[key]]
+            apply_outer_grads(e.bank[key], grads)
+            norms.append(math.sqrt(sum(float(g.pow(2).sum()) for g in grads)))
+        e.outer_opt.step()
+        e.outer_opt.zero_grad(set_to_none=True)
+        val = e._track_best(self.corpus, batch_size=batch_size) if self.corpus.has_validation else None
+        mean = sum(self.losses.values()) / len(self.losses) if self.losses else float("nan")
+        return RoundMetrics(round=generation, inner_loss=mean, per_path_loss=dict(self.losses),
+                            delta_norm=sum(norms) / len(norms) if norms else 0.0, val_loss=val)
 
 
+# ---------------------------------------------------------------------- scheduler
 class AsyncScheduler:
-    """Drives a :class:`DiPaCoEngine` (use ``materialize="serial"``) through the queue."""
+    """Drives a :class:`DiPaCoEngine` (use ``materialize="serial"``) through generations
+    of leased path tasks; ``_train_path`` is also the task body of the TCP workers."""
 
     def __init__(self, engine: DiPaCoEngine, *, num_workers: int = 4, lease_timeout: float = 30.0,
                  max_attempts: int = 3, min_fraction: float = 1.0):
@@ -190,29 +258,29 @@ class AsyncScheduler:
         self.errors: dict[Path, str] = {}
         self._last_batch_size = 1
 
-    # -- map ---------------------------------------------------------------
+    # -- one task
     def _train_path(self, path: Path, shard: torch.Tensor, batch_size: int, generation: int,
                     inner_steps: int | None = None, probe=None) -> Contribution:
         e = self.engine
         pidx = e.topology.path_index(path)
-        shard = shard.to(e.device)
         if shard.size(0) == 0:
             return Contribution(path, pidx, float("nan"), {}, {}, {}, empty=True)
-        pm = build_path_model(e.config, path, e.bank, deepcopy=True,
-                              dedup_private=getattr(e.diloco, "dedup_private", False)).to(e.device)
-        opt = make_inner_optimizer(pm, e.diloco)
+        shard = shard.to(e.device)
+        model = build_path_model(e.config, path, e.bank, deepcopy=True,
+                                 dedup_private=getattr(e.diloco, "dedup_private", False)).to(e.device)
+        opt = make_inner_optimizer(model, e.diloco)
         if e._opt_state.get(path) is not None:
             opt.load_state_dict(e._opt_state[path])
-        gen = torch.Generator().manual_seed(task_seed(self.seed, pidx, generation))
         steps = inner_steps or e.diloco.inner_steps
-        total = e.total_rounds * steps if e.total_rounds else None
         screening = probe is not None and not probe.empty
-        before = safe_probe_loss(probe, pm) if screening else None
-        loss = run_inner_steps(pm, opt, shard, batch_size, gen, inner_steps=steps, total_steps=total,
+        before = safe_probe_loss(probe, model) if screening else None
+        loss = run_inner_steps(model, opt, shard, batch_size, torch.Generator().manual_seed(task_seed(self.seed, pidx,
+                                                                                                      generation)),
+                               inner_steps=steps, total_steps=e.total_rounds * steps if e.total_rounds else None,
                                base_step=generation * steps, diloco=e.diloco, device=e.device)
-        after = safe_probe_loss(probe, pm) if screening else None
+        after = safe_probe_loss(probe, model) if screening else None
         shared, private = {}, {}
-        for key, mod in pm.modules_by_key().items():
+        for key, mod in model.modules_by_key().items():
             if is_private_key(key):
                 private[key] = _state_cpu(mod.state_dict())
             else:
@@ -220,96 +288,35 @@ class AsyncScheduler:
         return Contribution(path, pidx, loss, shared, private, _opt_state_cpu(opt.state_dict()),
                             probe_before=before, probe_after=after)
 
-    def _worker(self, gen: _Generation, corpus, batch_size, generation, fault_hook):
-        while True:
-            leased = gen.lease()
-            if leased is None:
-                return
+    def _work(self, board: LeaseBoard, corpus, batch_size: int, generation: int, fault_hook) -> None:
+        while (leased := board.lease()) is not None:
             path, attempt = leased
             try:
                 if fault_hook is not None:
                     fault_hook(path, attempt)
                 shard = corpus.shard(self.engine.topology.path_index(path))
-                gen.complete(path, self._train_path(path, shard, batch_size, generation))
+                board.complete(path, self._train_path(path, shard, batch_size, generation))
             except Preempt:
-                continue
-            except Exception as exc:  # recorded for debugging, then re-queued
+                continue  # the lease lapses; another worker picks the path up later
+            except Exception as exc:
                 self.errors[path] = repr(exc)
-                gen.nack(path)
+                board.nack(path)
 
-    def _monitor(self, gen: _Generation):
-        while not gen.is_done():
-            time.sleep(max(self.lease_timeout / 2, 0.005))
-            gen.reclaim()
-
-    # -- reduce --------------------------------------------------------------
-    def _new_accumulator(self) -> _OuterAccumulator:
-        e = self.engine
-        keys = [k for k in e.topology.module_keys() if not is_private_key(k) and k in e.bank]
-        return _OuterAccumulator({k: [torch.zeros_like(p) for p in e.bank[k].parameters()] for k in keys},
-                                 dict.fromkeys(keys, 0.0), {})
-
-    def _fold_contribution(self, acc: _OuterAccumulator, corpus, c: Contribution, *,
-                           persist_opt: bool = True) -> None:
-        if c.empty:
-            return
-        e = self.engine
-        acc.per_path_loss[c.path] = c.loss
-        for key, sd in c.private_state.items():
-            e.bank[key].load_state_dict({k: v.to(e.device) for k, v in sd.items()})
-        for key, delta in c.shared_delta.items():
-            w = e._outer_weight(key, c.path_idx, corpus)
-            for a, d in zip(acc.acc_sum[key], delta):
-                a.add_(w * d.to(e.device))
-            acc.acc_w[key] += w
-        if persist_opt and c.opt_state:
-            e._opt_state[c.path] = c.opt_state
-
-    def _finalize_outer_step(self, acc: _OuterAccumulator, corpus, generation) -> RoundMetrics:
-        e = self.engine
-        norms = []
-        for key, w in acc.acc_w.items():
-            if w == 0.0:
-                continue
-            avg = ([s / max(w, 1e-12) for s in acc.acc_sum[key]] if e.diloco.normalize_outer_delta
-                   else acc.acc_sum[key])
-            if e.diloco.rescale_by_sqrt_sharing:
-                sc = math.sqrt(e.topology.sharing_count(key))
-                avg = [a * sc for a in avg]
-            apply_outer_grads(e.bank[key], avg)
-            norms.append(math.sqrt(sum(float(a.pow(2).sum()) for a in avg)) if avg else 0.0)
-        e.outer_opt.step()
-        e.outer_opt.zero_grad(set_to_none=True)
-        val = e._track_best(corpus, batch_size=self._last_batch_size) if corpus.has_validation else None
-        losses = acc.per_path_loss
-        return RoundMetrics(round=generation,
-                            inner_loss=sum(losses.values()) / len(losses) if losses else float("nan"),
-                            per_path_loss=dict(losses),
-                            delta_norm=sum(norms) / len(norms) if norms else 0.0, val_loss=val)
-
-    def _apply_generation(self, corpus, contributions, generation) -> RoundMetrics:
-        acc = self._new_accumulator()
-        for c in sorted(contributions, key=lambda c: c.path_idx):
-            self._fold_contribution(acc, corpus, c)
-        return self._finalize_outer_step(acc, corpus, generation)
-
-    # -- drive ---------------------------------------------------------------
+    # -- generations
     def run_generation(self, corpus, batch_size, generation, *, fault_hook=None) -> RoundMetrics:
         self._last_batch_size = batch_size
-        paths = list(self.engine.topology.paths())
-        gen = _Generation(paths, self.lease_timeout, self.max_attempts,
-                          max(1, math.ceil(self.min_fraction * len(paths))))
-        threads = [threading.Thread(target=self._worker, args=(gen, corpus, batch_size, generation, fault_hook),
-                                    daemon=True) for _ in range(self.num_workers)]
-        mon = threading.Thread(target=self._monitor, args=(gen,), daemon=True)
-        for t in threads:
-            t.start()
-        mon.start()
-        for t in threads:
-            t.join()
-        mon.join()
-        self.dropped = set(gen.failed)
-        return self._apply_generation(corpus, list(gen.results.values()), generation)
+        board = LeaseBoard(list(self.engine.topology.paths()), self.lease_timeout, self.max_attempts)
+        workers = [threading.Thread(target=self._work, args=(board, corpus, batch_size, generation, fault_hook),
+                                    name=f"odp-task-{i}", daemon=True) for i in range(self.num_workers)]
+        for w in workers:
+            w.start()
+        for w in workers:
+            w.join()
+        self.dropped = board.failed
+        reducer = DeltaReducer(self.engine, corpus)
+        for c in sorted(board.results.values(), key=lambda c: c.path_idx):
+            reducer.add(c)
+        return reducer.step(generation, batch_size)
 
     def fit(self, corpus, num_generations: int, batch_size: int, *, total_generations: int | None = None,
             log_every: int = 1, fault_hook=None):
@@ -318,12 +325,12 @@ class AsyncScheduler:
             e.total_rounds = total_generations
         elif e.total_rounds is None:
             e.total_rounds = e._global_round + num_generations
-        hist = []
+        history = []
         for i in range(num_generations):
             m = self.run_generation(corpus, batch_size, e._global_round, fault_hook=fault_hook)
             e._global_round += 1
-            hist.append(m)
+            history.append(m)
             if log_every and (m.round % log_every == 0 or i == num_generations - 1):
-                drop = f" dropped={len(self.dropped)}" if self.dropped else ""
-                print(f"[gen {m.round:4d}] inner_loss={m.inner_loss:.4f} delta_norm={m.delta_norm:.4f}{drop}")
-        return hist
+                dropped = f" dropped={len(self.dropped)}" if self.dropped else ""
+                print(f"[gen {m.round:4d}] inner_loss={m.inner_loss:.4f} delta_norm={m.delta_norm:.4f}{dropped}")
+        return history

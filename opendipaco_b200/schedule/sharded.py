@@ -1353,7 +1353,7 @@ def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, 
     ``throttle.TokenBucket`` capping this worker's bandwidth; ``data_dir`` caches
     shards materialised from shipped specs (``verify_routing`` re-fits the shipped
     router from the public source first and refuses to train on a mismatch)."""
-    from .distributed import _ShardCache, _heartbeat_loop, _materialize_from_spec
+    from .distributed import ShardCache, heartbeats, materialize_shard_spec
 
     engine = _build_engine(config, diloco, device, seed)
     worker = AsyncScheduler(engine, num_workers=1)
@@ -1367,7 +1367,7 @@ def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, 
     except ConnectionError:
         return
     data_ctx = {"dir": data_dir, "source": data_source, "tokenizer": data_tokenizer, "verify": verify_routing}
-    warm, cache = set(), _ShardCache(max_shards)
+    warm, cache = set(), ShardCache(max_shards)
     versions, keyframes, residuals = {}, {}, {}
     caps = {"device": str(device), **({"max_batch": int(max_batch_size)} if max_batch_size else {})}
     done = 0
@@ -1386,35 +1386,30 @@ def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, 
             path, lease, routing = tuple(msg["path"]), msg["lease"], msg["routing"]
             worker.seed, engine.total_rounds = msg["seed"], msg["total_rounds"]
             keys = topo.path_module_keys(path)
-            stop_beat = threading.Event()
-            beat = threading.Thread(target=_heartbeat_loop, args=(link.sch_send, stop_beat, heartbeat_interval,
-                                                                   wid, lease, path), daemon=True)
-            beat.start()
             try:
-                if fault_hook is not None:
-                    fault_hook(path, 1)
-                pin = msg.get("base") if msg.get("check_only") else None
-                cold = {k for k in keys if is_private_key(k) and path not in warm}
-                fetched = _fetch_keys(link, routing, keys, versions, cold, keyframes, pin=pin)
-                for k, sd in fetched.items():
-                    engine.bank[k].load_state_dict({n: v.to(engine.device) for n, v in sd.items()})
-                base = {k: list(versions[k]) for k in keys if k in versions and not is_private_key(k)}
-                if msg.get("shard") is not None:
-                    cache[path] = restore_shard(msg["shard"])
-                elif msg.get("shard_spec") is not None and path not in cache:
-                    cache[path] = _materialize_from_spec(msg["shard_spec"], data_ctx)
-                if path not in warm:
-                    engine._opt_state.pop(path, None)
-                probe = TrustedProbe(msg["probe"], batch_size=msg.get("probe_batch", 8)) if msg.get("probe") is not None else None
-                contrib = worker._train_path(path, cache[path], msg["batch_size"], msg["gen_id"],
-                                             inner_steps=msg.get("inner_steps"), probe=probe)
+                with heartbeats(link.sch_send, heartbeat_interval,
+                                {"type": "heartbeat", "lease": lease, "path": path, "worker_id": wid}):
+                    if fault_hook is not None:
+                        fault_hook(path, 1)
+                    pin = msg.get("base") if msg.get("check_only") else None
+                    cold = {k for k in keys if is_private_key(k) and path not in warm}
+                    fetched = _fetch_keys(link, routing, keys, versions, cold, keyframes, pin=pin)
+                    for k, sd in fetched.items():
+                        engine.bank[k].load_state_dict({n: v.to(engine.device) for n, v in sd.items()})
+                    base = {k: list(versions[k]) for k in keys if k in versions and not is_private_key(k)}
+                    if msg.get("shard") is not None:
+                        cache[path] = restore_shard(msg["shard"])
+                    elif msg.get("shard_spec") is not None and path not in cache:
+                        cache[path] = materialize_shard_spec(msg["shard_spec"], data_ctx)
+                    if path not in warm:
+                        engine._opt_state.pop(path, None)
+                    probe = (TrustedProbe(msg["probe"], batch_size=msg.get("probe_batch", 8))
+                             if msg.get("probe") is not None else None)
+                    contrib = worker._train_path(path, cache[path], msg["batch_size"], msg["gen_id"],
+                                                 inner_steps=msg.get("inner_steps"), probe=probe)
             except Exception as exc:
-                stop_beat.set()
-                beat.join(timeout=1)
                 link.sch_rpc({"type": "nack", "lease": lease, "path": path, "error": repr(exc)})
                 continue
-            stop_beat.set()
-            beat.join(timeout=1)
             digest = pseudograd_digest(contrib.shared_delta) if (msg.get("audit") or msg.get("check_only")) else None
             commit = {"type": "commit", "lease": lease, "path": path, "gen_id": msg["gen_id"], "loss": contrib.loss,
                       "empty": contrib.empty, "worker_id": wid, "digest": digest, "base": base,

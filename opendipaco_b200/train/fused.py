@@ -208,7 +208,7 @@ class FusedExecutor:
             self.dp_counter = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.pms = dict(zip(self.paths, pms))
         if engine.materialize == "eager":
-            engine.path_models.update(self.pms)
+            engine._eager_views.update(self.pms)
         self.steps_taken = [0] * G
         self._inner_opts: dict[Path, torch.optim.Optimizer] = {}
 
@@ -551,10 +551,12 @@ class FusedExecutor:
             X_.adam8bit_step(self.W32.view(-1), self.GRAD.view(-1), self.MQ, self.MABS, self.VQ, self.VLO,
                              self.VSC, self.COEF, self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay,
                              False, self.W16.view(-1), P // ALIGN)
-        elif last and self.acc_fused:
+        elif self.acc_fused:
+            # region-per-CTA AdamW (faster than one path per thread); the round's last
+            # step also accumulates the outer pseudo-gradients
             X_.adamw_acc_step(self.W32, self.GRAD, self.MOM1, self.MOM2, self.W16, self.acc_ctas, P, P, self.COEF,
                               self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, rows, lay.emb, H, V, self.ACC_REG,
-                              self.acc_nregs, self.ACC_ENT)
+                              self.acc_nregs, self.ACC_ENT, last)
         else:
             X_.adamw_step(self.W32, self.GRAD, self.MOM1, self.MOM2, self.W16, P, P, P, G, self.COEF,
                           self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, rows, lay.emb, H, V)

@@ -1,7 +1,7 @@
 """The DiPaCo training engine.
 
-Reference: ``src/opendipaco/train/loop.py:44-527``. One round = one DiLoCo outer
-step:
+Public API of the reference engine (``src/opendipaco/train/loop.py:44-527``). One round
+= one DiLoCo outer step:
 
 1. every owned path takes ``inner_steps`` AdamW steps on its shard;
 2. each shared module's pseudo-gradient ``global - local`` is weighted (alpha =
@@ -10,10 +10,12 @@ step:
 3. optional normalisation and x sqrt(sharing count); outer SGD-Nesterov step;
 4. new globals are copied back into every working copy.
 
-Two executors implement a round:
+Two executors implement a round behind one interface (``run_round``, ``path_model``,
+``inner_state_dicts``, ``outer_state_dict``, ``load_states``, ``sync_bank_views``):
 
-* the *module* executor (CPU, or ``ExecOptions(fused=False)``) runs PyTorch
-  modules + ``torch.optim`` exactly like the reference; it is the oracle;
+* :class:`ModuleExecutor` (CPU, or ``ExecOptions(fused=False)``) runs PyTorch
+  modules + ``torch.optim`` with the reference's arithmetic, bit for bit on CPU; it is
+  the numerical oracle;
 * the *fused* executor (default on CUDA, ``opendipaco_b200/train/fused.py``) keeps
   every owned path's weights, grads and optimizer state in flat device buffers,
   runs all owned paths of a step in lock-step through the sm_100a kernels, captures
@@ -153,8 +155,140 @@ def run_inner_steps(pm, opt, shard, batch_size, gen, *, inner_steps, total_steps
     return last
 
 
+class _WeightedDeltas:
+    """Per shared key: sum over the paths of ``w * (global - local)`` and the weight sum,
+    accumulated in path order."""
+
+    def __init__(self, bank: dict, keys: list[str]):
+        self.keys = keys
+        self.sums = {k: [torch.zeros_like(p) for p in bank[k].parameters()] for k in keys}
+        self.weights = dict.fromkeys(keys, 0.0)
+
+    def add(self, key: str, w: float, deltas) -> None:
+        for acc, d in zip(self.sums[key], deltas):
+            acc.add_(w * d)
+        self.weights[key] += w
+
+
+class ModuleExecutor:
+    """Rounds on PyTorch modules: the reference's training arithmetic (the oracle).
+
+    ``materialize="eager"`` keeps one working model and inner optimizer per owned path;
+    ``"serial"`` builds each path's model from the bank when it trains and keeps only its
+    optimizer state between rounds (``engine._opt_state``), so memory holds one path.
+    """
+
+    def __init__(self, engine: "DiPaCoEngine"):
+        self.e = engine
+        self.models: dict[Path, nn.Module] = {}
+        self.opts: dict[Path, torch.optim.Optimizer] = {}
+        if engine.materialize == "eager":
+            for path in engine.backend.owned_paths():
+                self.models[path], self.opts[path] = self._fresh(path)
+
+    def _fresh(self, path: Path):
+        e = self.e
+        model = build_path_model(e.config, path, e.bank, deepcopy=True).to(e.device)
+        return model, make_inner_optimizer(model, e.diloco)
+
+    def _checkout(self, path: Path):
+        if path in self.models:
+            return self.models[path], self.opts[path]
+        model, opt = self._fresh(path)
+        if path in self.e._opt_state:
+            opt.load_state_dict(self.e._opt_state[path])
+        return model, opt
+
+    def _checkin(self, path: Path, opt) -> None:
+        if path not in self.opts:  # serial: only the optimizer state outlives the round
+            self.e._opt_state[path] = _opt_state_cpu(opt.state_dict())
+
+    def path_model(self, path: Path) -> nn.Module:
+        return self.models[path] if path in self.models else self._fresh(path)[0]
+
+    def _train(self, path: Path, corpus, batch_size: int, round_idx: int, sums: _WeightedDeltas):
+        """Inner steps of one path, then its contribution; returns its last loss (None
+        for an empty shard)."""
+        e = self.e
+        pidx = e.topology.path_index(path)
+        shard = corpus.shard(pidx).to(e.device)
+        if shard.size(0) == 0:
+            return None
+        model, opt = self._checkout(path)
+        steps = e.diloco.inner_steps
+        loss = run_inner_steps(model, opt, shard, batch_size, e._gen, inner_steps=steps,
+                               total_steps=e.total_rounds * steps if e.total_rounds else None,
+                               base_step=round_idx * steps, diloco=e.diloco, device=e.device)
+        for key, local in model.modules_by_key().items():
+            if not e.backend.owns_module(key):
+                continue
+            if is_private_key(key):
+                _copy_into(e.bank[key], local)
+            else:
+                sums.add(key, e._outer_weight(key, pidx, corpus), module_delta(e.bank[key], local))
+        self._checkin(path, opt)
+        return loss
+
+    def _outer_step(self, sums: _WeightedDeltas) -> list[float]:
+        e = self.e
+        norms = []
+        for key in sums.keys:
+            red = e.backend.global_reduce(key, ReducedDelta(sums.sums[key], sums.weights[key]))
+            grads = ([t / max(red.weight, 1e-12) for t in red.summed] if e.diloco.normalize_outer_delta
+                     else list(red.summed))
+            if e.diloco.rescale_by_sqrt_sharing:
+                scale = math.sqrt(e.topology.sharing_count(key))
+                grads = [g * scale for g in grads]
+            apply_outer_grads(e.bank[key], grads)
+            norms.append(math.sqrt(sum(float(g.pow(2).sum()) for g in grads)) if grads else 0.0)
+        e.outer_opt.step()
+        e.outer_opt.zero_grad(set_to_none=True)
+        return norms
+
+    def run_round(self, corpus, batch_size: int, round_idx: int, next_round=None):
+        e = self.e
+        shared = [k for k in e.topology.module_keys() if e.backend.owns_module(k) and not is_private_key(k)]
+        sums = _WeightedDeltas(e.bank, shared)
+        losses: dict[Path, float] = {}
+        for path in e.backend.owned_paths():
+            loss = self._train(path, corpus, batch_size, round_idx, sums)
+            if loss is not None:
+                losses[path] = loss
+        norms = self._outer_step(sums)
+        for model in self.models.values():  # eager working copies restart from the new globals
+            for key, local in model.modules_by_key().items():
+                if e.backend.owns_module(key) and not is_private_key(key):
+                    _copy_into(local, e.bank[key])
+        return losses, norms
+
+    # -- checkpoint glue
+    def sync_bank_views(self) -> None:
+        pass
+
+    def inner_state_dicts(self) -> dict:
+        if self.opts:
+            return {p: _opt_state_cpu(o.state_dict()) for p, o in self.opts.items()}
+        return dict(self.e._opt_state)
+
+    def outer_state_dict(self) -> dict:
+        return _opt_state_cpu(self.e.outer_opt.state_dict())
+
+    def load_states(self, outer_sd: dict, inner: dict) -> None:
+        e = self.e
+        e.outer_opt.load_state_dict(outer_sd)
+        if e.materialize == "serial":
+            e._opt_state = dict(inner)
+            return
+        for path in e.backend.owned_paths():
+            model, opt = self._fresh(path)
+            if path in inner:
+                opt.load_state_dict(inner[path])
+            self.models[path], self.opts[path] = model, opt
+
+
 class DiPaCoEngine:
-    """Backend-agnostic DiPaCo trainer (public API of the reference engine)."""
+    """Backend-agnostic DiPaCo trainer (the reference engine's public API); the rounds
+    run on a :class:`ModuleExecutor` or, on CUDA by default, a ``FusedExecutor``."""
 
     def __init__(self, config: DiPaCoConfig, diloco: DiLoCoConfig, backend: SyncBackend,
                  device: str | torch.device = "cpu", seed: int = 0,
@@ -170,167 +304,70 @@ class DiPaCoEngine:
         self._seed = seed
         self.total_rounds: int | None = None
         self._global_round = 0
+        self._opt_state: dict[Path, dict] = {}  # serial materialization: inner states between rounds
+        self.best_val_loss: dict[Path, float] = {}
+        self.best_path_state: dict[Path, dict] = {}
 
+        # module initialisation consumes the global RNG exactly as the reference does
         torch.manual_seed(seed)
-        full = build_module_bank(config)
-        self.bank: dict[str, nn.Module] = {
-            k: m.to(self.device) for k, m in full.items() if backend.owns_module(k)}
+        self.bank: dict[str, nn.Module] = {k: m.to(self.device) for k, m in build_module_bank(config).items()
+                                           if backend.owns_module(k)}
         if init_from is not None:
             warm_start_modules(self.bank, self.topology, init_from)
-        shared = {k: m for k, m in self.bank.items() if not is_private_key(k)}
-        self.outer_opt = make_outer_optimizer(shared, diloco)
+        self.outer_opt = make_outer_optimizer({k: m for k, m in self.bank.items() if not is_private_key(k)}, diloco)
 
-        self.path_models: dict[Path, nn.Module] = {}
-        self.inner_opts: dict[Path, torch.optim.Optimizer] = {}
-        self._opt_state: dict[Path, dict] = {}
-        self._fused = None
         use_fused = self.exec.fused if self.exec.fused is not None else self.device.type == "cuda"
+        self._modules = None
+        self._fused = None
         if use_fused:
             from .fused import FusedExecutor
 
             self._fused = FusedExecutor(self)
-        elif materialize == "eager":
-            for path in backend.owned_paths():
-                pm = build_path_model(config, path, self.bank, deepcopy=True).to(self.device)
-                self.path_models[path] = pm
-                self.inner_opts[path] = make_inner_optimizer(pm, diloco)
-
+        else:
+            self._modules = ModuleExecutor(self)
         self._gen = torch.Generator().manual_seed(seed + 1)
-        self.best_val_loss: dict[Path, float] = {}
-        self.best_path_state: dict[Path, dict] = {}
+
+    @property
+    def _executor(self):
+        return self._fused if self._fused is not None else self._modules
 
     @property
     def fused(self) -> bool:
         return self._fused is not None
 
-    # -- weights ------------------------------------------------------------
+    @property
+    def path_models(self) -> dict:
+        """Persistent per-path working models (eager materialization)."""
+        return self._modules.models if self._modules is not None else self._eager_views
+
+    @property
+    def _eager_views(self) -> dict:
+        if not hasattr(self, "_fused_views"):
+            self._fused_views = {}
+        return self._fused_views
+
+    @property
+    def inner_opts(self) -> dict:
+        return self._modules.opts if self._modules is not None else {}
+
+    # -- outer weights -------------------------------------------------------------
     def _outer_weight(self, key: str, path_idx: int, corpus) -> float:
+        """alpha of a path's pseudo-gradient for ``key``: its shard's token fraction, or
+        1 (normalised later by the weight sum), or 1 / (paths sharing the key)."""
         if self.diloco.shard_size_weighting:
             return corpus.shard_weight(path_idx)
-        if self.diloco.normalize_outer_delta:
-            return 1.0
-        return 1.0 / self.topology.sharing_count(key)
+        return 1.0 if self.diloco.normalize_outer_delta else 1.0 / self.topology.sharing_count(key)
 
     def outer_scale(self, key: str) -> float:
         return math.sqrt(self.topology.sharing_count(key)) if self.diloco.rescale_by_sqrt_sharing else 1.0
 
-    # -- module-executor materialisation ----------------------------------------
-    def _acquire(self, path: Path):
-        if self.materialize == "eager":
-            return self.path_models[path], self.inner_opts[path]
-        pm = build_path_model(self.config, path, self.bank, deepcopy=True).to(self.device)
-        opt = make_inner_optimizer(pm, self.diloco)
-        if path in self._opt_state:
-            opt.load_state_dict(self._opt_state[path])
-        return pm, opt
-
-    def _release(self, path: Path, opt) -> None:
-        if self.materialize == "serial":
-            self._opt_state[path] = _opt_state_cpu(opt.state_dict())
-
-    def _path_model_for(self, path: Path) -> nn.Module:
-        if self._fused is not None:
-            return self._fused.path_model(path)
-        if self.materialize == "eager":
-            return self.path_models[path]
-        return build_path_model(self.config, path, self.bank, deepcopy=True).to(self.device)
-
-    def _inner_train(self, pm, opt, shard, batch_size, round_idx) -> float:
-        steps = self.diloco.inner_steps
-        total = self.total_rounds * steps if self.total_rounds else None
-        return run_inner_steps(pm, opt, shard, batch_size, self._gen, inner_steps=steps,
-                               total_steps=total, base_step=round_idx * steps,
-                               diloco=self.diloco, device=self.device)
-
-    # -- one round ------------------------------------------------------------
+    # -- rounds ------------------------------------------------------------------------
     def run_round(self, corpus: ShardedCorpus, batch_size: int, round_idx: int = 0,
                   _next_round: int | None = None) -> RoundMetrics:
-        if self._fused is not None:
-            per_path_loss, delta_norms = self._fused.run_round(corpus, batch_size, round_idx, _next_round)
-        else:
-            per_path_loss, delta_norms = self._module_round(corpus, batch_size, round_idx)
+        losses, norms = self._executor.run_round(corpus, batch_size, round_idx, _next_round)
         val = self._track_best(corpus, batch_size) if corpus.has_validation else None
-        mean = sum(per_path_loss.values()) / len(per_path_loss) if per_path_loss else float("nan")
-        return RoundMetrics(round=round_idx, inner_loss=mean, per_path_loss=per_path_loss,
-                            delta_norm=sum(delta_norms) / len(delta_norms) if delta_norms else 0.0,
-                            val_loss=val)
-
-    def _module_round(self, corpus, batch_size, round_idx):
-        owned = [k for k in self.topology.module_keys() if self.backend.owns_module(k)]
-        shared = [k for k in owned if not is_private_key(k)]
-        acc = {k: [torch.zeros_like(p) for p in self.bank[k].parameters()] for k in shared}
-        acc_w = dict.fromkeys(shared, 0.0)
-        losses: dict[Path, float] = {}
-        for path in self.backend.owned_paths():
-            pidx = self.topology.path_index(path)
-            shard = corpus.shard(pidx).to(self.device)
-            if shard.size(0) == 0:
-                continue
-            pm, opt = self._acquire(path)
-            losses[path] = self._inner_train(pm, opt, shard, batch_size, round_idx)
-            for key, local in pm.modules_by_key().items():
-                if not self.backend.owns_module(key):
-                    continue
-                if is_private_key(key):
-                    _copy_into(self.bank[key], local)
-                    continue
-                w = self._outer_weight(key, pidx, corpus)
-                for a, d in zip(acc[key], module_delta(self.bank[key], local)):
-                    a.add_(w * d)
-                acc_w[key] += w
-            self._release(path, opt)
-            if self.materialize == "serial":
-                del pm, opt
-        norms = []
-        for key in shared:
-            red = self.backend.global_reduce(key, ReducedDelta(acc[key], acc_w[key]))
-            if self.diloco.normalize_outer_delta:
-                den = max(red.weight, 1e-12)
-                avg = [s / den for s in red.summed]
-            else:
-                avg = list(red.summed)
-            if self.diloco.rescale_by_sqrt_sharing:
-                sc = math.sqrt(self.topology.sharing_count(key))
-                avg = [a * sc for a in avg]
-            apply_outer_grads(self.bank[key], avg)
-            norms.append(math.sqrt(sum(float(a.pow(2).sum()) for a in avg)) if avg else 0.0)
-        self.outer_opt.step()
-        self.outer_opt.zero_grad(set_to_none=True)
-        if self.materialize == "eager":
-            for pm in self.path_models.values():
-                for key, local in pm.modules_by_key().items():
-                    if self.backend.owns_module(key) and not is_private_key(key):
-                        _copy_into(local, self.bank[key])
-        return losses, norms
-
-    # -- validation / early stopping -----------------------------------------------
-    @torch.no_grad()
-    def _eval_val(self, pm: nn.Module, seqs: torch.Tensor, batch_size: int) -> float:
-        pm.eval()
-        total, tokens = token_loss_sum(pm, seqs, batch_size=batch_size, device=self.device)
-        pm.train()
-        return total / max(tokens, 1)
-
-    def _track_best(self, corpus, batch_size: int) -> float | None:
-        losses = []
-        for path in self.backend.owned_paths():
-            val = corpus.val_shard(self.topology.path_index(path))
-            if val is None or val.size(0) == 0:
-                continue
-            pm = self._path_model_for(path)
-            loss = self._eval_val(pm, val, batch_size)
-            losses.append(loss)
-            if path not in self.best_val_loss or loss < self.best_val_loss[path]:
-                self.best_val_loss[path] = loss
-                self.best_path_state[path] = {k: v.detach().cpu().clone()
-                                              for k, v in pm.state_dict().items()}
-        return sum(losses) / len(losses) if losses else None
-
-    def compose_best(self, path: Path) -> nn.Module:
-        pm = build_path_model(self.config, path, self.bank, deepcopy=True).to(self.device)
-        if path in self.best_path_state:
-            pm.load_state_dict(self.best_path_state[path])
-        return pm
+        return RoundMetrics(round=round_idx, inner_loss=sum(losses.values()) / len(losses) if losses else float("nan"),
+                            per_path_loss=losses, delta_norm=sum(norms) / len(norms) if norms else 0.0, val_loss=val)
 
     def fit(self, corpus: ShardedCorpus, num_rounds: int, batch_size: int, log_every: int = 1,
             total_rounds: int | None = None):
@@ -338,47 +375,68 @@ class DiPaCoEngine:
             self.total_rounds = total_rounds
         elif self.total_rounds is None:
             self.total_rounds = self._global_round + num_rounds
-        hist = []
+        history = []
         for i in range(num_rounds):
             # the fused executor samples the next round's batches while this one runs on
-            # the GPU, when that round is certain to follow (no validation pass in between)
-            ahead = (self._global_round + 1 if i + 1 < num_rounds and not corpus.has_validation else None)
+            # the GPU, when that round is certain to follow (no validation pass between)
+            ahead = self._global_round + 1 if i + 1 < num_rounds and not corpus.has_validation else None
             m = self.run_round(corpus, batch_size, round_idx=self._global_round, _next_round=ahead)
             self._global_round += 1
-            hist.append(m)
+            history.append(m)
             if log_every and (m.round % log_every == 0 or i == num_rounds - 1):
-                print(f"[round {m.round:4d}] inner_loss={m.inner_loss:.4f} "
-                      f"delta_norm={m.delta_norm:.4f}")
-        return hist
+                print(f"[round {m.round:4d}] inner_loss={m.inner_loss:.4f} delta_norm={m.delta_norm:.4f}")
+        return history
+
+    # -- validation / best-path tracking -------------------------------------------
+    def _val_loss(self, model: nn.Module, seqs: torch.Tensor, batch_size: int) -> float:
+        model.eval()
+        total, tokens = token_loss_sum(model, seqs, batch_size=batch_size, device=self.device)
+        model.train()
+        return total / max(tokens, 1)
+
+    def _track_best(self, corpus, batch_size: int) -> float | None:
+        """Validation loss of every owned path with a validation shard; a path's best
+        state so far is kept for :meth:`compose_best`."""
+        seen = []
+        for path in self.backend.owned_paths():
+            val = corpus.val_shard(self.topology.path_index(path))
+            if val is None or val.size(0) == 0:
+                continue
+            model = self._executor.path_model(path)
+            loss = self._val_loss(model, val, batch_size)
+            seen.append(loss)
+            if loss < self.best_val_loss.get(path, math.inf):
+                self.best_val_loss[path] = loss
+                self.best_path_state[path] = _state_cpu(model.state_dict())
+        return sum(seen) / len(seen) if seen else None
+
+    def compose_best(self, path: Path) -> nn.Module:
+        model = build_path_model(self.config, path, self.bank, deepcopy=True).to(self.device)
+        if path in self.best_path_state:
+            model.load_state_dict(self.best_path_state[path])
+        return model
 
     def global_modules(self) -> dict[str, nn.Module]:
-        if self._fused is not None:
-            self._fused.sync_bank_views()
+        self._executor.sync_bank_views()
         return self.bank
 
-    # -- checkpoint ----------------------------------------------------------
-    def _gather_inner_state(self) -> dict[Path, dict]:
-        if self._fused is not None:
-            return self._fused.inner_state_dicts()
-        if self.materialize == "eager":
-            return {p: _opt_state_cpu(o.state_dict()) for p, o in self.inner_opts.items()}
-        return dict(self._opt_state)
-
+    # -- checkpoint ------------------------------------------------------------------
     def _world_size(self) -> int:
         return len({self.backend.rank_of_path(p) for p in self.topology.paths()})
 
     def state_dict(self) -> dict:
-        if self._fused is not None:
-            self._fused.sync_bank_views()
+        """The checkpoint payload (layout shared with the reference, so checkpoints load
+        in either framework)."""
+        ex = self._executor
+        ex.sync_bank_views()
         return {
             "format": 1,
             "fingerprint": config_fingerprint(self.config, self.diloco),
             "world_size": self._world_size(),
             "materialize": self.materialize,
             "bank": {k: _state_cpu(m.state_dict()) for k, m in self.bank.items()},
-            "outer_opt": (self._fused.outer_state_dict() if self._fused is not None
-                          else _opt_state_cpu(self.outer_opt.state_dict())),
-            "inner_opt_state": self._gather_inner_state(),
+            "outer_opt": ex.outer_state_dict(),
+            "inner_opt_state": ex.inner_state_dicts(),
             "global_round": self._global_round,
             "total_rounds": self.total_rounds,
             "best_val_loss": dict(self.best_val_loss),
@@ -389,33 +447,18 @@ class DiPaCoEngine:
 
     def load_state_dict(self, state: dict, *, strict: bool = True) -> None:
         if strict:
-            fp = config_fingerprint(self.config, self.diloco)
-            if state.get("fingerprint") != fp:
+            mine = config_fingerprint(self.config, self.diloco)
+            if state.get("fingerprint") != mine:
                 raise ValueError("checkpoint config fingerprint does not match this engine "
-                                 f"({state.get('fingerprint')} != {fp}); pass strict=False to override")
+                                 f"({state.get('fingerprint')} != {mine}); pass strict=False to override")
             if state.get("world_size") != self._world_size():
                 raise ValueError("checkpoint world_size does not match this engine "
                                  f"({state.get('world_size')} != {self._world_size()})")
         for key, sd in state["bank"].items():
             self.bank[key].load_state_dict({k: v.to(self.device) for k, v in sd.items()})
-        self._global_round = state["global_round"]
-        self.total_rounds = state["total_rounds"]
+        self._global_round, self.total_rounds = state["global_round"], state["total_rounds"]
         self.best_val_loss = dict(state["best_val_loss"])
         self.best_path_state = {p: dict(sd) for p, sd in state["best_path_state"].items()}
         self._gen.set_state(state["gen_state"])
         torch.set_rng_state(state["torch_rng_state"])
-        inner = state["inner_opt_state"]
-        if self._fused is not None:
-            self._fused.load_states(state["outer_opt"], inner)
-            return
-        self.outer_opt.load_state_dict(state["outer_opt"])
-        if self.materialize == "serial":
-            self._opt_state = dict(inner)
-            return
-        for path in self.backend.owned_paths():
-            pm = build_path_model(self.config, path, self.bank, deepcopy=True).to(self.device)
-            opt = make_inner_optimizer(pm, self.diloco)
-            if path in inner:
-                opt.load_state_dict(inner[path])
-            self.path_models[path] = pm
-            self.inner_opts[path] = opt
+        self._executor.load_states(state["outer_opt"], state["inner_opt_state"])

@@ -225,7 +225,10 @@ def bench_optim(G: int, H: int, V: int, F: int, layers: list[int], levels: list[
                                                  None, 0, 1, 1)),
              ("adamw_acc_step (+ outer pseudo-gradient)",
               lambda: x.adamw_acc_step(w32, gr, m1, m2, w16, ctas, P, P, coef, sched, 0.9, 0.95, 1e-8, 0.1, None, 0,
-                                       1, 1, rt, len(sizes), et))]
+                                       1, 1, rt, len(sizes), et, True)),
+             ("adamw_acc_step (no accumulation: the other inner steps)",
+              lambda: x.adamw_acc_step(w32, gr, m1, m2, w16, ctas, P, P, coef, sched, 0.9, 0.95, 1e-8, 0.1, None, 0,
+                                       1, 1, rt, len(sizes), et, False))]
     out = []
     _, bw, lab = _peaks()
     for name, fn in cases:

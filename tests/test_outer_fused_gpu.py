@@ -46,7 +46,7 @@ def test_adamw_acc_equals_adamw_then_accumulate_bitwise():
     glob = {k: torch.randn(4096, device=DEV) for k in ("a", "b0", "b1")}
     glob.update({f"c{g}": torch.zeros(4096, device=DEV) for g in range(G)})
 
-    def run(fused):
+    def run(fused, accumulate=True):
         w32, m1, m2 = W.clone(), M1.clone(), M2.clone()
         w16 = torch.zeros(G, P, device=DEV, dtype=torch.bfloat16)  # the inactive path's copy is never written
         gl = {k: v.clone() for k, v in glob.items()}
@@ -67,9 +67,12 @@ def test_adamw_acc_equals_adamw_then_accumulate_bitwise():
             rt = torch.from_numpy(reg.view(np.int64).copy()).to(DEV)
             et = torch.from_numpy(np.array(ents, dtype=ACC_ENTRY).view(np.int64).copy()).to(DEV)
             ext().adamw_acc_step(w32, GR, m1, m2, w16, ctas, P, P, coef, sched, 0.9, 0.95, 1e-8, 0.1, None, 0, 1,
-                                 1, rt, 3, et)
+                                 1, rt, 3, et, accumulate)
         else:
             ext().adamw_step(w32, GR, m1, m2, w16, P, P, P, G, coef, sched, 0.9, 0.95, 1e-8, 0.1, None, 0, 1, 1)
+            if not accumulate:
+                torch.cuda.synchronize()
+                return w32, w16, m1, m2, gl, delta
             segs = []
             for k in ("a", "b0", "b1"):
                 users = [g for g in range(G) if k in keys_of[g]]
@@ -93,6 +96,13 @@ def test_adamw_acc_equals_adamw_then_accumulate_bitwise():
         assert torch.equal(ref[5][k], got[5][k]), k
     # the inactive path's weights are untouched and its pseudo-gradient weight is zero
     assert torch.equal(got[0][3], W[3])
+    # the other inner steps: the same AdamW, and the outer buffers are left alone
+    plain, region = run(False, accumulate=False), run(True, accumulate=False)
+    for x, y in zip(plain[:4], region[:4]):
+        assert torch.equal(x, y)
+    for k in glob:
+        assert torch.equal(region[4][k], glob[k])
+    assert all(torch.isnan(region[5][k]).all() for k in ("a", "b0", "b1"))
 
 
 def test_outer_guard_skips_non_finite_elements():
