@@ -61,6 +61,12 @@ void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl
 void ce_backward(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor lse, torch::Tensor labels,
                  torch::Tensor inv_count, int64_t M, int64_t V, int64_t G);
 torch::Tensor cross_entropy_rows(torch::Tensor logits, torch::Tensor target);
+void ce_label_count(torch::Tensor labels, int64_t M, int64_t G, torch::Tensor inv_count);
+void ce_group_sum(torch::Tensor row_loss, torch::Tensor labels, int64_t M, int64_t G, torch::Tensor loss_sum,
+                  torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out, c10::optional<torch::Tensor> inv_given);
+void ce_rows_chunk(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t Mc, int64_t ms,
+                   int64_t V, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor inv,
+                   c10::optional<torch::Tensor> part, int64_t T, torch::Tensor err);
 void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, double max_norm, torch::Tensor work,
                     torch::Tensor coef, c10::optional<torch::Tensor> norm_out, c10::optional<torch::Tensor> rows,
                     int64_t r0, int64_t H, int64_t V);
@@ -128,6 +134,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_forward", &ce_forward);
   m.def("ce_backward", &ce_backward);
   m.def("cross_entropy_rows", &cross_entropy_rows);
+  m.def("ce_label_count", &ce_label_count);
+  m.def("ce_group_sum", &ce_group_sum);
+  m.def("ce_rows_chunk", &ce_rows_chunk);
   m.def("grad_clip_coef", &grad_clip_coef);
   m.def("adamw_step", &adamw_step);
   m.def("adam8bit_step", &adam8bit_step);

@@ -20,12 +20,15 @@
 
 namespace odp {
 
+// Per-row arrays (labels, lse, row_loss) of group g start at g * ms (ms = M unless the
+// call covers a chunk of each group's rows, the pointers then offset to the chunk).
 __global__ void ce_finalize_kernel(const float2* __restrict__ part, int T, const __nv_bfloat16* __restrict__ logits,
                                    long long ldl, long long sl, const int* __restrict__ labels, int M, int G,
-                                   float* __restrict__ lse, float* __restrict__ row_loss) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= G * M) return;
-  const float2* p = part + (long long)r * T;
+                                   float* __restrict__ lse, float* __restrict__ row_loss, long long ms) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= G * M) return;
+  const long long r = (long long)(q / M) * ms + q % M;
+  const float2* p = part + (long long)q * T;
   float mx = -INFINITY;
   for (int t = 0; t < T; ++t) mx = fmaxf(mx, p[t].x);
   float s = 0.f;
@@ -33,7 +36,7 @@ __global__ void ce_finalize_kernel(const float2* __restrict__ part, int T, const
   const float l = mx + logf(s);
   lse[r] = l;
   const int y = labels[r];
-  const int g = r / M, m = r % M;
+  const int g = q / M, m = q % M;
   float loss = 0.f;
   if (y >= 0) loss = l - __bfloat162float(logits[g * sl + (long long)m * ldl + y]);
   row_loss[r] = loss;
@@ -79,13 +82,14 @@ __global__ void group_sum_kernel(const float* __restrict__ row_loss, const int* 
 // In place: logits -> (softmax - onehot) * inv_count[g]; 8 bf16 per thread.
 __global__ void ce_backward_kernel(__nv_bfloat16* logits, long long ldl, long long sl, const float* __restrict__ lse,
                                    const int* __restrict__ labels, const float* __restrict__ inv_count, int M, int V,
-                                   int G) {
+                                   int G, long long ms) {
   const long long vec_per_row = V / 8;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)G * M * vec_per_row) return;
-  const long long r = idx / vec_per_row;
+  const long long q = idx / vec_per_row;
   const int c0 = (int)(idx % vec_per_row) * 8;
-  const int g = (int)(r / M), m = (int)(r % M);
+  const int g = (int)(q / M), m = (int)(q % M);
+  const long long r = (long long)g * ms + m;
   uint4* ptr = reinterpret_cast<uint4*>(logits + g * sl + (long long)m * ldl + c0);
   const int y = labels[r];
   if (y < 0) {
@@ -150,12 +154,12 @@ __global__ void __launch_bounds__(kCeThreads) ce_fused_kernel(__nv_bfloat16* log
                                                               const int* __restrict__ labels, int M, int V,
                                                               const float* __restrict__ inv_count,
                                                               float* __restrict__ lse_out, float* __restrict__ row_loss,
-                                                              int* err) {
+                                                              int* err, long long ms) {
   extern __shared__ __align__(16) uint8_t ce_smem[];
   __shared__ uint64_t bar;
   __shared__ float red_m[kCeThreads / 32], red_s[kCeThreads / 32];
-  const long long r = blockIdx.x;
-  const int g = (int)(r / M), m = (int)(r % M);
+  const int g = (int)(blockIdx.x / M), m = (int)(blockIdx.x % M);
+  const long long r = (long long)g * ms + m;  // index of the per-row arrays
   __nv_bfloat16* rowp = logits + g * sl + (long long)m * ldl;
   uint4* row = reinterpret_cast<uint4*>(rowp);
   const int nvec = V / 8;
@@ -287,7 +291,7 @@ void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl
   odp::ce_finalize_kernel<<<(R + 255) / 256, 256, 0, st>>>(
       reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)T,
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)G,
-      lse.data_ptr<float>(), row_loss.data_ptr<float>());
+      lse.data_ptr<float>(), row_loss.data_ptr<float>(), (long long)M);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
                                                  loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
@@ -321,7 +325,7 @@ void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor label
   odp::ce_fused_kernel<<<(unsigned)(G * M), odp::kCeThreads, (size_t)V * 2, st>>>(
       reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)V,
       given ? given : inv_count.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(),
-      err.data_ptr<int>());
+      err.data_ptr<int>(), (long long)M);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
                                                  loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
@@ -336,7 +340,68 @@ void ce_backward(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor ls
   const long long n = G * M * (V / 8);
   odp::ce_backward_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, lse.data_ptr<float>(), labels.data_ptr<int>(),
-      inv_count.data_ptr<float>(), (int)M, (int)V, (int)G);
+      inv_count.data_ptr<float>(), (int)M, (int)V, (int)G, (long long)M);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ---------------------------------------------------------------- row chunks
+// The loss over a batch computed in chunks of each group's rows (bounded logits memory):
+// ce_label_count once (the dlogits scale needs the whole batch's count), then per chunk
+// the GEMM's logits for rows [r0, r0 + Mc) and ce_rows_chunk (labels / lse / row_loss
+// passed offset to r0, group stride ms = the batch's rows), and ce_group_sum once over
+// all rows at the end.
+void ce_label_count(torch::Tensor labels, int64_t M, int64_t G, torch::Tensor inv_count) {
+  c10::cuda::CUDAGuard guard(labels.device());
+  odp::label_count_kernel<<<(int)G, 256, 0, at::cuda::getCurrentCUDAStream()>>>(labels.data_ptr<int>(), (int)M,
+                                                                                 inv_count.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ce_group_sum(torch::Tensor row_loss, torch::Tensor labels, int64_t M, int64_t G, torch::Tensor loss_sum,
+                  torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out, c10::optional<torch::Tensor> inv_given) {
+  c10::cuda::CUDAGuard guard(labels.device());
+  odp::group_sum_kernel<<<(int)G, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M, loss_sum.data_ptr<float>(),
+      inv_count.data_ptr<float>(), loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr,
+      inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// One chunk: logits [G][Mc] rows (row stride ldl, group stride sl) -> lse, row losses and
+// in-place dlogits scaled by inv (the batch's 1 / count per group). One-pass kernel for
+// V <= 32768; wider vocabularies merge the logits GEMM's (max, sum exp) partials
+// `part` ([G][Mc][T] float2) and then rewrite the logits.
+void ce_rows_chunk(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t Mc, int64_t ms,
+                   int64_t V, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor inv,
+                   c10::optional<torch::Tensor> part, int64_t T, torch::Tensor err) {
+  TORCH_CHECK(V % 8 == 0 && ldl % 8 == 0 && sl % 8 == 0, "ce_rows_chunk: vocab and strides multiples of 8");
+  c10::cuda::CUDAGuard guard(logits.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (!part.has_value()) {
+    TORCH_CHECK(V <= odp::kCeMaxV && reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0,
+                "ce_rows_chunk: the one-pass kernel takes at most 32768 columns, 16-byte aligned rows");
+    static bool attr = false;
+    if (!attr) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(odp::ce_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          odp::kCeMaxV * 2));
+      attr = true;
+    }
+    odp::ce_fused_kernel<<<(unsigned)(G * Mc), odp::kCeThreads, (size_t)V * 2, st>>>(
+        reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)Mc, (int)V,
+        inv.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(), err.data_ptr<int>(), ms);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  const int R = (int)(G * Mc);
+  odp::ce_finalize_kernel<<<(R + 255) / 256, 256, 0, st>>>(
+      reinterpret_cast<const float2*>(part->data_ptr<float>()), (int)T,
+      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)Mc, (int)G,
+      lse.data_ptr<float>(), row_loss.data_ptr<float>(), ms);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const long long n = G * Mc * (V / 8);
+  odp::ce_backward_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, lse.data_ptr<float>(), labels.data_ptr<int>(),
+      inv.data_ptr<float>(), (int)Mc, (int)V, (int)G, ms);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -1,6 +1,8 @@
 """``opendipaco`` command line (reference ``src/opendipaco/launch/cli.py``).
 
     opendipaco run          --config c.yaml        all roles in one process
+    opendipaco train        --config c.yaml        synchronous training on this node's GPUs
+                                                   (under torchrun: one process per GPU)
     opendipaco coordinator  --config c.yaml        single-node async coordinator
     opendipaco scheduler    --config c.yaml        sharded scheduler (holds no weights)
     opendipaco ps           --config c.yaml --shard-id N
@@ -37,6 +39,15 @@ def cmd_run(a):
     from .roles import run_local
 
     _report(*run_local(load_config(a.config)))
+    return 0
+
+
+def cmd_train(a):
+    from .train import run_train
+
+    hist = run_train(load_config(a.config))
+    if hist:
+        print(f"final inner loss {hist[-1].inner_loss:.4f} after {len(hist)} rounds")
     return 0
 
 
@@ -162,6 +173,7 @@ def build_parser() -> argparse.ArgumentParser:
         return s
 
     with_config("run", "stand up the whole cluster locally", cmd_run)
+    with_config("train", "synchronous DiLoCo training on this node's GPUs (comm / kernels sections)", cmd_train)
     with_config("coordinator", "run a single-node coordinator", cmd_coordinator)
     with_config("scheduler", "run the sharded scheduler", cmd_scheduler)
     with_config("ps", "run one parameter-server shard", cmd_ps).add_argument("--shard-id", type=int, required=True)

@@ -3,9 +3,13 @@
 One file (``.yaml``/``.yml``, ``.toml`` or ``.json``) describes a run; every host of
 the cluster reads the same file. Sections: ``model``, ``diloco``, ``data``,
 ``transport``, ``tls``, ``sharded``, ``tracker``, ``ownership``, ``robustness``,
-``schedule``, ``run`` (plus top-level ``mode``). Section names, keys and defaults
-are the reference's file format, so existing config files load unchanged; unknown
-keys and contradictory combinations are rejected when the file is loaded.
+``schedule``, ``run`` (plus top-level ``mode``) -- names, keys and defaults of the
+reference's file format, so existing config files load unchanged -- and two sections of
+this framework only: ``comm`` (the collective backend of synchronous multi-GPU training:
+NVLink / NCCL, compressed outer payloads, intra-path data parallelism) and ``kernels``
+(fused executor, CUDA graphs, attention kernels, cross-GPU wait bound). Neither enters
+the model / DiLoCo fingerprint. Unknown keys and contradictory combinations are rejected
+when the file is loaded.
 """
 
 from __future__ import annotations
@@ -203,9 +207,30 @@ class RunCfg:
     min_task_rate: float | None = None
 
 
+@dataclass
+class CommCfg:
+    """Collectives of synchronous multi-GPU training (``opendipaco train`` on one node,
+    one process per GPU). Not part of the model / DiLoCo fingerprint."""
+
+    backend: str = "auto"                   # "auto" | "nvlink" | "nccl" | "local"
+    outer_compress: str = "none"            # NVLink outer step payloads: "none" | "int4" | "topk"
+    outer_density: float = 0.01             # top-k: kept fraction of each 4096-element block
+    dp: int = 1                             # GPUs per path group (intra-path data parallelism)
+
+
+@dataclass
+class KernelsCfg:
+    """B200 execution options of the engine (not part of any fingerprint)."""
+
+    fused: bool | None = None               # None: fused executor on CUDA, module executor on CPU
+    cuda_graphs: bool = True                # one CUDA graph per round of inner steps
+    attention: str = "auto"                 # "auto" (tcgen05) | "mma" (older mma.sync kernels)
+    peer_wait_ms: float = 2000.0            # bound of every wait on another GPU's flag
+
+
 _SECTIONS = {"model": ModelCfg, "diloco": DiLoCoCfg, "data": DataCfg, "transport": TransportCfg, "tls": TLSCfg,
              "sharded": ShardedCfg, "tracker": TrackerCfg, "ownership": OwnershipCfg, "robustness": RobustnessCfg,
-             "schedule": ScheduleCfg, "run": RunCfg}
+             "schedule": ScheduleCfg, "run": RunCfg, "comm": CommCfg, "kernels": KernelsCfg}
 
 
 def _dial_host(host: str, connect_host: str | None) -> str:
@@ -226,6 +251,8 @@ class LaunchConfig:
     robustness: RobustnessCfg = field(default_factory=RobustnessCfg)
     schedule: ScheduleCfg = field(default_factory=ScheduleCfg)
     run: RunCfg = field(default_factory=RunCfg)
+    comm: CommCfg = field(default_factory=CommCfg)
+    kernels: KernelsCfg = field(default_factory=KernelsCfg)
 
     @classmethod
     def from_dict(cls, d: dict | None) -> "LaunchConfig":
@@ -249,6 +276,18 @@ class LaunchConfig:
         _choice("data.ship", dt.ship, ("bytes", "spec"))
         _choice("ownership.mode", own.mode, ("static", "rendezvous"))
         _choice("schedule.mode", sch.mode, ("central", "decentralized"))
+        c, k = self.comm, self.kernels
+        _choice("comm.backend", c.backend, ("auto", "nvlink", "nccl", "local"))
+        _choice("comm.outer_compress", c.outer_compress, ("none", "int4", "topk"))
+        _choice("kernels.attention", k.attention, ("auto", "mma"))
+        if not 0.0 < c.outer_density <= 1.0:
+            raise ValueError(f"comm.outer_density must be in (0, 1], got {c.outer_density!r}")
+        if c.dp < 1:
+            raise ValueError(f"comm.dp must be >= 1, got {c.dp}")
+        if (c.outer_compress != "none" or c.dp > 1) and c.backend not in ("auto", "nvlink"):
+            raise ValueError("comm.outer_compress and comm.dp > 1 need the NVLink backend (comm.backend: nvlink)")
+        if k.peer_wait_ms <= 0:
+            raise ValueError(f"kernels.peer_wait_ms must be positive, got {k.peer_wait_ms!r}")
         if t.down == "delta" and not sharded:
             raise ValueError("transport.down: delta requires mode: sharded (owners serve the deltas)")
         if not 0.0 < t.up_density <= 1.0:

@@ -311,23 +311,33 @@ class FusedExecutor:
         z = lambda *s, dt=f32: torch.zeros(*s, device=dev, dtype=dt)  # noqa: E731
         self.B, self.S, self.M, self.C, self.L = B, S, M, C, L
         self.T = 2 * ((V + 127) // 128)  # (max, sum exp) partials: two per 128-column tile
+        # activation checkpointing: only the layer inputs X are kept; each layer's other
+        # activations live in one shared slot and are recomputed before its backward
+        self.ckpt = bool(getattr(self.e.diloco, "activation_checkpoint", False)) and L > 1
+        nslot = 1 if self.ckpt else max(L, 1)
         self.X = z(L + 1, G, M, H)
-        self.HR = z(max(L, 1), G, M, H)
-        self.XN1 = z(max(L, 1), G, M, H, dt=b16)
-        self.XN2 = z(max(L, 1), G, M, H, dt=b16)
-        self.RS1 = z(max(L, 1), G, M)
-        self.RS2 = z(max(L, 1), G, M)
-        self.QKV = z(max(L, 1), G, M, C, dt=b16)
-        self.O = z(max(L, 1), G, M, H, dt=b16)
-        self.LSEA = z(max(L, 1), G * B, nh, S)
-        self.GU = z(max(L, 1), G, M, 2 * Fd, dt=b16)
-        self.ACT = z(max(L, 1), G, M, Fd, dt=b16)
+        self.HR = z(nslot, G, M, H)
+        self.XN1 = z(nslot, G, M, H, dt=b16)
+        self.XN2 = z(nslot, G, M, H, dt=b16)
+        self.RS1 = z(nslot, G, M)
+        self.RS2 = z(nslot, G, M)
+        self.QKV = z(nslot, G, M, C, dt=b16)
+        self.O = z(nslot, G, M, H, dt=b16)
+        self.LSEA = z(nslot, G * B, nh, S)
+        self.GU = z(nslot, G, M, 2 * Fd, dt=b16)
+        self.ACT = z(nslot, G, M, Fd, dt=b16)
         self.XNF = z(G, M, H, dt=b16)
         self.RSF = z(G, M)
-        self.LOGITS = z(G, M, V, dt=b16)
+        # loss_chunks > 1: the LM head runs over chunks of each path's sequences (as
+        # torch.chunk splits the batch), so the logits buffer holds one chunk
+        k = max(1, int(getattr(self.e.diloco, "loss_chunks", 1) or 1))
+        per = -(-B // k)
+        self.chunks = [(b0 * S, min(B, b0 + per) * S) for b0 in range(0, B, per)] if k > 1 else [(0, M)]
+        self.MCH = self.chunks[0][1] - self.chunks[0][0]  # rows of the logits buffer
+        self.LOGITS = z(G, self.MCH, V, dt=b16)
         # one-pass CE keeps a row in registers (<= 32768 columns); wider vocabularies use GEMM partials
         self.ce_fused = V % 8 == 0 and V <= 32768 and os.environ.get("ODP_CE_IMPL", "fused") == "fused"
-        self.PART = z(1) if self.ce_fused else z(G, M, self.T, 2)
+        self.PART = z(1) if self.ce_fused else z(G, self.MCH, self.T, 2)
         self.LSEC = z(G, M)
         self.ROWLOSS = z(G, M)
         self.LOSSSUM = z(G)
@@ -455,20 +465,13 @@ class FusedExecutor:
 
         # ---------------- forward
         X_.embedding_fwd(ids, w32[lay.emb:], P, self.X[0], M, H, G, V)
-        for l, lo in enumerate(lay.layers):
-            X_.rmsnorm_fwd(self.X[l], MH, w32[lo.ln1:], P, self.XN1[l], MH, self.RS1[l], M, H, G, self.eps)
-            self._gemm(self.XN1[l], H, MH, False, w16[lo.qkv:], H, P, False, self.QKV[l], C, MC, M, C, H, "bf16")
-            attn.fwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l], self.err)
-            self._gemm(self.O[l], H, MH, False, w16[lo.o:], H, P, False, self.HR[l], H, MH, M, H, H, "resid",
-                       R=self.X[l], ldr=H, sr=MH)
-            X_.rmsnorm_fwd(self.HR[l], MH, w32[lo.ln2:], P, self.XN2[l], MH, self.RS2[l], M, H, G, self.eps)
-            self._gemm(self.XN2[l], H, MH, False, w16[lo.gu:], H, P, False, self.ACT[l], Fd, MF, M, 2 * Fd, H,
-                       "swiglu", bn=128, aux=self.GU[l], ldx=2 * Fd, sx=MF2, f_half=Fd)
-            self._gemm(self.ACT[l], Fd, MF, False, w16[lo.down:], Fd, P, False, self.X[l + 1], H, MH, M, H, Fd,
-                       "resid", R=self.HR[l], ldr=H, sr=MH)
+        for l in range(self.L):
+            self._layer_fwd(l, down=True)
         L = self.L
         X_.rmsnorm_fwd(self.X[L], MH, w32[lay.normf:], P, self.XNF, MH, self.RSF, M, H, G, self.eps)
-        if self.ce_fused:
+        if len(self.chunks) > 1:
+            self._lm_head_chunked(s, labels)
+        elif self.ce_fused:
             # plain bf16 logits (TMA-stored), then loss + dlogits in one pass over each row
             self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "bf16",
                        bn=128)
@@ -483,9 +486,12 @@ class FusedExecutor:
             X_.ce_backward(self.LOGITS, V, M * V, self.LSEC, labels, self.INVCNT if given is None else given, M, V,
                            G)
         # ---------------- backward
-        self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
-        side = self._side
-        if side is not None:
+        side = self._side if len(self.chunks) == 1 else None
+        if len(self.chunks) == 1:
+            self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
+        if len(self.chunks) > 1:
+            pass  # the chunks already wrote DXN and the LM-head weight gradient
+        elif side is not None:
             # the LM-head weight gradient is needed only by the optimizer: on a side stream
             # with a capped grid it runs under the layers' backward, whose small GEMMs and
             # attention leave SMs idle; joined before the gradient norm
@@ -502,20 +508,23 @@ class FusedExecutor:
                        gr[lay.normf:], P, self.NORMWORK, M, H, G, 0.0)
         for l in range(L - 1, -1, -1):
             lo = lay.layers[l]
+            if self.ckpt:
+                self._layer_fwd(l, down=False)  # the layer's activations, recomputed into the slot
+            k = 0 if self.ckpt else l
             self._gemm(self.DX16, H, MH, False, w16[lo.down:], Fd, P, True, self.DGU, 2 * Fd, MF2, M, Fd, H,
-                       "swiglu_bwd", aux=self.GU[l], ldx=2 * Fd, sx=MF2, f_half=Fd)
-            self._wgrad(f"down{l}", self.DX16, H, MH, self.ACT[l], Fd, MF, gr[lo.down:], Fd, P, H, Fd, M)
+                       "swiglu_bwd", aux=self.GU[k], ldx=2 * Fd, sx=MF2, f_half=Fd)
+            self._wgrad(f"down{l}", self.DX16, H, MH, self.ACT[k], Fd, MF, gr[lo.down:], Fd, P, H, Fd, M)
             self._gemm(self.DGU, 2 * Fd, MF2, False, w16[lo.gu:], H, P, True, self.DXN, H, MH, M, H, 2 * Fd, "f32")
-            self._wgrad(f"gu{l}", self.DGU, 2 * Fd, MF2, self.XN2[l], H, MH, gr[lo.gu:], H, P, 2 * Fd, H, M)
-            X_.rmsnorm_bwd(self.HR[l], MH, w32[lo.ln2:], P, self.RS2[l], self.DXN, MH, self.DX, self.DX, MH,
+            self._wgrad(f"gu{l}", self.DGU, 2 * Fd, MF2, self.XN2[k], H, MH, gr[lo.gu:], H, P, 2 * Fd, H, M)
+            X_.rmsnorm_bwd(self.HR[k], MH, w32[lo.ln2:], P, self.RS2[k], self.DXN, MH, self.DX, self.DX, MH,
                            self.DX16, gr[lo.ln2:], P, self.NORMWORK, M, H, G, 0.0)
             self._gemm(self.DX16, H, MH, False, w16[lo.o:], H, P, True, self.DOUT, H, MH, M, H, H, "bf16")
-            self._wgrad(f"o{l}", self.DX16, H, MH, self.O[l], H, MH, gr[lo.o:], H, P, H, H, M)
-            attn.bwd(self.QKV[l], G * B, S, nh, nkv, self.cos, self.sin, self.O[l], self.LSEA[l], self.DOUT,
+            self._wgrad(f"o{l}", self.DX16, H, MH, self.O[k], H, MH, gr[lo.o:], H, P, H, H, M)
+            attn.bwd(self.QKV[k], G * B, S, nh, nkv, self.cos, self.sin, self.O[k], self.LSEA[k], self.DOUT,
                      self.DELTA, self.DQKV, self.err)
             self._gemm(self.DQKV, C, MC, False, w16[lo.qkv:], H, P, True, self.DXN, H, MH, M, H, C, "f32")
-            self._wgrad(f"qkv{l}", self.DQKV, C, MC, self.XN1[l], H, MH, gr[lo.qkv:], H, P, C, H, M)
-            X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[l], self.DXN, MH, self.DX, self.DX, MH,
+            self._wgrad(f"qkv{l}", self.DQKV, C, MC, self.XN1[k], H, MH, gr[lo.qkv:], H, P, C, H, M)
+            X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[k], self.DXN, MH, self.DX, self.DX, MH,
                            self.DX16, gr[lo.ln1:], P, self.NORMWORK, M, H, G, 0.0)
         emb_n = bb.vocab_size * H
         rows = self.emb_rows
@@ -560,6 +569,70 @@ class FusedExecutor:
         else:
             X_.adamw_step(self.W32, self.GRAD, self.MOM1, self.MOM2, self.W16, P, P, P, G, self.COEF,
                           self.SCHED[s], b1, b2, 1e-8, dl.inner_weight_decay, rows, lay.emb, H, V)
+
+    def _layer_fwd(self, l: int, down: bool) -> None:
+        """Forward of layer ``l`` from ``X[l]``: RMSNorm -> QKV -> attention -> O (+residual)
+        -> RMSNorm -> gate|up (SwiGLU) [-> down (+residual) into ``X[l + 1]``]. Its
+        activations go to slot ``l``, or to the one shared slot when checkpointing."""
+        X_ = ext()
+        bb, G, P = self.bb, self.G, self.P
+        H, Fd = bb.hidden_size, bb.intermediate_size
+        nh, nkv = bb.num_attention_heads, bb.kv_heads()
+        M, C, S, B = self.M, self.C, self.S, self.B
+        MH, MC, MF, MF2 = M * H, M * C, M * Fd, M * 2 * Fd
+        w32, w16 = self.W32.view(-1), self.W16.view(-1)
+        lo = self.layout.layers[l]
+        k = 0 if self.ckpt else l
+        X_.rmsnorm_fwd(self.X[l], MH, w32[lo.ln1:], P, self.XN1[k], MH, self.RS1[k], M, H, G, self.eps)
+        self._gemm(self.XN1[k], H, MH, False, w16[lo.qkv:], H, P, False, self.QKV[k], C, MC, M, C, H, "bf16")
+        attn.fwd(self.QKV[k], G * B, S, nh, nkv, self.cos, self.sin, self.O[k], self.LSEA[k], self.err)
+        self._gemm(self.O[k], H, MH, False, w16[lo.o:], H, P, False, self.HR[k], H, MH, M, H, H, "resid",
+                   R=self.X[l], ldr=H, sr=MH)
+        X_.rmsnorm_fwd(self.HR[k], MH, w32[lo.ln2:], P, self.XN2[k], MH, self.RS2[k], M, H, G, self.eps)
+        self._gemm(self.XN2[k], H, MH, False, w16[lo.gu:], H, P, False, self.ACT[k], Fd, MF, M, 2 * Fd, H,
+                   "swiglu", bn=128, aux=self.GU[k], ldx=2 * Fd, sx=MF2, f_half=Fd)
+        if down:
+            self._gemm(self.ACT[k], Fd, MF, False, w16[lo.down:], Fd, P, False, self.X[l + 1], H, MH, M, H, Fd,
+                       "resid", R=self.HR[k], ldr=H, sr=MH)
+
+    def _lm_head_chunked(self, s: int, labels) -> None:
+        """LM head + loss over row chunks: per chunk the logits GEMM, the chunk's loss rows
+        and in-place dlogits (scaled by the WHOLE batch's 1 / count), the input gradient of
+        its rows and the weight gradient accumulated over the chunks (fp32, the clip-norm
+        box sums on the last chunk); then the loss sum over all rows. The reference's
+        chunked loss (src/opendipaco/model.py:157-174) splits the batch the same way."""
+        from ..ops.gemm import gemm_wgrad
+
+        X_ = ext()
+        bb, G, P = self.bb, self.G, self.P
+        H, V = bb.hidden_size, bb.vocab_size
+        M, MH, mch = self.M, self.M * bb.hidden_size, self.MCH
+        w16, gr = self.W16.view(-1), self.GRAD.view(-1)
+        lm = self.layout.lm
+        given = self.INVC[s] if self.dp > 1 else None
+        if given is None:
+            X_.ce_label_count(labels, M, G, self.INVCNT)
+        inv = given if given is not None else self.INVCNT
+        xnf, dxn = self.XNF.view(-1), self.DXN.view(-1)
+        lab, lse, rloss = labels.view(-1), self.LSEC.view(-1), self.ROWLOSS.view(-1)
+        last = len(self.chunks) - 1
+        for ci, (r0, r1) in enumerate(self.chunks):
+            mc = r1 - r0
+            a = xnf[r0 * H:]
+            if self.ce_fused:
+                self._gemm(a, H, MH, False, w16[lm:], H, P, False, self.LOGITS, V, mch * V, mc, V, H, "bf16", bn=128)
+                part = None
+            else:
+                self._gemm(a, H, MH, False, w16[lm:], H, P, False, self.LOGITS, V, mch * V, mc, V, H, "logits",
+                           bn=128, part=self.PART)
+                part = self.PART
+            X_.ce_rows_chunk(self.LOGITS, V, mch * V, lab[r0:], mc, M, V, G, lse[r0:], rloss[r0:], inv, part,
+                             self.T, self.err)
+            self._gemm(self.LOGITS, V, mch * V, False, w16[lm:], H, P, True, dxn[r0 * H:], H, MH, mc, H, V, "f32")
+            sq = self._sq("lm") if ci == last else {}
+            gemm_wgrad(self.LOGITS, V, mch * V, a, H, MH, gr[lm:], H, P, V, H, mc, G, 1, self.WGWS, sq.get("sq"),
+                       sq.get("sq_ld", 0), self.err, beta=0.0 if ci == 0 else 1.0, bn=self._bn(V, H))
+        X_.ce_group_sum(self.ROWLOSS, labels, M, G, self.LOSSSUM, self.INVCNT, self.LOSSES[s], given)
 
     # ------------------------------------------------------------------ round inputs
     def _prepare(self, corpus, batch_size: int, round_idx: int, slot: int = 0):
@@ -813,6 +886,13 @@ class FusedExecutor:
         """Kernels of this package launched per round (inner steps + outer step)."""
         per_step = (14 + 22 * self.L + (2 if self.dp > 1 else 0) - (1 if self.sq_bases is not None else 0)
                     + sum(1 for sp in self.wg_split.values() if sp > 1))
+        if self.ckpt:  # recomputed layer forwards (all but the down projection): 6 launches each
+            per_step += 6 * self.L
+        if len(self.chunks) > 1:
+            # chunked LM head: label count + per chunk (logits, CE rows (two kernels from
+            # GEMM partials), dX, dW) + group sum, against 6 launches (+ a split-K reduce)
+            per_chunk = 4 if self.ce_fused else 5
+            per_step += per_chunk * len(self.chunks) + 2 - 6 - (1 if self.wg_split.get("lm", 1) > 1 else 0)
         be = self.e.backend
         outer = be.outer_launch_count(self) if getattr(be, "world_size", 1) > 1 else 1
         return self.e.diloco.inner_steps * per_step + outer

@@ -199,3 +199,41 @@ def test_split_k_weight_gradients_track_unsplit(monkeypatch):
         for p in a.per_path_loss:
             assert abs(a.per_path_loss[p] - b.per_path_loss[p]) < 1e-3 * b.per_path_loss[p]
     assert _bank_maxdiff(runs["2"][1], runs["1"][1]) < 1e-3
+
+
+def _bank_equal(a, b):
+    for k in a.bank:
+        for x, y in zip(a.bank[k].state_dict().values(), b.bank[k].state_dict().values()):
+            if not torch.equal(x, y):
+                return False
+    return True
+
+
+def test_activation_checkpoint_recompute_is_bitwise():
+    """Checkpointing keeps only the layer inputs and recomputes each layer's forward
+    before its backward with the same deterministic kernels: identical training."""
+    cfg = _cfg(layers=(2, 1))
+    corpus = _corpus(cfg)
+    a, b = _engine(cfg, "cuda"), _engine(cfg, "cuda", activation_checkpoint=True)
+    ha, hb = a.fit(corpus, 3, 4, log_every=0), b.fit(corpus, 3, 4, log_every=0)
+    assert b._fused.ckpt and b._fused.QKV.shape[0] == 1 and a._fused.QKV.shape[0] == 3
+    assert [m.per_path_loss for m in ha] == [m.per_path_loss for m in hb]
+    assert _bank_equal(a, b)
+
+
+@pytest.mark.parametrize("vocab_impl", ["fused", "partials"])
+def test_loss_chunks_track_the_whole_batch(vocab_impl, monkeypatch):
+    """loss_chunks = 3 on a 6-sequence batch: the logits buffer holds 2 sequences, the
+    loss is normalised by the whole batch, and training matches the unchunked run up to
+    the weight-gradient summation order (exactly for the loss of the first step)."""
+    if vocab_impl == "partials":
+        monkeypatch.setenv("ODP_CE_IMPL", "partials")
+    cfg = _cfg()
+    corpus = _corpus(cfg)
+    a, b = _engine(cfg, "cuda"), _engine(cfg, "cuda", loss_chunks=3)
+    ha, hb = a.fit(corpus, 3, 6, log_every=0), b.fit(corpus, 3, 6, log_every=0)
+    assert len(b._fused.chunks) == 3 and b._fused.LOGITS.shape[1] == 2 * 64
+    for x, y in zip(ha, hb):
+        for p in x.per_path_loss:
+            assert abs(x.per_path_loss[p] - y.per_path_loss[p]) < 1e-3 * x.per_path_loss[p], (p, x, y)
+    assert _bank_maxdiff(a, b) < 2e-3

@@ -3,6 +3,7 @@ process for every mode (coordinator, static sharded, rendezvous, decentralized),
 a volunteer ``join`` from a signed manifest. All on CPU over loopback TCP."""
 
 import json
+import os
 import threading
 
 import pytest
@@ -167,3 +168,62 @@ def test_join_from_signed_manifest(tmp_path):
     run_join(scheduler=addr, auth_key="s3cret", device="cpu", quiet=True, server_pub=ident.public_key_hex)
     th.join(timeout=120)
     _all_paths_done(box["r"][1])
+
+
+def _train_cfg(tmp_path, **comm):
+    from opendipaco_b200.launch.config import LaunchConfig
+
+    return LaunchConfig.from_dict({
+        "model": {"vocab_size": 256, "hidden_size": 64, "num_attention_heads": 2, "intermediate_size": 128,
+                  "layers_per_level": [1, 1], "level_sizes": [2, 2], "sequence_length": 32,
+                  "max_position_embeddings": 64},
+        "diloco": {"inner_steps": 2, "activation_checkpoint": False},
+        "data": {"num_documents": 64, "synthetic_doc_len": 48, "routing": "round_robin"},
+        "run": {"generations": 2, "batch_size": 2, "checkpoint_dir": str(tmp_path / "ck")},
+        "comm": comm, "kernels": {"fused": False}})
+
+
+def test_train_command_single_process(tmp_path):
+    from opendipaco_b200.launch.train import run_train
+
+    hist = run_train(_train_cfg(tmp_path))
+    assert len(hist) == 2 and all(m.inner_loss == m.inner_loss for m in hist)
+    assert (tmp_path / "ck" / "round000002" / "rank0.pt").exists()
+
+
+def test_comm_and_kernels_sections_validate():
+    from opendipaco_b200.launch.config import LaunchConfig
+
+    cfg = LaunchConfig.from_dict({"comm": {"backend": "nvlink", "outer_compress": "int4", "dp": 2},
+                                  "kernels": {"attention": "mma", "peer_wait_ms": 50}})
+    assert cfg.comm.dp == 2 and cfg.kernels.attention == "mma"
+    for bad in ({"comm": {"backend": "gloo"}}, {"comm": {"outer_compress": "int4", "backend": "nccl"}},
+                {"comm": {"outer_density": 0}}, {"kernels": {"attention": "triton"}}, {"kernels": {"peer": 1}}):
+        with pytest.raises(ValueError):
+            LaunchConfig.from_dict(bad)
+
+
+def test_train_command_two_gloo_ranks(tmp_path):
+    """``opendipaco train`` under torchrun: two CPU ranks (gloo) with the NCCL-style
+    backend; both ranks end with identical shared modules."""
+    import subprocess
+    import sys
+
+    import torch
+    import yaml
+
+    cfg = _train_cfg(tmp_path, backend="nccl").to_dict()
+    path = tmp_path / "c.yaml"
+    path.write_text(yaml.safe_dump(cfg))
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29633", "-m", "opendipaco_b200.launch",
+           "train", "--config", str(path)]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=dict(os.environ, OMP_NUM_THREADS="1"))
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    a = torch.load(tmp_path / "ck" / "round000002" / "rank0.pt", weights_only=False)
+    b = torch.load(tmp_path / "ck" / "round000002" / "rank1.pt", weights_only=False)
+    shared = [k for k in a["bank"] if k in b["bank"] and ".p" not in k]
+    assert shared
+    for k in shared:
+        for n in a["bank"][k]:
+            assert torch.equal(a["bank"][k][n], b["bank"][k][n]), (k, n)
