@@ -192,6 +192,7 @@ class ParameterServer(ReactorServer):
         self.min_owner_reputation = min_owner_reputation
         self.corpus_weights = dict(corpus_weights) if corpus_weights else None
         self._tracker = None
+        self._hb_paused = threading.Event()  # set: stop refreshing the tracker record (suspend)
         full = build_module_bank(config, seed=bank_seed)
         self.bank = {k: full[k].to(self.device) for k in self.owned_keys}
         self._versions = {k: (0, 0) for k in self.bank}
@@ -667,7 +668,7 @@ class ParameterServer(ReactorServer):
 
         def beat():
             while True:
-                for a in addrs:
+                for a in addrs if not self._hb_paused.is_set() else ():
                     try:
                         register_peer(a, self.identity, reachability="public", peer_addr=(advertise_host, self.port),
                                       roles=["owner"], auth_key=auth_key, tls=tls, timeout=5.0)
@@ -677,6 +678,16 @@ class ParameterServer(ReactorServer):
                     return
 
         threading.Thread(target=beat, daemon=True).start()
+
+    def pause_heartbeat(self) -> None:
+        """Stop re-registering on the tracker while the server keeps serving: a
+        deterministic suspend for failure tests. The record lapses after the tracker's
+        TTL, as a sleeping laptop's would."""
+        self._hb_paused.set()
+
+    def resume_heartbeat(self) -> None:
+        """Re-register again after :meth:`pause_heartbeat` (the machine woke up)."""
+        self._hb_paused.clear()
 
     def _drain_to_backups(self) -> dict:
         """A leaving primary pushes its latest state to each key's next owner."""
@@ -834,7 +845,9 @@ class Scheduler(ReactorServer):
         self._worker_rate: dict = {}
         self._parked: dict = {}
         self._audits: dict = {}
-        self._manifest = None
+        self._manifest = None          # run manifest served to `opendipaco join`
+        self._recovery = None          # signed recovery manifest of the last cluster checkpoint
+        self._epoch_floor = 0          # epochs published after a restart number from here
 
     def _handle(self, msg: dict, nbytes: int, peer_id: str | None = None):
         kind = msg.get("type")
@@ -865,7 +878,7 @@ class Scheduler(ReactorServer):
         if self.identity is None:
             raise ValueError("publishing an epoch needs a scheduler identity")
         with self._lock:
-            num = 0 if self._epoch_record is None else self._epoch_record["epoch"] + 1
+            num = max(self._epoch_floor, 0 if self._epoch_record is None else self._epoch_record["epoch"] + 1)
             rec = make_epoch_record(self.identity, epoch=num, owner_records=owner_records, k=k, salt=salt,
                                     bootstrap=bool(bootstrap) if bootstrap is not None else num == 0)
             self._epoch_record = rec
@@ -1141,9 +1154,17 @@ class Scheduler(ReactorServer):
             self._resolve_audit(key)
 
     def fit(self, num_generations: int, *, total_generations=None, log_every=0, reclaim_interval=0.05,
-            checkpoint_dir=None, checkpoint_every=0, resume=False):
+            checkpoint_dir=None, checkpoint_every=0, resume=False, recovery_poll: float = 0.5):
+        """Serve until every path has had about ``num_generations`` more updates. With
+        ``resume`` the scheduler state of ``checkpoint_dir`` is restored and, when that
+        checkpoint has a signed recovery manifest, no task is served until some live
+        owner holds at least the manifest's version of every key (owners catch up by
+        replication meanwhile): tasks served earlier would train on state older than the
+        recovery point."""
         if resume and checkpoint_dir and os.path.exists(os.path.join(checkpoint_dir, "scheduler.pt")):
             self._load_state(checkpoint_dir)
+            while self._recovery is not None and not (self._stop or self._dead) and not self._recovery_ready():
+                time.sleep(recovery_poll)
         self.total_rounds = total_generations or self.total_rounds or num_generations
         paths = list(self.topology.paths())
         with self._lock:
@@ -1172,44 +1193,85 @@ class Scheduler(ReactorServer):
         return dict(self._completed)
 
     def _checkpoint_cluster(self, dirpath: str) -> None:
-        """``scheduler.pt`` + every owner's modules + a (signed) ``manifest.json``."""
+        """Cluster checkpoint: every owner persists its modules, the scheduler writes
+        ``scheduler.pt`` and, with an identity and an owner epoch, a signed recovery
+        manifest (``manifest.json``: per key the highest version an owner persisted),
+        the floor a restarted cluster must reach before it serves tasks again. File
+        names and contents are the reference's, so either framework resumes the other's
+        checkpoint."""
         os.makedirs(dirpath, exist_ok=True)
-        owners = ([_addr(o["addr"]) for o in self._epoch_record["owners"]] if self._epoch_record is not None
-                  else sorted(set(self._ps_addrs)))
-        versions = {}
+        with self._lock:
+            record = self._epoch_record
+        owners = ([_addr(o["addr"]) for o in record["owners"]] if record is not None else sorted(set(self._ps_addrs)))
+        held: dict = {}
         for a in owners:
             try:
-                s = connect(a, self.auth_key, timeout=5.0)
+                s = connect(a, self.auth_key, timeout=5.0, tls=self.ps_tls)
                 try:
                     reply = rpc(s, {"type": "checkpoint", "dir": dirpath})
                 finally:
                     s.close()
-                for k, v in (reply.get("versions") or {}).items():
-                    versions[k] = max(versions.get(k, (0, 0)), _version_pair(v))
             except (OSError, ConnectionError, PermissionError):
-                continue
+                continue  # an owner out of reach now is checkpointed next time
+            for k, v in (reply.get("versions") or {}).items():
+                held[k] = max(held.get(k, (0, 0)), _version_pair(v))
+        if record is not None and self.identity is not None and held:
+            manifest = sign_record(self.identity, {"kind": "manifest", "epoch": record["epoch"],
+                                                   "keys": {k: list(v) for k, v in held.items()},
+                                                   "issued_at": time.time()})
+            tmp = os.path.join(dirpath, "manifest.json.tmp")
+            with open(tmp, "w", encoding="utf-8") as f:
+                json.dump(manifest, f)
+            os.replace(tmp, os.path.join(dirpath, "manifest.json"))
+            with self._lock:
+                self._recovery = manifest
         with self._lock:
-            blob = {"T": self._T, "completed": dict(self._completed),
-                    "epoch": self._epoch_record, "reputation": self.reputation.snapshot()}
+            state = {"T": self._T, "completed": dict(self._completed),
+                     "epoch": -1 if record is None else int(record["epoch"]), "reputation": self.reputation.snapshot()}
         tmp = os.path.join(dirpath, "scheduler.pt.tmp")
-        torch.save(blob, tmp)
+        torch.save(state, tmp)
         os.replace(tmp, os.path.join(dirpath, "scheduler.pt"))
-        manifest = {"kind": "recovery_manifest", "T": blob["T"],
-                    "versions": {k: list(v) for k, v in versions.items()}, "issued_at": time.time()}
-        if self.identity is not None:
-            manifest = sign_record(self.identity, manifest)
-        with open(os.path.join(dirpath, "manifest.json.tmp"), "w") as f:
-            json.dump(manifest, f, indent=2, sort_keys=True)
-        os.replace(os.path.join(dirpath, "manifest.json.tmp"), os.path.join(dirpath, "manifest.json"))
 
     def _load_state(self, dirpath: str) -> None:
-        blob = torch.load(os.path.join(dirpath, "scheduler.pt"), weights_only=False)
+        state = torch.load(os.path.join(dirpath, "scheduler.pt"), weights_only=True)
         with self._lock:
-            self._T = blob["T"]
-            self._completed = dict(blob["completed"])
-            if blob.get("epoch"):
-                self._epoch_record = blob["epoch"]
-            self.reputation.restore(blob.get("reputation") or {})
+            self._T = state["T"]
+            self._completed = dict(state["completed"])
+            self._epoch_floor = max(self._epoch_floor, int(state.get("epoch", -1)) + 1)
+        self.reputation.restore(state.get("reputation") or {})
+        mpath = os.path.join(dirpath, "manifest.json")
+        if self.identity is not None and os.path.exists(mpath):
+            with open(mpath, encoding="utf-8") as f:
+                manifest = json.load(f)
+            # only this scheduler's own signature counts: a planted manifest could lower
+            # (or inflate) the recovery floor
+            if (verify_record(manifest) and manifest.get("kind") == "manifest"
+                    and str(manifest.get("pub", "")).lower() == self.identity.public_key_hex):
+                with self._lock:
+                    self._recovery = manifest
+
+    def _recovery_ready(self) -> bool:
+        """True when, among the current epoch's owners that answer, some owner holds at
+        least the recovery manifest's version of every key."""
+        with self._lock:
+            record, manifest = self._epoch_record, self._recovery
+        if manifest is None:
+            return True
+        if record is None:
+            return False  # the owner set is not known yet (the tracker watch publishes it)
+        held: dict = {}
+        for a in sorted({_addr(o["addr"]) for o in record["owners"]}):
+            try:
+                s = connect(a, self.auth_key, timeout=5.0, tls=self.ps_tls)
+                try:
+                    reply = rpc(s, {"type": "status"})
+                finally:
+                    s.close()
+            except (OSError, ConnectionError, PermissionError):
+                continue
+            for k, v in ((reply or {}).get("versions") or {}).items():
+                held[k] = max(held.get(k, (-1, -1)), _version_pair(v))
+        return all(held.get(k, (-1, -1)) >= _version_pair(v) for k, v in manifest["keys"].items())
 
     def shutdown(self) -> None:
         with self._lock:
