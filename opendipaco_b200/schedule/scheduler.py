@@ -261,22 +261,35 @@ class AsyncScheduler:
     # -- one task
     def _train_path(self, path: Path, shard: torch.Tensor, batch_size: int, generation: int,
                     inner_steps: int | None = None, probe=None) -> Contribution:
+        """Train one path task from the current global modules. On CUDA the task runs on
+        the fused B200 kernels (``train/worker_trainer.py``: one CUDA graph per task, no
+        host sync per step); otherwise, or when the shape is not supported, on PyTorch
+        modules with the reference's arithmetic. Both draw the same batches."""
         e = self.engine
         pidx = e.topology.path_index(path)
         if shard.size(0) == 0:
             return Contribution(path, pidx, float("nan"), {}, {}, {}, empty=True)
+        steps = inner_steps or e.diloco.inner_steps
+        gen = torch.Generator().manual_seed(task_seed(self.seed, pidx, generation))
+        from ..train.worker_trainer import path_trainer_for
+
+        trainer = path_trainer_for(e) if e.device.type == "cuda" else None
+        if trainer is not None:
+            screening = probe is not None and not probe.empty
+            before = (safe_probe_loss(probe, build_path_model(e.config, path, e.bank, deepcopy=True).to(e.device))
+                      if screening else None)
+            loss, shared, private, opt_state = trainer.train(path, shard, batch_size, gen, steps, generation * steps)
+            after = safe_probe_loss(probe, trainer.model_view(path)) if screening else None
+            return Contribution(path, pidx, loss, shared, private, opt_state, probe_before=before, probe_after=after)
         shard = shard.to(e.device)
         model = build_path_model(e.config, path, e.bank, deepcopy=True,
                                  dedup_private=getattr(e.diloco, "dedup_private", False)).to(e.device)
         opt = make_inner_optimizer(model, e.diloco)
         if e._opt_state.get(path) is not None:
             opt.load_state_dict(e._opt_state[path])
-        steps = inner_steps or e.diloco.inner_steps
         screening = probe is not None and not probe.empty
         before = safe_probe_loss(probe, model) if screening else None
-        loss = run_inner_steps(model, opt, shard, batch_size, torch.Generator().manual_seed(task_seed(self.seed, pidx,
-                                                                                                      generation)),
-                               inner_steps=steps, total_steps=e.total_rounds * steps if e.total_rounds else None,
+        loss = run_inner_steps(model, opt, shard, batch_size, gen, inner_steps=steps, total_steps=e.total_rounds * steps if e.total_rounds else None,
                                base_step=generation * steps, diloco=e.diloco, device=e.device)
         after = safe_probe_loss(probe, model) if screening else None
         shared, private = {}, {}

@@ -207,7 +207,7 @@ class FusedExecutor:
             self.dp_tab = be.dp_table(self.W32, self.W16, self.GRAD, self.MOM1, self.MOM2, G, opt8)
             self.dp_counter = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.pms = dict(zip(self.paths, pms))
-        if engine.materialize == "eager":
+        if engine.materialize == "eager" and hasattr(engine, "_eager_views"):
             engine._eager_views.update(self.pms)
         self.steps_taken = [0] * G
         self._inner_opts: dict[Path, torch.optim.Optimizer] = {}
@@ -215,12 +215,15 @@ class FusedExecutor:
         # -- global bank as flat buffers -------------------------------------------
         self.glob: dict[str, torch.Tensor] = {}
         self.mom: dict[str, torch.Tensor] = {}
+        # solo: a one-path task trainer (worker) -- the engine's bank is only read, never
+        # rebound, and there is no outer step
+        self.solo = bool(getattr(engine, "solo", False))
         arena = None
-        if hasattr(engine.backend, "bank_arena"):
+        if hasattr(engine.backend, "bank_arena") and not self.solo:
             # cross-GPU backends place the bank in peer-addressable (symmetric) memory
             sizes = {k: self._region_size(k) for k in self.topo.module_keys()}
             arena = engine.backend.bank_arena(sizes, self.dev)
-        for key, mod in engine.bank.items():
+        for key, mod in ({} if self.solo else engine.bank).items():
             n = self._region_size(key)
             buf = arena[0][key] if arena else torch.zeros(n, device=self.dev, dtype=torch.float32)
             self._rebind_bank(key, mod, buf)
@@ -234,7 +237,8 @@ class FusedExecutor:
         # the last inner step's AdamW also accumulates the outer pseudo-gradient of every
         # module key (plain AdamW, one GPU per path group); the outer step then reads one
         # partial per key instead of every working copy again
-        self.acc_fused = (not self.opt8 and self.dp == 1 and os.environ.get("ODP_ACC_FUSED", "1") != "0")
+        self.acc_fused = (not self.opt8 and self.dp == 1 and not self.solo
+                          and os.environ.get("ODP_ACC_FUSED", "1") != "0")
         self._deltas: dict[str, torch.Tensor] = {}
         self._acc_w: dict[tuple[str, int], float] = {}
         self.ACC_REG = self.ACC_ENT = None
@@ -636,14 +640,19 @@ class FusedExecutor:
 
     # ------------------------------------------------------------------ round inputs
     def _prepare(self, corpus, batch_size: int, round_idx: int, slot: int = 0):
+        """Sample a round of every owned path's batches (path by path from the engine's
+        generator, like the module executor) into host slot ``slot``."""
+        steps = self.e.diloco.inner_steps
+        shards = [corpus.shard(self.topo.path_index(p)) for p in self.paths]
+        return self._prepare_rows(shards, corpus.seq_len, batch_size, [self.e._gen] * self.G,
+                                  [round_idx * steps] * self.G, steps, slot)
+
+    def _prepare_rows(self, shards, S: int, batch_size: int, gens, base_steps, steps: int, slot: int = 0):
+        """Batches of ``steps`` inner steps for path g from ``shards[g]`` with generator
+        ``gens[g]`` (drawn in path order), learning rates from global step
+        ``base_steps[g]``; returns the paths' active flags."""
         e = self.e
-        steps = e.diloco.inner_steps
-        S = corpus.seq_len
-        shards, active = [], []
-        for path in self.paths:
-            sh = corpus.shard(self.topo.path_index(path))
-            shards.append(sh)
-            active.append(sh.size(0) > 0)
+        active = [sh.size(0) > 0 for sh in shards]
         if batch_size % self.dp:
             raise ValueError(f"batch_size {batch_size} must be divisible by the data-parallel degree {self.dp}")
         B = batch_size // self.dp  # sequences of each step's batch trained on this GPU
@@ -668,7 +677,7 @@ class FusedExecutor:
                 lab[:, g].fill_(-100)
                 continue
             # every step of a round samples the same number of rows: gather the round at once
-            idx = torch.stack(batch_indices(sh.size(0), batch_size, steps, e._gen))  # [steps, rows]
+            idx = torch.stack(batch_indices(sh.size(0), batch_size, steps, gens[g]))  # [steps, rows]
             # the whole batch is sampled (same generator calls on every member), this GPU
             # trains rows [j0, j0 + B); the loss is normalised by the whole batch
             invc[:, g] = 1.0 / max(1, idx.size(1) * (S - 1))
@@ -683,7 +692,7 @@ class FusedExecutor:
             rows = []
             for i in range(steps):
                 t = self.steps_taken[g] + i + 1
-                lr = inner_lr_at(round_idx * steps + i, total, dl)
+                lr = inner_lr_at(base_steps[g] + i, total, dl)
                 # active flag 2.0 marks a path's very first optimizer step (8-bit Adam
                 # then treats the second moment as zero, like the reference)
                 rows.append([lr, lr / (1 - b1 ** t), math.sqrt(1 - b2 ** t), 2.0 if t == 1 else 1.0])
