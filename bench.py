@@ -22,6 +22,15 @@ each round's token batches on the host, copies them from pinned host memory and 
 the losses back every round. The per-round working set (weights, grads
 and optimizer state: ~570 MB per path) is far larger than the 126 MB L2.
 
+``--config`` picks the workload: ``c2`` (default) is the config above; ``c3`` is a 6x6
+DiPaCo (36 paths, hidden 512, sequence 256, batch 32, 40 inner steps) whose documents
+go to their two nearest paths; ``c4`` a 3-level [2,2,2] DiPaCo (hidden 1024, 12 layers,
+sequence 512) with private embedding / head, 8-bit Adam and top-1% sparse outer payloads;
+``c5`` a 1B Llama shape (hidden 2048, 32 / 8 heads, FFN 8192, 16 layers, vocab 128256,
+sequence 1024) on 16 paths with every path on 2 GPUs (8 GPUs). Where the reference
+cannot run a preset (intra-path data parallelism, paths not divisible by the GPUs) its
+arm prints an ``unavailable`` line.
+
 ``--impl reference`` runs the unmodified reference package installed in
 ``baseline/_ref`` (its own DiPaCoEngine, LocalBackend / TorchDistBackend over NCCL,
 bf16 autocast) on the same documents and shards.
@@ -50,9 +59,31 @@ sys.path.insert(0, ROOT)
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
-CFG = dict(levels=[4, 4], hidden=384, heads=6, ffn=1024, layers=[2, 2], vocab=32000, seq=128, batch=24,
-           inner_steps=20, outer_lr=0.7, outer_momentum=0.9, docs=20000, min_len=128, max_len=2048,
-           zipf=1.1)
+# Workloads: the headline 16-path config (c2, the default) and the other DiPaCo configs of
+# the north-star metric. Sizes the configs leave open (FFN width, document counts,
+# batch of c5) are fixed here and reported in the output's "config".
+PRESETS = {
+    "c2": dict(levels=[4, 4], hidden=384, heads=6, kv_heads=None, ffn=1024, layers=[2, 2], vocab=32000, seq=128,
+               batch=24, inner_steps=20, outer_lr=0.7, outer_momentum=0.9, docs=20000, min_len=128, max_len=2048,
+               zipf=1.1, private=False, optim_8bit=False, topk_routes=1, compress=None, dp=1,
+               model="DiPaCo 4x4 (16 paths) Llama hidden 384, 6 heads, ffn 1024, layers [2,2], vocab 32000"),
+    "c3": dict(levels=[6, 6], hidden=512, heads=8, kv_heads=None, ffn=1536, layers=[2, 2], vocab=32000, seq=256,
+               batch=32, inner_steps=40, outer_lr=0.7, outer_momentum=0.9, docs=20000, min_len=256, max_len=2048,
+               zipf=1.1, private=False, optim_8bit=False, topk_routes=2, compress=None, dp=1,
+               model="DiPaCo 6x6 (36 paths) Llama hidden 512, 8 heads, ffn 1536, layers [2,2], vocab 32000, "
+                     "documents routed to their 2 nearest paths"),
+    "c4": dict(levels=[2, 2, 2], hidden=1024, heads=16, kv_heads=None, ffn=2816, layers=[4, 4, 4], vocab=32000,
+               seq=512, batch=16, inner_steps=20, outer_lr=0.7, outer_momentum=0.9, docs=8000, min_len=512,
+               max_len=2048, zipf=1.1, private=True, optim_8bit=True, topk_routes=1, compress="topk", dp=1,
+               model="DiPaCo [2,2,2] (8 paths) Llama hidden 1024, 16 heads, ffn 2816, layers [4,4,4], vocab 32000, "
+                     "private embed/head, 8-bit Adam, top-1% sparse outer payloads on NVLink"),
+    "c5": dict(levels=[4, 4], hidden=2048, heads=32, kv_heads=8, ffn=8192, layers=[8, 8], vocab=128256, seq=1024,
+               batch=8, inner_steps=20, outer_lr=0.7, outer_momentum=0.9, docs=8000, min_len=1024, max_len=4096,
+               zipf=1.1, private=False, optim_8bit=False, topk_routes=1, compress=None, dp=2,
+               model="DiPaCo 4x4 (16 paths) 1B Llama shape hidden 2048, 32 heads / 8 kv, ffn 8192, "
+                     "16 layers [8,8], vocab 128256, every path over 2 GPUs"),
+}
+CFG = dict(PRESETS["c2"])
 BASELINE_VALUE = None  # the reference publishes no throughput number
 PEER_GBPS = 770.0      # measured peer-copy bandwidth per direction per GPU on this hardware (GB/s)
 
@@ -119,6 +150,13 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def _npaths() -> int:
+    n = 1
+    for k in CFG["levels"]:
+        n *= k
+    return n
+
+
 def build_documents_and_assignments(with_router: bool = False):
     """Zipf documents + k-means path assignments (identical on every rank / both arms)."""
     from opendipaco_b200.data import zipf_documents
@@ -128,11 +166,18 @@ def build_documents_and_assignments(with_router: bool = False):
     docs = zipf_documents(vocab_size=CFG["vocab"], num_documents=CFG["docs"], min_len=CFG["min_len"],
                           max_len=CFG["max_len"], exponent=CFG["zipf"], topics=16, seed=0)
     feat = BagOfTokensFeaturizer(CFG["vocab"], feature_dim=256, seed=0)
-    npaths = CFG["levels"][0] * CFG["levels"][1]
+    npaths = _npaths()
     router = KMeansRouter(npaths, seed=0).fit(feat([d[:32] for d in docs]))
+    if CFG["topk_routes"] > 1:
+        # overlapping shards: every document goes to each of its k nearest paths
+        near = router.predict_topk(feat([d[:32] for d in docs]), CFG["topk_routes"])
+        docs = [d for d, row in zip(docs, near) for _ in row]
+        assign = near.reshape(-1)
+    else:
+        assign = assign_paths(docs, router, feat)
     if with_router:
-        return docs, assign_paths(docs, router, feat), router, feat
-    return docs, assign_paths(docs, router, feat)
+        return docs, assign, router, feat
+    return docs, assign
 
 
 def run_quality(args) -> dict:
@@ -142,7 +187,7 @@ def run_quality(args) -> dict:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     docs, assign = build_documents_and_assignments()
-    npaths = CFG["levels"][0] * CFG["levels"][1]
+    npaths = _npaths()
     held = zipf_documents(vocab_size=CFG["vocab"], num_documents=512, min_len=256, max_len=1024,
                           exponent=CFG["zipf"], topics=16, seed=1)
     seqs = torch.stack([d[:256] for d in held])
@@ -172,8 +217,8 @@ def run_quality(args) -> dict:
     out = {"metric": "held-out routed perplexity", "value": round(float(ppl), 4), "unit": "ppl",
            "higher_is_better": False, "rounds": args.quality, "final_inner_loss": round(hist[-1].inner_loss, 4),
            "dtype": "bf16", "data": "synthetic Zipf(1.1), 512 held-out docs x 256 tokens, seed 1",
-           "config": {"model": "DiPaCo 4x4 (16 paths) Llama hidden 384, 6 heads, ffn 1024, layers [2,2], "
-                               "vocab 32000", "global_batch": 24 * npaths, "seq_len": CFG["seq"]}}
+           "config": {"model": CFG["model"], "preset": args.config, "global_batch": CFG["batch"] * npaths,
+                      "seq_len": CFG["seq"]}}
     if args.impl == "reference":
         out["impl"] = "reference"
     return out
@@ -181,11 +226,14 @@ def run_quality(args) -> dict:
 
 def make_configs(pkg):
     bb = pkg.BackboneConfig(vocab_size=CFG["vocab"], hidden_size=CFG["hidden"],
-                            num_attention_heads=CFG["heads"], intermediate_size=CFG["ffn"],
-                            layers_per_level=list(CFG["layers"]), max_position_embeddings=2048)
-    cfg = pkg.DiPaCoConfig(backbone=bb, level_sizes=list(CFG["levels"]), sequence_length=CFG["seq"])
+                            num_attention_heads=CFG["heads"], num_key_value_heads=CFG["kv_heads"],
+                            intermediate_size=CFG["ffn"], layers_per_level=list(CFG["layers"]),
+                            max_position_embeddings=max(2048, CFG["seq"]))
+    priv = "private" if CFG["private"] else "shared"
+    cfg = pkg.DiPaCoConfig(backbone=bb, level_sizes=list(CFG["levels"]), sequence_length=CFG["seq"],
+                           embedding=priv, head=priv)
     dl = pkg.DiLoCoConfig(inner_steps=CFG["inner_steps"], outer_lr=CFG["outer_lr"],
-                          outer_momentum=CFG["outer_momentum"], inner_autocast=True)
+                          outer_momentum=CFG["outer_momentum"], inner_autocast=True, optim_8bit=CFG["optim_8bit"])
     return cfg, dl
 
 
@@ -234,8 +282,16 @@ def run(args) -> dict:
         from datetime import timedelta
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    npaths = _npaths()
+    if args.impl == "reference":
+        why = None
+        if CFG["dp"] > 1:
+            why = "the reference has no intra-path data parallelism (a path on 2 GPUs)"
+        elif npaths % world:
+            why = f"the reference's TorchDistBackend needs num_paths % world == 0 ({npaths} paths, {world} GPUs)"
+        if why is not None:
+            return {"impl": "reference", "unavailable": why} if rank == 0 else {}
     docs, assign = build_documents_and_assignments()
-    npaths = CFG["levels"][0] * CFG["levels"][1]
 
     if args.impl == "reference":
         ref_dir = os.path.join(ROOT, "baseline", "_ref")
@@ -256,7 +312,14 @@ def run(args) -> dict:
     cfg, dl = make_configs(pkg)
     corpus = ShardedCorpus.from_assignments(docs, assign, npaths, CFG["seq"])
     topo = cfg.build_topology()
-    backend = backend_cls(topo) if world == 1 else backend_cls(topo, device=dev)
+    if world == 1:
+        if CFG["dp"] > 1:
+            raise SystemExit(f"--config {args.config} puts every path on {CFG['dp']} GPUs: run it on several")
+        backend = backend_cls(topo)
+    elif args.impl == "reference":
+        backend = backend_cls(topo, device=dev)
+    else:
+        backend = backend_cls(topo, device=dev, dp=CFG["dp"], compress=CFG["compress"], density=0.01)
     engine = pkg.DiPaCoEngine(cfg, dl, backend, device=dev, seed=0)
     engine.total_rounds = args.warmup + 2 * args.steps + 1
     B = CFG["batch"]
@@ -389,11 +452,11 @@ def run(args) -> dict:
         "ms_per_step": round(ms_per_round, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
         "dtype": "bf16", "data": "synthetic (Zipf(1.1) token ids, 20k docs, len U[128,2048]); random init",
-        "config": {"model": "DiPaCo 4x4 (16 paths) Llama hidden 384, 6 heads, ffn 1024, layers [2,2], "
-                            "vocab 32000", "global_batch": 24 * npaths, "seq_len": CFG["seq"],
-                   "parallelism": f"paths{world}", "paths_per_gpu": len(owned),
+        "config": {"model": CFG["model"], "preset": args.config, "global_batch": B * npaths, "seq_len": CFG["seq"],
+                   "parallelism": f"paths{world}" + (f"_dp{CFG['dp']}" if CFG["dp"] > 1 else ""),
+                   "paths_per_gpu": len(owned),
                    "inner_steps_per_step": CFG["inner_steps"],
-                   "l2": "per-round working set > L2 (weights+grads+optimizer ~570 MB/path)"},
+                   "l2": "per-round working set (weights, gradients, optimizer state of every path) > L2"},
         "clocks": clocks.summary(),
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(wall_ms / args.steps, 3)},
@@ -425,11 +488,15 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(PRESETS), default="c2",
+                    help="workload: c2 (default, the headline 16-path config), c3, c4 or c5")
     ap.add_argument("--quality", type=int, default=0, metavar="ROUNDS",
                     help="train ROUNDS rounds on one GPU and print the held-out routed perplexity")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    CFG.clear()
+    CFG.update(PRESETS[args.config])
     out = run_quality(args) if args.quality else run(args)
     if out:
         print(json.dumps(out), flush=True)
