@@ -105,7 +105,9 @@ void dequant_int4(torch::Tensor packed, torch::Tensor scale, int64_t n, int64_t 
 std::vector<torch::Tensor> quant_int8(torch::Tensor x, bool want_resid);
 torch::Tensor robust_combine(torch::Tensor stack, int64_t mode);
 torch::Tensor bag_of_tokens(torch::Tensor ids, torch::Tensor offs, torch::Tensor proj);
-std::vector<torch::Tensor> kmeans_assign(torch::Tensor x, torch::Tensor c, int64_t topk, bool want_dist);
+std::vector<torch::Tensor> kmeans_assign(torch::Tensor x, torch::Tensor c, int64_t topk, bool want_min,
+                                         bool want_dist, torch::Tensor err);
+std::vector<torch::Tensor> kmeans_cluster_sums(torch::Tensor x, torch::Tensor assign, int64_t K);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opendipaco_b200 sm_100a kernels";
@@ -153,4 +155,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("robust_combine", &robust_combine);
   m.def("bag_of_tokens", &bag_of_tokens);
   m.def("kmeans_assign", &kmeans_assign);
+  m.def("kmeans_cluster_sums", &kmeans_cluster_sums);
 }

@@ -5,8 +5,11 @@ per document; non-candidates stay ``+inf``) and reassign each document to its
 lowest-loss path (or top-k for overlapping shards). ``fit_discriminative_router``
 labels held-out documents by their best path and trains the test-time router.
 
-On CUDA, each candidate path's documents are scored with the sm_100a forward and
-the fused per-row log-softmax kernel (no fp32 [tokens, vocab] copy).
+On CUDA the candidates are scored side by side: ``GroupedScorer`` runs one grouped
+forward for up to 16 candidate paths over each batch of documents (the training
+step's grouped tcgen05 kernels, LM head in row chunks, per-row CE kernel), so a batch
+costs one set of launches instead of one per path. Shapes the fused kernels do not
+take fall back to the module forward path by path.
 """
 
 from __future__ import annotations
@@ -42,6 +45,10 @@ def path_losses(documents: list[torch.Tensor], config: DiPaCoConfig, bank: dict[
     dev = next(next(iter(bank.values())).parameters()).device
     docs = [d[:seq_len] for d in documents]
     out = torch.full((len(docs), topo.num_paths), float("inf"))
+    from .train.scorer import GroupedScorer
+
+    if docs and candidates and GroupedScorer.supported(config, dev):
+        return _grouped_path_losses(docs, config, bank, candidates, batch_size, pad_id, dev, out)
     for p in candidates:
         model = compose_path(config, bank, topo.path_from_index(p)).eval()
         for i in range(0, len(docs), batch_size):
@@ -50,6 +57,32 @@ def path_losses(documents: list[torch.Tensor], config: DiPaCoConfig, bank: dict[
             ce = _token_ce(logits[:, :-1, :], ids[:, 1:]).float()
             m = mask[:, 1:].float()
             out[i:i + ids.size(0), p] = ((ce * m).sum(1) / m.sum(1).clamp(min=1.0)).cpu()
+    return out
+
+
+def _grouped_path_losses(docs, config, bank, candidates, batch_size, pad_id, dev, out):
+    from .train.scorer import GroupedScorer, group_count, padded_len, shifted_targets
+
+    topo = config.build_topology()
+    G = group_count(config, bank, min(16, len(candidates)))
+    S = padded_len(max(max(int(d.numel()) for d in docs), 2))
+    B = min(batch_size, len(docs))
+    sc = GroupedScorer(config, bank, dev, G, B, S)
+    for c0 in range(0, len(candidates), G):
+        cands = candidates[c0:c0 + G]
+        for g in range(G):  # a short last wave repeats its first path in the spare groups
+            sc.load(g, topo.path_from_index(cands[g] if g < len(cands) else cands[0]))
+        for i in range(0, len(docs), B):
+            part = docs[i:i + B]
+            ids, mask = _pad_batch(part + [part[0][:0]] * (B - len(part)), pad_id, dev)
+            ids = torch.nn.functional.pad(ids, (0, S - ids.size(1)), value=pad_id)
+            mask = torch.nn.functional.pad(mask, (0, S - mask.size(1)), value=False)
+            tgt = shifted_targets(ids, mask)
+            ce = sc.token_losses(ids.expand(G, B, S), tgt.expand(G, B, S))
+            m = mask[:, 1:].float().sum(1).clamp(min=1.0)
+            loss = (ce.sum(2) / m).cpu()
+            for g, p in enumerate(cands):
+                out[i:i + len(part), p] = loss[g, :len(part)]
     return out
 
 

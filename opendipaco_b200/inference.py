@@ -9,9 +9,11 @@
   window and score each window under its path with the full preceding context
   recomputed (no KV cache), the reference's definition.
 
-On CUDA the per-path batches run through the sm_100a forward kernels, and the
-scored CE sum uses the fused log-softmax kernel in "sum" mode (no [tokens, vocab]
-fp32 logits copy).
+On CUDA ``routed_perplexity`` scores the routed sequences of up to 16 paths side by
+side (``GroupedScorer``: one grouped forward with the training step's tcgen05 kernels,
+LM head in row chunks, per-row CE kernel); otherwise, and for a custom ``compose_fn``,
+each path's batches run through its module forward and the per-row CE kernel (no
+[tokens, vocab] fp32 logits copy).
 """
 
 from __future__ import annotations
@@ -67,6 +69,12 @@ def routed_perplexity(config: DiPaCoConfig, bank: dict[str, nn.Module], sequence
                       batch_size: int = 8, compose_fn=None) -> float:
     paths = route([s[:prefix_len] for s in sequences], router, featurizer)
     start = max(prefix_len, 1)
+    if compose_fn is None and sequences.numel() and sequences.size(1) > start:
+        from .train.scorer import GroupedScorer
+
+        dev = next(next(iter(bank.values())).parameters()).device
+        if GroupedScorer.supported(config, dev):
+            return _grouped_routed_perplexity(config, bank, sequences, paths, start, batch_size, dev)
     total, count = 0.0, 0
     for pidx in paths.unique().tolist():
         path = config_path(config, pidx)
@@ -81,6 +89,40 @@ def routed_perplexity(config: DiPaCoConfig, bank: dict[str, nn.Module], sequence
             total += _ce_sum(logits[:, start - 1:-1, :], batch[:, start:])
             count += batch[:, start:].numel()
     return float("nan") if count == 0 else float(torch.exp(torch.tensor(total / count)))
+
+
+def _grouped_routed_perplexity(config, bank, sequences, paths, start, batch_size, dev) -> float:
+    """Token-level routed perplexity with the paths' batches scored side by side: a wave
+    takes the next batch of up to ``batch_size`` sequences of up to G paths."""
+    from .train.scorer import GroupedScorer, group_count, padded_len, shifted_targets
+
+    tasks = []
+    for pidx in paths.unique().tolist():
+        rows = (paths == pidx).nonzero(as_tuple=True)[0]
+        tasks += [(pidx, rows[i:i + batch_size]) for i in range(0, rows.numel(), batch_size)]
+    n, slen = sequences.shape
+    G = group_count(config, bank, min(16, len(tasks)))
+    B = min(batch_size, n)
+    S = padded_len(slen)
+    sc = GroupedScorer(config, bank, dev, G, B, S)
+    topo = config.build_topology()
+    total = torch.zeros((), dtype=torch.float64)
+    count = 0
+    for w0 in range(0, len(tasks), G):
+        wave = tasks[w0:w0 + G]
+        ids = torch.zeros(G, B, S, dtype=torch.long)
+        valid = torch.zeros(G, B, S, dtype=torch.bool)
+        for g in range(G):
+            pidx, rows = wave[g] if g < len(wave) else wave[0]
+            sc.load(g, topo.path_from_index(pidx))
+            if g < len(wave):
+                ids[g, :rows.numel(), :slen] = sequences[rows]
+                valid[g, :rows.numel(), :slen] = True
+                count += rows.numel() * (slen - start)
+        ids, valid = ids.to(dev), valid.to(dev)
+        tgt = shifted_targets(ids.view(G * B, S), valid.view(G * B, S), first=start).view(G, B, S)
+        total += sc.token_losses(ids, tgt).double().sum().cpu()
+    return float("nan") if count == 0 else float(torch.exp(total / count))
 
 
 @torch.no_grad()

@@ -5,9 +5,12 @@ points with a seeded generator; loop: distances -> argmin -> per-cluster mean (a
 empty cluster is re-seeded to the point farthest from its nearest centroid) ->
 stop when the centroid shift norm < ``tol``.
 
-On CUDA features the assignment step (``|x|^2 - 2 x.c + |c|^2``, argmin / top-k)
-runs in one sm_100a kernel and the centroid update is a deterministic ordered
-segmented mean (no float atomics), so the fit is reproducible run to run.
+On CUDA features every iteration runs on the device with no per-cluster host loop:
+the assignment (``|x|^2 - 2 x.c + |c|^2`` with x.c on the tensor cores, argmin / top-k
+fused into the epilogue) is one kernel, the per-cluster sums another (ordered, no float
+atomics, so the fit is reproducible run to run), and the mean, the re-seeding of empty
+clusters and the shift are a few tensor ops. The only host sync per iteration is the
+convergence test, as in the reference.
 """
 
 from __future__ import annotations
@@ -23,14 +26,6 @@ class KMeansRouter:
         self.tol = tol
         self.centroids: torch.Tensor | None = None
 
-    @staticmethod
-    def _dists(x: torch.Tensor, c: torch.Tensor) -> torch.Tensor:
-        if x.is_cuda:
-            from ..ops import routing as K
-
-            return K.sq_dists(x, c).clamp_min_(0).sqrt_()
-        return torch.cdist(x, c)
-
     def fit(self, features: torch.Tensor) -> "KMeansRouter":
         n = features.size(0)
         if n < self.num_paths:
@@ -38,8 +33,11 @@ class KMeansRouter:
         gen = torch.Generator(device=features.device).manual_seed(self.seed)
         idx = torch.randperm(n, generator=gen, device=features.device)[: self.num_paths]
         cent = features[idx].clone()
+        if features.is_cuda:
+            self.centroids = self._fit_device(features.float().contiguous(), cent.float())
+            return self
         for _ in range(self.max_iters):
-            d = self._dists(features, cent)
+            d = torch.cdist(features, cent)
             assign = d.argmin(dim=1)
             new = cent.clone()
             for k in range(self.num_paths):
@@ -54,6 +52,22 @@ class KMeansRouter:
                 break
         self.centroids = cent
         return self
+
+    def _fit_device(self, x: torch.Tensor, cent: torch.Tensor) -> torch.Tensor:
+        from ..ops import routing as K
+
+        for _ in range(self.max_iters):
+            idx, mind, _ = K.assign(x, cent, 1, want_min=True)
+            sums, counts = K.cluster_sums(x, idx, self.num_paths)
+            mean = sums / counts.clamp_min(1).unsqueeze(1).float()
+            # an empty cluster takes the point farthest from its nearest centroid
+            far = x[mind.argmax()]
+            new = torch.where((counts == 0).unsqueeze(1), far.unsqueeze(0), mean)
+            shift = (new - cent).norm()
+            cent = new
+            if shift < self.tol:
+                break
+        return cent
 
     def predict(self, features: torch.Tensor) -> torch.Tensor:
         if self.centroids is None:
