@@ -8,12 +8,14 @@ each kernel. Shapes are chosen so that each kernel's working set is larger than 
 MB L2 (its DRAM figures mean something) but the whole process stays within a few GB:
 
 * adamw:     region AdamW (+ pseudo-gradient) over 2 paths of the 16-path layout (~1.1 GB)
+* adam8bit:  blockwise 8-bit Adam over the same 2 x 31.7 M elements
 * outer:     the one-GPU outer step (APPLY + write-back) over 2 x 12.3 M elements
 * norm:      RMSNorm forward / backward, 2 x 3072 rows of 384
 * embedding: the sorted deterministic embedding backward, 2 x 3072 tokens, vocab 32000
 * attention: tcgen05 flash forward / backward, 4 x 1024 tokens, 32 / 8 heads
 * ce:        one-pass cross-entropy, 2 x 3072 rows of 32000
-* routing:   bag-of-tokens featurizer and k-means assignment, 20000 documents
+* routing:   bag-of-tokens featurizer, tensor-core k-means assignment and the ordered
+             centroid sums, 20000 documents x 256 features, 16 centroids
 * codec:     int4 quantisation with error feedback, 32 M elements
 """
 
@@ -38,6 +40,23 @@ def case_adamw() -> None:
 
     flush = torch.empty(1, device="cuda")
     bench_optim(2, 384, 32000, 1024, [2, 2], [4, 4], 1, flush)
+
+
+def case_adam8bit() -> None:
+    from ..ops._ext import ext
+
+    G, P = 2, 31_658_496
+    nb = P // 256
+    w = torch.randn(G * P, device="cuda") * 0.02
+    g = torch.randn(G * P, device="cuda") * 1e-3
+    w16 = torch.empty(G * P, device="cuda", dtype=torch.bfloat16)
+    mq = torch.zeros(G * nb, 256, device="cuda", dtype=torch.int8)
+    vq = torch.zeros(G * nb, 256, device="cuda", dtype=torch.uint8)
+    mabs, vlo, vsc = (torch.zeros(G * nb, device="cuda") for _ in range(3))
+    coef = torch.ones(G, device="cuda")
+    sched = torch.tensor([[1e-3, 1e-2, 0.2236, 1.0]] * G, device="cuda")  # lr, lr / bc1, sqrt(bc2), active
+    _thrice(lambda: ext().adam8bit_step(w, g, mq, mabs, vq, vlo, vsc, coef, sched, 0.9, 0.95, 1e-8, 0.1, False, w16,
+                                        nb))
 
 
 def case_outer() -> None:
@@ -124,6 +143,8 @@ def case_routing() -> None:
     c = torch.randn(K_, D, device="cuda")
     _thrice(lambda: K.bag_of_tokens(docs, proj, V))
     _thrice(lambda: K.kmeans_assign(x, c, 2))
+    idx = K.kmeans_assign(x, c, 1)
+    _thrice(lambda: K.cluster_sums(x, idx, K_))
 
 
 def case_codec() -> None:
@@ -133,7 +154,7 @@ def case_codec() -> None:
     _thrice(lambda: codec.quant_int4(x))
 
 
-CASES = {"adamw": case_adamw, "outer": case_outer, "norm": case_norm, "embedding": case_embedding,
+CASES = {"adamw": case_adamw, "adam8bit": case_adam8bit, "outer": case_outer, "norm": case_norm, "embedding": case_embedding,
          "attention": case_attention, "ce": case_ce, "routing": case_routing, "codec": case_codec}
 
 
