@@ -56,6 +56,8 @@ constexpr int kSqElemsPerBlock = 1 << 16;
 
 __global__ void sumsq_kernel(const float* __restrict__ g, long long P, long long sg, int nblk, float* __restrict__ part,
                              RowSkip skip) {
+  pdl_wait();
+  pdl_trigger();
   const int grp = blockIdx.y, b = blockIdx.x;
   const float* base = g + grp * sg;
   const long long e0 = (long long)b * kSqElemsPerBlock;
@@ -83,6 +85,8 @@ __global__ void sumsq_kernel(const float* __restrict__ g, long long P, long long
 
 __global__ void clip_coef_kernel(const float* __restrict__ part, int nblk, float max_norm, float* __restrict__ coef,
                                  float* __restrict__ norm_out) {
+  pdl_wait();
+  pdl_trigger();
   const int grp = blockIdx.x;
   __shared__ float red[256];
   float s = 0.f;
@@ -109,6 +113,8 @@ __global__ void clip_coef_parts_kernel(const float* __restrict__ parts, long lon
                                        int M, const float* __restrict__ grads, long long P,
                                        const long long* __restrict__ norm_offs, int n_norm, int H, float max_norm,
                                        float* __restrict__ coef, float* __restrict__ norm_out) {
+  pdl_wait();
+  pdl_trigger();
   const int g = blockIdx.x;
   float s = 0.f;
   for (long long i = threadIdx.x; i < nslot; i += blockDim.x) s += parts[g * nslot + i];
@@ -151,6 +157,8 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ p16, long long P, long long sp,
                              long long s16, const float* __restrict__ coef, const float* __restrict__ sched, float b1,
                              float b2, float eps, float wd, RowSkip skip) {
+  pdl_wait();
+  pdl_trigger();
   const int grp = blockIdx.y;
   const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (i >= P) return;
@@ -235,6 +243,8 @@ __global__ void __launch_bounds__(256) adamw_acc_kernel(
     __nv_bfloat16* __restrict__ p16, long long sp, long long s16, const float* __restrict__ coef,
     const float* __restrict__ sched, float b1, float b2, float eps, float wd, RowSkip skip,
     const AccRegion* __restrict__ regs, int nregs, const AccEntry* __restrict__ ents, int accumulate) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ AccRegion sR;
   __shared__ AccEntry sE[kAccMaxEntries];
   __shared__ float4 sS[kAccMaxEntries];  // lr, lr / bc1, sqrt(bc2), active of the entry's path
@@ -323,6 +333,8 @@ __global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__
                                 const float* __restrict__ coef,
                                 const float* __restrict__ sched, float b1, float b2, float eps, float wd, int first,
                                 __nv_bfloat16* __restrict__ p16) {
+  pdl_wait();
+  pdl_trigger();
   const long long blk = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (blk >= nblocks) return;
@@ -404,12 +416,12 @@ void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, doubl
   auto st = at::cuda::getCurrentCUDAStream();
   const int nblk = (int)((P + odp::kSqElemsPerBlock - 1) / odp::kSqElemsPerBlock);
   TORCH_CHECK(work.numel() >= G * nblk, "grad_clip_coef: work buffer too small");
-  odp::sumsq_kernel<<<dim3(nblk, (unsigned)G), odp::kSqBlock, 0, st>>>(grads.data_ptr<float>(), P, sg, nblk,
-                                                                      work.data_ptr<float>(), row_skip(rows, r0, H, V));
+  C10_CUDA_CHECK(odp::launch_pdl((odp::sumsq_kernel), dim3(dim3(nblk, (unsigned)G)), dim3(odp::kSqBlock), 0, st, grads.data_ptr<float>(), P, sg, nblk,
+                                                                      work.data_ptr<float>(), row_skip(rows, r0, H, V)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  odp::clip_coef_kernel<<<(unsigned)G, 256, 0, st>>>(work.data_ptr<float>(), nblk, (float)max_norm,
+  C10_CUDA_CHECK(odp::launch_pdl((odp::clip_coef_kernel), dim3((unsigned)G), dim3(256), 0, st, work.data_ptr<float>(), nblk, (float)max_norm,
                                                       coef.data_ptr<float>(),
-                                                      norm_out.has_value() ? norm_out->data_ptr<float>() : nullptr);
+                                                      norm_out.has_value() ? norm_out->data_ptr<float>() : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -418,10 +430,9 @@ void grad_clip_coef_parts(torch::Tensor parts, int64_t nslot, torch::Tensor esq,
                           c10::optional<torch::Tensor> norm_out) {
   c10::cuda::CUDAGuard guard(grads.device());
   TORCH_CHECK(parts.numel() >= G * nslot && esq.numel() >= G * M, "grad_clip_coef_parts: partials too small");
-  odp::clip_coef_parts_kernel<<<(unsigned)G, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      parts.data_ptr<float>(), nslot, esq.data_ptr<float>(), (int)M, grads.data_ptr<float>(), P,
+  C10_CUDA_CHECK(odp::launch_pdl((odp::clip_coef_parts_kernel), dim3((unsigned)G), dim3(256), 0, at::cuda::getCurrentCUDAStream(), parts.data_ptr<float>(), nslot, esq.data_ptr<float>(), (int)M, grads.data_ptr<float>(), P,
       reinterpret_cast<const long long*>(norm_offs.data_ptr<int64_t>()), (int)norm_offs.numel(), (int)H,
-      (float)max_norm, coef.data_ptr<float>(), norm_out.has_value() ? norm_out->data_ptr<float>() : nullptr);
+      (float)max_norm, coef.data_ptr<float>(), norm_out.has_value() ? norm_out->data_ptr<float>() : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -433,11 +444,10 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
   TORCH_CHECK(P % 4 == 0 || G == 1, "adamw_step: per-group length must be a multiple of 4");
   const long long threads = (P + 3) / 4;
   dim3 grid((unsigned)((threads + 255) / 256), (unsigned)G);
-  odp::adamw_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+  C10_CUDA_CHECK(odp::launch_pdl((odp::adamw_kernel), dim3(grid), dim3(256), 0, at::cuda::getCurrentCUDAStream(), p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), P, sp, s16,
       coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
-      (float)eps, (float)wd, row_skip(rows, r0, H, V));
+      (float)eps, (float)wd, row_skip(rows, r0, H, V)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -455,12 +465,11 @@ void adamw_acc_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Te
   TORCH_CHECK(sp % 4 == 0 && s16 % 4 == 0, "adamw_acc_step: strides must be multiples of 4");
   TORCH_CHECK(regions.is_cuda() && entries.is_cuda() && nregs >= 1 && ctas >= 1, "adamw_acc_step: tables on the device");
   TORCH_CHECK(odp::kAccCtaElems == 256 * 4, "adamw_acc_step: one CTA covers 256 x 4 elements");
-  odp::adamw_acc_kernel<<<(unsigned)ctas, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+  C10_CUDA_CHECK(odp::launch_pdl((odp::adamw_acc_kernel), dim3((unsigned)ctas), dim3(256), 0, at::cuda::getCurrentCUDAStream(), p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), sp, s16,
       coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
       (float)eps, (float)wd, row_skip(rows, r0, H, V), reinterpret_cast<const odp::AccRegion*>(regions.data_ptr()),
-      (int)nregs, reinterpret_cast<const odp::AccEntry*>(entries.data_ptr()), accumulate ? 1 : 0);
+      (int)nregs, reinterpret_cast<const odp::AccEntry*>(entries.data_ptr()), accumulate ? 1 : 0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -473,11 +482,10 @@ void adam8bit_step(torch::Tensor p, torch::Tensor g, torch::Tensor mq, torch::Te
   TORCH_CHECK(mq.numel() == nb * 256 && vq.numel() == nb * 256, "adam8bit_step: state must be [nblocks, 256]");
   TORCH_CHECK(nb * 256 >= n, "adam8bit_step: too few blocks");
   const long long threads = nb * 32;
-  odp::adam8bit_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      p.data_ptr<float>(), g.data_ptr<float>(), n, mq.data_ptr<int8_t>(), mabs.data_ptr<float>(),
+  C10_CUDA_CHECK(odp::launch_pdl((odp::adam8bit_kernel), dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, at::cuda::getCurrentCUDAStream(), p.data_ptr<float>(), g.data_ptr<float>(), n, mq.data_ptr<int8_t>(), mabs.data_ptr<float>(),
       vq.data_ptr<uint8_t>(), vlo.data_ptr<float>(), vsc.data_ptr<float>(), nb, blocks_per_group,
       coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
       (float)eps, (float)wd, first ? 1 : 0,
-      p16.has_value() ? reinterpret_cast<__nv_bfloat16*>(p16->data_ptr()) : nullptr);
+      p16.has_value() ? reinterpret_cast<__nv_bfloat16*>(p16->data_ptr()) : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
     fence_barrier_init();
   }
   if (warp == 0) tmem_alloc(&tmem_holder, 128);
+  pdl_wait();  // global memory only from here on
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   stage_async<128>(sQ, base, a.ld, h * D, a.S);
   stage_async<128>(sK, base, a.ld, (a.nh + kvh) * D, a.S);
@@ -260,6 +261,7 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tmem_holder;
+  pdl_trigger();  // after this CTA's TMEM allocation
   const uint32_t trow = tm + ((uint32_t)(warp * 32) << 16);
 
   if (threadIdx.x == 0) {
@@ -361,6 +363,7 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
     fence_barrier_init();
   }
   if (warp == 0) tmem_alloc(&tmem_holder, kCols);
+  pdl_wait();  // global memory only from here on
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
   stage_async<256>(sK, base, a.ld, (a.nh + kvh) * D, a.S);
@@ -369,6 +372,7 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tmem_holder;
+  pdl_trigger();  // after this CTA's TMEM allocation
   const uint32_t tS = tm, tdP = tm + 128;
   const uint32_t tdV = LEAN ? tm : tm + 256, tdK = LEAN ? tm + 64 : tm + 320, tdQ = LEAN ? tm + 128 : tm + 384;
   const float sl2 = a.scale * kLog2e;
@@ -644,6 +648,7 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
     fence_barrier_init();
   }
   if (warp == 0) tmem_alloc(&tmem_holder, 128);
+  pdl_wait();  // global memory only from here on
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   const int kend = min(a.S, q0 + T);  // causal: this tile needs keys [0, kend)
   const int nkt = (kend + KT - 1) / KT;
@@ -652,6 +657,7 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tmem_holder;
+  pdl_trigger();  // after this CTA's TMEM allocation
   const uint32_t trow = tm + ((uint32_t)(warp * 32) << 16);
   const uint32_t tS = trow, tO = trow + 64;
   const float sl2 = a.scale * kLog2e;
@@ -762,6 +768,7 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
     fence_barrier_init();
   }
   if (warp == 0) tmem_alloc(&tmem_holder, 256);
+  pdl_wait();  // global memory only from here on
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
   stage_rows<256>(sQ, base, a.ld, h * D, q0, T, a.S);
@@ -798,6 +805,7 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tmem_holder;
+  pdl_trigger();  // after this CTA's TMEM allocation
   const uint32_t tS = tm, tdP = tm + 64, tdQ = tm + 128;
   const float sl2 = a.scale * kLog2e;
   const float delta = sDelta[row], l2 = sLse[row];
@@ -889,6 +897,7 @@ __global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
     fence_barrier_init();
   }
   if (warp == 0) tmem_alloc(&tmem_holder, 256);
+  pdl_wait();  // global memory only from here on
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
   stage_rows<256>(sK, base, a.ld, (a.nh + kvh) * D, k0, T, a.S);
@@ -897,6 +906,7 @@ __global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tmem_holder;
+  pdl_trigger();  // after this CTA's TMEM allocation
   const uint32_t tS = tm, tdP = tm + 64, tdV = tm + 128, tdK = tm + 192;
   const float sl2 = a.scale * kLog2e;
   const int i0 = k0 / KT, nq = (a.S + KT - 1) / KT;  // query tiles at or after the diagonal
@@ -1023,7 +1033,7 @@ void attention_fwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
   }
   auto a = tc_args(qkv, S, nh, nkv, cosT, sinT, o, lse, err);
   dim3 grid((unsigned)nh, (unsigned)GB);
-  odp::attn_tc::fwd_kernel<<<grid, 128, odp::attn_tc::kFwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::fwd_kernel), dim3(grid), dim3(128), odp::attn_tc::kFwdSmem, at::cuda::getCurrentCUDAStream(), a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1048,9 +1058,9 @@ void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
   dim3 grid((unsigned)nkv, (unsigned)GB);
   const char* env = getenv("ODP_ATTN_BWD_LEAN");
   if (nh == nkv && !(env && env[0] == '0'))
-    odp::attn_tc::bwd_kernel<true><<<grid, 256, odp::attn_tc::kBwdSmemLean, at::cuda::getCurrentCUDAStream()>>>(a);
+    C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::bwd_kernel<true>), dim3(grid), dim3(256), odp::attn_tc::kBwdSmemLean, at::cuda::getCurrentCUDAStream(), a));
   else
-    odp::attn_tc::bwd_kernel<false><<<grid, 256, odp::attn_tc::kBwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
+    C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::bwd_kernel<false>), dim3(grid), dim3(256), odp::attn_tc::kBwdSmem, at::cuda::getCurrentCUDAStream(), a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1069,7 +1079,7 @@ void attention_fwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, i
   auto a = tc_args(qkv, S, nh, nkv, cosT, sinT, o, lse, err);
   const unsigned nqt = (unsigned)((S + odp::attn_tc::T - 1) / odp::attn_tc::T);
   dim3 grid(nqt, (unsigned)nh, (unsigned)GB);
-  odp::attn_tc::flash_fwd_kernel<<<grid, 128, odp::attn_tc::kFlashFwdSmem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::flash_fwd_kernel), dim3(grid), dim3(128), odp::attn_tc::kFlashFwdSmem, at::cuda::getCurrentCUDAStream(), a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1096,9 +1106,8 @@ void attention_bwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, i
   a.delta = delta.data_ptr<float>();
   auto st = at::cuda::getCurrentCUDAStream();
   const unsigned nt = (unsigned)((S + odp::attn_tc::T - 1) / odp::attn_tc::T);
-  odp::attn_tc::flash_bwd_dq_kernel<<<dim3(nt, (unsigned)nh, (unsigned)GB), 256, odp::attn_tc::kFlashDqSmem, st>>>(a);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::flash_bwd_dq_kernel), dim3(dim3(nt, (unsigned)nh, (unsigned)GB)), dim3(256), odp::attn_tc::kFlashDqSmem, st, a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  odp::attn_tc::flash_bwd_dkv_kernel<<<dim3(nt, (unsigned)nkv, (unsigned)GB), 256, odp::attn_tc::kFlashDkvSmem,
-                                       st>>>(a);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::flash_bwd_dkv_kernel), dim3(dim3(nt, (unsigned)nkv, (unsigned)GB)), dim3(256), odp::attn_tc::kFlashDkvSmem, st, a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -12,6 +12,9 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #define ODP_DEVICE __device__ __forceinline__
 
@@ -305,6 +308,47 @@ ODP_DEVICE bool elect_one() {
       "{\n .reg .b32 r;\n .reg .pred p;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}"
       : "=r"(pred));
   return pred != 0;
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// The kernels of an inner step run back to back in one stream (and one CUDA graph). With
+// programmatic dependent launch a kernel's CTAs may start while the previous kernel's last
+// CTAs still run: they do their prologue (barrier init, TMEM allocation, descriptor
+// prefetch) and then block in pdl_wait() until the previous grid has completed and its
+// writes are visible. Rules every kernel launched with launch_pdl() follows:
+//   * no global-memory access (read or write) before pdl_wait();
+//   * pdl_trigger() (which lets the NEXT kernel begin launching) only after this CTA's own
+//     TMEM allocation, so a dependent CTA can never hold TMEM that a CTA of this grid
+//     still needs.
+// Without a preceding programmatic dependency pdl_wait() returns at once.
+ODP_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+ODP_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Whether launch_pdl() sets the programmatic-serialization attribute (ODP_PDL=0 turns it
+// off for comparison runs); read once per process.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("ODP_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// Launch `kern` in `st` allowing it to overlap the previous kernel's tail (see above).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 }  // namespace odp

@@ -583,6 +583,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();     // global memory only from here on
+  pdl_trigger();  // after this CTA's TMEM allocation
 
   const int tiles_per_g = p.tiles_m * p.tiles_n;
   constexpr uint32_t kIdesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
@@ -798,6 +800,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // both CTAs' barriers are initialised before any remote signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  pdl_wait();     // global memory only from here on
+  pdl_trigger();  // after this CTA's TMEM allocation
   const int tiles_per_g = p.tiles_m * p.tiles_n;
   constexpr uint32_t kIdesc = umma_idesc_bf16(2 * BM, BN, A_MN, B_MN);
 
@@ -1043,7 +1047,7 @@ static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
     attr_set = true;
   }
   int grid = std::min(p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
-  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, mc, mx, p);
+  C10_CUDA_CHECK(odp::launch_pdl(kern, dim3(grid), dim3(kThreads), L::TOTAL, st, ma, mb, mc, mx, p));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1059,7 +1063,7 @@ static void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   }
   int grid = std::min(2 * p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
   grid &= ~1;  // whole CTA pairs
-  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, mc, mx, p);
+  C10_CUDA_CHECK(odp::launch_pdl(kern, dim3(grid), dim3(kThreads), L::TOTAL, st, ma, mb, mc, mx, p));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1205,6 +1209,8 @@ namespace odp {
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int S, int M, int N,
                                                             float* __restrict__ C, long long ldc, long long sc,
                                                             float* __restrict__ sqp, long long sq_ld, float beta) {
+  pdl_wait();
+  pdl_trigger();
   const int nbc = (N + 31) / 32, nbr = (M + 31) / 32;
   const int g = blockIdx.y, br = blockIdx.x / nbc, bc = blockIdx.x % nbc;
   const int r = br * 32 + threadIdx.x / 8, c = bc * 32 + (threadIdx.x % 8) * 4;
@@ -1313,8 +1319,9 @@ void gemm_splitk_reduce(torch::Tensor ws, int64_t S, int64_t G, int64_t M, int64
   c10::cuda::CUDAGuard guard(ws.device());
   TORCH_CHECK(ws.numel() >= G * S * M * N, "gemm_splitk_reduce: workspace too small");
   dim3 grid((unsigned)(((M + 31) / 32) * ((N + 31) / 32)), (unsigned)G);
-  odp::splitk_reduce_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ws.data_ptr<float>(), (int)S, (int)M, (int)N, C.data_ptr<float>(), ldc, sc,
-      sq_part.has_value() ? sq_part->data_ptr<float>() : nullptr, sq_ld, (float)beta);
+  C10_CUDA_CHECK(odp::launch_pdl(odp::splitk_reduce_kernel, grid, dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+                                 ws.data_ptr<float>(), (int)S, (int)M, (int)N, C.data_ptr<float>(), ldc, sc,
+                                 sq_part.has_value() ? sq_part->data_ptr<float>() : nullptr, sq_ld,
+                                 (float)beta));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -25,6 +25,8 @@ namespace odp {
 __global__ void ce_finalize_kernel(const float2* __restrict__ part, int T, const __nv_bfloat16* __restrict__ logits,
                                    long long ldl, long long sl, const int* __restrict__ labels, int M, int G,
                                    float* __restrict__ lse, float* __restrict__ row_loss, long long ms) {
+  pdl_wait();
+  pdl_trigger();
   const int q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= G * M) return;
   const long long r = (long long)(q / M) * ms + q % M;
@@ -48,6 +50,8 @@ __global__ void ce_finalize_kernel(const float2* __restrict__ part, int T, const
 __global__ void group_sum_kernel(const float* __restrict__ row_loss, const int* __restrict__ labels, int M,
                                  float* __restrict__ out_sum, float* __restrict__ out_inv_count,
                                  float* __restrict__ out_loss, const float* __restrict__ inv_given) {
+  pdl_wait();
+  pdl_trigger();
   const int g = blockIdx.x;
   __shared__ float ss[256];
   __shared__ int sc[256];
@@ -83,6 +87,8 @@ __global__ void group_sum_kernel(const float* __restrict__ row_loss, const int* 
 __global__ void ce_backward_kernel(__nv_bfloat16* logits, long long ldl, long long sl, const float* __restrict__ lse,
                                    const int* __restrict__ labels, const float* __restrict__ inv_count, int M, int V,
                                    int G, long long ms) {
+  pdl_wait();
+  pdl_trigger();
   const long long vec_per_row = V / 8;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)G * M * vec_per_row) return;
@@ -112,6 +118,8 @@ __global__ void ce_backward_kernel(__nv_bfloat16* logits, long long ldl, long lo
 
 // inv_count[g] = 1 / max(1, #labels >= 0 of group g): the dlogits scale, known before the loss.
 __global__ void label_count_kernel(const int* __restrict__ labels, int M, float* __restrict__ inv_count) {
+  pdl_wait();
+  pdl_trigger();
   const int g = blockIdx.x;
   __shared__ int sc[256];
   int c = 0;
@@ -155,6 +163,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_fused_kernel(__nv_bfloat16* log
                                                               const float* __restrict__ inv_count,
                                                               float* __restrict__ lse_out, float* __restrict__ row_loss,
                                                               int* err, long long ms) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t ce_smem[];
   __shared__ uint64_t bar;
   __shared__ float red_m[kCeThreads / 32], red_s[kCeThreads / 32];
@@ -288,15 +298,14 @@ void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl
   c10::cuda::CUDAGuard guard(logits.device());
   auto st = at::cuda::getCurrentCUDAStream();
   const int R = (int)(G * M);
-  odp::ce_finalize_kernel<<<(R + 255) / 256, 256, 0, st>>>(
-      reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)T,
+  C10_CUDA_CHECK(odp::launch_pdl((odp::ce_finalize_kernel), dim3((R + 255) / 256), dim3(256), 0, st, reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)T,
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)G,
-      lse.data_ptr<float>(), row_loss.data_ptr<float>(), (long long)M);
+      lse.data_ptr<float>(), row_loss.data_ptr<float>(), (long long)M));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
+  C10_CUDA_CHECK(odp::launch_pdl((odp::group_sum_kernel), dim3((int)G), dim3(256), 0, st, row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
                                                  loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
                                                  loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr,
-                                                 inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr);
+                                                 inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -319,17 +328,16 @@ void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor label
   }
   const float* given = inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr;
   if (!given) {
-    odp::label_count_kernel<<<(int)G, 256, 0, st>>>(labels.data_ptr<int>(), (int)M, inv_count.data_ptr<float>());
+    C10_CUDA_CHECK(odp::launch_pdl((odp::label_count_kernel), dim3((int)G), dim3(256), 0, st, labels.data_ptr<int>(), (int)M, inv_count.data_ptr<float>()));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
-  odp::ce_fused_kernel<<<(unsigned)(G * M), odp::kCeThreads, (size_t)V * 2, st>>>(
-      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)V,
+  C10_CUDA_CHECK(odp::launch_pdl((odp::ce_fused_kernel), dim3((unsigned)(G * M)), dim3(odp::kCeThreads), (size_t)V * 2, st, reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)V,
       given ? given : inv_count.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(),
-      err.data_ptr<int>(), (long long)M);
+      err.data_ptr<int>(), (long long)M));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  odp::group_sum_kernel<<<(int)G, 256, 0, st>>>(row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
+  C10_CUDA_CHECK(odp::launch_pdl((odp::group_sum_kernel), dim3((int)G), dim3(256), 0, st, row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
                                                  loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
-                                                 loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr, given);
+                                                 loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr, given));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -338,9 +346,8 @@ void ce_backward(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor ls
   TORCH_CHECK(V % 8 == 0 && ldl % 8 == 0, "ce_backward: vocab must be a multiple of 8");
   c10::cuda::CUDAGuard guard(logits.device());
   const long long n = G * M * (V / 8);
-  odp::ce_backward_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, lse.data_ptr<float>(), labels.data_ptr<int>(),
-      inv_count.data_ptr<float>(), (int)M, (int)V, (int)G, (long long)M);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::ce_backward_kernel), dim3((unsigned)((n + 255) / 256)), dim3(256), 0, at::cuda::getCurrentCUDAStream(), reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, lse.data_ptr<float>(), labels.data_ptr<int>(),
+      inv_count.data_ptr<float>(), (int)M, (int)V, (int)G, (long long)M));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -352,18 +359,17 @@ void ce_backward(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor ls
 // all rows at the end.
 void ce_label_count(torch::Tensor labels, int64_t M, int64_t G, torch::Tensor inv_count) {
   c10::cuda::CUDAGuard guard(labels.device());
-  odp::label_count_kernel<<<(int)G, 256, 0, at::cuda::getCurrentCUDAStream()>>>(labels.data_ptr<int>(), (int)M,
-                                                                                 inv_count.data_ptr<float>());
+  C10_CUDA_CHECK(odp::launch_pdl((odp::label_count_kernel), dim3((int)G), dim3(256), 0, at::cuda::getCurrentCUDAStream(), labels.data_ptr<int>(), (int)M,
+                                                                                 inv_count.data_ptr<float>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void ce_group_sum(torch::Tensor row_loss, torch::Tensor labels, int64_t M, int64_t G, torch::Tensor loss_sum,
                   torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out, c10::optional<torch::Tensor> inv_given) {
   c10::cuda::CUDAGuard guard(labels.device());
-  odp::group_sum_kernel<<<(int)G, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M, loss_sum.data_ptr<float>(),
+  C10_CUDA_CHECK(odp::launch_pdl((odp::group_sum_kernel), dim3((int)G), dim3(256), 0, at::cuda::getCurrentCUDAStream(), row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M, loss_sum.data_ptr<float>(),
       inv_count.data_ptr<float>(), loss_out.has_value() ? loss_out->data_ptr<float>() : nullptr,
-      inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr);
+      inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -386,22 +392,19 @@ void ce_rows_chunk(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor 
                                           odp::kCeMaxV * 2));
       attr = true;
     }
-    odp::ce_fused_kernel<<<(unsigned)(G * Mc), odp::kCeThreads, (size_t)V * 2, st>>>(
-        reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)Mc, (int)V,
-        inv.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(), err.data_ptr<int>(), ms);
+    C10_CUDA_CHECK(odp::launch_pdl((odp::ce_fused_kernel), dim3((unsigned)(G * Mc)), dim3(odp::kCeThreads), (size_t)V * 2, st, reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)Mc, (int)V,
+        inv.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(), err.data_ptr<int>(), ms));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }
   const int R = (int)(G * Mc);
-  odp::ce_finalize_kernel<<<(R + 255) / 256, 256, 0, st>>>(
-      reinterpret_cast<const float2*>(part->data_ptr<float>()), (int)T,
+  C10_CUDA_CHECK(odp::launch_pdl((odp::ce_finalize_kernel), dim3((R + 255) / 256), dim3(256), 0, st, reinterpret_cast<const float2*>(part->data_ptr<float>()), (int)T,
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)Mc, (int)G,
-      lse.data_ptr<float>(), row_loss.data_ptr<float>(), ms);
+      lse.data_ptr<float>(), row_loss.data_ptr<float>(), ms));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const long long n = G * Mc * (V / 8);
-  odp::ce_backward_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
-      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, lse.data_ptr<float>(), labels.data_ptr<int>(),
-      inv.data_ptr<float>(), (int)Mc, (int)V, (int)G, ms);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::ce_backward_kernel), dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, lse.data_ptr<float>(), labels.data_ptr<int>(),
+      inv.data_ptr<float>(), (int)Mc, (int)V, (int)G, ms));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

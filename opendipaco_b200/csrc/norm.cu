@@ -23,6 +23,8 @@ namespace odp {
 __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, long long sx, const float* __restrict__ w,
                                    long long sw, __nv_bfloat16* __restrict__ y, long long sy,
                                    float* __restrict__ rstd, int M, int H, int G, float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= G * M) return;
   const int g = warp / M, r = warp % M;
@@ -51,6 +53,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_reg_kernel(const float* __res
                                                               __nv_bfloat16* __restrict__ y, long long sy,
                                                               float* __restrict__ rstd, int M, int H, int G,
                                                               float eps) {
+  pdl_wait();
+  pdl_trigger();
   const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32 * R;
   const int lane = threadIdx.x % 32;
   float4 v[R][NV];
@@ -94,6 +98,8 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, long long sx, co
                                    long long sdy, const float* dres, float* dx, long long sdx,
                                    __nv_bfloat16* dx16, float* __restrict__ dw_part, int M, int H, int G,
                                    int rpb) {
+  pdl_wait();
+  pdl_trigger();
   // block = 256 threads = 8 warps; block handles kNormRowsPerBlock rows of one group
   const int nblk = (M + rpb - 1) / rpb;
   const int g = blockIdx.x / nblk, b = blockIdx.x % nblk;
@@ -162,6 +168,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const float* __res
                                                               const float* dres, float* dx, long long sdx,
                                                               __nv_bfloat16* dx16, float* __restrict__ dw_part, int M,
                                                               int H, int G, int rpb) {
+  pdl_wait();
+  pdl_trigger();
   const int nblk = (M + rpb - 1) / rpb;
   const int g = blockIdx.x / nblk, b = blockIdx.x % nblk;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -232,6 +240,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const float* __res
 // dw[g][i] = sum_b dw_part[g][b][i] in fixed order.
 __global__ void reduce_parts_kernel(const float* __restrict__ part, int nblk, int H, int G, float* dw, long long sdw,
                                     float beta) {
+  pdl_wait();
+  pdl_trigger();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= G * H) return;
   const int g = idx / H, i = idx % H;
@@ -245,6 +255,8 @@ __global__ void reduce_parts_kernel(const float* __restrict__ part, int nblk, in
 // ids: [G][M] int32; E: group g's table at E + g*se ([V][H] fp32); out: [G][M][H] fp32.
 __global__ void embedding_fwd_kernel(const int* __restrict__ ids, const float* __restrict__ E, long long se,
                                      float* __restrict__ out, int M, int H, int G, int V) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= G * M) return;
   const int g = warp / M;
@@ -258,6 +270,8 @@ __global__ void embedding_fwd_kernel(const int* __restrict__ ids, const float* _
 // One warp per token row. The row that first carries an id owns that id's gradient row.
 __global__ void embedding_bwd_kernel(const int* __restrict__ ids, const float* __restrict__ dx, long long sdx,
                                      float* __restrict__ dE, long long se, int M, int H, int G, int V) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= G * M) return;
   const int g = warp / M, r = warp % M;
@@ -301,6 +315,8 @@ constexpr int kSortMax = 4096;
 
 __global__ void __launch_bounds__(1024) embed_sort_kernel(const int* __restrict__ ids, int M,
                                                           unsigned* __restrict__ keys_out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ unsigned k[kSortMax];
   const int g = blockIdx.x;
   int n = 1;
@@ -330,6 +346,8 @@ template <int NT>
 __global__ void embed_runs_kernel(const unsigned* __restrict__ keys, const float* __restrict__ dx, long long sdx,
                                   float* __restrict__ dE, long long se, int M, int H, int G, int V,
                                   uint8_t* __restrict__ rows, float* __restrict__ sq) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= G * M) return;
   const int g = warp / M, i = warp % M;
@@ -405,21 +423,20 @@ void rmsnorm_fwd_rpw(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, t
 #define ODP_RMS_FWD(NV)                                                                                          \
   if (reg && nv == NV) {                                                                                         \
     if (few)                                                                                                     \
-      odp::rmsnorm_fwd_reg_kernel<NV, 1><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(                           \
+      C10_CUDA_CHECK(odp::launch_pdl((odp::rmsnorm_fwd_reg_kernel<NV, 1>), dim3(blocks_for(G * M * 32, 256)), dim3(256), 0, st, \
           x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,  \
-          rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);                                           \
+          rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps));                                           \
     else                                                                                                         \
-      odp::rmsnorm_fwd_reg_kernel<NV, 4><<<blocks_for(G * M * 8, 256), 256, 0, st>>>(                            \
+      C10_CUDA_CHECK(odp::launch_pdl((odp::rmsnorm_fwd_reg_kernel<NV, 4>), dim3(blocks_for(G * M * 8, 256)), dim3(256), 0, st, \
           x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,  \
-          rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);                                           \
+          rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps));                                           \
     C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                              \
     return;                                                                                                      \
   }
   ODP_RMS_FWD(1) ODP_RMS_FWD(2) ODP_RMS_FWD(3) ODP_RMS_FWD(4) ODP_RMS_FWD(8)
 #undef ODP_RMS_FWD
-  odp::rmsnorm_fwd_kernel<<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-      x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,
-      rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::rmsnorm_fwd_kernel), dim3(blocks_for(G * M * 32, 256)), dim3(256), 0, st, x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), sy,
+      rstd.data_ptr<float>(), (int)M, (int)H, (int)G, (float)eps));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -451,11 +468,11 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
   if (!launched && H % 128 == 0 && nv == NV) {                                                                    \
     if (smem > 48 * 1024)                                                                                         \
       cudaFuncSetAttribute(odp::rmsnorm_bwd_reg_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    odp::rmsnorm_bwd_reg_kernel<NV><<<(int)G * nblk, 256, smem, st>>>(                                            \
+    C10_CUDA_CHECK(odp::launch_pdl((odp::rmsnorm_bwd_reg_kernel<NV>), dim3((int)G * nblk), dim3(256), smem, st, \
         x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, rstd.data_ptr<float>(), dy.data_ptr<float>(), sdy,      \
         dres.has_value() ? dres->data_ptr<float>() : nullptr, dx.data_ptr<float>(), sdx,                          \
         dx16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx16->data_ptr()) : nullptr, work.data_ptr<float>(),  \
-        (int)M, (int)H, (int)G, rpb);                                                                             \
+        (int)M, (int)H, (int)G, rpb));                                                                             \
     launched = true;                                                                                              \
   }
   ODP_RMS_BWD(1) ODP_RMS_BWD(2) ODP_RMS_BWD(3) ODP_RMS_BWD(4) ODP_RMS_BWD(8)
@@ -463,15 +480,14 @@ void rmsnorm_bwd(torch::Tensor x, int64_t sx, torch::Tensor w, int64_t sw, torch
   if (!launched) {
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(odp::rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  odp::rmsnorm_bwd_kernel<<<(int)G * nblk, 256, smem, st>>>(
-      x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, rstd.data_ptr<float>(), dy.data_ptr<float>(), sdy,
+  C10_CUDA_CHECK(odp::launch_pdl((odp::rmsnorm_bwd_kernel), dim3((int)G * nblk), dim3(256), smem, st, x.data_ptr<float>(), sx, w.data_ptr<float>(), sw, rstd.data_ptr<float>(), dy.data_ptr<float>(), sdy,
       dres.has_value() ? dres->data_ptr<float>() : nullptr, dx.data_ptr<float>(), sdx,
       dx16.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx16->data_ptr()) : nullptr, work.data_ptr<float>(),
-      (int)M, (int)H, (int)G, rpb);
+      (int)M, (int)H, (int)G, rpb));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  odp::reduce_parts_kernel<<<blocks_for(G * H, 256), 256, 0, st>>>(work.data_ptr<float>(), nblk, (int)H, (int)G,
-                                                                    dw.data_ptr<float>(), sdw, (float)beta);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::reduce_parts_kernel), dim3(blocks_for(G * H, 256)), dim3(256), 0, st, work.data_ptr<float>(), nblk, (int)H, (int)G,
+                                                                    dw.data_ptr<float>(), sdw, (float)beta));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -480,8 +496,7 @@ void embedding_fwd(torch::Tensor ids, torch::Tensor E, int64_t se, torch::Tensor
   TORCH_CHECK(H % 4 == 0, "embedding: hidden size must be a multiple of 4");
   c10::cuda::CUDAGuard guard(E.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  odp::embedding_fwd_kernel<<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-      ids.data_ptr<int>(), E.data_ptr<float>(), se, out.data_ptr<float>(), (int)M, (int)H, (int)G, (int)V);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::embedding_fwd_kernel), dim3(blocks_for(G * M * 32, 256)), dim3(256), 0, st, ids.data_ptr<int>(), E.data_ptr<float>(), se, out.data_ptr<float>(), (int)M, (int)H, (int)G, (int)V));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -490,8 +505,7 @@ void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tens
   TORCH_CHECK(H % 32 == 0 && H <= 2048, "embedding_bwd: hidden size must be a multiple of 32 and <= 2048");
   c10::cuda::CUDAGuard guard(dE.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  odp::embedding_bwd_kernel<<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-      ids.data_ptr<int>(), dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::embedding_bwd_kernel), dim3(blocks_for(G * M * 32, 256)), dim3(256), 0, st, ids.data_ptr<int>(), dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -522,15 +536,13 @@ void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torc
     rp = rows->data_ptr<uint8_t>();
     C10_CUDA_CHECK(cudaMemsetAsync(rp, 0, (size_t)(G * V), st));
   }
-  odp::embed_sort_kernel<<<(int)G, 1024, 0, st>>>(ids.data_ptr<int>(), (int)M, kp);
+  C10_CUDA_CHECK(odp::launch_pdl((odp::embed_sort_kernel), dim3((int)G), dim3(1024), 0, st, ids.data_ptr<int>(), (int)M, kp));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (H <= 512)
-    odp::embed_runs_kernel<16><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp,
-        sq.has_value() ? sq->data_ptr<float>() : nullptr);
+    C10_CUDA_CHECK(odp::launch_pdl((odp::embed_runs_kernel<16>), dim3(blocks_for(G * M * 32, 256)), dim3(256), 0, st, kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp,
+        sq.has_value() ? sq->data_ptr<float>() : nullptr));
   else
-    odp::embed_runs_kernel<64><<<blocks_for(G * M * 32, 256), 256, 0, st>>>(
-        kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp,
-        sq.has_value() ? sq->data_ptr<float>() : nullptr);
+    C10_CUDA_CHECK(odp::launch_pdl((odp::embed_runs_kernel<64>), dim3(blocks_for(G * M * 32, 256)), dim3(256), 0, st, kp, dx.data_ptr<float>(), sdx, dE.data_ptr<float>(), se, (int)M, (int)H, (int)G, (int)V, rp,
+        sq.has_value() ? sq->data_ptr<float>() : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

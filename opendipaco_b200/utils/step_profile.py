@@ -2,7 +2,7 @@
 inner step is bracketed by CUDA events (warm caches, steady state, no profiler), and the
 times are summed per kernel and epilogue.
 
-    python -m opendipaco_b200.utils.step_profile [--levels 4 4] [--batch 24] [--steps 3]
+    python -m opendipaco_b200.utils.step_profile [--levels 4 4] [--batch 24] [--steps 3] [--graph]
 
 Defaults: the 16-path 4x4 DiPaCo, hidden 384, 6 heads, ffn 1024, layers [2, 2], vocab
 32000, 24 sequences of 128 tokens per path, 20 inner steps a round. The CPU is put ahead
@@ -80,6 +80,24 @@ def profile_inner_step(ex, steps: int = 3) -> dict:
             "other_ms": round(step - listed, 4)}
 
 
+def graph_step_ms(ex, rounds: int = 5) -> float:
+    """Device time of one inner step inside the captured round graph (a round's replay
+    divided by its inner steps; median of ``rounds`` replays after one warm-up)."""
+    steps = ex.e.diloco.inner_steps
+    ex._run_inner(steps)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(rounds):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ex._run_inner(steps)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2] / steps
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--levels", type=int, nargs=2, default=[4, 4])
@@ -90,6 +108,8 @@ def main() -> None:
     ap.add_argument("--ffn", type=int, default=1024)
     ap.add_argument("--vocab", type=int, default=32000)
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--graph", action="store_true",
+                    help="also time whole rounds replayed from the CUDA graph (no per-call events)")
     args = ap.parse_args()
 
     from .. import BackboneConfig, DiLoCoConfig, DiPaCoConfig, DiPaCoEngine, LocalBackend
@@ -105,6 +125,8 @@ def main() -> None:
     corpus = ShardedCorpus.from_assignments(docs, torch.arange(len(docs)) % P, P, args.seq)
     eng = DiPaCoEngine(cfg, dl, LocalBackend(cfg.build_topology()), device=torch.device("cuda"), seed=0)
     eng.fit(corpus, num_rounds=1, batch_size=args.batch, log_every=0)
+    if args.graph:
+        print(json.dumps({"graph_step_ms": round(graph_step_ms(eng._fused), 4)}))
     out = profile_inner_step(eng._fused, args.steps)
     print(json.dumps({"config": vars(args), "step_ms": round(out["step_ms"], 4), "other_ms": out["other_ms"]}))
     for row in out["calls"]:
