@@ -108,6 +108,7 @@ torch::Tensor bag_of_tokens(torch::Tensor ids, torch::Tensor offs, torch::Tensor
 std::vector<torch::Tensor> kmeans_assign(torch::Tensor x, torch::Tensor c, int64_t topk, bool want_min,
                                          bool want_dist, torch::Tensor err);
 std::vector<torch::Tensor> kmeans_cluster_sums(torch::Tensor x, torch::Tensor assign, int64_t K);
+void peer_copy(torch::Tensor table, int64_t max_elems);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opendipaco_b200 sm_100a kernels";
@@ -156,4 +157,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bag_of_tokens", &bag_of_tokens);
   m.def("kmeans_assign", &kmeans_assign);
   m.def("kmeans_cluster_sums", &kmeans_cluster_sums);
+  m.def("peer_copy", &peer_copy);
 }

@@ -352,21 +352,52 @@ class NVLinkBackend(TorchDistBackend):
         v = v.cpu()
         return {k: float(v[idx[k]].sqrt()) for k in self._all_keys if self.owns_module(k)}
 
+    def peer_copy(self, segments: list[tuple[int, int, int]]) -> None:
+        """One launch of our pull-copy kernel over (source address, destination address,
+        fp32 elements) segments; sources may be peer addresses of the symmetric arenas.
+        Addresses must be 16-byte aligned."""
+        if not segments:
+            return
+        from ...ops._ext import ext
+
+        for src, dst, n in segments:
+            if src % 16 or dst % 16:
+                raise ValueError("peer_copy: 16-byte aligned addresses only")
+        for i in range(0, len(segments), 65535):
+            part = segments[i:i + 65535]
+            tab = torch.tensor(part, dtype=torch.int64).to(self.dev)
+            ext().peer_copy(tab, max(n for _, _, n in part))
+
     def gather_momentum(self, ex) -> None:
-        """Fill the non-owned slices of each owned key's momentum from its owners."""
+        """Fill the non-owned slices of each owned key's momentum from its owners (peer
+        loads in one launch, between two barriers)."""
         torch.cuda.synchronize(self.dev)
         dist.barrier()
+        segs = []
         for key, buf in ex.mom.items():
             off = self._offs[key]
             for r in self.sharing_ranks(key):
                 if r == self.rank:
                     continue
-                peer = self._hm.get_buffer(r, (self.MOM.numel(),), torch.float32)
                 s0, s1 = self.slice_of(key, r)
                 if s1 > s0:
-                    buf[s0:s1].copy_(peer[off + s0:off + s1])
+                    segs.append((self._hm.buffer_ptrs[r] + 4 * (off + s0), buf.data_ptr() + 4 * s0, s1 - s0))
+        self.peer_copy(segs)
         torch.cuda.synchronize(self.dev)
         dist.barrier()
+
+    def bank_sources(self) -> dict[str, tuple[int, int]] | None:
+        """key -> (peer address of the key's region in the GLOB arena of the rank that
+        serves it, region length): the rank owning the key's lowest-index path, as in the
+        broadcast gather. None before the arenas exist."""
+        if self._offs is None:
+            return None
+        topo = self.topology
+        out = {}
+        for key in topo.module_keys():
+            src = self.rank_of_path(min(topo.paths_through_module(key), key=topo.path_index))
+            out[key] = (self._hg.buffer_ptrs[src] + 4 * self._offs[key], self._sizes[key])
+        return out
 
     def close(self) -> None:
         torch.cuda.synchronize(self.dev) if self._offs is not None else None

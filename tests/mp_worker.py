@@ -86,6 +86,16 @@ def main():
         ranks = backend.sharing_ranks(key)
         for r in ranks[1:]:
             consistent &= bool(torch.equal(allb[r], allb[ranks[0]]))
+    # full-bank gather: the NVLink pull equals the per-parameter broadcast bit for bit
+    gather_same = True
+    if base == "nvlink" and dp == 1:
+        from opendipaco_b200.parallel.gather import gather_full_bank
+
+        fb_peer = gather_full_bank(backend, eng.bank, cfg, method="peer")
+        fb_bc = gather_full_bank(backend, eng.bank, cfg, method="broadcast")
+        gather_same = sorted(fb_peer) == sorted(topo.module_keys()) and all(
+            torch.equal(a, b) for k in fb_peer
+            for a, b in zip(fb_peer[k].state_dict().values(), fb_bc[k].state_dict().values()))
     # checkpoint round trip (momentum gathered from the slice owners)
     ck = os.path.join(out_dir, f"ckpt_{mode}")
     save_checkpoint(eng, ck)
@@ -101,7 +111,7 @@ def main():
     resumed = h1[0].per_path_loss == h2[0].per_path_loss
     torch.save({"bank": {k: {n: t.detach().cpu() for n, t in m.state_dict().items()} for k, m in eng.bank.items()},
                 "init": init, "losses": [m.per_path_loss for m in hist], "consistent": consistent, "ckpt_same": same,
-                "resumed": resumed},
+                "gather_same": gather_same, "resumed": resumed},
                os.path.join(out_dir, f"{mode}_rank{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()

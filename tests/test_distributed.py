@@ -98,6 +98,7 @@ def test_nvlink_outer_step_matches_nccl(tmp_path):
     nc = _launch(tmp_path, "nccl", 2, 29615)
     for a, b in zip(nv, nc):
         assert a["consistent"] and b["consistent"]
+        assert a["gather_same"]  # NVLink pull of the full bank == per-parameter broadcast
         assert a["ckpt_same"] and a["resumed"]
         assert a["losses"] == b["losses"]
         for k in a["bank"]:

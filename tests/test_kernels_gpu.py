@@ -310,3 +310,19 @@ def test_outer_step_matches_torch_sgd():
             assert torch.equal(l, glob)
             l.add_(0.01 * torch.randn(n, device=DEV))
         p.data.copy_(glob)
+
+
+def test_peer_copy_segments_with_tails():
+    """The pull-copy kernel (used over NVLink for the full-bank gather) on local memory:
+    many segments, lengths not multiples of 4, one launch."""
+    from opendipaco_b200.ops._ext import ext
+
+    g = torch.Generator().manual_seed(3)
+    srcs = [torch.randn(n, generator=g).cuda() for n in (1, 4, 7, 1000, 4099, 70001)]
+    dsts = [torch.zeros_like(s) for s in srcs]
+    tab = torch.tensor([[s.data_ptr(), d.data_ptr(), s.numel()] for s, d in zip(srcs, dsts)],
+                       dtype=torch.int64).cuda()
+    ext().peer_copy(tab, max(s.numel() for s in srcs))
+    torch.cuda.synchronize()
+    for s, d in zip(srcs, dsts):
+        assert torch.equal(s, d)
