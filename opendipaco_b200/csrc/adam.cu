@@ -326,13 +326,30 @@ __global__ void __launch_bounds__(256) adamw_acc_kernel(
 }
 
 // ---------------------------------------------------------------- 8-bit Adam
-// One warp per 256-element block (8 consecutive elements per lane).
-__global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__ g, long long n, int8_t* __restrict__ mq,
-                                float* __restrict__ mabs, uint8_t* __restrict__ vq, float* __restrict__ vlo,
-                                float* __restrict__ vsc, long long nblocks, long long blocks_per_group,
-                                const float* __restrict__ coef,
-                                const float* __restrict__ sched, float b1, float b2, float eps, float wd, int first,
-                                __nv_bfloat16* __restrict__ p16) {
+// One warp per 256-element block (8 consecutive elements per lane). With `vec` (every base
+// 16-byte aligned, codes 8-byte aligned) a lane issues all of its loads up front as
+// vectors -- two float4 of gradient, two of weights, 8 bytes of each code -- so a warp has
+// its whole block in flight before the block reductions; the arithmetic per element is the
+// same in both forms.
+template <bool VEC>
+ODP_DEVICE void a8_load(const float* __restrict__ src, long long e0, long long n, float (&v)[8]) {
+  if (VEC) {
+    const float4 a = *reinterpret_cast<const float4*>(src + e0), b = *reinterpret_cast<const float4*>(src + e0 + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = e0 + k < n ? src[e0 + k] : 0.f;
+  }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(256) adam8bit_kernel(float* __restrict__ p, const float* __restrict__ g, long long n,
+                                                       int8_t* __restrict__ mq, float* __restrict__ mabs,
+                                                       uint8_t* __restrict__ vq, float* __restrict__ vlo,
+                                                       float* __restrict__ vsc, long long nblocks,
+                                                       long long blocks_per_group, const float* __restrict__ coef,
+                                                       const float* __restrict__ sched, float b1, float b2, float eps,
+                                                       float wd, int first, __nv_bfloat16* __restrict__ p16) {
   pdl_wait();
   pdl_trigger();
   const long long blk = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
@@ -341,25 +358,40 @@ __global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__
   const long long grp = blocks_per_group > 0 ? blk / blocks_per_group : 0;
   const float* scd = sched + grp * 4;  // per path: lr, lr / bc1, sqrt(bc2), active
   if (scd[3] == 0.f) return;
+  const long long e0 = blk * 256 + lane * 8;
+  const bool full = VEC && e0 + 8 <= n;
+  float gv[8], pv[8];
+  int8_t mc[8];
+  uint8_t vc[8];
+  if (full) {
+    a8_load<true>(g, e0, n, gv);
+    a8_load<true>(p, e0, n, pv);
+    *reinterpret_cast<uint2*>(mc) = *reinterpret_cast<const uint2*>(mq + e0);
+    *reinterpret_cast<uint2*>(vc) = *reinterpret_cast<const uint2*>(vq + e0);
+  } else {
+    a8_load<false>(g, e0, n, gv);
+    a8_load<false>(p, e0, n, pv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      mc[k] = mq[e0 + k];
+      vc[k] = vq[e0 + k];
+    }
+  }
   const float lr = scd[0], step_size = scd[1], bc2s = scd[2];
   const bool first_step = first || scd[3] > 1.5f;  // 2.0 marks a path's first step
   const float cf = coef ? coef[grp] : 1.f;
-  const long long e0 = blk * 256 + lane * 8;
   const float mscale = mabs[blk] / 127.f;
   const float lo = vlo[blk], sc = vsc[blk];
-  float mv[8], vv[8], gv[8];
-  const int8_t* mqp = mq + e0;
-  const uint8_t* vqp = vq + e0;
+  float mv[8], vv[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const long long e = e0 + k;
-    gv[k] = e < n ? g[e] * cf : 0.f;
-    mv[k] = (float)mqp[k] * mscale;
-    vv[k] = first_step ? 0.f : __expf((float)vqp[k] * sc + lo);
+    gv[k] = e0 + k < n ? gv[k] * cf : 0.f;
+    mv[k] = (float)mc[k] * mscale;
+    vv[k] = first_step ? 0.f : __expf((float)vc[k] * sc + lo);
     mv[k] = mv[k] * b1 + (1.f - b1) * gv[k];
     vv[k] = vv[k] * b2 + (1.f - b2) * gv[k] * gv[k];
   }
-  // requantise m: symmetric absmax
+  // requantise m: symmetric absmax; v: log domain over the block's range
   float amax = 0.f, lmin = INFINITY, lmax = -INFINITY;
   float lv[8];
 #pragma unroll
@@ -374,12 +406,10 @@ __global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__
   lmin = -warp_max(-lmin);
   const float qs = amax > 0.f ? amax / 127.f : 1.f;
   const float vs = fmaxf((lmax - lmin) / 255.f, 1e-12f);
-  int8_t* mqo = mq + e0;
-  uint8_t* vqo = vq + e0;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    mqo[k] = (int8_t)fminf(fmaxf(rintf(mv[k] / qs), -127.f), 127.f);
-    vqo[k] = (uint8_t)fminf(fmaxf(rintf((lv[k] - lmin) / vs), 0.f), 255.f);
+    mc[k] = (int8_t)fminf(fmaxf(rintf(mv[k] / qs), -127.f), 127.f);
+    vc[k] = (uint8_t)fminf(fmaxf(rintf((lv[k] - lmin) / vs), 0.f), 255.f);
   }
   if (lane == 0) {
     mabs[blk] = amax;
@@ -389,12 +419,27 @@ __global__ void adam8bit_kernel(float* __restrict__ p, const float* __restrict__
   const float decay = 1.f - lr * wd;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const long long e = e0 + k;
-    if (e >= n) break;
     const float den = sqrtf(vv[k]) / bc2s + eps;
-    const float nv = p[e] * decay - step_size * (mv[k] / den);
-    p[e] = nv;
-    if (p16) p16[e] = __float2bfloat16(nv);
+    pv[k] = pv[k] * decay - step_size * (mv[k] / den);
+  }
+  if (full) {
+    *reinterpret_cast<uint2*>(mq + e0) = *reinterpret_cast<const uint2*>(mc);
+    *reinterpret_cast<uint2*>(vq + e0) = *reinterpret_cast<const uint2*>(vc);
+    *reinterpret_cast<float4*>(p + e0) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+    *reinterpret_cast<float4*>(p + e0 + 4) = make_float4(pv[4], pv[5], pv[6], pv[7]);
+    if (p16)
+      *reinterpret_cast<uint4*>(p16 + e0) = make_uint4(pack_bf16(pv[0], pv[1]), pack_bf16(pv[2], pv[3]),
+                                                       pack_bf16(pv[4], pv[5]), pack_bf16(pv[6], pv[7]));
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      mq[e0 + k] = mc[k];
+      vq[e0 + k] = vc[k];
+      if (e0 + k < n) {
+        p[e0 + k] = pv[k];
+        if (p16) p16[e0 + k] = __float2bfloat16(pv[k]);
+      }
+    }
   }
 }
 
@@ -482,10 +527,16 @@ void adam8bit_step(torch::Tensor p, torch::Tensor g, torch::Tensor mq, torch::Te
   TORCH_CHECK(mq.numel() == nb * 256 && vq.numel() == nb * 256, "adam8bit_step: state must be [nblocks, 256]");
   TORCH_CHECK(nb * 256 >= n, "adam8bit_step: too few blocks");
   const long long threads = nb * 32;
-  C10_CUDA_CHECK(odp::launch_pdl((odp::adam8bit_kernel), dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, at::cuda::getCurrentCUDAStream(), p.data_ptr<float>(), g.data_ptr<float>(), n, mq.data_ptr<int8_t>(), mabs.data_ptr<float>(),
-      vq.data_ptr<uint8_t>(), vlo.data_ptr<float>(), vsc.data_ptr<float>(), nb, blocks_per_group,
-      coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(), (float)b1, (float)b2,
-      (float)eps, (float)wd, first ? 1 : 0,
-      p16.has_value() ? reinterpret_cast<__nv_bfloat16*>(p16->data_ptr()) : nullptr));
+  auto al = [](const void* q, int a) { return reinterpret_cast<uintptr_t>(q) % a == 0; };
+  const bool vec = al(p.data_ptr(), 16) && al(g.data_ptr(), 16) && al(mq.data_ptr(), 8) && al(vq.data_ptr(), 8) &&
+                   (!p16.has_value() || al(p16->data_ptr(), 16));
+  auto kern = vec ? odp::adam8bit_kernel<true> : odp::adam8bit_kernel<false>;
+  C10_CUDA_CHECK(odp::launch_pdl(kern, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0,
+                                 at::cuda::getCurrentCUDAStream(), p.data_ptr<float>(), g.data_ptr<float>(), n,
+                                 mq.data_ptr<int8_t>(), mabs.data_ptr<float>(), vq.data_ptr<uint8_t>(),
+                                 vlo.data_ptr<float>(), vsc.data_ptr<float>(), nb, blocks_per_group,
+                                 coef.has_value() ? coef->data_ptr<float>() : nullptr, sched.data_ptr<float>(),
+                                 (float)b1, (float)b2, (float)eps, (float)wd, first ? 1 : 0,
+                                 p16.has_value() ? reinterpret_cast<__nv_bfloat16*>(p16->data_ptr()) : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -19,26 +19,42 @@
 namespace odp {
 
 __global__ void quant_int4_kernel(const float* __restrict__ x, long long n, uint8_t* __restrict__ packed,
-                                  float* __restrict__ scale, float* __restrict__ resid, long long ngroups) {
+                                  float* __restrict__ scale, float* __restrict__ resid, long long ngroups, int vec) {
   const long long grp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (grp >= ngroups) return;
   const long long e0 = grp * 128 + lane * 4;
+  const bool full = vec && e0 + 4 <= n;  // one 16-byte load and store per lane
   float v[4];
+  if (full) {
+    const float4 a = *reinterpret_cast<const float4*>(x + e0);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  } else {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) v[i] = e0 + i < n ? x[e0 + i] : 0.f;
+    for (int i = 0; i < 4; ++i) v[i] = e0 + i < n ? x[e0 + i] : 0.f;
+  }
   float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
   am = warp_max(am);
   const float s = am / 7.0f;
   const float safe = s > 0.f ? s : 1.f;
   int q[4];
+  float r[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     q[i] = (int)fminf(fmaxf(rintf(v[i] / safe), -7.f), 7.f);
-    if (resid && e0 + i < n) resid[e0 + i] = v[i] - __fmul_rn((float)q[i], s);  // no FMA: same rounding as the host
+    r[i] = v[i] - __fmul_rn((float)q[i], s);  // no FMA: same rounding as the host
   }
-  packed[grp * 64 + lane * 2] = (uint8_t)(((q[0] + 8) << 4) | (q[1] + 8));
-  packed[grp * 64 + lane * 2 + 1] = (uint8_t)(((q[2] + 8) << 4) | (q[3] + 8));
+  if (resid) {
+    if (full) {
+      *reinterpret_cast<float4*>(resid + e0) = make_float4(r[0], r[1], r[2], r[3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (e0 + i < n) resid[e0 + i] = r[i];
+    }
+  }
+  const uint16_t two = (uint16_t)((((q[0] + 8) << 4) | (q[1] + 8)) | ((((q[2] + 8) << 4) | (q[3] + 8)) << 8));
+  *reinterpret_cast<uint16_t*>(packed + grp * 64 + lane * 2) = two;  // bytes in order: (q0 q1), (q2 q3)
   if (lane == 0) scale[grp] = s;
 }
 
@@ -133,7 +149,11 @@ std::vector<torch::Tensor> quant_int4(torch::Tensor x, bool want_resid) {
   if (ng)
     odp::quant_int4_kernel<<<nblk(ng * 32, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
         xf.data_ptr<float>(), n, packed.data_ptr<uint8_t>(), scale.data_ptr<float>(),
-        want_resid ? resid.data_ptr<float>() : nullptr, ng);
+        want_resid ? resid.data_ptr<float>() : nullptr, ng,
+        reinterpret_cast<uintptr_t>(xf.data_ptr()) % 16 == 0 &&
+                (!want_resid || reinterpret_cast<uintptr_t>(resid.data_ptr()) % 16 == 0)
+            ? 1
+            : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {packed, scale, want_resid ? resid.view(x.sizes()) : resid};
 }

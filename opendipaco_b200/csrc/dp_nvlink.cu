@@ -217,13 +217,21 @@ __global__ void adam8bit_kernel(const long long* tab, int me, int d, int G, long
   const uint8_t* vq = row_ptr<const uint8_t>(tab, VQ, me);
   const float mscale = row_ptr<const float>(tab, MABS, me)[blk] / 127.f;
   const float lo = row_ptr<const float>(tab, VLO, me)[blk], vsc = row_ptr<const float>(tab, VSC, me)[blk];
+  // every load of the lane in flight at once (16-byte gradient / weight loads, 8-byte codes)
+  const float4 g0 = *reinterpret_cast<const float4*>(gr + e0), g1 = *reinterpret_cast<const float4*>(gr + e0 + 4);
+  const float4 w0 = *reinterpret_cast<const float4*>(pw + e0), w1 = *reinterpret_cast<const float4*>(pw + e0 + 4);
+  const uint2 mcode = *reinterpret_cast<const uint2*>(mq + q0), vcode = *reinterpret_cast<const uint2*>(vq + q0);
+  const float gin[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+  const float win[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const int8_t* mc = reinterpret_cast<const int8_t*>(&mcode);
+  const uint8_t* vc = reinterpret_cast<const uint8_t*>(&vcode);
   float mv[8], vv[8], lv[8];
   float amax = 0.f, lmin = INFINITY, lmax = -INFINITY;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const float gv = gr[e0 + k] * cf;
-    const float m0 = (float)mq[q0 + k] * mscale;
-    const float v0 = first_step ? 0.f : __expf((float)vq[q0 + k] * vsc + lo);
+    const float gv = gin[k] * cf;
+    const float m0 = (float)mc[k] * mscale;
+    const float v0 = first_step ? 0.f : __expf((float)vc[k] * vsc + lo);
     mv[k] = m0 * b1 + (1.f - b1) * gv;
     vv[k] = v0 * b2 + (1.f - b2) * gv * gv;
     amax = fmaxf(amax, fabsf(mv[k]));
@@ -246,7 +254,7 @@ __global__ void adam8bit_kernel(const long long* tab, int me, int d, int G, long
     mo[k / 4] |= mb << (8 * (k % 4));
     vo[k / 4] |= vb << (8 * (k % 4));
     const float den = sqrtf(vv[k]) / bc2s + eps;
-    po[k] = pw[e0 + k] * decay - step_size * (mv[k] / den);
+    po[k] = win[k] * decay - step_size * (mv[k] / den);
   }
   const float4 p0 = make_float4(po[0], po[1], po[2], po[3]), p1 = make_float4(po[4], po[5], po[6], po[7]);
   const uint4 b16 = make_uint4(pack_bf16(po[0], po[1]), pack_bf16(po[2], po[3]), pack_bf16(po[4], po[5]),
