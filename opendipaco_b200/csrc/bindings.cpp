@@ -22,6 +22,10 @@ void embedding_bwd(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tens
 void embedding_bwd_sorted(torch::Tensor ids, torch::Tensor dx, int64_t sdx, torch::Tensor dE, int64_t se, int64_t M,
                           int64_t H, int64_t G, int64_t V, torch::Tensor keys, c10::optional<torch::Tensor> rows,
                           c10::optional<torch::Tensor> sq);
+void gemm_ce_grad(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tensor B, int64_t ldb, int64_t sb,
+                  bool b_mn, torch::Tensor C, int64_t ldc, int64_t sc, int64_t M, int64_t N, int64_t K, int64_t G,
+                  double beta, torch::Tensor err, c10::optional<torch::Tensor> sq_part, int64_t sq_ld, int64_t xf,
+                  torch::Tensor ob, torch::Tensor labels, torch::Tensor scale, int64_t ms, int64_t split);
 void gemm_splitk_reduce(torch::Tensor ws, int64_t S, int64_t G, int64_t M, int64_t N, torch::Tensor C, int64_t ldc,
                         int64_t sc, c10::optional<torch::Tensor> sq_part, int64_t sq_ld, double beta);
 void grad_clip_coef_parts(torch::Tensor parts, int64_t nslot, torch::Tensor esq, int64_t M, torch::Tensor grads,
@@ -44,7 +48,8 @@ void attention_bwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, i
                          torch::Tensor delta, torch::Tensor dqkv, torch::Tensor err);
 void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t M, int64_t V, int64_t G,
               torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum, torch::Tensor inv_count,
-              c10::optional<torch::Tensor> loss_out, torch::Tensor err, c10::optional<torch::Tensor> inv_given);
+              c10::optional<torch::Tensor> loss_out, torch::Tensor err, c10::optional<torch::Tensor> inv_given,
+              c10::optional<torch::Tensor> ob);
 void dp_barrier(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, torch::Tensor err);
 void dp_grad_reduce_norm(torch::Tensor tab, torch::Tensor counter, int64_t me, int64_t d, int64_t G, int64_t P,
                          int64_t stride, int64_t s0, int64_t s1, torch::Tensor part, double max_norm,
@@ -66,7 +71,7 @@ void ce_group_sum(torch::Tensor row_loss, torch::Tensor labels, int64_t M, int64
                   torch::Tensor inv_count, c10::optional<torch::Tensor> loss_out, c10::optional<torch::Tensor> inv_given);
 void ce_rows_chunk(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t Mc, int64_t ms,
                    int64_t V, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor inv,
-                   c10::optional<torch::Tensor> part, int64_t T, torch::Tensor err);
+                   c10::optional<torch::Tensor> part, int64_t T, torch::Tensor err, c10::optional<torch::Tensor> ob);
 void grad_clip_coef(torch::Tensor grads, int64_t P, int64_t sg, int64_t G, double max_norm, torch::Tensor work,
                     torch::Tensor coef, c10::optional<torch::Tensor> norm_out, c10::optional<torch::Tensor> rows,
                     int64_t r0, int64_t H, int64_t V);
@@ -114,6 +119,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "opendipaco_b200 sm_100a kernels";
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_splitk_reduce", &gemm_splitk_reduce);
+  m.def("gemm_ce_grad", &gemm_ce_grad);
   m.def("grad_clip_coef_parts", &grad_clip_coef_parts);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_fwd_rpw", &rmsnorm_fwd_rpw);
@@ -125,7 +131,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd_tc", &attention_fwd_tc);
   m.def("attention_fwd_flash", &attention_fwd_flash);
   m.def("attention_bwd_flash", &attention_bwd_flash);
-  m.def("ce_fused", &ce_fused);
+  m.def("ce_fused", &ce_fused, py::arg("logits"), py::arg("ldl"), py::arg("sl"), py::arg("labels"), py::arg("M"),
+        py::arg("V"), py::arg("G"), py::arg("lse"), py::arg("row_loss"), py::arg("loss_sum"), py::arg("inv_count"),
+        py::arg("loss_out"), py::arg("err"), py::arg("inv_given"), py::arg("ob") = py::none());
   m.def("embedding_bwd_sorted", &embedding_bwd_sorted);
   m.def("dp_barrier", &dp_barrier);
   m.def("dp_grad_reduce_norm", &dp_grad_reduce_norm);
@@ -139,7 +147,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_rows", &cross_entropy_rows);
   m.def("ce_label_count", &ce_label_count);
   m.def("ce_group_sum", &ce_group_sum);
-  m.def("ce_rows_chunk", &ce_rows_chunk);
+  m.def("ce_rows_chunk", &ce_rows_chunk, py::arg("logits"), py::arg("ldl"), py::arg("sl"), py::arg("labels"),
+        py::arg("Mc"), py::arg("ms"), py::arg("V"), py::arg("G"), py::arg("lse"), py::arg("row_loss"), py::arg("inv"),
+        py::arg("part"), py::arg("T"), py::arg("err"), py::arg("ob") = py::none());
   m.def("grad_clip_coef", &grad_clip_coef);
   m.def("adamw_step", &adamw_step);
   m.def("adam8bit_step", &adam8bit_step);

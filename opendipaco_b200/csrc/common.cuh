@@ -104,6 +104,33 @@ ODP_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
   }
 }
 
+// The same wait with cluster-scope acquire: for a phase completed by arrivals of the
+// peer CTA of a pair (its shared-memory writes, released at cluster scope, are then
+// visible to what this thread issues next, tensor-core reads included).
+ODP_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+ODP_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code,
+                                  unsigned long long bound_ns = kWaitBoundNs) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  unsigned long long t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (globaltimer() - t0 > bound_ns) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 ODP_DEVICE void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -284,6 +311,20 @@ ODP_DEVICE void umma_commit_pair(uint64_t* bar) {
 
 // ---------------------------------------------------------------- misc
 ODP_DEVICE float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+// ---------------------------------------------------------------- cross-entropy gradient
+// dlogits of one row with natural log-sum-exp l and batch scale sc (1 / valid labels):
+//   d = exp(x - l) * sc = 2^(x log2e - ob),  ob = l log2e - log2(sc),
+// the label's column minus sc. The CE kernels and the LM-head gradient GEMMs (which form
+// dlogits from the logits while staging their A operand) share these two functions, so
+// both produce the same bits.
+constexpr float kCeLog2e = 1.4426950408889634f;
+ODP_DEVICE float ce_ob(float l, float sc) { return __fmaf_rn(l, kCeLog2e, -log2f(sc)); }
+ODP_DEVICE float ce_exp(float x, float ob) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmaf_rn(x, kCeLog2e, -ob)));
+  return y;
+}
 
 ODP_DEVICE uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

@@ -56,6 +56,18 @@ struct GemmParams {
   int f_half;  // swiglu: F (rows of the gate block; up block starts at row F)
   int tma_store;  // bf16 / logits with BN 128: stage each warp's 32 x 64 sub-tile in smem, TMA-store it
   int* err;
+  // Softmax-gradient operand (gemm_ce_grad): A holds bf16 logits and is turned into the CE
+  // dlogits in shared memory before the MMAs read it. xf = 1: A = logits [tokens, vocab]
+  // (K-major, K = vocab; the input gradient); xf = 2: A = logits^T (MN-major, M = vocab,
+  // K = tokens; the weight gradient). Per token of path g: ob = ce_ob(lse, sc) and the
+  // label at xf_ob / xf_lab [g * xf_ms + token] (label < 0: row ignored), sc = xf_sc[g].
+  // GEMM group gg is path gg / xf_split, token offset (gg % xf_split) * K (split-K).
+  int xf;
+  const float* xf_ob;
+  const int* xf_lab;
+  const float* xf_sc;
+  long long xf_ms;
+  int xf_split;
 };
 
 constexpr int BM = 128;
@@ -68,6 +80,7 @@ constexpr int tmem_cols(int bn) {
   return c;
 }
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kThreadsXF = 448;  // + warps 10-13: softmax-gradient transform of the A operand
 
 // Staging bytes per epilogue warp: one 4 KB box for bf16 / logits outputs, two for the
 // other epilogues of the single-CTA kernel (two fp32 boxes in flight, or the three bf16
@@ -735,6 +748,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, tmem_cols(BN));
 }
 
+// ============================================================== softmax-gradient operand
+// One 64-element slab of dlogits in place: 8 x 16-byte chunks of bf16 logits at `row`
+// (swizzled chunk order), element e of chunk j at index base + 8 j + e along the vocab.
+// Same arithmetic as the CE kernel's pass 3 (ce_exp, RNE to bf16, label column minus sc).
+ODP_DEVICE void xf_slab(uint8_t* row, int swz, float ob, float sc, int y, int base) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4* c = reinterpret_cast<uint4*>(row + ((j ^ swz) << 4));
+    if (y < 0) {
+      *c = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const uint4 v = *c;
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int col = base + 8 * j + 2 * e;
+      float lo = ce_exp(__uint_as_float(w[e] << 16), ob);
+      float hi = ce_exp(__uint_as_float(w[e] & 0xffff0000u), ob);
+      if (col == y) lo -= sc;
+      if (col + 1 == y) hi -= sc;
+      o[e] = pack_bf16(lo, hi);
+    }
+    *c = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // ============================================================== CTA-pair variant
 // The same GEMM with each output tile (256 x BN) computed by a pair of CTAs on two SMs
 // (cluster of 2, tcgen05.mma.cta_group::2): each CTA loads its own 128 rows of A and its
@@ -757,8 +798,8 @@ struct SmemLayout2 {
   static_assert(TOTAL <= 232448, "shared memory budget");
 };
 
-template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI, int XF = 0>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(XF ? kThreadsXF : kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
   using L = SmemLayout2<BN, STAGES>;
@@ -774,7 +815,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* accfull = empty + STAGES;
   uint64_t* accempty = accfull + 2;
   uint64_t* wbar = accempty + 2;  // one per epilogue warp: inputs of the TMA-store epilogue
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(wbar + 8);
+  uint64_t* afull = wbar + 8;      // XF: this CTA's A tile of a stage has landed
+  uint64_t* xdone = afull + STAGES;  // XF (leader): both CTAs' A tiles of a stage are transformed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xdone + STAGES);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
@@ -791,6 +834,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&accempty[b], 16);  // one arrive per epilogue warp of both CTAs
     }
     for (int w = 0; w < 8; ++w) mbar_init(&wbar[w], 1);
+    if constexpr (XF != 0) {
+      for (int s = 0; s < STAGES; ++s) {
+        mbar_init(&afull[s], 1);
+        mbar_init(&xdone[s], 8);  // one arrival per transform warp of both CTAs
+      }
+    }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -825,14 +874,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           uint8_t* sA = smem + stage * L::STAGE_BYTES;
           uint8_t* sB = sA + L::A_BYTES;
-          if (leader) mbar_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
           const uint32_t fb = full_leader + stage * 8;
           const int k0 = kb * BK;
-          if constexpr (!A_MN) {
-            tma_load_3d_pair(&tmA, fb, sA, k0, row0, g);
+          if constexpr (XF != 0) {
+            // A lands on this CTA's own barrier (its transform warps rewrite it); the
+            // leader's barrier counts only the B halves of both CTAs
+            if (leader) mbar_expect_tx(&full[stage], 2 * L::B_BYTES);
+            mbar_expect_tx(&afull[stage], L::A_BYTES);
+            if constexpr (!A_MN) {
+              tma_load_3d(&tmA, &afull[stage], sA, k0, row0, g);
+            } else {
+              tma_load_3d(&tmA, &afull[stage], sA, row0, k0, g);
+              tma_load_3d(&tmA, &afull[stage], sA + 8192, row0 + 64, k0, g);
+            }
           } else {
-            tma_load_3d_pair(&tmA, fb, sA, row0, k0, g);
-            tma_load_3d_pair(&tmA, fb, sA + 8192, row0 + 64, k0, g);
+            if (leader) mbar_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
+            if constexpr (!A_MN) {
+              tma_load_3d_pair(&tmA, fb, sA, k0, row0, g);
+            } else {
+              tma_load_3d_pair(&tmA, fb, sA, row0, k0, g);
+              tma_load_3d_pair(&tmA, fb, sA + 8192, row0 + 64, k0, g);
+            }
           }
           if constexpr (!B_MN) {
             tma_load_3d_pair(&tmB, fb, sB, k0, col0, g);
@@ -880,6 +942,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if constexpr (XF != 0) {
+            if (!mbar_wait_cluster(&xdone[stage], phase, p.err, ERR_TIMEOUT_FULL)) {
+              ok = false;
+              break;
+            }
+          }
           tc_fence_after();
           if (lane == 0) {
             const uint32_t aaddr = smem_u32(smem + stage * L::STAGE_BYTES);
@@ -907,6 +975,62 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         acc ^= 1;
         if (acc == 0) accphase ^= 1;
+      }
+    }
+  } else if (XF != 0 && warp >= 10) {
+    // ------------------------------------------------------------ A transform (both CTAs)
+    // logits -> dlogits in shared memory, stage by stage, then one arrival per warp on the
+    // leader's xdone barrier (shared-memory writes fenced to the async proxy first)
+    const int tid = (warp - 10) * 32 + lane;  // 0..127
+    const uint32_t xdone_leader = mapa_rank(&xdone[0], 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+      const int gg = t / tiles_per_g, r = t % tiles_per_g;
+      const int tm = r / p.tiles_n;
+      const int path = gg / p.xf_split;
+      const long long tok0 = (long long)(gg % p.xf_split) * p.K;  // token offset of this split
+      const float sc = p.xf_sc[path];
+      const int row0 = tm * 2 * BM + (int)rank * BM;
+      float ob = 0.f;
+      int y = -1;
+      if (XF == 1) {  // one token per thread for the whole tile: row tid of A
+        const long long tok = row0 + tid;
+        if (tok < p.M) {
+          y = p.xf_lab[path * p.xf_ms + tok];
+          ob = p.xf_ob[path * p.xf_ms + tok];
+        }
+      }
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&afull[stage], phase, p.err, ERR_TIMEOUT_FULL)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sA = smem + stage * L::STAGE_BYTES;
+        if constexpr (XF == 1) {
+          // K-major: row tid holds vocab columns [kb * 64, kb * 64 + 64) of token row0 + tid
+          xf_slab(sA + tid * 128, tid & 7, ob, sc, y, kb * BK);
+        } else {
+          // MN-major: 64 token rows x (two 64-vocab halves); thread = (token k, half h)
+          const int k = tid & 63, h = tid >> 6;
+          const long long tok = (long long)kb * BK + k;
+          int yk = -1;
+          float obk = 0.f;
+          if (tok < p.K) {
+            yk = p.xf_lab[path * p.xf_ms + tok0 + tok];
+            obk = p.xf_ob[path * p.xf_ms + tok0 + tok];
+          }
+          xf_slab(sA + h * 8192 + k * 128, k & 7, obk, sc, yk, row0 + h * 64);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(xdone_leader + stage * 8);
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
     }
   } else {
@@ -1051,11 +1175,11 @@ static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
+template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI, int XF = 0>
 static void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mx,
                         GemmParams& p, cudaStream_t st, int max_ctas) {
   using L = SmemLayout2<BN, STAGES>;
-  auto kern = gemm2_kernel<A_MN, B_MN, BN, STAGES, EPI>;
+  auto kern = gemm2_kernel<A_MN, B_MN, BN, STAGES, EPI, XF>;
   static bool attr_set = false;
   if (!attr_set) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
@@ -1063,7 +1187,7 @@ static void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   }
   int grid = std::min(2 * p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
   grid &= ~1;  // whole CTA pairs
-  C10_CUDA_CHECK(odp::launch_pdl(kern, dim3(grid), dim3(kThreads), L::TOTAL, st, ma, mb, mc, mx, p));
+  C10_CUDA_CHECK(odp::launch_pdl(kern, dim3(grid), dim3(XF ? kThreadsXF : kThreads), L::TOTAL, st, ma, mb, mc, mx, p));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1128,6 +1252,26 @@ static bool dispatch_pair(const Operand& A, const Operand& B, GemmParams& p, cud
     }
     TORCH_CHECK(tma_ok || !p.sqp, "gemm: box sums of squares need a TMA-storable fp32 output");
     p.tma_store = tma_ok ? 1 : 0;
+    if constexpr (EPI == EPI_F32) {
+      if (p.xf) {
+        // softmax-gradient operand: the LM-head input gradient (A K-major, B MN-major) and
+        // weight gradient (both MN-major)
+        TORCH_CHECK((p.xf == 1 && !A.mn && B.mn) || (p.xf == 2 && A.mn && B.mn),
+                    "gemm_ce_grad: unsupported operand layout");
+#define ODP_GOX(AM, BNV, ST, X)                                                                          \
+  if (A.mn == AM && bn == BNV && p.xf == X) {                                                            \
+    launch_pair<AM, true, BNV, fit_stages((BM + BNV / 2) * BK * 2, 8 * 4096, ST), EPI, X>(ma, mb, mc, mx, p, \
+                                                                                        st, max_ctas);   \
+    return true;                                                                                         \
+  }
+        ODP_GOX(false, 256, 6, 1)
+        ODP_GOX(false, 192, 7, 1)
+        ODP_GOX(true, 256, 6, 2)
+        ODP_GOX(true, 192, 7, 2)
+#undef ODP_GOX
+        return false;
+      }
+    }
 #define ODP_GO2(AM, BMN, BNV, ST)                                                                        \
   if constexpr (cfg2_ok<EPI, AM, BMN, BNV>()) {                                                          \
     if (A.mn == AM && B.mn == BMN && bn == BNV) {                                                        \
@@ -1152,6 +1296,7 @@ static bool dispatch_pair(const Operand& A, const Operand& B, GemmParams& p, cud
 template <int EPI>
 static void dispatch(const Operand& A, const Operand& B, GemmParams& p, int bn, cudaStream_t st, int max_ctas) {
   if (dispatch_pair<EPI>(A, B, p, st, max_ctas)) return;
+  TORCH_CHECK(!p.xf, "gemm_ce_grad: needs the CTA-pair kernel (M >= 256 and N a multiple of 192 or 256)");
   const int rowsB = EPI == EPI_SWIGLU ? bn / 2 : bn;
   CUtensorMap ma = A.mn ? make_map(A.ptr, p.M, p.K, A.ld, p.G, A.sg, 64) : make_map(A.ptr, p.K, p.M, A.ld, p.G, A.sg, BM);
   long long b_rows_extent = EPI == EPI_SWIGLU ? 2LL * p.f_half : p.N;
@@ -1311,6 +1456,47 @@ void gemm_bf16(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tenso
     case EPI_LOGITS: dispatch<EPI_LOGITS>(a, b, p, (int)bn, st, (int)max_ctas); break;
     default: TORCH_CHECK(false, "unknown epilogue ", epi);
   }
+}
+
+// fp32 GEMM whose A operand is bf16 logits turned into the cross-entropy dlogits on the fly
+// (the CE kernel's stats-only form wrote ob per token): xf = 1 for the LM-head input
+// gradient (A = logits [tokens, vocab], K-major), xf = 2 for its weight gradient (A =
+// logits^T, MN-major, K = tokens, optionally split over K into xf_split parts that run as
+// G * xf_split groups). ob / labels: [paths][ms] with the token rows this GEMM sees at
+// offset 0; sc: [paths] (1 / valid labels). The logits are only read.
+void gemm_ce_grad(torch::Tensor A, int64_t lda, int64_t sa, bool a_mn, torch::Tensor B, int64_t ldb, int64_t sb,
+                  bool b_mn, torch::Tensor C, int64_t ldc, int64_t sc, int64_t M, int64_t N, int64_t K, int64_t G,
+                  double beta, torch::Tensor err, c10::optional<torch::Tensor> sq_part, int64_t sq_ld, int64_t xf,
+                  torch::Tensor ob, torch::Tensor labels, torch::Tensor scale, int64_t ms, int64_t split) {
+  using namespace odp;
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm_ce_grad: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_ce_grad: bf16 operands");
+  TORCH_CHECK(xf == 1 || xf == 2, "gemm_ce_grad: xf is 1 (input gradient) or 2 (weight gradient)");
+  TORCH_CHECK(ob.scalar_type() == at::kFloat && labels.scalar_type() == at::kInt && scale.scalar_type() == at::kFloat,
+              "gemm_ce_grad: fp32 ob / scale, int32 labels");
+  TORCH_CHECK(split >= 1 && G % split == 0, "gemm_ce_grad: G must be a multiple of split");
+  c10::cuda::CUDAGuard guard(A.device());
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.G = (int)G;
+  p.num_kb = (int)((K + BK - 1) / BK);
+  p.C = C.data_ptr();
+  p.ldc = ldc;
+  p.sc = sc;
+  p.sqp = sq_part.has_value() ? sq_part->data_ptr<float>() : nullptr;
+  p.sq_ld = sq_ld;
+  p.beta = (float)beta;
+  p.err = err.data_ptr<int>();
+  p.xf = (int)xf;
+  p.xf_ob = ob.data_ptr<float>();
+  p.xf_lab = labels.data_ptr<int>();
+  p.xf_sc = scale.data_ptr<float>();
+  p.xf_ms = ms;
+  p.xf_split = (int)split;
+  Operand a{A.data_ptr(), lda, sa, a_mn}, b{B.data_ptr(), ldb, sb, b_mn};
+  dispatch<EPI_F32>(a, b, p, 192, at::cuda::getCurrentCUDAStream(), 0);
 }
 
 // ws: [G * S][M][N] fp32 split partials (group-major); C: G groups of [M][N] at (ldc, sc).

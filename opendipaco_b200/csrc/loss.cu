@@ -158,11 +158,15 @@ ODP_DEVICE float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 //   dlogits = (exp(x - lse) - onehot(label)) * inv_count[g]   written in place as bf16.
 // Rows with label < 0 get loss 0 and zero dlogits. 64 KB per CTA: three CTAs per SM
 // overlap one row's copy with another's arithmetic.
+// GRAD = false (ce_stats): passes 1 and 2 only -- the logits are read, not rewritten -- and
+// ob = ce_ob(lse, sc) is written per row for the LM-head gradient GEMMs, which form the
+// same dlogits from the logits while staging their operand.
+template <bool GRAD>
 __global__ void __launch_bounds__(kCeThreads) ce_fused_kernel(__nv_bfloat16* logits, long long ldl, long long sl,
                                                               const int* __restrict__ labels, int M, int V,
                                                               const float* __restrict__ inv_count,
                                                               float* __restrict__ lse_out, float* __restrict__ row_loss,
-                                                              int* err, long long ms) {
+                                                              int* err, long long ms, float* __restrict__ ob_out) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t ce_smem[];
@@ -175,10 +179,12 @@ __global__ void __launch_bounds__(kCeThreads) ce_fused_kernel(__nv_bfloat16* log
   const int nvec = V / 8;
   const int y = labels[r];
   if (y < 0) {
-    for (int i = threadIdx.x; i < nvec; i += kCeThreads) row[i] = make_uint4(0, 0, 0, 0);
+    if (GRAD)
+      for (int i = threadIdx.x; i < nvec; i += kCeThreads) row[i] = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
       row_loss[r] = 0.f;
       lse_out[r] = 0.f;
+      if (!GRAD) ob_out[r] = 0.f;
     }
     return;
   }
@@ -240,19 +246,22 @@ __global__ void __launch_bounds__(kCeThreads) ce_fused_kernel(__nv_bfloat16* log
   }
   // pass 3: dlogits = exp(x - lse) * sc = 2^(x log2e - (lse log2e - log2 sc)), the label's
   // column minus sc afterwards by the thread that wrote its 16-byte group
-  const float ob = l * kLog2e - log2f(sc);
+  const float ob = ce_ob(l, sc);
+  if (!GRAD) {
+    if (threadIdx.x == 0) ob_out[r] = ob;
+    return;
+  }
   for (int i = threadIdx.x; i < nvec; i += kCeThreads) {
     const uint4 v = srow[i];
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     uint32_t o[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
-      o[e] = pack_bf16(ex2_approx(fmaf(bf_lo(w[e]), kLog2e, -ob)), ex2_approx(fmaf(bf_hi(w[e]), kLog2e, -ob)));
+    for (int e = 0; e < 4; ++e) o[e] = pack_bf16(ce_exp(bf_lo(w[e]), ob), ce_exp(bf_hi(w[e]), ob));
     row[i] = make_uint4(o[0], o[1], o[2], o[3]);
   }
   if ((y / 8) % kCeThreads == (int)threadIdx.x) {
     const float xy = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(ce_smem)[y] << 16);
-    rowp[y] = __float2bfloat16(ex2_approx(fmaf(xy, kLog2e, -ob)) - sc);
+    rowp[y] = __float2bfloat16(ce_exp(xy, ob) - sc);
   }
 }
 
@@ -309,31 +318,44 @@ void ce_forward(torch::Tensor part, int64_t T, torch::Tensor logits, int64_t ldl
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+static void ce_attrs() {
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::ce_fused_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        odp::kCeMaxV * 2));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::ce_fused_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        odp::kCeMaxV * 2));
+    attr = true;
+  }
+}
+
 // Loss and dlogits in one pass over bf16 logits [G][M][V] (row stride ldl, group stride sl):
 // lse, row_loss per row, loss_sum / inv_count / optional per-group mean loss per group;
-// logits are overwritten with dlogits = (softmax - onehot) / count.
+// logits are overwritten with dlogits = (softmax - onehot) / count. With `ob` the logits are
+// only read: ob = ce_ob(lse, 1 / count) per row is written instead, for GEMMs that form the
+// dlogits themselves (gemm_ce_grad).
 void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t M, int64_t V, int64_t G,
               torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum, torch::Tensor inv_count,
-              c10::optional<torch::Tensor> loss_out, torch::Tensor err, c10::optional<torch::Tensor> inv_given) {
+              c10::optional<torch::Tensor> loss_out, torch::Tensor err, c10::optional<torch::Tensor> inv_given,
+              c10::optional<torch::Tensor> ob) {
   TORCH_CHECK(V % 8 == 0 && ldl % 8 == 0 && sl % 8 == 0 && V <= odp::kCeMaxV,
               "ce_fused: vocab must be a multiple of 8 and at most 32768");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0, "ce_fused: logits must be 16-byte aligned");
   c10::cuda::CUDAGuard guard(logits.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  static bool attr = false;
-  if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(odp::ce_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        odp::kCeMaxV * 2));
-    attr = true;
-  }
+  ce_attrs();
   const float* given = inv_given.has_value() ? inv_given->data_ptr<float>() : nullptr;
   if (!given) {
     C10_CUDA_CHECK(odp::launch_pdl((odp::label_count_kernel), dim3((int)G), dim3(256), 0, st, labels.data_ptr<int>(), (int)M, inv_count.data_ptr<float>()));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
-  C10_CUDA_CHECK(odp::launch_pdl((odp::ce_fused_kernel), dim3((unsigned)(G * M)), dim3(odp::kCeThreads), (size_t)V * 2, st, reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)M, (int)V,
-      given ? given : inv_count.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(),
-      err.data_ptr<int>(), (long long)M));
+  C10_CUDA_CHECK(odp::launch_pdl(ob.has_value() ? odp::ce_fused_kernel<false> : odp::ce_fused_kernel<true>,
+                                 dim3((unsigned)(G * M)), dim3(odp::kCeThreads), (size_t)V * 2, st,
+                                 reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl,
+                                 labels.data_ptr<int>(), (int)M, (int)V,
+                                 given ? given : inv_count.data_ptr<float>(), lse.data_ptr<float>(),
+                                 row_loss.data_ptr<float>(), err.data_ptr<int>(), (long long)M,
+                                 ob.has_value() ? ob->data_ptr<float>() : nullptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   C10_CUDA_CHECK(odp::launch_pdl((odp::group_sum_kernel), dim3((int)G), dim3(256), 0, st, row_loss.data_ptr<float>(), labels.data_ptr<int>(), (int)M,
                                                  loss_sum.data_ptr<float>(), inv_count.data_ptr<float>(),
@@ -379,24 +401,24 @@ void ce_group_sum(torch::Tensor row_loss, torch::Tensor labels, int64_t M, int64
 // `part` ([G][Mc][T] float2) and then rewrite the logits.
 void ce_rows_chunk(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t Mc, int64_t ms,
                    int64_t V, int64_t G, torch::Tensor lse, torch::Tensor row_loss, torch::Tensor inv,
-                   c10::optional<torch::Tensor> part, int64_t T, torch::Tensor err) {
+                   c10::optional<torch::Tensor> part, int64_t T, torch::Tensor err, c10::optional<torch::Tensor> ob) {
   TORCH_CHECK(V % 8 == 0 && ldl % 8 == 0 && sl % 8 == 0, "ce_rows_chunk: vocab and strides multiples of 8");
   c10::cuda::CUDAGuard guard(logits.device());
   auto st = at::cuda::getCurrentCUDAStream();
   if (!part.has_value()) {
     TORCH_CHECK(V <= odp::kCeMaxV && reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0,
                 "ce_rows_chunk: the one-pass kernel takes at most 32768 columns, 16-byte aligned rows");
-    static bool attr = false;
-    if (!attr) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(odp::ce_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          odp::kCeMaxV * 2));
-      attr = true;
-    }
-    C10_CUDA_CHECK(odp::launch_pdl((odp::ce_fused_kernel), dim3((unsigned)(G * Mc)), dim3(odp::kCeThreads), (size_t)V * 2, st, reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)Mc, (int)V,
-        inv.data_ptr<float>(), lse.data_ptr<float>(), row_loss.data_ptr<float>(), err.data_ptr<int>(), ms));
+    ce_attrs();
+    C10_CUDA_CHECK(odp::launch_pdl(ob.has_value() ? odp::ce_fused_kernel<false> : odp::ce_fused_kernel<true>,
+                                   dim3((unsigned)(G * Mc)), dim3(odp::kCeThreads), (size_t)V * 2, st,
+                                   reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), ldl, sl,
+                                   labels.data_ptr<int>(), (int)Mc, (int)V, inv.data_ptr<float>(),
+                                   lse.data_ptr<float>(), row_loss.data_ptr<float>(), err.data_ptr<int>(), ms,
+                                   ob.has_value() ? ob->data_ptr<float>() : nullptr));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }
+  TORCH_CHECK(!ob.has_value(), "ce_rows_chunk: the stats-only form needs the one-pass kernel (V <= 32768)");
   const int R = (int)(G * Mc);
   C10_CUDA_CHECK(odp::launch_pdl((odp::ce_finalize_kernel), dim3((R + 255) / 256), dim3(256), 0, st, reinterpret_cast<const float2*>(part->data_ptr<float>()), (int)T,
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), ldl, sl, labels.data_ptr<int>(), (int)Mc, (int)G,

@@ -101,6 +101,26 @@ def splitk_factor(M: int, N: int, K: int, G: int, sms: int | None = None) -> int
     return s
 
 
+def gemm_ce_wgrad(logits, ldl, sl, X, ldx, sx, C, ldc, sc, V, H, T, G, S, ws, ob, labels, scale, ms, sq_part=None,
+                  sq_ld=0, err=None, beta=0.0):
+    """LM-head weight gradient C[g] (V x H) = dlogits[g]^T X[g] with the dlogits formed from
+    the bf16 logits inside the GEMM (``gemm_ce_grad``, mode 2); T tokens, split over them
+    into S parts (workspace ``ws``, fixed-order reduction) like ``gemm_wgrad``."""
+    x = ext()
+    e = err if err is not None else err_word(logits.device)
+    if S <= 1:
+        x.gemm_ce_grad(logits, ldl, sl, True, X, ldx, sx, True, C, ldc, sc, V, H, T, G, beta, e, sq_part, sq_ld, 2, ob,
+                       labels, scale, ms, 1)
+        return C
+    if sl != T * ldl or sx != T * ldx or T % (S * 64):
+        raise ValueError("gemm_ce_wgrad: split-K needs contiguous groups along the tokens and T % (64 S) == 0")
+    ts = T // S
+    x.gemm_ce_grad(logits, ldl, ts * ldl, True, X, ldx, ts * ldx, True, ws, H, V * H, V, H, ts, G * S, 0.0, e, None, 0,
+                   2, ob, labels, scale, ms, S)
+    x.gemm_splitk_reduce(ws, S, G, V, H, C, ldc, sc, sq_part, sq_ld, beta)
+    return C
+
+
 def gemm_wgrad(A, lda, sa, B, ldb, sb, C, ldc, sc, M, N, K, G, S, ws, sq_part=None, sq_ld=0, err=None,
                beta=0.0, bn=128):
     """fp32 weight gradient C[g] = A[g] B[g]^T with both operands MN-major (K = tokens),

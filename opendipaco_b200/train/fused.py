@@ -342,6 +342,12 @@ class FusedExecutor:
         # one-pass CE keeps a row in registers (<= 32768 columns); wider vocabularies use GEMM partials
         self.ce_fused = V % 8 == 0 and V <= 32768 and os.environ.get("ODP_CE_IMPL", "fused") == "fused"
         self.PART = z(1) if self.ce_fused else z(G, self.MCH, self.T, 2)
+        # the LM-head gradient GEMMs form the dlogits from the logits (CTA-pair kernel:
+        # at least 256 rows per chunk and vocabulary, hidden a multiple of 192 or 256)
+        pairable = H >= 256 and (H % 256 == 0 or H % 192 == 0)
+        self.ce_xf = (self.ce_fused and pairable and self.MCH >= 256 and V >= 256 and self._side_ctas == 0
+                      and os.environ.get("ODP_CE_GRAD_FUSED", "1") != "0")
+        self.CEOB = z(G, M) if self.ce_xf else None
         self.LSEC = z(G, M)
         self.ROWLOSS = z(G, M)
         self.LOSSSUM = z(G)
@@ -476,11 +482,14 @@ class FusedExecutor:
         if len(self.chunks) > 1:
             self._lm_head_chunked(s, labels)
         elif self.ce_fused:
-            # plain bf16 logits (TMA-stored), then loss + dlogits in one pass over each row
+            # plain bf16 logits (TMA-stored), then loss + dlogits in one pass over each row --
+            # or, when the gradient GEMMs form the dlogits themselves, a read-only pass that
+            # leaves the logits in place and writes each row's exponent offset
             self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "bf16",
                        bn=128)
             X_.ce_fused(self.LOGITS, V, M * V, labels, M, V, G, self.LSEC, self.ROWLOSS, self.LOSSSUM, self.INVCNT,
-                        self.LOSSES[s], self.err, self.INVC[s] if self.dp > 1 else None)
+                        self.LOSSES[s], self.err, self.INVC[s] if self.dp > 1 else None,
+                        self.CEOB if self.ce_xf else None)
         else:
             self._gemm(self.XNF, H, MH, False, w16[lay.lm:], H, P, False, self.LOGITS, V, M * V, M, V, H, "logits",
                        bn=128, part=self.PART)
@@ -490,11 +499,14 @@ class FusedExecutor:
             X_.ce_backward(self.LOGITS, V, M * V, self.LSEC, labels, self.INVCNT if given is None else given, M, V,
                            G)
         # ---------------- backward
-        side = self._side if len(self.chunks) == 1 else None
+        side = self._side if len(self.chunks) == 1 and not self.ce_xf else None
         if len(self.chunks) == 1:
-            self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
-        if len(self.chunks) > 1:
-            pass  # the chunks already wrote DXN and the LM-head weight gradient
+            if self.ce_xf:
+                self._ce_grad_gemms(labels, self.INVC[s] if self.dp > 1 else self.INVCNT)
+            else:
+                self._gemm(self.LOGITS, V, M * V, False, w16[lay.lm:], H, P, True, self.DXN, H, MH, M, H, V, "f32")
+        if len(self.chunks) > 1 or self.ce_xf:
+            pass  # the chunks (or the softmax-gradient GEMMs) already wrote DXN and the LM-head weight gradient
         elif side is not None:
             # the LM-head weight gradient is needed only by the optimizer: on a side stream
             # with a capped grid it runs under the layers' backward, whose small GEMMs and
@@ -599,6 +611,30 @@ class FusedExecutor:
             self._gemm(self.ACT[k], Fd, MF, False, w16[lo.down:], Fd, P, False, self.X[l + 1], H, MH, M, H, Fd,
                        "resid", R=self.HR[k], ldr=H, sr=MH)
 
+    def _ce_grad_gemms(self, labels, scale, r0: int = 0, rows: int | None = None, beta: float = 0.0,
+                       last: bool = True) -> None:
+        """The LM-head input and weight gradients straight from the logits: the GEMMs turn
+        each staged logits tile into dlogits (exp(x - lse) / count, label column minus
+        1 / count; the same bits as the CE kernel's in-place form) before the MMAs read it,
+        so the logits are never rewritten. Rows [r0, r0 + rows) of every path; the weight
+        gradient is accumulated when ``beta`` is 1 (row chunks)."""
+        from ..ops.gemm import gemm_ce_wgrad
+
+        X_ = ext()
+        bb, G, P = self.bb, self.G, self.P
+        H, V, M = bb.hidden_size, bb.vocab_size, self.M
+        mc = M - r0 if rows is None else rows
+        lm = self.layout.lm
+        w16, gr = self.W16.view(-1), self.GRAD.view(-1)
+        lab, ob = labels.view(-1)[r0:], self.CEOB.view(-1)[r0:]
+        mch = self.LOGITS.shape[1]
+        X_.gemm_ce_grad(self.LOGITS, V, mch * V, False, w16[lm:], H, P, True, self.DXN.view(-1)[r0 * H:], H, M * H,
+                        mc, H, V, G, 0.0, self.err, None, 0, 1, ob, lab, scale, M, 1)
+        sq = self._sq("lm") if last else {}
+        gemm_ce_wgrad(self.LOGITS, V, mch * V, self.XNF.view(-1)[r0 * H:], H, M * H, gr[lm:], H, P, V, H, mc, G,
+                      1 if rows is not None else self.wg_split["lm"], self.WGWS, ob, lab, scale, M, sq.get("sq"),
+                      sq.get("sq_ld", 0), self.err, beta=beta)
+
     def _lm_head_chunked(self, s: int, labels) -> None:
         """LM head + loss over row chunks: per chunk the logits GEMM, the chunk's loss rows
         and in-place dlogits (scaled by the WHOLE batch's 1 / count), the input gradient of
@@ -631,7 +667,10 @@ class FusedExecutor:
                            bn=128, part=self.PART)
                 part = self.PART
             X_.ce_rows_chunk(self.LOGITS, V, mch * V, lab[r0:], mc, M, V, G, lse[r0:], rloss[r0:], inv, part,
-                             self.T, self.err)
+                             self.T, self.err, self.CEOB.view(-1)[r0:] if self.ce_xf else None)
+            if self.ce_xf:
+                self._ce_grad_gemms(labels, inv, r0, mc, beta=0.0 if ci == 0 else 1.0, last=ci == last)
+                continue
             self._gemm(self.LOGITS, V, mch * V, False, w16[lm:], H, P, True, dxn[r0 * H:], H, MH, mc, H, V, "f32")
             sq = self._sq("lm") if ci == last else {}
             gemm_wgrad(self.LOGITS, V, mch * V, a, H, MH, gr[lm:], H, P, V, H, mc, G, 1, self.WGWS, sq.get("sq"),

@@ -39,3 +39,49 @@ def test_ce_fused_matches_fp32_reference(G, M, V):
     err = (d.float() - ref_d).abs().max().item()
     assert err <= 2e-2 * ref_d.abs().max().item(), err
     assert torch.all(d.reshape(-1, V)[~valid] == 0)
+
+
+@pytest.mark.parametrize("G,M,V,H,S", [(2, 3072, 32000, 384, 1), (2, 300, 1000, 256, 1), (1, 512, 2048, 384, 2)])
+def test_ce_gradient_gemms_equal_in_place_dlogits_bitwise(G, M, V, H, S):
+    """The LM-head gradient GEMMs that form the dlogits from the logits while staging their
+    operand give the same bits as the in-place CE pass followed by the plain GEMMs: input
+    gradient (K = vocab), weight gradient (K = tokens; S > 1: split over the tokens),
+    ignored labels, partial tiles."""
+    from opendipaco_b200.ops import check_errors
+    from opendipaco_b200.ops._ext import err_word, ext
+    from opendipaco_b200.ops.gemm import gemm_ce_wgrad, gemm_wgrad
+
+    g = torch.Generator(device="cpu").manual_seed(M + V)
+    logits = (torch.randn(G, M, V, generator=g) * 3).to(DEV).to(torch.bfloat16)
+    labels = torch.randint(0, V, (G, M), generator=g).to(DEV).to(torch.int32)
+    labels[0, ::7] = -100
+    lab = labels.reshape(-1).contiguous()
+    W = (torch.randn(V, H, generator=g) * 0.05).to(DEV).to(torch.bfloat16)  # lm_head weight, one per group
+    Wg = W.unsqueeze(0).expand(G, V, H).contiguous()
+    X = (torch.randn(G, M, H, generator=g)).to(DEV).to(torch.bfloat16)
+    err = err_word(DEV)
+    mk = lambda *s: torch.empty(*s, device=DEV)  # noqa: E731
+    lse, rows, lsum, inv, loss = mk(G * M), mk(G * M), mk(G), mk(G), mk(G)
+    # reference: in-place dlogits, then the plain fp32 GEMMs
+    d = logits.clone()
+    ext().ce_fused(d, V, M * V, lab, M, V, G, lse, rows, lsum, inv, loss, err, None)
+    dx_ref, dw_ref = torch.zeros(G, M, H, device=DEV), torch.zeros(G, V, H, device=DEV)
+    from opendipaco_b200.ops.gemm import EPI
+
+    ext().gemm_bf16(d, V, M * V, False, Wg, H, V * H, True, dx_ref, H, M * H, M, H, V, G, EPI["f32"], 128, None, 0,
+                    0, None, 0, 0, None, 0.0, 0, err, 0, None, 0)
+    ws = torch.empty(G * S * V * H, device=DEV)
+    gemm_wgrad(d, V, M * V, X, H, M * H, dw_ref, H, V * H, V, H, M, G, S, ws, err=err)
+    # fused: the logits stay untouched; ob per row from the read-only CE pass
+    ob, lse2, rows2, lsum2, inv2, loss2 = mk(G * M), mk(G * M), mk(G * M), mk(G), mk(G), mk(G)
+    keep = logits.clone()
+    ext().ce_fused(keep, V, M * V, lab, M, V, G, lse2, rows2, lsum2, inv2, loss2, err, None, ob)
+    assert torch.equal(keep, logits) and torch.equal(loss2, loss) and torch.equal(lse2, lse)
+    dx, dw = torch.zeros_like(dx_ref), torch.zeros_like(dw_ref)
+    ext().gemm_ce_grad(keep, V, M * V, False, Wg, H, V * H, True, dx, H, M * H, M, H, V, G, 0.0, err, None, 0, 1, ob,
+                       lab, inv2, M, 1)
+    gemm_ce_wgrad(keep, V, M * V, X, H, M * H, dw, H, V * H, V, H, M, G, S, ws, ob, lab, inv2, M, err=err)
+    torch.cuda.synchronize()
+    check_errors()
+    assert torch.equal(dx, dx_ref)
+    assert torch.equal(dw, dw_ref)

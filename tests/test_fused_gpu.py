@@ -237,3 +237,23 @@ def test_loss_chunks_track_the_whole_batch(vocab_impl, monkeypatch):
         for p in x.per_path_loss:
             assert abs(x.per_path_loss[p] - y.per_path_loss[p]) < 1e-3 * x.per_path_loss[p], (p, x, y)
     assert _bank_maxdiff(a, b) < 2e-3
+
+
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_ce_gradient_gemms_train_bitwise_like_the_in_place_pass(chunks, monkeypatch):
+    """Hidden 256: the LM-head gradient GEMMs form the dlogits themselves (the logits are
+    read once by a stats-only CE pass and never rewritten); training is bit for bit the
+    run with the in-place CE pass, unchunked and with two loss chunks."""
+    bb = BackboneConfig(vocab_size=512, hidden_size=256, num_attention_heads=4, intermediate_size=512,
+                        layers_per_level=[1, 1], max_position_embeddings=128)
+    cfg = DiPaCoConfig(backbone=bb, level_sizes=[2, 2], sequence_length=64)
+    corpus = _corpus(cfg)
+    a = _engine(cfg, "cuda", loss_chunks=chunks)
+    ha = a.fit(corpus, 2, 8, log_every=0)
+    assert a._fused.ce_xf
+    monkeypatch.setenv("ODP_CE_GRAD_FUSED", "0")
+    b = _engine(cfg, "cuda", loss_chunks=chunks)
+    hb = b.fit(corpus, 2, 8, log_every=0)
+    assert not b._fused.ce_xf
+    assert [m.per_path_loss for m in ha] == [m.per_path_loss for m in hb]
+    assert _bank_equal(a, b)
