@@ -343,7 +343,7 @@ ODP_DEVICE void a8_load(const float* __restrict__ src, long long e0, long long n
 }
 
 template <bool VEC>
-__global__ void __launch_bounds__(256) adam8bit_kernel(float* __restrict__ p, const float* __restrict__ g, long long n,
+__global__ void __launch_bounds__(256, 4) adam8bit_kernel(float* __restrict__ p, const float* __restrict__ g, long long n,
                                                        int8_t* __restrict__ mq, float* __restrict__ mabs,
                                                        uint8_t* __restrict__ vq, float* __restrict__ vlo,
                                                        float* __restrict__ vsc, long long nblocks,

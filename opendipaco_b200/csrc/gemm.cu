@@ -152,7 +152,7 @@ ODP_DEVICE void load_bf16x32(const __nv_bfloat16* src, float* v) {
 
 // Epilogue of one tile for one thread: TMEM lane row q*32+lane, column half `ch`
 // (two warps share a lane quarter; each drains BN/2 columns).
-template <int BN, int EPI>
+template <int BN, int EPI, int STGW = 4096>
 ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int ch, int lane, int g, int tm,
                               int tn, uint8_t* stg, const CUtensorMap* tmC) {
   const int row = q * 32 + lane;
@@ -189,7 +189,35 @@ ODP_DEVICE void epilogue_tile(const GemmParams& p, uint32_t tmem_acc, int q, int
     store_bf16x32(GU, gg);
     store_bf16x32(GU + p.f_half, uu);
   } else {
-    if constexpr (EPI == EPI_BF16 && (BN == 128 || BN == 256)) {
+    if constexpr (EPI == EPI_BF16 && (BN == 128 || BN == 256) && STGW >= (BN / 2) * 64) {
+      if (p.tma_store) {
+        // every box of this warp's 32 x HALF slab staged at once: one proxy fence, then
+        // one TMA store per box (the buffer is free again once the previous tile's stores
+        // have been read out, long before)
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+#pragma unroll 1
+        for (int b = 0; b < HALF; b += 64)
+#pragma unroll 1
+          for (int c = 0; c < 64; c += 32) {
+            uint32_t r[32];
+            load32(tbase + ch * HALF + b + c, r);
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            stage_bf16x32(stg + (b / 64) * 4096, lane, c, v);
+          }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          for (int b = 0; b < HALF; b += 64)
+            tma_store_3d(tmC, stg + (b / 64) * 4096, tn * BN + ch * HALF + b, tm * BM + q * 32, g);
+          bulk_commit();
+        }
+        __syncwarp();
+        return;
+      }
+    } else if constexpr (EPI == EPI_BF16 && (BN == 128 || BN == 256)) {
       if (p.tma_store) {
 #pragma unroll 1
         for (int b = 0; b < HALF; b += 64) {  // one 32 x 64 box at a time through the 4 KB buffer
@@ -753,28 +781,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 // (swizzled chunk order), element e of chunk j at index base + 8 j + e along the vocab.
 // Same arithmetic as the CE kernel's pass 3 (ce_exp, RNE to bf16, label column minus sc).
 ODP_DEVICE void xf_slab(uint8_t* row, int swz, float ob, float sc, int y, int base) {
+  // all eight 16-byte loads first, then the 64 exponentials, then the stores: nothing
+  // orders a load after an earlier store of the slab, so the chunks overlap
+  uint4 v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = *reinterpret_cast<const uint4*>(row + ((j ^ swz) << 4));
+  const bool live = y >= 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    uint4* c = reinterpret_cast<uint4*>(row + ((j ^ swz) << 4));
-    if (y < 0) {
-      *c = make_uint4(0, 0, 0, 0);
-      continue;
-    }
-    const uint4 v = *c;
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
     uint32_t o[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int col = base + 8 * j + 2 * e;
-      float lo = ce_exp(__uint_as_float(w[e] << 16), ob);
-      float hi = ce_exp(__uint_as_float(w[e] & 0xffff0000u), ob);
-      if (col == y) lo -= sc;
-      if (col + 1 == y) hi -= sc;
-      o[e] = pack_bf16(lo, hi);
+      const float lo = ce_exp(__uint_as_float(w[e] << 16), ob);
+      const float hi = ce_exp(__uint_as_float(w[e] & 0xffff0000u), ob);
+      o[e] = pack_bf16(col == y ? lo - sc : lo, col + 1 == y ? hi - sc : hi);
     }
-    *c = make_uint4(o[0], o[1], o[2], o[3]);
+    v[j] = live ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0, 0, 0, 0);
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(row + ((j ^ swz) << 4)) = v[j];
 }
+
+// Staging bytes per epilogue warp of the pair kernel: a 256-wide bf16 tile stages both of a
+// warp's 32 x 64 boxes before one proxy fence and two TMA stores; other tiles one 4 KB box.
+constexpr int stg2_bytes(int epi, int bn) { return (epi == EPI_BF16 && bn == 256) ? 8192 : 4096; }
 
 // ============================================================== CTA-pair variant
 // The same GEMM with each output tile (256 x BN) computed by a pair of CTAs on two SMs
@@ -785,14 +817,14 @@ ODP_DEVICE void xf_slab(uint8_t* row, int swz, float ob, float sc, int y, int ba
 // on the leader CTA's mbarrier; the leader alone issues MMAs; commits arrive on both
 // CTAs' barriers; each CTA's epilogue drains its own 128 TMEM lanes and the peer's
 // epilogue warps release the accumulator on the leader's barrier remotely.
-template <int BN, int STAGES>
+template <int BN, int STAGES, int STGW = 4096>
 struct SmemLayout2 {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BN / 2) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static_assert(STAGE_BYTES % 1024 == 0, "stages start on a swizzle-atom boundary");
   static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-  static constexpr int STG_BYTES = 8 * 4096;  // one staging box per epilogue warp
+  static constexpr int STG_BYTES = 8 * STGW;  // STGW staging bytes per epilogue warp
   static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
   static constexpr int TOTAL = BAR_OFF + 512 + 1024;
   static_assert(TOTAL <= 232448, "shared memory budget");
@@ -802,7 +834,7 @@ template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI, int XF = 0>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(XF ? kThreadsXF : kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
-  using L = SmemLayout2<BN, STAGES>;
+  using L = SmemLayout2<BN, STAGES, stg2_bytes(EPI, BN)>;
   constexpr int HB = BN / 2;  // B rows held by each CTA
   // an MN-major B half that is not a whole number of 64-element 128-byte atoms (HB = 96)
   // is held as 32-element 64-byte-swizzled atoms
@@ -1001,6 +1033,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(XF ? kThreadsXF : kT
           y = p.xf_lab[path * p.xf_ms + tok];
           ob = p.xf_ob[path * p.xf_ms + tok];
         }
+      } else {  // the first k-block's token of this thread
+        const long long tok = tid & 63;
+        if (tok < p.K) {
+          y = p.xf_lab[path * p.xf_ms + tok0 + tok];
+          ob = p.xf_ob[path * p.xf_ms + tok0 + tok];
+        }
       }
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait(&afull[stage], phase, p.err, ERR_TIMEOUT_FULL)) {
@@ -1012,14 +1050,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(XF ? kThreadsXF : kT
           // K-major: row tid holds vocab columns [kb * 64, kb * 64 + 64) of token row0 + tid
           xf_slab(sA + tid * 128, tid & 7, ob, sc, y, kb * BK);
         } else {
-          // MN-major: 64 token rows x (two 64-vocab halves); thread = (token k, half h)
+          // MN-major: 64 token rows x (two 64-vocab halves); thread = (token k, half h).
+          // This k-block's (label, ob) were loaded during the previous one.
           const int k = tid & 63, h = tid >> 6;
-          const long long tok = (long long)kb * BK + k;
-          int yk = -1;
-          float obk = 0.f;
-          if (tok < p.K) {
-            yk = p.xf_lab[path * p.xf_ms + tok0 + tok];
-            obk = p.xf_ob[path * p.xf_ms + tok0 + tok];
+          const int yk = y;
+          const float obk = ob;
+          const long long nxt = (long long)(kb + 1) * BK + k;
+          y = -1;
+          if (kb + 1 < p.num_kb && nxt < p.K) {
+            y = p.xf_lab[path * p.xf_ms + tok0 + nxt];
+            ob = p.xf_ob[path * p.xf_ms + tok0 + nxt];
           }
           xf_slab(sA + h * 8192 + k * 128, k & 7, obk, sc, yk, row0 + h * 64);
         }
@@ -1038,7 +1078,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(XF ? kThreadsXF : kT
     const int q = warp % 4;
     const int ch = (warp - 2) / 4;
     const uint32_t accempty_leader = mapa_rank(&accempty[0], 0);
-    uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;
+    constexpr int STGW = stg2_bytes(EPI, BN);
+    uint8_t* stg = smem + L::STG_OFF + (warp - 2) * STGW;
     int acc = 0;
     uint32_t accphase = 0, wphase = 0;
     EpiCtx ectx{stg, 4096, &wbar[warp - 2], &wphase, &tmC, &tmX};
@@ -1051,9 +1092,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(XF ? kThreadsXF : kT
       bool ok = true;
       if constexpr (EPI == EPI_F32) {
         if (p.tma_store) ok = epilogue_tma<BN, EPI>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, ectx);
-        else epilogue_tile<BN, EPI>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, stg, &tmC);
+        else epilogue_tile<BN, EPI, STGW>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, stg, &tmC);
       } else {
-        epilogue_tile<BN, EPI>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, stg, &tmC);
+        epilogue_tile<BN, EPI, STGW>(p, tmem_base + acc * BN, q, ch, lane, g, tm * 2 + (int)rank, tn, stg, &tmC);
       }
       tc_fence_before();
       __syncwarp();
@@ -1178,7 +1219,7 @@ static void launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
 template <bool A_MN, bool B_MN, int BN, int STAGES, int EPI, int XF = 0>
 static void launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mx,
                         GemmParams& p, cudaStream_t st, int max_ctas) {
-  using L = SmemLayout2<BN, STAGES>;
+  using L = SmemLayout2<BN, STAGES, stg2_bytes(EPI, BN)>;
   auto kern = gemm2_kernel<A_MN, B_MN, BN, STAGES, EPI, XF>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -1260,7 +1301,7 @@ static bool dispatch_pair(const Operand& A, const Operand& B, GemmParams& p, cud
                     "gemm_ce_grad: unsupported operand layout");
 #define ODP_GOX(AM, BNV, ST, X)                                                                          \
   if (A.mn == AM && bn == BNV && p.xf == X) {                                                            \
-    launch_pair<AM, true, BNV, fit_stages((BM + BNV / 2) * BK * 2, 8 * 4096, ST), EPI, X>(ma, mb, mc, mx, p, \
+    launch_pair<AM, true, BNV, fit_stages((BM + BNV / 2) * BK * 2, 8 * stg2_bytes(EPI, BNV), ST), EPI, X>(ma, mb, mc, mx, p, \
                                                                                         st, max_ctas);   \
     return true;                                                                                         \
   }
@@ -1275,7 +1316,7 @@ static bool dispatch_pair(const Operand& A, const Operand& B, GemmParams& p, cud
 #define ODP_GO2(AM, BMN, BNV, ST)                                                                        \
   if constexpr (cfg2_ok<EPI, AM, BMN, BNV>()) {                                                          \
     if (A.mn == AM && B.mn == BMN && bn == BNV) {                                                        \
-      launch_pair<AM, BMN, BNV, fit_stages((BM + BNV / 2) * BK * 2, 8 * 4096, ST), EPI>(ma, mb, mc, mx, p, \
+      launch_pair<AM, BMN, BNV, fit_stages((BM + BNV / 2) * BK * 2, 8 * stg2_bytes(EPI, BNV), ST), EPI>(ma, mb, mc, mx, p, \
                                                                                         st, max_ctas);   \
       return true;                                                                                       \
     }                                                                                                    \

@@ -346,7 +346,7 @@ class FusedExecutor:
         # at least 256 rows per chunk and vocabulary, hidden a multiple of 192 or 256)
         pairable = H >= 256 and (H % 256 == 0 or H % 192 == 0)
         self.ce_xf = (self.ce_fused and pairable and self.MCH >= 256 and V >= 256 and self._side_ctas == 0
-                      and os.environ.get("ODP_CE_GRAD_FUSED", "1") != "0")
+                      and os.environ.get("ODP_CE_GRAD_FUSED", "0") == "1")
         self.CEOB = z(G, M) if self.ce_xf else None
         self.LSEC = z(G, M)
         self.ROWLOSS = z(G, M)

@@ -248,6 +248,7 @@ def test_ce_gradient_gemms_train_bitwise_like_the_in_place_pass(chunks, monkeypa
                         layers_per_level=[1, 1], max_position_embeddings=128)
     cfg = DiPaCoConfig(backbone=bb, level_sizes=[2, 2], sequence_length=64)
     corpus = _corpus(cfg)
+    monkeypatch.setenv("ODP_CE_GRAD_FUSED", "1")
     a = _engine(cfg, "cuda", loss_chunks=chunks)
     ha = a.fit(corpus, 2, 8, log_every=0)
     assert a._fused.ce_xf
