@@ -80,7 +80,7 @@ constexpr int tmem_cols(int bn) {
   return c;
 }
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kThreadsXF = 448;  // + warps 10-13: softmax-gradient transform of the A operand
+constexpr int kThreadsXF = 576;  // + warps 10-17: softmax-gradient transform of the A operand
 
 // Staging bytes per epilogue warp: one 4 KB box for bf16 / logits outputs, two for the
 // other epilogues of the single-CTA kernel (two fp32 boxes in flight, or the three bf16
@@ -1011,62 +1011,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(XF ? kThreadsXF : kT
     }
   } else if (XF != 0 && warp >= 10) {
     // ------------------------------------------------------------ A transform (both CTAs)
-    // logits -> dlogits in shared memory, stage by stage, then one arrival per warp on the
-    // leader's xdone barrier (shared-memory writes fenced to the async proxy first)
-    const int tid = (warp - 10) * 32 + lane;  // 0..127
+    // logits -> dlogits in shared memory, then one arrival per warp on the leader's xdone
+    // barrier (shared-memory writes fenced to the async proxy first). Two groups of four
+    // warps take alternate stages, so one group's waits and fences overlap the other's
+    // arithmetic.
+    const int grp = (warp - 10) / 4;
+    const int tid = ((warp - 10) % 4) * 32 + lane;  // 0..127 within the group
     const uint32_t xdone_leader = mapa_rank(&xdone[0], 0);
     int stage = 0;
     uint32_t phase = 0;
+    long long it = 0;  // stage uses so far (both groups' share)
     bool ok = true;
     for (int t = pair; t < p.num_tiles && ok; t += npairs) {
       const int gg = t / tiles_per_g, r = t % tiles_per_g;
       const int tm = r / p.tiles_n;
       const int path = gg / p.xf_split;
       const long long tok0 = (long long)(gg % p.xf_split) * p.K;  // token offset of this split
+      const long long rbase = path * p.xf_ms + tok0;
       const float sc = p.xf_sc[path];
       const int row0 = tm * 2 * BM + (int)rank * BM;
-      float ob = 0.f;
-      int y = -1;
-      if (XF == 1) {  // one token per thread for the whole tile: row tid of A
-        const long long tok = row0 + tid;
-        if (tok < p.M) {
-          y = p.xf_lab[path * p.xf_ms + tok];
-          ob = p.xf_ob[path * p.xf_ms + tok];
+      // (label, ob) of this thread's token: XF 1 one per tile (row tid of A); XF 2 one per
+      // k-block (token row kb * 64 + tid % 64), fetched one own-stage ahead
+      auto fetch = [&](long long tok, long long lim, int& y, float& ob) {
+        y = -1;
+        ob = 0.f;
+        if (tok < lim) {
+          y = p.xf_lab[rbase + tok];
+          ob = p.xf_ob[rbase + tok];
         }
-      } else {  // the first k-block's token of this thread
-        const long long tok = tid & 63;
-        if (tok < p.K) {
-          y = p.xf_lab[path * p.xf_ms + tok0 + tok];
-          ob = p.xf_ob[path * p.xf_ms + tok0 + tok];
-        }
-      }
-      for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!mbar_wait(&afull[stage], phase, p.err, ERR_TIMEOUT_FULL)) {
-          ok = false;
-          break;
-        }
-        uint8_t* sA = smem + stage * L::STAGE_BYTES;
-        if constexpr (XF == 1) {
-          // K-major: row tid holds vocab columns [kb * 64, kb * 64 + 64) of token row0 + tid
-          xf_slab(sA + tid * 128, tid & 7, ob, sc, y, kb * BK);
-        } else {
-          // MN-major: 64 token rows x (two 64-vocab halves); thread = (token k, half h).
-          // This k-block's (label, ob) were loaded during the previous one.
-          const int k = tid & 63, h = tid >> 6;
-          const int yk = y;
-          const float obk = ob;
-          const long long nxt = (long long)(kb + 1) * BK + k;
-          y = -1;
-          if (kb + 1 < p.num_kb && nxt < p.K) {
-            y = p.xf_lab[path * p.xf_ms + tok0 + nxt];
-            ob = p.xf_ob[path * p.xf_ms + tok0 + nxt];
+      };
+      int y, yn;
+      float ob, obn;
+      const int k = tid & 63, h = tid >> 6;
+      if (XF == 1) fetch(row0 + tid, p.M, y, ob);
+      const int kb0 = (int)((grp - (it & 1) + 2) & 1);  // this group's first k-block of the tile
+      if (XF == 2) fetch((long long)kb0 * BK + k, p.K, yn, obn);
+      for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        if ((it & 1) == grp) {
+          if (!mbar_wait(&afull[stage], phase, p.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
           }
-          xf_slab(sA + h * 8192 + k * 128, k & 7, obk, sc, yk, row0 + h * 64);
+          uint8_t* sA = smem + stage * L::STAGE_BYTES;
+          if constexpr (XF == 1) {
+            // K-major: row tid holds vocab columns [kb * 64, kb * 64 + 64) of token row0 + tid
+            xf_slab(sA + tid * 128, tid & 7, ob, sc, y, kb * BK);
+          } else {
+            // MN-major: 64 token rows x (two 64-vocab halves); thread = (token k, half h)
+            y = yn;
+            ob = obn;
+            fetch((long long)(kb + 2) * BK + k, kb + 2 < p.num_kb ? p.K : 0, yn, obn);
+            xf_slab(sA + h * 8192 + k * 128, k & 7, ob, sc, y, row0 + h * 64);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(xdone_leader + stage * 8);
+          __syncwarp();
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(xdone_leader + stage * 8);
-        __syncwarp();
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
