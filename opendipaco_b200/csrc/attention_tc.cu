@@ -64,6 +64,10 @@ struct Args {
   float* delta;      // [GB, nh, S] rowsum(dO o), written by the flash dQ kernel
   float scale;
   int* err;
+  // flash kernels: q|k with RoPE already applied ([GB, S, (nh + nkv) * 64], row stride ldr),
+  // written once per call by rope_qk_kernel; null = rotate each staged tile instead
+  const __nv_bfloat16* qkr;
+  long long ldr;
 };
 
 // bf16 round-to-nearest-even on the integer pipe: add 0x7FFF plus the lowest kept bit and
@@ -609,6 +613,31 @@ ODP_DEVICE void rope_rows(uint8_t* tile, int r0, int nrows, int S, const float* 
   }
 }
 
+// RoPE once per call for the flash kernels: CTA (b, head, sequence) rotates rows
+// [64 b, 64 b + 64) of one q or k head with the same staging and rope_rows code the
+// kernels would run on each staged tile (so the rotated values are the same bits), and
+// writes them to a.qkr. Without it every query tile would rotate every key tile again
+// (and every (query head, tile) pair of a kv group), reading the cos / sin tables each time.
+__global__ void __launch_bounds__(128) rope_qk_kernel(Args a) {
+  __shared__ __align__(1024) uint8_t tile[TILE64];
+  const int r0 = blockIdx.x * KT, hd = blockIdx.y, gb = blockIdx.z;
+  pdl_wait();
+  pdl_trigger();
+  const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
+  stage_rows<128>(tile, base, a.ld, hd * D, r0, KT, a.S);
+  cp_async_wait_all();
+  __syncthreads();
+  rope_rows<128>(tile, r0, KT, a.S, a.cosT, a.sinT);
+  __syncthreads();
+  __nv_bfloat16* out = const_cast<__nv_bfloat16*>(a.qkr) + (long long)gb * a.S * a.ldr + hd * D;
+  for (int i = threadIdx.x; i < KT * 8; i += 128) {
+    const int r = i >> 3, c8 = (i & 7) * 8;
+    if (r0 + r < a.S)
+      *reinterpret_cast<uint4*>(out + (long long)(r0 + r) * a.ldr + c8) =
+          *reinterpret_cast<const uint4*>(tile + sw_off(r, c8));
+  }
+}
+
 // Every thread of the CTA: publish shared-memory writes to the tensor core and order the
 // block around tcgen05 operations.
 ODP_DEVICE void publish_smem_sync() {
@@ -652,7 +681,10 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   const int kend = min(a.S, q0 + T);  // causal: this tile needs keys [0, kend)
   const int nkt = (kend + KT - 1) / KT;
-  stage_rows<128>(sQ, base, a.ld, h * D, q0, T, a.S);
+  const bool pre = a.qkr != nullptr;  // q|k rotated already
+  const __nv_bfloat16* qkb = pre ? a.qkr + (long long)gb * a.S * a.ldr : base;
+  const long long qkld = pre ? a.ldr : a.ld;
+  stage_rows<128>(sQ, qkb, qkld, h * D, q0, T, a.S);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -669,12 +701,14 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
   bool ok = true;
   for (int j = 0; j < nkt && ok; ++j) {
     const int k0 = j * KT;
-    stage_rows<128>(sK, base, a.ld, (a.nh + kvh) * D, k0, KT, a.S);
+    stage_rows<128>(sK, qkb, qkld, (a.nh + kvh) * D, k0, KT, a.S);
     stage_rows<128>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, k0, KT, a.S);
     cp_async_wait_all();
     __syncthreads();
-    if (j == 0) rope_rows<128>(sQ, q0, T, a.S, a.cosT, a.sinT);
-    rope_rows<128>(sK, k0, KT, a.S, a.cosT, a.sinT);
+    if (!pre) {
+      if (j == 0) rope_rows<128>(sQ, q0, T, a.S, a.cosT, a.sinT);
+      rope_rows<128>(sK, k0, KT, a.S, a.cosT, a.sinT);
+    }
     publish_smem_sync();
     if (threadIdx.x == 0) {
       constexpr uint32_t idS = umma_idesc_bf16(T, KT, false, false);
@@ -771,7 +805,10 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
   pdl_wait();  // global memory only from here on
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
-  stage_rows<256>(sQ, base, a.ld, h * D, q0, T, a.S);
+  const bool pre = a.qkr != nullptr;  // q|k rotated already
+  const __nv_bfloat16* qkb = pre ? a.qkr + (long long)gb * a.S * a.ldr : base;
+  const long long qkld = pre ? a.ldr : a.ld;
+  stage_rows<256>(sQ, qkb, qkld, h * D, q0, T, a.S);
   stage_rows<256>(sdO, dobase, a.ldo, h * D, q0, T, a.S);
   // this thread's O row (threads < 128), for delta = rowsum(dO o), loaded while the tiles stream in
   uint4 opk[8];
@@ -815,12 +852,14 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
   bool ok = true;
   for (int j = 0; j < nkt && ok; ++j) {
     const int k0 = j * KT;
-    stage_rows<256>(sK, base, a.ld, (a.nh + kvh) * D, k0, KT, a.S);
+    stage_rows<256>(sK, qkb, qkld, (a.nh + kvh) * D, k0, KT, a.S);
     stage_rows<256>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, k0, KT, a.S);
     cp_async_wait_all();
     __syncthreads();
-    if (j == 0) rope_rows<256>(sQ, q0, T, a.S, a.cosT, a.sinT);
-    rope_rows<256>(sK, k0, KT, a.S, a.cosT, a.sinT);
+    if (!pre) {
+      if (j == 0) rope_rows<256>(sQ, q0, T, a.S, a.cosT, a.sinT);
+      rope_rows<256>(sK, k0, KT, a.S, a.cosT, a.sinT);
+    }
     publish_smem_sync();
     if (threadIdx.x == 0) {
       constexpr uint32_t idS = umma_idesc_bf16(T, KT, false, false);
@@ -900,7 +939,10 @@ __global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
   pdl_wait();  // global memory only from here on
   const __nv_bfloat16* base = a.qkv + (long long)gb * a.S * a.ld;
   const __nv_bfloat16* dobase = a.dout + (long long)gb * a.S * a.ldo;
-  stage_rows<256>(sK, base, a.ld, (a.nh + kvh) * D, k0, T, a.S);
+  const bool pre = a.qkr != nullptr;  // q|k rotated already
+  const __nv_bfloat16* qkb = pre ? a.qkr + (long long)gb * a.S * a.ldr : base;
+  const long long qkld = pre ? a.ldr : a.ld;
+  stage_rows<256>(sK, qkb, qkld, (a.nh + kvh) * D, k0, T, a.S);
   stage_rows<256>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, k0, T, a.S);
   tc_fence_before();
   __syncthreads();
@@ -916,7 +958,7 @@ __global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
     const int h = kvh * grp + hi;
     for (int i = i0; i < nq && ok; ++i) {
       const int qs = i * KT;
-      stage_rows<256>(sQ, base, a.ld, h * D, qs, KT, a.S);
+      stage_rows<256>(sQ, qkb, qkld, h * D, qs, KT, a.S);
       stage_rows<256>(sdO, dobase, a.ldo, h * D, qs, KT, a.S);
       if (threadIdx.x < KT) {
         const int qq = qs + (int)threadIdx.x;
@@ -926,8 +968,10 @@ __global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
       }
       cp_async_wait_all();
       __syncthreads();
-      if (hi == 0 && i == i0) rope_rows<256>(sK, k0, T, a.S, a.cosT, a.sinT);
-      rope_rows<256>(sQ, qs, KT, a.S, a.cosT, a.sinT);
+      if (!pre) {
+        if (hi == 0 && i == i0) rope_rows<256>(sK, k0, T, a.S, a.cosT, a.sinT);
+        rope_rows<256>(sQ, qs, KT, a.S, a.cosT, a.sinT);
+      }
       publish_smem_sync();
       if (threadIdx.x == 0) {
         constexpr uint32_t idS = umma_idesc_bf16(T, KT, false, false);
@@ -1066,8 +1110,23 @@ void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
 
 // Any S >= 1 (used for S > 128): qkv [GB, S, (nh+2nkv)*64] bf16 -> o [GB, S, nh*64] bf16,
 // lse [GB, nh, S] fp32.
+// With `qkr` ([GB, S, (nh + nkv) * 64] bf16 scratch) q|k are rotated once into it first
+// (one more launch) instead of in every staged tile.
+static void rope_prepass(odp::attn_tc::Args& a, c10::optional<torch::Tensor>& qkr, int64_t GB, int64_t S,
+                         int64_t nh, int64_t nkv, cudaStream_t st) {
+  if (!qkr.has_value()) return;
+  TORCH_CHECK(qkr->is_cuda() && qkr->scalar_type() == at::kBFloat16 && qkr->is_contiguous() &&
+                  qkr->numel() >= GB * S * (nh + nkv) * odp::attn_tc::D,
+              "attention: qkr must be a contiguous bf16 [GB, S, (nh + nkv) * 64] tensor");
+  a.qkr = reinterpret_cast<const __nv_bfloat16*>(qkr->data_ptr());
+  a.ldr = (nh + nkv) * odp::attn_tc::D;
+  dim3 grid((unsigned)((S + odp::attn_tc::KT - 1) / odp::attn_tc::KT), (unsigned)(nh + nkv), (unsigned)GB);
+  C10_CUDA_CHECK(odp::launch_pdl(odp::attn_tc::rope_qk_kernel, grid, dim3(128), 0, st, a));
+}
+
 void attention_fwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
-                         torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err) {
+                         torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err,
+                         c10::optional<torch::Tensor> qkr) {
   c10::cuda::CUDAGuard guard(qkv.device());
   static bool attr = false;
   if (!attr) {
@@ -1077,9 +1136,11 @@ void attention_fwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, i
   }
   TORCH_CHECK(cosT.size(0) >= S && sinT.size(0) >= S, "attention: RoPE tables shorter than S");
   auto a = tc_args(qkv, S, nh, nkv, cosT, sinT, o, lse, err);
+  auto st = at::cuda::getCurrentCUDAStream();
+  rope_prepass(a, qkr, GB, S, nh, nkv, st);
   const unsigned nqt = (unsigned)((S + odp::attn_tc::T - 1) / odp::attn_tc::T);
   dim3 grid(nqt, (unsigned)nh, (unsigned)GB);
-  C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::flash_fwd_kernel), dim3(grid), dim3(128), odp::attn_tc::kFlashFwdSmem, at::cuda::getCurrentCUDAStream(), a));
+  C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::flash_fwd_kernel), dim3(grid), dim3(128), odp::attn_tc::kFlashFwdSmem, st, a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1087,7 +1148,8 @@ void attention_fwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, i
 // dK / dV, both into dqkv [GB, S, (nh+2nkv)*64] (gradients w.r.t. the pre-RoPE q|k|v).
 void attention_bwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                          torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout,
-                         torch::Tensor delta, torch::Tensor dqkv, torch::Tensor err) {
+                         torch::Tensor delta, torch::Tensor dqkv, torch::Tensor err,
+                         c10::optional<torch::Tensor> qkr) {
   c10::cuda::CUDAGuard guard(qkv.device());
   static bool attr = false;
   if (!attr) {
@@ -1105,6 +1167,7 @@ void attention_bwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, i
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   a.delta = delta.data_ptr<float>();
   auto st = at::cuda::getCurrentCUDAStream();
+  rope_prepass(a, qkr, GB, S, nh, nkv, st);
   const unsigned nt = (unsigned)((S + odp::attn_tc::T - 1) / odp::attn_tc::T);
   C10_CUDA_CHECK(odp::launch_pdl((odp::attn_tc::flash_bwd_dq_kernel), dim3(dim3(nt, (unsigned)nh, (unsigned)GB)), dim3(256), odp::attn_tc::kFlashDqSmem, st, a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -42,10 +42,12 @@ void attention_bwd_tc(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int6
                       torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout, torch::Tensor dqkv,
                       torch::Tensor err);
 void attention_fwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
-                         torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err);
+                         torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor err,
+                         c10::optional<torch::Tensor> qkr);
 void attention_bwd_flash(torch::Tensor qkv, int64_t GB, int64_t S, int64_t nh, int64_t nkv, torch::Tensor cosT,
                          torch::Tensor sinT, torch::Tensor o, torch::Tensor lse, torch::Tensor dout,
-                         torch::Tensor delta, torch::Tensor dqkv, torch::Tensor err);
+                         torch::Tensor delta, torch::Tensor dqkv, torch::Tensor err,
+                         c10::optional<torch::Tensor> qkr);
 void ce_fused(torch::Tensor logits, int64_t ldl, int64_t sl, torch::Tensor labels, int64_t M, int64_t V, int64_t G,
               torch::Tensor lse, torch::Tensor row_loss, torch::Tensor loss_sum, torch::Tensor inv_count,
               c10::optional<torch::Tensor> loss_out, torch::Tensor err, c10::optional<torch::Tensor> inv_given,
@@ -129,8 +131,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd", &attention_fwd);
   m.def("attention_bwd", &attention_bwd);
   m.def("attention_fwd_tc", &attention_fwd_tc);
-  m.def("attention_fwd_flash", &attention_fwd_flash);
-  m.def("attention_bwd_flash", &attention_bwd_flash);
+  m.def("attention_fwd_flash", &attention_fwd_flash, py::arg("qkv"), py::arg("GB"), py::arg("S"), py::arg("nh"),
+        py::arg("nkv"), py::arg("cosT"), py::arg("sinT"), py::arg("o"), py::arg("lse"), py::arg("err"),
+        py::arg("qkr") = py::none());
+  m.def("attention_bwd_flash", &attention_bwd_flash, py::arg("qkv"), py::arg("GB"), py::arg("S"), py::arg("nh"),
+        py::arg("nkv"), py::arg("cosT"), py::arg("sinT"), py::arg("o"), py::arg("lse"), py::arg("dout"),
+        py::arg("delta"), py::arg("dqkv"), py::arg("err"), py::arg("qkr") = py::none());
   m.def("ce_fused", &ce_fused, py::arg("logits"), py::arg("ldl"), py::arg("sl"), py::arg("labels"), py::arg("M"),
         py::arg("V"), py::arg("G"), py::arg("lse"), py::arg("row_loss"), py::arg("loss_sum"), py::arg("inv_count"),
         py::arg("loss_out"), py::arg("err"), py::arg("inv_given"), py::arg("ob") = py::none());

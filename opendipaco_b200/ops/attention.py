@@ -36,28 +36,34 @@ def use_tc(S: int) -> bool:
     return impl_for(S) != "mma"
 
 
-def fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, err=None) -> None:
-    """Launch the forward kernel on preallocated outputs (no allocation)."""
+def qkr_shape(GB: int, S: int, nh: int, nkv: int) -> tuple | None:
+    """Shape of the rotated-q|k scratch the flash kernels take (None: not used for S)."""
+    return (GB, S, (nh + nkv) * 64) if impl_for(S) == "flash" else None
+
+
+def fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, err=None, qkr=None) -> None:
+    """Launch the forward kernel on preallocated outputs (no allocation). Flash path: with
+    ``qkr`` (bf16 ``qkr_shape``) q|k are rotated once into it, else in every staged tile."""
     impl = impl_for(S)
     e = err if err is not None else err_word(qkv.device)
     if impl == "tc":
         ext().attention_fwd_tc(qkv, GB, S, nh, nkv, cos, sin, o, lse, e)
     elif impl == "flash":
-        ext().attention_fwd_flash(qkv, GB, S, nh, nkv, cos, sin, o, lse, e)
+        ext().attention_fwd_flash(qkv, GB, S, nh, nkv, cos, sin, o, lse, e, qkr)
     else:
         ext().attention_fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse)
 
 
-def bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv, err=None) -> None:
+def bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv, err=None, qkr=None) -> None:
     """Launch the backward kernels on preallocated buffers. ``delta`` [GB, nh, S] fp32
     receives rowsum(dO o) (flash and mma paths); the one-tile kernel computes it in
-    registers and leaves ``delta`` untouched."""
+    registers and leaves ``delta`` untouched. ``qkr`` as in :func:`fwd`."""
     impl = impl_for(S)
     e = err if err is not None else err_word(qkv.device)
     if impl == "tc":
         ext().attention_bwd_tc(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, dqkv, e)
     elif impl == "flash":
-        ext().attention_bwd_flash(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv, e)
+        ext().attention_bwd_flash(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv, e, qkr)
     else:
         ext().attention_bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, dout, delta, dqkv)
 
@@ -68,7 +74,9 @@ def attention_fwd(qkv: torch.Tensor, nh: int, nkv: int, cos: torch.Tensor, sin: 
     assert C == (nh + 2 * nkv) * 64 and (impl_for(S) != "mma" or S % 64 == 0)
     o = torch.empty(B, S, nh * 64, device=qkv.device, dtype=torch.bfloat16)
     lse = torch.empty(B, nh, S, device=qkv.device, dtype=torch.float32)
-    fwd(qkv, B, S, nh, nkv, cos, sin, o, lse)
+    shp = qkr_shape(B, S, nh, nkv)
+    qkr = torch.empty(shp, device=qkv.device, dtype=torch.bfloat16) if shp else None
+    fwd(qkv, B, S, nh, nkv, cos, sin, o, lse, qkr=qkr)
     return o, lse
 
 
@@ -77,5 +85,7 @@ def attention_bwd(qkv, o, lse, dout, nh, nkv, cos, sin):
     B, S, C = qkv.shape
     dqkv = torch.empty_like(qkv)
     delta = torch.empty(B, nh, S, device=qkv.device, dtype=torch.float32)
-    bwd(qkv, B, S, nh, nkv, cos, sin, o, lse, dout.contiguous(), delta, dqkv)
+    shp = qkr_shape(B, S, nh, nkv)
+    qkr = torch.empty(shp, device=qkv.device, dtype=torch.bfloat16) if shp else None
+    bwd(qkv, B, S, nh, nkv, cos, sin, o, lse, dout.contiguous(), delta, dqkv, qkr=qkr)
     return dqkv

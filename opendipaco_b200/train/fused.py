@@ -359,6 +359,9 @@ class FusedExecutor:
         self.DOUT = z(G, M, H, dt=b16)
         self.DQKV = z(G, M, C, dt=b16)
         self.DELTA = z(G * B, nh, S)
+        # flash attention (S > 128): q|k rotated once per call into this scratch
+        shp = attn.qkr_shape(G * B, S, nh, nkv)
+        self.QKR = z(*shp, dt=b16) if shp else None
         self.NORMWORK = z(G * ((M + 7) // 8) * H)  # RMSNorm weight-gradient partials (8-row blocks at most)
         self.CLIPWORK = z(G * ((self.P + (1 << 16) - 1) // (1 << 16)))
         self.COEF = z(G)
@@ -537,7 +540,7 @@ class FusedExecutor:
             self._gemm(self.DX16, H, MH, False, w16[lo.o:], H, P, True, self.DOUT, H, MH, M, H, H, "bf16")
             self._wgrad(f"o{l}", self.DX16, H, MH, self.O[k], H, MH, gr[lo.o:], H, P, H, H, M)
             attn.bwd(self.QKV[k], G * B, S, nh, nkv, self.cos, self.sin, self.O[k], self.LSEA[k], self.DOUT,
-                     self.DELTA, self.DQKV, self.err)
+                     self.DELTA, self.DQKV, self.err, self.QKR)
             self._gemm(self.DQKV, C, MC, False, w16[lo.qkv:], H, P, True, self.DXN, H, MH, M, H, C, "f32")
             self._wgrad(f"qkv{l}", self.DQKV, C, MC, self.XN1[k], H, MH, gr[lo.qkv:], H, P, C, H, M)
             X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[k], self.DXN, MH, self.DX, self.DX, MH,
@@ -601,7 +604,8 @@ class FusedExecutor:
         k = 0 if self.ckpt else l
         X_.rmsnorm_fwd(self.X[l], MH, w32[lo.ln1:], P, self.XN1[k], MH, self.RS1[k], M, H, G, self.eps)
         self._gemm(self.XN1[k], H, MH, False, w16[lo.qkv:], H, P, False, self.QKV[k], C, MC, M, C, H, "bf16")
-        attn.fwd(self.QKV[k], G * B, S, nh, nkv, self.cos, self.sin, self.O[k], self.LSEA[k], self.err)
+        attn.fwd(self.QKV[k], G * B, S, nh, nkv, self.cos, self.sin, self.O[k], self.LSEA[k], self.err,
+                 getattr(self, "QKR", None))
         self._gemm(self.O[k], H, MH, False, w16[lo.o:], H, P, False, self.HR[k], H, MH, M, H, H, "resid",
                    R=self.X[l], ldr=H, sr=MH)
         X_.rmsnorm_fwd(self.HR[k], MH, w32[lo.ln2:], P, self.XN2[k], MH, self.RS2[k], M, H, G, self.eps)
@@ -936,6 +940,8 @@ class FusedExecutor:
                     + sum(1 for sp in self.wg_split.values() if sp > 1))
         if self.ckpt:  # recomputed layer forwards (all but the down projection): 6 launches each
             per_step += 6 * self.L
+        if self.QKR is not None:  # flash attention: rotation pass in forward and backward, two backward kernels
+            per_step += 3 * self.L + (self.L if self.ckpt else 0)
         if len(self.chunks) > 1:
             # chunked LM head: label count + per chunk (logits, CE rows (two kernels from
             # GEMM partials), dX, dW) + group sum, against 6 launches (+ a split-K reduce)

@@ -66,11 +66,16 @@ def bench_attention(GB: int, S: int, nh: int, nkv: int, reps: int, flush) -> lis
     tri = GB * nh * S * (S + 1) / 2
     fwd_flops, bwd_flops = 2 * 2 * tri * D, 5 * 2 * tri * D
     tf, _, lab = _peaks()
-    for impl in ("auto", "mma"):
+    shp = attn.qkr_shape(GB, S, nh, nkv)
+    qkr = torch.empty(shp, device=dev, dtype=torch.bfloat16) if shp else None
+    variants = [("auto", qkr)] + ([("auto", None)] if qkr is not None else []) + [("mma", None)]
+    for impl, q in variants:
         os.environ["ODP_ATTN_IMPL"] = impl
         name = {"tc": "tcgen05 one-tile", "flash": "tcgen05 flash", "mma": "mma.sync"}[attn.impl_for(S)]
-        f = _timeit(lambda: attn.fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse), reps, flush)
-        b = _timeit(lambda: attn.bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, do, delta, dqkv), reps, flush)
+        if attn.impl_for(S) == "flash":
+            name += ", q|k rotated once" if q is not None else ", q|k rotated per tile"
+        f = _timeit(lambda: attn.fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, qkr=q), reps, flush)
+        b = _timeit(lambda: attn.bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, do, delta, dqkv, qkr=q), reps, flush)
         check_errors()
         # algorithmic bytes: fwd reads q|k|v, writes o + lse; bwd reads q|k|v, o, do, lse, writes dq|dk|dv
         fb = qkv.numel() * 2 + o.numel() * 2 + lse.numel() * 4

@@ -159,3 +159,30 @@ def test_flash_attention_is_deterministic(monkeypatch):
     b = _run("auto", qkv, nh, nkv, cos, sin, do, monkeypatch)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("B,S,nh,nkv", [(2, 200, 4, 1), (1, 384, 8, 2)])
+def test_flash_rotation_pass_gives_the_same_bits(B, S, nh, nkv):
+    """q|k rotated once into a scratch by a separate pass, or in every staged tile: the
+    same rotation code on the same bits, so forward and backward agree exactly."""
+    from opendipaco_b200.models.llama import rope_cos_sin
+    from opendipaco_b200.ops import attention as attn
+    from opendipaco_b200.ops import check_errors
+
+    cos, sin = rope_cos_sin(D, 10000.0, S, DEV)
+    qkv = _bf(B, S, (nh + 2 * nkv) * D, seed=7)
+    do = _bf(B, S, nh * D, seed=8)
+    outs = []
+    for use in (False, True):
+        o = torch.empty(B, S, nh * D, device=DEV, dtype=torch.bfloat16)
+        lse = torch.empty(B, nh, S, device=DEV)
+        delta = torch.empty(B, nh, S, device=DEV)
+        dqkv = torch.zeros_like(qkv)
+        qkr = torch.empty(attn.qkr_shape(B, S, nh, nkv), device=DEV, dtype=torch.bfloat16) if use else None
+        attn.fwd(qkv, B, S, nh, nkv, cos, sin, o, lse, qkr=qkr)
+        attn.bwd(qkv, B, S, nh, nkv, cos, sin, o, lse, do, delta, dqkv, qkr=qkr)
+        torch.cuda.synchronize()
+        check_errors()
+        outs.append((o, lse, dqkv))
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
