@@ -580,7 +580,7 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
 
 constexpr int KT = 64;              // keys (forward, dQ) or queries (dK / dV) per inner tile
 constexpr int TILE64 = KT * 128;    // bytes of a [64][64] bf16 tile
-constexpr int kFlashFwdSmem = 2 * TILE + 2 * TILE64 + 1024;
+constexpr int kFlashFwdSmem = 2 * TILE + 4 * TILE64 + 1024;  // K / V double-buffered
 constexpr int kFlashDqSmem = 3 * TILE + 2 * TILE64 + 1024;
 constexpr int kFlashDkvSmem = 4 * TILE + 2 * TILE64 + 1024;
 
@@ -662,8 +662,7 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
   uint8_t* sm = align1024(smem_raw);
   uint8_t* sQ = sm;
   uint8_t* sP = sm + TILE;
-  uint8_t* sK = sm + 2 * TILE;
-  uint8_t* sV = sK + TILE64;
+  uint8_t* sKV = sm + 2 * TILE;  // two (K, V) tile pairs: tile j + 1 streams in during tile j
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_holder;
   const int nqt = (a.S + T - 1) / T;
@@ -685,6 +684,8 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
   const __nv_bfloat16* qkb = pre ? a.qkr + (long long)gb * a.S * a.ldr : base;
   const long long qkld = pre ? a.ldr : a.ld;
   stage_rows<128>(sQ, qkb, qkld, h * D, q0, T, a.S);
+  stage_rows<128>(sKV, qkb, qkld, (a.nh + kvh) * D, 0, KT, a.S);
+  stage_rows<128>(sKV + TILE64, base, a.ld, (a.nh + a.nkv + kvh) * D, 0, KT, a.S);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -701,9 +702,9 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
   bool ok = true;
   for (int j = 0; j < nkt && ok; ++j) {
     const int k0 = j * KT;
-    stage_rows<128>(sK, qkb, qkld, (a.nh + kvh) * D, k0, KT, a.S);
-    stage_rows<128>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, k0, KT, a.S);
-    cp_async_wait_all();
+    uint8_t* sK = sKV + (j & 1) * 2 * TILE64;
+    uint8_t* sV = sK + TILE64;
+    cp_async_wait_all();  // tile j (issued one iteration ahead) has landed
     __syncthreads();
     if (!pre) {
       if (j == 0) rope_rows<128>(sQ, q0, T, a.S, a.cosT, a.sinT);
@@ -717,6 +718,11 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(Args a) {
       umma_commit(&bar);
     }
     __syncwarp();
+    if (j + 1 < nkt) {  // the other pair was last read by tile j - 1's MMAs, which completed
+      uint8_t* nK = sKV + ((j + 1) & 1) * 2 * TILE64;
+      stage_rows<128>(nK, qkb, qkld, (a.nh + kvh) * D, k0 + KT, KT, a.S);
+      stage_rows<128>(nK + TILE64, base, a.ld, (a.nh + a.nkv + kvh) * D, k0 + KT, KT, a.S);
+    }
     ok = wait_mma(&bar, phase, ok, a.err);
     // valid keys of this row in the tile: k0 + e <= q and k0 + e < S
     const int nvalid = q < a.S ? max(0, min(KT, min(q + 1, a.S) - k0)) : 0;
