@@ -581,8 +581,8 @@ __global__ void __launch_bounds__(256, LEAN ? 2 : 1) bwd_kernel(Args a) {
 constexpr int KT = 64;              // keys (forward, dQ) or queries (dK / dV) per inner tile
 constexpr int TILE64 = KT * 128;    // bytes of a [64][64] bf16 tile
 constexpr int kFlashFwdSmem = 2 * TILE + 4 * TILE64 + 1024;  // K / V double-buffered
-constexpr int kFlashDqSmem = 3 * TILE + 2 * TILE64 + 1024;
-constexpr int kFlashDkvSmem = 4 * TILE + 2 * TILE64 + 1024;
+constexpr int kFlashDqSmem = 3 * TILE + 4 * TILE64 + 1024;  // K / V double-buffered
+constexpr int kFlashDkvSmem = 4 * TILE + 4 * TILE64 + 1024;  // Q / dO double-buffered
 
 // Stage rows [r0, r0 + nrows) of 64 columns at col0 of a [S, ld] bf16 matrix into a
 // swizzled tile (tile row r = matrix row r0 + r); rows >= S are zero-filled.
@@ -789,8 +789,7 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
   uint8_t* sQ = sm;
   uint8_t* sdO = sm + TILE;
   uint8_t* sdS = sm + 2 * TILE;  // [128 queries][64 keys]
-  uint8_t* sK = sm + 3 * TILE;
-  uint8_t* sV = sK + TILE64;
+  uint8_t* sKV = sm + 3 * TILE;  // two (K, V) tile pairs: tile j + 1 streams in during tile j
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_holder;
   __shared__ float sDelta[T], sLse[T];
@@ -816,6 +815,8 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
   const long long qkld = pre ? a.ldr : a.ld;
   stage_rows<256>(sQ, qkb, qkld, h * D, q0, T, a.S);
   stage_rows<256>(sdO, dobase, a.ldo, h * D, q0, T, a.S);
+  stage_rows<256>(sKV, qkb, qkld, (a.nh + kvh) * D, 0, KT, a.S);
+  stage_rows<256>(sKV + TILE64, base, a.ld, (a.nh + a.nkv + kvh) * D, 0, KT, a.S);
   // this thread's O row (threads < 128), for delta = rowsum(dO o), loaded while the tiles stream in
   uint4 opk[8];
   const int qr = q0 + (int)threadIdx.x;
@@ -858,9 +859,9 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
   bool ok = true;
   for (int j = 0; j < nkt && ok; ++j) {
     const int k0 = j * KT;
-    stage_rows<256>(sK, qkb, qkld, (a.nh + kvh) * D, k0, KT, a.S);
-    stage_rows<256>(sV, base, a.ld, (a.nh + a.nkv + kvh) * D, k0, KT, a.S);
-    cp_async_wait_all();
+    uint8_t* sK = sKV + (j & 1) * 2 * TILE64;
+    uint8_t* sV = sK + TILE64;
+    cp_async_wait_all();  // tile j (issued one iteration ahead) has landed
     __syncthreads();
     if (!pre) {
       if (j == 0) rope_rows<256>(sQ, q0, T, a.S, a.cosT, a.sinT);
@@ -877,6 +878,11 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_kernel(Args a) {
       umma_commit(&bar);
     }
     __syncwarp();
+    if (j + 1 < nkt) {  // the other pair was last read by tile j - 1's MMAs, which completed
+      uint8_t* nK = sKV + ((j + 1) & 1) * 2 * TILE64;
+      stage_rows<256>(nK, qkb, qkld, (a.nh + kvh) * D, k0 + KT, KT, a.S);
+      stage_rows<256>(nK + TILE64, base, a.ld, (a.nh + a.nkv + kvh) * D, k0 + KT, KT, a.S);
+    }
     ok = wait_mma(&bar, phase, ok, a.err);
     const int nvalid = q < a.S ? max(0, min(KT, min(q + 1, a.S) - k0)) : 0;
 #pragma unroll
@@ -925,11 +931,10 @@ __global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
   uint8_t* sV = sm + TILE;
   uint8_t* sPT = sm + 2 * TILE;   // [128 keys][64 queries]
   uint8_t* sdST = sm + 3 * TILE;  // [128 keys][64 queries]
-  uint8_t* sQ = sm + 4 * TILE;    // [64 queries][64]
-  uint8_t* sdO = sQ + TILE64;
+  uint8_t* sQdO = sm + 4 * TILE;  // two (Q [64 queries][64], dO) pairs: the next streams in during this one
   __shared__ uint64_t bar;
   __shared__ uint32_t tmem_holder;
-  __shared__ float sDelta[KT], sLse[KT];
+  __shared__ float sDelta2[2][KT], sLse2[2][KT];
   const int kt = blockIdx.x, kvh = blockIdx.y, gb = blockIdx.z;
   const int grp = a.nh / a.nkv;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -960,19 +965,32 @@ __global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
   const int i0 = k0 / KT, nq = (a.S + KT - 1) / KT;  // query tiles at or after the diagonal
   uint32_t phase = 0;
   bool ok = true, accumulated = false;
+  // iteration it = (query head hi, query tile i) in order; its Q / dO tiles, lse and delta
+  // go to pair it & 1, issued one iteration ahead
+  auto stage_it = [&](int hi, int i, int b) {
+    const int h = kvh * grp + hi, qs = i * KT;
+    uint8_t* q = sQdO + b * 2 * TILE64;
+    stage_rows<256>(q, qkb, qkld, h * D, qs, KT, a.S);
+    stage_rows<256>(q + TILE64, dobase, a.ldo, h * D, qs, KT, a.S);
+    if (threadIdx.x < KT) {
+      const int qq = qs + (int)threadIdx.x;
+      const long long li = ((long long)gb * a.nh + h) * a.S + qq;
+      sLse2[b][threadIdx.x] = qq < a.S ? a.lse[li] * kLog2e : 0.f;
+      sDelta2[b][threadIdx.x] = qq < a.S ? a.delta[li] : 0.f;
+    }
+  };
+  if (i0 < nq) stage_it(0, i0, 0);
+  int it = 0;
   for (int hi = 0; hi < grp && ok; ++hi) {
     const int h = kvh * grp + hi;
-    for (int i = i0; i < nq && ok; ++i) {
+    for (int i = i0; i < nq && ok; ++i, ++it) {
       const int qs = i * KT;
-      stage_rows<256>(sQ, qkb, qkld, h * D, qs, KT, a.S);
-      stage_rows<256>(sdO, dobase, a.ldo, h * D, qs, KT, a.S);
-      if (threadIdx.x < KT) {
-        const int qq = qs + (int)threadIdx.x;
-        const long long li = ((long long)gb * a.nh + h) * a.S + qq;
-        sLse[threadIdx.x] = qq < a.S ? a.lse[li] * kLog2e : 0.f;
-        sDelta[threadIdx.x] = qq < a.S ? a.delta[li] : 0.f;
-      }
-      cp_async_wait_all();
+      const int b = it & 1;
+      uint8_t* sQ = sQdO + b * 2 * TILE64;
+      uint8_t* sdO = sQ + TILE64;
+      const float* sLse = sLse2[b];
+      const float* sDelta = sDelta2[b];
+      cp_async_wait_all();  // this iteration's tiles (issued one iteration ahead) have landed
       __syncthreads();
       if (!pre) {
         if (hi == 0 && i == i0) rope_rows<256>(sK, k0, T, a.S, a.cosT, a.sinT);
@@ -990,6 +1008,11 @@ __global__ void __launch_bounds__(256) flash_bwd_dkv_kernel(Args a) {
         umma_commit(&bar);
       }
       __syncwarp();
+      {  // the other pair was last read by the previous iteration's MMAs, which completed
+        const bool last_i = i + 1 >= nq;
+        if (!last_i) stage_it(hi, i + 1, b ^ 1);
+        else if (hi + 1 < grp) stage_it(hi + 1, i0, b ^ 1);
+      }
       ok = wait_mma(&bar, phase, ok, a.err);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
