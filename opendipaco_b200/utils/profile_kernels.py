@@ -12,7 +12,7 @@ MB L2 (its DRAM figures mean something) but the whole process stays within a few
 * outer:     the one-GPU outer step (APPLY + write-back) over 2 x 12.3 M elements
 * norm:      RMSNorm forward / backward, 2 x 3072 rows of 384
 * embedding: the sorted deterministic embedding backward, 2 x 3072 tokens, vocab 32000
-* attention: tcgen05 flash forward / backward, 4 x 1024 tokens, 32 / 8 heads
+* attention: tcgen05 flash forward / backward (q|k rotated once), 4 x 1024 tokens, 32 / 8 heads
 * ce:        one-pass cross-entropy, 2 x 3072 rows of 32000
 * routing:   bag-of-tokens featurizer, tensor-core k-means assignment and the ordered
              centroid sums, 20000 documents x 256 features, 16 centroids
@@ -116,8 +116,9 @@ def case_attention() -> None:
     do = torch.randn_like(o)
     delta = torch.empty(GB, nh, S, device="cuda")
     dqkv = torch.empty_like(qkv)
-    _thrice(lambda: attn.fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse))
-    _thrice(lambda: attn.bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, do, delta, dqkv))
+    qkr = torch.empty(attn.qkr_shape(GB, S, nh, nkv), device="cuda", dtype=torch.bfloat16)
+    _thrice(lambda: attn.fwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, qkr=qkr))
+    _thrice(lambda: attn.bwd(qkv, GB, S, nh, nkv, cos, sin, o, lse, do, delta, dqkv, qkr=qkr))
 
 
 def case_ce() -> None:
