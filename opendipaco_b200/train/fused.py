@@ -358,6 +358,25 @@ class FusedExecutor:
         self.DGU = z(G, M, 2 * Fd, dt=b16)
         self.DOUT = z(G, M, H, dt=b16)
         self.DQKV = z(G, M, C, dt=b16)
+        # Weight gradients on a second stream (few paths per GPU): each is needed only by the
+        # optimizer, and with few paths the grids of the backward's small GEMMs, norms and
+        # attention leave SMs idle that the weight-gradient GEMMs can use. The buffers they
+        # read (dY of each projection) are rewritten by the next layer, so each gets a ring of
+        # two slots; the main stream waits for the side stream to finish reading a slot before
+        # writing it again, and joins the side stream before the optimizer.
+        mode = os.environ.get("ODP_WGRAD_STREAM", "auto")
+        few = G * M <= 16384
+        self.wg_side = (mode == "1" or (mode == "auto" and few)) and not self.ckpt and len(self.chunks) == 1 \
+            and self._side_ctas == 0
+        self._wgs = torch.cuda.Stream(device=dev) if self.wg_side else None
+        self._rings, self._ring_i, self._ring_ev, self._ring_busy = {}, {}, {}, {}
+        for name, buf in (("dx16", self.DX16), ("dgu", self.DGU), ("dqkv", self.DQKV)):
+            slots = [buf, torch.empty_like(buf)] if self.wg_side else [buf]
+            self._rings[name], self._ring_i[name] = slots, 0
+            self._ring_ev[name] = [torch.cuda.Event() for _ in slots] if self.wg_side else []
+            self._ring_busy[name] = [False] * len(slots)
+        self._wg_fork = torch.cuda.Event() if self.wg_side else None
+        self._wg_join = torch.cuda.Event() if self.wg_side else None
         self.DELTA = z(G * B, nh, S)
         # flash attention (S > 128): q|k rotated once per call into this scratch
         shp = attn.qkr_shape(G * B, S, nh, nkv)
@@ -455,6 +474,44 @@ class FusedExecutor:
         gemm_wgrad(A, lda, sa, B, ldb, sb, C, ldc, sc, M, N, K, self.G, self.wg_split[name], self.WGWS,
                    sq.get("sq"), sq.get("sq_ld", 0), self.err, bn=self._bn(M, N))
 
+    def _ring_write(self, name: str) -> torch.Tensor:
+        """The ring slot to write next for buffer ``name``: the main stream first waits
+        until the side stream has read what that slot held."""
+        slots = self._rings[name]
+        if len(slots) == 1:
+            return slots[0]
+        i = (self._ring_i[name] + 1) % len(slots)
+        self._ring_i[name] = i
+        if self._ring_busy[name][i]:
+            torch.cuda.current_stream(self.dev).wait_event(self._ring_ev[name][i])
+            self._ring_busy[name][i] = False
+        return slots[i]
+
+    def _wgrad_async(self, ring: str | None, name: str, *args) -> None:
+        """``_wgrad`` on the side stream (when enabled), after everything issued so far on
+        the main stream; marks the ring slot it reads as busy until it has run."""
+        if self._wgs is None:
+            self._wgrad(name, *args)
+            return
+        cur = torch.cuda.current_stream(self.dev)
+        self._wg_fork.record(cur)
+        self._wgs.wait_event(self._wg_fork)
+        with torch.cuda.stream(self._wgs):
+            self._wgrad(name, *args)
+        if ring is not None:
+            i = self._ring_i[ring]
+            self._ring_ev[ring][i].record(self._wgs)
+            self._ring_busy[ring][i] = True
+
+    def _wgrad_join(self) -> None:
+        """The main stream waits for every weight gradient issued on the side stream."""
+        if self._wgs is None:
+            return
+        self._wg_join.record(self._wgs)
+        torch.cuda.current_stream(self.dev).wait_event(self._wg_join)
+        for name in self._ring_busy:
+            self._ring_busy[name] = [False] * len(self._ring_busy[name])
+
     def _gemm(self, A, lda, sa, amn, B, ldb, sb, bmn, C, ldc, sc, M, N, K, epi, bn=None, **kw):
         from ..ops.gemm import EPI
 
@@ -522,29 +579,34 @@ class FusedExecutor:
                            max_ctas=self._side_ctas, **self._sq("lm"))
                 self._ev_join.record(side)
         else:
-            self._wgrad("lm", self.LOGITS, V, M * V, self.XNF, H, MH, gr[lay.lm:], H, P, V, H, M)
-        X_.rmsnorm_bwd(self.X[L], MH, w32[lay.normf:], P, self.RSF, self.DXN, MH, None, self.DX, MH, self.DX16,
+            self._wgrad_async(None, "lm", self.LOGITS, V, M * V, self.XNF, H, MH, gr[lay.lm:], H, P, V, H, M)
+        dx16 = self._ring_write("dx16")
+        X_.rmsnorm_bwd(self.X[L], MH, w32[lay.normf:], P, self.RSF, self.DXN, MH, None, self.DX, MH, dx16,
                        gr[lay.normf:], P, self.NORMWORK, M, H, G, 0.0)
         for l in range(L - 1, -1, -1):
             lo = lay.layers[l]
             if self.ckpt:
                 self._layer_fwd(l, down=False)  # the layer's activations, recomputed into the slot
             k = 0 if self.ckpt else l
-            self._gemm(self.DX16, H, MH, False, w16[lo.down:], Fd, P, True, self.DGU, 2 * Fd, MF2, M, Fd, H,
+            dgu = self._ring_write("dgu")
+            self._gemm(dx16, H, MH, False, w16[lo.down:], Fd, P, True, dgu, 2 * Fd, MF2, M, Fd, H,
                        "swiglu_bwd", aux=self.GU[k], ldx=2 * Fd, sx=MF2, f_half=Fd)
-            self._wgrad(f"down{l}", self.DX16, H, MH, self.ACT[k], Fd, MF, gr[lo.down:], Fd, P, H, Fd, M)
-            self._gemm(self.DGU, 2 * Fd, MF2, False, w16[lo.gu:], H, P, True, self.DXN, H, MH, M, H, 2 * Fd, "f32")
-            self._wgrad(f"gu{l}", self.DGU, 2 * Fd, MF2, self.XN2[k], H, MH, gr[lo.gu:], H, P, 2 * Fd, H, M)
+            self._wgrad_async("dx16", f"down{l}", dx16, H, MH, self.ACT[k], Fd, MF, gr[lo.down:], Fd, P, H, Fd, M)
+            self._gemm(dgu, 2 * Fd, MF2, False, w16[lo.gu:], H, P, True, self.DXN, H, MH, M, H, 2 * Fd, "f32")
+            self._wgrad_async("dgu", f"gu{l}", dgu, 2 * Fd, MF2, self.XN2[k], H, MH, gr[lo.gu:], H, P, 2 * Fd, H, M)
+            dx16 = self._ring_write("dx16")
             X_.rmsnorm_bwd(self.HR[k], MH, w32[lo.ln2:], P, self.RS2[k], self.DXN, MH, self.DX, self.DX, MH,
-                           self.DX16, gr[lo.ln2:], P, self.NORMWORK, M, H, G, 0.0)
-            self._gemm(self.DX16, H, MH, False, w16[lo.o:], H, P, True, self.DOUT, H, MH, M, H, H, "bf16")
-            self._wgrad(f"o{l}", self.DX16, H, MH, self.O[k], H, MH, gr[lo.o:], H, P, H, H, M)
+                           dx16, gr[lo.ln2:], P, self.NORMWORK, M, H, G, 0.0)
+            self._gemm(dx16, H, MH, False, w16[lo.o:], H, P, True, self.DOUT, H, MH, M, H, H, "bf16")
+            self._wgrad_async("dx16", f"o{l}", dx16, H, MH, self.O[k], H, MH, gr[lo.o:], H, P, H, H, M)
+            dqkv = self._ring_write("dqkv")
             attn.bwd(self.QKV[k], G * B, S, nh, nkv, self.cos, self.sin, self.O[k], self.LSEA[k], self.DOUT,
-                     self.DELTA, self.DQKV, self.err, self.QKR)
-            self._gemm(self.DQKV, C, MC, False, w16[lo.qkv:], H, P, True, self.DXN, H, MH, M, H, C, "f32")
-            self._wgrad(f"qkv{l}", self.DQKV, C, MC, self.XN1[k], H, MH, gr[lo.qkv:], H, P, C, H, M)
+                     self.DELTA, dqkv, self.err, self.QKR)
+            self._gemm(dqkv, C, MC, False, w16[lo.qkv:], H, P, True, self.DXN, H, MH, M, H, C, "f32")
+            self._wgrad_async("dqkv", f"qkv{l}", dqkv, C, MC, self.XN1[k], H, MH, gr[lo.qkv:], H, P, C, H, M)
+            dx16 = self._ring_write("dx16")
             X_.rmsnorm_bwd(self.X[l], MH, w32[lo.ln1:], P, self.RS1[k], self.DXN, MH, self.DX, self.DX, MH,
-                           self.DX16, gr[lo.ln1:], P, self.NORMWORK, M, H, G, 0.0)
+                           dx16, gr[lo.ln1:], P, self.NORMWORK, M, H, G, 0.0)
         emb_n = bb.vocab_size * H
         rows = self.emb_rows
         if rows is None:
@@ -553,6 +615,7 @@ class FusedExecutor:
                                 self.EMBSQ if self.sq_bases is not None else None)
         if side is not None:
             torch.cuda.current_stream(self.dev).wait_event(self._ev_join)
+        self._wgrad_join()
         # ---------------- optimizer
         clip = self.e.diloco.inner_grad_clip
         clipv = float(clip) if clip is not None else 0.0
