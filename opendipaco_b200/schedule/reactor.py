@@ -306,6 +306,12 @@ class ReactorServer:
             try:
                 self._loop.run_forever()
             finally:
+                # sessions still waiting on a handler or a read end here, not at exit
+                pending = [t for t in asyncio.all_tasks(self._loop) if not t.done()]
+                for t in pending:
+                    t.cancel()
+                if pending:
+                    self._loop.run_until_complete(asyncio.gather(*pending, return_exceptions=True))
                 self._loop.run_until_complete(self._loop.shutdown_asyncgens())
                 self._loop.close()
 

@@ -729,6 +729,13 @@ class ParameterServer(ReactorServer):
         self._repl_stop.set()
         super().shutdown()
 
+    def simulate_crash(self) -> None:
+        """A killed owner: connections drop, and with the process gone its replication
+        loop and tracker heartbeat stop too (no drain, no deregistration), so the record
+        lapses after the tracker's TTL."""
+        self._repl_stop.set()
+        super().simulate_crash()
+
     # -- persistence ------------------------------------------------------------
     @staticmethod
     def _module_file(key: str) -> str:
