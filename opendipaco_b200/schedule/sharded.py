@@ -153,6 +153,7 @@ def _addr(a):
 # ===================================================================== parameter server
 class ParameterServer(ReactorServer):
     _SEEN_GRANTS_MAX = 4096
+    _PROPOSALS_MAX = 16       # live private-state proposals kept per key
 
     def __init__(self, config, owned_keys, diloco, *, host="0.0.0.0", port=0, auth_key=None, device="cpu",
                  resume_dir=None, grant_key=None, scheduler_pub=None, max_update_norm=None, compress="none",
@@ -502,11 +503,17 @@ class ParameterServer(ReactorServer):
                     skipped.append(k)
                     continue
                 if self.private_policy == "proposal":
-                    # apply only once private_quorum proposals agree byte for byte
+                    # apply only once private_quorum distinct proposers (peer identity, or the
+                    # single-use grant without one) agree byte for byte; one live proposal per
+                    # proposer, at most _PROPOSALS_MAX per key (the oldest are dropped)
                     dg = state_digest(sd)
-                    props = self._proposals.setdefault(k, [])
-                    props.append((dg, sd))
-                    if sum(1 for d, _ in props if d == dg) >= self.private_quorum:
+                    props = self._proposals.setdefault(k, collections.OrderedDict())
+                    who = peer_id or grant["token"]
+                    props[who] = (dg, sd)
+                    props.move_to_end(who)
+                    while len(props) > self._PROPOSALS_MAX:
+                        props.popitem(last=False)
+                    if sum(1 for d, _ in props.values() if d == dg) >= self.private_quorum:
                         self._record_history(k)
                         self.bank[k].load_state_dict({n: v.to(self.device) for n, v in sd.items()})
                         self._bump(k)
