@@ -605,8 +605,7 @@ def _local_decentralized(cfg: LaunchConfig):
             for path in topo.paths():
                 prim = path_primary(topo.path_module_keys(path), epoch0)
                 ps = by_id.get(prim["peer_id"]) if prim else None
-                with ps._lock:
-                    completed[topo.path_index(path)] = ps._gen_counters.get(tuple(path), 0)
+                completed[topo.path_index(path)] = ps.generation_of(path)
             if all(v >= target for v in completed.values()):
                 break
             time.sleep(0.05)

@@ -43,7 +43,7 @@ from ..parallel.backend.local import LocalBackend
 from ..topology import is_private_key
 from ..train.loop import _opt_state_cpu, _state_cpu
 from .aggregate import check_aggregate, robust_delta
-from .assignment import coordinator_key, is_assignee
+from .assignment import coordinator_key, is_assignee, version_lag
 from .compress import (apply_state_delta, check_mode, compress_delta, compress_shard, compress_state,
                        encode_state_delta, maybe_dequantize, pseudograd_digest, restore_shard, state_digest)
 from .guard import all_finite, clip_norm_, loss_ok
@@ -51,7 +51,7 @@ from .identity import peer_id_of, sign_record, verify_record
 from .ownership import (EpochManager, derive_epoch, epoch_newer, make_epoch_record, owners_for,
                         verify_epoch_record)
 from .probe import TrustedProbe, as_finite_float, is_harmful
-from .quorum import read_quorum_versions
+from .quorum import confirm_version, divergent_peers, read_quorum_versions
 from .ratelimit import RateLimiter
 from .reactor import ReactorServer
 from .reputation import Reputation
@@ -162,10 +162,12 @@ class ParameterServer(ReactorServer):
                  version_history=1, private_policy="overwrite", schedule_mode="central", down="full",
                  coordinates=None, scheduler_addr=None, peer_tls=None, private_quorum=2, salt="", k=3,
                  lease_ttl=20.0, read_quorum=1, directory_ttl=30.0, reputation=None, rate_limiter=None,
-                 min_owner_reputation=0.0, corpus_weights=None, **kw):
+                 min_owner_reputation=0.0, corpus_weights=None, worker_set=None, staleness_bound=None,
+                 staleness_weight="inverse", replica_audit_interval=30.0, **kw):
         super().__init__(host=host, port=port, auth_key=auth_key, **kw)
         self.config, self.diloco, self.device = config, diloco, torch.device(device)
         self._topology = config.build_topology()
+        self._paths = set(self._topology.paths())
         # an owner with an identity and no fixed keys is dynamic: it holds the whole seeded
         # bank and serves/writes only the keys the current epoch places on it
         self.dynamic = not owned_keys and identity is not None
@@ -181,7 +183,22 @@ class ParameterServer(ReactorServer):
         self.aggregate = check_aggregate(aggregate)
         self.version_history = max(1, int(version_history))
         self.private_policy = private_policy
+        if schedule_mode not in ("central", "decentralized"):
+            raise ValueError(f"schedule_mode must be 'central' or 'decentralized', got {schedule_mode!r}")
+        if schedule_mode == "decentralized" and self.compress != "none":
+            # a worker's base must be the exact replica state that quorum reads confirm by
+            # digest, so the down-link carries full-precision weights
+            raise ValueError("schedule_mode='decentralized' needs compress='none'")
         self.schedule_mode = schedule_mode
+        # decentralized coordination: the live worker set for the HRW-assignee check (a
+        # callable; else the workers of the last tracker directory), the staleness bound in
+        # base-version lag, and how often co-owner replicas are audited by digest
+        self.worker_set = worker_set
+        self.staleness_bound = 2 * self._topology.num_paths if staleness_bound is None else staleness_bound
+        self.staleness_weight = staleness_weight
+        self.replica_audit_interval = replica_audit_interval
+        self._dir_workers: list = []
+        self._last_audit = time.monotonic()
         self.down = down
         self.replicate_interval = replicate_interval
         self.scheduler_addr = _addr(scheduler_addr) if scheduler_addr is not None else None
@@ -212,7 +229,7 @@ class ParameterServer(ReactorServer):
         self._draining = False
         self._repl_stop = threading.Event()
         self._repl_thread = None
-        self._gen_counters: dict = {}
+        self._gen_counters: dict = {}   # path -> [open generation, monotonic time it opened]
         self._coordinates = set(coordinates or [])
         if resume_dir:
             if os.path.exists(os.path.join(resume_dir, self._shard_name())):
@@ -531,30 +548,152 @@ class ParameterServer(ReactorServer):
         return {"type": "ack", "applied": True}
 
     # -- decentralized coordination (path primary mints grants) ----------------
-    def _generation(self, msg: dict) -> dict:
-        path = tuple(msg.get("path") or ())
+    def _path_or_none(self, raw):
+        try:
+            path = tuple(int(i) for i in raw)
+        except (TypeError, ValueError):
+            return None
+        return path if path in self._paths else None
+
+    def _coordinates_path(self, path) -> bool:
+        """Decentralized: this owner coordinates ``path`` when it is the active primary of
+        the path's coordinator key (the path's private key when it has one)."""
+        if self.schedule_mode != "decentralized" or self._epoch is None:
+            return False
+        return self._primary(coordinator_key(self._topology.path_module_keys(path)))
+
+    def generation_of(self, path) -> int:
+        """The open generation of ``path`` on this owner (its coordinator's is the truth)."""
         with self._lock:
-            return {"type": "generation", "generation": self._gen_counters.get(path, 0)}
+            return self._gen_counters.get(tuple(path), (0, 0.0))[0]
+
+    def _worker_ids(self) -> list:
+        if self.worker_set is not None:
+            return sorted(set(self.worker_set() or []))
+        return list(self._dir_workers)
+
+    def _generation(self, msg: dict) -> dict:
+        """The path's open generation and how long it has been open (``age``): a worker
+        feeds the age to the same takeover rule the coordinator applies at commit, so the
+        two agree without sharing a clock."""
+        path = self._path_or_none(msg.get("path"))
+        if path is None:
+            return {"type": "generation", "ok": False}
+        with self._lock:
+            if not self._coordinates_path(path):
+                return {"type": "generation", "ok": False, "reason": "not_coordinator", "epoch": self._epoch_num}
+            gen, opened = self._gen_counters.setdefault(path, [0, time.monotonic()])
+            return {"type": "generation", "ok": True, "generation": gen, "age": max(0.0, time.monotonic() - opened),
+                    "epoch": self._epoch_num, "lease_ttl": self.lease_ttl, "staleness_bound": self.staleness_bound}
 
     def _commit(self, msg: dict, peer_id: str | None = None) -> dict:
-        """Decentralized commit: the path's coordinating owner checks the generation
-        and signs a grant with its own identity."""
-        path = tuple(msg.get("path") or ())
-        if self.identity is None or not path:
-            return {"type": "commit_ack", "accepted": False}
+        """Decentralized commit of ``(path, gen_id)`` to the path's coordinating owner.
+
+        Gates, in order: this owner coordinates the path; the generation is the open one
+        (a version fence: the slot closes at the first accepted commit); the committer is
+        the HRW assignee of the slot over the live worker set, or its successor once the
+        slot has been open ``lease_ttl`` per rank (skipped without a worker set); the rate
+        limit at the committer's reputation; a finite loss; the lag of the committer's
+        base versions behind this owner's (same epoch, at most ``staleness_bound``). An
+        accepted commit advances the generation and returns a grant signed with this
+        owner's identity, which the path's co-owners check against the epoch. Reference
+        behaviour: ``src/opendipaco/schedule/sharded.py:1328-1408``."""
+        def nack(reason, **extra):
+            return {"type": "commit_ack", "accepted": False, "reason": reason, **extra}
+
+        if self.schedule_mode != "decentralized" or self.identity is None:
+            return nack("not_decentralized")
+        path = self._path_or_none(msg.get("path"))
+        if path is None:
+            return nack("bad_path")
+        member = peer_id or msg.get("worker_id")
+        outcome = None
+        try:
+            with self._lock:
+                if not self._coordinates_path(path):
+                    return nack("not_coordinator", epoch=self._epoch_num)
+                slot = self._gen_counters.setdefault(path, [0, time.monotonic()])
+                gen, opened = slot
+                if msg.get("gen_id") != gen:
+                    return nack("stale_generation", generation=gen)
+                workers = self._worker_ids()
+                if workers and not is_assignee(member, path, gen, workers, salt=self.salt,
+                                               elapsed=time.monotonic() - opened, lease_ttl=self.lease_ttl):
+                    return nack("not_assignee")
+                if self.rate_limiter is not None and not self.rate_limiter.allow(
+                        peer_id, reputation=self.reputation.get(peer_id)):
+                    return nack("throttled")
+                if not loss_ok(msg.get("loss"), empty=bool(msg.get("empty"))):
+                    self.metrics.record_invalid_reject()
+                    outcome = False
+                    return nack("bad_loss")
+                base = msg.get("base_versions")
+                base = base if isinstance(base, dict) else {}
+                held = {k: self._versions[k] for k in base if k in self._active}
+                theirs = {k: _safe_version(base[k]) for k in held}
+                lag = None if any(v is None for v in theirs.values()) else version_lag(theirs, held)
+                if lag is None or lag > self.staleness_bound:
+                    self.metrics.record_stale_reject()
+                    return nack("stale")
+                slot[0], slot[1] = gen + 1, time.monotonic()
+                if self.corpus_weights is not None:
+                    w = float(self.corpus_weights.get(self._topology.path_index(path), 0.0))
+                else:
+                    w = as_finite_float(msg.get("weight"))
+                    w = 1.0 if w is None else min(max(w, 0.0), 1.0)
+                if self.staleness_weight == "inverse":
+                    w /= 1.0 + lag
+                grant = make_grant(path, self._topology.path_module_keys(path), w, uuid.uuid4().hex,
+                                   identity=self.identity)
+                self.metrics.record_update(lag)
+                outcome = True
+                return {"type": "commit_ack", "accepted": True, "generation": gen + 1, "grant": grant,
+                        "push_weight": w}
+        finally:
+            if outcome is True:
+                self.reputation.credit(peer_id)
+            elif outcome is False:
+                self.reputation.debit(peer_id)
+
+    def audit_replicas_once(self) -> dict:
+        """Decentralized: compare this owner's ``(version, digest)`` of every active key
+        with its co-owners'. A replica whose digest at the version a quorum confirms
+        differs loses reputation -- with ``min_owner_reputation`` set it then drops out of
+        the next derived epoch. A co-owner that does not answer is not blamed, nor is one
+        that is only behind. Returns ``{key: flagged peer ids}``."""
+        if self.schedule_mode != "decentralized" or self._epoch is None or self.peer_id is None:
+            return {}
         with self._lock:
-            gen = self._gen_counters.get(path, 0)
-            if msg.get("gen_id") != gen or not loss_ok(msg.get("loss"), empty=bool(msg.get("empty"))):
-                return {"type": "commit_ack", "accepted": False}
-            self._gen_counters[path] = gen + 1
-        keys = self._topology.path_module_keys(path)
-        if self.corpus_weights is not None:
-            w = float(self.corpus_weights.get(self._topology.path_index(path), 0.0))
-        else:
-            w = as_finite_float(msg.get("weight"))
-            w = 1.0 if w is None else min(max(w, 0.0), 1.0)
-        grant = make_grant(path, keys, w, uuid.uuid4().hex, identity=self.identity)
-        return {"type": "commit_ack", "accepted": True, "grant": grant, "push_weight": w}
+            keys, epoch = sorted(self._active), self._epoch
+        reports = {k: {self.peer_id: (tuple(v), d)} for k, (v, d) in self._digests({"keys": keys})["digests"].items()}
+        asks: dict = {}
+        for k in keys:
+            for o in owners_for(k, epoch):
+                if o["peer_id"] != self.peer_id and o.get("addr"):
+                    asks.setdefault((o["peer_id"], _addr(o["addr"])), []).append(k)
+        for (pid, addr), ks in asks.items():
+            try:
+                reply = self._peer_rpc(addr, {"type": "digest", "keys": ks})
+            except (OSError, ConnectionError, PermissionError):
+                continue
+            for k, rep in (reply.get("digests") or {}).items():
+                if k in reports and k in ks and isinstance(rep, (list, tuple)) and len(rep) == 2:
+                    v = _safe_version(rep[0])
+                    if v is not None and isinstance(rep[1], str):
+                        reports[k][pid] = (v, rep[1])
+        return self.apply_replica_audit(reports)
+
+    def apply_replica_audit(self, reports: dict) -> dict:
+        """The audit rule on gathered ``{key: {peer_id: (version, digest)}}`` reports."""
+        flagged = {}
+        q = max(2, self.read_quorum)
+        for k, by_peer in reports.items():
+            bad = divergent_peers(by_peer, confirm_version(list(by_peer.values()), q))
+            for pid in bad:
+                self.reputation.debit(pid)
+            if bad:
+                flagged[k] = bad
+        return flagged
 
     def _digests(self, msg: dict) -> dict:
         out = {}
@@ -632,10 +771,11 @@ class ParameterServer(ReactorServer):
         from .tracker import fetch_directory
 
         try:
-            recs = fetch_directory(self._tracker["addr"], roles=["owner"], auth_key=self._tracker["auth"],
-                                   tls=self._tracker["tls"])
+            everyone = fetch_directory(self._tracker["addr"], auth_key=self._tracker["auth"], tls=self._tracker["tls"])
         except (OSError, ConnectionError, PermissionError):
             return
+        self._dir_workers = _worker_directory_ids(everyone)
+        recs = [r for r in everyone if "owner" in (r.get("roles") or [])]
         eligible = (lambda pid: self.reputation.get(pid) >= self.min_owner_reputation) \
             if self.min_owner_reputation else None
         prev = self._epoch if self._epoch is not None and self._epoch.get("deterministic") else None
@@ -650,6 +790,10 @@ class ParameterServer(ReactorServer):
                 self._poll_scheduler_epoch()
                 self._derive_from_directory()
                 self._replicate_once()
+                if (self.schedule_mode == "decentralized"
+                        and time.monotonic() - self._last_audit >= self.replica_audit_interval):
+                    self._last_audit = time.monotonic()
+                    self.audit_replicas_once()
             except Exception:
                 logger.exception("replication pass failed")
 
@@ -1598,15 +1742,21 @@ def run_decentralized_worker(config, diloco, tracker, corpus, *, identity, auth_
                 keys = topo.path_module_keys(path)
                 coord = owners_for(coordinator_key(keys), epoch)[0]
                 try:
-                    gen = link.ps_rpc(coord["addr"], {"type": "generation", "path": path})["generation"]
+                    reply = link.ps_rpc(coord["addr"], {"type": "generation", "path": path})
                 except (OSError, ConnectionError, PermissionError):
                     continue
+                if not reply.get("ok", "generation" in reply):
+                    continue  # not the coordinator under its epoch (yet): ask again next pass
+                gen = reply["generation"]
                 if total_rounds is not None and gen >= total_rounds:
                     finished.add(path)
                     continue
+                # the coordinator's age of the open slot drives takeover on both sides
                 t0 = t_open.setdefault((path, gen), time.monotonic())
-                if is_assignee(identity.peer_id, path, gen, workers, salt=salt,
-                               elapsed=time.monotonic() - t0, lease_ttl=lease_ttl):
+                age = as_finite_float(reply.get("age"))
+                elapsed = age if age is not None else time.monotonic() - t0
+                if is_assignee(identity.peer_id, path, gen, workers, salt=salt, elapsed=elapsed,
+                               lease_ttl=lease_ttl):
                     picked = (path, gen, coord)
                     break
             if picked is None:
@@ -1617,7 +1767,7 @@ def run_decentralized_worker(config, diloco, tracker, corpus, *, identity, auth_
             path, gen, coord = picked
             try:
                 if _decentralized_task(engine, worker, link, topo, corpus, epoch, path, gen, coord, batch_size,
-                                       read_quorum):
+                                       read_quorum, identity.peer_id):
                     done += 1
             except (OSError, ConnectionError, PermissionError, ValueError):
                 time.sleep(poll_interval)
@@ -1626,19 +1776,22 @@ def run_decentralized_worker(config, diloco, tracker, corpus, *, identity, auth_
         link.close()
 
 
-def _decentralized_task(engine, worker, link, topo, corpus, epoch, path, gen, coord, batch_size, read_quorum) -> bool:
+def _decentralized_task(engine, worker, link, topo, corpus, epoch, path, gen, coord, batch_size, read_quorum,
+                        worker_id=None) -> bool:
     routing = _decentralized_routing(topo, path, epoch)
     keys = topo.path_module_keys(path)
     shared = [k for k in keys if not is_private_key(k)]
     confirmed = read_quorum_versions(list({_addr(a) for k in shared for a in routing[k]}), shared, read_quorum,
                                      lambda a, m: link.ps_rpc(a, m)) if read_quorum > 1 else {}
-    fetched = _fetch_keys(link, routing, keys, {}, {k for k in keys if is_private_key(k)}, {},
+    base: dict = {}
+    fetched = _fetch_keys(link, routing, keys, base, {k for k in keys if is_private_key(k)}, {},
                           pin={k: list(v[0]) for k, v in confirmed.items()} or None)
     for k, sd in fetched.items():
         engine.bank[k].load_state_dict({n: v.to(engine.device) for n, v in sd.items()})
     contrib = worker._train_path(path, corpus.shard(topo.path_index(path)), batch_size, gen)
     ack = link.ps_rpc(coord["addr"], {"type": "commit", "path": path, "gen_id": gen, "loss": contrib.loss,
-                                     "empty": contrib.empty, "weight": corpus.shard_weight(topo.path_index(path))})
+                                     "empty": contrib.empty, "weight": corpus.shard_weight(topo.path_index(path)),
+                                     "worker_id": worker_id, "base_versions": {k: list(v) for k, v in base.items()}})
     if not ack.get("accepted"):
         return False
     # one push per owner (a grant token is single-use per owner), carrying every key it replicates
