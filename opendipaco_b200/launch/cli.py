@@ -10,7 +10,7 @@
     opendipaco join         --scheduler HOST:PORT | --tracker HOST:PORT [--auth S]
     opendipaco ingest       --config c.yaml --shard-id N
     opendipaco tracker      --config c.yaml
-    opendipaco relay        --config c.yaml        (needs the optional libp2p packages)
+    opendipaco relay        --config c.yaml        (circuit relay for peers behind NAT)
     opendipaco init-config  --out c.yaml [--mode sharded]
     opendipaco gen-cert     --out certs/
     opendipaco gen-identity --out peer.pem
@@ -196,7 +196,7 @@ def build_parser() -> argparse.ArgumentParser:
     with_config("ingest", "resumably ingest a data shard", cmd_ingest).add_argument("--shard-id", type=int,
                                                                                       required=True)
     with_config("tracker", "run the rendezvous directory", cmd_tracker)
-    with_config("relay", "run a libp2p circuit relay", cmd_relay)
+    with_config("relay", "run a circuit relay for peers behind NAT", cmd_relay)
     g = sub.add_parser("gen-identity", help="generate an Ed25519 peer identity")
     g.add_argument("--out", required=True, help="path of the private-key PEM")
     g.set_defaults(func=cmd_gen_identity)

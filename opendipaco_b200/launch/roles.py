@@ -358,9 +358,17 @@ def run_parameter_server(cfg: LaunchConfig, shard_id: int = 0, *, port=None, on_
                              peer_tls=build_tls_client(cfg), **_decentralized_kw(cfg), **common,
                              **_server_kw(cfg, extra_admitted))
         ps.start()
+        circuits = None
+        if t.relays and t.kind == "tcp":
+            # behind NAT: reachable only through reservations on the configured relays
+            from ..schedule.relay import serve_via_relays
+
+            circuits = serve_via_relays(ps, t.relays, ident)
+            if not circuits:
+                raise RuntimeError(f"no relay of {t.relays} accepted a reservation")
         ps.start_tracker_heartbeat(tracker_addr or cfg.tracker_connect_addr(), _advertise_host(cfg),
                                    interval=own.heartbeat_interval, auth_key=t.auth_key, tls=build_tls_client(cfg),
-                                   seeds=cfg.tracker.seeds)
+                                   seeds=cfg.tracker.seeds, circuit_addrs=circuits)
     else:
         keys = sorted(model.build_topology().module_keys())
         owned = [k for k, s in assign_shards(keys, cfg.sharded.num_shards).items() if s == shard_id]
@@ -433,15 +441,21 @@ def run_tracker(cfg: LaunchConfig, *, on_start=None, stop_event=None):
     return tracker
 
 
-def run_relay(cfg: LaunchConfig, *, on_start=None, stop_event=None):
-    """A libp2p circuit relay; needs the optional libp2p packages."""
-    from ..schedule.p2p import Libp2pTransport
+def run_relay(cfg: LaunchConfig, *, on_start=None, stop_event=None, port=None):
+    """A circuit relay for NAT peers on ``transport.host:port`` (``schedule/relay.py``);
+    ``transport.admitted_peers`` (public keys), when set, limits who may reserve."""
+    from ..schedule.identity import peer_id_of
+    from ..schedule.relay import RelayServer
 
-    relay = Libp2pTransport(_identity(cfg, generate=True), relay=True, listen_addrs=tuple(cfg.transport.libp2p_listen),
-                            dcutr=cfg.transport.dcutr)
+    t = cfg.transport
+    admitted = [peer_id_of(p) for p in t.admitted_peers] or None
+    relay = RelayServer(_identity(cfg, generate=True), host=t.host, port=t.port if port is None else port,
+                        admitted=admitted).start()
+    print(f"relay listening: {relay.multiaddr(_advertise_host(cfg))}", flush=True)
     if on_start:
         on_start(relay)
     (stop_event or _signal_event()).wait()
+    relay.shutdown()
     return relay
 
 

@@ -53,6 +53,14 @@ def _signature_ok(public_key_hex: str, signature_hex: str, message: bytes) -> bo
     return True
 
 
+def verify_signature(public_key_hex, signature_hex, message: bytes) -> bool:
+    """Ed25519 check of a signature over ``message`` exactly (callers add their own
+    domain-separation prefix); malformed inputs fail."""
+    if not isinstance(public_key_hex, str) or not isinstance(signature_hex, str):
+        return False
+    return _signature_ok(public_key_hex, signature_hex, message)
+
+
 class PeerIdentity:
     """An Ed25519 key pair with its derived ``peer_id``."""
 

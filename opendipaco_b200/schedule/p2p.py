@@ -11,8 +11,10 @@ in this framework's image, so this module keeps the *interface*:
   seam: ``sch_rpc`` / ``sch_send`` / ``ps_rpc`` / ``close``) import libp2p lazily
   and raise ``Libp2pUnavailable`` with a clear message when it is missing.
 
-Everything else in ``schedule`` runs over the TCP reactor (optionally TLS), which
-covers ``public`` peers; ``nat`` peers need this tier.
+Everything else in ``schedule`` runs over the TCP reactor (optionally TLS). ``nat``
+peers are reached through this framework's own TCP circuit relay (``relay.py``):
+reservations, circuit multiaddrs of the same form, end-to-end authenticated sessions,
+without hole punching.
 """
 
 from __future__ import annotations

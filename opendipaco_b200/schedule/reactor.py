@@ -231,6 +231,9 @@ class ReactorServer:
         self.auth_keys = acceptable_keys(auth_key, accept_keys)
         self._admit_lock = threading.Lock()
         self.admitted_peers = None if admitted_peers is None else {self._hex(p) for p in admitted_peers}
+        # peer ids admitted without their key at hand (the owners of a signed epoch list
+        # peer ids, which hash from their public keys)
+        self._admitted_ids: set = set()
         self.max_msg_bytes = max_msg_bytes
         self.tls = tls
         self.io_threads = max(1, io_threads)
@@ -255,15 +258,30 @@ class ReactorServer:
         raise NotImplementedError
 
     # -------------------------------------------------------------- admission
+    def _identity_auth_on(self) -> bool:
+        return self.admitted_peers is not None or bool(self._admitted_ids)
+
     def peer_admitted(self, pub: str) -> bool:
         with self._admit_lock:
-            return self.admitted_peers is not None and pub.lower() in self.admitted_peers
+            if self.admitted_peers is not None and pub.lower() in self.admitted_peers:
+                return True
+            try:
+                return bool(self._admitted_ids) and peer_id_of(pub) in self._admitted_ids
+            except ValueError:  # not a hex key
+                return False
 
     def peer_id_admitted(self, peer_id: str) -> bool:
         with self._admit_lock:
-            if self.admitted_peers is None:
+            if peer_id in self._admitted_ids:
                 return True
+            if self.admitted_peers is None:
+                return not self._admitted_ids
             return any(peer_id_of(p) == peer_id for p in self.admitted_peers)
+
+    def admit_peer_id(self, peer_id: str) -> None:
+        """Admit the identity whose public key hashes to ``peer_id``."""
+        with self._admit_lock:
+            self._admitted_ids.add(str(peer_id))
 
     def admit_peer(self, pub) -> None:
         with self._admit_lock:
@@ -365,8 +383,28 @@ class ReactorServer:
         tests of failover, reconnect and restart-in-place)."""
         self._dead = True
         self._stop = True
+        for obs in self._observers:
+            obs.stop()
         self._on_loop(lambda: self._teardown(abort=True))
         self._finish()
+
+    def adopt_socket(self, sock: socket.socket) -> None:
+        """Serve an already-connected socket (a relayed circuit the server dialled out
+        for) exactly like an accepted connection: TLS when configured, the challenge,
+        then framed requests."""
+        async def serve():
+            loop = asyncio.get_running_loop()
+            reader = asyncio.StreamReader(limit=1 << 22)
+            protocol = asyncio.StreamReaderProtocol(reader)
+            transport, _ = await loop.connect_accepted_socket(
+                lambda: protocol, sock=sock, **({"ssl": self.tls, "ssl_handshake_timeout": 30.0} if self.tls else {}))
+            await self._session(reader, asyncio.StreamWriter(transport, protocol, reader, loop))
+
+        if self._loop is None or not self._loop.is_running() or self._stop:
+            sock.close()
+            return
+        sock.setblocking(False)
+        asyncio.run_coroutine_threadsafe(serve(), self._loop)
 
     # -------------------------------------------------------------- one connection
     async def _read_frame(self, reader: asyncio.StreamReader, cap: int) -> tuple[bytes, int]:
@@ -383,7 +421,7 @@ class ReactorServer:
 
     async def _authenticate(self, reader, writer) -> tuple[bool, str | None]:
         """Challenge / response when the server requires it: (accepted, peer id)."""
-        if self.auth_keys is None and self.admitted_peers is None:
+        if self.auth_keys is None and not self._identity_auth_on():
             return True, None
         nonce = os.urandom(32)
         writer.write(self._frame({"type": "challenge", "nonce": nonce.hex()}))
@@ -394,7 +432,7 @@ class ReactorServer:
             return False, None
         if self.auth_keys is not None and "mac" in msg and verify_mac(msg.get("mac", ""), nonce, self.auth_keys):
             accepted, peer = True, None
-        elif (self.admitted_peers is not None and "pub" in msg and self.peer_admitted(msg.get("pub", ""))
+        elif (self._identity_auth_on() and "pub" in msg and self.peer_admitted(msg.get("pub", ""))
               and verify_auth(msg["pub"], msg.get("sig", ""), nonce)):
             accepted, peer = True, peer_id_of(msg["pub"])
         else:

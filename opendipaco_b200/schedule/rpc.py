@@ -9,12 +9,28 @@ import ssl
 import threading
 import time
 
+from .p2p import CIRCUIT_SEP
 from .wire import DEFAULT_MAX_MSG_BYTES, client_handshake, recv_msg, send_msg
 
 
 def connect(addr, auth_key=None, max_msg_bytes: int = DEFAULT_MAX_MSG_BYTES, timeout: float = 10.0, *, tls=None,
             server_hostname: str | None = None) -> socket.socket:
-    """Dial ``(host, port)`` (retrying until ``timeout``), optionally wrap in TLS, authenticate."""
+    """Dial ``(host, port)`` (retrying until ``timeout``), optionally wrap in TLS, authenticate.
+
+    ``addr`` may also be a relay circuit address (a NAT peer reached through a relay) or
+    a list of addresses tried in order (a peer's several relays)."""
+    if isinstance(addr, str):
+        return _connect_circuit(addr, auth_key, timeout, tls, server_hostname)
+    if _address_list(addr):
+        last = None
+        for a in addr:
+            try:
+                return connect(a, auth_key, max_msg_bytes, timeout, tls=tls, server_hostname=server_hostname)
+            except (OSError, ConnectionError) as exc:
+                if isinstance(exc, PermissionError):
+                    raise
+                last = exc
+        raise ConnectionError(f"no address of {addr!r} answered: {last}")
     host, port = addr[0], int(addr[1])
     deadline, last = time.monotonic() + timeout, None
     while time.monotonic() < deadline:
@@ -38,6 +54,36 @@ def connect(addr, auth_key=None, max_msg_bytes: int = DEFAULT_MAX_MSG_BYTES, tim
     raise ConnectionError(f"could not connect to {host}:{port}: {last}")
 
 
+def _address_list(addr) -> bool:
+    """A list of addresses (circuit strings or ``(host, port)`` pairs), not one pair."""
+    return (isinstance(addr, (list, tuple)) and len(addr) > 0
+            and all((isinstance(a, str) and CIRCUIT_SEP in a) or isinstance(a, (list, tuple)) for a in addr))
+
+
+def _hostname(addr):
+    """The TLS server name of a ``(host, port)`` address (None for circuits and lists)."""
+    if isinstance(addr, (list, tuple)) and not _address_list(addr) and isinstance(addr[0], str):
+        return addr[0]
+    return None
+
+
+def _connect_circuit(addr: str, auth_key, timeout: float, tls, server_hostname):
+    from .relay import dial_circuit
+
+    s = dial_circuit(addr, timeout)
+    try:
+        if tls is not None:
+            s = tls.wrap_socket(s, server_hostname=server_hostname or "localhost")
+        s.settimeout(timeout)
+        if not client_handshake(s, auth_key):
+            raise PermissionError(f"{addr} rejected authentication")
+        s.settimeout(None)
+        return s
+    except BaseException:
+        s.close()
+        raise
+
+
 def rpc(sock: socket.socket, msg: dict, max_msg_bytes: int = DEFAULT_MAX_MSG_BYTES):
     send_msg(sock, msg)
     reply = recv_msg(sock, max_msg_bytes)
@@ -54,7 +100,7 @@ def rpc_locked(sock, lock: threading.Lock, msg: dict, max_msg_bytes: int = DEFAU
 def one_shot(addr, msg: dict, *, auth_key=None, tls=None, timeout: float = 10.0,
              max_msg_bytes: int = DEFAULT_MAX_MSG_BYTES):
     """Connect, send one request, return the reply, close."""
-    s = connect(addr, auth_key, max_msg_bytes, timeout, tls=tls, server_hostname=addr[0])
+    s = connect(addr, auth_key, max_msg_bytes, timeout, tls=tls, server_hostname=_hostname(addr))
     try:
         return rpc(s, msg, max_msg_bytes)
     finally:

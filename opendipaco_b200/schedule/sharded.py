@@ -163,7 +163,7 @@ class ParameterServer(ReactorServer):
                  coordinates=None, scheduler_addr=None, peer_tls=None, private_quorum=2, salt="", k=3,
                  lease_ttl=20.0, read_quorum=1, directory_ttl=30.0, reputation=None, rate_limiter=None,
                  min_owner_reputation=0.0, corpus_weights=None, worker_set=None, staleness_bound=None,
-                 staleness_weight="inverse", replica_audit_interval=30.0, **kw):
+                 staleness_weight="inverse", replica_audit_interval=30.0, sync_timeout=60.0, **kw):
         super().__init__(host=host, port=port, auth_key=auth_key, **kw)
         self.config, self.diloco, self.device = config, diloco, torch.device(device)
         self._topology = config.build_topology()
@@ -230,6 +230,14 @@ class ParameterServer(ReactorServer):
         self._repl_stop = threading.Event()
         self._repl_thread = None
         self._gen_counters: dict = {}   # path -> [open generation, monotonic time it opened]
+        # a server without any authentication trusts every session (a closed test cluster);
+        # otherwise exact state (weights + momentum) only goes to, and drains only come
+        # from, sessions identity-authenticated as owners of the key
+        self._open = self.auth_keys is None and self.admitted_peers is None
+        # keys gained in a non-bootstrap epoch, waiting for a previous replica's state:
+        # key -> (monotonic time of the first attempt, the epoch to sync from)
+        self._syncing: dict = {}
+        self.sync_timeout = sync_timeout
         self._coordinates = set(coordinates or [])
         if resume_dir:
             if os.path.exists(os.path.join(resume_dir, self._shard_name())):
@@ -296,29 +304,86 @@ class ParameterServer(ReactorServer):
         if not record:
             return
         boot = bool(record.get("bootstrap")) if bootstrap is None else bootstrap
+        if not self._open:
+            # the owners of a verified epoch may dial this server by identity
+            for o in record.get("owners") or []:
+                if isinstance(o.get("peer_id"), str):
+                    self.admit_peer_id(o["peer_id"])
         with self._lock:
             prev = self._epoch
             act = {k for k in self.bank if self.peer_id in {o["peer_id"] for o in owners_for(k, record)}}
             gained = act - self._active
+        pending = set()
         if gained and not boot and prev is not None:
-            self._sync_keys(sorted(gained), prev)
+            pending = set(gained) - self._sync_keys(sorted(gained), prev, record)
         with self._lock:
             self._epoch = record
             self._epoch_num = int(record.get("epoch", 0))
-            self._active = act
+            now = time.monotonic()
+            self._syncing = {k: self._syncing.get(k, (now, prev)) for k in pending}
+            self._active = act - pending
 
-    def _sync_keys(self, keys, epoch) -> None:
+    def _sync_keys(self, keys, epoch, claim=None) -> set:
+        """Pull the newest state of ``keys`` from their other replicas under ``epoch``,
+        presenting ``claim`` (the epoch in which this owner holds them); returns the keys
+        some replica answered for."""
         plan: dict = {}
         for k in keys:
             for o in owners_for(k, epoch):
                 if o["peer_id"] != self.peer_id:
                     plan.setdefault(_addr(o["addr"]), []).append(k)
+        answered = set()
         for addr, ks in plan.items():
+            msg = {"type": "fetch", "keys": ks, "include_state": True, "have": {}}
+            if claim is not None:
+                msg["epoch"] = claim
             try:
-                reply = self._peer_rpc(addr, {"type": "fetch", "keys": ks, "include_state": True, "have": {}})
+                reply = self._peer_rpc(addr, msg)
             except (OSError, ConnectionError, PermissionError):
                 continue
             self._adopt(reply)
+            answered |= set(reply.get("versions") or {}) & set(ks)
+        return answered
+
+    def _retry_sync(self) -> None:
+        """Keys still syncing: ask the previous replicas again; a key none of them has
+        answered for ``sync_timeout`` seconds is served from the local state (its
+        replicas are gone, and waiting longer cannot bring the state back)."""
+        with self._lock:
+            todo, claim = dict(self._syncing), self._epoch
+        if not todo:
+            return
+        done = set()
+        for src in {id(e): e for _, e in todo.values()}.values():
+            keys = sorted(k for k, (_, e) in todo.items() if e is src)
+            done |= self._sync_keys(keys, src, claim)
+        now = time.monotonic()
+        expired = {k for k, (t0, _) in todo.items() if k not in done and now - t0 >= self.sync_timeout}
+        if expired:
+            logger.warning("no previous replica answered for %s within %.0fs: serving the local state",
+                           sorted(expired), self.sync_timeout)
+        with self._lock:
+            for k in done | expired:
+                if self._syncing.pop(k, None) is not None and claim is self._epoch and \
+                        self.peer_id in {o["peer_id"] for o in owners_for(k, self._epoch)}:
+                    self._active.add(k)
+
+    def _state_allowed(self, key, peer_id, claim=None) -> bool:
+        """May this session pull exact state of ``key`` or drain it here? Without an
+        epoch (a fixed shard) or on an open server: yes. Otherwise only a session
+        authenticated as an owner of the key, under this server's epoch or under a newer
+        valid epoch the session presents (a new owner syncing before this server has
+        seen that epoch)."""
+        if self._epoch is None or self._open:
+            return True
+        if peer_id is None:
+            return False
+        if peer_id in {o["peer_id"] for o in owners_for(key, self._epoch)}:
+            return True
+        return (isinstance(claim, dict) and not epoch_newer(self._epoch, claim)
+                and verify_epoch_record(claim, signer_pub=self.scheduler_pub,
+                                        allow_deterministic=self.schedule_mode == "decentralized")
+                and peer_id in {o["peer_id"] for o in owners_for(key, claim)})
 
     def _adopt(self, reply) -> dict:
         """Take every key of an ``include_state`` fetch reply that is newer than ours."""
@@ -377,6 +442,9 @@ class ParameterServer(ReactorServer):
                         weights[k], versions[k] = compress_state(snap, self.compress), tuple(pin[k])
                     continue
                 if want_state:
+                    if not self._state_allowed(k, peer_id, msg.get("epoch")):
+                        missing.append(k)
+                        continue
                     versions[k] = self._versions[k]
                     if tuple(have.get(k) or ()) != self._versions[k]:
                         weights[k] = _state_cpu(self.bank[k].state_dict())
@@ -705,10 +773,15 @@ class ParameterServer(ReactorServer):
 
     # -- replication ------------------------------------------------------------
     def _drain_recv(self, msg: dict, peer_id: str | None = None) -> dict:
+        """A leaving primary's newest state, adopted when strictly newer and sent by an
+        owner of the key. Refused in decentralized mode: a pushed version is not
+        quorum-confirmed there, so a Byzantine owner could poison its co-owners."""
         adopted = []
+        if self.schedule_mode == "decentralized":
+            return {"type": "drained", "adopted": adopted}
         with self._lock:
             for k, p in (msg.get("states") or {}).items():
-                if k not in self.bank or not isinstance(p, dict):
+                if k not in self.bank or not isinstance(p, dict) or not self._state_allowed(k, peer_id):
                     continue
                 v, sd = _safe_version(p.get("version")), p.get("weights")
                 if v is None or sd is None or v <= self._versions[k]:
@@ -720,8 +793,18 @@ class ParameterServer(ReactorServer):
                 adopted.append(k)
         return {"type": "drained", "adopted": adopted}
 
+    def _peer_cred(self):
+        """What this owner presents when dialing another owner: ``peer_auth`` when given,
+        else its identity (so the other side can gate exact state on the session), else
+        the shared key; nothing towards open servers."""
+        if self.peer_auth is not None:
+            return self.peer_auth
+        if self._open:
+            return None
+        return self.identity if self.identity is not None else self.auth_key
+
     def _peer_rpc(self, addr, msg):
-        cred = next((c for c in (self.peer_auth, self.auth_key, self.identity) if c is not None), None)
+        cred = self._peer_cred()
         s = connect(_addr(addr), cred, timeout=5.0, tls=self.peer_tls)
         try:
             return rpc(s, msg)
@@ -743,11 +826,39 @@ class ParameterServer(ReactorServer):
         for addr, keys in plan.items():
             try:
                 reply = self._peer_rpc(addr, {"type": "fetch", "keys": keys, "include_state": True,
-                                              "have": {k: list(have[k]) for k in keys}})
+                                              "have": {k: list(have[k]) for k in keys}, "epoch": self._epoch})
             except (OSError, ConnectionError, PermissionError):
                 continue
+            if self.schedule_mode == "decentralized" and self.read_quorum > 1:
+                reply = self._quorum_filter(reply, addr)
             pulled.update(self._adopt(reply))
         return pulled
+
+    def _quorum_filter(self, reply: dict, source) -> dict:
+        """Decentralized: keep only pulled states that ``read_quorum`` replicas (the
+        source included) report at the same ``(version, digest)``, so one Byzantine
+        primary cannot poison its backups through replication."""
+        weights = dict(reply.get("weights") or {})
+        with self._lock:
+            epoch = self._epoch
+        for k in list(weights):
+            v = _safe_version((reply.get("versions") or {}).get(k))
+            want = (v, state_digest(weights[k])) if v is not None else None
+            votes = 1 if want is not None else 0
+            for o in owners_for(k, epoch):
+                if want is None or votes >= self.read_quorum:
+                    break
+                if o["peer_id"] == self.peer_id or _addr(o["addr"]) == _addr(source):
+                    continue
+                try:
+                    rep = (self._peer_rpc(o["addr"], {"type": "digest", "keys": [k]}).get("digests") or {}).get(k)
+                except (OSError, ConnectionError, PermissionError):
+                    continue
+                if isinstance(rep, (list, tuple)) and len(rep) == 2 and (_safe_version(rep[0]), rep[1]) == want:
+                    votes += 1
+            if votes < self.read_quorum:
+                weights.pop(k)
+        return dict(reply, weights=weights)
 
     def _poll_scheduler_epoch(self) -> None:
         if self.scheduler_addr is None:
@@ -789,6 +900,7 @@ class ParameterServer(ReactorServer):
                 self._sweep_buffers()
                 self._poll_scheduler_epoch()
                 self._derive_from_directory()
+                self._retry_sync()
                 self._replicate_once()
                 if (self.schedule_mode == "decentralized"
                         and time.monotonic() - self._last_audit >= self.replica_audit_interval):
@@ -806,9 +918,12 @@ class ParameterServer(ReactorServer):
                 threading.Thread(target=self._poll_scheduler_epoch, daemon=True).start()
 
     def start_tracker_heartbeat(self, tracker_addr, advertise_host, *, interval=10.0, auth_key=None, tls=None,
-                                seeds=()):
+                                seeds=(), circuit_addrs=None):
         """Keep this owner's signed record registered on the tracker(s) (re-register every
-        ``interval`` s, below the tracker's TTL); deregistered on a graceful shutdown."""
+        ``interval`` s, below the tracker's TTL); deregistered on a graceful shutdown.
+        With ``circuit_addrs`` (from :func:`relay.serve_via_relays`) the owner registers
+        as a ``nat`` peer reachable through those relays instead of at
+        ``advertise_host``."""
         from .tracker import dedup_seeds, register_peer
 
         if self.identity is None:
@@ -821,8 +936,13 @@ class ParameterServer(ReactorServer):
             while True:
                 for a in addrs if not self._hb_paused.is_set() else ():
                     try:
-                        register_peer(a, self.identity, reachability="public", peer_addr=(advertise_host, self.port),
-                                      roles=["owner"], auth_key=auth_key, tls=tls, timeout=5.0)
+                        if circuit_addrs:
+                            register_peer(a, self.identity, reachability="nat", circuit_addrs=list(circuit_addrs),
+                                          roles=["owner"], auth_key=auth_key, tls=tls, timeout=5.0)
+                        else:
+                            register_peer(a, self.identity, reachability="public",
+                                          peer_addr=(advertise_host, self.port), roles=["owner"], auth_key=auth_key,
+                                          tls=tls, timeout=5.0)
                     except (OSError, ConnectionError, PermissionError):
                         continue
                 if stop.wait(interval):

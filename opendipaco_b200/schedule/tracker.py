@@ -201,10 +201,11 @@ def tracker_rpc(addr, msg, *, auth_key=None, tls=None, timeout: float = 10.0,
 
 
 def register_peer(addr, identity: PeerIdentity, *, reachability: str = "nat", peer_addr=None, roles=(),
-                  capabilities=None, auth_key=None, tls=None, timeout: float = 10.0) -> dict:
-    """Register (or refresh, before ``ttl`` runs out) this peer's record."""
+                  capabilities=None, auth_key=None, tls=None, timeout: float = 10.0, circuit_addrs=None) -> dict:
+    """Register (or refresh, before ``ttl`` runs out) this peer's record; a ``nat`` peer
+    may advertise the relay ``circuit_addrs`` it is reachable through."""
     rec = make_peer_record(identity, reachability=reachability, addr=peer_addr, roles=roles,
-                           capabilities=capabilities)
+                           capabilities=capabilities, circuit_addrs=circuit_addrs)
     return tracker_rpc(addr, {"type": "register", "record": rec}, auth_key=auth_key, tls=tls, timeout=timeout)
 
 
