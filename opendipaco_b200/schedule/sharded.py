@@ -181,7 +181,8 @@ class ParameterServer(ReactorServer):
         self.robust = robustness
         self.quorum_target, self.quorum_timeout = quorum_target, quorum_timeout
         self.aggregate = check_aggregate(aggregate)
-        self.version_history = max(1, int(version_history))
+        # delta-down needs past versions to diff against: a ring of 8 unless one was given
+        self.version_history = max(1, int(version_history)) if down != "delta" or version_history > 1 else 8
         self.private_policy = private_policy
         if schedule_mode not in ("central", "decentralized"):
             raise ValueError(f"schedule_mode must be 'central' or 'decentralized', got {schedule_mode!r}")
@@ -1644,14 +1645,16 @@ def _fetch_keys(link, routing, keys, versions, cold_keys, keyframes, pin=None):
         reply = link.ps_rpc(addr, msg)
         for k, payload in (reply.get("weights") or {}).items():
             if isinstance(payload, dict) and "delta" in payload:
-                base = keyframes.get((k, tuple(payload["base"])))
-                if base is None:
-                    raise ValueError(f"delta for {k} against unknown keyframe")
-                payload = apply_state_delta(base, payload["delta"])
+                held = keyframes.get(k)
+                if held is None or held[0] != tuple(payload["base"]):
+                    versions.pop(k, None)  # ask for full weights next time
+                    raise ValueError(f"delta for {k} against a keyframe this worker does not hold")
+                payload = apply_state_delta(held[1], payload["delta"])
             out[k] = payload
             v = _version_pair(reply["versions"][k])
             versions[k] = v
-            keyframes[(k, v)] = {n: t.float() if t.is_floating_point() else t for n, t in payload.items()}
+            # one keyframe per key: the state at the version this worker reports as held
+            keyframes[k] = (v, {n: t.float() if t.is_floating_point() else t for n, t in payload.items()})
     return out
 
 
