@@ -240,6 +240,10 @@ class ParameterServer(ReactorServer):
         self._syncing: dict = {}
         self.sync_timeout = sync_timeout
         self._coordinates = set(coordinates or [])
+        # restarted from disk: before serving its first epoch's keys, this owner reconciles
+        # them with their other replicas (the newest version wins), since a backup may have
+        # trained past this owner's checkpoint
+        self._resumed = bool(resume_dir)
         if resume_dir:
             if os.path.exists(os.path.join(resume_dir, self._shard_name())):
                 self.load_shard(resume_dir)
@@ -317,6 +321,10 @@ class ParameterServer(ReactorServer):
         pending = set()
         if gained and not boot and prev is not None:
             pending = set(gained) - self._sync_keys(sorted(gained), prev, record)
+        elif gained and prev is None and self._resumed:
+            # a restart: reconcile with the co-owners of the epoch it rejoins
+            prev = record
+            pending = set(gained) - self._sync_keys(sorted(gained), record, record)
         with self._lock:
             self._epoch = record
             self._epoch_num = int(record.get("epoch", 0))
@@ -327,13 +335,15 @@ class ParameterServer(ReactorServer):
     def _sync_keys(self, keys, epoch, claim=None) -> set:
         """Pull the newest state of ``keys`` from their other replicas under ``epoch``,
         presenting ``claim`` (the epoch in which this owner holds them); returns the keys
-        some replica answered for."""
+        some replica answered for, and the keys no other replica holds (nothing to wait for)."""
         plan: dict = {}
-        for k in keys:
-            for o in owners_for(k, epoch):
-                if o["peer_id"] != self.peer_id:
-                    plan.setdefault(_addr(o["addr"]), []).append(k)
         answered = set()
+        for k in keys:
+            others = [o for o in owners_for(k, epoch) if o["peer_id"] != self.peer_id]
+            if not others:
+                answered.add(k)
+            for o in others:
+                plan.setdefault(_addr(o["addr"]), []).append(k)
         for addr, ks in plan.items():
             msg = {"type": "fetch", "keys": ks, "include_state": True, "have": {}}
             if claim is not None:

@@ -168,3 +168,47 @@ def test_decentralized_backup_adopts_only_quorum_confirmed_state():
         assert b1._replicate_once().get(key) == prim._versions[key]
     finally:
         _shutdown(pss)
+
+
+def test_restarted_owner_adopts_the_newest_replica_before_serving(tmp_path):
+    """A primary restarts from a checkpoint older than its backup's state: it pulls the
+    backup's newer version (weights and momentum) before it serves the key, and a lone
+    owner (no other replica) serves its checkpoint at once."""
+    cfg, sched = tiny_config(), PeerIdentity.generate()
+    pss = _servers(2, cfg, sched)
+    try:
+        epoch = make_epoch_record(sched, epoch=0, owner_records=_recs(pss), k=2, bootstrap=True)
+        for ps in pss:
+            ps.apply_epoch(epoch)
+        key = "L1E1"
+        prim_id = owners_for(key, epoch)[0]["peer_id"]
+        prim = next(p for p in pss if p.peer_id == prim_id)
+        back = next(p for p in pss if p is not prim)
+        prim.save_modules(str(tmp_path))                    # checkpoint at (0, 0)
+        with torch.no_grad():
+            next(iter(back.bank[key].parameters())).add_(0.25)
+        back._versions[key] = (0, 4)                        # the backup trained on
+        ident = prim.identity
+        prim.shutdown()
+        again = ParameterServer(cfg, [], DL, host="127.0.0.1", auth_key=KEY, identity=ident,
+                                replicate_interval=3600, scheduler_pub=sched.public_key_hex,
+                                resume_dir=str(tmp_path))
+        again.start()
+        try:
+            moved = make_epoch_record(sched, epoch=1, owner_records=_recs([again, back]), k=2)
+            back.apply_epoch(moved)
+            again.apply_epoch(moved)
+            assert key in again._active and again._versions[key] == (0, 4)
+            assert torch.equal(next(iter(again.bank[key].parameters())), next(iter(back.bank[key].parameters())))
+        finally:
+            again.shutdown()
+        lone = ParameterServer(cfg, [], DL, host="127.0.0.1", auth_key=KEY, identity=ident, replicate_interval=3600,
+                               scheduler_pub=sched.public_key_hex, resume_dir=str(tmp_path))
+        lone.start()
+        try:
+            lone.apply_epoch(make_epoch_record(sched, epoch=2, owner_records=_recs([lone]), k=1))
+            assert key in lone._active and not lone._syncing
+        finally:
+            lone.shutdown()
+    finally:
+        _shutdown(pss)
