@@ -400,6 +400,11 @@ def run_worker_role(cfg: LaunchConfig, *, addr=None, scheduler_addr=None, max_ta
         from ..schedule.p2p import _require_libp2p
 
         _require_libp2p()
+    if stop_event is None and (cfg.mode == "sharded" or cfg.schedule.mode == "decentralized"):
+        # SIGINT / SIGTERM end these loops between tasks (a graceful leave); the
+        # coordinator's worker keeps the default handlers, as nothing there would
+        # consume the event and the signal would otherwise be swallowed
+        stop_event = _signal_event()
     if cfg.schedule.mode == "decentralized":
         own = cfg.ownership
         corpus = build_corpus(cfg, model, build_documents(cfg))
