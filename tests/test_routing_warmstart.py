@@ -1,5 +1,6 @@
-"""Warm start from a pretrained dense Llama (models/init.py) and the discriminative
-router (routing/discriminative.py), both against the reference's results."""
+"""Warm start from a pretrained dense Llama (models/init.py): layers copied by depth, the
+warm-started path reproduces the pretrained logits, and the discriminative router
+(routing/discriminative.py), both against the reference's results."""
 
 import torch
 
@@ -75,3 +76,41 @@ def test_discriminative_router_matches_reference(reference_pkg):
             assert torch.equal(ours.state_dict()[n], t)
         assert (ours.predict(x) == y).float().mean() > 0.75
         assert ours.predict_topk(x, 9).shape == (200, 4)
+
+
+def test_warm_started_path_reproduces_the_pretrained_logits():
+    """A path whose modules were warm-started from a pretrained Llama of the same depth
+    computes that model's logits (fp32, same token ids)."""
+    from opendipaco_b200.models.path import build_path_model
+
+    bb = BackboneConfig(vocab_size=300, hidden_size=64, num_attention_heads=4, num_key_value_heads=2,
+                        intermediate_size=128, layers_per_level=[1, 2], max_position_embeddings=64)
+    cfg = DiPaCoConfig(backbone=bb, level_sizes=[2, 2], sequence_length=32)
+    topo = cfg.build_topology()
+    bank = build_module_bank(cfg, seed=0)
+    hf = _hf_llama(bb, 3)
+    hf.config.rms_norm_eps = bb.rms_norm_eps  # the pretrained model's norm epsilon matches the backbone's
+    for m in hf.modules():
+        if hasattr(m, "variance_epsilon"):
+            m.variance_epsilon = bb.rms_norm_eps
+    warm_start_modules(bank, topo, hf)
+    ids = torch.randint(0, 300, (2, 24), generator=torch.Generator().manual_seed(0))
+    with torch.no_grad():
+        want = hf(input_ids=ids).logits
+        for p in range(cfg.num_paths):
+            model = build_path_model(cfg, topo.path_from_index(p), bank).eval()
+            out = model(ids)
+            got = out[0] if isinstance(out, tuple) else out
+            torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-4)
+
+
+def test_eval_sequence_length_defaults_and_validation():
+    import pytest
+
+    bb = BackboneConfig(vocab_size=64, hidden_size=32, num_attention_heads=4, intermediate_size=64,
+                        layers_per_level=[1, 1], max_position_embeddings=256)
+    assert DiPaCoConfig(backbone=bb, level_sizes=[2, 2], sequence_length=32).eval_seq_len == 32
+    assert DiPaCoConfig(backbone=bb, level_sizes=[2, 2], sequence_length=32,
+                        eval_sequence_length=128).eval_seq_len == 128
+    with pytest.raises(ValueError):
+        DiPaCoConfig(backbone=bb, level_sizes=[2, 2], sequence_length=32, eval_sequence_length=0)
