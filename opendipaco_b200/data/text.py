@@ -25,7 +25,7 @@ def train_tokenizer(texts: Iterable[str], *, vocab_size: int = 32000, model: str
                     unk_token: str = "<unk>", eos_token: str = "</s>", pad_token: str = "<pad>"):
     """Train a fresh Unigram (SentencePiece-style) or byte-level BPE tokenizer."""
     try:
-        from tokenizers import Tokenizer, models, pre_tokenizers, trainers
+        from tokenizers import Tokenizer, decoders, models, pre_tokenizers, trainers
         from transformers import PreTrainedTokenizerFast
     except ImportError as exc:  # pragma: no cover
         raise ImportError(_HINT) from exc
@@ -33,11 +33,13 @@ def train_tokenizer(texts: Iterable[str], *, vocab_size: int = 32000, model: str
     if model == "unigram":
         tok = Tokenizer(models.Unigram())
         tok.pre_tokenizer = pre_tokenizers.Metaspace()
+        tok.decoder = decoders.Metaspace()
         trainer = trainers.UnigramTrainer(vocab_size=vocab_size, special_tokens=specials,
                                           unk_token=unk_token)
     elif model == "bpe":
         tok = Tokenizer(models.BPE(unk_token=unk_token))
         tok.pre_tokenizer = pre_tokenizers.ByteLevel()
+        tok.decoder = decoders.ByteLevel()
         trainer = trainers.BpeTrainer(vocab_size=vocab_size, special_tokens=specials)
     else:
         raise ValueError(f"model must be 'unigram' or 'bpe', got {model!r}")
