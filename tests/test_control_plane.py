@@ -176,3 +176,20 @@ def test_drain_ignores_older_versions():
     reply = ps._drain_recv({"states": {key: {"version": [0, 4], "weights": sd, "state": None}}})
     assert reply["adopted"] == [key] and ps._versions[key] == (0, 4)
     assert all(torch.equal(a, sd[n]) for n, a in ps.bank[key].state_dict().items())
+
+
+def test_rate_guards_empty_commits_and_reclaimed_leases():
+    s = _sched()
+    for bad in ((None, 100, 1.0), ("w", 0, 1.0), ("w", 100, 0.0), ("w", -5, 1.0)):
+        s._record_rate(*bad)
+    assert s.worker_rate("w") is None
+    t = _req(s, "w")
+    s._lease_at[tuple(t["path"])] -= 1.0
+    assert _commit(s, t, "w", empty=True, loss=None)["accepted"]  # an empty shard trains nothing
+    assert s.worker_rate("w") is None
+    s2 = _sched(heartbeat_timeout=0.01)
+    t = _req(s2, "z")
+    time.sleep(0.05)
+    with s2._lock:
+        s2._reclaim_locked()              # the lease ran out: the late commit is refused, no rate
+    assert not _commit(s2, t, "z")["accepted"] and s2.worker_rate("z") is None
