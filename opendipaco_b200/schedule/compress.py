@@ -290,6 +290,34 @@ def maybe_dequantize(items) -> list[torch.Tensor]:
 
 
 # ------------------------------------------------------------------ digests
+def declared_shape(payload):
+    """The dense shape a pseudo-gradient payload claims, read without decoding it (None
+    when it is not a payload)."""
+    try:
+        if torch.is_tensor(payload):
+            return tuple(payload.shape)
+        if isinstance(payload, dict):
+            if torch.is_tensor(payload.get("q")):
+                return tuple(payload["q"].shape)
+            if "q4" in payload:
+                return tuple(int(s) for s in payload["shape"])
+            if "sp" in payload:
+                return tuple(int(s) for s in payload["sp"])
+    except (TypeError, ValueError, KeyError):
+        return None
+    return None
+
+
+def decode_checked(items, shapes) -> list[torch.Tensor]:
+    """Decode a pseudo-gradient list after checking that the shapes it declares are
+    exactly ``shapes`` (before anything is allocated: a payload claiming a huge shape is
+    refused, not materialised)."""
+    if not isinstance(items, list) or len(items) != len(shapes) or any(
+            declared_shape(p) != tuple(s) for p, s in zip(items, shapes)):
+        raise ValueError("pseudo-gradient payload does not match the module's shapes")
+    return maybe_dequantize(items)
+
+
 def _digest_tensor(h, t: torch.Tensor) -> None:
     enc, _ = _Int8.encode(t.detach().cpu())
     s = enc["s"]

@@ -46,7 +46,7 @@ from ..optim.diloco import apply_outer_grads, make_outer_optimizer
 from ..parallel.backend.local import LocalBackend
 from ..topology import Path, is_private_key
 from ..train.loop import _opt_state_cpu, _state_cpu
-from .compress import check_mode, compress_delta, compress_shard, compress_state, maybe_dequantize, restore_shard
+from .compress import check_mode, compress_delta, compress_shard, compress_state, decode_checked, restore_shard
 from .guard import clip_norm_, contribution_ok
 from .reactor import ReactorServer
 from .rpc import connect
@@ -167,12 +167,20 @@ class CoordinatorServer(ReactorServer):
     def _decode_upload(self, msg: dict):
         """(shared pseudo-gradients or None when malformed, private states, valid)."""
         e = self.engine
-        try:
-            shared = {k: maybe_dequantize(v) for k, v in (msg.get("shared_grad") or {}).items()
-                      if k in self._versions}
+        raw, priv = msg.get("shared_grad") or {}, msg.get("private_weights") or {}
+        if not (isinstance(raw, dict) and isinstance(priv, dict)):
+            return {}, {}, False
+        try:  # declared shapes are screened before any payload is decoded
+            shared = {k: decode_checked(v, [tuple(p.shape) for p in e.bank[k].parameters()])
+                      for k, v in raw.items() if k in self._versions}
         except (TypeError, KeyError, ValueError):
             shared = None
-        private = {k: v for k, v in (msg.get("private_weights") or {}).items() if is_private_key(k) and k in e.bank}
+        private = {k: v for k, v in priv.items() if is_private_key(k) and k in e.bank}
+        for k, sd in private.items():
+            ref = e.bank[k].state_dict()
+            if not isinstance(sd, dict) or set(sd) != set(ref) or any(
+                    not torch.is_tensor(sd[n]) or sd[n].shape != ref[n].shape for n in ref):
+                return {}, {}, False
         valid = shared is not None and contribution_ok(msg.get("loss"), msg.get("empty"), shared, private)
         return shared or {}, private, valid
 

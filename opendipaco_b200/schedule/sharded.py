@@ -45,7 +45,8 @@ from ..train.loop import _opt_state_cpu, _state_cpu
 from .aggregate import check_aggregate, robust_delta
 from .assignment import coordinator_key, is_assignee, version_lag
 from .compress import (apply_state_delta, check_mode, compress_delta, compress_shard, compress_state,
-                       encode_state_delta, maybe_dequantize, pseudograd_digest, restore_shard, state_digest)
+                       declared_shape, encode_state_delta, maybe_dequantize, pseudograd_digest, restore_shard,
+                       state_digest)
 from .guard import all_finite, clip_norm_, loss_ok
 from .identity import peer_id_of, sign_record, verify_record
 from .ownership import (EpochManager, derive_epoch, epoch_newer, make_epoch_record, owners_for,
@@ -129,21 +130,7 @@ def _safe_version(v):
     return None
 
 
-def _declared_shape(payload):
-    """The dense shape a pseudo-gradient payload claims, without decoding it."""
-    try:
-        if torch.is_tensor(payload):
-            return tuple(payload.shape)
-        if isinstance(payload, dict):
-            if torch.is_tensor(payload.get("q")):
-                return tuple(payload["q"].shape)
-            if "q4" in payload:
-                return tuple(int(s) for s in payload["shape"])
-            if "sp" in payload:
-                return tuple(int(s) for s in payload["sp"])
-    except (TypeError, ValueError, KeyError):
-        return None
-    return None
+_declared_shape = declared_shape
 
 
 def _addr(a):
