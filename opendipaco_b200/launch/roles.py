@@ -533,7 +533,10 @@ def _local_sharded(cfg: LaunchConfig):
         t.join(timeout=10)
     for w in ws:
         w.join(timeout=5)
-    return box["result"]
+    sched, completed = box["result"]
+    # the trained global modules, read from their owners (for evaluation after the run)
+    sched.owner_banks = {k: ps.bank[k] for ps, _, _ in pss for k in ps.owned_keys}
+    return sched, completed
 
 
 def _local_rendezvous(cfg: LaunchConfig):
