@@ -1686,13 +1686,15 @@ def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, 
                        poll_interval=0.02, max_tasks=None, fault_hook=None, tls=None, tls_hostname=None,
                        stop_event=None, max_batch_size=None, max_shards=None, reconnect=True,
                        reconnect_timeout=30.0, data_dir=None, data_source=None, data_tokenizer=None,
-                       verify_routing=False, bucket=None, identity=None):
+                       verify_routing=False, bucket=None, identity=None, contribution_hook=None):
     """Lease -> fetch from owners -> train -> commit (grant) -> push to owners.
 
     ``auth_key`` (or ``identity``) is the credential; ``bucket`` a shared
     ``throttle.TokenBucket`` capping this worker's bandwidth; ``data_dir`` caches
     shards materialised from shipped specs (``verify_routing`` re-fits the shipped
-    router from the public source first and refuses to train on a mismatch)."""
+    router from the public source first and refuses to train on a mismatch).
+    ``contribution_hook(path, contribution) -> contribution`` rewrites each finished
+    task before it is committed (adversary and fault injection in harnesses)."""
     from .distributed import ShardCache, heartbeats, materialize_shard_spec
 
     engine = _build_engine(config, diloco, device, seed)
@@ -1747,6 +1749,8 @@ def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, 
                              if msg.get("probe") is not None else None)
                     contrib = worker._train_path(path, cache[path], msg["batch_size"], msg["gen_id"],
                                                  inner_steps=msg.get("inner_steps"), probe=probe)
+                    if contribution_hook is not None:  # fault / adversary injection in harnesses
+                        contrib = contribution_hook(path, contrib)
             except Exception as exc:
                 link.sch_rpc({"type": "nack", "lease": lease, "path": path, "error": repr(exc)})
                 continue
