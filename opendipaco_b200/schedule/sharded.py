@@ -1752,14 +1752,20 @@ def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, 
                     if contribution_hook is not None:  # fault / adversary injection in harnesses
                         contrib = contribution_hook(path, contrib)
             except Exception as exc:
-                link.sch_rpc({"type": "nack", "lease": lease, "path": path, "error": repr(exc)})
+                try:
+                    link.sch_rpc({"type": "nack", "lease": lease, "path": path, "error": repr(exc)})
+                except (OSError, ConnectionError):
+                    return      # the scheduler is gone as well
                 continue
             digest = pseudograd_digest(contrib.shared_delta) if (msg.get("audit") or msg.get("check_only")) else None
             commit = {"type": "commit", "lease": lease, "path": path, "gen_id": msg["gen_id"], "loss": contrib.loss,
                       "empty": contrib.empty, "worker_id": wid, "digest": digest, "base": base,
                       "check_only": bool(msg.get("check_only")), "probe_before": contrib.probe_before,
                       "probe_after": contrib.probe_after}
-            ack = link.sch_rpc(commit)
+            try:
+                ack = link.sch_rpc(commit)
+            except (OSError, ConnectionError):
+                return          # the scheduler went away while this task trained
             if msg.get("check_only") or not ack.get("accepted"):
                 continue
             engine._opt_state[path] = contrib.opt_state
@@ -1774,7 +1780,10 @@ def run_sharded_worker(config, diloco, scheduler_addr, *, device="cpu", seed=0, 
             private_p = {k: compress_state(sd, mode) for k, sd in contrib.private_state.items()}
             refused = _push_group(routing, ack["grant"], shared_p, private_p, link)
             if refused:
-                fresh = link.sch_rpc({"type": "routing", "keys": sorted(refused)}).get("routing", {})
+                try:
+                    fresh = link.sch_rpc({"type": "routing", "keys": sorted(refused)}).get("routing", {})
+                except (OSError, ConnectionError):
+                    return
                 routing = {**routing, **fresh}
                 refused = _push_group(routing, ack["grant"], {k: v for k, v in shared_p.items() if k in refused},
                                       {k: v for k, v in private_p.items() if k in refused}, link)
