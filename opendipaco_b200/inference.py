@@ -6,8 +6,11 @@
   score only targets at positions >= prefix_len (the paper's protocol), token-level
   sum / count, exp.
 * ``routed_window_perplexity``: re-route every ``window`` tokens from the previous
-  window and score each window under its path with the full preceding context
-  recomputed (no KV cache), the reference's definition.
+  window and score each window under its path with the full preceding context, the
+  reference's definition. By default the context is not recomputed: each (sequence,
+  path) pair keeps the per-layer keys and values of the tokens it has processed and
+  only extends them, so every token passes each path at most once instead of once per
+  later window (``kv_cache=False`` recomputes the prefix like the reference).
 
 On CUDA ``routed_perplexity`` scores the routed sequences of up to 16 paths side by
 side (``GroupedScorer``: one grouped forward with the training step's tcgen05 kernels,
@@ -25,6 +28,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from .config import DiPaCoConfig
+from .models.llama import apply_rope, rope_cos_sin
 from .models.path import PathModel, build_path_model
 from .routing.base import Featurizer, Router
 from .topology import Path
@@ -125,13 +129,109 @@ def _grouped_routed_perplexity(config, bank, sequences, paths, start, batch_size
     return float("nan") if count == 0 else float(torch.exp(total / count))
 
 
+def _norm(mod, x: torch.Tensor) -> torch.Tensor:
+    h = x.float()
+    return mod.weight * (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + mod.variance_epsilon))
+
+
+def _extend(model: PathModel, ids: torch.Tensor, cache: list | None, start: int):
+    """Run tokens ``ids`` [b, n] at positions ``start, start + 1, ...`` through ``model``
+    given each layer's cached (keys, values) of positions ``< start``; returns the
+    logits [b, n, vocab] and the extended cache. Plain fp32 tensor ops on any device
+    (the same arithmetic as the modules' reference forward)."""
+    bb = model.config.backbone
+    x = F.embedding(ids, model.embed.embed_tokens.weight).float()
+    b, n = ids.shape
+    cos, sin = rope_cos_sin(bb.head_dim, bb.rope_theta, n, ids.device, offset=start)
+    layers = [layer for block in model.body for layer in block.layers]
+    out = []
+    for i, layer in enumerate(layers):
+        att = layer.self_attn
+        h = _norm(layer.input_layernorm, x)
+        q = F.linear(h, att.q_proj.weight).view(b, n, att.num_heads, att.head_dim).transpose(1, 2)
+        k = F.linear(h, att.k_proj.weight).view(b, n, att.num_kv, att.head_dim).transpose(1, 2)
+        v = F.linear(h, att.v_proj.weight).view(b, n, att.num_kv, att.head_dim).transpose(1, 2)
+        q, k = apply_rope(q, cos, sin).to(v.dtype), apply_rope(k, cos, sin).to(v.dtype)
+        if cache is not None:
+            k, v = torch.cat([cache[i][0], k], dim=2), torch.cat([cache[i][1], v], dim=2)
+        out.append((k, v))
+        if att.num_kv != att.num_heads:
+            rep = att.num_heads // att.num_kv
+            k, v = k.repeat_interleave(rep, dim=1), v.repeat_interleave(rep, dim=1)
+        total = k.shape[2]
+        mask = torch.ones(n, total, dtype=torch.bool, device=ids.device).tril(diagonal=total - n)
+        o = F.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+        x = x + F.linear(o.transpose(1, 2).reshape(b, n, att.num_heads * att.head_dim), att.o_proj.weight)
+        h = _norm(layer.post_attention_layernorm, x)
+        mlp = layer.mlp
+        x = x + F.linear(F.silu(F.linear(h, mlp.gate_proj.weight)) * F.linear(h, mlp.up_proj.weight),
+                         mlp.down_proj.weight)
+    return F.linear(_norm(model.head.norm, x), model.head.lm_head.weight), out
+
+
+def _cached_windows(models, route_window, sequences, window, prefix_len, batch_size, dev):
+    """Token-level (CE sum, count) of the windowed protocol with per-(sequence, path)
+    key/value caches; a cache is cut back to the position whose logits score the
+    window's first target before it is extended."""
+    nseq, slen = sequences.shape
+    caches: dict = {}  # (sequence, path) -> (cached length, [(k, v)] per layer, each [1, kv, len, d])
+    total, count = 0.0, 0
+    for w in range(math.ceil(slen / window)):
+        w0, w1 = w * window, min((w + 1) * window, slen)
+        t0 = max(w0, prefix_len, 1)
+        if t0 >= w1:
+            continue
+        paths = route_window(w)
+        for pidx in paths.unique().tolist():
+            model = models(pidx)
+            rows = (paths == pidx).nonzero(as_tuple=True)[0].tolist()
+            by_start: dict = {}
+            for r in rows:  # resume each sequence from what its cache under this path holds
+                c = min(caches.get((r, pidx), (0, None))[0], t0 - 1)
+                by_start.setdefault(c, []).append(r)
+            for c, rs in sorted(by_start.items()):
+                for s0 in range(0, len(rs), batch_size):
+                    part = rs[s0:s0 + batch_size]
+                    ids = sequences[part, c:w1].to(dev)
+                    cache = None
+                    if c > 0:
+                        per = [caches[(r, pidx)][1] for r in part]
+                        cache = [(torch.cat([p[i][0][:, :, :c] for p in per]),
+                                  torch.cat([p[i][1][:, :, :c] for p in per])) for i in range(len(per[0]))]
+                    logits, new = _extend(model, ids, cache, c)
+                    for j, r in enumerate(part):
+                        caches[(r, pidx)] = (w1, [(k[j:j + 1], v[j:j + 1]) for k, v in new])
+                    total += _ce_sum(logits[:, t0 - 1 - c:w1 - 1 - c, :], ids[:, t0 - c:])
+                    count += len(part) * (w1 - t0)
+    return total, count
+
+
 @torch.no_grad()
 def routed_window_perplexity(config: DiPaCoConfig, bank: dict[str, nn.Module],
                              sequences: torch.Tensor, router: Router, featurizer: Featurizer,
                              window: int = 64, batch_size: int = 8, compose_fn=None,
-                             prefix_len: int = 32) -> float:
+                             prefix_len: int = 32, kv_cache: bool = True) -> float:
     if sequences.numel() == 0:
         return float("nan")
+    if kv_cache:
+        dev = next(next(iter(bank.values())).parameters()).device
+        topo = config.build_topology()
+        nseq, slen = sequences.shape
+        built: dict = {}
+
+        def models(pidx):
+            if pidx not in built:
+                p = topo.path_from_index(pidx)
+                built[pidx] = (compose_fn(p) if compose_fn is not None else compose_path(config, bank, p)).eval()
+            return built[pidx]
+
+        def route_window(w):
+            rc = w - 1 if w > 0 else 0
+            return route([sequences[n, rc * window:min((rc + 1) * window, slen)] for n in range(nseq)],
+                         router, featurizer)
+
+        total, count = _cached_windows(models, route_window, sequences, window, prefix_len, batch_size, dev)
+        return float("nan") if count == 0 else float(torch.exp(torch.tensor(total / count)))
     dev = next(next(iter(bank.values())).parameters()).device
     topo = config.build_topology()
     nseq, slen = sequences.shape

@@ -513,7 +513,8 @@ class ParameterServer(ReactorServer):
             return
         now = time.monotonic()
         with self._lock:
-            for k in [k for k, ts in self._buffer_ts.items() if self._buffers.get(k) and now - ts >= self.quorum_timeout]:
+            due = [k for k, ts in self._buffer_ts.items() if self._buffers.get(k) and now - ts >= self.quorum_timeout]
+            for k in due:
                 self._flush_buffer(k)
 
     def _private_ok(self, private) -> bool:

@@ -64,8 +64,9 @@ def vram_table(*, hidden: int, heads: int, kv_heads: int | None, ffn: int, layer
     from ..config import BackboneConfig, DiPaCoConfig
     from ..train.memory import fused_breakdown, vram_breakdown
 
-    bb = BackboneConfig(vocab_size=vocab, hidden_size=hidden, num_attention_heads=heads, num_key_value_heads=kv_heads,
-                        intermediate_size=ffn, layers_per_level=list(layers), max_position_embeddings=max(2048, seq_len))
+    bb = BackboneConfig(vocab_size=vocab, hidden_size=hidden, num_attention_heads=heads,
+                        num_key_value_heads=kv_heads, intermediate_size=ffn, layers_per_level=list(layers),
+                        max_position_embeddings=max(2048, seq_len))
     cfg = DiPaCoConfig(backbone=bb, level_sizes=list(levels), sequence_length=seq_len)
     out = {"module_executor": vram_breakdown(cfg, batch_size=batch, seq_len=seq_len),
            "module_executor_bf16_ckpt": vram_breakdown(cfg, batch_size=batch, seq_len=seq_len, autocast=True,

@@ -150,3 +150,24 @@ def test_windowed_evaluation_matches_one_path_and_reroutes_on_a_topic_shift():
     r = routed_window_perplexity(cfg, bank, shifted, _ByFirstToken(), _first_token, window=12, prefix_len=4)
     p0 = routed_window_perplexity(cfg, bank, shifted, _Const(0), _first_token, window=12, prefix_len=4)
     assert math.isfinite(r) and r != pytest.approx(p0, rel=1e-6)
+
+
+@pytest.mark.parametrize("window,prefix", [(12, 4), (7, 10), (16, 0), (50, 4)])
+def test_cached_windowed_evaluation_equals_recomputing_the_prefix(window, prefix):
+    cfg = tiny_config(heads=4, kv=2)
+    bank = build_module_bank(cfg, seed=0)
+    with torch.no_grad():
+        for k in ("L1E1", "L0E1"):
+            for p in bank[k].parameters():
+                p.add_(0.3 * torch.randn(p.shape, generator=torch.Generator().manual_seed(2)))
+
+    class _Mod4:
+        def predict(self, feats):
+            return (feats[:, 0] % 4).long()
+
+    seqs = torch.randint(0, 48, (5, 50), generator=torch.Generator().manual_seed(3))
+    cached = routed_window_perplexity(cfg, bank, seqs, _Mod4(), _first_token, window=window, prefix_len=prefix,
+                                      batch_size=2)
+    again = routed_window_perplexity(cfg, bank, seqs, _Mod4(), _first_token, window=window, prefix_len=prefix,
+                                     batch_size=2, kv_cache=False)
+    assert cached == pytest.approx(again, rel=1e-5)
