@@ -56,7 +56,7 @@ from .quorum import confirm_version, divergent_peers, read_quorum_versions
 from .ratelimit import RateLimiter
 from .reactor import ReactorServer
 from .reputation import Reputation
-from .rpc import connect, rpc
+from .rpc import connect, record_issued_at, rpc
 from .scheduler import AsyncScheduler
 from .throttle import tailor_encoding
 from .wire import DEFAULT_MAX_MSG_BYTES, _kb
@@ -198,6 +198,8 @@ class ParameterServer(ReactorServer):
         self.min_owner_reputation = min_owner_reputation
         self.corpus_weights = dict(corpus_weights) if corpus_weights else None
         self._tracker = None
+        self._directory: dict = {}       # decentralized gossip: peer id -> newest signed record
+        self._self_record = None
         self._hb_paused = threading.Event()  # set: stop refreshing the tracker record (suspend)
         full = build_module_bank(config, seed=bank_seed)
         self.bank = {k: full[k].to(self.device) for k in self.owned_keys}
@@ -251,6 +253,8 @@ class ParameterServer(ReactorServer):
             return self._drain_recv(msg, peer_id)
         if kind == "digest":
             return self._digests(msg)
+        if kind == "directory":
+            return self._directory_rpc(msg)
         if kind == "commit":
             return self._commit(msg, peer_id)
         if kind == "generation":
@@ -802,9 +806,9 @@ class ParameterServer(ReactorServer):
             return None
         return self.identity if self.identity is not None else self.auth_key
 
-    def _peer_rpc(self, addr, msg):
+    def _peer_rpc(self, addr, msg, timeout: float = 5.0):
         cred = self._peer_cred()
-        s = connect(_addr(addr), cred, timeout=5.0, tls=self.peer_tls)
+        s = connect(_addr(addr), cred, timeout=timeout, tls=self.peer_tls)
         try:
             return rpc(s, msg)
         finally:
@@ -874,15 +878,64 @@ class ParameterServer(ReactorServer):
         if rec and verify_epoch_record(rec, signer_pub=self.scheduler_pub) and epoch_newer(rec, self._epoch):
             self.apply_epoch(rec)
 
+    def import_directory(self, records) -> int:
+        """Merge signed peer records into this owner's directory (gossip): a record
+        replaces its peer's held one only when newer, and records older than
+        ``directory_ttl`` are not taken. Returns how many were taken."""
+        now, taken = time.time(), 0
+        with self._lock:
+            for r in records or []:
+                if not (verify_record(r) and r.get("kind") == "peer"):
+                    continue
+                ts = record_issued_at(r)
+                if ts is None or now - ts > self.directory_ttl:
+                    continue
+                held = self._directory.get(r["peer_id"])
+                if held is None or ts > record_issued_at(held):
+                    self._directory[r["peer_id"]] = r
+                    taken += 1
+        return taken
+
+    def directory(self) -> list:
+        """The live records this owner knows (its own first), stale ones dropped."""
+        now = time.time()
+        with self._lock:
+            for pid in [p for p, r in self._directory.items() if now - record_issued_at(r) > self.directory_ttl]:
+                del self._directory[pid]
+            recs = [r for p, r in self._directory.items() if p != self.peer_id]
+        own = self._self_record
+        return ([own] if own is not None else []) + recs
+
+    def _directory_rpc(self, msg: dict) -> dict:
+        return {"type": "directory", "records": self.directory()}
+
     def _derive_from_directory(self) -> None:
-        """Decentralized: every owner derives the same epoch from the tracker directory."""
+        """Decentralized: gather signed peer records from the trackers (bootstrap seeds)
+        and from the current co-owners' directories (gossip), then derive the epoch that
+        every owner derives from the same records. With the trackers gone the owners
+        keep converging through one another."""
         if self._tracker is None or self.schedule_mode != "decentralized":
             return
         from .tracker import fetch_directory
 
-        try:
-            everyone = fetch_directory(self._tracker["addr"], auth_key=self._tracker["auth"], tls=self._tracker["tls"])
-        except (OSError, ConnectionError, PermissionError):
+        wait = min(2.0, self.directory_ttl / 4)  # a dead seed or peer must not stall the pass
+        for a in self._tracker["all"]:
+            try:
+                self.import_directory(fetch_directory(a, auth_key=self._tracker["auth"], tls=self._tracker["tls"],
+                                                      timeout=wait))
+            except (OSError, ConnectionError, PermissionError):
+                continue
+        with self._lock:
+            peers = {o["peer_id"]: o["addr"] for o in (self._epoch or {}).get("owners", []) if o.get("addr")}
+        for pid, addr in peers.items():
+            if pid == self.peer_id:
+                continue
+            try:
+                self.import_directory(self._peer_rpc(addr, {"type": "directory"}, timeout=wait).get("records"))
+            except (OSError, ConnectionError, PermissionError):
+                continue
+        everyone = self.directory()
+        if not everyone:
             return
         self._dir_workers = _worker_directory_ids(everyone)
         recs = [r for r in everyone if "owner" in (r.get("roles") or [])]
@@ -923,7 +976,7 @@ class ParameterServer(ReactorServer):
         With ``circuit_addrs`` (from :func:`relay.serve_via_relays`) the owner registers
         as a ``nat`` peer reachable through those relays instead of at
         ``advertise_host``."""
-        from .tracker import dedup_seeds, register_peer
+        from .tracker import dedup_seeds
 
         if self.identity is None:
             raise ValueError("a tracker heartbeat needs an owner identity")
@@ -931,19 +984,26 @@ class ParameterServer(ReactorServer):
         self._tracker = {"addr": addrs[0], "all": addrs, "auth": auth_key, "tls": tls}
         stop = self._repl_stop
 
+        from .tracker import make_peer_record, tracker_rpc
+
         def beat():
             while True:
-                for a in addrs if not self._hb_paused.is_set() else ():
-                    try:
-                        if circuit_addrs:
-                            register_peer(a, self.identity, reachability="nat", circuit_addrs=list(circuit_addrs),
-                                          roles=["owner"], auth_key=auth_key, tls=tls, timeout=5.0)
-                        else:
-                            register_peer(a, self.identity, reachability="public",
-                                          peer_addr=(advertise_host, self.port), roles=["owner"], auth_key=auth_key,
-                                          tls=tls, timeout=5.0)
-                    except (OSError, ConnectionError, PermissionError):
-                        continue
+                if not self._hb_paused.is_set():
+                    # a fresh signed record each beat: registered on the trackers and served to
+                    # co-owners that gossip directories (decentralized mode)
+                    if circuit_addrs:
+                        rec = make_peer_record(self.identity, reachability="nat", circuit_addrs=list(circuit_addrs),
+                                               roles=["owner"])
+                    else:
+                        rec = make_peer_record(self.identity, reachability="public",
+                                               addr=(advertise_host, self.port), roles=["owner"])
+                    self._self_record = rec
+                    for a in addrs:  # a dead tracker must not hold back the next beat
+                        try:
+                            tracker_rpc(a, {"type": "register", "record": rec}, auth_key=auth_key, tls=tls,
+                                        timeout=min(5.0, max(0.5, interval)))
+                        except (OSError, ConnectionError, PermissionError):
+                            continue
                 if stop.wait(interval):
                     return
 

@@ -228,3 +228,41 @@ def test_decentralized_workers_train_every_path_over_tcp(cluster):
         states = [ps.bank[key].state_dict() for ps in reps]
         assert all(torch.equal(states[0][n], s[n]) for s in states[1:] for n in states[0]), key
         assert len({ps._versions[key] for ps in reps}) == 1
+
+
+def test_owners_keep_converging_by_gossip_after_the_tracker_is_gone():
+    """Decentralized owners fed by a tracker: once it is gone they exchange their
+    directories, and an owner that crashes ages out of every survivor's derived epoch."""
+    from opendipaco_b200.schedule import Tracker
+
+    cfg = tiny_config()
+    tracker = Tracker(host="127.0.0.1", open_enrollment=True, ttl=30.0)
+    tracker.start()
+    ids = [PeerIdentity.generate() for _ in range(3)]
+    owners = [ParameterServer(cfg, [], DL, host="127.0.0.1", identity=i, schedule_mode="decentralized", k=2,
+                              replicate_interval=0.2, auth_key=KEY, directory_ttl=3.0) for i in ids]
+    try:
+        for ps in owners:
+            ps.start()
+            ps.start_tracker_heartbeat(("127.0.0.1", tracker.port), "127.0.0.1", interval=0.3)
+
+        def converged(pss, n):
+            eps = [ps._epoch for ps in pss]
+            return all(e is not None and len(e["owners"]) == n for e in eps) and len({e["epoch"] for e in eps}) == 1
+
+        deadline = time.monotonic() + 15
+        while time.monotonic() < deadline and not converged(owners, 3):
+            time.sleep(0.1)
+        assert converged(owners, 3)
+        tracker.shutdown()
+        owners[2].simulate_crash()
+        deadline = time.monotonic() + 20
+        while time.monotonic() < deadline and not converged(owners[:2], 2):
+            time.sleep(0.1)
+        assert converged(owners[:2], 2)
+        assert {o["peer_id"] for o in owners[0]._epoch["owners"]} == {ids[0].peer_id, ids[1].peer_id}
+        assert owners[0].directory()[0]["peer_id"] == ids[0].peer_id  # its own record first
+    finally:
+        for ps in owners:
+            ps.shutdown()
+        tracker.shutdown()
