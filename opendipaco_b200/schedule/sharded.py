@@ -1862,6 +1862,21 @@ def _verified_peers(records) -> list:
     return [r for r in records if verify_record(r) and r.get("kind") == "peer"]
 
 
+def _owner_directories(link, epoch) -> list:
+    """The newest verified record of every peer the owners of ``epoch`` know."""
+    best: dict = {}
+    for o in epoch.get("owners") or []:
+        try:
+            recs = link.ps_rpc(o["addr"], {"type": "directory"}).get("records") or []
+        except (OSError, ConnectionError, PermissionError):
+            continue
+        for r in _verified_peers(recs):
+            ts = record_issued_at(r)
+            if ts is not None and (r["peer_id"] not in best or ts > record_issued_at(best[r["peer_id"]])):
+                best[r["peer_id"]] = r
+    return list(best.values())
+
+
 def _worker_directory_ids(records) -> list[str]:
     return sorted(r["peer_id"] for r in _verified_peers(records) if "worker" in (r.get("roles") or []))
 
@@ -1911,7 +1926,11 @@ def run_decentralized_worker(config, diloco, tracker, corpus, *, identity, auth_
         threading.Thread(target=beat, daemon=True).start()
 
         def epoch_fn():
-            recs, _ = fetch_directory_multi(seed_list, auth_key=auth_key, tls=tls, seed_quorum=seed_quorum)
+            recs, answered = fetch_directory_multi(seed_list, auth_key=auth_key, tls=tls, seed_quorum=seed_quorum,
+                                                   timeout=2.0)
+            if not answered and state["epoch"] is not None:
+                # every seed is gone: read the directories the last epoch's owners gossip
+                recs = _owner_directories(link, state["epoch"])
             owners = [r for r in recs if "owner" in (r.get("roles") or [])]
             state["workers"] = _worker_directory_ids(recs)
             if owners:

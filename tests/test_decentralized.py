@@ -266,3 +266,25 @@ def test_owners_keep_converging_by_gossip_after_the_tracker_is_gone():
         for ps in owners:
             ps.shutdown()
         tracker.shutdown()
+
+
+def test_workers_read_the_owners_directories_when_every_seed_is_gone():
+    from opendipaco_b200.schedule.sharded import _owner_directories
+
+    a, b, c = (PeerIdentity.generate() for _ in range(3))
+    old = make_peer_record(c, reachability="public", addr=("10.0.0.3", 1), roles=["owner"])
+    time.sleep(0.01)
+    new = make_peer_record(c, reachability="public", addr=("10.0.0.3", 2), roles=["owner"])
+    dirs = {"x": [make_peer_record(a, roles=["worker"]), old], "y": [new, dict(old, roles=["scheduler"])]}
+
+    class _Link:
+        def ps_rpc(self, addr, msg):
+            if addr == "dead":
+                raise ConnectionError("gone")
+            assert msg == {"type": "directory"}
+            return {"records": dirs[addr]}
+
+    epoch = {"owners": [{"addr": "x"}, {"addr": "dead"}, {"addr": "y"}]}
+    got = {r["peer_id"]: r for r in _owner_directories(_Link(), epoch)}
+    assert set(got) == {a.peer_id, c.peer_id} and got[c.peer_id]["addr"] == ["10.0.0.3", 2]  # newest, tamper dropped
+    assert b.peer_id not in got
