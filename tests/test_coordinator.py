@@ -1,6 +1,7 @@
 """The TCP coordinator's policies, driven message by message (CPU): staleness bound,
 fencing of a reclaimed lease, heartbeats, nack, warm shipping of private and unchanged
-shared weights, update-norm clipping and non-finite rejection; plus the transport's
+shared weights, update-norm clipping and non-finite rejection, idle backoff and batch
+caps; plus the transport's
 connection cap and a bounded handler pool serving many clients at once.
 
 Behaviours of the reference's ``tests/test_scheduler_distributed.py``
@@ -156,3 +157,18 @@ def test_bounded_handler_pool_serves_many_clients():
     finally:
         srv.shutdown()
     assert out == {i: i for i in range(24)} and 1 <= len(seen) <= 2
+
+
+def test_idle_replies_carry_the_backoff_and_batches_are_capped():
+    c, e = _coord(idle_backoff=0.7)
+    paths = list(e.topology.paths())
+    held = [_req(c, f"w{i}") for i in range(len(paths))]  # every path leased
+    idle = _req(c, "late")
+    assert idle["type"] == "idle" and idle["retry_in"] == 0.7
+    c._handle({"type": "nack", "path": list(held[0]["path"]), "lease": held[0]["lease"]}, 0)
+    small = _req(c, "small", capabilities={"max_batch": 2})
+    assert small["type"] == "task" and small["batch_size"] == 2
+    plain, _ = _coord()
+    for i in range(len(paths)):
+        _req(plain, f"w{i}")
+    assert _req(plain, "late") == {"type": "idle"}  # no backoff configured: the worker's own poll
