@@ -242,3 +242,37 @@ def test_relay_role_and_a_nat_owner_in_the_directory():
         tracker.shutdown()
         stop.set()
         th.join(timeout=10)
+
+
+def test_tls_runs_end_to_end_through_the_relay(relay, tmp_path):
+    """With TLS the session is encrypted between client and NAT server: the relay only
+    sees the handshake and ciphertext, never the frames' plaintext."""
+    from opendipaco_b200.schedule.tls import client_context, generate_selfsigned_cert, server_context
+
+    cert, key = generate_selfsigned_cert(str(tmp_path))
+    srv, _, addr = _nat_echo(relay, tls=server_context(cert, key), auth_key="k")
+    seen = []
+    real_pipe = relay._pipe
+
+    async def spy(src, dst):  # record what crosses the relay
+        orig_write = dst.write
+
+        def write(chunk):
+            seen.append(bytes(chunk))
+            orig_write(chunk)
+
+        dst.write = write
+        await real_pipe(src, dst)
+
+    relay._pipe = spy
+    try:
+        s = connect(addr, auth_key="k", tls=client_context(cafile=cert, check_hostname=False))
+        try:
+            marker = "plaintext-marker-0123456789"
+            assert rpc(s, {"type": "x", "x": marker})["x"] == marker
+            assert s.version() in ("TLSv1.2", "TLSv1.3")
+        finally:
+            s.close()
+        assert seen and not any(marker.encode() in c for c in seen)
+    finally:
+        srv.shutdown()
