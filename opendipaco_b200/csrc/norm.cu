@@ -160,8 +160,11 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, long long sx, co
 // Register-resident variant (H = 128 * NV): each warp loads its row's x, dy and residual
 // grad once, keeps the weights and its dw partial in registers, and folds the partials of
 // its block's 8 warps in a fixed order at the end. Same arithmetic as rmsnorm_bwd_kernel.
+// Up to H = 384 the row fits in 80 registers, so three blocks (24 warps) share an SM
+// instead of two; wider rows keep the compiler's own register count.
 template <int NV>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const float* __restrict__ x, long long sx,
+__global__ void __launch_bounds__(256, (NV <= 3) ? 3 : 1)
+    rmsnorm_bwd_reg_kernel(const float* __restrict__ x, long long sx,
                                                               const float* __restrict__ w, long long sw,
                                                               const float* __restrict__ rstd,
                                                               const float* __restrict__ dy, long long sdy,
@@ -237,7 +240,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const float* __res
   }
 }
 
-// dw[g][i] = sum_b dw_part[g][b][i] in fixed order.
+// dw[g][i] = sum_b dw_part[g][b][i] in a fixed order: eight interleaved running sums
+// (block b feeds sum b % 8), so eight independent loads are in flight per thread instead
+// of one dependent chain of nblk loads, then a fixed pairwise fold of the eight.
 __global__ void reduce_parts_kernel(const float* __restrict__ part, int nblk, int H, int G, float* dw, long long sdw,
                                     float beta) {
   pdl_wait();
@@ -246,10 +251,21 @@ __global__ void reduce_parts_kernel(const float* __restrict__ part, int nblk, in
   if (idx >= G * H) return;
   const int g = idx / H, i = idx % H;
   const float* p = part + (long long)g * nblk * H + i;
-  float s = 0.f;
-  for (int b = 0; b < nblk; ++b) s += p[(long long)b * H];
+  float s[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) s[k] = 0.f;
+  int b = 0;
+  for (; b + 8 <= nblk; b += 8) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = p[(long long)(b + k) * H];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s[k] += v[k];
+  }
+  for (int k = 0; b < nblk; ++b, ++k) s[k] += p[(long long)b * H];
+  const float t = ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
   float* d = dw + g * sdw + i;
-  *d = beta != 0.f ? s + beta * *d : s;
+  *d = beta != 0.f ? t + beta * *d : t;
 }
 
 // ids: [G][M] int32; E: group g's table at E + g*se ([V][H] fp32); out: [G][M][H] fp32.
