@@ -44,7 +44,9 @@ from .wire import _LEN, decode, encode, recv_msg, send_msg
 
 logger = logging.getLogger("opendipaco_b200.schedule")
 
-RELAY_CONTEXT = b"opendipaco-relay:"
+# distinct signing contexts: a relay's proof to a client can never pass as a reservation
+RESERVE_CONTEXT = b"opendipaco-relay-reserve:"
+CIRCUIT_CONTEXT = b"opendipaco-relay-circuit:"
 CONTROL_MAX_BYTES = 64 * 1024  # relay control frames are tiny
 
 
@@ -191,7 +193,7 @@ class RelayServer:
 
     async def _reservation(self, msg, nonce, reader, writer) -> None:
         pub = msg.get("pub")
-        if not (isinstance(pub, str) and verify_signature(pub, msg.get("sig"), RELAY_CONTEXT + nonce)):
+        if not (isinstance(pub, str) and verify_signature(pub, msg.get("sig"), RESERVE_CONTEXT + nonce)):
             await self._write(writer, {"type": "refused", "reason": "bad signature"})
             writer.transport.abort()
             return
@@ -235,7 +237,7 @@ class RelayServer:
             t_reader, t_writer = await asyncio.wait_for(fut, self.connect_timeout)
             nonce = bytes.fromhex(str(msg.get("nonce", "")))
             await self._write(writer, {"type": "connected", "relay_pub": self.identity.public_key_hex,
-                                       "sig": self.identity.sign(RELAY_CONTEXT + nonce).hex()})
+                                       "sig": self.identity.sign(CIRCUIT_CONTEXT + nonce).hex()})
             self.stats["circuits"] += 1
             await asyncio.gather(self._pipe(reader, t_writer), self._pipe(t_reader, writer))
         except (asyncio.TimeoutError, ConnectionError, OSError, ValueError):
@@ -289,7 +291,7 @@ def dial_circuit(addr: str, timeout: float = 10.0) -> socket.socket:
                                   f"{reply.get('reason', 'closed')}")
         pub = reply.get("relay_pub")
         if not (isinstance(pub, str) and peer_id_of(pub) == relay_id
-                and verify_signature(pub, reply.get("sig"), RELAY_CONTEXT + nonce)):
+                and verify_signature(pub, reply.get("sig"), CIRCUIT_CONTEXT + nonce)):
             raise PermissionError(f"the relay at {host}:{port} is not {relay_id[:12]}")
         s.settimeout(None)
         return s
@@ -337,7 +339,7 @@ class RelayReservation:
         if ch.get("type") != "challenge":
             s.close()
             raise ConnectionError("not a relay")
-        sig = self.identity.sign(RELAY_CONTEXT + bytes.fromhex(ch["nonce"])).hex()
+        sig = self.identity.sign(RESERVE_CONTEXT + bytes.fromhex(ch["nonce"])).hex()
         send_msg(s, {"type": "reserve", "pub": self.identity.public_key_hex, "sig": sig})
         reply = recv_msg(s, CONTROL_MAX_BYTES) or {}
         if reply.get("type") != "reserved" or reply.get("relay") != self.relay_id:
