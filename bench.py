@@ -84,7 +84,7 @@ PRESETS = {
                      "16 layers [8,8], vocab 128256, every path over 2 GPUs"),
 }
 CFG = dict(PRESETS["c2"])
-BASELINE_VALUE = None  # the reference publishes no throughput number
+PUBLISHED_VALUE = None  # the reference publishes no throughput number
 PEER_GBPS = 770.0      # measured peer-copy bandwidth per direction per GPU on this hardware (GB/s)
 
 
@@ -450,7 +450,7 @@ def run(args) -> dict:
         "metric": "tokens/sec/box", "value": round(value, 1), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_round, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+        "vs_baseline": None if PUBLISHED_VALUE is None else value / PUBLISHED_VALUE,
         "dtype": "bf16", "data": "synthetic (Zipf(1.1) token ids, 20k docs, len U[128,2048]); random init",
         "config": {"model": CFG["model"], "preset": args.config, "global_batch": B * npaths, "seq_len": CFG["seq"],
                    "parallelism": f"paths{world}" + (f"_dp{CFG['dp']}" if CFG["dp"] > 1 else ""),

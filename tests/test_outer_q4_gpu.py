@@ -62,7 +62,7 @@ def test_quant_kernel_matches_reference_with_error_feedback():
         assert torch.equal(res_k[off:off + n], r)
     assert torch.all(qd[1536 // 2:2048 // 2] == 0xAA) and torch.all(qs[1536 // G:2048 // G] == -1.0)
     assert torch.equal(res_k[1536:2048], res[1536:2048])
-    # error feedback: what round 1 dropped is carried into round 2's codes
+    # error feedback: what the first outer step dropped is carried into the second step's codes
     q1 = _unpack(qd[:768]).float() * qs[:12].repeat_interleave(G)
     ext().outer_nvlink_quant(regs, nregs, groups, delta, res_k, qd, qs)
     torch.cuda.synchronize()
