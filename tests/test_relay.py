@@ -276,3 +276,29 @@ def test_tls_runs_end_to_end_through_the_relay(relay, tmp_path):
         assert seen and not any(marker.encode() in c for c in seen)
     finally:
         srv.shutdown()
+
+
+def test_a_circuit_proof_cannot_be_replayed_as_a_reservation(relay):
+    """The relay signs the client's nonce to prove itself; that signature is made in the
+    circuit context, so presenting it to another relay as a reservation fails."""
+    import socket as _s
+
+    from opendipaco_b200.schedule.wire import recv_msg, send_msg
+
+    srv, _, addr = _nat_echo(relay)
+    other = RelayServer(host="127.0.0.1").start()
+    try:
+        victim = _s.create_connection(("127.0.0.1", other.port), timeout=5)
+        nonce = recv_msg(victim)["nonce"]              # the other relay's reservation challenge
+        c = _s.create_connection(("127.0.0.1", relay.port), timeout=5)
+        recv_msg(c)
+        send_msg(c, {"type": "circuit", "target": addr.rsplit("/", 1)[1], "nonce": nonce})
+        proof = recv_msg(c)
+        assert proof["type"] == "connected"
+        send_msg(victim, {"type": "reserve", "pub": proof["relay_pub"], "sig": proof["sig"]})
+        assert recv_msg(victim)["type"] == "refused" and other.reserved_peers() == []
+        c.close()
+        victim.close()
+    finally:
+        other.shutdown()
+        srv.shutdown()
