@@ -1690,29 +1690,49 @@ class _WorkerLink:
 
 
 def _fetch_keys(link, routing, keys, versions, cold_keys, keyframes, pin=None):
-    """Fetch the listed keys from their first reachable owner; returns {key: state_dict}."""
-    by_owner: dict = {}
-    for k in keys:
-        by_owner.setdefault(_addr(routing[k][0]), []).append(k)
-    out = {}
-    for addr, ks in by_owner.items():
-        msg = {"type": "fetch", "keys": ks, "have": {k: list(versions[k]) for k in ks if k in versions},
-               "cold": any(k in cold_keys for k in ks)}
-        if pin:
-            msg["pin"] = {k: pin[k] for k in ks if k in pin}
-        reply = link.ps_rpc(addr, msg)
-        for k, payload in (reply.get("weights") or {}).items():
-            if isinstance(payload, dict) and "delta" in payload:
-                held = keyframes.get(k)
-                if held is None or held[0] != tuple(payload["base"]):
-                    versions.pop(k, None)  # ask for full weights next time
-                    raise ValueError(f"delta for {k} against a keyframe this worker does not hold")
-                payload = apply_state_delta(held[1], payload["delta"])
-            out[k] = payload
-            v = _version_pair(reply["versions"][k])
-            versions[k] = v
-            # one keyframe per key: the state at the version this worker reports as held
-            keyframes[k] = (v, {n: t.float() if t.is_floating_point() else t for n, t in payload.items()})
+    """Fetch the listed keys from their owners, primary first: a key an owner reports
+    missing (not active there yet, or an aged-out pinned version) or an owner that does
+    not answer falls back to the key's next replica. Returns {key: state_dict}; raises
+    ConnectionError when no replica serves some key."""
+    out: dict = {}
+    pending = list(keys)
+    rank = 0
+    while pending:
+        by_owner: dict = {}
+        unserved = []
+        for k in pending:
+            owners = routing[k]
+            if rank < len(owners):
+                by_owner.setdefault(_addr(owners[rank]), []).append(k)
+            else:
+                unserved.append(k)
+        if unserved:
+            raise ConnectionError(f"no replica served {sorted(unserved)}")
+        retry = []
+        for addr, ks in by_owner.items():
+            msg = {"type": "fetch", "keys": ks, "have": {k: list(versions[k]) for k in ks if k in versions},
+                   "cold": any(k in cold_keys for k in ks)}
+            if pin:
+                msg["pin"] = {k: pin[k] for k in ks if k in pin}
+            try:
+                reply = link.ps_rpc(addr, msg)
+            except (OSError, ConnectionError):
+                retry += ks
+                continue
+            retry += [k for k in (reply.get("missing") or []) if k in ks]
+            for k, payload in (reply.get("weights") or {}).items():
+                if isinstance(payload, dict) and "delta" in payload:
+                    held = keyframes.get(k)
+                    if held is None or held[0] != tuple(payload["base"]):
+                        versions.pop(k, None)  # ask for full weights next time
+                        raise ValueError(f"delta for {k} against a keyframe this worker does not hold")
+                    payload = apply_state_delta(held[1], payload["delta"])
+                out[k] = payload
+                v = _version_pair(reply["versions"][k])
+                versions[k] = v
+                # one keyframe per key: the state at the version this worker reports as held
+                keyframes[k] = (v, {n: t.float() if t.is_floating_point() else t for n, t in payload.items()})
+        pending, rank = retry, rank + 1
     return out
 
 

@@ -2,7 +2,8 @@
 the version the worker holds while that version is in its ring (8 deep by default),
 full weights after it ages out; ``down="full"`` never ships a delta; the worker keeps
 one keyframe per key and recovers with a full fetch when it lacks the base; whole
-sharded runs train with delta-down, with audits and across path switches.
+sharded runs train with delta-down, with audits and across path switches; a fetch falls back
+to the next replica when the primary lacks a key or does not answer.
 
 Behaviours of the reference's ``tests/test_w2_delta.py``.
 """
@@ -111,3 +112,27 @@ def test_sharded_runs_train_with_delta_down(audits):
     sched, completed = run_local(LaunchConfig.from_dict(d))
     assert len(completed) == 4 and min(completed.values()) >= 3
     assert sched.metrics.accepted_updates >= 12
+
+
+def test_fetch_falls_back_to_the_next_replica():
+    """A key its primary reports missing (syncing, not active there yet) or a primary
+    that does not answer is fetched from the key's next replica."""
+    a, key = _owner()
+    b, _ = _owner()
+    _push(b, key, "t1")
+    a._active.discard(key)                       # the primary still syncs this key
+
+    class _Owners:
+        def ps_rpc(self, addr, msg):
+            if addr == "down":
+                raise ConnectionError("gone")
+            return {"a": a, "b": b}[addr]._fetch(msg)
+
+    versions, keyframes = {}, {}
+    got = _fetch_keys(_Owners(), {key: ["a", "b"]}, [key], versions, set(), keyframes)
+    assert versions[key] == b._versions[key] and torch.equal(got[key]["layers.0.mlp.up_proj.weight"],
+                                                             b.bank[key].state_dict()["layers.0.mlp.up_proj.weight"])
+    versions.clear()
+    assert key in _fetch_keys(_Owners(), {key: ["down", "b"]}, [key], versions, set(), keyframes)
+    with pytest.raises(ConnectionError):
+        _fetch_keys(_Owners(), {key: ["down", "a"]}, [key], {}, set(), {})
